@@ -1,0 +1,86 @@
+"""ctypes binding of libabra_b200.so (the C ABI in include/abra_b200.h).
+
+The shared library is built in-tree by ``python -m abra_b200.build``.  There
+is no fallback: if the library is missing or does not load, importing this
+module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libabra_b200.so"
+
+ABRA_OK = 0
+ABRA_E_INVALID = -1
+ABRA_E_CUDA = -2
+ABRA_E_UNSUPPORTED = -3
+ABRA_MMVQ_PDL = 1
+
+_vp, _i32, _i64, _u64, _f32 = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_float
+_fp = C.c_void_p  # float* passed as an address
+
+# name -> (restype, argtypes); every symbol declared in include/abra_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "abra_version": (C.c_char_p, []),
+    "abra_last_error": (C.c_char_p, []),
+    "abra_device_error": (C.c_int, [C.POINTER(C.c_uint32), _i32]),
+    "abra_q4k_mmvq": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _vp]),
+    "abra_q4k_mmvq_candidate": (C.c_int, [_i32, _vp, _vp, _fp, _i64, _i64, _i32, _vp]),
+    "abra_q4k_mmvq_ex": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _i32, _vp]),
+    "abra_q4k_mmvq_partials": (C.c_int, [_vp, _vp, _fp, _vp, _vp, _i64, _i64, _i32, _i32, _vp]),
+    "launch_pinned_upstream_mmvq": (None, [_vp, _vp, _fp, _i64, _i64, _vp]),
+    "abra_quantize_q8_1": (C.c_int, [_fp, _vp, _i64, _i32, _vp]),
+    "launch_pinned_upstream_q8_1_quantize": (None, [_fp, _vp, _i64, _vp]),
+    "abra_rmsnorm_quantize_q8_1": (C.c_int, [_fp, _fp, _f32, _vp, _fp, _i64, _i32, _vp]),
+    "abra_gen_q4k": (C.c_int, [_vp, _i64, _u64, _u64, _i64, _vp]),
+    "abra_gen_uniform_f32": (C.c_int, [_fp, _i64, _u64, _u64, _i64, _f32, _f32, _vp]),
+    "abra_candidate_count": (C.c_int, []),
+    "abra_candidate_info": (C.c_int, [_i32] + [C.POINTER(C.c_int32)] * 5),
+    "abra_tune_set": (C.c_int, [_i64, _i64, _i32, _i32]),
+    "abra_tune_get": (C.c_int, [_i64, _i64, _i32]),
+    "abra_tune_clear": (C.c_int, []),
+}
+
+
+class AbraError(RuntimeError):
+    """A C-ABI call returned an error code."""
+
+    def __init__(self, code: int, func: str, msg: str):
+        super().__init__(f"{func} failed ({code}): {msg}")
+        self.code = code
+
+
+def _load() -> C.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m abra_b200.build` "
+            "(there is no CPU fallback)")
+    lib = C.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def last_error() -> str:
+    msg = lib.abra_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, func: str) -> None:
+    if rc != ABRA_OK:
+        msg = last_error()
+        if rc == ABRA_E_INVALID:
+            raise ValueError(f"{func}: {msg}")
+        raise AbraError(rc, func, msg)
+
+
+def call(name: str, *args) -> int:
+    rc = getattr(lib, name)(*args)
+    check(rc, name)
+    return rc

@@ -1,0 +1,209 @@
+// api.cu -- the extern "C" surface of libabra_b200.so (declared in
+// include/abra_b200.h).  Argument checking, error strings, the tuning table.
+#include <cstdarg>
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "../../include/abra_b200.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(ABRA_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+std::mutex g_tune_mu;
+std::map<std::tuple<int64_t, int64_t, int>, int> g_tune;
+
+// Default when the table has no entry: more k-parts for few rows or long K.
+int default_candidate(int64_t N, int64_t K, int ncols) {
+    const int64_t rg = (N + 7) / 8;
+    const int64_t nsb = K / 256;
+    if (rg < 148) return nsb >= 16 ? 802 : 404;
+    if (rg < 4 * 148) return nsb >= 16 ? 402 : 202;
+    (void)ncols;
+    return nsb >= 24 ? 202 : 102;
+}
+
+int check_mmvq_args(const void *w, const void *x, const float *y, int64_t N, int64_t K,
+                    int32_t ncols, int64_t ldy) {
+    if (!w || !x || !y) return fail(ABRA_E_INVALID, "null pointer");
+    if (N <= 0 || K <= 0) return fail(ABRA_E_INVALID, "N and K must be positive (N=%lld K=%lld)", (long long)N, (long long)K);
+    if (K % 256 != 0) return fail(ABRA_E_INVALID, "K must be a multiple of QK_K=256 (K=%lld)", (long long)K);
+    if (K > 65536) return fail(ABRA_E_UNSUPPORTED, "K=%lld too large (max 65536)", (long long)K);
+    if (N > (int64_t)0x7fffffff - 8) return fail(ABRA_E_UNSUPPORTED, "N=%lld too large", (long long)N);
+    if (ncols < 1 || ncols > 8) return fail(ABRA_E_UNSUPPORTED, "ncols must be in 1..8 (got %d)", ncols);
+    if (ldy < N) return fail(ABRA_E_INVALID, "ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
+    if (!aligned16(w) || !aligned16(x)) return fail(ABRA_E_INVALID, "weights and activations must be 16-byte aligned");
+    return ABRA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *abra_version(void) { return "abra_b200 0.1.0 sm_100a"; }
+const char *abra_last_error(void) { return g_err; }
+
+int abra_device_error(uint32_t *out, int32_t clear) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+    unsigned v = 0;
+    e = abra::error_word_gen_quant(&v, clear != 0);
+    if (e == cudaSuccess) e = abra::error_word_mmvq(&v, clear != 0);
+    if (e != cudaSuccess) return cuda_fail(e, "device error word");
+    if (out) *out = v;
+    return ABRA_OK;
+}
+
+int abra_q4k_mmvq_ex(const void *w, const void *x, float *y, int64_t N, int64_t K,
+                     int32_t ncols, int64_t ldy, int32_t candidate, int32_t flags,
+                     void *stream) {
+    int rc = check_mmvq_args(w, x, y, N, K, ncols, ldy);
+    if (rc) return rc;
+    int id = candidate;
+    if (id == 0) id = abra_tune_get(N, K, ncols);
+    const abra::MmvqConfig *cfg = abra::mmvq_candidate_by_id(id);
+    if (!cfg) return fail(ABRA_E_INVALID, "unknown candidate id %d", id);
+    cudaError_t e = abra::launch_mmvq_q4k(*cfg, w, x, y, N, K, ncols, ldy,
+                                          (flags & ABRA_MMVQ_PDL) ? abra::MMVQ_PDL : 0,
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "mmvq launch");
+    return ABRA_OK;
+}
+
+int abra_q4k_mmvq(const void *w, const void *x, float *y, int64_t N, int64_t K, int32_t ncols,
+                  void *stream) {
+    return abra_q4k_mmvq_ex(w, x, y, N, K, ncols, N, 0, 0, stream);
+}
+
+int abra_q4k_mmvq_candidate(int32_t candidate, const void *w, const void *x, float *y,
+                            int64_t N, int64_t K, int32_t ncols, void *stream) {
+    if (candidate == 0) return fail(ABRA_E_INVALID, "candidate id 0 is the tuned dispatch; use abra_q4k_mmvq");
+    return abra_q4k_mmvq_ex(w, x, y, N, K, ncols, N, candidate, 0, stream);
+}
+
+int abra_q4k_mmvq_partials(const void *w, const void *x, float *y, int32_t *P, int32_t *M,
+                           int64_t N, int64_t K, int32_t ncols, int32_t ks, void *stream) {
+    int rc = check_mmvq_args(w, x, y, N, K, ncols, N);
+    if (rc) return rc;
+    if (!P || !M) return fail(ABRA_E_INVALID, "null partials pointer");
+    if (!(ncols == 1 || ncols == 2 || ncols == 4 || ncols == 8))
+        return fail(ABRA_E_UNSUPPORTED, "partials: ncols must be 1, 2, 4 or 8");
+    if (!(ks == 1 || ks == 2 || ks == 4)) return fail(ABRA_E_UNSUPPORTED, "partials: ks must be 1, 2 or 4");
+    cudaError_t e = abra::launch_mmvq_q4k_partials(w, x, y, P, M, N, K, ncols, ks,
+                                                   static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "mmvq partials launch");
+    return ABRA_OK;
+}
+
+void launch_pinned_upstream_mmvq(const void *d_w_q4, const void *d_x_q8, float *d_y, int64_t N,
+                                 int64_t K, void *stream) {
+    abra_q4k_mmvq(d_w_q4, d_x_q8, d_y, N, K, 1, stream);
+}
+
+int abra_quantize_q8_1(const float *x, void *xq, int64_t K, int32_t ncols, void *stream) {
+    if (!x || !xq) return fail(ABRA_E_INVALID, "null pointer");
+    if (K <= 0 || K % 32 != 0) return fail(ABRA_E_INVALID, "K must be a positive multiple of QK8_1=32 (K=%lld)", (long long)K);
+    if (ncols < 1) return fail(ABRA_E_INVALID, "ncols must be >= 1");
+    if ((reinterpret_cast<uintptr_t>(x) & 3u) || (reinterpret_cast<uintptr_t>(xq) & 3u))
+        return fail(ABRA_E_INVALID, "x and x_q8_1 must be 4-byte aligned");
+    cudaError_t e = abra::launch_quantize_q8_1(x, xq, K, ncols, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+    return ABRA_OK;
+}
+
+void launch_pinned_upstream_q8_1_quantize(const float *d_x_f32, void *d_x_q8, int64_t K,
+                                          void *stream) {
+    abra_quantize_q8_1(d_x_f32, d_x_q8, K, 1, stream);
+}
+
+int abra_rmsnorm_quantize_q8_1(const float *x, const float *w, float eps, void *xq,
+                               float *xn_out, int64_t K, int32_t ncols, void *stream) {
+    if (!x || !w || !xq) return fail(ABRA_E_INVALID, "null pointer");
+    if (K <= 0 || K % 32 != 0 || K > 16384)
+        return fail(ABRA_E_INVALID, "K must be a multiple of 32 in 32..16384 (K=%lld)", (long long)K);
+    if (ncols < 1) return fail(ABRA_E_INVALID, "ncols must be >= 1");
+    cudaError_t e = abra::launch_rmsnorm_quantize_q8_1(x, w, eps, xq, xn_out, K, ncols,
+                                                       static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
+    return ABRA_OK;
+}
+
+int abra_gen_q4k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                 int64_t block_offset, void *stream) {
+    if (!dst || nblocks < 0 || block_offset < 0) return fail(ABRA_E_INVALID, "bad generator arguments");
+    if (reinterpret_cast<uintptr_t>(dst) & 7u) return fail(ABRA_E_INVALID, "dst must be 8-byte aligned");
+    cudaError_t e = abra::launch_gen_q4k(dst, nblocks, seed, tensor_id, block_offset,
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "gen_q4k launch");
+    return ABRA_OK;
+}
+
+int abra_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
+                         int64_t offset_index, float scale, float offset, void *stream) {
+    if (!dst || n < 0 || offset_index < 0) return fail(ABRA_E_INVALID, "bad generator arguments");
+    cudaError_t e = abra::launch_gen_uniform_f32(dst, n, seed, tensor_id, offset_index, scale,
+                                                 offset, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "gen_uniform launch");
+    return ABRA_OK;
+}
+
+int abra_candidate_count(void) {
+    int n = 0;
+    abra::mmvq_candidates(&n);
+    return n;
+}
+
+int abra_candidate_info(int32_t index, int32_t *id, int32_t *ks, int32_t *ncw,
+                        int32_t *ctas_per_sm, int32_t *stage_kb) {
+    int n = 0;
+    const abra::MmvqConfig *c = abra::mmvq_candidates(&n);
+    if (index < 0 || index >= n) return fail(ABRA_E_INVALID, "candidate index %d out of range", index);
+    if (id) *id = c[index].id;
+    if (ks) *ks = c[index].ks;
+    if (ncw) *ncw = c[index].ncw;
+    if (ctas_per_sm) *ctas_per_sm = c[index].ctas_per_sm;
+    if (stage_kb) *stage_kb = c[index].stage_kb;
+    return ABRA_OK;
+}
+
+int abra_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t candidate) {
+    if (!abra::mmvq_candidate_by_id(candidate)) return fail(ABRA_E_INVALID, "unknown candidate id %d", candidate);
+    std::lock_guard<std::mutex> lock(g_tune_mu);
+    g_tune[std::make_tuple(N, K, static_cast<int>(ncols))] = candidate;
+    return ABRA_OK;
+}
+
+int abra_tune_get(int64_t N, int64_t K, int32_t ncols) {
+    {
+        std::lock_guard<std::mutex> lock(g_tune_mu);
+        auto it = g_tune.find(std::make_tuple(N, K, static_cast<int>(ncols)));
+        if (it != g_tune.end()) return it->second;
+    }
+    return default_candidate(N, K, ncols);
+}
+
+int abra_tune_clear(void) {
+    std::lock_guard<std::mutex> lock(g_tune_mu);
+    g_tune.clear();
+    return ABRA_OK;
+}
+
+}  // extern "C"

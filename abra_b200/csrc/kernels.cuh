@@ -1,0 +1,56 @@
+// kernels.cuh -- host-side launchers shared between the .cu files of
+// libabra_b200.  Nothing here crosses the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace abra {
+
+// ---------------------------------------------------------------- MMVQ ---
+// One tuning candidate of the Q4_K x Q8_1 MMVQ family.
+struct MmvqConfig {
+    int id;           // stable candidate id (used in tuning tables)
+    int ks;           // k-parts per row group (1, 2, 4, 8): warps sharing a row group
+    int ncw;          // consumer warps per CTA (4 or 8)
+    int ctas_per_sm;  // grid = min(row groups, SMs * ctas_per_sm)
+    int stage_kb;     // shared-memory budget for the weight ring, KiB
+};
+
+const MmvqConfig *mmvq_candidates(int *count);
+const MmvqConfig *mmvq_candidate_by_id(int id);
+
+// flags for launch_mmvq_q4k
+enum : int {
+    MMVQ_PDL = 1,  // launch with programmatic dependent launch (weights must be immutable)
+};
+
+cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *x_q8, float *y,
+                            int64_t N, int64_t K, int ncols, int64_t ldy, int flags,
+                            cudaStream_t stream);
+// Debug: same kernel, additionally storing the exact int32 partials
+// P[c][r][b][s] and M[c][b][s].
+cudaError_t launch_mmvq_q4k_partials(const void *w, const void *x_q8, float *y, int32_t *P,
+                                     int32_t *M, int64_t N, int64_t K, int ncols, int ks,
+                                     cudaStream_t stream);
+
+// ------------------------------------------------------------ quantize ---
+cudaError_t launch_quantize_q8_1(const float *x, void *y, int64_t K, int ncols,
+                                 cudaStream_t stream);
+cudaError_t launch_rmsnorm_quantize_q8_1(const float *x, const float *w, float eps, void *y,
+                                         float *xn_out, int64_t K, int ncols,
+                                         cudaStream_t stream);
+
+// ----------------------------------------------------------- generator ---
+cudaError_t launch_gen_q4k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                           int64_t block_offset, cudaStream_t stream);
+cudaError_t launch_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
+                                   int64_t offset_index, float scale, float offset,
+                                   cudaStream_t stream);
+
+int device_sm_count();
+
+// Per-translation-unit device error words (see common.cuh).
+cudaError_t error_word_gen_quant(unsigned *value, bool clear);
+cudaError_t error_word_mmvq(unsigned *value, bool clear);
+
+}  // namespace abra

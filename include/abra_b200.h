@@ -1,0 +1,126 @@
+/*
+ * abra_b200.h -- C ABI of libabra_b200.so, the sm_100a Q4_K x Q8_1 decode
+ * path.
+ *
+ * Conventions (all entry points):
+ *   - Pointers are device pointers on the calling thread's current CUDA
+ *     device unless stated otherwise; `stream` is a cudaStream_t (NULL = the
+ *     legacy default stream).  Work is stream-ordered and asynchronous.
+ *   - Return 0 on success, a negative ABRA_E* code on error; the message is
+ *     available from abra_last_error() (thread-local).  No exception crosses
+ *     the ABI.  The reference throws std::invalid_argument for the same
+ *     conditions (kernels/q4k/q4k_q8_mmvq.cu:266-268,302,312-314;
+ *     kernels/q4k/q4k_family.cu:200-202,279).
+ *   - Layouts are ggml's: Q4_K rows of K/256 superblocks of 144 B, row-major;
+ *     Q8_1 activation columns of K/32 blocks of 36 B, column after column;
+ *     fp32 outputs y[c * ldy + r].  Weight and activation buffers must be
+ *     16-byte aligned.
+ *   - The library allocates no device memory in these calls.
+ */
+#ifndef ABRA_B200_H
+#define ABRA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ABRA_OK 0
+#define ABRA_E_INVALID (-1)     /* bad shape, alignment, id or pointer */
+#define ABRA_E_CUDA (-2)        /* a CUDA runtime call failed */
+#define ABRA_E_UNSUPPORTED (-3) /* shape/batch outside what the kernels cover */
+
+/* Flags for abra_q4k_mmvq_ex. */
+#define ABRA_MMVQ_PDL 1 /* programmatic dependent launch: weights are
+                           prefetched before the previous kernel in the
+                           stream completes, so the weights must not be
+                           written by that kernel */
+
+/* ---------------------------------------------------------- library ---- */
+const char *abra_version(void);
+const char *abra_last_error(void);
+/* Device error word set by kernels whose bounded waits gave up (bit 0: an
+ * mbarrier wait, bit 1: a cross-rank flag wait).  clear != 0 resets it.
+ * Synchronises the current device. */
+int abra_device_error(uint32_t *out, int32_t clear);
+
+/* ------------------------------------------------------------- MMVQ ---- */
+/* y = W x for Q4_K W (N x K) and ncols Q8_1 columns, 1 <= ncols <= 8,
+ * K % 256 == 0, K <= 65536 (configurations whose staging does not fit in
+ * shared memory return ABRA_E_CUDA).  Picks the tuned candidate for (N, K, ncols).
+ * Replaces launch_q4k_autotuned (kernels/q4k/q4k_family.cuh:89-97) and the
+ * mul_mat_vec_q hook abra_dispatch_mmvq (kernels/q4k/abra-mmvq.cuh:209-220). */
+int abra_q4k_mmvq(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, int64_t K,
+                  int32_t ncols, void *stream);
+
+/* One named candidate of the family (ids from abra_candidate_info).
+ * Replaces launch_q4k_candidate (kernels/q4k/q4k_family.cuh:63-71). */
+int abra_q4k_mmvq_candidate(int32_t candidate, const void *w_q4k, const void *x_q8_1,
+                            float *y, int64_t N, int64_t K, int32_t ncols, void *stream);
+
+/* Full form: explicit output column stride ldy >= N, candidate (0 = tuned)
+ * and ABRA_MMVQ_* flags. */
+int abra_q4k_mmvq_ex(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, int64_t K,
+                     int32_t ncols, int64_t ldy, int32_t candidate, int32_t flags,
+                     void *stream);
+
+/* Debug form of the same kernel: also stores the exact int32 sub-block dot
+ * products P[c][r][b][s] (ncols*N*(K/256)*8) and activation sums
+ * M[c][b][s] (ncols*(K/256)*8).  ks selects the k-split (1, 2 or 4);
+ * ncols in {1, 2, 4, 8}.  The reference computes the same integers inside
+ * vec_dot_q4_K_q8_1_impl_vmmq (kernels/q4k/q4k_vecdot.cuh:35-36). */
+int abra_q4k_mmvq_partials(const void *w_q4k, const void *x_q8_1, float *y, int32_t *P,
+                           int32_t *M, int64_t N, int64_t K, int32_t ncols, int32_t ks,
+                           void *stream);
+
+/* Drop-in for the reference's C shim of the same name and signature
+ * (kernels/q4k/upstream_adapter.cuh:12-19): one Q8_1 column. */
+void launch_pinned_upstream_mmvq(const void *d_w_q4, const void *d_x_q8, float *d_y,
+                                 int64_t N, int64_t K, void *stream);
+
+/* --------------------------------------------------------- Q8_1 -------- */
+/* x: ncols columns of K fp32 (K % 32 == 0) -> ncols x K/32 Q8_1 blocks.
+ * Replaces launch_quantize_f32_to_q8_1 / launch_custom_reference_q8_1_quantizer
+ * (kernels/q4k/q4k_q8_mmvq.cuh:91-103; semantics q4k_q8_mmvq.cu:223-255). */
+int abra_quantize_q8_1(const float *x, void *x_q8_1, int64_t K, int32_t ncols, void *stream);
+
+/* Drop-in for kernels/q4k/upstream_adapter.cuh:21-26 (one column). */
+void launch_pinned_upstream_q8_1_quantize(const float *d_x_f32, void *d_x_q8, int64_t K,
+                                          void *stream);
+
+/* Fused RMSNorm -> Q8_1, quantize once: xn = (x * r) * w with
+ * r = 1/sqrt(mean(x^2) + eps); xn is quantized to Q8_1 (and also written to
+ * xn_out when it is not NULL).  K % 32 == 0, K <= 16384.  Replaces the
+ * RMSNorm + per-consumer quantize pair that the reference's Q8 reuse cache
+ * de-duplicates (kernels/q4k/abra-q8-reuse.cuh:3-71). */
+int abra_rmsnorm_quantize_q8_1(const float *x, const float *w, float eps, void *x_q8_1,
+                               float *xn_out, int64_t K, int32_t ncols, void *stream);
+
+/* ------------------------------------------------------- generators ---- */
+/* Seeded synthetic Q4_K superblocks [block_offset, block_offset+nblocks) of
+ * tensor tensor_id: d, dmin ~ U(0.001, 0.02) fp16, scales/mins ~ U{0..63},
+ * nibbles ~ U{0..15}.  dst 8-byte aligned. */
+int abra_gen_q4k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                 int64_t block_offset, void *stream);
+/* dst[i] = fmaf(u_i, scale, offset), u_i ~ U[0,1) on a 2^-24 grid. */
+int abra_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
+                         int64_t offset_index, float scale, float offset, void *stream);
+
+/* --------------------------------------------------------- autotuner --- */
+/* Candidate enumeration: index 0..abra_candidate_count()-1 -> id, k-split,
+ * consumer warps, CTAs per SM, stage budget (KiB).  Replaces
+ * get_all_candidate_ids / get_candidate_spec (kernels/q4k/q4k_family.cuh:59-61). */
+int abra_candidate_count(void);
+int abra_candidate_info(int32_t index, int32_t *id, int32_t *ks, int32_t *ncw,
+                        int32_t *ctas_per_sm, int32_t *stage_kb);
+/* Tuning table keyed by (N, K, ncols).  Replaces register_autotuned_table_entry /
+ * get_autotuned_candidate_for_shape (kernels/q4k/q4k_family.cuh:86-87). */
+int abra_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t candidate);
+int abra_tune_get(int64_t N, int64_t K, int32_t ncols); /* returns candidate id */
+int abra_tune_clear(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ABRA_B200_H */

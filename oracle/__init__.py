@@ -1,0 +1,214 @@
+"""CPU oracle of the Q4_K x Q8_1 decode path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
+package, and only as the checker (or the timed CPU restatement); the product
+library never imports it.
+
+``liborc.so`` (q4k_oracle.c) restates the reference's arithmetic in C:
+block layouts kernels/q4k/q4k_q8_mmvq.cuh:42-57, scale unpack
+tests/q4k_q8_test.cu:44-52, the f64 oracle tests/q4k_q8_test.cu:54-107,
+vec_dot_q4_K_q8_1 kernels/q4k/q4k_vecdot.cuh:23-87 and the Q8_1 quantizer
+kernels/q4k/q4k_q8_mmvq.cu:223-255 (paths inside talystalys/abra).
+
+``_ref/libq4k_ref.so`` is the reference's own kernel family compiled from its
+sources (see Makefile); ``ref`` binds it when present.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORC_PATH = HERE / "liborc.so"
+REF_PATH = HERE / "_ref" / "libq4k_ref.so"
+
+QK_K, QK8_1, Q4K_BYTES, Q81_BYTES = 256, 32, 144, 36
+
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_i64, _i32, _u64, _f32 = C.c_int64, C.c_int32, C.c_uint64, C.c_float
+
+
+def build(ref: bool = True) -> None:
+    """Build liborc.so (and _ref/ when the reference sources are present)."""
+    subprocess.run(["make", "-s", "-C", str(HERE), "all" if ref else "orc"], check=True)
+
+
+def _load() -> C.CDLL:
+    if not ORC_PATH.exists():
+        build(ref=False)
+    lib = C.CDLL(str(ORC_PATH))
+    sig = {
+        "orc_f32_to_f16": (C.c_uint16, [C.c_float]),
+        "orc_f16_to_f32": (C.c_float, [C.c_uint16]),
+        "orc_gen_q4k": (None, [_u8p, _i64, _u64, _u64, _i64]),
+        "orc_gen_uniform_f32": (None, [_f32p, _i64, _u64, _u64, _i64, _f32, _f32]),
+        "orc_quantize_q8_1": (None, [_f32p, _u8p, _i64, _i32]),
+        "orc_rmsnorm_quantize_q8_1": (None, [_f32p, _f32p, _f32, _u8p, C.c_void_p, _i64, _i32]),
+        "orc_rms_scale": (C.c_float, [_f32p, _f32, _i64]),
+        "orc_q4k_partials": (None, [_u8p, _u8p, _i32p, _i32p, _i64, _i64, _i32]),
+        "orc_q4k_gemv": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i32, _i32]),
+        "orc_q4k_gemv_slices": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i32]),
+        "orc_q4k_gemv_f64": (None, [_u8p, _u8p, _f64p, _i64, _i64, _i32]),
+        "orc_q4k_absdot_f64": (None, [_u8p, _u8p, _f64p, _i64, _i64, _i32]),
+        "orc_dequant_q4k": (None, [_u8p, _f32p, _i64]),
+        "orc_slice_starts": (None, [_i32, _i32p]),
+        "orc_max_threads": (C.c_int32, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res, args
+    return lib
+
+
+lib = _load()
+
+
+# ------------------------------------------------------------ generators ---
+def gen_q4k(N: int, K: int, seed: int, tensor_id: int, row_offset: int = 0) -> np.ndarray:
+    """Q4_K rows [row_offset, row_offset+N) of a K-wide tensor, as uint8 (N, K/256*144)."""
+    nsb = K // QK_K
+    out = np.empty(N * nsb * Q4K_BYTES, dtype=np.uint8)
+    lib.orc_gen_q4k(out, N * nsb, seed, tensor_id, row_offset * nsb)
+    return out.reshape(N, nsb * Q4K_BYTES)
+
+
+def gen_uniform_f32(n: int, seed: int, tensor_id: int, scale: float, offset: float,
+                    offset_index: int = 0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib.orc_gen_uniform_f32(out, n, seed, tensor_id, offset_index, scale, offset)
+    return out
+
+
+def gen_normal_f32(shape, seed: int) -> np.ndarray:
+    """x ~ N(0, 1), host-side only (numpy PCG64)."""
+    return np.random.default_rng(seed).standard_normal(shape, dtype=np.float32)
+
+
+# -------------------------------------------------------------- Q8_1 ------
+def quantize_q8_1(x: np.ndarray) -> np.ndarray:
+    """x: (ncols, K) or (K,) fp32 -> uint8 (ncols, K/32*36)."""
+    x2 = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    ncols, K = x2.shape
+    out = np.empty(ncols * (K // QK8_1) * Q81_BYTES, dtype=np.uint8)
+    lib.orc_quantize_q8_1(x2, out, K, ncols)
+    return out.reshape(ncols, -1)
+
+
+def rmsnorm_quantize_q8_1(x: np.ndarray, w: np.ndarray, eps: float):
+    x2 = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    ncols, K = x2.shape
+    q = np.empty(ncols * (K // QK8_1) * Q81_BYTES, dtype=np.uint8)
+    xn = np.empty((ncols, K), dtype=np.float32)
+    lib.orc_rmsnorm_quantize_q8_1(x2, np.ascontiguousarray(w, dtype=np.float32), eps, q,
+                                  xn.ctypes.data, K, ncols)
+    return q.reshape(ncols, -1), xn
+
+
+# -------------------------------------------------------------- MMVQ ------
+def _shape(w: np.ndarray, xq: np.ndarray, K: int):
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+    xq2 = np.ascontiguousarray(np.atleast_2d(xq), dtype=np.uint8)
+    ncols = xq2.shape[0]
+    N = w.size // ((K // QK_K) * Q4K_BYTES)
+    return w, xq2.reshape(-1), N, ncols
+
+
+def partials(w, xq, K: int):
+    """Exact int32 P (ncols, N, K/256, 8) and M (ncols, K/256, 8)."""
+    w, xq, N, ncols = _shape(w, xq, K)
+    nsb = K // QK_K
+    P = np.empty(ncols * N * nsb * 8, dtype=np.int32)
+    M = np.empty(ncols * nsb * 8, dtype=np.int32)
+    lib.orc_q4k_partials(w, xq, P, M, N, K, ncols)
+    return P.reshape(ncols, N, nsb, 8), M.reshape(ncols, nsb, 8)
+
+
+def gemv(w, xq, K: int, nthreads: int = 1) -> np.ndarray:
+    """Canonical fp32 GEMV (bit-exact target of the CUDA kernels), (ncols, N)."""
+    w, xq, N, ncols = _shape(w, xq, K)
+    y = np.empty(ncols * N, dtype=np.float32)
+    lib.orc_q4k_gemv(w, xq, y, N, K, ncols, nthreads)
+    return y.reshape(ncols, N)
+
+
+def gemv_slices(w, xq, K: int) -> np.ndarray:
+    w, xq, N, ncols = _shape(w, xq, K)
+    v = np.empty(ncols * N * 8, dtype=np.float32)
+    lib.orc_q4k_gemv_slices(w, xq, v, N, K, ncols)
+    return v.reshape(ncols, N, 8)
+
+
+def gemv_f64(w, xq, K: int) -> np.ndarray:
+    w, xq, N, ncols = _shape(w, xq, K)
+    y = np.empty(ncols * N, dtype=np.float64)
+    lib.orc_q4k_gemv_f64(w, xq, y, N, K, ncols)
+    return y.reshape(ncols, N)
+
+
+def absdot_f64(w, xq, K: int) -> np.ndarray:
+    w, xq, N, ncols = _shape(w, xq, K)
+    s = np.empty(ncols * N, dtype=np.float64)
+    lib.orc_q4k_absdot_f64(w, xq, s, N, K, ncols)
+    return s.reshape(ncols, N)
+
+
+def dequant_q4k(w: np.ndarray) -> np.ndarray:
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+    nb = w.size // Q4K_BYTES
+    out = np.empty(nb * QK_K, dtype=np.float32)
+    lib.orc_dequant_q4k(w, out, nb)
+    return out
+
+
+def slice_starts(nsb: int) -> np.ndarray:
+    s = np.empty(9, dtype=np.int32)
+    lib.orc_slice_starts(nsb, s)
+    return s
+
+
+def f32_to_f16_bits(f: float) -> int:
+    return int(lib.orc_f32_to_f16(f))
+
+
+def max_threads() -> int:
+    return int(lib.orc_max_threads())
+
+
+# --------------------------------------------- reference kernel family ----
+class RefFamily:
+    """The reference's own MMVQ family (oracle/_ref/libq4k_ref.so), GPU only."""
+
+    def __init__(self, path: Path = REF_PATH):
+        if not path.exists():
+            raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+        L = C.CDLL(str(path))
+        vp = C.c_void_p
+        L.ref_launch_candidate.argtypes = [C.c_int, vp, vp, vp, C.c_int, C.c_int, vp]
+        L.ref_launch_variant.argtypes = [C.c_int, vp, vp, vp, C.c_int, C.c_int, vp]
+        L.ref_quantize_q8_1.argtypes = [vp, vp, C.c_int, vp]
+        L.ref_candidate_ids.argtypes = [C.POINTER(C.c_int), C.c_int]
+        L.ref_autotuned_candidate.argtypes = [C.c_int, C.c_int, C.c_int]
+        self.lib = L
+
+    def candidate_ids(self) -> list[int]:
+        buf = (C.c_int * 64)()
+        n = self.lib.ref_candidate_ids(buf, 64)
+        return list(buf[:n])
+
+    def launch_candidate(self, cid: int, w: int, x: int, y: int, N: int, K: int,
+                         stream: int = 0) -> None:
+        if self.lib.ref_launch_candidate(cid, w, x, y, N, K, stream) != 0:
+            raise ValueError(f"reference launch_q4k_candidate({cid}) threw")
+
+    def quantize(self, x: int, y: int, K: int, stream: int = 0) -> None:
+        if self.lib.ref_quantize_q8_1(x, y, K, stream) != 0:
+            raise ValueError("reference quantizer threw")
+
+    def autotuned_candidate(self, N: int, K: int, arch: int = 61) -> int:
+        return int(self.lib.ref_autotuned_candidate(N, K, arch))

@@ -1,0 +1,438 @@
+/*
+ * q4k_oracle.c -- CPU oracle for the Q4_K x Q8_1 decode path.
+ *
+ * TEST INFRASTRUCTURE ONLY (see q4k_oracle.h).  Compiled with
+ * -ffp-contract=off so that every fp32 operation below rounds exactly once,
+ * in the order written; the CUDA kernels use __fmul_rn/__fadd_rn/__fmaf_rn in
+ * the same order, which is what makes the two bit-identical.
+ *
+ * Reference formulas restated here (paths inside talystalys/abra):
+ *   block_q4_K / block_q8_1 ........ kernels/q4k/q4k_q8_mmvq.cuh:42-57
+ *   get_scale_min_k4 ............... tests/q4k_q8_test.cu:44-52
+ *   f64 oracle ..................... tests/q4k_q8_test.cu:54-107
+ *   vec_dot_q4_K_q8_1 .............. kernels/q4k/q4k_vecdot.cuh:23-87
+ *   Q8_1 quantizer ................. kernels/q4k/q4k_q8_mmvq.cu:223-255
+ */
+#include "q4k_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define QK_K 256
+#define QK8_1 32
+#define Q4K_BYTES 144
+#define Q81_BYTES 36
+
+/* ------------------------------------------------------------------------ */
+/* fp16 <-> fp32, IEEE binary16 with round-to-nearest-even                  */
+/* ------------------------------------------------------------------------ */
+float orc_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31;
+    const uint32_t exp = (h >> 10) & 0x1f;
+    const uint32_t man = h & 0x3ff;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else { /* subnormal: value = man * 2^-24, exact in fp32 */
+            float v = (float)man * 5.9604644775390625e-08f;
+            memcpy(&bits, &v, 4);
+            bits |= sign;
+        }
+    } else if (exp == 0x1f) {
+        bits = sign | 0x7f800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 112u) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+uint16_t orc_f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+    const uint32_t ax = x & 0x7fffffffu;
+    if (ax >= 0x7f800000u) { /* inf or nan */
+        return (uint16_t)(sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0u));
+    }
+    if (ax >= 0x477ff000u) { /* rounds to >= 65520 -> inf */
+        return (uint16_t)(sign | 0x7c00u);
+    }
+    if (ax < 0x38800000u) { /* below 2^-14: subnormal half (or zero) */
+        /* value / 2^-24, rounded to nearest even, as an integer 0..1024 */
+        const uint32_t e = ax >> 23;
+        if (e < 102) return sign; /* < 2^-25: rounds to 0 */
+        const uint32_t m = (ax & 0x7fffffu) | 0x800000u;
+        const uint32_t shift = 126 - e; /* 14 + (126-14-e) ... */
+        /* value = m * 2^(e-150); in units of 2^-24 -> m * 2^(e-126) */
+        const uint32_t q = m >> shift;
+        const uint32_t rem = m & ((1u << shift) - 1u);
+        const uint32_t half = 1u << (shift - 1);
+        uint32_t r = q;
+        if (rem > half || (rem == half && (q & 1u))) r++;
+        return (uint16_t)(sign | r);
+    }
+    /* normal half */
+    uint32_t r = ((ax >> 13) - (112u << 10));
+    const uint32_t rem = ax & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) r++;
+    return (uint16_t)(sign | r);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Counter-based generator: word i of a stream is the splitmix64 finaliser   */
+/* applied to key + (i+1) * golden-gamma, i.e. the i-th splitmix64 output.   */
+/* ------------------------------------------------------------------------ */
+static inline uint64_t mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+static inline uint64_t stream_key(uint64_t seed, uint64_t tensor_id) {
+    return mix64(seed + 0x9E3779B97F4A7C15ull) ^ mix64(tensor_id * 0xD1B54A32D192ED03ull + 1ull);
+}
+static inline uint64_t stream_word(uint64_t key, uint64_t i) {
+    return mix64(key + (i + 1ull) * 0x9E3779B97F4A7C15ull);
+}
+static inline float unit24(uint64_t bits24) { /* exact: 24-bit int * 2^-24 */
+    return (float)(uint32_t)bits24 * 5.9604644775390625e-08f;
+}
+
+void orc_gen_q4k(uint8_t *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                 int64_t block_offset) {
+    const uint64_t key = stream_key(seed, tensor_id);
+    for (int64_t i = 0; i < nblocks; ++i) {
+        const uint64_t gb = (uint64_t)(block_offset + i);
+        uint8_t *blk = dst + i * Q4K_BYTES;
+        for (int w = 0; w < 18; ++w) {
+            const uint64_t h = stream_word(key, gb * 18u + (uint64_t)w);
+            memcpy(blk + 8 * w, &h, 8); /* little-endian host */
+        }
+        const uint64_t h0 = stream_word(key, gb * 18u);
+        const float d = fmaf(unit24(h0 >> 40), 0.019f, 0.001f);
+        const float dmin = fmaf(unit24((h0 >> 16) & 0xffffffu), 0.019f, 0.001f);
+        const uint16_t hd = orc_f32_to_f16(d), hm = orc_f32_to_f16(dmin);
+        memcpy(blk + 0, &hd, 2);
+        memcpy(blk + 2, &hm, 2);
+    }
+}
+
+void orc_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
+                         int64_t offset_index, float scale, float offset) {
+    const uint64_t key = stream_key(seed, tensor_id);
+    for (int64_t i = 0; i < n; ++i) {
+        const uint64_t h = stream_word(key, (uint64_t)(offset_index + i));
+        dst[i] = fmaf(unit24(h >> 40), scale, offset);
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Q8_1 quantizer.  Restates kernels/q4k/q4k_q8_mmvq.cu:223-255: amax over   */
+/* 32, d = amax/127, id = d>0 ? 1/d : 0, q = (int8)roundf(x*id), s = d*sum.  */
+/* ------------------------------------------------------------------------ */
+static void quantize_block(const float *x, uint8_t *out) {
+    float amax = 0.0f;
+    for (int j = 0; j < QK8_1; ++j) {
+        const float v = fabsf(x[j]);
+        if (v > amax) amax = v;
+    }
+    const float d = amax / 127.0f;
+    const float id = d > 0.0f ? 1.0f / d : 0.0f;
+    int sum = 0;
+    int8_t *qs = (int8_t *)(out + 4);
+    for (int j = 0; j < QK8_1; ++j) {
+        const int8_t q = (int8_t)roundf(x[j] * id);
+        qs[j] = q;
+        sum += q;
+    }
+    const uint16_t hd = orc_f32_to_f16(d);
+    const uint16_t hs = orc_f32_to_f16(d * (float)sum);
+    memcpy(out + 0, &hd, 2);
+    memcpy(out + 2, &hs, 2);
+}
+
+void orc_quantize_q8_1(const float *x, uint8_t *y, int64_t K, int32_t ncols) {
+    const int64_t nb = K / QK8_1;
+    for (int32_t c = 0; c < ncols; ++c)
+        for (int64_t i = 0; i < nb; ++i)
+            quantize_block(x + c * K + i * QK8_1, y + (c * nb + i) * Q81_BYTES);
+}
+
+/* Canonical sum of squares: 256 threads; thread t accumulates x[t + 256 i]
+ * with fmaf in increasing i; each 32-lane warp reduces with an xor butterfly
+ * (masks 16, 8, 4, 2, 1); the eight warp sums are added in warp order. */
+static float canonical_sumsq(const float *x, int64_t K) {
+    float lane[256];
+    for (int t = 0; t < 256; ++t) {
+        float acc = 0.0f;
+        for (int64_t i = t; i < K; i += 256) acc = fmaf(x[i], x[i], acc);
+        lane[t] = acc;
+    }
+    float warp[8];
+    for (int w = 0; w < 8; ++w) {
+        float v[32], tmp[32];
+        for (int l = 0; l < 32; ++l) v[l] = lane[w * 32 + l];
+        for (int m = 16; m >= 1; m >>= 1) {
+            for (int l = 0; l < 32; ++l) tmp[l] = v[l] + v[l ^ m];
+            memcpy(v, tmp, sizeof v);
+        }
+        warp[w] = v[0];
+    }
+    float total = warp[0];
+    for (int w = 1; w < 8; ++w) total = total + warp[w];
+    return total;
+}
+
+float orc_rms_scale(const float *x, float eps, int64_t K) {
+    const float mean = canonical_sumsq(x, K) / (float)K;
+    return 1.0f / sqrtf(mean + eps);
+}
+
+void orc_rmsnorm_quantize_q8_1(const float *x, const float *w, float eps, uint8_t *y,
+                               float *xn_out, int64_t K, int32_t ncols) {
+    float *tmp = (float *)malloc((size_t)K * sizeof(float));
+    for (int32_t c = 0; c < ncols; ++c) {
+        const float *xc = x + c * K;
+        const float r = orc_rms_scale(xc, eps, K);
+        for (int64_t i = 0; i < K; ++i) tmp[i] = (xc[i] * r) * w[i];
+        if (xn_out) memcpy(xn_out + c * K, tmp, (size_t)K * sizeof(float));
+        orc_quantize_q8_1(tmp, y + c * (K / QK8_1) * Q81_BYTES, K, 1);
+    }
+    free(tmp);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Q4_K helpers                                                             */
+/* ------------------------------------------------------------------------ */
+/* 6-bit scale and min of sub-block j (tests/q4k_q8_test.cu:44-52). */
+static inline void scale_min(const uint8_t *q, int j, int *sc, int *m) {
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+static inline float half_at(const uint8_t *p) {
+    uint16_t h;
+    memcpy(&h, p, 2);
+    return orc_f16_to_f32(h);
+}
+
+/* Exact int32 partials of one superblock against one column's 8 Q8_1 blocks.
+ * Sub-block 2p uses the low nibbles of qs[32p..32p+31], sub-block 2p+1 the
+ * high nibbles of the same bytes (tests/q4k_q8_test.cu:76-102). */
+static inline void sb_partials(const uint8_t *blk, const uint8_t *xb, int32_t P[8],
+                               int32_t M[8]) {
+    const uint8_t *qs = blk + 16;
+    for (int p = 0; p < 4; ++p) {
+        const int8_t *q8lo = (const int8_t *)(xb + (2 * p) * Q81_BYTES + 4);
+        const int8_t *q8hi = (const int8_t *)(xb + (2 * p + 1) * Q81_BYTES + 4);
+        int32_t plo = 0, phi = 0, mlo = 0, mhi = 0;
+        for (int l = 0; l < 32; ++l) {
+            const int byte = qs[32 * p + l];
+            plo += (byte & 0xF) * q8lo[l];
+            phi += (byte >> 4) * q8hi[l];
+            mlo += q8lo[l];
+            mhi += q8hi[l];
+        }
+        P[2 * p] = plo;
+        P[2 * p + 1] = phi;
+        M[2 * p] = mlo;
+        M[2 * p + 1] = mhi;
+    }
+}
+
+/* Canonical fp32 value of one superblock (the order the kernels follow):
+ *   t_s = d8_s * float(P_s * sc_s)      u_s = (d8_s * float(M_s)) * float(m_s)
+ *   tp_p = t_2p + t_2p+1                 up_p = u_2p + u_2p+1
+ *   Sd = (tp_0 + tp_1) + (tp_2 + tp_3)   Sm likewise
+ *   value = fmaf(d, Sd, -(dmin * Sm))
+ * d8_s*float(M_s) and P_s*sc_s are exact, so each t_s/u_s rounds once. */
+static inline float sb_value(const uint8_t *blk, const uint8_t *xb, const int32_t P[8],
+                             const int32_t M[8]) {
+    const float d = half_at(blk), dmin = half_at(blk + 2);
+    float tp[4], up[4];
+    for (int p = 0; p < 4; ++p) {
+        float t[2], u[2];
+        for (int i = 0; i < 2; ++i) {
+            const int s = 2 * p + i;
+            int sc, m;
+            scale_min(blk + 4, s, &sc, &m);
+            const float d8 = half_at(xb + s * Q81_BYTES);
+            t[i] = d8 * (float)(P[s] * sc);
+            const float A = d8 * (float)M[s];
+            u[i] = A * (float)m;
+        }
+        tp[p] = t[0] + t[1];
+        up[p] = u[0] + u[1];
+    }
+    const float Sd = (tp[0] + tp[1]) + (tp[2] + tp[3]);
+    const float Sm = (up[0] + up[1]) + (up[2] + up[3]);
+    return fmaf(d, Sd, -(dmin * Sm));
+}
+
+void orc_slice_starts(int32_t nsb, int32_t *start9) {
+    start9[0] = 0;
+    for (int i = 0; i < 8; ++i) start9[i + 1] = start9[i] + nsb / 8 + (i < nsb % 8 ? 1 : 0);
+}
+
+static inline float tree8(const float v[8]) {
+    return ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+}
+
+/* Slice sums of one row against one column: sequential within a slice,
+ * +0.0f for an empty slice. */
+static void row_slices(const uint8_t *wrow, const uint8_t *xcol, int32_t nsb,
+                       const int32_t start9[9], float v[8]) {
+    for (int i = 0; i < 8; ++i) {
+        float acc = 0.0f;
+        for (int b = start9[i]; b < start9[i + 1]; ++b) {
+            int32_t P[8], M[8];
+            const uint8_t *blk = wrow + (int64_t)b * Q4K_BYTES;
+            const uint8_t *xb = xcol + (int64_t)b * 8 * Q81_BYTES;
+            sb_partials(blk, xb, P, M);
+            const float c = sb_value(blk, xb, P, M);
+            acc = (b == start9[i]) ? c : acc + c;
+        }
+        v[i] = acc;
+    }
+}
+
+void orc_q4k_partials(const uint8_t *w, const uint8_t *xq, int32_t *P, int32_t *M,
+                      int64_t N, int64_t K, int32_t ncols) {
+    const int64_t nsb = K / QK_K;
+    for (int32_t c = 0; c < ncols; ++c) {
+        const uint8_t *xcol = xq + (int64_t)c * (K / QK8_1) * Q81_BYTES;
+        for (int64_t r = 0; r < N; ++r)
+            for (int64_t b = 0; b < nsb; ++b) {
+                int32_t p8[8], m8[8];
+                sb_partials(w + (r * nsb + b) * Q4K_BYTES, xcol + b * 8 * Q81_BYTES, p8, m8);
+                memcpy(P + ((c * N + r) * nsb + b) * 8, p8, sizeof p8);
+                if (r == 0) memcpy(M + (c * nsb + b) * 8, m8, sizeof m8);
+            }
+    }
+}
+
+void orc_q4k_gemv(const uint8_t *w, const uint8_t *xq, float *y, int64_t N, int64_t K,
+                  int32_t ncols, int32_t nthreads) {
+    const int32_t nsb = (int32_t)(K / QK_K);
+    int32_t start9[9];
+    orc_slice_starts(nsb, start9);
+    if (nthreads < 1) nthreads = 1;
+#pragma omp parallel for num_threads(nthreads) schedule(static)
+    for (int64_t r = 0; r < N; ++r) {
+        for (int32_t c = 0; c < ncols; ++c) {
+            float v[8];
+            row_slices(w + r * nsb * Q4K_BYTES, xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, nsb,
+                       start9, v);
+            y[(int64_t)c * N + r] = tree8(v);
+        }
+    }
+}
+
+void orc_q4k_gemv_slices(const uint8_t *w, const uint8_t *xq, float *v, int64_t N,
+                         int64_t K, int32_t ncols) {
+    const int32_t nsb = (int32_t)(K / QK_K);
+    int32_t start9[9];
+    orc_slice_starts(nsb, start9);
+    for (int32_t c = 0; c < ncols; ++c)
+        for (int64_t r = 0; r < N; ++r)
+            row_slices(w + r * nsb * Q4K_BYTES, xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, nsb,
+                       start9, v + ((int64_t)c * N + r) * 8);
+}
+
+/* Independent f64 oracle, restating tests/q4k_q8_test.cu:54-107. */
+void orc_q4k_gemv_f64(const uint8_t *w, const uint8_t *xq, double *y, int64_t N,
+                      int64_t K, int32_t ncols) {
+    const int64_t nsb = K / QK_K;
+    for (int32_t c = 0; c < ncols; ++c) {
+        const uint8_t *xcol = xq + (int64_t)c * (K / QK8_1) * Q81_BYTES;
+        for (int64_t r = 0; r < N; ++r) {
+            double acc = 0.0;
+            for (int64_t b = 0; b < nsb; ++b) {
+                const uint8_t *blk = w + (r * nsb + b) * Q4K_BYTES;
+                const double d = half_at(blk), dmin = half_at(blk + 2);
+                for (int p = 0; p < 4; ++p) {
+                    int sc0, m0, sc1, m1;
+                    scale_min(blk + 4, 2 * p, &sc0, &m0);
+                    scale_min(blk + 4, 2 * p + 1, &sc1, &m1);
+                    const uint8_t *x0 = xcol + (b * 8 + 2 * p) * Q81_BYTES;
+                    const uint8_t *x1 = xcol + (b * 8 + 2 * p + 1) * Q81_BYTES;
+                    const double d80 = half_at(x0), d81 = half_at(x1);
+                    for (int l = 0; l < 32; ++l) {
+                        const int byte = blk[16 + 32 * p + l];
+                        const double w0 = d * sc0 * (byte & 0xF) - dmin * m0;
+                        const double w1 = d * sc1 * (byte >> 4) - dmin * m1;
+                        acc += w0 * (d80 * ((const int8_t *)(x0 + 4))[l]) +
+                               w1 * (d81 * ((const int8_t *)(x1 + 4))[l]);
+                    }
+                }
+            }
+            y[(int64_t)c * N + r] = acc;
+        }
+    }
+}
+
+void orc_q4k_absdot_f64(const uint8_t *w, const uint8_t *xq, double *s, int64_t N,
+                        int64_t K, int32_t ncols) {
+    const int64_t nsb = K / QK_K;
+    for (int32_t c = 0; c < ncols; ++c) {
+        const uint8_t *xcol = xq + (int64_t)c * (K / QK8_1) * Q81_BYTES;
+        for (int64_t r = 0; r < N; ++r) {
+            double acc = 0.0;
+            for (int64_t b = 0; b < nsb; ++b) {
+                const uint8_t *blk = w + (r * nsb + b) * Q4K_BYTES;
+                const double d = half_at(blk), dmin = half_at(blk + 2);
+                for (int p = 0; p < 4; ++p)
+                    for (int i = 0; i < 2; ++i) {
+                        int sc, m;
+                        scale_min(blk + 4, 2 * p + i, &sc, &m);
+                        const uint8_t *xb = xcol + (b * 8 + 2 * p + i) * Q81_BYTES;
+                        const double d8 = half_at(xb);
+                        for (int l = 0; l < 32; ++l) {
+                            const int byte = blk[16 + 32 * p + l];
+                            const int q = i ? (byte >> 4) : (byte & 0xF);
+                            acc += fabs(d * sc * q - dmin * m) *
+                                   fabs(d8 * ((const int8_t *)(xb + 4))[l]);
+                        }
+                    }
+            }
+            s[(int64_t)c * N + r] = acc;
+        }
+    }
+}
+
+void orc_dequant_q4k(const uint8_t *w, float *out, int64_t nblocks) {
+    for (int64_t i = 0; i < nblocks; ++i) {
+        const uint8_t *blk = w + i * Q4K_BYTES;
+        const float d = half_at(blk), dmin = half_at(blk + 2);
+        for (int p = 0; p < 4; ++p)
+            for (int h = 0; h < 2; ++h) {
+                int sc, m;
+                scale_min(blk + 4, 2 * p + h, &sc, &m);
+                const float a = d * (float)sc;
+                const float bm = dmin * (float)m;
+                for (int l = 0; l < 32; ++l) {
+                    const int byte = blk[16 + 32 * p + l];
+                    const int q = h ? (byte >> 4) : (byte & 0xF);
+                    out[i * QK_K + 64 * p + 32 * h + l] = fmaf(a, (float)q, -bm);
+                }
+            }
+    }
+}
+
+int32_t orc_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
