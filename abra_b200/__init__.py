@@ -31,6 +31,7 @@ from .q4k import (
     load_tuning_table,
     mmvq,
     mmvq_partials,
+    mmvq_swiglu,
     q4k_nbytes,
     q8_1_nbytes,
     register_autotuned_table_entry,

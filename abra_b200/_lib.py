@@ -28,6 +28,7 @@ SIGNATURES: dict[str, tuple] = {
     "abra_q4k_mmvq": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _vp]),
     "abra_q4k_mmvq_candidate": (C.c_int, [_i32, _vp, _vp, _fp, _i64, _i64, _i32, _vp]),
     "abra_q4k_mmvq_ex": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _i32, _vp]),
+    "abra_q4k_mmvq_swiglu": (C.c_int, [_vp, _vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _i32, _vp]),
     "abra_q4k_mmvq_partials": (C.c_int, [_vp, _vp, _fp, _vp, _vp, _i64, _i64, _i32, _i32, _vp]),
     "launch_pinned_upstream_mmvq": (None, [_vp, _vp, _fp, _i64, _i64, _vp]),
     "abra_quantize_q8_1": (C.c_int, [_fp, _vp, _i64, _i32, _vp]),
@@ -36,9 +37,9 @@ SIGNATURES: dict[str, tuple] = {
     "abra_gen_q4k": (C.c_int, [_vp, _i64, _u64, _u64, _i64, _vp]),
     "abra_gen_uniform_f32": (C.c_int, [_fp, _i64, _u64, _u64, _i64, _f32, _f32, _vp]),
     "abra_candidate_count": (C.c_int, []),
-    "abra_candidate_info": (C.c_int, [_i32] + [C.POINTER(C.c_int32)] * 5),
-    "abra_tune_set": (C.c_int, [_i64, _i64, _i32, _i32]),
-    "abra_tune_get": (C.c_int, [_i64, _i64, _i32]),
+    "abra_candidate_info": (C.c_int, [_i32] + [C.POINTER(C.c_int32)] * 6),
+    "abra_tune_set": (C.c_int, [_i64, _i64, _i32, _i32, _i32]),
+    "abra_tune_get": (C.c_int, [_i64, _i64, _i32, _i32]),
     "abra_tune_clear": (C.c_int, []),
 }
 
@@ -54,7 +55,7 @@ class AbraError(RuntimeError):
 def _load() -> C.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m abra_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python abra_b200/build.py` "
             "(there is no CPU fallback)")
     lib = C.CDLL(str(LIB_PATH))
     for name, (res, args) in SIGNATURES.items():

@@ -4,7 +4,7 @@ Each ``csrc/*.cu`` is compiled to an object in ``abra_b200/_build/`` (in
 parallel), then linked into ``abra_b200/libabra_b200.so`` with the static CUDA
 runtime.  NCCL is not linked: collectives go through torch.distributed.
 
-    python -m abra_b200.build [--force] [--verbose]
+    python abra_b200/build.py [--force] [--verbose]
 """
 from __future__ import annotations
 

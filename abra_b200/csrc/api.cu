@@ -5,6 +5,7 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <vector>
 
 #include "../../include/abra_b200.h"
 #include "common.cuh"
@@ -29,16 +30,17 @@ int cuda_fail(cudaError_t e, const char *what) {
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 std::mutex g_tune_mu;
-std::map<std::tuple<int64_t, int64_t, int>, int> g_tune;
+std::map<std::tuple<int64_t, int64_t, int, int>, int> g_tune;
 
 // Default when the table has no entry: more k-parts for few rows or long K.
-int default_candidate(int64_t N, int64_t K, int ncols) {
+int default_candidate(int64_t N, int64_t K, int ncols, int nmat) {
+    (void)nmat;
     const int64_t rg = (N + 7) / 8;
     const int64_t nsb = K / 256;
-    if (rg < 148) return nsb >= 16 ? 802 : 404;
-    if (rg < 4 * 148) return nsb >= 16 ? 402 : 202;
     (void)ncols;
-    return nsb >= 24 ? 202 : 102;
+    if (rg < 148) return nsb >= 16 ? 3082 : 3042;
+    if (rg < 4 * 148) return nsb >= 16 ? 3042 : 3022;
+    return nsb >= 24 ? 3022 : 3012;
 }
 
 int check_mmvq_args(const void *w, const void *x, const float *y, int64_t N, int64_t K,
@@ -56,6 +58,24 @@ int check_mmvq_args(const void *w, const void *x, const float *y, int64_t N, int
 
 }  // namespace
 
+namespace abra {
+static std::vector<ErrorWordFn> &error_words() {
+    static std::vector<ErrorWordFn> v;
+    return v;
+}
+int register_error_word(ErrorWordFn fn) {
+    error_words().push_back(fn);
+    return 1;
+}
+cudaError_t read_error_words(unsigned *value, bool clear) {
+    for (ErrorWordFn fn : error_words()) {
+        cudaError_t e = fn(value, clear);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+}  // namespace abra
+
 extern "C" {
 
 const char *abra_version(void) { return "abra_b200 0.1.0 sm_100a"; }
@@ -65,27 +85,40 @@ int abra_device_error(uint32_t *out, int32_t clear) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
     unsigned v = 0;
-    e = abra::error_word_gen_quant(&v, clear != 0);
-    if (e == cudaSuccess) e = abra::error_word_mmvq(&v, clear != 0);
+    e = abra::read_error_words(&v, clear != 0);
     if (e != cudaSuccess) return cuda_fail(e, "device error word");
     if (out) *out = v;
+    return ABRA_OK;
+}
+
+static int mmvq_common(const void *w, const void *w2, const void *x, float *y, int64_t N,
+                       int64_t K, int32_t ncols, int64_t ldy, int32_t candidate, int32_t flags,
+                       void *stream) {
+    int rc = check_mmvq_args(w, x, y, N, K, ncols, ldy);
+    if (rc) return rc;
+    if (w2 && !aligned16(w2)) return fail(ABRA_E_INVALID, "weights must be 16-byte aligned");
+    int id = candidate;
+    if (id == 0) id = abra_tune_get(N, K, ncols, w2 ? 2 : 1);
+    const abra::MmvqConfig *cfg = abra::mmvq_candidate_by_id(id);
+    if (!cfg) return fail(ABRA_E_INVALID, "unknown candidate id %d", id);
+    cudaError_t e = abra::launch_mmvq_q4k(*cfg, w, w2, x, y, N, K, ncols, ldy,
+                                          (flags & ABRA_MMVQ_PDL) ? abra::MMVQ_PDL : 0,
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "mmvq launch");
     return ABRA_OK;
 }
 
 int abra_q4k_mmvq_ex(const void *w, const void *x, float *y, int64_t N, int64_t K,
                      int32_t ncols, int64_t ldy, int32_t candidate, int32_t flags,
                      void *stream) {
-    int rc = check_mmvq_args(w, x, y, N, K, ncols, ldy);
-    if (rc) return rc;
-    int id = candidate;
-    if (id == 0) id = abra_tune_get(N, K, ncols);
-    const abra::MmvqConfig *cfg = abra::mmvq_candidate_by_id(id);
-    if (!cfg) return fail(ABRA_E_INVALID, "unknown candidate id %d", id);
-    cudaError_t e = abra::launch_mmvq_q4k(*cfg, w, x, y, N, K, ncols, ldy,
-                                          (flags & ABRA_MMVQ_PDL) ? abra::MMVQ_PDL : 0,
-                                          static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) return cuda_fail(e, "mmvq launch");
-    return ABRA_OK;
+    return mmvq_common(w, nullptr, x, y, N, K, ncols, ldy, candidate, flags, stream);
+}
+
+int abra_q4k_mmvq_swiglu(const void *w_gate, const void *w_up, const void *x, float *y,
+                         int64_t N, int64_t K, int32_t ncols, int64_t ldy, int32_t candidate,
+                         int32_t flags, void *stream) {
+    if (!w_up) return fail(ABRA_E_INVALID, "null pointer");
+    return mmvq_common(w_gate, w_up, x, y, N, K, ncols, ldy, candidate, flags, stream);
 }
 
 int abra_q4k_mmvq(const void *w, const void *x, float *y, int64_t N, int64_t K, int32_t ncols,
@@ -171,33 +204,35 @@ int abra_candidate_count(void) {
     return n;
 }
 
-int abra_candidate_info(int32_t index, int32_t *id, int32_t *ks, int32_t *ncw,
+int abra_candidate_info(int32_t index, int32_t *id, int32_t *mode, int32_t *ks, int32_t *ncw,
                         int32_t *ctas_per_sm, int32_t *stage_kb) {
     int n = 0;
     const abra::MmvqConfig *c = abra::mmvq_candidates(&n);
     if (index < 0 || index >= n) return fail(ABRA_E_INVALID, "candidate index %d out of range", index);
     if (id) *id = c[index].id;
+    if (mode) *mode = c[index].mode;
     if (ks) *ks = c[index].ks;
-    if (ncw) *ncw = c[index].ncw;
+    if (ncw) *ncw = 8;
     if (ctas_per_sm) *ctas_per_sm = c[index].ctas_per_sm;
     if (stage_kb) *stage_kb = c[index].stage_kb;
     return ABRA_OK;
 }
 
-int abra_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t candidate) {
+int abra_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t nmat, int32_t candidate) {
     if (!abra::mmvq_candidate_by_id(candidate)) return fail(ABRA_E_INVALID, "unknown candidate id %d", candidate);
+    if (nmat != 1 && nmat != 2) return fail(ABRA_E_INVALID, "nmat must be 1 or 2");
     std::lock_guard<std::mutex> lock(g_tune_mu);
-    g_tune[std::make_tuple(N, K, static_cast<int>(ncols))] = candidate;
+    g_tune[std::make_tuple(N, K, static_cast<int>(ncols), static_cast<int>(nmat))] = candidate;
     return ABRA_OK;
 }
 
-int abra_tune_get(int64_t N, int64_t K, int32_t ncols) {
+int abra_tune_get(int64_t N, int64_t K, int32_t ncols, int32_t nmat) {
     {
         std::lock_guard<std::mutex> lock(g_tune_mu);
-        auto it = g_tune.find(std::make_tuple(N, K, static_cast<int>(ncols)));
+        auto it = g_tune.find(std::make_tuple(N, K, static_cast<int>(ncols), static_cast<int>(nmat)));
         if (it != g_tune.end()) return it->second;
     }
-    return default_candidate(N, K, ncols);
+    return default_candidate(N, K, ncols, nmat);
 }
 
 int abra_tune_clear(void) {

@@ -34,12 +34,19 @@ static_assert(sizeof(block_q8_1) == Q81_BYTES, "block_q8_1 must be 36 bytes");
 
 // Error bits written by kernels into the device error word.
 enum : unsigned {
-    ERR_WAIT_TIMEOUT = 1u << 0,  // an mbarrier wait exceeded its iteration limit
-    ERR_FLAG_TIMEOUT = 1u << 1,  // a cross-rank flag wait exceeded its limit
+    ERR_WAIT_TIMEOUT = 1u << 0,  // a consumer's wait for staged data gave up
+    ERR_FLAG_TIMEOUT = 1u << 1,  // a cross-rank flag wait gave up
+    ERR_WAIT_EMPTY = 1u << 2,    // a producer's wait for a free stage gave up
 };
 
-// Upper bound of try_wait polls before a wait gives up and reports.
-constexpr uint32_t WAIT_LIMIT = 1u << 24;
+// Wall-clock bound of every spin-wait in these kernels (nanoseconds).
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 // Each translation unit has its own error word (internal linkage, so no
 // relocatable device code is needed); ABRA_ERROR_WORD_ACCESSOR defines the
@@ -82,11 +89,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: returns false (and reports) if the phase never completed.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+// Bounded wait: returns false (and reports `err`) if the phase did not
+// complete within WAIT_LIMIT_NS of wall time.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          unsigned err = ERR_WAIT_TIMEOUT) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-    report_error(ERR_WAIT_TIMEOUT);
+        if ((i & 63u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) break;
+    }
+    report_error(err);
     return false;
 }
 // Bulk (non-tensor) async copy global -> this CTA's shared memory.  Both
@@ -162,6 +175,39 @@ __host__ __device__ __forceinline__ int slice_start(int nsb, int i) {
     return i * q + (i < r ? i : r);
 }
 
+// ---------------------------------------------------------------- exp ---
+// Cody & Waite range reduction x = k ln2 + r (ln2 split into a 16-bit head
+// and a tail), e^r by the degree-7 Taylor polynomial in Horner form, then
+// scaling by 2^k.  Every step is one IEEE fp32 operation, mirrored operation
+// for operation by the CPU oracle (orc_expf), so both return the same bits.
+__device__ __forceinline__ float pow2i(int k) { return __int_as_float((k + 127) << 23); }
+
+__device__ __forceinline__ float abra_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.75f) return __int_as_float(0x7f800000);
+    if (x < -104.0f) return 0.0f;
+    const float kf = rintf(__fmul_rn(x, 0x1.715476p+0f));
+    float r = __fmaf_rn(kf, -0x1.62e400p-1f, x);
+    r = __fmaf_rn(kf, -0x1.7f7d1cp-20f, r);
+    float p = 0x1.a01a02p-13f;
+    p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
+    p = __fmaf_rn(p, r, 0x1.111112p-7f);
+    p = __fmaf_rn(p, r, 0x1.555556p-5f);
+    p = __fmaf_rn(p, r, 0x1.555556p-3f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int k = static_cast<int>(kf);
+    if (k > 127) return __fmul_rn(__fmul_rn(p, pow2i(127)), pow2i(k - 127));
+    if (k < -126) return __fmul_rn(__fmul_rn(p, pow2i(k + 64)), pow2i(-64));
+    return __fmul_rn(p, pow2i(k));
+}
+
+// silu(g) = g / (1 + exp(-g)), the formula of ggml's silu.
+__device__ __forceinline__ float abra_silu(float g) {
+    return __fdiv_rn(g, __fadd_rn(1.0f, abra_expf(-g)));
+}
+
 // ---------------------------------------------------------- generator ---
 __host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
@@ -180,6 +226,12 @@ __device__ __forceinline__ float unit24(uint64_t bits24) {
 
 }  // namespace abra
 
+namespace abra {
+using ErrorWordFn = cudaError_t (*)(unsigned *value, bool clear);
+// Host-side registry of the per-translation-unit error words (api.cu).
+int register_error_word(ErrorWordFn fn);
+}  // namespace abra
+
 #define ABRA_ERROR_WORD_ACCESSOR(fname)                                              \
     namespace abra {                                                                 \
     cudaError_t fname(unsigned *value, bool clear) {                                 \
@@ -194,4 +246,5 @@ __device__ __forceinline__ float unit24(uint64_t bits24) {
         *value |= v;                                                                 \
         return cudaSuccess;                                                          \
     }                                                                                \
+    static const int fname##_registered = register_error_word(fname);               \
     }

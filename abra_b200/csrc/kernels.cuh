@@ -10,10 +10,10 @@ namespace abra {
 // One tuning candidate of the Q4_K x Q8_1 MMVQ family.
 struct MmvqConfig {
     int id;           // stable candidate id (used in tuning tables)
+    int mode;         // MmvqMode: 0 TMA per-row copies, 1 TMA whole unit, 2 direct loads
     int ks;           // k-parts per row group (1, 2, 4, 8): warps sharing a row group
-    int ncw;          // consumer warps per CTA (4 or 8)
     int ctas_per_sm;  // grid = min(row groups, SMs * ctas_per_sm)
-    int stage_kb;     // shared-memory budget for the weight ring, KiB
+    int stage_kb;     // shared-memory budget for the weight ring, KiB (TMA modes)
 };
 
 const MmvqConfig *mmvq_candidates(int *count);
@@ -24,9 +24,10 @@ enum : int {
     MMVQ_PDL = 1,  // launch with programmatic dependent launch (weights must be immutable)
 };
 
-cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *x_q8, float *y,
-                            int64_t N, int64_t K, int ncols, int64_t ldy, int flags,
-                            cudaStream_t stream);
+// w2 != nullptr selects the fused gate/up form: y = (w2 x) * silu(w x).
+cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2,
+                            const void *x_q8, float *y, int64_t N, int64_t K, int ncols,
+                            int64_t ldy, int flags, cudaStream_t stream);
 // Debug: same kernel, additionally storing the exact int32 partials
 // P[c][r][b][s] and M[c][b][s].
 cudaError_t launch_mmvq_q4k_partials(const void *w, const void *x_q8, float *y, int32_t *P,
@@ -49,8 +50,7 @@ cudaError_t launch_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_
 
 int device_sm_count();
 
-// Per-translation-unit device error words (see common.cuh).
-cudaError_t error_word_gen_quant(unsigned *value, bool clear);
-cudaError_t error_word_mmvq(unsigned *value, bool clear);
+// Reads (and optionally clears) every translation unit's device error word.
+cudaError_t read_error_words(unsigned *value, bool clear);
 
 }  // namespace abra

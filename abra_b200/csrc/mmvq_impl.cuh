@@ -1,0 +1,458 @@
+// mmvq_impl.cuh -- the Q4_K x Q8_1 MMVQ kernel template (sm_100a).
+//
+// Computes y[c][r] = sum_k w[r][k] * x[c][k] for Q4_K rows w and Q8_1
+// activation columns x -- the operation of the reference's
+// vec_dot_q4_K_q8_1 / mul_mat_vec_q family (kernels/q4k/q4k_vecdot.cuh:23-87,
+// kernels/q4k/q4k_family.cu:12-90) -- and, with NMAT == 2, the fused gate/up
+// form y = (W_up x) * silu(W_gate x) of the reference's GATE kernel
+// (kernels/q4k/abra-mmvq.cuh:118-143,175-186).
+//
+// Work unit: 8 rows x one k-part (KS k-parts per row).  Three ways to feed it:
+//   MODE_TMA_ROWS   a producer warp fetches each unit with one cp.async.bulk per
+//                   row into a ring of shared-memory stages (mbarrier-guarded);
+//                   the row pitch is padded to an odd number of 16-byte chunks so
+//                   eight rows' 128-bit loads hit eight distinct bank groups;
+//   MODE_TMA_WHOLE  same ring, one bulk copy per unit (8 consecutive rows are
+//                   contiguous in HBM when KS == 1), unpadded pitch;
+//   MODE_DIRECT     no producer: consumer lanes load their superblock bytes
+//                   with 128-bit ld.global.nc, one superblock ahead.
+// No copy uses cluster multicast.
+//
+// Consumer lane (p = lane/8, g = lane%8) owns row g of the unit and nibble
+// pair p (sub-blocks 2p, 2p+1): two exact int32 sub-block dot products by
+// dp4a (the high nibbles as unsigned bytes masked in place, 16x the product).
+// The eight lanes of a quarter warp share p, so activation loads broadcast.
+//
+// Canonical fp32 order (shared with the CPU oracle, bit for bit):
+//   t_s = d8_s * float(P_s * sc_s),  u_s = (d8_s * float(M_s)) * float(m_s)
+//   S   = ((t_0 + t_1) + (t_2 + t_3)) + ((t_4 + t_5) + (t_6 + t_7))  [xor 8, 16]
+//   value(superblock) = fmaf(d, S_d, -(dmin * S_m))
+//   eight canonical K-slices, sequential within a slice, then a fixed tree;
+// k-parts are subtrees of that tree, so every candidate gives the same bits,
+// and so does any split of K across GPUs along slice boundaries.
+#pragma once
+
+#include "common.cuh"
+
+namespace abra {
+
+enum MmvqMode : int { MODE_TMA_ROWS = 0, MODE_TMA_WHOLE = 1, MODE_DIRECT = 2 };
+
+struct MmvqParams {
+    const uint8_t *W[2];  // matrix 0 (gate when NMAT == 2), matrix 1 (up)
+    const uint8_t *X;     // Q8_1 columns
+    float *Y;
+    int N, nsb;
+    int64_t ldy;
+    int rg_total, nstage, pitch;
+    int32_t *P, *M;  // debug partials (EMIT_P)
+};
+
+__host__ __device__ __forceinline__ int align_up(int v, int a) { return (v + a - 1) / a * a; }
+
+struct MmvqLayout {
+    int off_full, off_empty, off_red, off_qs, off_d8, off_A, off_stage, bytes;
+};
+
+__host__ __device__ __forceinline__ MmvqLayout mmvq_layout(int ncols, int ks, int ncw, int nsb,
+                                                           int nstage, int pitch, int nmat,
+                                                           bool staged) {
+    MmvqLayout L;
+    L.off_full = 0;
+    L.off_empty = 8 * nstage;
+    int o = staged ? 16 * nstage : 0;
+    L.off_red = align_up(o, 16);
+    o = L.off_red + (ks > 1 ? 2 * ncw * 8 * ncols * nmat * 4 : 0);
+    L.off_qs = align_up(o, 128);
+    o = L.off_qs + ncols * nsb * 256;
+    L.off_d8 = align_up(o, 16);
+    o = L.off_d8 + ncols * nsb * 8 * 4;
+    L.off_A = o;
+    o += ncols * nsb * 8 * 4;
+    L.off_stage = align_up(o, 128);
+    L.bytes = L.off_stage + (staged ? nstage * 8 * nmat * pitch : 0);
+    return L;
+}
+
+// Weight side of one superblock for lane pair p: scales, mins, nibbles.
+struct SbWeights {
+    float d, dmin, fm0, fm1;
+    int sc0, sc1;
+    uint32_t lo[8], hi[8];
+};
+
+struct SbRaw {
+    uint4 hdr, qa, qb;
+};
+
+__device__ __forceinline__ void fetch_sb_smem(const uint8_t *sbp, int p, SbRaw &r) {
+    r.hdr = *reinterpret_cast<const uint4 *>(sbp);
+    r.qa = *reinterpret_cast<const uint4 *>(sbp + 16 + 32 * p);
+    r.qb = *reinterpret_cast<const uint4 *>(sbp + 32 + 32 * p);
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void fetch_sb_global(const uint8_t *sbp, int p, SbRaw &r) {
+    r.hdr = ldg_nc_v4(sbp);
+    r.qa = ldg_nc_v4(sbp + 16 + 32 * p);
+    r.qb = ldg_nc_v4(sbp + 32 + 32 * p);
+}
+
+__device__ __forceinline__ void decode_sb(const SbRaw &r, int p, SbWeights &w) {
+    int m0, m1;
+    scale_min_pair(r.hdr.y, r.hdr.z, r.hdr.w, p, w.sc0, m0, w.sc1, m1);
+    w.d = half_lo(r.hdr.x);
+    w.dmin = half_hi(r.hdr.x);
+    w.fm0 = static_cast<float>(m0);
+    w.fm1 = static_cast<float>(m1);
+    const uint32_t qw[8] = {r.qa.x, r.qa.y, r.qa.z, r.qa.w, r.qb.x, r.qb.y, r.qb.z, r.qb.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        w.lo[k] = qw[k] & 0x0F0F0F0Fu;
+        w.hi[k] = qw[k] & 0xF0F0F0F0u;
+    }
+}
+
+// Values of one superblock for every column and each of NMAT matrices that
+// share the activation; aq/ad8/aA point at the staged activation.
+template <int NCOLS, int NMAT>
+__device__ __forceinline__ void sb_values(const SbWeights (&w)[NMAT], int p, const uint8_t *aq,
+                                          const float *ad8, const float *aA, int nsb, int b,
+                                          float (&v)[NMAT][NCOLS], int (&P0)[NCOLS],
+                                          int (&P1)[NCOLS]) {
+#pragma unroll
+    for (int c = 0; c < NCOLS; ++c) {
+        const uint4 *a = reinterpret_cast<const uint4 *>(aq + (c * nsb + b) * 256 + 64 * p);
+        const uint4 a0 = a[0], a1 = a[1], a2 = a[2], a3 = a[3];
+        const float2 d8 = *reinterpret_cast<const float2 *>(ad8 + (c * nsb + b) * 8 + 2 * p);
+        const float2 A = *reinterpret_cast<const float2 *>(aA + (c * nsb + b) * 8 + 2 * p);
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            const uint32_t *lo = w[m].lo, *hi = w[m].hi;
+            int s0 = 0, s1 = 0;
+            s0 = dp4a_ss(lo[0], a0.x, s0);
+            s0 = dp4a_ss(lo[1], a0.y, s0);
+            s0 = dp4a_ss(lo[2], a0.z, s0);
+            s0 = dp4a_ss(lo[3], a0.w, s0);
+            s0 = dp4a_ss(lo[4], a1.x, s0);
+            s0 = dp4a_ss(lo[5], a1.y, s0);
+            s0 = dp4a_ss(lo[6], a1.z, s0);
+            s0 = dp4a_ss(lo[7], a1.w, s0);
+            s1 = dp4a_us(hi[0], a2.x, s1);
+            s1 = dp4a_us(hi[1], a2.y, s1);
+            s1 = dp4a_us(hi[2], a2.z, s1);
+            s1 = dp4a_us(hi[3], a2.w, s1);
+            s1 = dp4a_us(hi[4], a3.x, s1);
+            s1 = dp4a_us(hi[5], a3.y, s1);
+            s1 = dp4a_us(hi[6], a3.z, s1);
+            s1 = dp4a_us(hi[7], a3.w, s1);
+            s1 >>= 4;  // exact: the masked high nibbles carry a factor of 16
+            if (m == 0) {
+                P0[c] = s0;
+                P1[c] = s1;
+            }
+            const float t0 = __fmul_rn(d8.x, __int2float_rn(s0 * w[m].sc0));
+            const float t1 = __fmul_rn(d8.y, __int2float_rn(s1 * w[m].sc1));
+            float tp = __fadd_rn(t0, t1);
+            float up = __fadd_rn(__fmul_rn(A.x, w[m].fm0), __fmul_rn(A.y, w[m].fm1));
+            tp = __fadd_rn(tp, __shfl_xor_sync(0xffffffffu, tp, 8));
+            up = __fadd_rn(up, __shfl_xor_sync(0xffffffffu, up, 8));
+            tp = __fadd_rn(tp, __shfl_xor_sync(0xffffffffu, tp, 16));
+            up = __fadd_rn(up, __shfl_xor_sync(0xffffffffu, up, 16));
+            v[m][c] = __fmaf_rn(w[m].d, tp, -__fmul_rn(w[m].dmin, up));
+        }
+    }
+}
+
+template <int N>
+__device__ __forceinline__ float tree_sum(const float *a) {
+    if constexpr (N == 1) {
+        return a[0];
+    } else if constexpr (N == 2) {
+        return __fadd_rn(a[0], a[1]);
+    } else if constexpr (N == 4) {
+        return __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
+    } else {
+        return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
+                         __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
+    }
+}
+
+template <int NCOLS, int KS, int NCW, int MODE, int NMAT, bool EMIT_P>
+__global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MODE == MODE_DIRECT ? 2 : 1)
+    mmvq_q4k_kernel(const MmvqParams prm) {
+    constexpr int NSL = 8 / KS;     // canonical slices per k-part
+    constexpr int NGRP = NCW / KS;  // warp groups, one row group each at a time
+    constexpr bool STAGED = MODE != MODE_DIRECT;
+    static_assert(NCW % KS == 0, "consumer warps must be a multiple of KS");
+    static_assert(MODE != MODE_TMA_WHOLE || KS == 1, "whole-unit copies need KS == 1");
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int N = prm.N, nsb = prm.nsb, nstage = prm.nstage, pitch = prm.pitch;
+    const MmvqLayout L = mmvq_layout(NCOLS, KS, NCW, nsb, nstage, pitch, NMAT, STAGED);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_full);
+    uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L.off_empty);
+    float *red = reinterpret_cast<float *>(smem + L.off_red);
+    uint8_t *aq = smem + L.off_qs;
+    float *ad8 = reinterpret_cast<float *>(smem + L.off_d8);
+    float *aA = reinterpret_cast<float *>(smem + L.off_A);
+    uint8_t *stage = smem + L.off_stage;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x;
+    const int rg_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * prm.rg_total / G);
+    const int rg_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * prm.rg_total / G);
+    const int nrg = rg_end - rg_begin;
+
+    if constexpr (STAGED) {
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < nstage; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            fence_mbar_init();
+        }
+        __syncthreads();
+    }
+    pdl_launch_dependents();
+
+    if constexpr (STAGED) {
+        if (warp == NCW) {
+            // ------------------------------------------------ producer ---
+            const uint64_t pol = policy_evict_first();
+            const int U = nrg * KS;
+            for (int u = 0; u < U; ++u) {
+                const int s = u % nstage, k = u / nstage;
+                if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1, ERR_WAIT_EMPTY)) break;
+                const int rg = rg_begin + u / KS, j = u % KS;
+                const int sb_lo = slice_start(nsb, j * NSL), sb_hi = slice_start(nsb, (j + 1) * NSL);
+                const uint32_t part_bytes = static_cast<uint32_t>(sb_hi - sb_lo) * Q4K_BYTES;
+                const int row0 = rg * 8;
+                const int nvalid = min(8, N - row0);
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], NMAT * nvalid * part_bytes);
+                __syncwarp();
+                if (part_bytes > 0) {
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) {
+                        uint8_t *dst = stage + (s * NMAT + m) * 8 * pitch;
+                        if constexpr (MODE == MODE_TMA_WHOLE) {
+                            if (lane == 0)
+                                bulk_g2s(dst, prm.W[m] + static_cast<int64_t>(row0) * nsb * Q4K_BYTES,
+                                         nvalid * part_bytes, &full[s], pol);
+                        } else {
+                            if (lane < nvalid)
+                                bulk_g2s(dst + lane * pitch,
+                                         prm.W[m] + (static_cast<int64_t>(row0 + lane) * nsb + sb_lo) *
+                                                        Q4K_BYTES,
+                                         part_bytes, &full[s], pol);
+                        }
+                    }
+                }
+            }
+            return;
+        }
+    }
+
+    // -------------------------------------------------------- consumers ---
+    pdl_wait();  // x is produced by the preceding kernel
+    const int nblk = nsb * 8;
+    for (int i = threadIdx.x; i < NCOLS * nblk; i += NCW * 32) {
+        const int c = i / nblk, blk = i - c * nblk;
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(
+            prm.X + (static_cast<int64_t>(c) * nblk + blk) * Q81_BYTES);
+        const uint32_t h = __ldg(src);
+        uint32_t q[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) q[k] = __ldg(src + 1 + k);
+        uint4 *dst = reinterpret_cast<uint4 *>(aq + static_cast<int64_t>(i) * 32);
+        dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+        dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+        int msum = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) msum = dp4a_ss(0x01010101, static_cast<int>(q[k]), msum);
+        const float d8 = half_lo(h);
+        ad8[i] = d8;
+        aA[i] = __fmul_rn(d8, __int2float_rn(msum));  // exact: 11 x 12 bits
+        if constexpr (EMIT_P) {
+            if (blockIdx.x == 0) prm.M[i] = msum;
+        }
+    }
+    named_bar_sync(1, NCW * 32);
+
+    const int grp = warp / KS, j = warp % KS;
+    const int p = lane >> 3, g = lane & 7;
+    const int sb_part = slice_start(nsb, j * NSL);
+    const int sb_part_end = slice_start(nsb, (j + 1) * NSL);
+    bool poisoned = false;
+    int round = 0;
+    for (int r = grp; r < nrg; r += NGRP, ++round) {
+        const int u = r * KS + j;
+        const int s = u % nstage, k = u / nstage;
+        const int row = (rg_begin + r) * 8 + g;
+        const uint8_t *base[NMAT];
+        if constexpr (STAGED) {
+            if (!poisoned && !mbar_wait(&full[s], k & 1)) poisoned = true;
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) base[m] = stage + ((s * NMAT + m) * 8 + g) * pitch;
+        } else {
+            const int64_t rr = row < N ? row : N - 1;  // clamp: a tail lane reads a valid row
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) base[m] = prm.W[m] + (rr * nsb + sb_part) * Q4K_BYTES;
+        }
+        float acc[NMAT][NCOLS][NSL];
+        SbRaw nxt[NMAT];
+        if constexpr (!STAGED) {
+            if (sb_part < sb_part_end) {
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) fetch_sb_global(base[m], p, nxt[m]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < NSL; ++i) {
+            const int b0 = slice_start(nsb, j * NSL + i), b1 = slice_start(nsb, j * NSL + i + 1);
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                for (int c = 0; c < NCOLS; ++c) acc[m][c][i] = 0.0f;
+            for (int b = b0; b < b1; ++b) {
+                SbWeights w[NMAT];
+                if constexpr (STAGED) {
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) {
+                        SbRaw raw;
+                        fetch_sb_smem(base[m] + (b - sb_part) * Q4K_BYTES, p, raw);
+                        decode_sb(raw, p, w[m]);
+                    }
+                } else {
+                    SbRaw cur[NMAT];
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) cur[m] = nxt[m];
+                    if (b + 1 < sb_part_end) {
+#pragma unroll
+                        for (int m = 0; m < NMAT; ++m)
+                            fetch_sb_global(base[m] + (b + 1 - sb_part) * Q4K_BYTES, p, nxt[m]);
+                    }
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) decode_sb(cur[m], p, w[m]);
+                }
+                float v[NMAT][NCOLS];
+                int P0[NCOLS], P1[NCOLS];
+                sb_values<NCOLS, NMAT>(w, p, aq, ad8, aA, nsb, b, v, P0, P1);
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int c = 0; c < NCOLS; ++c)
+                        acc[m][c][i] = (b == b0) ? v[m][c] : __fadd_rn(acc[m][c][i], v[m][c]);
+                if constexpr (EMIT_P) {
+                    if (row < N) {
+#pragma unroll
+                        for (int c = 0; c < NCOLS; ++c) {
+                            int32_t *dst = prm.P + ((static_cast<int64_t>(c) * N + row) * nsb + b) * 8 + 2 * p;
+                            dst[0] = P0[c];
+                            dst[1] = P1[c];
+                        }
+                    }
+                }
+            }
+        }
+        if constexpr (STAGED) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        float sub[NMAT][NCOLS];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int c = 0; c < NCOLS; ++c) sub[m][c] = tree_sum<NSL>(acc[m][c]);
+        if constexpr (KS > 1) {
+            float *slot = red + ((round & 1) * NCW + warp) * 8 * NCOLS * NMAT;
+            if (p == 0) {
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int c = 0; c < NCOLS; ++c) slot[(g * NMAT + m) * NCOLS + c] = sub[m][c];
+            }
+            named_bar_sync(2 + grp, KS * 32);
+            if (j == 0 && p == 0) {
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int c = 0; c < NCOLS; ++c) {
+                        float parts[KS];
+#pragma unroll
+                        for (int jj = 0; jj < KS; ++jj)
+                            parts[jj] = red[((round & 1) * NCW + grp * KS + jj) * 8 * NCOLS * NMAT +
+                                            (g * NMAT + m) * NCOLS + c];
+                        sub[m][c] = tree_sum<KS>(parts);
+                    }
+            }
+        }
+        if (j == 0 && p == 0 && row < N) {
+#pragma unroll
+            for (int c = 0; c < NCOLS; ++c) {
+                float yv = sub[0][c];
+                if constexpr (NMAT == 2) yv = __fmul_rn(sub[1][c], abra_silu(sub[0][c]));
+                prm.Y[c * prm.ldy + row] = yv;
+            }
+        }
+    }
+}
+
+using MmvqFn = void (*)(const MmvqParams);
+
+// Kernel table for one batch width: index [mode][ks index][nmat-1].
+// ks index: 0 -> 1, 1 -> 2, 2 -> 4, 3 -> 8.
+struct MmvqTable {
+    MmvqFn fn[3][4][2];
+    MmvqFn partials[3];  // MODE_TMA_ROWS, NMAT 1, KS 1/2/4, EMIT_P
+};
+
+#define ABRA_MMVQ_NCW 8
+
+template <int NC>
+MmvqTable make_mmvq_table() {
+    MmvqTable t = {};
+    constexpr int W = ABRA_MMVQ_NCW;
+    t.fn[MODE_TMA_ROWS][0][0] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_ROWS, 1, false>;
+    t.fn[MODE_TMA_ROWS][1][0] = mmvq_q4k_kernel<NC, 2, W, MODE_TMA_ROWS, 1, false>;
+    t.fn[MODE_TMA_ROWS][2][0] = mmvq_q4k_kernel<NC, 4, W, MODE_TMA_ROWS, 1, false>;
+    t.fn[MODE_TMA_ROWS][3][0] = mmvq_q4k_kernel<NC, 8, W, MODE_TMA_ROWS, 1, false>;
+    t.fn[MODE_TMA_ROWS][0][1] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_ROWS, 2, false>;
+    t.fn[MODE_TMA_ROWS][1][1] = mmvq_q4k_kernel<NC, 2, W, MODE_TMA_ROWS, 2, false>;
+    t.fn[MODE_TMA_ROWS][2][1] = mmvq_q4k_kernel<NC, 4, W, MODE_TMA_ROWS, 2, false>;
+    t.fn[MODE_TMA_ROWS][3][1] = mmvq_q4k_kernel<NC, 8, W, MODE_TMA_ROWS, 2, false>;
+    t.fn[MODE_TMA_WHOLE][0][0] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_WHOLE, 1, false>;
+    t.fn[MODE_TMA_WHOLE][0][1] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_WHOLE, 2, false>;
+    t.fn[MODE_DIRECT][0][0] = mmvq_q4k_kernel<NC, 1, W, MODE_DIRECT, 1, false>;
+    t.fn[MODE_DIRECT][1][0] = mmvq_q4k_kernel<NC, 2, W, MODE_DIRECT, 1, false>;
+    t.fn[MODE_DIRECT][2][0] = mmvq_q4k_kernel<NC, 4, W, MODE_DIRECT, 1, false>;
+    t.fn[MODE_DIRECT][3][0] = mmvq_q4k_kernel<NC, 8, W, MODE_DIRECT, 1, false>;
+    t.fn[MODE_DIRECT][0][1] = mmvq_q4k_kernel<NC, 1, W, MODE_DIRECT, 2, false>;
+    t.fn[MODE_DIRECT][1][1] = mmvq_q4k_kernel<NC, 2, W, MODE_DIRECT, 2, false>;
+    t.fn[MODE_DIRECT][2][1] = mmvq_q4k_kernel<NC, 4, W, MODE_DIRECT, 2, false>;
+    t.fn[MODE_DIRECT][3][1] = mmvq_q4k_kernel<NC, 8, W, MODE_DIRECT, 2, false>;
+    if constexpr (NC == 1 || NC == 2 || NC == 4 || NC == 8) {
+        t.partials[0] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_ROWS, 1, true>;
+        t.partials[1] = mmvq_q4k_kernel<NC, 2, W, MODE_TMA_ROWS, 1, true>;
+        t.partials[2] = mmvq_q4k_kernel<NC, 4, W, MODE_TMA_ROWS, 1, true>;
+    }
+    return t;
+}
+
+// Defined in mmvq_c<N>.cu, one translation unit per batch width.
+const MmvqTable &mmvq_table_c1();
+const MmvqTable &mmvq_table_c2();
+const MmvqTable &mmvq_table_c3();
+const MmvqTable &mmvq_table_c4();
+const MmvqTable &mmvq_table_c5();
+const MmvqTable &mmvq_table_c6();
+const MmvqTable &mmvq_table_c7();
+const MmvqTable &mmvq_table_c8();
+
+}  // namespace abra

@@ -67,10 +67,14 @@ def q8_1_nbytes(K: int, ncols: int = 1) -> int:
 
 
 # ----------------------------------------------------------- candidates ---
+MODE_NAMES = {0: "TMAROWS", 1: "TMAWHOLE", 2: "DIRECT"}
+
+
 @dataclass(frozen=True)
 class Q4KCandidateSpec:
     id: int
     name: str
+    mode: int        # 0 TMA per-row bulk copies, 1 TMA whole unit, 2 direct loads
     ks: int          # k-parts per row group (warps sharing 8 rows)
     ncw: int         # consumer warps per CTA
     ctas_per_sm: int
@@ -78,16 +82,17 @@ class Q4KCandidateSpec:
 
     @property
     def threads_per_block(self) -> int:
-        return (self.ncw + 1) * 32
+        return (self.ncw + (0 if self.mode == 2 else 1)) * 32
 
 
 def _enumerate() -> dict[int, Q4KCandidateSpec]:
     out = {}
     for i in range(lib.abra_candidate_count()):
-        vals = [C.c_int32() for _ in range(5)]
+        vals = [C.c_int32() for _ in range(6)]
         call("abra_candidate_info", i, *[C.byref(v) for v in vals])
-        cid, ks, ncw, cps, skb = (v.value for v in vals)
-        out[cid] = Q4KCandidateSpec(cid, f"Q4K_SM100_KS{ks}_W{ncw}_C{cps}", ks, ncw, cps, skb)
+        cid, mode, ks, ncw, cps, skb = (v.value for v in vals)
+        out[cid] = Q4KCandidateSpec(cid, f"Q4K_SM100_{MODE_NAMES[mode]}_KS{ks}_C{cps}", mode, ks,
+                                    ncw, cps, skb)
     return out
 
 
@@ -112,15 +117,15 @@ def get_candidate_name(cid: int) -> str:
 
 # ------------------------------------------------------------ tuning ------
 def register_autotuned_table_entry(N: int, K: int, arch: int, winning_candidate: int,
-                                   ncols: int = 1) -> None:
+                                   ncols: int = 1, nmat: int = 1) -> None:
     if arch != ARCH_SM100:
         raise ValueError(f"only arch {ARCH_SM100} is tuned here (got {arch})")
-    call("abra_tune_set", N, K, ncols, winning_candidate)
+    call("abra_tune_set", N, K, ncols, nmat, winning_candidate)
 
 
 def get_autotuned_candidate_for_shape(N: int, K: int, arch: int = ARCH_SM100,
-                                      ncols: int = 1) -> int:
-    return int(lib.abra_tune_get(N, K, ncols))
+                                      ncols: int = 1, nmat: int = 1) -> int:
+    return int(lib.abra_tune_get(N, K, ncols, nmat))
 
 
 def load_tuning_table(path: Path | str = TUNING_FILE) -> int:
@@ -132,7 +137,7 @@ def load_tuning_table(path: Path | str = TUNING_FILE) -> int:
     n = 0
     for e in data.get("entries", []):
         call("abra_tune_set", int(e["N"]), int(e["K"]), int(e.get("ncols", 1)),
-             int(e["candidate"]))
+             int(e.get("nmat", 1)), int(e["candidate"]))
         n += 1
     return n
 
@@ -164,6 +169,16 @@ def mmvq(d_w, d_x, d_y, N: int, K: int, ncols: int = 1, ldy: int | None = None,
     """y[c*ldy + r] = sum_k W[r,k] x[c,k] (full form of the C ABI)."""
     _check_k(K)
     call("abra_q4k_mmvq_ex", ptr(d_w), ptr(d_x), ptr(d_y), N, K, ncols,
+         N if ldy is None else ldy, candidate, _lib.ABRA_MMVQ_PDL if pdl else 0,
+         stream_handle(stream))
+
+
+def mmvq_swiglu(d_w_gate, d_w_up, d_x, d_y, N: int, K: int, ncols: int = 1,
+                ldy: int | None = None, candidate: int = 0, pdl: bool = False,
+                stream=None) -> None:
+    """y = (W_up x) * silu(W_gate x), one pass over the shared activation."""
+    _check_k(K)
+    call("abra_q4k_mmvq_swiglu", ptr(d_w_gate), ptr(d_w_up), ptr(d_x), ptr(d_y), N, K, ncols,
          N if ldy is None else ldy, candidate, _lib.ABRA_MMVQ_PDL if pdl else 0,
          stream_handle(stream))
 

@@ -1,0 +1,168 @@
+"""Autotuner for the sm_100a MMVQ family.
+
+For every (N, K, ncols, nmat) in the shape list it times every candidate of
+the family as one CUDA graph of back-to-back launches (programmatic
+dependent launch on) over enough distinct weight copies that their total is
+at least 4 x L2 (at least 4 copies), keeps the best of a few replays, and
+writes the winners -- with every candidate's time -- to
+``abra_b200/tuning/sm100.json``, which ``abra_b200`` loads at import.
+
+This replaces the reference's offline tuner (tools/run-m4-autotune.py,
+synthesize_tuning_table at :168-240) and its hand-copied table
+(kernels/q4k/q4k_family.cu:378-397).  Ties within 0.5 % go to the lower
+candidate id, mirroring the reference's tie-break rule (:200-206).
+
+    python -m abra_b200.tune [--ncols 1 8] [--out PATH] [--quick]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+from . import _lib
+from .q4k import TUNING_FILE, get_all_candidate_ids, get_candidate_spec, stream_handle
+
+L2_BYTES = 126 * 1024 * 1024
+
+# Qwen3-4B decode shapes: q, k/v, o, gate/up, down, output, fused q|k|v;
+# nmat 2 = fused gate/up SwiGLU (9728 x 2560 each).
+DECODE_SHAPES = [
+    (4096, 2560, 1), (1024, 2560, 1), (2560, 4096, 1), (9728, 2560, 1), (2560, 9728, 1),
+    (151936, 2560, 1), (6144, 2560, 1), (9728, 2560, 2),
+]
+
+
+def q4k_bytes(N: int, K: int) -> int:
+    return N * (K // 256) * 144
+
+
+def time_candidate(torch, plan, ncols, nmat, cid, reps=3, failures=None):
+    from .q4k import device_error
+
+    f_mm = _lib.lib.abra_q4k_mmvq_ex
+    f_sw = _lib.lib.abra_q4k_mmvq_swiglu
+
+    def run(items=plan):
+        st = stream_handle(None)
+        for w, w2, x, y, N, K in items:
+            if nmat == 1:
+                rc = f_mm(w, x, y, N, K, ncols, N, cid, _lib.ABRA_MMVQ_PDL, st)
+            else:
+                rc = f_sw(w, w2, x, y, N, K, ncols, N, cid, _lib.ABRA_MMVQ_PDL, st)
+            if rc:
+                return rc
+        return 0
+
+    # one launch, then two back to back, each checked before anything longer runs
+    for items in (plan[:1], plan[:2], plan):
+        rc = run(items)
+        torch.cuda.synchronize()
+        err = device_error(clear=True)
+        if rc or err:
+            if failures is not None and err:
+                failures.append({"candidate": cid, "device_error": err, "launches": len(items)})
+            return None
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run()
+    best = float("inf")
+    for _ in range(reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e) * 1e3 / len(plan))
+    del g
+    return best
+
+
+def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None) -> dict:
+    import torch
+
+    import abra_b200 as A
+
+    dev = torch.device("cuda:0")
+    ids = ids or get_all_candidate_ids()
+    entries = []
+    failures = []
+    for (N, K, nmat) in shapes:
+        per = q4k_bytes(N, K) * nmat
+        copies = max(4, -(-4 * L2_BYTES // per))
+        if quick:
+            copies = max(2, copies // 4)
+        nb = N * K // 256
+        bufs = []
+        for i in range(copies * nmat):
+            t = torch.empty(nb * 144, dtype=torch.uint8, device=dev)
+            A.gen_q4k(t, nb, 0, 7000 + i)
+            bufs.append(t)
+        for ncols in ncols_list:
+            x = torch.from_numpy(np.random.default_rng(K).standard_normal(ncols * K, dtype=np.float32)).to(dev)
+            xq = torch.empty(ncols * (K // 32) * 36, dtype=torch.uint8, device=dev)
+            A.launch_quantize_f32_to_q8_1(x, xq, K, ncols=ncols)
+            y = torch.empty(ncols * N, dtype=torch.float32, device=dev)
+            plan = []
+            for i in range(copies):
+                w = bufs[i * nmat].data_ptr()
+                w2 = bufs[i * nmat + 1].data_ptr() if nmat == 2 else 0
+                plan.append((w, w2, xq.data_ptr(), y.data_ptr(), N, K))
+            times = {}
+            for cid in ids:
+                nf = len(failures)
+                us = time_candidate(torch, plan, ncols, nmat, cid, failures=failures)
+                if len(failures) > nf:
+                    failures[-1].update({"N": N, "K": K, "ncols": ncols, "nmat": nmat})
+                    print(json.dumps({"failure": failures[-1]}), flush=True)
+                if us is not None:
+                    times[cid] = us
+            assert times, f"no candidate ran for {(N, K, ncols, nmat)}"
+            fastest = min(times.values())
+            winner = min(c for c, t in times.items() if t <= fastest * 1.005)
+            nbytes = per + ncols * (K // 32) * 36 + ncols * N * 4
+            e = {"N": N, "K": K, "ncols": ncols, "nmat": nmat, "candidate": winner,
+                 "name": get_candidate_spec(winner).name, "us": round(times[winner], 3),
+                 "GBps": round(nbytes / (times[winner] * 1e-6) / 1e9, 1), "copies": copies,
+                 "all_us": {str(c): round(t, 3) for c, t in sorted(times.items())}}
+            entries.append(e)
+            print(json.dumps({k: e[k] for k in ("N", "K", "ncols", "nmat", "name", "us", "GBps")}),
+                  flush=True)
+        del bufs
+        torch.cuda.empty_cache()
+    data = {"arch": 100, "device": torch.cuda.get_device_name(0),
+            "when": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime()),
+            "method": "CUDA graph of back-to-back launches over >= 4 x L2 of weight copies, "
+                      "PDL on, best of 3 replays; ties within 0.5% to the lower id",
+            "entries": entries, "failures": failures}
+    out.parent.mkdir(parents=True, exist_ok=True)
+    out.write_text(json.dumps(data, indent=1) + "\n")
+    return data
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--ncols", type=int, nargs="+", default=[1, 8])
+    ap.add_argument("--out", default=str(TUNING_FILE))
+    ap.add_argument("--quick", action="store_true", help="fewer weight copies")
+    ap.add_argument("--shape", type=int, nargs=3, action="append", metavar=("N", "K", "NMAT"),
+                    help="tune only these shapes (repeatable)")
+    ap.add_argument("--ids", type=int, nargs="+", help="only these candidate ids")
+    a = ap.parse_args(argv)
+    shapes = [tuple(s) for s in a.shape] if a.shape else DECODE_SHAPES
+    tune(shapes, a.ncols, Path(a.out), a.quick, a.ids)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

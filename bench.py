@@ -1,19 +1,25 @@
 #!/usr/bin/env python
 """Benchmark of the Q4_K x Q8_1 MMVQ path on B200.
 
-Workload ("qwen3_4b_decode_gemv_sweep"): one step is one pass of MMVQ over
-every Qwen3-4B-shaped decode matrix of the model -- per layer q 4096x2560,
-k and v 1024x2560, o 2560x4096, gate and up 9728x2560, down 2560x9728, for
-36 layers, then the tied 151936x2560 output -- at batch 1 (``--batch``),
-all Q4_K with d, dmin ~ U(0.001, 0.02), 6-bit scales/mins ~ U{0..63},
-nibbles ~ U{0..15}, activations N(0,1) quantized to Q8_1 (seed 0).  That is
-2,262,528,000 bytes of weights per step, larger than L2, so every launch
-reads HBM.  The metric is algorithmic bytes / time in GB/s (weights +
-Q8_1 activations + fp32 outputs, the reference's formula,
-bench/micro/q4k_q8_bench.cu:330-333), aggregated over ranks.
+Workload ("qwen3_4b_decode_weight_sweep"): one step is one pass of MMVQ over
+the full Qwen3-4B-shaped decode weight set, in the operators a decode step
+runs: per layer the fused q|k|v projection (6144 x 2560), o (2560 x 4096),
+the fused gate/up SwiGLU (2 x 9728 x 2560) and down (2560 x 9728), for 36
+layers, then the tied 151936 x 2560 output -- 145 launches, 2,262,528,000
+bytes of Q4_K weights (d, dmin ~ U(0.001, 0.02), 6-bit scales/mins
+~ U{0..63}, nibbles ~ U{0..15}; activations N(0,1) quantized to Q8_1; seed
+0), at batch 1 (``--batch``).  The weights exceed L2, so every launch reads
+HBM.  The metric is algorithmic bytes / time in GB/s (weights + Q8_1
+activations + fp32 outputs, the reference's formula,
+bench/micro/q4k_q8_bench.cu:330-333), aggregated over ranks (each rank runs
+the full set on its own GPU: weak scaling, no collective).
 
-``--impl reference`` times the CPU restatement of the reference's
-vec_dot_q4_K_q8_1 (oracle/, OpenMP on all host cores) on a bounded sample of
+Also reported: every config-1 shape separately (q, k, v, o, gate, up, down,
+output), the reference's own kernel family on the same GPU over the
+unfused sweep, the sweep end to end through the C ABI with host buffers,
+and the CPU restatement of vec_dot_q4_K_q8_1 (oracle/, all host cores).
+
+``--impl reference`` times that CPU restatement alone on a bounded sample of
 the same workload; the reference's ggml CPU path is not available.
 
 Run: python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
@@ -36,10 +42,15 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 LAYERS = 36
-LAYER_SHAPES = [("q", 4096, 2560), ("k", 1024, 2560), ("v", 1024, 2560), ("o", 2560, 4096),
-                ("gate", 9728, 2560), ("up", 9728, 2560), ("down", 2560, 9728)]
-OUTPUT_SHAPE = ("output", 151936, 2560)
-WORKLOAD = "qwen3_4b_decode_gemv_sweep"
+# (name, N, K, nmat): nmat 2 = fused gate/up SwiGLU over two N x K matrices
+LAYER_OPS = [("qkv", 6144, 2560, 1), ("o", 2560, 4096, 1), ("gate_up", 9728, 2560, 2),
+             ("down", 2560, 9728, 1)]
+OUTPUT_OP = ("output", 151936, 2560, 1)
+# config 1: every decode matrix separately
+CONFIG1_SHAPES = [("q", 4096, 2560), ("k", 1024, 2560), ("v", 1024, 2560), ("o", 2560, 4096),
+                  ("gate", 9728, 2560), ("up", 9728, 2560), ("down", 2560, 9728),
+                  ("output", 151936, 2560)]
+WORKLOAD = "qwen3_4b_decode_weight_sweep"
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -47,18 +58,18 @@ def q4k_bytes(N, K):
     return N * (K // 256) * 144
 
 
-def alg_bytes(N, K, B):
+def alg_bytes(N, K, B, nmat=1):
     """Reference formula: Q4_K weights + Q8_1 activations + fp32 outputs."""
-    return q4k_bytes(N, K) + B * (K // 32) * 36 + B * N * 4
+    return nmat * q4k_bytes(N, K) + B * (K // 32) * 36 + B * N * 4
 
 
-def sweep_shapes():
-    out = []
+def sweep_ops():
+    ops = []
     for layer in range(LAYERS):
-        for i, (name, N, K) in enumerate(LAYER_SHAPES):
-            out.append((f"{name}.{layer}", N, K, layer * 16 + i + 1))
-    out.append((OUTPUT_SHAPE[0], OUTPUT_SHAPE[1], OUTPUT_SHAPE[2], 1))
-    return out
+        for i, (name, N, K, nmat) in enumerate(LAYER_OPS):
+            ops.append((f"{name}.{layer}", N, K, nmat, layer * 16 + 2 * i + 1))
+    ops.append((OUTPUT_OP[0], OUTPUT_OP[1], OUTPUT_OP[2], 1, 1))
+    return ops
 
 
 def measured_peaks():
@@ -168,17 +179,16 @@ class Dist:
 # --------------------------------------------------------------- CPU arm ---
 def cpu_sample_rate(batch: int, budget_s: float, seed: int = 0):
     """CPU restatement of vec_dot_q4_K_q8_1 (OpenMP, all host cores) on a
-    sample of the workload: the first 512 rows of every layer-0 matrix and of
-    the output, repeated until ``budget_s`` seconds elapse.  Returns GB/s by
-    the same byte formula."""
+    sample of the workload: the first 512 rows of every config-1 matrix,
+    repeated until ``budget_s`` seconds elapse.  Returns GB/s by the same
+    byte formula."""
     import oracle as O
 
     threads = os.cpu_count() or 1
     rows = 512
     sample = []
-    for i, (name, N, K) in enumerate(LAYER_SHAPES + [OUTPUT_SHAPE]):
-        tid = i + 1 if name != "output" else 1
-        w = O.gen_q4k(min(rows, N), K, seed, tid)
+    for i, (name, N, K) in enumerate(CONFIG1_SHAPES):
+        w = O.gen_q4k(min(rows, N), K, seed, i + 1)
         xq = O.quantize_q8_1(O.gen_normal_f32((batch, K), seed + 1000 + K))
         sample.append((w, xq, min(rows, N), K))
     nbytes = sum(alg_bytes(n, k, batch) for _, _, n, k in sample)
@@ -192,11 +202,29 @@ def cpu_sample_rate(batch: int, budget_s: float, seed: int = 0):
         el = time.perf_counter() - t0
         if el >= budget_s:
             break
-    gbs = reps * nbytes / el / 1e9
-    return gbs, threads, reps, el
+    return reps * nbytes / el / 1e9, threads, reps, el
 
 
 # --------------------------------------------------------------- GPU arm ---
+def launch_ops(plan, ncols: int, pdl: bool, stream=None):
+    """Launch (w, w2, x, y, N, K, nmat) MMVQs through the C ABI with the least
+    host overhead: the stream is resolved once, the symbols are pre-bound."""
+    from abra_b200 import _lib
+    from abra_b200.q4k import stream_handle
+
+    f1 = _lib.lib.abra_q4k_mmvq_ex
+    f2 = _lib.lib.abra_q4k_mmvq_swiglu
+    st = stream_handle(stream)
+    flags = _lib.ABRA_MMVQ_PDL if pdl else 0
+    for w, w2, x, y, N, K, nmat in plan:
+        if nmat == 1:
+            rc = f1(w, x, y, N, K, ncols, N, 0, flags, st)
+        else:
+            rc = f2(w, w2, x, y, N, K, ncols, N, 0, flags, st)
+        if rc:
+            _lib.check(rc, "abra_q4k_mmvq")
+
+
 class Sweep:
     def __init__(self, dev, batch: int, seed: int = 0):
         import torch
@@ -204,35 +232,55 @@ class Sweep:
         import abra_b200 as A
         import oracle as O
 
-        self.A = A
-        self.torch = torch
-        self.dev = dev
-        self.B = batch
-        self.shapes = sweep_shapes()
+        self.A, self.torch, self.dev, self.B = A, torch, dev, batch
+        self.ops = sweep_ops()
         self.w = {}
-        for name, N, K, tid in self.shapes:
+        for name, N, K, nmat, tid in self.ops:
             nb = N * K // 256
-            buf = torch.empty(nb * 144, dtype=torch.uint8, device=dev)
-            A.gen_q4k(buf, nb, seed, tid)
-            self.w[name] = buf
-        self.Ks = sorted({K for _, _, K, _ in self.shapes})
-        self.x = {K: O.gen_normal_f32((batch, K), seed + 1000 + K) for K in self.Ks}
+            bufs = []
+            for m in range(nmat):
+                buf = torch.empty(nb * 144, dtype=torch.uint8, device=dev)
+                A.gen_q4k(buf, nb, seed, tid + m)
+                bufs.append(buf)
+            self.w[name] = bufs
+        self.Ks = sorted({K for _, _, K, _, _ in self.ops})
         self.xq = {}
         for K in self.Ks:
+            x = O.gen_normal_f32((batch, K), seed + 1000 + K)
             xq = torch.empty(batch * (K // 32) * 36, dtype=torch.uint8, device=dev)
-            A.launch_quantize_f32_to_q8_1(torch.from_numpy(self.x[K].reshape(-1)).to(dev), xq, K,
+            A.launch_quantize_f32_to_q8_1(torch.from_numpy(x.reshape(-1)).to(dev), xq, K,
                                           ncols=batch)
             self.xq[K] = xq
-        maxn = max(N for _, N, _, _ in self.shapes)
+        maxn = max(N for _, N, _, _, _ in self.ops)
         self.y = torch.empty(batch * maxn, dtype=torch.float32, device=dev)
-        self.bytes = sum(alg_bytes(N, K, batch) for _, N, K, _ in self.shapes)
-        self.launches = len(self.shapes)
+        self.bytes = sum(alg_bytes(N, K, batch, nmat) for _, N, K, nmat, _ in self.ops)
+        self.weight_bytes = sum(nmat * q4k_bytes(N, K) for _, N, K, nmat, _ in self.ops)
+        self.launches = len(self.ops)
+        self.plan = []
+        for name, N, K, nmat, _ in self.ops:
+            b = self.w[name]
+            self.plan.append((b[0].data_ptr(), b[1].data_ptr() if nmat == 2 else 0,
+                              self.xq[K].data_ptr(), self.y.data_ptr(), N, K, nmat))
         torch.cuda.synchronize()
 
     def step(self, pdl=True):
-        A, B = self.A, self.B
-        for name, N, K, _ in self.shapes:
-            A.mmvq(self.w[name], self.xq[K], self.y, N, K, ncols=B, pdl=pdl)
+        """One pass over the decode weight set, launched through the C ABI."""
+        launch_ops(self.plan, self.B, pdl)
+
+    def capture(self, fn=None):
+        """Capture ``fn`` (default: one step) into a CUDA graph."""
+        torch = self.torch
+        fn = fn or self.step
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        torch.cuda.synchronize()
+        return g
 
     def timed(self, steps: int, fn=None):
         torch = self.torch
@@ -249,97 +297,87 @@ class Sweep:
 
 class E2E:
     """The same sweep through the public API with host buffers: per step one
-    H2D copy of every activation (fp32, pinned) and one D2H copy of every
-    output; quantization on the device inside the step."""
+    H2D copy of every operator input (fp32, pinned), their quantization on
+    the device, the MMVQs, and one D2H copy of every output."""
 
     def __init__(self, sw: Sweep):
         torch = sw.torch
         self.sw = sw
         B = sw.B
-        # one activation column per distinct layer input (q/k/v share, o,
-        # gate/up share, down) plus the output's input
-        self.inputs = []
-        for layer in range(LAYERS):
-            self.inputs += [(f"attn.{layer}", 2560), (f"o.{layer}", 4096),
-                            (f"ffn.{layer}", 2560), (f"down.{layer}", 9728)]
-        self.inputs.append(("out", 2560))
-        total_x = sum(K for _, K in self.inputs) * B
+        total_x = sum(K for _, _, K, _, _ in sw.ops) * B
         self.h_x = torch.empty(total_x, dtype=torch.float32).pin_memory()
-        rng = np.random.default_rng(7)
-        self.h_x.numpy()[:] = rng.standard_normal(total_x, dtype=np.float32)
+        self.h_x.numpy()[:] = np.random.default_rng(7).standard_normal(total_x, dtype=np.float32)
         self.d_x = torch.empty(total_x, dtype=torch.float32, device=sw.dev)
-        self.off = {}
-        o = 0
-        for name, K in self.inputs:
-            self.off[name] = (o, K)
-            o += K * B
-        self.d_q = torch.empty(sum(K // 32 * 36 for _, K in self.inputs) * B, dtype=torch.uint8,
-                               device=sw.dev)
-        self.qoff = {}
-        o = 0
-        for name, K in self.inputs:
-            self.qoff[name] = o
-            o += K // 32 * 36 * B
-        total_y = sum(N for _, N, _, _ in sw.shapes) * B
+        self.d_q = torch.empty(sum(K // 32 * 36 for _, _, K, _, _ in sw.ops) * B,
+                               dtype=torch.uint8, device=sw.dev)
+        total_y = sum(N for _, N, _, _, _ in sw.ops) * B
         self.d_y = torch.empty(total_y, dtype=torch.float32, device=sw.dev)
         self.h_y = torch.empty(total_y, dtype=torch.float32).pin_memory()
-        self.h2d = total_x * 4
-        self.d2h = total_y * 4
+        self.h2d, self.d2h = total_x * 4, total_y * 4
+        xb, qb, yb = self.d_x.data_ptr(), self.d_q.data_ptr(), self.d_y.data_ptr()
+        self.qplan, self.mplan = [], []
+        xo = qo = yo = 0
+        for name, N, K, nmat, _ in sw.ops:
+            w = sw.w[name]
+            self.qplan.append((xb + xo * 4, qb + qo, K))
+            self.mplan.append((w[0].data_ptr(), w[1].data_ptr() if nmat == 2 else 0, qb + qo,
+                               yb + yo * 4, N, K, nmat))
+            xo += K * B
+            qo += K // 32 * 36 * B
+            yo += N * B
 
     def step(self):
-        sw, A, B = self.sw, self.sw.A, self.sw.B
+        from abra_b200 import _lib
+        from abra_b200.q4k import stream_handle
+
+        B = self.sw.B
+        st = stream_handle(None)
         self.d_x.copy_(self.h_x, non_blocking=True)
-        for name, K in self.inputs:
-            o, _ = self.off[name]
-            A.launch_quantize_f32_to_q8_1(self.d_x[o:o + K * B], self.d_q[self.qoff[name]:], K,
-                                          ncols=B)
-        yo = 0
-        for name, N, K, _ in sw.shapes:
-            kind, _, layer = name.partition(".")
-            src = {"q": "attn", "k": "attn", "v": "attn", "o": "o", "gate": "ffn", "up": "ffn",
-                   "down": "down"}.get(kind)
-            key = f"{src}.{layer}" if src else "out"
-            A.mmvq(sw.w[name], self.d_q[self.qoff[key]:], self.d_y[yo:], N, K, ncols=B)
-            yo += N * B
+        fq = _lib.lib.abra_quantize_q8_1
+        for x, q, K in self.qplan:
+            rc = fq(x, q, K, B, st)
+            if rc:
+                _lib.check(rc, "abra_quantize_q8_1")
+        launch_ops(self.mplan, B, pdl=False, stream=st)
         self.h_y.copy_(self.d_y, non_blocking=True)
 
 
-def per_shape_table(sw: Sweep, reps: int = 3):
-    """GB/s of each distinct shape, back-to-back over >= 4 x L2 of weight copies."""
+def shape_table(sw: Sweep, reps: int = 3):
+    """Each config-1 shape (and the fused operators) alone: one CUDA graph of
+    back-to-back launches over >= 4 x L2 (at least 8) distinct weight copies,
+    best of ``reps`` replays."""
     torch, A = sw.torch, sw.A
     out = {}
-    for name, N, K in LAYER_SHAPES + [OUTPUT_SHAPE]:
-        nb = N * K // 256
-        per = nb * 144
+    shapes = [(n, N, K, 1) for n, N, K in CONFIG1_SHAPES] + [
+        ("qkv_fused", 6144, 2560, 1), ("gate_up_swiglu", 9728, 2560, 2)]
+    for name, N, K, nmat in shapes:
+        per = nmat * q4k_bytes(N, K)
         copies = max(8, -(-4 * L2_BYTES // per))
-        bufs = [sw.w[f"{name}.{i}"] if f"{name}.{i}" in sw.w else None for i in range(LAYERS)]
-        bufs = [b for b in bufs if b is not None][:copies]
-        if name == "output":
-            bufs = [sw.w["output"]]
-        extra = []
-        while len(bufs) + len(extra) < copies:
-            t = torch.empty(per, dtype=torch.uint8, device=sw.dev)
-            A.gen_q4k(t, nb, 0, 9000 + len(extra))
-            extra.append(t)
-        allb = bufs + extra
-
-        def run():
-            for b in allb:
-                A.mmvq(b, sw.xq[K], sw.y, N, K, ncols=sw.B, pdl=True)
-
-        run()
-        ms = min(sw.timed(1, run) for _ in range(reps))
-        per_launch_us = ms * 1e3 / len(allb)
-        out[name] = {"N": N, "K": K, "us": round(per_launch_us, 3),
-                     "GBps": round(alg_bytes(N, K, sw.B) / (per_launch_us * 1e-6) / 1e9, 1),
-                     "copies": len(allb)}
-        del extra
+        nb = N * K // 256
+        bufs = []
+        for i in range(copies * nmat):
+            t = torch.empty(nb * 144, dtype=torch.uint8, device=sw.dev)
+            A.gen_q4k(t, nb, 0, 9000 + i)
+            bufs.append(t)
+        plan = [(bufs[i * nmat].data_ptr(), bufs[i * nmat + 1].data_ptr() if nmat == 2 else 0,
+                 sw.xq[K].data_ptr(), sw.y.data_ptr(), N, K, nmat) for i in range(copies)]
+        g = sw.capture(lambda: launch_ops(plan, sw.B, True))
+        ms = min(sw.timed(1, g.replay) for _ in range(reps))
+        us = ms * 1e3 / copies
+        out[name] = {"N": N, "K": K, "nmat": nmat, "us": round(us, 3),
+                     "GBps": round(alg_bytes(N, K, sw.B, nmat) / (us * 1e-6) / 1e9, 1),
+                     "copies": copies,
+                     "candidate": A.get_autotuned_candidate_for_shape(N, K, ncols=sw.B, nmat=nmat)}
+        del g, bufs, plan
+        torch.cuda.empty_cache()
     return out
 
 
 def ref_gpu_sweep(sw: Sweep, steps: int):
-    """The reference's own kernel family (oracle/_ref) on the same sweep, batch 1,
-    with the reference's dispatch rule (get_autotuned_candidate_for_shape)."""
+    """The reference's own kernel family (oracle/_ref) on the same weights,
+    unfused (q, k, v, gate, up as separate launches -- it has no fused forms),
+    batch 1, with the reference's dispatch rule
+    (get_autotuned_candidate_for_shape), captured in a CUDA graph."""
     import oracle as O
 
     try:
@@ -348,23 +386,99 @@ def ref_gpu_sweep(sw: Sweep, steps: int):
         return None
     if sw.B != 1:
         return None
-    stream = sw.torch.cuda.current_stream().cuda_stream
     plan = []
-    for name, N, K, _ in sw.shapes:
-        cid = ref.autotuned_candidate(N, K, 61)
-        if cid == 0:
-            cid = 204
-        plan.append((sw.w[name].data_ptr(), sw.xq[K].data_ptr(), N, K, cid))
+    for name, N, K, nmat, _ in sw.ops:
+        w = sw.w[name]
+        if name.startswith("qkv"):
+            base = w[0].data_ptr()
+            for rows, off in ((4096, 0), (1024, 4096), (1024, 5120)):
+                plan.append((base + off * q4k_bytes(1, K), sw.xq[K].data_ptr(), rows, K))
+        else:
+            for m in range(nmat):
+                plan.append((w[m].data_ptr(), sw.xq[K].data_ptr(), N, K))
+    plan = [(wp, xp, N, K, ref.autotuned_candidate(N, K, 61) or 204) for wp, xp, N, K in plan]
     yp = sw.y.data_ptr()
 
     def run():
-        for w, x, N, K, cid in plan:
-            ref.launch_candidate(cid, w, x, yp, N, K, stream)
+        stream = sw.torch.cuda.current_stream().cuda_stream
+        for wp, xp, N, K, cid in plan:
+            ref.launch_candidate(cid, wp, xp, yp, N, K, stream)
 
-    run()
-    ms = sw.timed(steps, run)
+    g = sw.capture(run)
+    ms = sw.timed(steps, g.replay)
     return {"GBps": round(sw.bytes / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms, 4),
+            "launches_per_step": len(plan),
             "dispatch": "reference get_autotuned_candidate_for_shape(N, K, 61)"}
+
+
+def run_case(a):
+    """Profiling case: one operator, ``--copies`` weight copies, eager launches
+    (warm-up passes then timed passes), for ncu captures."""
+    import torch
+
+    import abra_b200 as A
+    import oracle as O
+
+    table = {n: (N, K, 1) for n, N, K in CONFIG1_SHAPES}
+    table.update({"qkv": (6144, 2560, 1), "gate_up": (9728, 2560, 2)})
+    N, K, nmat = table[a.case]
+    dev = torch.device("cuda:0")
+    nb = N * K // 256
+    bufs = []
+    for i in range(a.copies * nmat):
+        t = torch.empty(nb * 144, dtype=torch.uint8, device=dev)
+        A.gen_q4k(t, nb, 0, 500 + i)
+        bufs.append(t)
+    xq = torch.empty(a.batch * (K // 32) * 36, dtype=torch.uint8, device=dev)
+    A.launch_quantize_f32_to_q8_1(
+        torch.from_numpy(O.gen_normal_f32((a.batch, K), 1).reshape(-1)).to(dev), xq, K,
+        ncols=a.batch)
+    y = torch.empty(a.batch * N, dtype=torch.float32, device=dev)
+    plan = [(bufs[i * nmat].data_ptr(), bufs[i * nmat + 1].data_ptr() if nmat == 2 else 0,
+             xq.data_ptr(), y.data_ptr(), N, K, nmat) for i in range(a.copies)]
+    for _ in range(a.warmup):
+        launch_ops(plan, a.batch, True)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(a.steps):
+        launch_ops(plan, a.batch, True)
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1e3 / (a.steps * len(plan))
+    print(json.dumps({"case": a.case, "N": N, "K": K, "nmat": nmat, "batch": a.batch,
+                      "copies": a.copies, "us_per_launch_eager": round(us, 3),
+                      "GBps_eager": round(alg_bytes(N, K, a.batch, nmat) / (us * 1e-6) / 1e9, 1),
+                      "candidate": A.get_autotuned_candidate_for_shape(N, K, ncols=a.batch,
+                                                                       nmat=nmat),
+                      "device_error": A.device_error()}), flush=True)
+    return 0
+
+
+def reference_arm(a, dist):
+    if dist.rank != 0:
+        return 0
+    for _ in range(a.warmup):
+        cpu_sample_rate(a.batch, budget_s=0.5)
+    per = max(1.0, min(20.0, 150.0 / max(1, a.steps)))
+    rates = [cpu_sample_rate(a.batch, budget_s=per) for _ in range(a.steps)]
+    gbs = statistics.median(r[0] for r in rates)
+    threads = rates[0][1]
+    line = {
+        "impl": "reference", "metric": "Q4_K GEMV HBM GB/s", "value": round(gbs, 3),
+        "unit": "GB/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u4 x s8 dot, fp32 scale", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": a.batch},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"first 512 rows of every config-1 matrix, batch {a.batch}, "
+                                   f"{per:.0f}s per step; CPU restatement of vec_dot_q4_K_q8_1 "
+                                   "(the ggml CPU path is not available)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def main():
@@ -375,61 +489,43 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU baseline work")
-    ap.add_argument("--no-extras", action="store_true", help="skip per-shape table and reference GPU family")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the per-shape table and the reference kernel family")
+    ap.add_argument("--case", choices=[n for n, _, _ in CONFIG1_SHAPES] + ["qkv", "gate_up"],
+                    help="profiling mode: one operator, eager launches")
+    ap.add_argument("--copies", type=int, default=2, help="weight copies in --case mode")
     a = ap.parse_args()
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
-    peak, peak_kind = measured_peaks()
+    if a.case:
+        return run_case(a)
     dist = Dist()
-
     if a.impl == "reference":
-        if dist.rank != 0:
-            return 0
-        rates = []
-        for _ in range(a.warmup):
-            cpu_sample_rate(a.batch, budget_s=0.5)
-        per = max(1.0, min(20.0, 150.0 / max(1, a.steps)))
-        for _ in range(a.steps):
-            rates.append(cpu_sample_rate(a.batch, budget_s=per))
-        gbs = statistics.median(r[0] for r in rates)
-        threads = rates[0][1]
-        line = {
-            "impl": "reference", "metric": "Q4_K GEMV HBM GB/s", "value": round(gbs, 3),
-            "unit": "GB/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8/u4 dot, fp32 scale", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch": a.batch},
-            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
-                             "kind": "port",
-                             "sample": f"first 512 rows of each layer-0 matrix and of the output, "
-                                       f"batch {a.batch}, {per:.0f}s per step; CPU restatement of "
-                                       "vec_dot_q4_K_q8_1 (ggml CPU path unavailable)"},
-            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0},
-        }
-        print(json.dumps(line), flush=True)
-        return 0
+        return reference_arm(a, dist)
 
     import torch
 
+    peak, peak_kind = measured_peaks()
     torch.cuda.set_device(dist.local)
     dist.init("nccl" if dist.world > 1 else "gloo")
     dev = torch.device("cuda", dist.local)
     sw = Sweep(dev, a.batch)
+    sw.step()
+    graph = sw.capture()  # one CUDA graph per step: 145 MMVQ launches
     for _ in range(a.warmup):
-        sw.step()
+        graph.replay()
     torch.cuda.synchronize()
     dist.barrier()
     with ClockSampler(dist.local) as clk:
-        ms = sw.timed(a.steps)
+        ms = sw.timed(a.steps, graph.replay)
         dist.barrier()
     clocks = clk.summary()
     ms_max = dist.max(ms)
     value = dist.world * sw.bytes / (ms_max * 1e-3) / 1e9
-    achieved = sw.bytes / (ms * 1e-3) / 1e9  # per GPU: only MMVQ launches in the step
+    achieved = sw.bytes / (ms * 1e-3) / 1e9  # per GPU; only MMVQ launches in the step
     err = sw.A.device_error()
+    del graph
 
-    # end to end through the C ABI with host buffers
     e2e = E2E(sw)
     for _ in range(3):
         e2e.step()
@@ -439,16 +535,16 @@ def main():
     extras = {}
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not a.no_extras:
-        extras["per_shape"] = per_shape_table(sw)
+        extras["per_shape"] = shape_table(sw)
         r = ref_gpu_sweep(sw, max(3, a.steps // 2))
         if r:
             extras["reference_kernels_on_b200"] = r
     if dist.rank == 0 and dist.world == 1:
         gbs, threads, reps, el = cpu_sample_rate(a.batch, a.cpu_budget)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"first 512 rows of each layer-0 matrix and of the output, batch "
-                         f"{a.batch}, {reps} reps in {el:.1f}s; CPU restatement of "
-                         "vec_dot_q4_K_q8_1 (ggml CPU path unavailable)"}
+               "sample": f"first 512 rows of every config-1 matrix, batch {a.batch}, {reps} reps "
+                         f"in {el:.1f}s; CPU restatement of vec_dot_q4_K_q8_1 (the ggml CPU "
+                         "path is not available)"}
 
     traffic = None
     tp = ROOT / "profiles" / f"traffic_{WORKLOAD}_b{a.batch}.json"
@@ -460,13 +556,13 @@ def main():
             "metric": "Q4_K GEMV HBM GB/s", "value": round(value, 1), "unit": "GB/s",
             "n_gpus": dist.world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8/u4 dot, fp32 scale", "data": "synthetic",
+            "vs_baseline": None, "dtype": "u4 x s8 dot, fp32 scale", "data": "synthetic",
             "config": {"workload": WORKLOAD, "batch": a.batch, "layers": LAYERS,
-                       "launches_per_step": sw.launches,
-                       "weight_bytes_per_step": sum(q4k_bytes(N, K) for _, N, K, _ in sw.shapes),
+                       "launches_per_step": sw.launches, "weight_bytes_per_step": sw.weight_bytes,
                        "alg_bytes_per_step": sw.bytes,
                        "l2": "inputs larger than L2 (2.26 GB of weights per step)",
-                       "parallelism": f"replica x{dist.world}"},
+                       "parallelism": f"replica x{dist.world}",
+                       "launch": "one CUDA graph per step, programmatic dependent launch"},
             "gpu_launches": sw.launches * a.steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),

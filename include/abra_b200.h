@@ -65,6 +65,14 @@ int abra_q4k_mmvq_ex(const void *w_q4k, const void *x_q8_1, float *y, int64_t N,
                      int32_t ncols, int64_t ldy, int32_t candidate, int32_t flags,
                      void *stream);
 
+/* Fused gate/up with SwiGLU, one pass over the shared activation:
+ * y = (W_up x) * silu(W_gate x), silu(g) = g / (1 + exp(-g)).  W_gate and
+ * W_up are N x K Q4_K each.  Replaces the reference's GATE kernel
+ * (kernels/q4k/abra-mmvq.cuh:118-143,175-186) with GGML_GLU_OP_SWIGLU. */
+int abra_q4k_mmvq_swiglu(const void *w_gate, const void *w_up, const void *x_q8_1, float *y,
+                         int64_t N, int64_t K, int32_t ncols, int64_t ldy, int32_t candidate,
+                         int32_t flags, void *stream);
+
 /* Debug form of the same kernel: also stores the exact int32 sub-block dot
  * products P[c][r][b][s] (ncols*N*(K/256)*8) and activation sums
  * M[c][b][s] (ncols*(K/256)*8).  ks selects the k-split (1, 2 or 4);
@@ -108,16 +116,18 @@ int abra_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_i
                          int64_t offset_index, float scale, float offset, void *stream);
 
 /* --------------------------------------------------------- autotuner --- */
-/* Candidate enumeration: index 0..abra_candidate_count()-1 -> id, k-split,
- * consumer warps, CTAs per SM, stage budget (KiB).  Replaces
+/* Candidate enumeration: index 0..abra_candidate_count()-1 -> id, feed mode
+ * (0 TMA per-row bulk copies, 1 TMA whole-unit copy, 2 direct 128-bit loads),
+ * k-split, consumer warps, CTAs per SM, stage budget (KiB).  Replaces
  * get_all_candidate_ids / get_candidate_spec (kernels/q4k/q4k_family.cuh:59-61). */
 int abra_candidate_count(void);
-int abra_candidate_info(int32_t index, int32_t *id, int32_t *ks, int32_t *ncw,
+int abra_candidate_info(int32_t index, int32_t *id, int32_t *mode, int32_t *ks, int32_t *ncw,
                         int32_t *ctas_per_sm, int32_t *stage_kb);
-/* Tuning table keyed by (N, K, ncols).  Replaces register_autotuned_table_entry /
+/* Tuning table keyed by (N, K, ncols, nmat), nmat = 1 for MMVQ and 2 for the
+ * fused gate/up form.  Replaces register_autotuned_table_entry /
  * get_autotuned_candidate_for_shape (kernels/q4k/q4k_family.cuh:86-87). */
-int abra_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t candidate);
-int abra_tune_get(int64_t N, int64_t K, int32_t ncols); /* returns candidate id */
+int abra_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t nmat, int32_t candidate);
+int abra_tune_get(int64_t N, int64_t K, int32_t ncols, int32_t nmat); /* candidate id */
 int abra_tune_clear(void);
 
 #ifdef __cplusplus

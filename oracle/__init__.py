@@ -59,6 +59,9 @@ def _load() -> C.CDLL:
         "orc_dequant_q4k": (None, [_u8p, _f32p, _i64]),
         "orc_slice_starts": (None, [_i32, _i32p]),
         "orc_max_threads": (C.c_int32, []),
+        "orc_expf": (C.c_float, [C.c_float]),
+        "orc_silu": (C.c_float, [C.c_float]),
+        "orc_swiglu": (None, [_f32p, _f32p, _f32p, _i64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -170,6 +173,23 @@ def slice_starts(nsb: int) -> np.ndarray:
     s = np.empty(9, dtype=np.int32)
     lib.orc_slice_starts(nsb, s)
     return s
+
+
+def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """up * silu(gate), elementwise, in the kernels' operation order."""
+    g = np.ascontiguousarray(gate, dtype=np.float32)
+    u = np.ascontiguousarray(up, dtype=np.float32)
+    y = np.empty_like(g)
+    lib.orc_swiglu(g.reshape(-1), u.reshape(-1), y.reshape(-1), g.size)
+    return y
+
+
+def gemv_swiglu(w_gate, w_up, xq, K: int, nthreads: int = 1) -> np.ndarray:
+    return swiglu(gemv(w_gate, xq, K, nthreads), gemv(w_up, xq, K, nthreads))
+
+
+def expf(x: float) -> float:
+    return float(lib.orc_expf(x))
 
 
 def f32_to_f16_bits(f: float) -> int:

@@ -208,6 +208,50 @@ void orc_rmsnorm_quantize_q8_1(const float *x, const float *w, float eps, uint8_
 }
 
 /* ------------------------------------------------------------------------ */
+/* exp: Cody & Waite range reduction x = k ln2 + r (ln2 split into a 16-bit  */
+/* head and a tail), e^r by the degree-7 Taylor polynomial in Horner form,   */
+/* then scaling by 2^k.  Every step is an IEEE fp32 operation (fmaf, *), so  */
+/* the CUDA copy in abra_b200/csrc/common.cuh returns the same bits.          */
+/* Error about 2 ulp against the exact exponential.                           */
+/* ------------------------------------------------------------------------ */
+static inline float pow2i(int k) { /* 2^k for -126 <= k <= 127 */
+    const uint32_t bits = (uint32_t)(k + 127) << 23;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+float orc_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.75f) return INFINITY;
+    if (x < -104.0f) return 0.0f;
+    const float kf = rintf(x * 0x1.715476p+0f);        /* x * log2(e) */
+    float r = fmaf(kf, -0x1.62e400p-1f, x);            /* - k * ln2 (head) */
+    r = fmaf(kf, -0x1.7f7d1cp-20f, r);                 /* - k * ln2 (tail) */
+    float p = 0x1.a01a02p-13f;                         /* 1/5040 */
+    p = fmaf(p, r, 0x1.6c16c2p-10f);                   /* 1/720 */
+    p = fmaf(p, r, 0x1.111112p-7f);                    /* 1/120 */
+    p = fmaf(p, r, 0x1.555556p-5f);                    /* 1/24 */
+    p = fmaf(p, r, 0x1.555556p-3f);                    /* 1/6 */
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int k = (int)kf;
+    if (k > 127) return (p * pow2i(127)) * pow2i(k - 127);
+    if (k < -126) return (p * pow2i(k + 64)) * pow2i(-64);
+    return p * pow2i(k);
+}
+
+/* silu(g) = g / (1 + exp(-g)) (ggml's ggml_cuda_op_silu_single formula). */
+float orc_silu(float g) { return g / (1.0f + orc_expf(-g)); }
+
+/* y = up * silu(gate), the GLU epilogue of the fused gate/up kernel
+ * (reference: kernels/q4k/abra-mmvq.cuh:175-186, GGML_GLU_OP_SWIGLU). */
+void orc_swiglu(const float *gate, const float *up, float *y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = up[i] * orc_silu(gate[i]);
+}
+
+/* ------------------------------------------------------------------------ */
 /* Q4_K helpers                                                             */
 /* ------------------------------------------------------------------------ */
 /* 6-bit scale and min of sub-block j (tests/q4k_q8_test.cu:44-52). */

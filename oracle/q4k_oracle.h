@@ -47,6 +47,11 @@ void orc_rmsnorm_quantize_q8_1(const float *x, const float *w, float eps, uint8_
                                float *xn_out, int64_t K, int32_t ncols);
 float orc_rms_scale(const float *x, float eps, int64_t K);
 
+/* ---- elementwise math (same op sequence as the CUDA kernels) ----------- */
+float orc_expf(float x);
+float orc_silu(float g);
+void orc_swiglu(const float *gate, const float *up, float *y, int64_t n);
+
 /* ---- MMVQ ---------------------------------------------------------------- */
 /* Exact int32 partials.  P[c][r][b][s] = sum_{l<32} q4 * q8 over sub-block s
  * of superblock b of row r against column c; M[c][b][s] = sum_{l<32} q8. */

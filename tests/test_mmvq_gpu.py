@@ -121,16 +121,92 @@ def test_qwen_shapes_tuned(dev, N, K, ncols):
     tol_check(y, O.gemv_f64(w, xq, K), O.absdot_f64(w, xq, K), TOL)
 
 
-def test_every_candidate_bit_identical(dev):
+@pytest.mark.parametrize("N,K", [(1000, 4096), (77, 9728), (2049, 2560)])
+def test_every_candidate_bit_identical(dev, N, K):
     import abra_b200 as A
 
-    N, K = 1000, 4096
     for ncols in (1, 2):
         w, _, xq = _case(N, K, ncols, seed=7)
         ref = O.gemv(w, xq, K, nthreads=8)
         for cid in A.get_all_candidate_ids():
-            y = _run(dev, w, xq, N, K, ncols, candidate=cid)
+            y = _run(dev, w, xq, N, K, ncols, candidate=cid, pdl=bool(cid % 2))
             assert np.array_equal(y, ref), f"candidate {cid} ncols={ncols} differs"
+
+
+@pytest.mark.parametrize("nmat", [1, 2])
+def test_ring_reuse_every_candidate_pdl_chain(dev, nmat):
+    """N large enough that every CTA cycles its shared-memory ring several
+    times; three back-to-back launches with programmatic dependent launch into
+    three outputs; every candidate bit-exact and no bounded wait gives up."""
+    import torch
+    import abra_b200 as A
+
+    N, K, ncols = 148 * 8 * 40, 2560, 1
+    ws = [O.gen_q4k(N, K, 2, 51 + m) for m in range(nmat)]
+    xq = O.quantize_q8_1(O.gen_normal_f32((ncols, K), 9) * (0.05 if nmat == 2 else 1.0))
+    ref = O.gemv(ws[0], xq, K, 8) if nmat == 1 else O.gemv_swiglu(ws[0], ws[1], xq, K, 8)
+    dws = [to_dev(w.reshape(-1), dev) for w in ws]
+    dx = to_dev(xq.reshape(-1), dev)
+    for cid in A.get_all_candidate_ids():
+        ys = [torch.full((N,), float("nan"), dtype=torch.float32, device=dev) for _ in range(3)]
+        for y in ys:
+            if nmat == 1:
+                A.mmvq(dws[0], dx, y, N, K, candidate=cid, pdl=True)
+            else:
+                A.mmvq_swiglu(dws[0], dws[1], dx, y, N, K, candidate=cid, pdl=True)
+        torch.cuda.synchronize()
+        assert A.device_error() == 0, f"candidate {cid}: a bounded wait gave up"
+        for y in ys:
+            assert np.array_equal(y.cpu().numpy(), ref[0]), f"candidate {cid} nmat={nmat}"
+
+
+def _run_swiglu(dev, wg, wu, xq, N, K, ncols, candidate=0):
+    import torch
+    import abra_b200 as A
+
+    dy = torch.full((ncols * N,), float("nan"), dtype=torch.float32, device=dev)
+    A.mmvq_swiglu(to_dev(wg.reshape(-1), dev), to_dev(wu.reshape(-1), dev),
+                  to_dev(xq.reshape(-1), dev), dy, N, K, ncols=ncols, candidate=candidate)
+    torch.cuda.synchronize()
+    assert A.device_error() == 0
+    return dy.cpu().numpy().reshape(ncols, N)
+
+
+@pytest.mark.parametrize("N,K,ncols", [(9728, 2560, 1), (9728, 2560, 8), (333, 4096, 3), (8, 256, 1)])
+def test_swiglu_fused_bit_exact(dev, N, K, ncols):
+    wg = O.gen_q4k(N, K, 0, 21)
+    wu = O.gen_q4k(N, K, 0, 22)
+    x = O.gen_normal_f32((ncols, K), 5) * 0.05  # keep silu away from saturation
+    xq = O.quantize_q8_1(x)
+    y = _run_swiglu(dev, wg, wu, xq, N, K, ncols)
+    ref = O.gemv_swiglu(wg, wu, xq, K, nthreads=8)
+    assert np.array_equal(y, ref)
+
+
+def test_swiglu_every_candidate(dev):
+    import abra_b200 as A
+
+    N, K, ncols = 700, 2560, 2
+    wg, wu = O.gen_q4k(N, K, 1, 31), O.gen_q4k(N, K, 1, 32)
+    xq = O.quantize_q8_1(O.gen_normal_f32((ncols, K), 6) * 0.05)
+    ref = O.gemv_swiglu(wg, wu, xq, K, nthreads=8)
+    for cid in A.get_all_candidate_ids():
+        assert np.array_equal(_run_swiglu(dev, wg, wu, xq, N, K, ncols, cid), ref), cid
+
+
+def test_expf_matches_oracle(dev):
+    """silu's exp: the device copy returns the oracle's bits on a dense sweep."""
+    import torch
+    import abra_b200 as A
+
+    N, K = 4096, 256
+    wg = O.gen_q4k(N, K, 3, 41)
+    wu = O.gen_q4k(N, K, 3, 42)
+    rng = np.random.default_rng(8)
+    for scale in (1e-3, 0.02, 0.2):
+        xq = O.quantize_q8_1(rng.standard_normal((1, K)).astype(np.float32) * scale)
+        assert np.array_equal(_run_swiglu(dev, wg, wu, xq, N, K, 1),
+                              O.gemv_swiglu(wg, wu, xq, K))
 
 
 @pytest.mark.parametrize("ncols", [1, 2, 3, 4, 5, 6, 7, 8])
