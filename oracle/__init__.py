@@ -232,3 +232,114 @@ class RefFamily:
 
     def autotuned_candidate(self, N: int, K: int, arch: int = 61) -> int:
         return int(self.lib.ref_autotuned_candidate(N, K, arch))
+
+
+# ------------------------------------------------------------ decode model --
+class OrcModelConfig(C.Structure):
+    _fields_ = [("n_layers", C.c_int32), ("hidden", C.c_int32), ("n_heads", C.c_int32),
+                ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("ffn", C.c_int32),
+                ("vocab", C.c_int32), ("max_ctx", C.c_int32), ("rope_theta", C.c_float),
+                ("eps", C.c_float), ("seed", C.c_uint64)]
+
+
+def _bind_model():
+    vp = C.c_void_p
+    sig = {
+        "orc_model_default_config": (None, [C.POINTER(OrcModelConfig)]),
+        "orc_tensor_id": (C.c_uint64, [C.c_int32, C.c_int32]),
+        "orc_rope_table": (None, [_f32p, C.c_int32, C.c_int32, C.c_float]),
+        "orc_model_create": (vp, [C.POINTER(OrcModelConfig)]),
+        "orc_model_destroy": (None, [vp]),
+        "orc_model_step": (C.c_int32, [vp, C.c_int32, C.c_int32, vp, C.c_int32]),
+        "orc_model_generate": (None, [vp, vp, C.c_int32, C.c_int32, vp, C.c_int32]),
+        "orc_model_hidden": (C.POINTER(C.c_float), [vp]),
+        "orc_add_rmsnorm_quantize": (None, [_f32p, vp, _f32p, C.c_float, _u8p, _i64]),
+        "orc_qk_norm_rope": (None, [_f32p, _f32p, _f32p, C.c_float, _f32p, C.c_int, C.c_int,
+                                    C.c_int, _f32p, vp, vp]),
+        "orc_attention_head": (None, [_f32p, vp, vp, C.c_int, C.c_int, C.c_float, _f32p]),
+        "orc_argmax": (C.c_int32, [_f32p, _i64]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res, args
+
+
+_bind_model()
+
+
+def model_config(**kw) -> OrcModelConfig:
+    c = OrcModelConfig()
+    lib.orc_model_default_config(C.byref(c))
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def tensor_id(layer: int, which: int) -> int:
+    return int(lib.orc_tensor_id(layer, which))
+
+
+def rope_table(ctx: int, head_dim: int, theta: float) -> np.ndarray:
+    out = np.empty(ctx * head_dim, dtype=np.float32)
+    lib.orc_rope_table(out, ctx, head_dim, theta)
+    return out.reshape(ctx, head_dim // 2, 2)
+
+
+class OrcModel:
+    """CPU evaluation of the seeded Qwen3-4B-shaped model, bit-identical in
+    order of operations to abra_b200's decode runtime."""
+
+    def __init__(self, **cfg):
+        self.cfg = model_config(**cfg)
+        self.ptr = lib.orc_model_create(C.byref(self.cfg))
+        self.threads = max_threads()
+
+    def close(self):
+        if self.ptr:
+            lib.orc_model_destroy(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        self.close()
+
+    def step(self, token: int, pos: int, logits: bool = False):
+        out = np.empty(self.cfg.vocab, dtype=np.float32) if logits else None
+        tok = lib.orc_model_step(self.ptr, token, pos, out.ctypes.data if logits else None,
+                                 self.threads)
+        return (tok, out) if logits else tok
+
+    def hidden(self) -> np.ndarray:
+        p = lib.orc_model_hidden(self.ptr)
+        return np.ctypeslib.as_array(p, shape=(self.cfg.hidden,)).copy()
+
+    def generate(self, prompt, n_gen: int) -> np.ndarray:
+        pr = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(n_gen, dtype=np.int32)
+        lib.orc_model_generate(self.ptr, pr.ctypes.data, pr.size, n_gen, out.ctypes.data,
+                               self.threads)
+        return out
+
+
+def attention_head(q: np.ndarray, K16: np.ndarray, V16: np.ndarray, L: int, scale: float):
+    hd = q.size
+    out = np.empty(hd, dtype=np.float32)
+    lib.orc_attention_head(np.ascontiguousarray(q, dtype=np.float32),
+                           np.ascontiguousarray(K16).ctypes.data,
+                           np.ascontiguousarray(V16).ctypes.data, L, hd, scale, out)
+    return out
+
+
+def qk_norm_rope(qkv, q_norm, k_norm, eps, cs_row, n_heads, n_kv, hd):
+    q = np.empty(n_heads * hd, dtype=np.float32)
+    k = np.empty(n_kv * hd, dtype=np.uint16)
+    v = np.empty(n_kv * hd, dtype=np.uint16)
+    lib.orc_qk_norm_rope(np.ascontiguousarray(qkv, dtype=np.float32),
+                         np.ascontiguousarray(q_norm, dtype=np.float32),
+                         np.ascontiguousarray(k_norm, dtype=np.float32), eps,
+                         np.ascontiguousarray(cs_row, dtype=np.float32).reshape(-1),
+                         n_heads, n_kv, hd, q, k.ctypes.data, v.ctypes.data)
+    return q, k, v
+
+
+def argmax(x: np.ndarray) -> int:
+    return int(lib.orc_argmax(np.ascontiguousarray(x, dtype=np.float32), x.size))

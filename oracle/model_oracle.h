@@ -1,0 +1,50 @@
+/*
+ * model_oracle.h -- CPU oracle of the Qwen3-4B-shaped Q4_K decode step.
+ * TEST INFRASTRUCTURE ONLY; see model_oracle.c.
+ */
+#ifndef ABRA_MODEL_ORACLE_H
+#define ABRA_MODEL_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, max_ctx;
+    float rope_theta, eps;
+    uint64_t seed;
+} orc_model_config;
+
+typedef struct orc_model orc_model;
+
+void orc_model_default_config(orc_model_config *c);
+/* Seeded tensor ids: layer -1 -> which (1 embedding/output, 2 out_norm);
+ * layer l -> 100 + 16 l + which (0 attn_norm, 1 wqkv, 2 q_norm, 3 k_norm,
+ * 4 wo, 5 ffn_norm, 6 wgate, 7 wup, 8 wdown). */
+uint64_t orc_tensor_id(int32_t layer, int32_t which);
+void orc_rope_table(float *out, int32_t ctx, int32_t head_dim, float theta);
+
+orc_model *orc_model_create(const orc_model_config *cfg);
+void orc_model_destroy(orc_model *m);
+int32_t orc_model_step(orc_model *m, int32_t token, int32_t pos, float *logits_out,
+                       int32_t nthreads);
+void orc_model_generate(orc_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
+                        int32_t *out, int32_t nthreads);
+const float *orc_model_hidden(const orc_model *m);
+
+/* canonical pieces, exposed for unit tests */
+void orc_add_rmsnorm_quantize(float *h, const float *delta, const float *w, float eps,
+                              uint8_t *xq, int64_t K);
+void orc_qk_norm_rope(const float *qkv, const float *q_norm, const float *k_norm, float eps,
+                      const float *cs_row, int n_heads, int n_kv, int hd, float *q_out,
+                      uint16_t *k_out, uint16_t *v_out);
+void orc_attention_head(const float *q, const uint16_t *K, const uint16_t *V, int L, int hd,
+                        float scale, float *out);
+int32_t orc_argmax(const float *x, int64_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

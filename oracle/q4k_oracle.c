@@ -132,6 +132,17 @@ void orc_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_i
     }
 }
 
+/* Norm weights of the synthetic model: magnitude fmaf(u, 0.4, 0.8) ~ U(0.8,
+ * 1.2) from bits 63..40 of the stream word, sign from bit 0. */
+void orc_gen_norm_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id) {
+    const uint64_t key = stream_key(seed, tensor_id);
+    for (int64_t i = 0; i < n; ++i) {
+        const uint64_t h = stream_word(key, (uint64_t)i);
+        const float v = fmaf(unit24(h >> 40), 0.4f, 0.8f);
+        dst[i] = (h & 1u) ? -v : v;
+    }
+}
+
 /* ------------------------------------------------------------------------ */
 /* Q8_1 quantizer.  Restates kernels/q4k/q4k_q8_mmvq.cu:223-255: amax over   */
 /* 32, d = amax/127, id = d>0 ? 1/d : 0, q = (int8)roundf(x*id), s = d*sum.  */

@@ -37,6 +37,9 @@ void orc_gen_q4k(uint8_t *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_i
 void orc_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
                          int64_t offset_index, float scale, float offset);
 
+/* Synthetic-model norm weights: +-U(0.8, 1.2), random sign (bit 0). */
+void orc_gen_norm_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id);
+
 /* ---- Q8_1 quantizer (reference semantics, q4k_q8_mmvq.cu:223-255) ------- */
 /* x: ncols x K fp32 (column-contiguous); y: ncols x (K/32) blocks of 36 B. */
 void orc_quantize_q8_1(const float *x, uint8_t *y, int64_t K, int32_t ncols);
