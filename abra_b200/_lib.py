@@ -41,6 +41,18 @@ SIGNATURES: dict[str, tuple] = {
     "abra_tune_set": (C.c_int, [_i64, _i64, _i32, _i32, _i32]),
     "abra_tune_get": (C.c_int, [_i64, _i64, _i32, _i32]),
     "abra_tune_clear": (C.c_int, []),
+    # decode model
+    "abra_model_default_config": (C.c_int, [_vp]),
+    "abra_model_create": (C.c_int, [_vp, C.POINTER(C.c_void_p)]),
+    "abra_model_destroy": (C.c_int, [_vp]),
+    "abra_model_reset": (C.c_int, [_vp, _vp, _i32]),
+    "abra_model_step": (C.c_int, [_vp, _i32]),
+    "abra_model_sync": (C.c_int, [_vp]),
+    "abra_model_read": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),
+    "abra_model_generate": (C.c_int, [_vp, _vp, _i32, _i32, _vp]),
+    "abra_model_info": (C.c_int, [_vp, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64),
+                                  C.POINTER(C.c_uint64)]),
+    "abra_model_last_error": (C.c_char_p, []),
 }
 
 

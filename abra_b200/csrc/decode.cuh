@@ -1,0 +1,39 @@
+// decode.cuh -- launchers of the decode-step kernels (decode_kernels.cu) and
+// the generator options used by the model runtime (model.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace abra {
+
+// Up to eight fp32 partial deltas summed in a fixed tree before the residual
+// add: G = 1: p0; 2: p0+p1; 4: (p0+p1)+(p2+p3); 8: three levels.  G = 0: none.
+struct DeltaSet {
+    const float *p[8];
+    int G;
+};
+
+cudaError_t launch_embed(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
+                         float *h, bool pdl, cudaStream_t s);
+cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const float *w,
+                                          float eps, void *y, int K, int ncols, bool pdl,
+                                          cudaStream_t s);
+cudaError_t launch_qk_norm_rope_kv(const float *qkv, const float *q_norm, const float *k_norm,
+                                   float eps, const float *rope, const int32_t *pos, float *q_out,
+                                   void *kc, void *vc, int n_heads, int n_kv, int max_ctx,
+                                   bool pdl, cudaStream_t s);
+cudaError_t launch_attention(const float *q, const void *kc, const void *vc, const int32_t *pos,
+                             float scale, int n_heads, int n_kv, int max_ctx, float *part_m,
+                             float *part_l, float *part_o, float *out_f32, void *out_q8,
+                             bool pdl, cudaStream_t s);
+cudaError_t launch_argmax_advance(const float *logits, int n, int32_t *tokens, int32_t *picks,
+                                  int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
+                                  cudaStream_t s);
+
+// Generator variants (gen_quant.cu).
+cudaError_t launch_gen_q4k_ex(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                              int64_t block_offset, int flags, cudaStream_t stream);
+cudaError_t launch_gen_norm_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
+                                cudaStream_t stream);
+
+}  // namespace abra

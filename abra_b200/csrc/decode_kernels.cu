@@ -1,0 +1,475 @@
+// decode_kernels.cu -- the non-GEMV kernels of the Qwen3-4B-shaped decode
+// step: tied-embedding dequantization, residual add + RMSNorm + Q8_1,
+// QK-RMSNorm + NEOX RoPE + fp16 KV append, chunked attention with a fixed
+// log-sum-exp merge (+ Q8_1 of the result), and greedy argmax.
+//
+// Every fp32 operation uses an explicit-rounding intrinsic in the order the
+// CPU oracle (oracle/model_oracle.c) performs it, so the decode step is
+// bit-identical to the oracle.  Positions and tokens are read from device
+// memory so one captured CUDA graph serves every step.
+#include "common.cuh"
+#include "decode.cuh"
+#include "quant_common.cuh"
+
+namespace abra {
+
+// 6-bit scale and min of sub-block j (get_scale_min_k4, tests/q4k_q8_test.cu:44-52).
+__device__ __forceinline__ void scale_min_one(const uint8_t *q, int j, int &sc, int &m) {
+    if (j < 4) {
+        sc = q[j] & 63;
+        m = q[j + 4] & 63;
+    } else {
+        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+// ---------------------------------------------------------------- embed ---
+// h = dequant(E[tokens[*pos]]): w = fmaf(d * sc, q, -(dmin * m)).
+__global__ void embed_kernel(const uint8_t *__restrict__ E, int hidden,
+                             const int32_t *__restrict__ tokens, const int32_t *__restrict__ pos,
+                             float *__restrict__ h) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int tok = tokens[*pos];
+    const uint8_t *row = E + static_cast<int64_t>(tok) * (hidden / QK_K) * Q4K_BYTES;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += blockDim.x * gridDim.x) {
+        const int b = i >> 8, r = i & 255, p = r >> 6, hh = (r >> 5) & 1, l = r & 31;
+        const uint8_t *blk = row + b * Q4K_BYTES;
+        const float d = __half2float(*reinterpret_cast<const __half *>(blk));
+        const float dmin = __half2float(*reinterpret_cast<const __half *>(blk + 2));
+        int sc, m;
+        scale_min_one(blk + 4, 2 * p + hh, sc, m);
+        const int byte = blk[16 + 32 * p + l];
+        const int q = hh ? (byte >> 4) : (byte & 15);
+        const float a = __fmul_rn(d, static_cast<float>(sc));
+        const float bm = __fmul_rn(dmin, static_cast<float>(m));
+        h[i] = __fmaf_rn(a, static_cast<float>(q), -bm);
+    }
+}
+
+// ------------------------------------------ residual + RMSNorm + Q8_1 ---
+// h = h + D (D = fixed-order tree of G partial deltas, G in {0,1,2,4,8}),
+// then Q8_1 of (h * r) * w, r = 1/sqrt(mean(h^2) + eps).  One CTA per column.
+__device__ __forceinline__ float delta_tree(const DeltaSet &ds, int64_t i) {
+    const float *const *p = ds.p;
+    switch (ds.G) {
+        case 1: return p[0][i];
+        case 2: return __fadd_rn(p[0][i], p[1][i]);
+        case 4: return __fadd_rn(__fadd_rn(p[0][i], p[1][i]), __fadd_rn(p[2][i], p[3][i]));
+        default:
+            return __fadd_rn(__fadd_rn(__fadd_rn(p[0][i], p[1][i]), __fadd_rn(p[2][i], p[3][i])),
+                             __fadd_rn(__fadd_rn(p[4][i], p[5][i]), __fadd_rn(p[6][i], p[7][i])));
+    }
+}
+
+__global__ void __launch_bounds__(RMS_THREADS)
+    residual_rmsnorm_quant_kernel(float *__restrict__ h, const DeltaSet ds,
+                                  const float *__restrict__ w, float eps,
+                                  block_q8_1 *__restrict__ y, int K) {
+    extern __shared__ float s_x[];
+    __shared__ float red[RMS_THREADS / 32];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int c = blockIdx.x;
+    float *hc = h + static_cast<int64_t>(c) * K;
+    for (int i = threadIdx.x; i < K; i += RMS_THREADS) {
+        float v = hc[i];
+        if (ds.G > 0) {
+            v = __fadd_rn(v, delta_tree(ds, static_cast<int64_t>(c) * K + i));
+            hc[i] = v;
+        }
+        s_x[i] = v;
+    }
+    __syncthreads();
+    const float total = block_sumsq_canonical(s_x, K, red);
+    const float r =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), eps)));
+    for (int i = threadIdx.x; i < K; i += RMS_THREADS) s_x[i] = __fmul_rn(__fmul_rn(s_x[i], r), w[i]);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    block_q8_1 *yc = y + static_cast<int64_t>(c) * (K / QK8_1);
+    for (int b = warp; b < K / QK8_1; b += RMS_THREADS / 32)
+        quantize_block_warp(s_x[b * QK8_1 + lane], yc + b, lane);
+}
+
+// ------------------------------------------- QK-norm + RoPE + KV append ---
+// One warp per head of qkv = [q heads | k heads | v heads] x 128.  Lane t
+// holds elements 4t..4t+3.  q/k: RMSNorm over the head (fmaf over the lane's
+// four, xor butterfly 16..1), times the norm weight, then NEOX RoPE pairs
+// (i, i+64) with the host cos/sin table row of this position.  q stays fp32;
+// k and v are stored fp16 at kv[head][pos][128].
+__global__ void __launch_bounds__(256)
+    qk_norm_rope_kv_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
+                           const float *__restrict__ k_norm, float eps,
+                           const float *__restrict__ rope, const int32_t *__restrict__ pos_p,
+                           float *__restrict__ q_out, __half *__restrict__ kc,
+                           __half *__restrict__ vc, int n_heads, int n_kv, int max_ctx) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int hw = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (hw >= n_heads + 2 * n_kv) return;
+    const int pos = *pos_p;
+    if (pos >= max_ctx) return;  // the host never steps past max_ctx; no write out of range
+    const float4 xv = *reinterpret_cast<const float4 *>(qkv + static_cast<int64_t>(hw) * 128 + 4 * lane);
+    const float x[4] = {xv.x, xv.y, xv.z, xv.w};
+    if (hw >= n_heads + n_kv) {  // v head: store fp16 as is
+        const int g = hw - n_heads - n_kv;
+        __half *dst = vc + (static_cast<int64_t>(g) * max_ctx + pos) * 128 + 4 * lane;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = __float2half_rn(x[k]);
+        return;
+    }
+    const float *nw = hw < n_heads ? q_norm : k_norm;
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc = __fmaf_rn(x[k], x[k], acc);
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, 128.0f), eps)));
+    float y[4], o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) y[k] = __fmul_rn(__fmul_rn(x[k], r), nw[4 * lane + k]);
+    const float *cs = rope + static_cast<int64_t>(pos) * 128;  // [64][2]
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float partner = __shfl_xor_sync(0xffffffffu, y[k], 16);
+        const int i = 4 * (lane & 15) + k;
+        const float c = cs[2 * i], s = cs[2 * i + 1];
+        if (lane < 16)
+            o[k] = __fmaf_rn(y[k], c, -__fmul_rn(partner, s));  // x0 = y, x1 = partner
+        else
+            o[k] = __fmaf_rn(partner, s, __fmul_rn(y[k], c));   // x0 = partner, x1 = y
+    }
+    if (hw < n_heads) {
+        *reinterpret_cast<float4 *>(q_out + static_cast<int64_t>(hw) * 128 + 4 * lane) =
+            make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+        const int g = hw - n_heads;
+        __half *dst = kc + (static_cast<int64_t>(g) * max_ctx + pos) * 128 + 4 * lane;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = __float2half_rn(o[k]);
+    }
+}
+
+// ------------------------------------------------------------ attention ---
+// Partials of one (kv head g, chunk c of 256 positions) for its GQA group of
+// q heads.  Thread t owns slot t (position c*256 + t): scores by a
+// sequential fmaf over d = 0..127, times scale.  m = chunk max, e = exp(s -
+// m) (0 past L), l = per-warp xor butterfly then warps in order.  PV: warp w
+// walks its 32 slots in order, lane l owns dims 4l..4l+3 (fmaf chain);
+// warps are added in order.
+constexpr int ATT_CHUNK = 256;
+constexpr int ATT_MAXG = 8;  // q heads per kv head supported
+
+__global__ void __launch_bounds__(256)
+    attention_chunk_kernel(const float *__restrict__ q, const __half *__restrict__ kc,
+                           const __half *__restrict__ vc, const int32_t *__restrict__ pos_p,
+                           float scale, int gq, int max_ctx, int max_chunks,
+                           float *__restrict__ part_m, float *__restrict__ part_l,
+                           float *__restrict__ part_o) {
+    __shared__ float s_q[ATT_MAXG][128];
+    __shared__ float s_e[ATT_MAXG][ATT_CHUNK];
+    __shared__ float s_red[ATT_MAXG][8];
+    __shared__ float s_o[8][ATT_MAXG][128];  // 32 KB for gq = 8
+    pdl_wait();
+    pdl_launch_dependents();
+    const int L = min(*pos_p + 1, max_ctx);
+    const int c = blockIdx.y, g = blockIdx.x;
+    if (c * ATT_CHUNK >= L) return;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    for (int i = t; i < gq * 128; i += 256) s_q[i / 128][i % 128] = q[static_cast<int64_t>(g * gq) * 128 + i];
+    __syncthreads();
+    const int j = c * ATT_CHUNK + t;
+    const bool valid = j < L;
+    float s[ATT_MAXG];
+#pragma unroll
+    for (int h = 0; h < ATT_MAXG; ++h) s[h] = 0.0f;
+    if (valid) {
+        const uint4 *krow = reinterpret_cast<const uint4 *>(kc + (static_cast<int64_t>(g) * max_ctx + j) * 128);
+        for (int d8 = 0; d8 < 16; ++d8) {
+            const uint4 kv = __ldg(krow + d8);
+            const __half2 *k2 = reinterpret_cast<const __half2 *>(&kv);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 kf = __half22float2(k2[e]);
+#pragma unroll
+                for (int h = 0; h < ATT_MAXG; ++h) {
+                    if (h < gq) {
+                        s[h] = __fmaf_rn(s_q[h][d8 * 8 + 2 * e], kf.x, s[h]);
+                        s[h] = __fmaf_rn(s_q[h][d8 * 8 + 2 * e + 1], kf.y, s[h]);
+                    }
+                }
+            }
+        }
+    }
+    // chunk max per head
+    float ev[ATT_MAXG];
+#pragma unroll
+    for (int h = 0; h < ATT_MAXG; ++h) {
+        if (h >= gq) break;
+        float sv = valid ? __fmul_rn(s[h], scale) : -INFINITY;
+        float mx = sv;
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+        if (lane == 0) s_red[h][warp] = mx;
+        s[h] = sv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < ATT_MAXG; ++h) {
+        if (h >= gq) break;
+        float mx = s_red[h][0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_red[h][w]);
+        ev[h] = valid ? abra_expf(__fsub_rn(s[h], mx)) : 0.0f;
+        s_e[h][t] = ev[h];
+        if (t == 0) part_m[static_cast<int64_t>(g * gq + h) * max_chunks + c] = mx;
+    }
+    __syncthreads();  // s_red reused below
+#pragma unroll
+    for (int h = 0; h < ATT_MAXG; ++h) {
+        if (h >= gq) break;
+        float v = ev[h];
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+        if (lane == 0) s_red[h][warp] = v;
+    }
+    // PV over this warp's 32 slots, in order
+    float acc[ATT_MAXG][4];
+#pragma unroll
+    for (int h = 0; h < ATT_MAXG; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[h][k] = 0.0f;
+    __syncwarp();
+    for (int jj = 0; jj < 32; ++jj) {
+        const int jv = c * ATT_CHUNK + warp * 32 + jj;
+        if (jv >= L) break;
+        const uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vc + (static_cast<int64_t>(g) * max_ctx + jv) * 128 + 4 * lane));
+        const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
+        const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+        const float vf[4] = {v01.x, v01.y, v23.x, v23.y};
+#pragma unroll
+        for (int h = 0; h < ATT_MAXG; ++h) {
+            if (h >= gq) break;
+            const float e = s_e[h][warp * 32 + jj];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc[h][k] = __fmaf_rn(e, vf[k], acc[h][k]);
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < ATT_MAXG; ++h) {
+        if (h >= gq) break;
+        *reinterpret_cast<float4 *>(&s_o[warp][h][4 * lane]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    }
+    __syncthreads();
+    for (int i = t; i < gq * 128; i += 256) {
+        const int h = i / 128, d = i % 128;
+        float o = s_o[0][h][d];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) o = __fadd_rn(o, s_o[w][h][d]);
+        part_o[(static_cast<int64_t>(g * gq + h) * max_chunks + c) * 128 + d] = o;
+    }
+    if (t < gq) {
+        float l = s_red[t][0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) l = __fadd_rn(l, s_red[t][w]);
+        part_l[static_cast<int64_t>(g * gq + t) * max_chunks + c] = l;
+    }
+}
+
+// Merge the chunk partials of one q head (one warp per head, lane owns dims
+// 4l..4l+3): M = max m_c, w_c = exp(m_c - M), L = fmaf(l_c, w_c, L),
+// O = fmaf(o_c, w_c, O) over chunks in order, out = O / L; then Q8_1 of the
+// head's 128 values (4 blocks of 32, 8 lanes per block).
+__global__ void __launch_bounds__(256)
+    attention_merge_quant_kernel(const float *__restrict__ part_m,
+                                 const float *__restrict__ part_l,
+                                 const float *__restrict__ part_o,
+                                 const int32_t *__restrict__ pos_p, int n_heads, int max_chunks,
+                                 float *__restrict__ out_f32, block_q8_1 *__restrict__ out_q8) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int hq = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (hq >= n_heads) return;
+    const int L = min(*pos_p + 1, max_chunks * ATT_CHUNK);
+    const int nch = (L + ATT_CHUNK - 1) / ATT_CHUNK;
+    const float *pm = part_m + static_cast<int64_t>(hq) * max_chunks;
+    const float *pl = part_l + static_cast<int64_t>(hq) * max_chunks;
+    float M = pm[0];
+    for (int c = 1; c < nch; ++c) M = fmaxf(M, pm[c]);
+    float Ls = 0.0f, O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int c = 0; c < nch; ++c) {
+        const float wc = abra_expf(__fsub_rn(pm[c], M));
+        Ls = __fmaf_rn(pl[c], wc, Ls);
+        const float4 o = *reinterpret_cast<const float4 *>(part_o + (static_cast<int64_t>(hq) * max_chunks + c) * 128 + 4 * lane);
+        O[0] = __fmaf_rn(o.x, wc, O[0]);
+        O[1] = __fmaf_rn(o.y, wc, O[1]);
+        O[2] = __fmaf_rn(o.z, wc, O[2]);
+        O[3] = __fmaf_rn(o.w, wc, O[3]);
+    }
+    float x[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x[k] = __fdiv_rn(O[k], Ls);
+    if (out_f32)
+        *reinterpret_cast<float4 *>(out_f32 + static_cast<int64_t>(hq) * 128 + 4 * lane) = make_float4(x[0], x[1], x[2], x[3]);
+    // Q8_1 (reference semantics): 8 lanes x 4 values per 32-block
+    float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+    amax = fmaxf(0.0f, amax);
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    int qv[4], sum = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        qv[k] = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x[k], id)))));
+        sum += qv[k];
+    }
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+    block_q8_1 *blk = out_q8 + static_cast<int64_t>(hq) * 4 + (lane >> 3);
+    uint32_t *o32 = reinterpret_cast<uint32_t *>(blk);
+    o32[1 + (lane & 7)] = (static_cast<uint32_t>(qv[0]) & 0xffu) | ((static_cast<uint32_t>(qv[1]) & 0xffu) << 8) |
+                          ((static_cast<uint32_t>(qv[2]) & 0xffu) << 16) | ((static_cast<uint32_t>(qv[3]) & 0xffu) << 24);
+    if ((lane & 7) == 0) {
+        const uint32_t hd = __half_as_ushort(__float2half_rn(d));
+        const uint32_t hs = __half_as_ushort(__float2half_rn(__fmul_rn(d, static_cast<float>(sum))));
+        o32[0] = hd | (hs << 16);
+    }
+}
+
+// --------------------------------------------------------------- argmax ---
+// Greedy token: largest logit, ties to the lowest index.  Writes
+// tokens[*pos + 1] unless that slot still belongs to the prompt (first
+// *n_prompt_p tokens), records the pick in picks[*pos], then advances *pos.
+__global__ void __launch_bounds__(1024)
+    argmax_advance_kernel(const float *__restrict__ x, int n, int32_t *__restrict__ tokens,
+                          int32_t *__restrict__ picks, int32_t *__restrict__ pos_p,
+                          const int32_t *__restrict__ n_prompt_p, int max_ctx) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    pdl_wait();
+    pdl_launch_dependents();
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i];
+        if (v > bv) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        const int p = *pos_p;
+        if (bi == 0x7fffffff) bi = 0;
+        if (p < max_ctx) {  // the host never steps past max_ctx
+            picks[p] = bi;
+            if (p + 1 >= *n_prompt_p) tokens[p + 1] = bi;
+            *pos_p = p + 1;
+        }
+    }
+}
+
+// ----------------------------------------------------------- launchers ---
+static cudaLaunchAttribute pdl_attr() {
+    cudaLaunchAttribute a;
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = 1;
+    return a;
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
+cudaError_t launch_embed(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
+                         float *h, bool pdl, cudaStream_t s) {
+    return launch_pdl(embed_kernel, dim3((hidden + 255) / 256), dim3(256), 0, s, pdl,
+                      static_cast<const uint8_t *>(E), hidden, tokens, pos, h);
+}
+
+cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const float *w,
+                                          float eps, void *y, int K, int ncols, bool pdl,
+                                          cudaStream_t s) {
+    const size_t smem = static_cast<size_t>(K) * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(residual_rmsnorm_quant_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    return launch_pdl(residual_rmsnorm_quant_kernel, dim3(ncols), dim3(RMS_THREADS), smem, s, pdl,
+                      h, ds, w, eps, static_cast<block_q8_1 *>(y), K);
+}
+
+cudaError_t launch_qk_norm_rope_kv(const float *qkv, const float *q_norm, const float *k_norm,
+                                   float eps, const float *rope, const int32_t *pos, float *q_out,
+                                   void *kc, void *vc, int n_heads, int n_kv, int max_ctx,
+                                   bool pdl, cudaStream_t s) {
+    const int heads = n_heads + 2 * n_kv;
+    return launch_pdl(qk_norm_rope_kv_kernel, dim3((heads + 7) / 8), dim3(256), 0, s, pdl, qkv,
+                      q_norm, k_norm, eps, rope, pos, q_out, static_cast<__half *>(kc),
+                      static_cast<__half *>(vc), n_heads, n_kv, max_ctx);
+}
+
+cudaError_t launch_attention(const float *q, const void *kc, const void *vc, const int32_t *pos,
+                             float scale, int n_heads, int n_kv, int max_ctx, float *part_m,
+                             float *part_l, float *part_o, float *out_f32, void *out_q8,
+                             bool pdl, cudaStream_t s) {
+    const int gq = n_heads / n_kv;
+    if (gq > ATT_MAXG || n_heads % n_kv) return cudaErrorInvalidValue;
+    const int max_chunks = (max_ctx + ATT_CHUNK - 1) / ATT_CHUNK;
+    cudaError_t e = launch_pdl(attention_chunk_kernel, dim3(n_kv, max_chunks), dim3(256), 0, s,
+                               pdl, q, static_cast<const __half *>(kc),
+                               static_cast<const __half *>(vc), pos, scale, gq, max_ctx,
+                               max_chunks, part_m, part_l, part_o);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(attention_merge_quant_kernel, dim3((n_heads + 7) / 8), dim3(256), 0, s, pdl,
+                      static_cast<const float *>(part_m), static_cast<const float *>(part_l),
+                      static_cast<const float *>(part_o), pos, n_heads, max_chunks, out_f32,
+                      static_cast<block_q8_1 *>(out_q8));
+}
+
+cudaError_t launch_argmax_advance(const float *logits, int n, int32_t *tokens, int32_t *picks,
+                                  int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
+                                  cudaStream_t s) {
+    return launch_pdl(argmax_advance_kernel, dim3(1), dim3(1024), 0, s, pdl, logits, n, tokens,
+                      picks, pos, n_prompt, max_ctx);
+}
+
+}  // namespace abra
+
+ABRA_ERROR_WORD_ACCESSOR(error_word_decode)

@@ -9,19 +9,73 @@
 // order, so the Q8_1 bytes agree bit for bit.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "quant_common.cuh"
 
 namespace abra {
 
 // ------------------------------------------------------------ generator ---
 // One thread per 8-byte word of the superblock array.  Word 0 of each block
 // carries d and dmin ~ U(0.001, 0.02) in its low four bytes.
+// Centred variant (flags bit 0): keep d, the scales and the nibbles, set
+// dmin = 7.5 d max(sc) / 63 and m_s = round(63 sc_s / max(sc)) so each
+// sub-block's weights have mean ~0.  Words 0 and 1 (bytes 0..15: d, dmin,
+// the 12 scale bytes) are then written together by the word-0 thread.
+__device__ void centre_header(uint64_t &w0, uint64_t &w1) {
+    uint8_t b[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        b[i] = static_cast<uint8_t>(w0 >> (8 * i));
+        b[8 + i] = static_cast<uint8_t>(w1 >> (8 * i));
+    }
+    const uint8_t *q = b + 4;
+    int sc[8], m[8], mx = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        sc[j] = q[j] & 63;
+        sc[j + 4] = (q[j + 8] & 0xF) | ((q[j] >> 6) << 4);
+    }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) mx = sc[s] > mx ? sc[s] : mx;
+    uint16_t hm = 0;
+    if (mx == 0) {
+#pragma unroll
+        for (int s = 0; s < 8; ++s) m[s] = 0;
+    } else {
+        const float df = __half2float(__ushort_as_half(static_cast<unsigned short>(b[0] | (b[1] << 8))));
+        hm = __half_as_ushort(__float2half_rn(
+            __fdiv_rn(__fmul_rn(__fmul_rn(7.5f, df), static_cast<float>(mx)), 63.0f)));
+#pragma unroll
+        for (int s = 0; s < 8; ++s) m[s] = (63 * sc[s] + mx / 2) / mx;
+    }
+    uint8_t o[16];
+    o[0] = b[0];
+    o[1] = b[1];
+    o[2] = static_cast<uint8_t>(hm & 0xff);
+    o[3] = static_cast<uint8_t>(hm >> 8);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        o[4 + j] = static_cast<uint8_t>((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+        o[8 + j] = static_cast<uint8_t>((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+        o[12 + j] = static_cast<uint8_t>((sc[j + 4] & 15) | ((m[j + 4] & 15) << 4));
+    }
+    w0 = 0;
+    w1 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        w0 |= static_cast<uint64_t>(o[i]) << (8 * i);
+        w1 |= static_cast<uint64_t>(o[8 + i]) << (8 * i);
+    }
+}
+
 __global__ void gen_q4k_kernel(uint64_t *__restrict__ dst, int64_t nblocks, uint64_t key,
-                               int64_t block_offset) {
+                               int64_t block_offset, int flags) {
     const int64_t nwords = nblocks * 18;
+    const bool centred = (flags & 1) != 0;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nwords;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t blk = i / 18;
         const int w = static_cast<int>(i - blk * 18);
+        if (centred && w == 1) continue;  // written by the word-0 thread
         const uint64_t gword = static_cast<uint64_t>(block_offset + blk) * 18u + w;
         uint64_t h = stream_word(key, gword);
         if (w == 0) {
@@ -30,8 +84,23 @@ __global__ void gen_q4k_kernel(uint64_t *__restrict__ dst, int64_t nblocks, uint
             const uint64_t hd = __half_as_ushort(__float2half_rn(d));
             const uint64_t hm = __half_as_ushort(__float2half_rn(dmin));
             h = (h & 0xffffffff00000000ull) | hd | (hm << 16);
+            if (centred) {
+                uint64_t h1 = stream_word(key, gword + 1);
+                centre_header(h, h1);
+                dst[i + 1] = h1;
+            }
         }
         dst[i] = h;
+    }
+}
+
+// Norm weights of the synthetic model: +-U(0.8, 1.2), sign from bit 0.
+__global__ void gen_norm_f32_kernel(float *__restrict__ dst, int64_t n, uint64_t key) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const uint64_t h = stream_word(key, static_cast<uint64_t>(i));
+        const float v = __fmaf_rn(unit24(h >> 40), 0.4f, 0.8f);
+        dst[i] = (h & 1u) ? -v : v;
     }
 }
 
@@ -44,15 +113,30 @@ __global__ void gen_uniform_f32_kernel(float *__restrict__ dst, int64_t n, uint6
     }
 }
 
-cudaError_t launch_gen_q4k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
-                           int64_t block_offset, cudaStream_t stream) {
+cudaError_t launch_gen_q4k_ex(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                              int64_t block_offset, int flags, cudaStream_t stream) {
     if (nblocks <= 0) return cudaSuccess;
     const int64_t nwords = nblocks * 18;
     const int threads = 256;
     const int64_t want = (nwords + threads - 1) / threads;
     const int grid = static_cast<int>(want < 148 * 32 ? want : 148 * 32);
     gen_q4k_kernel<<<grid, threads, 0, stream>>>(static_cast<uint64_t *>(dst), nblocks,
-                                                 stream_key(seed, tensor_id), block_offset);
+                                                 stream_key(seed, tensor_id), block_offset, flags);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gen_q4k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                           int64_t block_offset, cudaStream_t stream) {
+    return launch_gen_q4k_ex(dst, nblocks, seed, tensor_id, block_offset, 0, stream);
+}
+
+cudaError_t launch_gen_norm_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
+                                cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    const int threads = 256;
+    const int64_t want = (n + threads - 1) / threads;
+    const int grid = static_cast<int>(want < 148 * 32 ? want : 148 * 32);
+    gen_norm_f32_kernel<<<grid, threads, 0, stream>>>(dst, n, stream_key(seed, tensor_id));
     return cudaGetLastError();
 }
 
@@ -66,34 +150,6 @@ cudaError_t launch_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_
     gen_uniform_f32_kernel<<<grid, threads, 0, stream>>>(dst, n, stream_key(seed, tensor_id),
                                                          offset_index, scale, offset);
     return cudaGetLastError();
-}
-
-// ------------------------------------------------------------ quantizer ---
-// One warp quantizes one 32-element block; lane j owns element j.
-__device__ __forceinline__ void quantize_block_warp(float x, block_q8_1 *out, int lane) {
-    float amax = fmaxf(0.0f, fabsf(x));
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-    const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    const int q = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x, id)))));
-    int sum = q;
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-    // gather four bytes per word: lane k (k < 8) assembles qs[4k .. 4k+3]
-    const uint32_t qb = static_cast<uint32_t>(q) & 0xffu;
-    const int src = (lane & 7) * 4;
-    const uint32_t b0 = __shfl_sync(0xffffffffu, qb, src + 0);
-    const uint32_t b1 = __shfl_sync(0xffffffffu, qb, src + 1);
-    const uint32_t b2 = __shfl_sync(0xffffffffu, qb, src + 2);
-    const uint32_t b3 = __shfl_sync(0xffffffffu, qb, src + 3);
-    uint32_t *o = reinterpret_cast<uint32_t *>(out);
-    if (lane < 8) o[1 + lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-    if (lane == 8) {
-        const uint32_t hd = __half_as_ushort(__float2half_rn(d));
-        const uint32_t hs = __half_as_ushort(__float2half_rn(__fmul_rn(d, static_cast<float>(sum))));
-        o[0] = hd | (hs << 16);
-    }
 }
 
 __global__ void quantize_q8_1_kernel(const float *__restrict__ x, block_q8_1 *__restrict__ y,
@@ -121,23 +177,6 @@ cudaError_t launch_quantize_q8_1(const float *x, void *y, int64_t K, int ncols,
 // One 256-thread CTA per column.  Sum of squares in the canonical order:
 // thread t accumulates x[t + 256 i] with fmaf, each warp reduces with an xor
 // butterfly (masks 16..1), the eight warp sums are added in warp order.
-constexpr int RMS_THREADS = 256;
-
-__device__ __forceinline__ float block_sumsq_canonical(const float *x, int K, float *red) {
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    float acc = 0.0f;
-    for (int i = t; i < K; i += RMS_THREADS) acc = __fmaf_rn(x[i], x[i], acc);
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
-    if (lane == 0) red[warp] = acc;
-    __syncthreads();
-    float total = red[0];
-#pragma unroll
-    for (int w = 1; w < RMS_THREADS / 32; ++w) total = __fadd_rn(total, red[w]);
-    __syncthreads();
-    return total;
-}
-
 __global__ void __launch_bounds__(RMS_THREADS)
     rmsnorm_quantize_q8_1_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                  float eps, block_q8_1 *__restrict__ y, float *__restrict__ xn_out,

@@ -28,6 +28,10 @@ enum : int {
 cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2,
                             const void *x_q8, float *y, int64_t N, int64_t K, int ncols,
                             int64_t ldy, int flags, cudaStream_t stream);
+// Sets the kernel attributes a later launch of this candidate needs (done
+// outside stream capture).
+cudaError_t prepare_mmvq(const MmvqConfig &cfg, int ncols, int nmat);
+
 // Debug: same kernel, additionally storing the exact int32 partials
 // P[c][r][b][s] and M[c][b][s].
 cudaError_t launch_mmvq_q4k_partials(const void *w, const void *x_q8, float *y, int32_t *P,

@@ -181,6 +181,14 @@ cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2
     return launch_plan(fn, pl, (flags & MMVQ_PDL) != 0, prm, stream);
 }
 
+cudaError_t prepare_mmvq(const MmvqConfig &cfg, int ncols, int nmat) {
+    const MmvqTable *t = table_for(ncols);
+    const int ki = ks_index(cfg.ks);
+    if (!t || ki < 0 || nmat < 1 || nmat > 2) return cudaErrorInvalidValue;
+    MmvqFn fn = t->fn[cfg.mode][ki][nmat - 1];
+    return fn ? ensure_smem_attr(fn) : cudaErrorInvalidValue;
+}
+
 cudaError_t launch_mmvq_q4k_partials(const void *w, const void *x_q8, float *y, int32_t *P,
                                      int32_t *M, int64_t N, int64_t K, int ncols, int ks,
                                      cudaStream_t stream) {

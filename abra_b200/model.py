@@ -1,0 +1,111 @@
+"""Qwen3-4B-shaped Q4_K decode on one B200.
+
+Thin host wrapper of the native runtime in libabra_b200 (abra_model_* in
+include/abra_b200.h): weights are generated on the device from a seed, the
+decode step is one CUDA graph replayed per token, and prompt feeding and
+greedy generation never leave the device.  The reference runs the same
+architecture through llama.cpp (tools/qwen3-4b.py, tests/runtime_logits.cpp).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [("n_layers", C.c_int32), ("hidden", C.c_int32), ("n_heads", C.c_int32),
+                ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("ffn", C.c_int32),
+                ("vocab", C.c_int32), ("max_ctx", C.c_int32), ("rope_theta", C.c_float),
+                ("eps", C.c_float), ("seed", C.c_uint64), ("centered", C.c_int32),
+                ("flags", C.c_int32)]
+
+
+EAGER = 1   # ABRA_MODEL_EAGER
+NO_PDL = 2  # ABRA_MODEL_NO_PDL
+
+
+def default_config(**overrides) -> ModelConfig:
+    c = ModelConfig()
+    _lib.lib.abra_model_default_config(C.byref(c))
+    for k, v in overrides.items():
+        setattr(c, k, v)
+    return c
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != _lib.ABRA_OK:
+        msg = _lib.lib.abra_model_last_error()
+        raise _lib.AbraError(rc, what, msg.decode() if msg else "")
+
+
+class DecodeModel:
+    """A seeded Qwen3-4B-shaped model resident on the current CUDA device."""
+
+    def __init__(self, **config):
+        self.handle = None
+        self.cfg = default_config(**config)
+        h = C.c_void_p()
+        _check(_lib.lib.abra_model_create(C.byref(self.cfg), C.byref(h)), "abra_model_create")
+        self.handle = h
+
+    def close(self) -> None:
+        if self.handle:
+            _lib.lib.abra_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- state ------------------------------------------------------------
+    def reset(self, prompt) -> None:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        _check(_lib.lib.abra_model_reset(self.handle, p.ctypes.data, p.size), "abra_model_reset")
+
+    def step(self, n: int = 1) -> None:
+        """Queue n decode steps on the model's stream (asynchronous)."""
+        _check(_lib.lib.abra_model_step(self.handle, n), "abra_model_step")
+
+    def sync(self) -> None:
+        _check(_lib.lib.abra_model_sync(self.handle), "abra_model_sync")
+
+    def tokens(self, n: int) -> np.ndarray:
+        out = np.empty(n, dtype=np.int32)
+        _check(_lib.lib.abra_model_read(self.handle, out.ctypes.data, n, None, None), "abra_model_read")
+        return out
+
+    def logits(self) -> np.ndarray:
+        out = np.empty(self.cfg.vocab, dtype=np.float32)
+        _check(_lib.lib.abra_model_read(self.handle, None, 0, out.ctypes.data, None), "abra_model_read")
+        return out
+
+    def position(self) -> int:
+        p = C.c_int32()
+        _check(_lib.lib.abra_model_read(self.handle, None, 0, None, C.byref(p)), "abra_model_read")
+        return p.value
+
+    def generate(self, prompt, n_gen: int) -> np.ndarray:
+        """Greedy: feed the prompt, return the n_gen picked token ids."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(n_gen, dtype=np.int32)
+        _check(_lib.lib.abra_model_generate(self.handle, p.ctypes.data, p.size, n_gen,
+                                            out.ctypes.data), "abra_model_generate")
+        return out
+
+    def info(self) -> dict:
+        st, wb, kb = C.c_void_p(), C.c_uint64(), C.c_uint64()
+        _check(_lib.lib.abra_model_info(self.handle, C.byref(st), C.byref(wb), C.byref(kb)),
+               "abra_model_info")
+        return {"stream": st.value or 0, "weight_bytes": wb.value, "kv_bytes": kb.value}
+
+    @property
+    def stream(self) -> int:
+        return self.info()["stream"]

@@ -130,6 +130,45 @@ int abra_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t nmat, int32_t can
 int abra_tune_get(int64_t N, int64_t K, int32_t ncols, int32_t nmat); /* candidate id */
 int abra_tune_clear(void);
 
+/* ------------------------------------------------------ decode model --- */
+/* Qwen3-4B-shaped decode with every linear layer Q4_K:
+ * the native runtime that the reference delegates to llama.cpp.  Weights
+ * are generated on the device from a seed (the same counter-based generator
+ * as abra_gen_q4k; tensor ids: 1 embedding/output (tied), 2 output norm,
+ * 100 + 16 l + {0 attn_norm, 1 q|k|v, 2 q_norm, 3 k_norm, 4 o, 5 ffn_norm,
+ * 6 gate, 7 up, 8 down}); norm weights are +-U(0.8, 1.2) with random sign.
+ * Unlike the kernel entry points above, the model allocates (weights, fp16
+ * KV cache for max_ctx positions, activations) and owns a CUDA stream. */
+typedef struct {
+    int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, max_ctx;
+    float rope_theta, eps;
+    uint64_t seed;
+    int32_t centered; /* 1: centred Q4_K variant (zero-mean sub-blocks) */
+    int32_t flags;    /* ABRA_MODEL_* */
+} abra_model_config;
+
+#define ABRA_MODEL_EAGER 1  /* launch kernels per step instead of a CUDA graph */
+#define ABRA_MODEL_NO_PDL 2 /* no programmatic dependent launch */
+
+int abra_model_default_config(abra_model_config *cfg); /* Qwen3-4B, max_ctx 4096 */
+int abra_model_create(const abra_model_config *cfg, void **model);
+int abra_model_destroy(void *model);
+/* Load a prompt (token ids) and rewind to position 0 (synchronous). */
+int abra_model_reset(void *model, const int32_t *prompt, int32_t n_prompt);
+/* Run n decode steps (asynchronous on the model's stream): each consumes
+ * tokens[pos], appends the greedy pick once past the prompt, pos += 1. */
+int abra_model_step(void *model, int32_t n_steps);
+int abra_model_sync(void *model);
+/* Synchronises, then copies tokens[0..n_tokens) (prompt then picks), the
+ * last step's logits (vocab floats) and the position; NULL skips an item. */
+int abra_model_read(void *model, int32_t *tokens, int32_t n_tokens, float *logits,
+                    int32_t *pos);
+/* reset + (n_prompt + n_gen - 1) steps; out receives the n_gen picks. */
+int abra_model_generate(void *model, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
+                        int32_t *out);
+int abra_model_info(void *model, void **stream, uint64_t *weight_bytes, uint64_t *kv_bytes);
+const char *abra_model_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,8 @@ def _load() -> C.CDLL:
         "orc_f32_to_f16": (C.c_uint16, [C.c_float]),
         "orc_f16_to_f32": (C.c_float, [C.c_uint16]),
         "orc_gen_q4k": (None, [_u8p, _i64, _u64, _u64, _i64]),
+        "orc_gen_q4k_ex": (None, [_u8p, _i64, _u64, _u64, _i64, _i32]),
+        "orc_gen_norm_f32": (None, [_f32p, _i64, _u64, _u64]),
         "orc_gen_uniform_f32": (None, [_f32p, _i64, _u64, _u64, _i64, _f32, _f32]),
         "orc_quantize_q8_1": (None, [_f32p, _u8p, _i64, _i32]),
         "orc_rmsnorm_quantize_q8_1": (None, [_f32p, _f32p, _f32, _u8p, C.c_void_p, _i64, _i32]),
@@ -73,12 +75,20 @@ lib = _load()
 
 
 # ------------------------------------------------------------ generators ---
-def gen_q4k(N: int, K: int, seed: int, tensor_id: int, row_offset: int = 0) -> np.ndarray:
+def gen_q4k(N: int, K: int, seed: int, tensor_id: int, row_offset: int = 0,
+            centered: bool = False) -> np.ndarray:
     """Q4_K rows [row_offset, row_offset+N) of a K-wide tensor, as uint8 (N, K/256*144)."""
     nsb = K // QK_K
     out = np.empty(N * nsb * Q4K_BYTES, dtype=np.uint8)
-    lib.orc_gen_q4k(out, N * nsb, seed, tensor_id, row_offset * nsb)
+    lib.orc_gen_q4k_ex(out, N * nsb, seed, tensor_id, row_offset * nsb, 1 if centered else 0)
     return out.reshape(N, nsb * Q4K_BYTES)
+
+
+def gen_norm_f32(n: int, seed: int, tensor_id: int) -> np.ndarray:
+    """+-U(0.8, 1.2) with a random sign: the synthetic model's norm weights."""
+    out = np.empty(n, dtype=np.float32)
+    lib.orc_gen_norm_f32(out, n, seed, tensor_id)
+    return out
 
 
 def gen_uniform_f32(n: int, seed: int, tensor_id: int, scale: float, offset: float,
@@ -239,7 +249,8 @@ class OrcModelConfig(C.Structure):
     _fields_ = [("n_layers", C.c_int32), ("hidden", C.c_int32), ("n_heads", C.c_int32),
                 ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("ffn", C.c_int32),
                 ("vocab", C.c_int32), ("max_ctx", C.c_int32), ("rope_theta", C.c_float),
-                ("eps", C.c_float), ("seed", C.c_uint64)]
+                ("eps", C.c_float), ("seed", C.c_uint64), ("centered", C.c_int32),
+                ("reserved", C.c_int32)]
 
 
 def _bind_model():

@@ -53,6 +53,8 @@ void orc_model_default_config(orc_model_config *c) {
     c->rope_theta = 1000000.0f;
     c->eps = 1e-6f;
     c->seed = 0;
+    c->centered = 0;
+    c->reserved = 0;
 }
 
 uint64_t orc_tensor_id(int32_t layer, int32_t which) {
@@ -60,14 +62,15 @@ uint64_t orc_tensor_id(int32_t layer, int32_t which) {
     return 100u + 16u * (uint64_t)layer + (uint64_t)which;
 }
 
-static uint8_t *gen_q4k_tensor(int64_t rows, int64_t cols, uint64_t seed, uint64_t tid) {
+static uint8_t *gen_q4k_tensor(int64_t rows, int64_t cols, uint64_t seed, uint64_t tid,
+                               int32_t flags) {
     const int64_t nb = rows * (cols / 256);
     uint8_t *p = (uint8_t *)malloc((size_t)nb * Q4K_BYTES);
     const int64_t chunk = 1 << 16;
 #pragma omp parallel for schedule(static)
     for (int64_t b = 0; b < nb; b += chunk) {
         const int64_t n = nb - b < chunk ? nb - b : chunk;
-        orc_gen_q4k(p + b * Q4K_BYTES, n, seed, tid, b);
+        orc_gen_q4k_ex(p + b * Q4K_BYTES, n, seed, tid, b, flags);
     }
     return p;
 }
@@ -96,20 +99,20 @@ orc_model *orc_model_create(const orc_model_config *cfg) {
     const orc_model_config *c = &m->cfg;
     const uint64_t s = c->seed;
     const int64_t qkv_rows = (int64_t)(c->n_heads + 2 * c->n_kv_heads) * c->head_dim;
-    m->embd = gen_q4k_tensor(c->vocab, c->hidden, s, orc_tensor_id(-1, 1));
+    m->embd = gen_q4k_tensor(c->vocab, c->hidden, s, orc_tensor_id(-1, 1), c->centered);
     m->out_norm = gen_norm(c->hidden, s, orc_tensor_id(-1, 2));
     m->L = calloc((size_t)c->n_layers, sizeof *m->L);
     for (int l = 0; l < c->n_layers; ++l) {
         struct layer *y = &m->L[l];
         y->attn_norm = gen_norm(c->hidden, s, orc_tensor_id(l, 0));
-        y->wqkv = gen_q4k_tensor(qkv_rows, c->hidden, s, orc_tensor_id(l, 1));
+        y->wqkv = gen_q4k_tensor(qkv_rows, c->hidden, s, orc_tensor_id(l, 1), c->centered);
         y->q_norm = gen_norm(c->head_dim, s, orc_tensor_id(l, 2));
         y->k_norm = gen_norm(c->head_dim, s, orc_tensor_id(l, 3));
-        y->wo = gen_q4k_tensor(c->hidden, (int64_t)c->n_heads * c->head_dim, s, orc_tensor_id(l, 4));
+        y->wo = gen_q4k_tensor(c->hidden, (int64_t)c->n_heads * c->head_dim, s, orc_tensor_id(l, 4), c->centered);
         y->ffn_norm = gen_norm(c->hidden, s, orc_tensor_id(l, 5));
-        y->wgate = gen_q4k_tensor(c->ffn, c->hidden, s, orc_tensor_id(l, 6));
-        y->wup = gen_q4k_tensor(c->ffn, c->hidden, s, orc_tensor_id(l, 7));
-        y->wdown = gen_q4k_tensor(c->hidden, c->ffn, s, orc_tensor_id(l, 8));
+        y->wgate = gen_q4k_tensor(c->ffn, c->hidden, s, orc_tensor_id(l, 6), c->centered);
+        y->wup = gen_q4k_tensor(c->ffn, c->hidden, s, orc_tensor_id(l, 7), c->centered);
+        y->wdown = gen_q4k_tensor(c->hidden, c->ffn, s, orc_tensor_id(l, 8), c->centered);
     }
     const size_t kv = (size_t)c->n_layers * c->n_kv_heads * c->max_ctx * c->head_dim;
     m->kcache = (uint16_t *)calloc(kv, 2);

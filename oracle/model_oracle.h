@@ -15,6 +15,8 @@ typedef struct {
     int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, max_ctx;
     float rope_theta, eps;
     uint64_t seed;
+    int32_t centered; /* 1: centred Q4_K variant (orc_gen_q4k_ex flag 1) */
+    int32_t reserved;
 } orc_model_config;
 
 typedef struct orc_model orc_model;

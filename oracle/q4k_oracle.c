@@ -104,8 +104,26 @@ static inline float unit24(uint64_t bits24) { /* exact: 24-bit int * 2^-24 */
     return (float)(uint32_t)bits24 * 5.9604644775390625e-08f;
 }
 
-void orc_gen_q4k(uint8_t *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
-                 int64_t block_offset) {
+/* 12 packed scale bytes <-> eight 6-bit scales and mins (the packing that
+ * get_scale_min_k4, tests/q4k_q8_test.cu:44-52, reads). */
+static void unpack_scales(const uint8_t *q, int sc[8], int m[8]) {
+    for (int j = 0; j < 4; ++j) {
+        sc[j] = q[j] & 63;
+        m[j] = q[j + 4] & 63;
+        sc[j + 4] = (q[j + 8] & 0xF) | ((q[j] >> 6) << 4);
+        m[j + 4] = (q[j + 8] >> 4) | ((q[j + 4] >> 6) << 4);
+    }
+}
+static void pack_scales(const int sc[8], const int m[8], uint8_t *q) {
+    for (int j = 0; j < 4; ++j) {
+        q[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+        q[j + 4] = (uint8_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+        q[j + 8] = (uint8_t)((sc[j + 4] & 15) | ((m[j + 4] & 15) << 4));
+    }
+}
+
+void orc_gen_q4k_ex(uint8_t *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                    int64_t block_offset, int32_t flags) {
     const uint64_t key = stream_key(seed, tensor_id);
     for (int64_t i = 0; i < nblocks; ++i) {
         const uint64_t gb = (uint64_t)(block_offset + i);
@@ -117,10 +135,32 @@ void orc_gen_q4k(uint8_t *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_i
         const uint64_t h0 = stream_word(key, gb * 18u);
         const float d = fmaf(unit24(h0 >> 40), 0.019f, 0.001f);
         const float dmin = fmaf(unit24((h0 >> 16) & 0xffffffu), 0.019f, 0.001f);
-        const uint16_t hd = orc_f32_to_f16(d), hm = orc_f32_to_f16(dmin);
+        const uint16_t hd = orc_f32_to_f16(d);
+        uint16_t hm = orc_f32_to_f16(dmin);
+        if (flags & 1) {
+            /* centred: dmin * m_s ~= 7.5 * d * sc_s, so every sub-block of
+             * d*sc*q - dmin*m has mean ~0 over nibbles ~ U{0..15} */
+            int sc[8], m[8], mx = 0;
+            unpack_scales(blk + 4, sc, m);
+            for (int s = 0; s < 8; ++s) mx = sc[s] > mx ? sc[s] : mx;
+            if (mx == 0) {
+                hm = 0;
+                for (int s = 0; s < 8; ++s) m[s] = 0;
+            } else {
+                const float df = orc_f16_to_f32(hd);
+                hm = orc_f32_to_f16(((7.5f * df) * (float)mx) / 63.0f);
+                for (int s = 0; s < 8; ++s) m[s] = (63 * sc[s] + mx / 2) / mx;
+            }
+            pack_scales(sc, m, blk + 4);
+        }
         memcpy(blk + 0, &hd, 2);
         memcpy(blk + 2, &hm, 2);
     }
+}
+
+void orc_gen_q4k(uint8_t *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                 int64_t block_offset) {
+    orc_gen_q4k_ex(dst, nblocks, seed, tensor_id, block_offset, 0);
 }
 
 void orc_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,

@@ -33,6 +33,11 @@ float    orc_f16_to_f32(uint16_t h);
  * 6-bit sc/m values ~ U{0..63}) and 128 nibble bytes (nibbles ~ U{0..15}). */
 void orc_gen_q4k(uint8_t *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
                  int64_t block_offset);
+/* flags bit 0: centred variant -- same d, scales and nibbles, but
+ * dmin = 7.5 d max(sc) / 63 and m_s = round(63 sc_s / max(sc)), so each
+ * sub-block's weights have mean ~0. */
+void orc_gen_q4k_ex(uint8_t *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                    int64_t block_offset, int32_t flags);
 /* fp32 values fmaf(u, scale, offset) with u ~ U[0,1) on a 2^-24 grid. */
 void orc_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
                          int64_t offset_index, float scale, float offset);

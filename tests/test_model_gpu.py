@@ -1,0 +1,90 @@
+"""GPU parity of the Qwen3-4B-shaped decode runtime
+against the CPU oracle model, through the C ABI.
+
+The runtime follows the oracle's operation order everywhere, so the bar is
+bit-identical logits at every step (which implies identical greedy tokens).
+The reference's own integration check compares full-vocabulary logit dumps
+step by step (tests/runtime_logits.cpp:59-108, tools/compare-runtime-logits.py)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _pair(**cfg):
+    from abra_b200.model import DecodeModel
+
+    return DecodeModel(**cfg), O.OrcModel(**cfg)
+
+
+def _prompt(n, vocab, seed):
+    return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int32)
+
+
+@pytest.mark.parametrize("centered", [1, 0])
+def test_small_model_logits_bit_exact_across_chunks(centered):
+    """2 layers, vocab 4096, 600 positions: attention crosses the 256-position
+    chunk boundaries; logits compared at every step of a window around each."""
+    cfg = dict(n_layers=2, vocab=4096, max_ctx=600, centered=centered, seed=3)
+    g, c = _pair(**cfg)
+    prompt = _prompt(5, 4096, 1)
+    g.reset(prompt)
+    check = set(range(0, 12)) | set(range(250, 262)) | set(range(508, 516)) | {598}
+    tok = None
+    for pos in range(599):
+        feed = int(prompt[pos]) if pos < len(prompt) else tok
+        want_tok, want = c.step(feed, pos, logits=True)
+        g.step(1)
+        if pos in check:
+            got = g.logits()
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"logits differ at pos {pos}"
+        tok = want_tok
+    toks = g.tokens(600)
+    assert g.position() == 599
+    assert np.array_equal(toks[:5], prompt)
+    g.close()
+    c.close()
+
+
+def test_graph_eager_and_no_pdl_agree():
+    from abra_b200.model import EAGER, NO_PDL, DecodeModel
+
+    cfg = dict(n_layers=3, vocab=2048, max_ctx=300, centered=1, seed=5)
+    prompt = _prompt(7, 2048, 2)
+    outs = []
+    for flags in (0, EAGER, NO_PDL, EAGER | NO_PDL):
+        with DecodeModel(flags=flags, **cfg) as m:
+            toks = m.generate(prompt, 280)
+            outs.append((toks, m.logits()))
+    for toks, lg in outs[1:]:
+        assert np.array_equal(toks, outs[0][0])
+        assert np.array_equal(lg.view(np.uint32), outs[0][1].view(np.uint32))
+
+
+@pytest.mark.parametrize("centered", [1, 0])
+def test_full_qwen3_4b_shape_greedy_bit_exact(centered):
+    """The full 36-layer Qwen3-4B shape, 16-token prompt, 16 greedy steps:
+    logits bit-identical to the CPU oracle at every step."""
+    cfg = dict(max_ctx=64, centered=centered, seed=0)
+    g, c = _pair(**cfg)
+    prompt = _prompt(16, 151936, 7)
+    g.reset(prompt)
+    tok = None
+    picks = []
+    for pos in range(32):
+        feed = int(prompt[pos]) if pos < 16 else tok
+        tok, want = c.step(feed, pos, logits=True)
+        g.step(1)
+        got = g.logits()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"pos {pos}"
+        if pos >= 15:
+            picks.append(tok)
+    assert np.array_equal(g.tokens(33)[16:33], np.array(picks, dtype=np.int32))
+    if centered:
+        assert len(set(picks)) > 4, "centred model should not collapse to one token"
+    g.close()
+    c.close()
