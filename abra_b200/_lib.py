@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "abra_model_sync": (C.c_int, [_vp]),
     "abra_model_read": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),
     "abra_model_generate": (C.c_int, [_vp, _vp, _i32, _i32, _vp]),
+    "abra_model_decode_streaming": (C.c_int, [_vp, _i32, _vp]),
     "abra_model_info": (C.c_int, [_vp, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64),
                                   C.POINTER(C.c_uint64)]),
     "abra_model_last_error": (C.c_char_p, []),

@@ -168,6 +168,25 @@ __device__ __forceinline__ void scale_min_pair(uint32_t s0, uint32_t s1, uint32_
     }
 }
 
+// Up to eight fp32 partial deltas summed in a fixed tree before a residual
+// add: G = 1: p0; 2: p0+p1; 4: (p0+p1)+(p2+p3); 8: three levels.  G = 0: none.
+struct DeltaSet {
+    const float *p[8];
+    int G;
+};
+
+__device__ __forceinline__ float delta_tree(const DeltaSet &ds, int64_t i) {
+    const float *const *p = ds.p;
+    switch (ds.G) {
+        case 1: return p[0][i];
+        case 2: return __fadd_rn(p[0][i], p[1][i]);
+        case 4: return __fadd_rn(__fadd_rn(p[0][i], p[1][i]), __fadd_rn(p[2][i], p[3][i]));
+        default:
+            return __fadd_rn(__fadd_rn(__fadd_rn(p[0][i], p[1][i]), __fadd_rn(p[2][i], p[3][i])),
+                             __fadd_rn(__fadd_rn(p[4][i], p[5][i]), __fadd_rn(p[6][i], p[7][i])));
+    }
+}
+
 // Canonical K-slices: eight contiguous superblock ranges, the first nsb % 8
 // one superblock longer.  Slice i starts at slice_start(nsb, i).
 __host__ __device__ __forceinline__ int slice_start(int nsb, int i) {

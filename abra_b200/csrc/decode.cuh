@@ -6,13 +6,6 @@
 
 namespace abra {
 
-// Up to eight fp32 partial deltas summed in a fixed tree before the residual
-// add: G = 1: p0; 2: p0+p1; 4: (p0+p1)+(p2+p3); 8: three levels.  G = 0: none.
-struct DeltaSet {
-    const float *p[8];
-    int G;
-};
-
 cudaError_t launch_embed(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
                          float *h, bool pdl, cudaStream_t s);
 cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const float *w,
@@ -26,6 +19,10 @@ cudaError_t launch_attention(const float *q, const void *kc, const void *vc, con
                              float scale, int n_heads, int n_kv, int max_ctx, float *part_m,
                              float *part_l, float *part_o, float *out_f32, void *out_q8,
                              bool pdl, cudaStream_t s);
+// Reads the argmax key left by the output MMVQ, resets it, appends the pick.
+cudaError_t launch_argmax_finish(unsigned long long *key, int32_t *tokens, int32_t *picks,
+                                 int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
+                                 cudaStream_t s);
 cudaError_t launch_argmax_advance(const float *logits, int n, int32_t *tokens, int32_t *picks,
                                   int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
                                   cudaStream_t s);

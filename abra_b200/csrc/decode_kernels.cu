@@ -51,29 +51,23 @@ __global__ void embed_kernel(const uint8_t *__restrict__ E, int hidden,
 // ------------------------------------------ residual + RMSNorm + Q8_1 ---
 // h = h + D (D = fixed-order tree of G partial deltas, G in {0,1,2,4,8}),
 // then Q8_1 of (h * r) * w, r = 1/sqrt(mean(h^2) + eps).  One CTA per column.
-__device__ __forceinline__ float delta_tree(const DeltaSet &ds, int64_t i) {
-    const float *const *p = ds.p;
-    switch (ds.G) {
-        case 1: return p[0][i];
-        case 2: return __fadd_rn(p[0][i], p[1][i]);
-        case 4: return __fadd_rn(__fadd_rn(p[0][i], p[1][i]), __fadd_rn(p[2][i], p[3][i]));
-        default:
-            return __fadd_rn(__fadd_rn(__fadd_rn(p[0][i], p[1][i]), __fadd_rn(p[2][i], p[3][i])),
-                             __fadd_rn(__fadd_rn(p[4][i], p[5][i]), __fadd_rn(p[6][i], p[7][i])));
-    }
-}
+// 1024 threads: the canonical 256-lane sum of squares runs on threads
+// 0..255 (same order as block_sumsq_canonical), every thread takes part in
+// the residual add, the scaling and (as 32 warps) the Q8_1 blocks.
+constexpr int RES_THREADS = 1024;
 
-__global__ void __launch_bounds__(RMS_THREADS)
+__global__ void __launch_bounds__(RES_THREADS)
     residual_rmsnorm_quant_kernel(float *__restrict__ h, const DeltaSet ds,
                                   const float *__restrict__ w, float eps,
                                   block_q8_1 *__restrict__ y, int K) {
     extern __shared__ float s_x[];
     __shared__ float red[RMS_THREADS / 32];
+    __shared__ float s_r;
     pdl_wait();
     pdl_launch_dependents();
-    const int c = blockIdx.x;
+    const int c = blockIdx.x, t = threadIdx.x;
     float *hc = h + static_cast<int64_t>(c) * K;
-    for (int i = threadIdx.x; i < K; i += RMS_THREADS) {
+    for (int i = t; i < K; i += RES_THREADS) {
         float v = hc[i];
         if (ds.G > 0) {
             v = __fadd_rn(v, delta_tree(ds, static_cast<int64_t>(c) * K + i));
@@ -82,14 +76,27 @@ __global__ void __launch_bounds__(RMS_THREADS)
         s_x[i] = v;
     }
     __syncthreads();
-    const float total = block_sumsq_canonical(s_x, K, red);
-    const float r =
-        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), eps)));
-    for (int i = threadIdx.x; i < K; i += RMS_THREADS) s_x[i] = __fmul_rn(__fmul_rn(s_x[i], r), w[i]);
+    if (t < RMS_THREADS) {
+        float acc = 0.0f;
+        for (int i = t; i < K; i += RMS_THREADS) acc = __fmaf_rn(s_x[i], s_x[i], acc);
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+        if ((t & 31) == 0) red[t >> 5] = acc;
+    }
     __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (t == 0) {
+        float total = red[0];
+#pragma unroll
+        for (int k = 1; k < RMS_THREADS / 32; ++k) total = __fadd_rn(total, red[k]);
+        s_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), eps)));
+    }
+    __syncthreads();
+    const float r = s_r;
+    for (int i = t; i < K; i += RES_THREADS) s_x[i] = __fmul_rn(__fmul_rn(s_x[i], r), w[i]);
+    __syncthreads();
+    const int lane = t & 31, warp = t >> 5;
     block_q8_1 *yc = y + static_cast<int64_t>(c) * (K / QK8_1);
-    for (int b = warp; b < K / QK8_1; b += RMS_THREADS / 32)
+    for (int b = warp; b < K / QK8_1; b += RES_THREADS / 32)
         quantize_block_warp(s_x[b * QK8_1 + lane], yc + b, lane);
 }
 
@@ -163,53 +170,55 @@ __global__ void __launch_bounds__(256)
 constexpr int ATT_CHUNK = 256;
 constexpr int ATT_MAXG = 8;  // q heads per kv head supported
 
+template <int GQ>
 __global__ void __launch_bounds__(256)
     attention_chunk_kernel(const float *__restrict__ q, const __half *__restrict__ kc,
                            const __half *__restrict__ vc, const int32_t *__restrict__ pos_p,
-                           float scale, int gq, int max_ctx, int max_chunks,
+                           float scale, int max_ctx, int max_chunks,
                            float *__restrict__ part_m, float *__restrict__ part_l,
                            float *__restrict__ part_o) {
-    __shared__ float s_q[ATT_MAXG][128];
-    __shared__ float s_e[ATT_MAXG][ATT_CHUNK];
-    __shared__ float s_red[ATT_MAXG][8];
-    __shared__ float s_o[8][ATT_MAXG][128];  // 32 KB for gq = 8
+    __shared__ __align__(16) float s_q[GQ][128];
+    __shared__ float s_e[GQ][ATT_CHUNK];
+    __shared__ float s_red[GQ][8];
+    __shared__ __align__(16) float s_o[8][GQ][128];
     pdl_wait();
     pdl_launch_dependents();
     const int L = min(*pos_p + 1, max_ctx);
     const int c = blockIdx.y, g = blockIdx.x;
     if (c * ATT_CHUNK >= L) return;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    for (int i = t; i < gq * 128; i += 256) s_q[i / 128][i % 128] = q[static_cast<int64_t>(g * gq) * 128 + i];
+    for (int i = t; i < GQ * 128; i += 256) s_q[i / 128][i % 128] = q[static_cast<int64_t>(g * GQ) * 128 + i];
     __syncthreads();
     const int j = c * ATT_CHUNK + t;
     const bool valid = j < L;
-    float s[ATT_MAXG];
+    // scores: sequential fmaf over d = 0..127 (all 16 row loads issued first)
+    float s[GQ];
 #pragma unroll
-    for (int h = 0; h < ATT_MAXG; ++h) s[h] = 0.0f;
+    for (int h = 0; h < GQ; ++h) s[h] = 0.0f;
     if (valid) {
         const uint4 *krow = reinterpret_cast<const uint4 *>(kc + (static_cast<int64_t>(g) * max_ctx + j) * 128);
+        uint4 kv[16];
+#pragma unroll
+        for (int d8 = 0; d8 < 16; ++d8) kv[d8] = __ldg(krow + d8);
+#pragma unroll
         for (int d8 = 0; d8 < 16; ++d8) {
-            const uint4 kv = __ldg(krow + d8);
-            const __half2 *k2 = reinterpret_cast<const __half2 *>(&kv);
+            const __half2 *k2 = reinterpret_cast<const __half2 *>(&kv[d8]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const float2 kf = __half22float2(k2[e]);
 #pragma unroll
-                for (int h = 0; h < ATT_MAXG; ++h) {
-                    if (h < gq) {
-                        s[h] = __fmaf_rn(s_q[h][d8 * 8 + 2 * e], kf.x, s[h]);
-                        s[h] = __fmaf_rn(s_q[h][d8 * 8 + 2 * e + 1], kf.y, s[h]);
-                    }
+                for (int h = 0; h < GQ; ++h) {
+                    const float2 qv = *reinterpret_cast<const float2 *>(&s_q[h][d8 * 8 + 2 * e]);
+                    s[h] = __fmaf_rn(qv.x, kf.x, s[h]);
+                    s[h] = __fmaf_rn(qv.y, kf.y, s[h]);
                 }
             }
         }
     }
-    // chunk max per head
-    float ev[ATT_MAXG];
+    // chunk max per head, e = exp(s - m), per-warp butterfly sums
 #pragma unroll
-    for (int h = 0; h < ATT_MAXG; ++h) {
-        if (h >= gq) break;
-        float sv = valid ? __fmul_rn(s[h], scale) : -INFINITY;
+    for (int h = 0; h < GQ; ++h) {
+        const float sv = valid ? __fmul_rn(s[h], scale) : -INFINITY;
         float mx = sv;
 #pragma unroll
         for (int m = 16; m >= 1; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
@@ -217,65 +226,72 @@ __global__ void __launch_bounds__(256)
         s[h] = sv;
     }
     __syncthreads();
+    float ev[GQ];
 #pragma unroll
-    for (int h = 0; h < ATT_MAXG; ++h) {
-        if (h >= gq) break;
+    for (int h = 0; h < GQ; ++h) {
         float mx = s_red[h][0];
 #pragma unroll
         for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_red[h][w]);
         ev[h] = valid ? abra_expf(__fsub_rn(s[h], mx)) : 0.0f;
         s_e[h][t] = ev[h];
-        if (t == 0) part_m[static_cast<int64_t>(g * gq + h) * max_chunks + c] = mx;
+        if (t == 0) part_m[static_cast<int64_t>(g * GQ + h) * max_chunks + c] = mx;
     }
-    __syncthreads();  // s_red reused below
+    __syncthreads();  // s_red is reused for the sums
 #pragma unroll
-    for (int h = 0; h < ATT_MAXG; ++h) {
-        if (h >= gq) break;
+    for (int h = 0; h < GQ; ++h) {
         float v = ev[h];
 #pragma unroll
         for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
         if (lane == 0) s_red[h][warp] = v;
     }
-    // PV over this warp's 32 slots, in order
-    float acc[ATT_MAXG][4];
+    __syncwarp();
+    // PV: this warp's 32 slots in order, V segments fetched 8 slots at a time
+    float acc[GQ][4];
 #pragma unroll
-    for (int h = 0; h < ATT_MAXG; ++h)
+    for (int h = 0; h < GQ; ++h)
 #pragma unroll
         for (int k = 0; k < 4; ++k) acc[h][k] = 0.0f;
-    __syncwarp();
-    for (int jj = 0; jj < 32; ++jj) {
-        const int jv = c * ATT_CHUNK + warp * 32 + jj;
-        if (jv >= L) break;
-        const uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vc + (static_cast<int64_t>(g) * max_ctx + jv) * 128 + 4 * lane));
-        const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
-        const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
-        const float vf[4] = {v01.x, v01.y, v23.x, v23.y};
+    const int j0 = c * ATT_CHUNK + warp * 32;
+    const int nv = max(0, min(32, L - j0));
+    const __half *vbase = vc + (static_cast<int64_t>(g) * max_ctx + j0) * 128 + 4 * lane;
 #pragma unroll
-        for (int h = 0; h < ATT_MAXG; ++h) {
-            if (h >= gq) break;
-            const float e = s_e[h][warp * 32 + jj];
+    for (int g8 = 0; g8 < 4; ++g8) {
+        if (g8 * 8 >= nv) break;
+        uint2 vv[8];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) acc[h][k] = __fmaf_rn(e, vf[k], acc[h][k]);
+        for (int u = 0; u < 8; ++u)
+            if (g8 * 8 + u < nv) vv[u] = __ldg(reinterpret_cast<const uint2 *>(vbase + (g8 * 8 + u) * 128));
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (g8 * 8 + u < nv) {
+                const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vv[u].x));
+                const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vv[u].y));
+                const float vf[4] = {v01.x, v01.y, v23.x, v23.y};
+#pragma unroll
+                for (int h = 0; h < GQ; ++h) {
+                    const float e = s_e[h][warp * 32 + g8 * 8 + u];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) acc[h][k] = __fmaf_rn(e, vf[k], acc[h][k]);
+                }
+            }
         }
     }
 #pragma unroll
-    for (int h = 0; h < ATT_MAXG; ++h) {
-        if (h >= gq) break;
+    for (int h = 0; h < GQ; ++h)
         *reinterpret_cast<float4 *>(&s_o[warp][h][4 * lane]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-    }
     __syncthreads();
-    for (int i = t; i < gq * 128; i += 256) {
+    for (int i = t; i < GQ * 128; i += 256) {
         const int h = i / 128, d = i % 128;
         float o = s_o[0][h][d];
 #pragma unroll
         for (int w = 1; w < 8; ++w) o = __fadd_rn(o, s_o[w][h][d]);
-        part_o[(static_cast<int64_t>(g * gq + h) * max_chunks + c) * 128 + d] = o;
+        part_o[(static_cast<int64_t>(g * GQ + h) * max_chunks + c) * 128 + d] = o;
     }
-    if (t < gq) {
+    if (t < GQ) {
         float l = s_red[t][0];
 #pragma unroll
         for (int w = 1; w < 8; ++w) l = __fadd_rn(l, s_red[t][w]);
-        part_l[static_cast<int64_t>(g * gq + t) * max_chunks + c] = l;
+        part_l[static_cast<int64_t>(g * GQ + t) * max_chunks + c] = l;
     }
 }
 
@@ -393,6 +409,27 @@ __global__ void __launch_bounds__(1024)
     }
 }
 
+// Finish of the argmax fused into the output MMVQ: decode the winning key
+// (ties already resolved to the lowest row), reset it for the next step,
+// record the pick, append it past the prompt, advance *pos.
+__global__ void argmax_finish_kernel(unsigned long long *__restrict__ key,
+                                     int32_t *__restrict__ tokens, int32_t *__restrict__ picks,
+                                     int32_t *__restrict__ pos_p,
+                                     const int32_t *__restrict__ n_prompt_p, int max_ctx) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x != 0) return;
+    const unsigned long long k = *key;
+    *key = 0ull;
+    const int bi = static_cast<int>(0xFFFFFFFFu - static_cast<unsigned>(k & 0xFFFFFFFFull));
+    const int p = *pos_p;
+    if (p < max_ctx) {  // the host never steps past max_ctx
+        picks[p] = bi;
+        if (p + 1 >= *n_prompt_p) tokens[p + 1] = bi;
+        *pos_p = p + 1;
+    }
+}
+
 // ----------------------------------------------------------- launchers ---
 static cudaLaunchAttribute pdl_attr() {
     cudaLaunchAttribute a;
@@ -431,7 +468,7 @@ cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const fl
                                              static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
-    return launch_pdl(residual_rmsnorm_quant_kernel, dim3(ncols), dim3(RMS_THREADS), smem, s, pdl,
+    return launch_pdl(residual_rmsnorm_quant_kernel, dim3(ncols), dim3(RES_THREADS), smem, s, pdl,
                       h, ds, w, eps, static_cast<block_q8_1 *>(y), K);
 }
 
@@ -452,15 +489,29 @@ cudaError_t launch_attention(const float *q, const void *kc, const void *vc, con
     const int gq = n_heads / n_kv;
     if (gq > ATT_MAXG || n_heads % n_kv) return cudaErrorInvalidValue;
     const int max_chunks = (max_ctx + ATT_CHUNK - 1) / ATT_CHUNK;
-    cudaError_t e = launch_pdl(attention_chunk_kernel, dim3(n_kv, max_chunks), dim3(256), 0, s,
-                               pdl, q, static_cast<const __half *>(kc),
-                               static_cast<const __half *>(vc), pos, scale, gq, max_ctx,
-                               max_chunks, part_m, part_l, part_o);
+    const dim3 grid(n_kv, max_chunks);
+    const __half *k = static_cast<const __half *>(kc);
+    const __half *v = static_cast<const __half *>(vc);
+    cudaError_t e;
+    switch (gq) {
+        case 1: e = launch_pdl(attention_chunk_kernel<1>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, max_chunks, part_m, part_l, part_o); break;
+        case 2: e = launch_pdl(attention_chunk_kernel<2>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, max_chunks, part_m, part_l, part_o); break;
+        case 4: e = launch_pdl(attention_chunk_kernel<4>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, max_chunks, part_m, part_l, part_o); break;
+        case 8: e = launch_pdl(attention_chunk_kernel<8>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, max_chunks, part_m, part_l, part_o); break;
+        default: return cudaErrorInvalidValue;
+    }
     if (e != cudaSuccess) return e;
     return launch_pdl(attention_merge_quant_kernel, dim3((n_heads + 7) / 8), dim3(256), 0, s, pdl,
                       static_cast<const float *>(part_m), static_cast<const float *>(part_l),
                       static_cast<const float *>(part_o), pos, n_heads, max_chunks, out_f32,
                       static_cast<block_q8_1 *>(out_q8));
+}
+
+cudaError_t launch_argmax_finish(unsigned long long *key, int32_t *tokens, int32_t *picks,
+                                 int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
+                                 cudaStream_t s) {
+    return launch_pdl(argmax_finish_kernel, dim3(1), dim3(32), 0, s, pdl, key, tokens, picks, pos,
+                      n_prompt, max_ctx);
 }
 
 cudaError_t launch_argmax_advance(const float *logits, int n, int32_t *tokens, int32_t *picks,

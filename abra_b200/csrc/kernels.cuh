@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace abra {
 
 // ---------------------------------------------------------------- MMVQ ---
@@ -25,12 +27,30 @@ enum : int {
 };
 
 // w2 != nullptr selects the fused gate/up form: y = (w2 x) * silu(w x).
+// amax != nullptr: also atomicMax an argmax key (value, row) per column into
+// amax[c] (keys must start at 0).
 cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2,
                             const void *x_q8, float *y, int64_t N, int64_t K, int ncols,
-                            int64_t ldy, int flags, cudaStream_t stream);
+                            int64_t ldy, int flags, cudaStream_t stream,
+                            unsigned long long *amax = nullptr);
+// Fused input of launch_mmvq_q4k_xin: x = h_in + tree(deltas) (written to
+// h_out when not null), quantized as Q8_1 of RMSNorm(x) * norm_w.
+struct MmvqXin {
+    const float *h_in;
+    float *h_out;
+    DeltaSet deltas;
+    const float *norm_w;
+    float eps;
+};
+// Batch-1 MMVQ whose activation is built in each CTA from the fp32 residual
+// stream (residual add + RMSNorm + Q8_1 fused into the prologue).
+cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void *w2,
+                                const MmvqXin &xin, float *y, int64_t N, int64_t K, int flags,
+                                cudaStream_t stream, unsigned long long *amax = nullptr);
+
 // Sets the kernel attributes a later launch of this candidate needs (done
 // outside stream capture).
-cudaError_t prepare_mmvq(const MmvqConfig &cfg, int ncols, int nmat);
+cudaError_t prepare_mmvq(const MmvqConfig &cfg, int ncols, int nmat, bool xin = false);
 
 // Debug: same kernel, additionally storing the exact int32 partials
 // P[c][r][b][s] and M[c][b][s].

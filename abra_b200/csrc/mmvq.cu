@@ -65,7 +65,10 @@ static const MmvqTable *table_for(int ncols) {
 
 static int ks_index(int ks) { return ks == 1 ? 0 : ks == 2 ? 1 : ks == 4 ? 2 : ks == 8 ? 3 : -1; }
 
-constexpr int kMaxSmem = 227 * 1024;
+// Dynamic shared memory a plan may use: the 227 KiB opt-in limit less room
+// for the kernel's static shared memory (a few bytes of argmax keys).
+constexpr int kOptinSmem = 227 * 1024;
+constexpr int kMaxSmem = kOptinSmem - 1024;
 
 static cudaError_t ensure_smem_attr(MmvqFn fn) {
     // Raise the dynamic shared-memory limit once per (kernel, device).
@@ -78,8 +81,12 @@ static cudaError_t ensure_smem_attr(MmvqFn fn) {
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < ndone; ++i)
         if (done[i] == reinterpret_cast<const void *>(fn) && done_dev[i] == dev) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void *>(fn),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(fn));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(reinterpret_cast<const void *>(fn),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kOptinSmem - static_cast<int>(fa.sharedSizeBytes));
     if (e != cudaSuccess) return e;
     if (ndone < 1024) {
         done[ndone] = reinterpret_cast<const void *>(fn);
@@ -94,7 +101,7 @@ struct MmvqPlan {
 };
 
 static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int nmat,
-                      MmvqPlan &pl) {
+                      MmvqPlan &pl, bool xin = false) {
     const int ks = cfg.ks;
     const bool staged = cfg.mode != MODE_DIRECT;
     const int nsl = 8 / ks;
@@ -123,7 +130,7 @@ static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int 
         nstage = want >= units ? units : (want / W > 0 ? want / W * W : (units < W ? units : W));
     }
     for (;;) {
-        const MmvqLayout L = mmvq_layout(ncols, ks, W, nsb, nstage, pitch, nmat, staged);
+        const MmvqLayout L = mmvq_layout(ncols, ks, W, nsb, nstage, pitch, nmat, staged, xin);
         if (L.bytes <= kMaxSmem) {
             pl.nstage = nstage;
             pl.smem = L.bytes;
@@ -160,7 +167,8 @@ static cudaError_t launch_plan(MmvqFn fn, const MmvqPlan &pl, bool pdl, MmvqPara
 
 cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2,
                             const void *x_q8, float *y, int64_t N, int64_t K, int ncols,
-                            int64_t ldy, int flags, cudaStream_t stream) {
+                            int64_t ldy, int flags, cudaStream_t stream,
+                            unsigned long long *amax) {
     const int nsb = static_cast<int>(K / QK_K);
     const int nmat = w2 ? 2 : 1;
     const MmvqTable *t = table_for(ncols);
@@ -178,14 +186,43 @@ cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2
     prm.N = static_cast<int>(N);
     prm.nsb = nsb;
     prm.ldy = ldy;
+    prm.amax = amax;
     return launch_plan(fn, pl, (flags & MMVQ_PDL) != 0, prm, stream);
 }
 
-cudaError_t prepare_mmvq(const MmvqConfig &cfg, int ncols, int nmat) {
+cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void *w2,
+                                const MmvqXin &xin, float *y, int64_t N, int64_t K, int flags,
+                                cudaStream_t stream, unsigned long long *amax) {
+    const int nsb = static_cast<int>(K / QK_K);
+    const int nmat = w2 ? 2 : 1;
+    const int ki = ks_index(cfg.ks);
+    if (ki < 0) return cudaErrorInvalidValue;
+    MmvqFn fn = mmvq_table_c1().xin[cfg.mode][ki][nmat - 1];
+    if (!fn || !xin.h_in || !xin.norm_w) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(xin.norm_w) & 15) return cudaErrorInvalidValue;  // float4 loads
+    MmvqPlan pl;
+    if (!plan_mmvq(cfg, N, nsb, 1, nmat, pl, true)) return cudaErrorInvalidConfiguration;
+    MmvqParams prm = {};
+    prm.W[0] = static_cast<const uint8_t *>(w);
+    prm.W[1] = static_cast<const uint8_t *>(w2);
+    prm.Y = y;
+    prm.N = static_cast<int>(N);
+    prm.nsb = nsb;
+    prm.ldy = N;
+    prm.amax = amax;
+    prm.h_in = xin.h_in;
+    prm.h_out = xin.h_out;
+    prm.deltas = xin.deltas;
+    prm.norm_w = xin.norm_w;
+    prm.eps = xin.eps;
+    return launch_plan(fn, pl, (flags & MMVQ_PDL) != 0, prm, stream);
+}
+
+cudaError_t prepare_mmvq(const MmvqConfig &cfg, int ncols, int nmat, bool xin) {
     const MmvqTable *t = table_for(ncols);
     const int ki = ks_index(cfg.ks);
     if (!t || ki < 0 || nmat < 1 || nmat > 2) return cudaErrorInvalidValue;
-    MmvqFn fn = t->fn[cfg.mode][ki][nmat - 1];
+    MmvqFn fn = xin ? t->xin[cfg.mode][ki][nmat - 1] : t->fn[cfg.mode][ki][nmat - 1];
     return fn ? ensure_smem_attr(fn) : cudaErrorInvalidValue;
 }
 

@@ -45,18 +45,36 @@ struct MmvqParams {
     int N, nsb;
     int64_t ldy;
     int rg_total, nstage, pitch;
-    int32_t *P, *M;  // debug partials (EMIT_P)
+    int32_t *P, *M;              // debug partials (EMIT_P)
+    unsigned long long *amax;    // optional per-column argmax keys (argmax_key)
+    // fp32 input with the residual add + RMSNorm + Q8_1 fused in (XIN):
+    // x = h_in + tree(deltas), written to h_out by CTA 0; every CTA quantizes
+    // (x * r) * norm_w in its own shared memory.
+    const float *h_in;
+    float *h_out;
+    DeltaSet deltas;
+    const float *norm_w;
+    float eps;
 };
+
+// Order-preserving 64-bit key of (value, row): the float's bits mapped to an
+// unsigned order in the high word, ~row in the low word, so the largest key
+// is the largest value and, among equal values, the lowest row.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+    unsigned u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<unsigned>(row));
+}
 
 __host__ __device__ __forceinline__ int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
 struct MmvqLayout {
-    int off_full, off_empty, off_red, off_qs, off_d8, off_A, off_stage, bytes;
+    int off_full, off_empty, off_red, off_qs, off_d8, off_A, off_x, off_stage, bytes;
 };
 
 __host__ __device__ __forceinline__ MmvqLayout mmvq_layout(int ncols, int ks, int ncw, int nsb,
                                                            int nstage, int pitch, int nmat,
-                                                           bool staged) {
+                                                           bool staged, bool xin = false) {
     MmvqLayout L;
     L.off_full = 0;
     L.off_empty = 8 * nstage;
@@ -69,6 +87,8 @@ __host__ __device__ __forceinline__ MmvqLayout mmvq_layout(int ncols, int ks, in
     o = L.off_d8 + ncols * nsb * 8 * 4;
     L.off_A = o;
     o += ncols * nsb * 8 * 4;
+    L.off_x = align_up(o, 16);
+    o = L.off_x + (xin ? 2 * nsb * 256 * 4 : 0);  // x and the norm weights (batch 1)
     L.off_stage = align_up(o, 128);
     L.bytes = L.off_stage + (staged ? nstage * 8 * nmat * pitch : 0);
     return L;
@@ -185,7 +205,7 @@ __device__ __forceinline__ float tree_sum(const float *a) {
     }
 }
 
-template <int NCOLS, int KS, int NCW, int MODE, int NMAT, bool EMIT_P>
+template <int NCOLS, int KS, int NCW, int MODE, int NMAT, bool EMIT_P, bool XIN = false>
 __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MODE == MODE_DIRECT ? 2 : 1)
     mmvq_q4k_kernel(const MmvqParams prm) {
     constexpr int NSL = 8 / KS;     // canonical slices per k-part
@@ -193,9 +213,13 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
     constexpr bool STAGED = MODE != MODE_DIRECT;
     static_assert(NCW % KS == 0, "consumer warps must be a multiple of KS");
     static_assert(MODE != MODE_TMA_WHOLE || KS == 1, "whole-unit copies need KS == 1");
+    static_assert(!XIN || NCW * 32 == 256, "the fused RMSNorm uses the canonical 256 lanes");
+    static_assert(!XIN || NCOLS == 1, "the fused RMSNorm input is batch 1");
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ unsigned long long s_amax[NCOLS];
+    __shared__ float s_nred[1][8];
     const int N = prm.N, nsb = prm.nsb, nstage = prm.nstage, pitch = prm.pitch;
-    const MmvqLayout L = mmvq_layout(NCOLS, KS, NCW, nsb, nstage, pitch, NMAT, STAGED);
+    const MmvqLayout L = mmvq_layout(NCOLS, KS, NCW, nsb, nstage, pitch, NMAT, STAGED, XIN);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.off_full);
     uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L.off_empty);
     float *red = reinterpret_cast<float *>(smem + L.off_red);
@@ -260,9 +284,94 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
     }
 
     // -------------------------------------------------------- consumers ---
-    pdl_wait();  // x is produced by the preceding kernel
     const int nblk = nsb * 8;
-    for (int i = threadIdx.x; i < NCOLS * nblk; i += NCW * 32) {
+    if constexpr (XIN) {
+        // the norm weights are immutable: stage them before waiting on the
+        // kernel that produced the residual stream
+        const int K = nsb * QK_K;
+        float *s_w = reinterpret_cast<float *>(smem + L.off_x) + K;
+        for (int i = threadIdx.x * 4; i < K; i += NCW * 32 * 4)
+            *reinterpret_cast<float4 *>(s_w + i) = __ldg(reinterpret_cast<const float4 *>(prm.norm_w + i));
+    }
+    pdl_wait();  // x is produced by the preceding kernel
+    if constexpr (XIN) {
+        // residual add + RMSNorm + Q8_1 of the fp32 input, in this CTA's shared
+        // memory, in the canonical order: thread t sums x[t + 256 k]^2 with
+        // fmaf in k order, xor butterfly 16..1, the eight warp sums in order;
+        // r = 1 / sqrt(sum / K + eps); then (x * r) * w and the reference Q8_1
+        // rounding per 32-block.  Loads are issued eight at a time.
+        const int K = nsb * QK_K;
+        float *s_x = reinterpret_cast<float *>(smem + L.off_x);
+        const float *s_w = s_x + K;
+        const int t = threadIdx.x;
+        float acc = 0.0f;
+        for (int i0 = t; i0 < K; i0 += 256 * 8) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int i = i0 + k * 256;
+                v[k] = i < K ? prm.h_in[i] : 0.0f;
+            }
+            if (prm.deltas.G > 0) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int i = i0 + k * 256;
+                    if (i < K) v[k] = __fadd_rn(v[k], delta_tree(prm.deltas, i));
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int i = i0 + k * 256;
+                if (i < K) {
+                    if (blockIdx.x == 0 && prm.h_out) prm.h_out[i] = v[k];
+                    s_x[i] = v[k];
+                    acc = __fmaf_rn(v[k], v[k], acc);
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+        if (lane == 0) s_nred[0][warp] = acc;
+        named_bar_sync(1, NCW * 32);
+        float total = s_nred[0][0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) total = __fadd_rn(total, s_nred[0][w]);
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), prm.eps)));
+        // eight lanes per 32-block, four elements each; a warp covers four
+        // consecutive blocks (nblk is a multiple of 8, so all four exist)
+        const int sub = lane & 7;
+        for (int b0 = warp * 4; b0 < nblk; b0 += NCW * 4) {
+            const int i = b0 + (lane >> 3);
+            const float4 xv = *reinterpret_cast<const float4 *>(s_x + i * QK8_1 + sub * 4);
+            const float4 wv = *reinterpret_cast<const float4 *>(s_w + i * QK8_1 + sub * 4);
+            const float x0 = __fmul_rn(__fmul_rn(xv.x, r), wv.x);
+            const float x1 = __fmul_rn(__fmul_rn(xv.y, r), wv.y);
+            const float x2 = __fmul_rn(__fmul_rn(xv.z, r), wv.z);
+            const float x3 = __fmul_rn(__fmul_rn(xv.w, r), wv.w);
+            float amax = fmaxf(fmaxf(fabsf(x0), fabsf(x1)), fmaxf(fabsf(x2), fabsf(x3)));
+            amax = fmaxf(0.0f, amax);
+#pragma unroll
+            for (int m = 4; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            const int q0 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x0, id)))));
+            const int q1 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x1, id)))));
+            const int q2 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x2, id)))));
+            const int q3 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x3, id)))));
+            int sum = (q0 + q1) + (q2 + q3);
+#pragma unroll
+            for (int m = 4; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+            *reinterpret_cast<uint32_t *>(aq + i * 32 + sub * 4) =
+                (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
+                ((static_cast<uint32_t>(q2) & 0xffu) << 16) | (static_cast<uint32_t>(q3) << 24);
+            if (sub == 0) {
+                const float d8 = __half2float(__float2half_rn(d));
+                ad8[i] = d8;
+                aA[i] = __fmul_rn(d8, __int2float_rn(sum));
+            }
+        }
+    }
+    for (int i = threadIdx.x; i < (XIN ? 0 : NCOLS * nblk); i += NCW * 32) {
         const int c = i / nblk, blk = i - c * nblk;
         const uint32_t *src = reinterpret_cast<const uint32_t *>(
             prm.X + (static_cast<int64_t>(c) * nblk + blk) * Q81_BYTES);
@@ -283,6 +392,7 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
             if (blockIdx.x == 0) prm.M[i] = msum;
         }
     }
+    if (threadIdx.x < NCOLS) s_amax[threadIdx.x] = 0ull;
     named_bar_sync(1, NCW * 32);
 
     const int grp = warp / KS, j = warp % KS;
@@ -393,14 +503,27 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
                     }
             }
         }
-        if (j == 0 && p == 0 && row < N) {
+        if (j == 0 && p == 0) {
 #pragma unroll
             for (int c = 0; c < NCOLS; ++c) {
                 float yv = sub[0][c];
                 if constexpr (NMAT == 2) yv = __fmul_rn(sub[1][c], abra_silu(sub[0][c]));
-                prm.Y[c * prm.ldy + row] = yv;
+                if (row < N) prm.Y[c * prm.ldy + row] = yv;
+                if (prm.amax) {  // lanes 0..7 hold the unit's eight rows
+                    unsigned long long key = row < N ? argmax_key(yv, row) : 0ull;
+#pragma unroll
+                    for (int m = 1; m < 8; m <<= 1) {
+                        const unsigned long long o = __shfl_xor_sync(0x000000ffu, key, m);
+                        key = o > key ? o : key;
+                    }
+                    if (g == 0) atomicMax(&s_amax[c], key);
+                }
             }
         }
+    }
+    if (prm.amax) {
+        named_bar_sync(1, NCW * 32);
+        if (threadIdx.x < NCOLS) atomicMax(&prm.amax[threadIdx.x], s_amax[threadIdx.x]);
     }
 }
 
@@ -411,6 +534,7 @@ using MmvqFn = void (*)(const MmvqParams);
 struct MmvqTable {
     MmvqFn fn[3][4][2];
     MmvqFn partials[3];  // MODE_TMA_ROWS, NMAT 1, KS 1/2/4, EMIT_P
+    MmvqFn xin[3][4][2]; // fused residual + RMSNorm + Q8_1 input (batch 1 only)
 };
 
 #define ABRA_MMVQ_NCW 8
@@ -441,6 +565,26 @@ MmvqTable make_mmvq_table() {
         t.partials[0] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_ROWS, 1, true>;
         t.partials[1] = mmvq_q4k_kernel<NC, 2, W, MODE_TMA_ROWS, 1, true>;
         t.partials[2] = mmvq_q4k_kernel<NC, 4, W, MODE_TMA_ROWS, 1, true>;
+    }
+    if constexpr (NC == 1) {
+        t.xin[MODE_TMA_ROWS][0][0] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_ROWS, 1, false, true>;
+        t.xin[MODE_TMA_ROWS][1][0] = mmvq_q4k_kernel<NC, 2, W, MODE_TMA_ROWS, 1, false, true>;
+        t.xin[MODE_TMA_ROWS][2][0] = mmvq_q4k_kernel<NC, 4, W, MODE_TMA_ROWS, 1, false, true>;
+        t.xin[MODE_TMA_ROWS][3][0] = mmvq_q4k_kernel<NC, 8, W, MODE_TMA_ROWS, 1, false, true>;
+        t.xin[MODE_TMA_ROWS][0][1] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_ROWS, 2, false, true>;
+        t.xin[MODE_TMA_ROWS][1][1] = mmvq_q4k_kernel<NC, 2, W, MODE_TMA_ROWS, 2, false, true>;
+        t.xin[MODE_TMA_ROWS][2][1] = mmvq_q4k_kernel<NC, 4, W, MODE_TMA_ROWS, 2, false, true>;
+        t.xin[MODE_TMA_ROWS][3][1] = mmvq_q4k_kernel<NC, 8, W, MODE_TMA_ROWS, 2, false, true>;
+        t.xin[MODE_TMA_WHOLE][0][0] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_WHOLE, 1, false, true>;
+        t.xin[MODE_TMA_WHOLE][0][1] = mmvq_q4k_kernel<NC, 1, W, MODE_TMA_WHOLE, 2, false, true>;
+        t.xin[MODE_DIRECT][0][0] = mmvq_q4k_kernel<NC, 1, W, MODE_DIRECT, 1, false, true>;
+        t.xin[MODE_DIRECT][1][0] = mmvq_q4k_kernel<NC, 2, W, MODE_DIRECT, 1, false, true>;
+        t.xin[MODE_DIRECT][2][0] = mmvq_q4k_kernel<NC, 4, W, MODE_DIRECT, 1, false, true>;
+        t.xin[MODE_DIRECT][3][0] = mmvq_q4k_kernel<NC, 8, W, MODE_DIRECT, 1, false, true>;
+        t.xin[MODE_DIRECT][0][1] = mmvq_q4k_kernel<NC, 1, W, MODE_DIRECT, 2, false, true>;
+        t.xin[MODE_DIRECT][1][1] = mmvq_q4k_kernel<NC, 2, W, MODE_DIRECT, 2, false, true>;
+        t.xin[MODE_DIRECT][2][1] = mmvq_q4k_kernel<NC, 4, W, MODE_DIRECT, 2, false, true>;
+        t.xin[MODE_DIRECT][3][1] = mmvq_q4k_kernel<NC, 8, W, MODE_DIRECT, 2, false, true>;
     }
     return t;
 }

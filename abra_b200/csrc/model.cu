@@ -46,14 +46,17 @@ struct Model {
     std::vector<LayerW> layers;
     __half *kc = nullptr, *vc = nullptr;
     float *rope = nullptr;
-    float *h, *delta, *qkv, *q, *att, *part_m, *part_l, *part_o, *act, *logits;
+    float *h, *h2;  // residual stream, ping-pong: each fused MMVQ reads one, writes the other
+    float *delta, *qkv, *q, *att, *part_m, *part_l, *part_o, *act, *logits;
     uint8_t *xq, *oq, *aq;
     int32_t *tokens, *picks, *pos, *nprompt;
+    unsigned long long *amax = nullptr;  // argmax key of the output MMVQ
     int max_chunks = 0;
     cudaStream_t stream = nullptr;
     cudaGraphExec_t graph = nullptr;
     size_t weight_bytes = 0, kv_bytes = 0;
-    int32_t host_pos = 0;  // position after the queued steps (mirrors *pos)
+    int32_t host_pos = 0;      // position after the queued steps (mirrors *pos)
+    int32_t *pinned = nullptr; // 2 pinned ints for the streaming loop
 };
 
 static uint64_t tensor_id(int layer, int which) {
@@ -134,6 +137,7 @@ static cudaError_t build(Model &m) {
     int64_t mx = c.hidden > c.ffn ? c.hidden : c.ffn;
     if (qd > mx) mx = qd;
     TRY(alloc(m, &m.h, c.hidden * 4));
+    TRY(alloc(m, &m.h2, c.hidden * 4));
     TRY(alloc(m, &m.delta, c.hidden * 4));
     TRY(alloc(m, &m.qkv, qkv_rows * 4));
     TRY(alloc(m, &m.q, qd * 4));
@@ -150,6 +154,8 @@ static cudaError_t build(Model &m) {
     TRY(alloc(m, &m.picks, (c.max_ctx + 1) * 4));
     TRY(alloc(m, &m.pos, 4));
     TRY(alloc(m, &m.nprompt, 4));
+    TRY(alloc(m, &m.amax, 8));
+    TRY(cudaMemsetAsync(m.amax, 0, 8, st));
     TRY(cudaMemsetAsync(m.tokens, 0, (c.max_ctx + 1) * 4, st));
     TRY(cudaMemsetAsync(m.picks, 0, (c.max_ctx + 1) * 4, st));
     TRY(cudaMemsetAsync(m.pos, 0, 4, st));
@@ -158,11 +164,12 @@ static cudaError_t build(Model &m) {
 }
 
 static cudaError_t mmvq(const Model &m, const void *w, const void *w2, const void *x, float *y,
-                        int64_t N, int64_t K, bool pdl, cudaStream_t st) {
+                        int64_t N, int64_t K, bool pdl, cudaStream_t st,
+                        unsigned long long *amax = nullptr) {
     const int id = abra_tune_get(N, K, 1, w2 ? 2 : 1);
     const MmvqConfig *cfg = mmvq_candidate_by_id(id);
     if (!cfg) return cudaErrorInvalidValue;
-    return launch_mmvq_q4k(*cfg, w, w2, x, y, N, K, 1, N, pdl ? MMVQ_PDL : 0, st);
+    return launch_mmvq_q4k(*cfg, w, w2, x, y, N, K, 1, N, pdl ? MMVQ_PDL : 0, st, amax);
 }
 
 // The decode step for the token at tokens[*pos] (recorded into the graph).
@@ -177,12 +184,23 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
     none.G = 0;
     one.p[0] = m.delta;
     one.G = 1;
-    TRY(launch_embed(m.embd, c.hidden, m.tokens, m.pos, m.h, pdl, st));
+    // residual stream ping-pong: every MMVQ with a fused RMSNorm prologue
+    // reads h[cur] (+ the pending delta) and CTA 0 writes the sum to h[cur^1]
+    float *h[2] = {m.h, m.h2};
+    int cur = 0;
+    auto fused = [&](const void *w, const void *w2, const DeltaSet &ds, const float *norm,
+                     float *y, int64_t N, unsigned long long *amax) -> cudaError_t {
+        const MmvqConfig *cfg = mmvq_candidate_by_id(abra_tune_get(N, c.hidden, 1, w2 ? 2 : 1));
+        if (!cfg) return cudaErrorInvalidValue;
+        MmvqXin xin = {h[cur], h[cur ^ 1], ds, norm, c.eps};
+        cur ^= 1;
+        return launch_mmvq_q4k_xin(*cfg, w, w2, xin, y, N, c.hidden, pdl ? MMVQ_PDL : 0, st, amax);
+    };
+    TRY(launch_embed(m.embd, c.hidden, m.tokens, m.pos, h[cur], pdl, st));
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW &y = m.layers[l];
-        TRY(launch_residual_rmsnorm_quant(m.h, l == 0 ? none : one, y.attn_norm, c.eps, m.xq,
-                                          c.hidden, 1, pdl, st));
-        TRY(mmvq(m, y.wqkv, nullptr, m.xq, m.qkv, qkv_rows, c.hidden, pdl, st));
+        // residual + RMSNorm + Q8_1 fused into the q|k|v MMVQ
+        TRY(fused(y.wqkv, nullptr, l == 0 ? none : one, y.attn_norm, m.qkv, qkv_rows, nullptr));
         TRY(launch_qk_norm_rope_kv(m.qkv, y.q_norm, y.k_norm, c.eps, m.rope, m.pos, m.q,
                                    m.kc + l * kv_layer, m.vc + l * kv_layer, c.n_heads,
                                    c.n_kv_heads, c.max_ctx, pdl, st));
@@ -190,28 +208,29 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
                              c.n_heads, c.n_kv_heads, c.max_ctx, m.part_m, m.part_l, m.part_o,
                              m.att, m.oq, pdl, st));
         TRY(mmvq(m, y.wo, nullptr, m.oq, m.delta, c.hidden, qd, pdl, st));
-        TRY(launch_residual_rmsnorm_quant(m.h, one, y.ffn_norm, c.eps, m.xq, c.hidden, 1, pdl, st));
-        TRY(mmvq(m, y.wgate, y.wup, m.xq, m.act, c.ffn, c.hidden, pdl, st));
+        // residual + RMSNorm + Q8_1 fused into the gate/up SwiGLU MMVQ
+        TRY(fused(y.wgate, y.wup, one, y.ffn_norm, m.act, c.ffn, nullptr));
         TRY(launch_quantize_q8_1(m.act, m.aq, c.ffn, 1, st));
         TRY(mmvq(m, y.wdown, nullptr, m.aq, m.delta, c.hidden, c.ffn, pdl, st));
     }
-    TRY(launch_residual_rmsnorm_quant(m.h, c.n_layers > 0 ? one : none, m.out_norm, c.eps, m.xq,
-                                      c.hidden, 1, pdl, st));
-    TRY(mmvq(m, m.embd, nullptr, m.xq, m.logits, c.vocab, c.hidden, pdl, st));
-    return launch_argmax_advance(m.logits, c.vocab, m.tokens, m.picks, m.pos, m.nprompt,
-                                 c.max_ctx, pdl, st);
+    // final residual + RMSNorm fused into the tied output MMVQ, which also
+    // reduces the greedy argmax (ties to the lowest id)
+    TRY(fused(m.embd, nullptr, c.n_layers > 0 ? one : none, m.out_norm, m.logits, c.vocab, m.amax));
+    return launch_argmax_finish(m.amax, m.tokens, m.picks, m.pos, m.nprompt, c.max_ctx, pdl, st);
 }
 
 static cudaError_t prepare(const Model &m) {
     const abra_model_config &c = m.cfg;
     const int64_t qkv_rows = static_cast<int64_t>(c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
     const int64_t qd = static_cast<int64_t>(c.n_heads) * c.head_dim;
-    const int64_t shapes[5][3] = {{qkv_rows, c.hidden, 1}, {c.hidden, qd, 1}, {c.ffn, c.hidden, 2},
-                                  {c.hidden, c.ffn, 1}, {c.vocab, c.hidden, 1}};
+    // {N, K, nmat, fused RMSNorm input}
+    const int64_t shapes[5][4] = {{qkv_rows, c.hidden, 1, 1}, {c.hidden, qd, 1, 0},
+                                  {c.ffn, c.hidden, 2, 1}, {c.hidden, c.ffn, 1, 0},
+                                  {c.vocab, c.hidden, 1, 1}};
     for (const auto &sh : shapes) {
         const MmvqConfig *cfg = mmvq_candidate_by_id(abra_tune_get(sh[0], sh[1], 1, static_cast<int>(sh[2])));
         if (!cfg) return cudaErrorInvalidValue;
-        TRY(prepare_mmvq(*cfg, 1, static_cast<int>(sh[2])));
+        TRY(prepare_mmvq(*cfg, 1, static_cast<int>(sh[2]), sh[3] != 0));
     }
     return cudaSuccess;
 }
@@ -295,6 +314,7 @@ int abra_model_destroy(void *model) {
     if (!m) return ABRA_OK;
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->pinned) cudaFreeHost(m->pinned);
     for (void *p : m->allocs) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -367,6 +387,37 @@ int abra_model_generate(void *model, const int32_t *prompt, int32_t n_prompt, in
     if (rc) return rc;
     std::memcpy(out, all.data() + n_prompt, n_gen * 4);
     return ABRA_OK;
+}
+
+int abra_model_decode_streaming(void *model, int32_t n, int32_t *out) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || !out || n < 1) return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
+    if (static_cast<int64_t>(m->host_pos) + n > m->cfg.max_ctx)
+        return model_fail(ABRA_E_INVALID, "steps would pass max_ctx", cudaSuccess);
+    cudaError_t e = abra::capture(*m);
+    if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "graph capture", e);
+    if (!m->pinned) {
+        e = cudaHostAlloc(reinterpret_cast<void **>(&m->pinned), 2 * sizeof(int32_t), cudaHostAllocDefault);
+        if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "pinned buffer", e);
+    }
+    int32_t *in = m->pinned, *pick = m->pinned + 1;
+    // the token the next step consumes
+    e = cudaMemcpyAsync(in, m->tokens + m->host_pos, 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    for (int32_t i = 0; i < n && e == cudaSuccess; ++i) {
+        const int32_t p = m->host_pos;
+        e = cudaMemcpyAsync(m->tokens + p, in, 4, cudaMemcpyHostToDevice, m->stream);
+        if (e == cudaSuccess)
+            e = m->graph ? cudaGraphLaunch(m->graph, m->stream) : abra::record_step(*m, m->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(pick, m->picks + p, 4, cudaMemcpyDeviceToHost, m->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+        if (e == cudaSuccess) {
+            out[i] = *pick;
+            *in = *pick;
+            m->host_pos = p + 1;
+        }
+    }
+    return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "streaming decode", e);
 }
 
 int abra_model_info(void *model, void **stream, uint64_t *weight_bytes, uint64_t *kv_bytes) {

@@ -100,6 +100,13 @@ class DecodeModel:
                                             out.ctypes.data), "abra_model_generate")
         return out
 
+    def decode_streaming(self, n: int) -> np.ndarray:
+        """Serving loop: one token at a time with a host round trip each."""
+        out = np.empty(n, dtype=np.int32)
+        _check(_lib.lib.abra_model_decode_streaming(self.handle, n, out.ctypes.data),
+               "abra_model_decode_streaming")
+        return out
+
     def info(self) -> dict:
         st, wb, kb = C.c_void_p(), C.c_uint64(), C.c_uint64()
         _check(_lib.lib.abra_model_info(self.handle, C.byref(st), C.byref(wb), C.byref(kb)),

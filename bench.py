@@ -455,26 +455,152 @@ def run_case(a):
     return 0
 
 
+DECODE_WORKLOAD = "qwen3_4b_q4k_decode_tg"
+PROMPT = 16
+
+
+def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, seed: int = 0):
+    """One decode measurement: a model sized for the prompt + depth prefix +
+    warm-up + timed tokens; the prefix is fed untimed (token by token through
+    the same step), then ``warmup`` untimed tokens, then ``steps`` timed
+    tokens (one CUDA graph replay each), timed with CUDA events on the model's
+    stream.  With ``streaming`` the timed tokens go through the per-token
+    host round trip of abra_model_decode_streaming instead."""
+    from abra_b200.model import DecodeModel
+
+    n_prompt = PROMPT + depth
+    m = DecodeModel(max_ctx=n_prompt + warmup + steps, seed=seed)
+    prompt = np.random.default_rng(seed + depth).integers(0, m.cfg.vocab, n_prompt).astype(np.int32)
+    m.reset(prompt)
+    m.step(n_prompt - 1 + warmup)
+    m.sync()
+    st = torch.cuda.ExternalStream(m.stream)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(st)
+    if streaming:
+        m.decode_streaming(steps)
+    else:
+        m.step(steps)
+    e.record(st)
+    e.synchronize()
+    ms = s.elapsed_time(e) / steps
+    info = m.info()
+    toks = m.tokens(n_prompt + warmup + steps)[n_prompt:]
+    m.close()
+    return {"depth": depth, "ms_per_token": round(ms, 4), "tok_s": round(1000.0 / ms, 2),
+            "weight_bytes": info["weight_bytes"],
+            "kv_read_bytes_per_token": 36 * 2 * 8 * 128 * 2 * (n_prompt + warmup + steps // 2),
+            "tokens_head": toks[:8].tolist()}
+
+
+def decode_main(a, dist):
+    import torch
+
+    peak, peak_kind = measured_peaks()
+    torch.cuda.set_device(dist.local)
+    dist.init("nccl" if dist.world > 1 else "gloo")
+    depths = [0] if a.quick else [0, 2048, 8192]
+    dist.barrier()
+    with ClockSampler(dist.local) as clk:
+        res = decode_depth(torch, 0, a.warmup, a.steps, streaming=False)
+        dist.barrier()
+    clocks = clk.summary()
+    ms = dist.max(res["ms_per_token"])
+    tok_s = dist.world * 1000.0 / ms  # replicas: each rank decodes its own sequence
+    e2e = decode_depth(torch, 0, a.warmup, a.steps, streaming=True)
+    e2e_ms = dist.max(e2e["ms_per_token"])
+    extras = {"decode": {"depth0": res}}
+    for d in depths[1:]:
+        extras["decode"][f"depth{d}"] = decode_depth(torch, d, a.warmup, a.steps, streaming=False)
+    # the dominant kernel (MMVQ): its launches in the decode step, as one graph
+    sw = Sweep(torch.device("cuda", dist.local), 1)
+    g = sw.capture()
+    for _ in range(3):
+        g.replay()
+    ms_sw = sw.timed(max(3, a.steps // 16), g.replay)
+    achieved = sw.bytes / (ms_sw * 1e-3) / 1e9
+    del g
+    extras["gemv_sweep"] = {"workload": WORKLOAD, "GBps": round(achieved, 1),
+                            "ms_per_step": round(ms_sw, 4), "launches_per_step": sw.launches}
+    cpu = None
+    if dist.rank == 0 and dist.world == 1:
+        if not a.no_extras:
+            extras["per_shape"] = shape_table(sw)
+            r = ref_gpu_sweep(sw, 5)
+            if r:
+                extras["reference_kernels_on_b200"] = r
+        gbs, threads, reps, el = cpu_sample_rate(1, a.cpu_budget)
+        # the CPU restatement's decode rate: weight bytes per token at its GEMV rate
+        cpu_tok_s = gbs * 1e9 / res["weight_bytes"]
+        cpu = {"value": round(cpu_tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"first 512 rows of every config-1 matrix, {reps} reps in {el:.1f}s "
+                         f"({gbs:.2f} GB/s), scaled to the 2.26 GB of Q4_K weights a token "
+                         "reads; CPU restatement of vec_dot_q4_K_q8_1 (ggml CPU path not available)"}
+    traffic = None
+    tp = ROOT / "profiles" / f"traffic_{WORKLOAD}_b1.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+    if dist.rank == 0:
+        line = {
+            "metric": "Qwen3-4B-shape decode tok/s", "value": round(tok_s, 2), "unit": "tok/s",
+            "n_gpus": dist.world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u4 x s8 dot, fp32 accumulate",
+            "data": "synthetic (seeded random-init Qwen3-4B shape, all linear weights Q4_K)",
+            "config": {"workload": DECODE_WORKLOAD, "model": "qwen3-4b-shape-q4k",
+                       "global_batch": dist.world, "batch_per_gpu": 1, "seq_len": PROMPT + a.warmup + a.steps,
+                       "depth": 0, "prompt": PROMPT, "gen": a.steps,
+                       "parallelism": f"replica x{dist.world}",
+                       "l2": "inputs larger than L2 (2.26 GB of weights per token)",
+                       "launch": "one CUDA graph per token, programmatic dependent launch"},
+            "gpu_launches": a.steps * (36 * 11 + 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic, "kernel": "mmvq_q4k_kernel",
+                         "measured_on": f"the decode step's {sw.launches} MMVQ launches as one graph"},
+            "e2e": {"value": round(dist.world * 1000.0 / e2e_ms, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "ms_per_step": round(e2e_ms, 4), "path": "abra_model_decode_streaming"},
+            "clocks": clocks,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    dist.close()
+    return 0
+
+
 def reference_arm(a, dist):
     if dist.rank != 0:
         return 0
     for _ in range(a.warmup):
         cpu_sample_rate(a.batch, budget_s=0.5)
-    per = max(1.0, min(20.0, 150.0 / max(1, a.steps)))
+    # each step a bounded sample: the whole --steps/--warmup run stays within minutes
+    per = max(0.5, min(20.0, 150.0 / max(1, a.steps)))
     rates = [cpu_sample_rate(a.batch, budget_s=per) for _ in range(a.steps)]
     gbs = statistics.median(r[0] for r in rates)
     threads = rates[0][1]
+    sample = (f"first 512 rows of every config-1 matrix, batch {a.batch}, {per:.1f}s per step; "
+              "CPU restatement of vec_dot_q4_K_q8_1 (the ggml CPU path is not available)")
+    if a.workload == "decode":
+        weight_bytes = sum(nmat * q4k_bytes(N, K) for _, N, K, nmat, _ in sweep_ops())
+        val, unit, metric = gbs * 1e9 / weight_bytes, "tok/s", "Qwen3-4B-shape decode tok/s"
+        cfg = {"workload": DECODE_WORKLOAD, "model": "qwen3-4b-shape-q4k", "depth": 0,
+               "prompt": PROMPT, "gen": a.steps, "batch_per_gpu": 1}
+        sample += ", scaled to the 2.26 GB of Q4_K weights a token reads"
+    else:
+        val, unit, metric = gbs, "GB/s", "Q4_K GEMV HBM GB/s"
+        cfg = {"workload": WORKLOAD, "batch": a.batch}
     line = {
-        "impl": "reference", "metric": "Q4_K GEMV HBM GB/s", "value": round(gbs, 3),
-        "unit": "GB/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+        "impl": "reference", "metric": metric, "value": round(val, 3),
+        "unit": unit, "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u4 x s8 dot, fp32 scale", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": a.batch},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"first 512 rows of every config-1 matrix, batch {a.batch}, "
-                                   f"{per:.0f}s per step; CPU restatement of vec_dot_q4_K_q8_1 "
-                                   "(the ggml CPU path is not available)"},
-        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+        "config": cfg,
+        "cpu_baseline": {"value": round(val, 3), "unit": unit, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(val, 3), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -484,24 +610,33 @@ def reference_arm(a, dist):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode",
+                    help="decode: Qwen3-4B-shape tg at depths 0/2048/8192 (headline: depth 0); "
+                         "gemv: the decode weight sweep alone")
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps: tokens for decode (default 128), sweeps for gemv (20)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the per-shape table and the reference kernel family")
+    ap.add_argument("--quick", action="store_true", help="decode: depth 0 only")
     ap.add_argument("--case", choices=[n for n, _, _ in CONFIG1_SHAPES] + ["qkv", "gate_up"],
                     help="profiling mode: one operator, eager launches")
     ap.add_argument("--copies", type=int, default=2, help="weight copies in --case mode")
     a = ap.parse_args()
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if a.steps is None:
+        a.steps = 128 if a.workload == "decode" else 20
     if a.case:
         return run_case(a)
     dist = Dist()
     if a.impl == "reference":
         return reference_arm(a, dist)
+    if a.workload == "decode":
+        return decode_main(a, dist)
 
     import torch
 

@@ -166,6 +166,10 @@ int abra_model_read(void *model, int32_t *tokens, int32_t n_tokens, float *logit
 /* reset + (n_prompt + n_gen - 1) steps; out receives the n_gen picks. */
 int abra_model_generate(void *model, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
                         int32_t *out);
+/* Serving loop from the current position: per token, copy the token to
+ * feed from pinned host memory to the device, run one step, copy the pick
+ * back and wait for it (the host sees every token as it is produced). */
+int abra_model_decode_streaming(void *model, int32_t n, int32_t *out);
 int abra_model_info(void *model, void **stream, uint64_t *weight_bytes, uint64_t *kv_bytes);
 const char *abra_model_last_error(void);
 

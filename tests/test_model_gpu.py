@@ -65,6 +65,22 @@ def test_graph_eager_and_no_pdl_agree():
         assert np.array_equal(lg.view(np.uint32), outs[0][1].view(np.uint32))
 
 
+def test_streaming_loop_matches_graph_replay():
+    from abra_b200.model import DecodeModel
+
+    cfg = dict(n_layers=2, vocab=3000, max_ctx=80, centered=1, seed=11)
+    prompt = _prompt(9, 3000, 4)
+    with DecodeModel(**cfg) as a, DecodeModel(**cfg) as b:
+        want = a.generate(prompt, 40)
+        b.reset(prompt)
+        b.step(len(prompt) - 1)
+        got = b.decode_streaming(40)
+        assert np.array_equal(got, want)
+        assert b.position() == len(prompt) - 1 + 40
+        with pytest.raises(Exception):
+            b.step(80)  # would pass max_ctx: refused on the host
+
+
 @pytest.mark.parametrize("centered", [1, 0])
 def test_full_qwen3_4b_shape_greedy_bit_exact(centered):
     """The full 36-layer Qwen3-4B shape, 16-token prompt, 16 greedy steps:
