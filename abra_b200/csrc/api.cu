@@ -126,6 +126,17 @@ int abra_q4k_mmvq(const void *w, const void *x, float *y, int64_t N, int64_t K, 
     return abra_q4k_mmvq_ex(w, x, y, N, K, ncols, N, 0, 0, stream);
 }
 
+int abra_q4k_mmvq_combined(int32_t candidate, const void *w, const float *x, void *xq,
+                           float *y, int64_t N, int64_t K, int32_t ncols, void *stream) {
+    if (!x) return fail(ABRA_E_INVALID, "null pointer");
+    int rc = check_mmvq_args(w, xq, y, N, K, ncols, N);
+    if (rc) return rc;
+    if (reinterpret_cast<uintptr_t>(x) & 3u) return fail(ABRA_E_INVALID, "x must be 4-byte aligned");
+    cudaError_t e = abra::launch_quantize_q8_1(x, xq, K, ncols, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+    return mmvq_common(w, nullptr, xq, y, N, K, ncols, N, candidate, 0, stream);
+}
+
 int abra_q4k_mmvq_candidate(int32_t candidate, const void *w, const void *x, float *y,
                             int64_t N, int64_t K, int32_t ncols, void *stream) {
     if (candidate == 0) return fail(ABRA_E_INVALID, "candidate id 0 is the tuned dispatch; use abra_q4k_mmvq");

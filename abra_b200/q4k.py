@@ -207,15 +207,20 @@ def rmsnorm_quantize_q8_1(d_x, d_w, eps: float, d_x_q8, K: int, ncols: int = 1,
 
 def launch_q4k_candidate_combined_pipeline(candidate: int, d_w, d_x_f32, d_x_q8_scratch, d_y,
                                            N: int, K: int, stream=None, ncols: int = 1) -> None:
-    launch_quantize_f32_to_q8_1(d_x_f32, d_x_q8_scratch, K, stream, ncols=ncols)
-    launch_q4k_candidate(candidate, d_w, d_x_q8_scratch, d_y, N, K, stream, ncols=ncols)
+    _check_k(K)
+    if candidate != CANDIDATE_AUTOTUNED_DISPATCH:
+        get_candidate_spec(candidate)
+    cid = 0 if candidate == CANDIDATE_AUTOTUNED_DISPATCH else candidate
+    call("abra_q4k_mmvq_combined", cid, ptr(d_w), ptr(d_x_f32), ptr(d_x_q8_scratch),
+         ptr(d_y), N, K, ncols, stream_handle(stream))
 
 
 def launch_q4k_autotuned_combined_pipeline(d_w, d_x_f32, d_x_q8_scratch, d_y, N: int, K: int,
                                            arch: int = ARCH_SM100, stream=None,
                                            ncols: int = 1) -> None:
-    launch_quantize_f32_to_q8_1(d_x_f32, d_x_q8_scratch, K, stream, ncols=ncols)
-    launch_q4k_autotuned(d_w, d_x_q8_scratch, d_y, N, K, arch, stream, ncols=ncols)
+    _check_k(K)
+    call("abra_q4k_mmvq_combined", 0, ptr(d_w), ptr(d_x_f32), ptr(d_x_q8_scratch), ptr(d_y), N,
+         K, ncols, stream_handle(stream))
 
 
 # ------------------------------------------------------------ generator ---

@@ -59,6 +59,15 @@ int abra_q4k_mmvq(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, in
 int abra_q4k_mmvq_candidate(int32_t candidate, const void *w_q4k, const void *x_q8_1,
                             float *y, int64_t N, int64_t K, int32_t ncols, void *stream);
 
+/* Combined pipeline: quantize ncols fp32 columns x (K each) to Q8_1 in the
+ * caller's scratch x_q8_1_scratch (ncols * K/32 * 36 bytes, 16-byte
+ * aligned), then y = W x with the named candidate (0 = tuned).  Replaces
+ * launch_q4k_candidate_combined_pipeline / launch_q4k_autotuned_combined_pipeline
+ * (kernels/q4k/q4k_family.cuh:73-82,99-108; q4k_family.cu:283-295,451-463). */
+int abra_q4k_mmvq_combined(int32_t candidate, const void *w_q4k, const float *x,
+                           void *x_q8_1_scratch, float *y, int64_t N, int64_t K, int32_t ncols,
+                           void *stream);
+
 /* Full form: explicit output column stride ldy >= N, candidate (0 = tuned)
  * and ABRA_MMVQ_* flags. */
 int abra_q4k_mmvq_ex(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, int64_t K,

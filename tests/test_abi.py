@@ -71,6 +71,8 @@ def test_rejects_bad_arguments_without_gpu():
     assert "16-byte" in _lib.last_error()
     assert lib.abra_q4k_mmvq_ex(16, 16, 16, 8, 256, 1, 4, 0, 0, None) == _lib.ABRA_E_INVALID  # ldy
     assert lib.abra_quantize_q8_1(16, 16, 33, 1, None) == _lib.ABRA_E_INVALID
+    assert lib.abra_q4k_mmvq_combined(0, 16, None, 16, 16, 8, 256, 1, None) == _lib.ABRA_E_INVALID
+    assert lib.abra_q4k_mmvq_combined(0, 16, 16, 16, 16, 8, 300, 1, None) == _lib.ABRA_E_INVALID
     assert lib.abra_rmsnorm_quantize_q8_1(16, 16, 1e-6, 16, None, 32768, 1, None) == _lib.ABRA_E_INVALID
     with pytest.raises(ValueError):
         A.launch_quantize_f32_to_q8_1(16, 16, 33)

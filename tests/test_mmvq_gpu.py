@@ -121,6 +121,29 @@ def test_qwen_shapes_tuned(dev, N, K, ncols):
     tol_check(y, O.gemv_f64(w, xq, K), O.absdot_f64(w, xq, K), TOL)
 
 
+@pytest.mark.parametrize("N,K,ncols", [(9728, 2560, 1), (2560, 9728, 8), (1183, 4096, 3)])
+def test_combined_pipeline(dev, N, K, ncols):
+    """fp32 input -> Q8_1 scratch -> MMVQ in one call (tuned and named
+    candidates): the scratch holds the oracle's Q8_1 bytes and y is
+    bit-exact to the canonical oracle."""
+    import torch
+    import abra_b200 as A
+
+    w, x, xq = _case(N, K, ncols, seed=11)
+    ref = O.gemv(w, xq, K, nthreads=8)
+    dw, dx = to_dev(w.reshape(-1), dev), to_dev(x.reshape(-1), dev)
+    for cid in (0, 3022, 1041):
+        scratch = torch.zeros(ncols * K // 32 * 36, dtype=torch.uint8, device=dev)
+        dy = torch.full((ncols * N,), float("nan"), dtype=torch.float32, device=dev)
+        if cid == 0:
+            A.launch_q4k_autotuned_combined_pipeline(dw, dx, scratch, dy, N, K, ncols=ncols)
+        else:
+            A.launch_q4k_candidate_combined_pipeline(cid, dw, dx, scratch, dy, N, K, ncols=ncols)
+        torch.cuda.synchronize()
+        assert np.array_equal(scratch.cpu().numpy(), xq.reshape(-1))
+        assert np.array_equal(dy.cpu().numpy().reshape(ncols, N), ref), f"candidate {cid}"
+
+
 @pytest.mark.parametrize("N,K", [(1000, 4096), (77, 9728), (2049, 2560)])
 def test_every_candidate_bit_identical(dev, N, K):
     import abra_b200 as A
