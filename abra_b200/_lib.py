@@ -33,6 +33,7 @@ SIGNATURES: dict[str, tuple] = {
     "launch_pinned_upstream_mmvq": (None, [_vp, _vp, _fp, _i64, _i64, _vp]),
     "abra_quantize_q8_1": (C.c_int, [_fp, _vp, _i64, _i32, _vp]),
     "abra_q4k_mmvq_combined": (C.c_int, [_i32, _vp, _fp, _vp, _fp, _i64, _i64, _i32, _vp]),
+    "abra_q4k_mmvq_combined_static": (C.c_int, [_i32, _vp, _fp, _fp, _i64, _i64, _i32, _vp]),
     "launch_pinned_upstream_q8_1_quantize": (None, [_fp, _vp, _i64, _vp]),
     "abra_rmsnorm_quantize_q8_1": (C.c_int, [_fp, _fp, _f32, _vp, _fp, _i64, _i32, _vp]),
     "abra_gen_q4k": (C.c_int, [_vp, _i64, _u64, _u64, _i64, _vp]),

@@ -58,6 +58,8 @@ int check_mmvq_args(const void *w, const void *x, const float *y, int64_t N, int
 
 }  // namespace
 
+int abra::record_failure(int code, const char *msg) { return fail(code, "%s", msg); }
+
 namespace abra {
 static std::vector<ErrorWordFn> &error_words() {
     static std::vector<ErrorWordFn> v;

@@ -77,4 +77,8 @@ int device_sm_count();
 // Reads (and optionally clears) every translation unit's device error word.
 cudaError_t read_error_words(unsigned *value, bool clear);
 
+// Records msg for abra_last_error and returns code (for entry points that
+// live outside api.cu).
+int record_failure(int code, const char *msg);
+
 }  // namespace abra

@@ -68,6 +68,17 @@ int abra_q4k_mmvq_combined(int32_t candidate, const void *w_q4k, const float *x,
                            void *x_q8_1_scratch, float *y, int64_t N, int64_t K, int32_t ncols,
                            void *stream);
 
+/* The same combined pipeline with no caller scratch and no allocation: the
+ * Q8_1 blocks go to a static device array of 147,456 bytes (K * ncols <=
+ * 131,072; larger requests return ABRA_E_UNSUPPORTED).  For callers that may
+ * not allocate device memory where they multiply.  The first call on each
+ * device resolves that device's scratch address; make it before any stream
+ * capture.  Nothing in the scratch needs to start at zero.  Calls that can
+ * overlap on one device (different streams or threads) race on the scratch.
+ * This entry point has no counterpart in the reference. */
+int abra_q4k_mmvq_combined_static(int32_t candidate, const void *w_q4k, const float *x,
+                                  float *y, int64_t N, int64_t K, int32_t ncols, void *stream);
+
 /* Full form: explicit output column stride ldy >= N, candidate (0 = tuned)
  * and ABRA_MMVQ_* flags. */
 int abra_q4k_mmvq_ex(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, int64_t K,
