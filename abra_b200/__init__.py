@@ -30,12 +30,14 @@ from .q4k import (
     launch_quantize_f32_to_q8_1,
     load_tuning_table,
     mmvq,
+    mmvq_kshard,
     mmvq_partials,
     mmvq_swiglu,
     q4k_nbytes,
     q8_1_nbytes,
     register_autotuned_table_entry,
     rmsnorm_quantize_q8_1,
+    slice_start,
 )
 
 __version__ = _lib.lib.abra_version().decode()

@@ -32,6 +32,7 @@ SIGNATURES: dict[str, tuple] = {
     "abra_q4k_mmvq_partials": (C.c_int, [_vp, _vp, _fp, _vp, _vp, _i64, _i64, _i32, _i32, _vp]),
     "launch_pinned_upstream_mmvq": (None, [_vp, _vp, _fp, _i64, _i64, _vp]),
     "abra_quantize_q8_1": (C.c_int, [_fp, _vp, _i64, _i32, _vp]),
+    "abra_q4k_mmvq_kshard": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _i32, _i32, _vp]),
     "abra_q4k_mmvq_combined": (C.c_int, [_i32, _vp, _fp, _vp, _fp, _i64, _i64, _i32, _vp]),
     "abra_q4k_mmvq_combined_static": (C.c_int, [_i32, _vp, _fp, _fp, _i64, _i64, _i32, _vp]),
     "launch_pinned_upstream_q8_1_quantize": (None, [_fp, _vp, _i64, _vp]),
@@ -56,6 +57,10 @@ SIGNATURES: dict[str, tuple] = {
     "abra_model_info": (C.c_int, [_vp, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64),
                                   C.POINTER(C.c_uint64)]),
     "abra_model_last_error": (C.c_char_p, []),
+    "abra_tp_shard_info": (C.c_int, [_vp, _i32, _i32, _vp]),
+    "abra_model_create_tp": (C.c_int, [_vp, _i32, _i32, C.POINTER(C.c_void_p)]),
+    "abra_model_tp_handle": (C.c_int, [_vp, _vp, _i32]),
+    "abra_model_tp_connect": (C.c_int, [_vp, _vp, _i32]),
 }
 
 

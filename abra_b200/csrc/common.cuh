@@ -168,8 +168,51 @@ __device__ __forceinline__ void scale_min_pair(uint32_t s0, uint32_t s1, uint32_
     }
 }
 
+// Release add / acquire load at system scope (peer GPUs over NVLink).
+__device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long atom_add_acq_rel_gpu(unsigned long long *p,
+                                                                   unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Spins until *cnt >= target or WAIT_LIMIT_NS passes (then flags
+// ERR_FLAG_TIMEOUT and returns false); polls with relaxed loads and acquires
+// once at the end.  Once a cross-rank wait of this translation unit has
+// given up, later ones return at once: a rank that is gone costs one time
+// limit, not one per wait.
+__device__ __forceinline__ bool wait_count(const unsigned long long *cnt, unsigned long long target) {
+    if (ld_acquire_sys(cnt) >= target) return true;
+    if (*static_cast<volatile unsigned *>(&g_abra_device_error) & ERR_FLAG_TIMEOUT) return false;
+    const unsigned long long t0 = globaltimer_ns();
+    for (unsigned i = 1;; ++i) {
+        if (ld_relaxed_sys(cnt) >= target) return ld_acquire_sys(cnt) >= target;
+        if ((i & 255u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+            report_error(ERR_FLAG_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 // Up to eight fp32 partial deltas summed in a fixed tree before a residual
 // add: G = 1: p0; 2: p0+p1; 4: (p0+p1)+(p2+p3); 8: three levels.  G = 0: none.
+// With p_g the K-shard partial of rank g (shards on canonical slice
+// boundaries), the tree is the top of the unsharded slice tree.  Loads go
+// through L2 (.cg): the partials may have been written by peer GPUs.
 struct DeltaSet {
     const float *p[8];
     int G;
@@ -178,12 +221,16 @@ struct DeltaSet {
 __device__ __forceinline__ float delta_tree(const DeltaSet &ds, int64_t i) {
     const float *const *p = ds.p;
     switch (ds.G) {
-        case 1: return p[0][i];
-        case 2: return __fadd_rn(p[0][i], p[1][i]);
-        case 4: return __fadd_rn(__fadd_rn(p[0][i], p[1][i]), __fadd_rn(p[2][i], p[3][i]));
+        case 1: return __ldcg(p[0] + i);
+        case 2: return __fadd_rn(__ldcg(p[0] + i), __ldcg(p[1] + i));
+        case 4:
+            return __fadd_rn(__fadd_rn(__ldcg(p[0] + i), __ldcg(p[1] + i)),
+                             __fadd_rn(__ldcg(p[2] + i), __ldcg(p[3] + i)));
         default:
-            return __fadd_rn(__fadd_rn(__fadd_rn(p[0][i], p[1][i]), __fadd_rn(p[2][i], p[3][i])),
-                             __fadd_rn(__fadd_rn(p[4][i], p[5][i]), __fadd_rn(p[6][i], p[7][i])));
+            return __fadd_rn(__fadd_rn(__fadd_rn(__ldcg(p[0] + i), __ldcg(p[1] + i)),
+                                       __fadd_rn(__ldcg(p[2] + i), __ldcg(p[3] + i))),
+                             __fadd_rn(__fadd_rn(__ldcg(p[4] + i), __ldcg(p[5] + i)),
+                                       __fadd_rn(__ldcg(p[6] + i), __ldcg(p[7] + i))));
     }
 }
 

@@ -20,9 +20,14 @@ cudaError_t launch_attention(const float *q, const void *kc, const void *vc, con
                              float *part_l, float *part_o, float *out_f32, void *out_q8,
                              bool pdl, cudaStream_t s);
 // Reads the argmax key left by the output MMVQ, resets it, appends the pick.
+// Tensor parallel (epoch != nullptr): first waits until *wait_cnt >=
+// (*epoch + 1) * per_step (every rank's keys have arrived), then advances
+// *epoch.
 cudaError_t launch_argmax_finish(unsigned long long *key, int32_t *tokens, int32_t *picks,
                                  int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
-                                 cudaStream_t s);
+                                 cudaStream_t s, const unsigned long long *wait_cnt = nullptr,
+                                 unsigned long long *epoch = nullptr,
+                                 unsigned long long per_step = 0);
 cudaError_t launch_argmax_advance(const float *logits, int n, int32_t *tokens, int32_t *picks,
                                   int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
                                   cudaStream_t s);
@@ -32,5 +37,11 @@ cudaError_t launch_gen_q4k_ex(void *dst, int64_t nblocks, uint64_t seed, uint64_
                               int64_t block_offset, int flags, cudaStream_t stream);
 cudaError_t launch_gen_norm_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
                                 cudaStream_t stream);
+// Rows [row0, row0 + rows) x superblock columns [sb_lo, sb_hi) of a Q4_K
+// tensor with rows of nsb_g superblocks (a K-shard), bytes identical to the
+// same blocks of the whole tensor.
+cudaError_t launch_gen_q4k_cols(void *dst, int64_t rows, int64_t nsb_g, int64_t sb_lo,
+                                int64_t sb_hi, uint64_t seed, uint64_t tensor_id, int64_t row0,
+                                int flags, cudaStream_t stream);
 
 }  // namespace abra

@@ -415,11 +415,18 @@ __global__ void __launch_bounds__(1024)
 __global__ void argmax_finish_kernel(unsigned long long *__restrict__ key,
                                      int32_t *__restrict__ tokens, int32_t *__restrict__ picks,
                                      int32_t *__restrict__ pos_p,
-                                     const int32_t *__restrict__ n_prompt_p, int max_ctx) {
+                                     const int32_t *__restrict__ n_prompt_p, int max_ctx,
+                                     const unsigned long long *wait_cnt,
+                                     unsigned long long *epoch, unsigned long long per_step) {
     pdl_wait();
     pdl_launch_dependents();
     if (threadIdx.x != 0) return;
-    const unsigned long long k = *key;
+    if (epoch) {  // tensor parallel: every rank's keys have arrived
+        const unsigned long long e = __ldcg(epoch);
+        if (wait_cnt) wait_count(wait_cnt, (e + 1ull) * per_step);
+        *epoch = e + 1ull;
+    }
+    const unsigned long long k = __ldcg(key);
     *key = 0ull;
     const int bi = static_cast<int>(0xFFFFFFFFu - static_cast<unsigned>(k & 0xFFFFFFFFull));
     const int p = *pos_p;
@@ -509,9 +516,10 @@ cudaError_t launch_attention(const float *q, const void *kc, const void *vc, con
 
 cudaError_t launch_argmax_finish(unsigned long long *key, int32_t *tokens, int32_t *picks,
                                  int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
-                                 cudaStream_t s) {
+                                 cudaStream_t s, const unsigned long long *wait_cnt,
+                                 unsigned long long *epoch, unsigned long long per_step) {
     return launch_pdl(argmax_finish_kernel, dim3(1), dim3(32), 0, s, pdl, key, tokens, picks, pos,
-                      n_prompt, max_ctx);
+                      n_prompt, max_ctx, wait_cnt, epoch, per_step);
 }
 
 cudaError_t launch_argmax_advance(const float *logits, int n, int32_t *tokens, int32_t *picks,

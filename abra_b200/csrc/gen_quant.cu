@@ -67,8 +67,11 @@ __device__ void centre_header(uint64_t &w0, uint64_t &w1) {
     }
 }
 
+// Local block blk is global block block_offset + (blk / width) * gstride +
+// blk % width: a contiguous run when width >= nblocks, or a column range of
+// width superblocks out of rows of gstride (a K-shard).
 __global__ void gen_q4k_kernel(uint64_t *__restrict__ dst, int64_t nblocks, uint64_t key,
-                               int64_t block_offset, int flags) {
+                               int64_t block_offset, int64_t width, int64_t gstride, int flags) {
     const int64_t nwords = nblocks * 18;
     const bool centred = (flags & 1) != 0;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nwords;
@@ -76,7 +79,8 @@ __global__ void gen_q4k_kernel(uint64_t *__restrict__ dst, int64_t nblocks, uint
         const int64_t blk = i / 18;
         const int w = static_cast<int>(i - blk * 18);
         if (centred && w == 1) continue;  // written by the word-0 thread
-        const uint64_t gword = static_cast<uint64_t>(block_offset + blk) * 18u + w;
+        const int64_t gblk = block_offset + (blk / width) * gstride + blk % width;
+        const uint64_t gword = static_cast<uint64_t>(gblk) * 18u + w;
         uint64_t h = stream_word(key, gword);
         if (w == 0) {
             const float d = __fmaf_rn(unit24(h >> 40), 0.019f, 0.001f);
@@ -121,7 +125,23 @@ cudaError_t launch_gen_q4k_ex(void *dst, int64_t nblocks, uint64_t seed, uint64_
     const int64_t want = (nwords + threads - 1) / threads;
     const int grid = static_cast<int>(want < 148 * 32 ? want : 148 * 32);
     gen_q4k_kernel<<<grid, threads, 0, stream>>>(static_cast<uint64_t *>(dst), nblocks,
-                                                 stream_key(seed, tensor_id), block_offset, flags);
+                                                 stream_key(seed, tensor_id), block_offset,
+                                                 nblocks, 0, flags);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gen_q4k_cols(void *dst, int64_t rows, int64_t nsb_g, int64_t sb_lo,
+                                int64_t sb_hi, uint64_t seed, uint64_t tensor_id, int64_t row0,
+                                int flags, cudaStream_t stream) {
+    const int64_t width = sb_hi - sb_lo, nblocks = rows * width;
+    if (nblocks <= 0) return cudaSuccess;
+    const int64_t nwords = nblocks * 18;
+    const int threads = 256;
+    const int64_t want = (nwords + threads - 1) / threads;
+    const int grid = static_cast<int>(want < 148 * 32 ? want : 148 * 32);
+    gen_q4k_kernel<<<grid, threads, 0, stream>>>(static_cast<uint64_t *>(dst), nblocks,
+                                                 stream_key(seed, tensor_id), row0 * nsb_g + sb_lo,
+                                                 width, nsb_g, flags);
     return cudaGetLastError();
 }
 

@@ -26,13 +26,37 @@ enum : int {
     MMVQ_PDL = 1,  // launch with programmatic dependent launch (weights must be immutable)
 };
 
+// Tensor-parallel options of one MMVQ launch (all off by default).
+struct MmvqTp {
+    // K-shard slicing: the shard holds global canonical slices
+    // [sl_base, sl_base + sl_cnt) of rows of sl_nsb superblocks (0: unsharded)
+    int sl_nsb = 0, sl_base = 0, sl_cnt = 8;
+    int row_offset = 0;  // global id of local row 0 (argmax keys)
+    // push: rows to peer_y[q] (when set); CTAs count themselves on cta_cnt
+    // (this GPU, never reset: a multiple of the grid after each launch); the
+    // last one forwards the argmax keys to peer_amax[q] (when set) and adds
+    // one arrival to peer_cnt[q], for q < npeer
+    int npeer = 0;
+    float *peer_y[8] = {};
+    unsigned long long *peer_amax[8] = {};
+    unsigned long long *peer_cnt[8] = {};
+    unsigned long long *cta_cnt = nullptr;
+    // fused-input wait: *wait_cnt >= (*epoch + 1) * wait_per_step
+    const unsigned long long *wait_cnt = nullptr;
+    const unsigned long long *epoch = nullptr;
+    unsigned long long wait_per_step = 0;
+};
+
 // w2 != nullptr selects the fused gate/up form: y = (w2 x) * silu(w x).
 // amax != nullptr: also atomicMax an argmax key (value, row) per column into
 // amax[c] (keys must start at 0).
 cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2,
                             const void *x_q8, float *y, int64_t N, int64_t K, int ncols,
                             int64_t ldy, int flags, cudaStream_t stream,
-                            unsigned long long *amax = nullptr);
+                            unsigned long long *amax = nullptr, const MmvqTp *tp = nullptr);
+// Grid size the launch above would use (for arrival counts).
+int mmvq_grid(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, bool xin,
+              const MmvqTp *tp = nullptr);
 // Fused input of launch_mmvq_q4k_xin: x = h_in + tree(deltas) (written to
 // h_out when not null), quantized as Q8_1 of RMSNorm(x) * norm_w.
 struct MmvqXin {
@@ -46,7 +70,8 @@ struct MmvqXin {
 // stream (residual add + RMSNorm + Q8_1 fused into the prologue).
 cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void *w2,
                                 const MmvqXin &xin, float *y, int64_t N, int64_t K, int flags,
-                                cudaStream_t stream, unsigned long long *amax = nullptr);
+                                cudaStream_t stream, unsigned long long *amax = nullptr,
+                                const MmvqTp *tp = nullptr);
 
 // Sets the kernel attributes a later launch of this candidate needs (done
 // outside stream capture).

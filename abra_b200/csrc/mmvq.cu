@@ -100,12 +100,35 @@ struct MmvqPlan {
     int grid, block, nstage, pitch, smem, rg_total;
 };
 
+// Slicing of a launch: unsharded unless tp names a K-shard.  Returns false
+// when the shard's slices do not add up to nsb superblocks.
+static bool shard_of(const MmvqTp *tp, int nsb, int &sl_nsb, int &sl_base, int &sl_cnt) {
+    sl_nsb = nsb;
+    sl_base = 0;
+    sl_cnt = 8;
+    if (tp && tp->sl_nsb > 0) {
+        sl_nsb = tp->sl_nsb;
+        sl_base = tp->sl_base;
+        sl_cnt = tp->sl_cnt;
+    }
+    if (sl_base < 0 || sl_cnt < 1 || sl_base + sl_cnt > 8) return false;
+    return shard_slice(sl_nsb, sl_base, sl_cnt, 8) == nsb;
+}
+
 static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int nmat,
-                      MmvqPlan &pl, bool xin = false) {
+                      MmvqPlan &pl, bool xin = false, const MmvqTp *tp = nullptr) {
     const int ks = cfg.ks;
     const bool staged = cfg.mode != MODE_DIRECT;
     const int nsl = 8 / ks;
-    const int max_part = slice_start(nsb, nsl) * Q4K_BYTES;
+    int sl_nsb, sl_base, sl_cnt;
+    if (!shard_of(tp, nsb, sl_nsb, sl_base, sl_cnt)) return false;
+    int max_sb = 0;
+    for (int j = 0; j < ks; ++j) {
+        const int w = shard_slice(sl_nsb, sl_base, sl_cnt, (j + 1) * nsl) -
+                      shard_slice(sl_nsb, sl_base, sl_cnt, j * nsl);
+        max_sb = w > max_sb ? w : max_sb;
+    }
+    const int max_part = max_sb * Q4K_BYTES;
     int pitch = max_part;
     if (cfg.mode == MODE_TMA_ROWS && ((pitch / 16) & 1) == 0) pitch += 16;
     pl.pitch = pitch;
@@ -145,6 +168,27 @@ static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int 
     }
 }
 
+// Copies the tensor-parallel options into the kernel parameters.
+static bool apply_tp(MmvqParams &prm, const MmvqTp *tp) {
+    if (!shard_of(tp, prm.nsb, prm.sl_nsb, prm.sl_base, prm.sl_cnt)) return false;
+    if (!tp) return true;
+    if (tp->npeer < 0 || tp->npeer > 8) return false;
+    prm.row_offset = tp->row_offset;
+    prm.npeer = tp->npeer;
+    for (int q = 0; q < tp->npeer; ++q) {
+        if (!tp->peer_cnt[q]) return false;
+        prm.peer_y[q] = tp->peer_y[q];
+        prm.peer_amax[q] = tp->peer_amax[q];
+        prm.peer_cnt[q] = tp->peer_cnt[q];
+    }
+    if (tp->npeer > 0 && !tp->cta_cnt) return false;
+    prm.cta_cnt = tp->cta_cnt;
+    prm.wait_cnt = tp->wait_cnt;
+    prm.epoch = tp->epoch;
+    prm.wait_per_step = tp->wait_per_step;
+    return !prm.wait_cnt || prm.epoch;
+}
+
 static cudaError_t launch_plan(MmvqFn fn, const MmvqPlan &pl, bool pdl, MmvqParams prm,
                                cudaStream_t stream) {
     cudaError_t e = ensure_smem_attr(fn);
@@ -168,7 +212,7 @@ static cudaError_t launch_plan(MmvqFn fn, const MmvqPlan &pl, bool pdl, MmvqPara
 cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2,
                             const void *x_q8, float *y, int64_t N, int64_t K, int ncols,
                             int64_t ldy, int flags, cudaStream_t stream,
-                            unsigned long long *amax) {
+                            unsigned long long *amax, const MmvqTp *tp) {
     const int nsb = static_cast<int>(K / QK_K);
     const int nmat = w2 ? 2 : 1;
     const MmvqTable *t = table_for(ncols);
@@ -177,7 +221,7 @@ cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2
     MmvqFn fn = t->fn[cfg.mode][ki][nmat - 1];
     if (!fn) return cudaErrorInvalidValue;
     MmvqPlan pl;
-    if (!plan_mmvq(cfg, N, nsb, ncols, nmat, pl)) return cudaErrorInvalidConfiguration;
+    if (!plan_mmvq(cfg, N, nsb, ncols, nmat, pl, false, tp)) return cudaErrorInvalidConfiguration;
     MmvqParams prm = {};
     prm.W[0] = static_cast<const uint8_t *>(w);
     prm.W[1] = static_cast<const uint8_t *>(w2);
@@ -187,12 +231,20 @@ cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2
     prm.nsb = nsb;
     prm.ldy = ldy;
     prm.amax = amax;
+    if (!apply_tp(prm, tp)) return cudaErrorInvalidValue;
     return launch_plan(fn, pl, (flags & MMVQ_PDL) != 0, prm, stream);
+}
+
+int mmvq_grid(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, bool xin,
+              const MmvqTp *tp) {
+    MmvqPlan pl;
+    if (!plan_mmvq(cfg, N, static_cast<int>(K / QK_K), ncols, nmat, pl, xin, tp)) return -1;
+    return pl.grid;
 }
 
 cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void *w2,
                                 const MmvqXin &xin, float *y, int64_t N, int64_t K, int flags,
-                                cudaStream_t stream, unsigned long long *amax) {
+                                cudaStream_t stream, unsigned long long *amax, const MmvqTp *tp) {
     const int nsb = static_cast<int>(K / QK_K);
     const int nmat = w2 ? 2 : 1;
     const int ki = ks_index(cfg.ks);
@@ -201,7 +253,7 @@ cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void
     if (!fn || !xin.h_in || !xin.norm_w) return cudaErrorInvalidValue;
     if (reinterpret_cast<uintptr_t>(xin.norm_w) & 15) return cudaErrorInvalidValue;  // float4 loads
     MmvqPlan pl;
-    if (!plan_mmvq(cfg, N, nsb, 1, nmat, pl, true)) return cudaErrorInvalidConfiguration;
+    if (!plan_mmvq(cfg, N, nsb, 1, nmat, pl, true, tp)) return cudaErrorInvalidConfiguration;
     MmvqParams prm = {};
     prm.W[0] = static_cast<const uint8_t *>(w);
     prm.W[1] = static_cast<const uint8_t *>(w2);
@@ -215,6 +267,7 @@ cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void
     prm.deltas = xin.deltas;
     prm.norm_w = xin.norm_w;
     prm.eps = xin.eps;
+    if (!apply_tp(prm, tp)) return cudaErrorInvalidValue;
     return launch_plan(fn, pl, (flags & MMVQ_PDL) != 0, prm, stream);
 }
 
@@ -245,6 +298,7 @@ cudaError_t launch_mmvq_q4k_partials(const void *w, const void *x_q8, float *y, 
     prm.ldy = N;
     prm.P = P;
     prm.M = M;
+    if (!apply_tp(prm, nullptr)) return cudaErrorInvalidValue;
     return launch_plan(t->partials[ki], pl, false, prm, stream);
 }
 

@@ -55,7 +55,33 @@ struct MmvqParams {
     DeltaSet deltas;
     const float *norm_w;
     float eps;
+    // K-shard slicing: local canonical slice i is global slice sl_base + i of
+    // a row of sl_nsb superblocks for i < sl_cnt, and empty after that, so a
+    // shard's sum is a subtree of the unsharded tree (sl_nsb == nsb,
+    // sl_base == 0, sl_cnt == 8 when K is not sharded).
+    int sl_nsb, sl_base, sl_cnt;
+    int row_offset;  // added to row ids in argmax keys (vocab shards)
+    // Tensor-parallel push (npeer > 0): output rows go to peer_y[q] for every
+    // rank q; each CTA then counts itself on cta_cnt (GPU scope, acq_rel), and
+    // the launch's last CTA forwards this rank's argmax keys (amax, read and
+    // reset) to peer_amax[q] and adds 1 to peer_cnt[q] with release
+    // semantics at system scope.
+    int npeer;
+    float *peer_y[8];
+    unsigned long long *peer_amax[8];
+    unsigned long long *peer_cnt[8];
+    unsigned long long *cta_cnt;
+    // Tensor-parallel wait (fused input only): before reading the deltas,
+    // *wait_cnt >= (*epoch + 1) * wait_per_step, bounded in time.
+    const unsigned long long *wait_cnt;
+    const unsigned long long *epoch;
+    unsigned long long wait_per_step;
 };
+
+// First superblock (relative to the shard) of local canonical slice i.
+__host__ __device__ __forceinline__ int shard_slice(int sl_nsb, int sl_base, int sl_cnt, int i) {
+    return slice_start(sl_nsb, sl_base + (i < sl_cnt ? i : sl_cnt)) - slice_start(sl_nsb, sl_base);
+}
 
 // Order-preserving 64-bit key of (value, row): the float's bits mapped to an
 // unsigned order in the high word, ~row in the low word, so the largest key
@@ -255,7 +281,8 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
                 const int s = u % nstage, k = u / nstage;
                 if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1, ERR_WAIT_EMPTY)) break;
                 const int rg = rg_begin + u / KS, j = u % KS;
-                const int sb_lo = slice_start(nsb, j * NSL), sb_hi = slice_start(nsb, (j + 1) * NSL);
+                const int sb_lo = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, j * NSL);
+                const int sb_hi = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, (j + 1) * NSL);
                 const uint32_t part_bytes = static_cast<uint32_t>(sb_hi - sb_lo) * Q4K_BYTES;
                 const int row0 = rg * 8;
                 const int nvalid = min(8, N - row0);
@@ -294,6 +321,13 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
             *reinterpret_cast<float4 *>(s_w + i) = __ldg(reinterpret_cast<const float4 *>(prm.norm_w + i));
     }
     pdl_wait();  // x is produced by the preceding kernel
+    if constexpr (XIN) {
+        if (prm.wait_cnt) {  // the other ranks' partial sums have arrived
+            if (threadIdx.x == 0)
+                wait_count(prm.wait_cnt, (__ldcg(prm.epoch) + 1ull) * prm.wait_per_step);
+            named_bar_sync(1, NCW * 32);
+        }
+    }
     if constexpr (XIN) {
         // residual add + RMSNorm + Q8_1 of the fp32 input, in this CTA's shared
         // memory, in the canonical order: thread t sums x[t + 256 k]^2 with
@@ -397,8 +431,8 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
 
     const int grp = warp / KS, j = warp % KS;
     const int p = lane >> 3, g = lane & 7;
-    const int sb_part = slice_start(nsb, j * NSL);
-    const int sb_part_end = slice_start(nsb, (j + 1) * NSL);
+    const int sb_part = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, j * NSL);
+    const int sb_part_end = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, (j + 1) * NSL);
     bool poisoned = false;
     int round = 0;
     for (int r = grp; r < nrg; r += NGRP, ++round) {
@@ -425,7 +459,8 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
         }
 #pragma unroll
         for (int i = 0; i < NSL; ++i) {
-            const int b0 = slice_start(nsb, j * NSL + i), b1 = slice_start(nsb, j * NSL + i + 1);
+            const int b0 = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, j * NSL + i);
+            const int b1 = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, j * NSL + i + 1);
 #pragma unroll
             for (int m = 0; m < NMAT; ++m)
 #pragma unroll
@@ -508,9 +543,15 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
             for (int c = 0; c < NCOLS; ++c) {
                 float yv = sub[0][c];
                 if constexpr (NMAT == 2) yv = __fmul_rn(sub[1][c], abra_silu(sub[0][c]));
-                if (row < N) prm.Y[c * prm.ldy + row] = yv;
+                if (row < N) {
+                    if (prm.npeer > 0 && prm.peer_y[0]) {  // push the partial to every rank
+                        for (int q = 0; q < prm.npeer; ++q) prm.peer_y[q][c * prm.ldy + row] = yv;
+                    } else {
+                        prm.Y[c * prm.ldy + row] = yv;
+                    }
+                }
                 if (prm.amax) {  // lanes 0..7 hold the unit's eight rows
-                    unsigned long long key = row < N ? argmax_key(yv, row) : 0ull;
+                    unsigned long long key = row < N ? argmax_key(yv, row + prm.row_offset) : 0ull;
 #pragma unroll
                     for (int m = 1; m < 8; m <<= 1) {
                         const unsigned long long o = __shfl_xor_sync(0x000000ffu, key, m);
@@ -521,7 +562,28 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
             }
         }
     }
-    if (prm.amax) {
+    if (prm.npeer > 0) {
+        // every consumer's stores are done: count this CTA on this GPU; the
+        // last CTA of the launch publishes the whole launch to each rank
+        named_bar_sync(1, NCW * 32);
+        if (threadIdx.x == 0) {
+            if (prm.amax)
+                for (int c = 0; c < NCOLS; ++c) atomicMax(&prm.amax[c], s_amax[c]);
+            const unsigned long long old = atom_add_acq_rel_gpu(prm.cta_cnt, 1ull);
+            if ((old + 1ull) % gridDim.x == 0ull) {
+                if (prm.amax && prm.peer_amax[0]) {
+                    for (int c = 0; c < NCOLS; ++c) {
+                        const unsigned long long key = atomicExch(&prm.amax[c], 0ull);
+                        for (int q = 0; q < prm.npeer; ++q) atomicMax_system(prm.peer_amax[q] + c, key);
+                    }
+                }
+                // release at system scope: every store this launch made
+                // (ordered before this point by the acq_rel count) is visible
+                // to a rank that acquires the arrival
+                for (int q = 0; q < prm.npeer; ++q) red_release_sys_add(prm.peer_cnt[q], 1ull);
+            }
+        }
+    } else if (prm.amax) {
         named_bar_sync(1, NCW * 32);
         if (threadIdx.x < NCOLS) atomicMax(&prm.amax[threadIdx.x], s_amax[threadIdx.x]);
     }

@@ -1,5 +1,5 @@
 // model.cu -- native decode runtime of the Qwen3-4B-shaped Q4_K model
-// (BASELINE config 3) behind the C ABI (include/abra_b200.h, abra_model_*).
+// behind the C ABI (include/abra_b200.h, abra_model_*).
 //
 // One decode step is recorded once into a CUDA graph and replayed per
 // token.  The position, the token history and the prompt length live in
@@ -37,9 +37,49 @@ struct LayerW {
     uint8_t *wqkv, *wo, *wgate, *wup, *wdown;
 };
 
+// What one rank of a tensor-parallel group holds (world == 1: everything).
+// K-sharded layers (o, down) are cut on canonical K-slice boundaries, so the
+// ranks' partial sums combine, in the fixed slice tree, to the bits of the
+// unsharded layer; every other layer is split by output rows.
+static int tp_shard(const abra_model_config &c, int rank, int world, abra_tp_shard &s) {
+    if (!(world == 1 || world == 2 || world == 4 || world == 8) || rank < 0 || rank >= world)
+        return ABRA_E_INVALID;
+    if (c.n_heads % world || c.n_kv_heads % world || c.vocab < world) return ABRA_E_UNSUPPORTED;
+    const int per = 8 / world;
+    const int qd = c.n_heads * c.head_dim;
+    const int nsb_o = qd / QK_K, nsb_f = c.ffn / QK_K;
+    s.rank = rank;
+    s.world = world;
+    s.q_heads = c.n_heads / world;
+    s.kv_heads = c.n_kv_heads / world;
+    s.q_head_lo = rank * s.q_heads;
+    s.kv_head_lo = rank * s.kv_heads;
+    s.sl_base = rank * per;
+    s.sl_cnt = per;
+    // o: this rank's heads must be exactly its canonical slices of K
+    for (int r = 0; r <= world; ++r)
+        if (slice_start(nsb_o, r * per) * QK_K != r * (qd / world)) return ABRA_E_UNSUPPORTED;
+    s.ffn_lo = slice_start(nsb_f, rank * per) * QK_K;
+    s.ffn_hi = slice_start(nsb_f, (rank + 1) * per) * QK_K;
+    if (s.ffn_hi <= s.ffn_lo) return ABRA_E_UNSUPPORTED;
+    s.vocab_lo = static_cast<int64_t>(c.vocab) * rank / world;
+    s.vocab_hi = static_cast<int64_t>(c.vocab) * (rank + 1) / world;
+    return ABRA_OK;
+}
+
 struct Model {
     abra_model_config cfg;
+    abra_tp_shard sh = {};
     int device = 0;
+    // tensor-parallel exchange arena (world > 1), one cudaMalloc shared by
+    // IPC: recv[2 * n_layers][world][hidden] fp32 partial sums (slot 2l: o of
+    // layer l, 2l+1: down), then u64 words: rank arrivals cnt[2 * n_layers + 1]
+    // (the last for the argmax keys), the combined argmax key, the step
+    // epoch, and this GPU's own CTA counters ccnt[2 * n_layers + 1].
+    uint8_t *arena = nullptr;
+    size_t arena_recv = 0, arena_bytes = 0;
+    uint8_t *peer[8] = {};  // every rank's arena as mapped here (peer[rank] == arena)
+    bool connected = false;
     std::vector<void *> allocs;
     uint8_t *embd = nullptr;
     float *out_norm = nullptr;
@@ -57,6 +97,16 @@ struct Model {
     size_t weight_bytes = 0, kv_bytes = 0;
     int32_t host_pos = 0;      // position after the queued steps (mirrors *pos)
     int32_t *pinned = nullptr; // 2 pinned ints for the streaming loop
+
+    float *recv(int q, int slot) const {  // rank q's partial in slot, in peer[..]'s layout
+        return reinterpret_cast<float *>(arena) + (static_cast<size_t>(slot) * sh.world + q) * cfg.hidden;
+    }
+    unsigned long long *cnt_of(uint8_t *base, int slot) const {
+        return reinterpret_cast<unsigned long long *>(base + arena_recv) + slot;
+    }
+    unsigned long long *key_of(uint8_t *base) const { return cnt_of(base, 2 * cfg.n_layers + 1); }
+    unsigned long long *epoch() const { return cnt_of(arena, 2 * cfg.n_layers + 2); }
+    unsigned long long *cta_cnt(int slot) const { return cnt_of(arena, 2 * cfg.n_layers + 3 + slot); }
 };
 
 static uint64_t tensor_id(int layer, int which) {
@@ -84,37 +134,62 @@ static size_t q4k_bytes(int64_t rows, int64_t cols) {
 
 static cudaError_t build(Model &m) {
     const abra_model_config &c = m.cfg;
+    const abra_tp_shard &sh = m.sh;
     const int flags = c.centered ? 1 : 0;
     const uint64_t s = c.seed;
-    const int64_t qkv_rows = static_cast<int64_t>(c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
-    const int64_t qd = static_cast<int64_t>(c.n_heads) * c.head_dim;
+    const int64_t hd = c.head_dim;
+    const int64_t qd = static_cast<int64_t>(c.n_heads) * hd, kvd = static_cast<int64_t>(c.n_kv_heads) * hd;
+    const int64_t qd_l = sh.q_heads * hd, kvd_l = sh.kv_heads * hd, qkv_l = qd_l + 2 * kvd_l;
+    const int64_t ffn_l = sh.ffn_hi - sh.ffn_lo, vocab_l = sh.vocab_hi - sh.vocab_lo;
+    const int64_t nsb_h = c.hidden / QK_K, nsb_o = qd / QK_K, nsb_f = c.ffn / QK_K;
     cudaStream_t st = m.stream;
-    auto q4k = [&](uint8_t **p, int64_t rows, int64_t cols, uint64_t tid) -> cudaError_t {
+    auto walloc = [&](uint8_t **p, int64_t rows, int64_t cols) -> cudaError_t {
         const size_t b = q4k_bytes(rows, cols);
         TRY(alloc(m, p, b));
         m.weight_bytes += b;
-        return launch_gen_q4k_ex(*p, rows * (cols / QK_K), s, tid, 0, flags, st);
+        return cudaSuccess;
+    };
+    // full-K rows [row0, row0 + n) of a tensor, at dst
+    auto rows = [&](uint8_t *dst, int64_t row0, int64_t n, uint64_t tid) -> cudaError_t {
+        return launch_gen_q4k_ex(dst, n * nsb_h, s, tid, row0 * nsb_h, flags, st);
     };
     auto norm = [&](float **p, int64_t n, uint64_t tid) -> cudaError_t {
         TRY(alloc(m, p, n * sizeof(float)));
         return launch_gen_norm_f32(*p, n, s, tid, st);
     };
-    TRY(q4k(&m.embd, c.vocab, c.hidden, tensor_id(-1, 1)));
+    // the whole tied table on every rank: embedding lookups need any row;
+    // the output MMVQ reads this rank's vocab rows of it
+    TRY(walloc(&m.embd, c.vocab, c.hidden));
+    TRY(rows(m.embd, 0, c.vocab, tensor_id(-1, 1)));
     TRY(norm(&m.out_norm, c.hidden, tensor_id(-1, 2)));
     m.layers.resize(c.n_layers);
     for (int l = 0; l < c.n_layers; ++l) {
         LayerW &y = m.layers[l];
         TRY(norm(&y.attn_norm, c.hidden, tensor_id(l, 0)));
-        TRY(q4k(&y.wqkv, qkv_rows, c.hidden, tensor_id(l, 1)));
+        // q|k|v rows of this rank's heads, fused: [q heads | k heads | v heads]
+        TRY(walloc(&y.wqkv, qkv_l, c.hidden));
+        const size_t rb = q4k_bytes(1, c.hidden);
+        TRY(rows(y.wqkv, sh.q_head_lo * hd, qd_l, tensor_id(l, 1)));
+        TRY(rows(y.wqkv + qd_l * rb, qd + sh.kv_head_lo * hd, kvd_l, tensor_id(l, 1)));
+        TRY(rows(y.wqkv + (qd_l + kvd_l) * rb, qd + kvd + sh.kv_head_lo * hd, kvd_l, tensor_id(l, 1)));
         TRY(norm(&y.q_norm, c.head_dim, tensor_id(l, 2)));
         TRY(norm(&y.k_norm, c.head_dim, tensor_id(l, 3)));
-        TRY(q4k(&y.wo, c.hidden, qd, tensor_id(l, 4)));
+        // o: K-shard = this rank's canonical slices = its heads' columns
+        TRY(walloc(&y.wo, c.hidden, qd_l));
+        TRY(launch_gen_q4k_cols(y.wo, c.hidden, nsb_o, slice_start(nsb_o, sh.sl_base),
+                                slice_start(nsb_o, sh.sl_base + sh.sl_cnt), s, tensor_id(l, 4), 0,
+                                flags, st));
         TRY(norm(&y.ffn_norm, c.hidden, tensor_id(l, 5)));
-        TRY(q4k(&y.wgate, c.ffn, c.hidden, tensor_id(l, 6)));
-        TRY(q4k(&y.wup, c.ffn, c.hidden, tensor_id(l, 7)));
-        TRY(q4k(&y.wdown, c.hidden, c.ffn, tensor_id(l, 8)));
+        TRY(walloc(&y.wgate, ffn_l, c.hidden));
+        TRY(rows(y.wgate, sh.ffn_lo, ffn_l, tensor_id(l, 6)));
+        TRY(walloc(&y.wup, ffn_l, c.hidden));
+        TRY(rows(y.wup, sh.ffn_lo, ffn_l, tensor_id(l, 7)));
+        // down: K-shard = this rank's FFN units
+        TRY(walloc(&y.wdown, c.hidden, ffn_l));
+        TRY(launch_gen_q4k_cols(y.wdown, c.hidden, nsb_f, sh.ffn_lo / QK_K, sh.ffn_hi / QK_K, s,
+                                tensor_id(l, 8), 0, flags, st));
     }
-    const size_t kv = static_cast<size_t>(c.n_layers) * c.n_kv_heads * c.max_ctx * c.head_dim * 2;
+    const size_t kv = static_cast<size_t>(c.n_layers) * sh.kv_heads * c.max_ctx * c.head_dim * 2;
     TRY(alloc(m, &m.kc, kv));
     TRY(alloc(m, &m.vc, kv));
     TRY(cudaMemsetAsync(m.kc, 0, kv, st));
@@ -134,22 +209,22 @@ static cudaError_t build(Model &m) {
     TRY(alloc(m, &m.rope, rope.size() * sizeof(float)));
     TRY(cudaMemcpyAsync(m.rope, rope.data(), rope.size() * sizeof(float), cudaMemcpyHostToDevice, st));
     m.max_chunks = (c.max_ctx + 255) / 256;
-    int64_t mx = c.hidden > c.ffn ? c.hidden : c.ffn;
-    if (qd > mx) mx = qd;
+    int64_t mx = c.hidden > ffn_l ? c.hidden : ffn_l;
+    if (qd_l > mx) mx = qd_l;
     TRY(alloc(m, &m.h, c.hidden * 4));
     TRY(alloc(m, &m.h2, c.hidden * 4));
     TRY(alloc(m, &m.delta, c.hidden * 4));
-    TRY(alloc(m, &m.qkv, qkv_rows * 4));
-    TRY(alloc(m, &m.q, qd * 4));
-    TRY(alloc(m, &m.att, qd * 4));
-    TRY(alloc(m, &m.part_m, static_cast<size_t>(c.n_heads) * m.max_chunks * 4));
-    TRY(alloc(m, &m.part_l, static_cast<size_t>(c.n_heads) * m.max_chunks * 4));
-    TRY(alloc(m, &m.part_o, static_cast<size_t>(c.n_heads) * m.max_chunks * c.head_dim * 4));
-    TRY(alloc(m, &m.act, c.ffn * 4));
-    TRY(alloc(m, &m.logits, static_cast<size_t>(c.vocab) * 4));
+    TRY(alloc(m, &m.qkv, qkv_l * 4));
+    TRY(alloc(m, &m.q, qd_l * 4));
+    TRY(alloc(m, &m.att, qd_l * 4));
+    TRY(alloc(m, &m.part_m, static_cast<size_t>(sh.q_heads) * m.max_chunks * 4));
+    TRY(alloc(m, &m.part_l, static_cast<size_t>(sh.q_heads) * m.max_chunks * 4));
+    TRY(alloc(m, &m.part_o, static_cast<size_t>(sh.q_heads) * m.max_chunks * c.head_dim * 4));
+    TRY(alloc(m, &m.act, ffn_l * 4));
+    TRY(alloc(m, &m.logits, static_cast<size_t>(vocab_l) * 4));
     TRY(alloc(m, &m.xq, (mx / QK8_1) * Q81_BYTES));
-    TRY(alloc(m, &m.oq, (qd / QK8_1) * Q81_BYTES));
-    TRY(alloc(m, &m.aq, (c.ffn / QK8_1) * Q81_BYTES));
+    TRY(alloc(m, &m.oq, (qd_l / QK8_1) * Q81_BYTES));
+    TRY(alloc(m, &m.aq, (ffn_l / QK8_1) * Q81_BYTES));
     TRY(alloc(m, &m.tokens, (c.max_ctx + 1) * 4));
     TRY(alloc(m, &m.picks, (c.max_ctx + 1) * 4));
     TRY(alloc(m, &m.pos, 4));
@@ -160,75 +235,159 @@ static cudaError_t build(Model &m) {
     TRY(cudaMemsetAsync(m.picks, 0, (c.max_ctx + 1) * 4, st));
     TRY(cudaMemsetAsync(m.pos, 0, 4, st));
     TRY(cudaMemsetAsync(m.nprompt, 0, 4, st));
+    if (sh.world > 1) {
+        const size_t recv = static_cast<size_t>(2 * c.n_layers) * sh.world * c.hidden * 4;
+        m.arena_recv = (recv + 255) / 256 * 256;
+        m.arena_bytes = m.arena_recv + (static_cast<size_t>(4 * c.n_layers + 4) * 8 + 255) / 256 * 256;
+        TRY(cudaMalloc(&m.arena, m.arena_bytes));
+        TRY(cudaMemsetAsync(m.arena, 0, m.arena_bytes, st));
+        m.peer[sh.rank] = m.arena;
+    }
     return cudaStreamSynchronize(st);
 }
 
-static cudaError_t mmvq(const Model &m, const void *w, const void *w2, const void *x, float *y,
-                        int64_t N, int64_t K, bool pdl, cudaStream_t st,
-                        unsigned long long *amax = nullptr) {
-    const int id = abra_tune_get(N, K, 1, w2 ? 2 : 1);
-    const MmvqConfig *cfg = mmvq_candidate_by_id(id);
-    if (!cfg) return cudaErrorInvalidValue;
-    return launch_mmvq_q4k(*cfg, w, w2, x, y, N, K, 1, N, pdl ? MMVQ_PDL : 0, st, amax);
+// Local MMVQ shapes of one rank: {N, K, nmat, fused RMSNorm input}.
+struct StepShapes {
+    int64_t qkv[4], o[4], gate_up[4], down[4], out[4];
+};
+
+static StepShapes step_shapes(const abra_model_config &c, const abra_tp_shard &sh) {
+    const int64_t hd = c.head_dim;
+    const int64_t qkv_l = (sh.q_heads + 2 * sh.kv_heads) * hd, qd_l = sh.q_heads * hd;
+    const int64_t ffn_l = sh.ffn_hi - sh.ffn_lo, vocab_l = sh.vocab_hi - sh.vocab_lo;
+    return {{qkv_l, c.hidden, 1, 1}, {c.hidden, qd_l, 1, 0}, {ffn_l, c.hidden, 2, 1},
+            {c.hidden, ffn_l, 1, 0}, {vocab_l, c.hidden, 1, 1}};
+}
+
+static const MmvqConfig *tuned(const int64_t sh[4]) {
+    return mmvq_candidate_by_id(abra_tune_get(sh[0], sh[1], 1, static_cast<int>(sh[2])));
 }
 
 // The decode step for the token at tokens[*pos] (recorded into the graph).
 static cudaError_t record_step(const Model &m, cudaStream_t st) {
     const abra_model_config &c = m.cfg;
+    const abra_tp_shard &sh = m.sh;
+    const int W = sh.world;
+    const bool tp = W > 1;
     const bool pdl = (c.flags & ABRA_MODEL_NO_PDL) == 0;
-    const int64_t qkv_rows = static_cast<int64_t>(c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
-    const int64_t qd = static_cast<int64_t>(c.n_heads) * c.head_dim;
-    const size_t kv_layer = static_cast<size_t>(c.n_kv_heads) * c.max_ctx * c.head_dim;
+    const int pf = pdl ? MMVQ_PDL : 0;
+    const StepShapes ss = step_shapes(c, sh);
+    const size_t kv_layer = static_cast<size_t>(sh.kv_heads) * c.max_ctx * c.head_dim;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
+    const int L = c.n_layers;
     DeltaSet none = {}, one = {};
     none.G = 0;
     one.p[0] = m.delta;
     one.G = 1;
+    // K-sharded outputs (o, down) of every rank land in slot 2l / 2l+1 of
+    // each rank's arena; the consumer sums them in the canonical tree
+    auto slot_deltas = [&](int slot) {
+        DeltaSet d = {};
+        d.G = W;
+        for (int q = 0; q < W; ++q) d.p[q] = m.recv(q, slot);
+        return d;
+    };
+    MmvqTp kshard;  // slicing of this rank's o / down K-shard
+    kshard.sl_nsb = 0;
+    if (tp) {
+        kshard.sl_base = sh.sl_base;
+        kshard.sl_cnt = sh.sl_cnt;
+    }
+    MmvqTp proto_o = kshard, proto_down = kshard;
+    proto_o.sl_nsb = static_cast<int>(c.n_heads * c.head_dim / QK_K);
+    proto_down.sl_nsb = c.ffn / QK_K;
+    // each rank's launch publishes once per step (its last CTA)
+    const int64_t per_o = W, per_down = W, per_out = W;
+    auto push_to = [&](MmvqTp &t, int slot) {
+        t.npeer = W;
+        t.cta_cnt = m.cta_cnt(slot);
+        for (int q = 0; q < W; ++q) {
+            t.peer_y[q] = reinterpret_cast<float *>(m.peer[q]) +
+                          (static_cast<size_t>(slot) * W + sh.rank) * c.hidden;
+            t.peer_cnt[q] = m.cnt_of(m.peer[q], slot);
+        }
+    };
+    auto wait_on = [&](MmvqTp &t, int slot, int64_t per_step) {
+        t.wait_cnt = m.cnt_of(m.arena, slot);
+        t.epoch = m.epoch();
+        t.wait_per_step = static_cast<unsigned long long>(per_step);
+    };
     // residual stream ping-pong: every MMVQ with a fused RMSNorm prologue
-    // reads h[cur] (+ the pending delta) and CTA 0 writes the sum to h[cur^1]
+    // reads h[cur] (+ the pending deltas) and CTA 0 writes the sum to h[cur^1]
     float *h[2] = {m.h, m.h2};
     int cur = 0;
     auto fused = [&](const void *w, const void *w2, const DeltaSet &ds, const float *norm,
-                     float *y, int64_t N, unsigned long long *amax) -> cudaError_t {
-        const MmvqConfig *cfg = mmvq_candidate_by_id(abra_tune_get(N, c.hidden, 1, w2 ? 2 : 1));
+                     float *y, const int64_t shp[4], unsigned long long *amax,
+                     const MmvqTp *t) -> cudaError_t {
+        const MmvqConfig *cfg = tuned(shp);
         if (!cfg) return cudaErrorInvalidValue;
         MmvqXin xin = {h[cur], h[cur ^ 1], ds, norm, c.eps};
         cur ^= 1;
-        return launch_mmvq_q4k_xin(*cfg, w, w2, xin, y, N, c.hidden, pdl ? MMVQ_PDL : 0, st, amax);
+        return launch_mmvq_q4k_xin(*cfg, w, w2, xin, y, shp[0], shp[1], pf, st, amax, t);
+    };
+    auto plain = [&](const void *w, const void *x, float *y, const int64_t shp[4],
+                     const MmvqTp *t) -> cudaError_t {
+        const MmvqConfig *cfg = tuned(shp);
+        if (!cfg) return cudaErrorInvalidValue;
+        return launch_mmvq_q4k(*cfg, w, nullptr, x, y, shp[0], shp[1], 1, shp[0], pf, st, nullptr, t);
     };
     TRY(launch_embed(m.embd, c.hidden, m.tokens, m.pos, h[cur], pdl, st));
-    for (int l = 0; l < c.n_layers; ++l) {
+    for (int l = 0; l < L; ++l) {
         const LayerW &y = m.layers[l];
         // residual + RMSNorm + Q8_1 fused into the q|k|v MMVQ
-        TRY(fused(y.wqkv, nullptr, l == 0 ? none : one, y.attn_norm, m.qkv, qkv_rows, nullptr));
+        MmvqTp tq;
+        if (tp && l > 0) wait_on(tq, 2 * l - 1, per_down);
+        TRY(fused(y.wqkv, nullptr, l == 0 ? none : (tp ? slot_deltas(2 * l - 1) : one), y.attn_norm,
+                  m.qkv, ss.qkv, nullptr, tp && l > 0 ? &tq : nullptr));
         TRY(launch_qk_norm_rope_kv(m.qkv, y.q_norm, y.k_norm, c.eps, m.rope, m.pos, m.q,
-                                   m.kc + l * kv_layer, m.vc + l * kv_layer, c.n_heads,
-                                   c.n_kv_heads, c.max_ctx, pdl, st));
+                                   m.kc + l * kv_layer, m.vc + l * kv_layer, sh.q_heads,
+                                   sh.kv_heads, c.max_ctx, pdl, st));
         TRY(launch_attention(m.q, m.kc + l * kv_layer, m.vc + l * kv_layer, m.pos, scale,
-                             c.n_heads, c.n_kv_heads, c.max_ctx, m.part_m, m.part_l, m.part_o,
+                             sh.q_heads, sh.kv_heads, c.max_ctx, m.part_m, m.part_l, m.part_o,
                              m.att, m.oq, pdl, st));
-        TRY(mmvq(m, y.wo, nullptr, m.oq, m.delta, c.hidden, qd, pdl, st));
+        MmvqTp to = proto_o;
+        if (tp) push_to(to, 2 * l);
+        TRY(plain(y.wo, m.oq, m.delta, ss.o, tp ? &to : nullptr));
         // residual + RMSNorm + Q8_1 fused into the gate/up SwiGLU MMVQ
-        TRY(fused(y.wgate, y.wup, one, y.ffn_norm, m.act, c.ffn, nullptr));
-        TRY(launch_quantize_q8_1(m.act, m.aq, c.ffn, 1, st));
-        TRY(mmvq(m, y.wdown, nullptr, m.aq, m.delta, c.hidden, c.ffn, pdl, st));
+        MmvqTp tg;
+        if (tp) wait_on(tg, 2 * l, per_o);
+        TRY(fused(y.wgate, y.wup, tp ? slot_deltas(2 * l) : one, y.ffn_norm, m.act, ss.gate_up,
+                  nullptr, tp ? &tg : nullptr));
+        TRY(launch_quantize_q8_1(m.act, m.aq, ss.gate_up[0], 1, st));
+        MmvqTp td = proto_down;
+        if (tp) push_to(td, 2 * l + 1);
+        TRY(plain(y.wdown, m.aq, m.delta, ss.down, tp ? &td : nullptr));
     }
-    // final residual + RMSNorm fused into the tied output MMVQ, which also
-    // reduces the greedy argmax (ties to the lowest id)
-    TRY(fused(m.embd, nullptr, c.n_layers > 0 ? one : none, m.out_norm, m.logits, c.vocab, m.amax));
-    return launch_argmax_finish(m.amax, m.tokens, m.picks, m.pos, m.nprompt, c.max_ctx, pdl, st);
+    // final residual + RMSNorm fused into the tied output MMVQ over this
+    // rank's vocab rows, which also reduces the greedy argmax (ties to the
+    // lowest id); with TP every rank's keys meet in every rank's key word
+    if (!tp) {
+        TRY(fused(m.embd, nullptr, L > 0 ? one : none, m.out_norm, m.logits, ss.out, m.amax, nullptr));
+        return launch_argmax_finish(m.amax, m.tokens, m.picks, m.pos, m.nprompt, c.max_ctx, pdl, st);
+    }
+    // this rank's CTAs reduce into the local key m.amax; the last one
+    // forwards it to every rank's combined key
+    MmvqTp tout;
+    tout.row_offset = static_cast<int>(sh.vocab_lo);
+    tout.npeer = W;
+    tout.cta_cnt = m.cta_cnt(2 * L);
+    for (int q = 0; q < W; ++q) {
+        tout.peer_amax[q] = m.key_of(m.peer[q]);
+        tout.peer_cnt[q] = m.cnt_of(m.peer[q], 2 * L);
+    }
+    if (L > 0) wait_on(tout, 2 * L - 1, per_down);
+    const uint8_t *out_w = m.embd + static_cast<size_t>(sh.vocab_lo) * q4k_bytes(1, c.hidden);
+    TRY(fused(out_w, nullptr, L > 0 ? slot_deltas(2 * L - 1) : none, m.out_norm, m.logits, ss.out,
+              m.amax, &tout));
+    return launch_argmax_finish(m.key_of(m.arena), m.tokens, m.picks, m.pos, m.nprompt, c.max_ctx,
+                                pdl, st, m.cnt_of(m.arena, 2 * L), m.epoch(),
+                                static_cast<unsigned long long>(per_out));
 }
 
 static cudaError_t prepare(const Model &m) {
-    const abra_model_config &c = m.cfg;
-    const int64_t qkv_rows = static_cast<int64_t>(c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
-    const int64_t qd = static_cast<int64_t>(c.n_heads) * c.head_dim;
-    // {N, K, nmat, fused RMSNorm input}
-    const int64_t shapes[5][4] = {{qkv_rows, c.hidden, 1, 1}, {c.hidden, qd, 1, 0},
-                                  {c.ffn, c.hidden, 2, 1}, {c.hidden, c.ffn, 1, 0},
-                                  {c.vocab, c.hidden, 1, 1}};
-    for (const auto &sh : shapes) {
-        const MmvqConfig *cfg = mmvq_candidate_by_id(abra_tune_get(sh[0], sh[1], 1, static_cast<int>(sh[2])));
+    const StepShapes ss = step_shapes(m.cfg, m.sh);
+    for (const int64_t *sh : {ss.qkv, ss.o, ss.gate_up, ss.down, ss.out}) {
+        const MmvqConfig *cfg = tuned(sh);
         if (!cfg) return cudaErrorInvalidValue;
         TRY(prepare_mmvq(*cfg, 1, static_cast<int>(sh[2]), sh[3] != 0));
     }
@@ -287,7 +446,18 @@ int abra_model_default_config(abra_model_config *c) {
 
 const char *abra_model_last_error(void) { return g_model_err; }
 
+int abra_tp_shard_info(const abra_model_config *cfg, int32_t rank, int32_t world,
+                       abra_tp_shard *out) {
+    if (!cfg || !out) return model_fail(ABRA_E_INVALID, "null pointer", cudaSuccess);
+    const int rc = abra::tp_shard(*cfg, rank, world, *out);
+    return rc == ABRA_OK ? ABRA_OK : model_fail(rc, "no tensor-parallel split of this configuration", cudaSuccess);
+}
+
 int abra_model_create(const abra_model_config *cfg, void **out) {
+    return abra_model_create_tp(cfg, 0, 1, out);
+}
+
+int abra_model_create_tp(const abra_model_config *cfg, int32_t rank, int32_t world, void **out) {
     if (!cfg || !out) return model_fail(ABRA_E_INVALID, "null pointer", cudaSuccess);
     const abra_model_config &c = *cfg;
     if (c.head_dim != 128 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads ||
@@ -295,9 +465,14 @@ int abra_model_create(const abra_model_config *cfg, void **out) {
         (c.n_heads * c.head_dim) % 256 || c.vocab <= 0 || c.max_ctx <= 0 || c.n_layers < 0 ||
         c.hidden > 16384)
         return model_fail(ABRA_E_UNSUPPORTED, "unsupported model configuration", cudaSuccess);
+    abra_tp_shard shard = {};
+    const int src = abra::tp_shard(c, rank, world, shard);
+    if (src != ABRA_OK) return model_fail(src, "no tensor-parallel split of this configuration", cudaSuccess);
     Model *m = new (std::nothrow) Model();
     if (!m) return model_fail(ABRA_E_INVALID, "out of host memory", cudaSuccess);
     m->cfg = c;
+    m->sh = shard;
+    m->connected = world == 1;
     cudaGetDevice(&m->device);
     cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = abra::build(*m);
@@ -315,10 +490,45 @@ int abra_model_destroy(void *model) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->pinned) cudaFreeHost(m->pinned);
+    for (int q = 0; q < m->sh.world; ++q)
+        if (m->peer[q] && m->peer[q] != m->arena) cudaIpcCloseMemHandle(m->peer[q]);
+    if (m->arena) cudaFree(m->arena);
     for (void *p : m->allocs) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
     return ABRA_OK;
+}
+
+int abra_model_tp_handle(void *model, void *handle, int32_t size) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || !handle || size < static_cast<int32_t>(sizeof(cudaIpcMemHandle_t)))
+        return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
+    if (!m->arena) return model_fail(ABRA_E_INVALID, "not a tensor-parallel model", cudaSuccess);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, m->arena);
+    if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "cudaIpcGetMemHandle", e);
+    std::memcpy(handle, &h, sizeof h);
+    return ABRA_OK;
+}
+
+int abra_model_tp_connect(void *model, const void *handles, int32_t size_each) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || !handles || size_each < static_cast<int32_t>(sizeof(cudaIpcMemHandle_t)))
+        return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
+    if (!m->arena || m->connected) return model_fail(ABRA_E_INVALID, "not a fresh tensor-parallel model", cudaSuccess);
+    for (int q = 0; q < m->sh.world; ++q) {
+        if (q == m->sh.rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t *>(handles) + static_cast<size_t>(q) * size_each, sizeof h);
+        void *p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "cudaIpcOpenMemHandle", e);
+        m->peer[q] = static_cast<uint8_t *>(p);
+    }
+    m->connected = true;
+    // record the step now, so that the ranks' first steps start together
+    cudaError_t e = abra::capture(*m);
+    return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "graph capture", e);
 }
 
 int abra_model_reset(void *model, const int32_t *prompt, int32_t n_prompt) {
@@ -342,6 +552,7 @@ int abra_model_step(void *model, int32_t n_steps) {
     if (!m || n_steps < 0) return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
     if (static_cast<int64_t>(m->host_pos) + n_steps > m->cfg.max_ctx)
         return model_fail(ABRA_E_INVALID, "steps would pass max_ctx", cudaSuccess);
+    if (!m->connected) return model_fail(ABRA_E_INVALID, "tensor-parallel model not connected", cudaSuccess);
     m->host_pos += n_steps;
     cudaError_t e = abra::capture(*m);
     if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "graph capture", e);
@@ -368,7 +579,8 @@ int abra_model_read(void *model, int32_t *tokens, int32_t n_tokens, float *logit
     if (e == cudaSuccess && tokens && n_tokens)
         e = cudaMemcpy(tokens, m->tokens, n_tokens * 4, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && logits)
-        e = cudaMemcpy(logits, m->logits, static_cast<size_t>(m->cfg.vocab) * 4, cudaMemcpyDeviceToHost);
+        e = cudaMemcpy(logits, m->logits, static_cast<size_t>(m->sh.vocab_hi - m->sh.vocab_lo) * 4,
+                       cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && pos) e = cudaMemcpy(pos, m->pos, 4, cudaMemcpyDeviceToHost);
     return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "read", e);
 }
@@ -394,6 +606,7 @@ int abra_model_decode_streaming(void *model, int32_t n, int32_t *out) {
     if (!m || !out || n < 1) return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
     if (static_cast<int64_t>(m->host_pos) + n > m->cfg.max_ctx)
         return model_fail(ABRA_E_INVALID, "steps would pass max_ctx", cudaSuccess);
+    if (!m->connected) return model_fail(ABRA_E_INVALID, "tensor-parallel model not connected", cudaSuccess);
     cudaError_t e = abra::capture(*m);
     if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "graph capture", e);
     if (!m->pinned) {

@@ -1,4 +1,4 @@
-"""Qwen3-4B-shaped Q4_K decode on one B200.
+"""Qwen3-4B-shaped Q4_K decode on B200: one GPU, or tensor parallel over 2/4/8.
 
 Thin host wrapper of the native runtime in libabra_b200 (abra_model_* in
 include/abra_b200.h): weights are generated on the device from a seed, the
@@ -23,8 +23,42 @@ class ModelConfig(C.Structure):
                 ("flags", C.c_int32)]
 
 
+class TpShard(C.Structure):
+    """What one rank of a tensor-parallel group holds (abra_tp_shard)."""
+    _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("q_head_lo", C.c_int32),
+                ("q_heads", C.c_int32), ("kv_head_lo", C.c_int32), ("kv_heads", C.c_int32),
+                ("ffn_lo", C.c_int32), ("ffn_hi", C.c_int32), ("sl_base", C.c_int32),
+                ("sl_cnt", C.c_int32), ("vocab_lo", C.c_int64), ("vocab_hi", C.c_int64)]
+
+    def as_dict(self) -> dict:
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
 EAGER = 1   # ABRA_MODEL_EAGER
 NO_PDL = 2  # ABRA_MODEL_NO_PDL
+IPC_HANDLE_BYTES = 64
+
+
+def exchange_handles(mine: bytes, world: int, group=None) -> bytes:
+    """All ranks' fixed-size handles, concatenated in rank order (one
+    all_gather over the torch.distributed group)."""
+    import torch.distributed as dist
+
+    if len(mine) != IPC_HANDLE_BYTES:
+        raise ValueError(f"handle must be {IPC_HANDLE_BYTES} bytes")
+    handles = [None] * world
+    dist.all_gather_object(handles, mine, group=group)
+    if any(not isinstance(h, bytes) or len(h) != IPC_HANDLE_BYTES for h in handles):
+        raise RuntimeError("a rank sent a malformed arena handle")
+    return b"".join(handles)
+
+
+def shard_info(rank: int, world: int, **config) -> TpShard:
+    """The split rank `rank` of `world` would hold (no GPU needed)."""
+    c = default_config(**config)
+    s = TpShard()
+    _check(_lib.lib.abra_tp_shard_info(C.byref(c), rank, world, C.byref(s)), "abra_tp_shard_info")
+    return s
 
 
 def default_config(**overrides) -> ModelConfig:
@@ -42,14 +76,37 @@ def _check(rc: int, what: str) -> None:
 
 
 class DecodeModel:
-    """A seeded Qwen3-4B-shaped model resident on the current CUDA device."""
+    """A seeded Qwen3-4B-shaped model resident on the current CUDA device.
 
-    def __init__(self, **config):
+    With ``world > 1`` this process holds rank ``rank`` of a tensor-parallel
+    group (one process per GPU): the ranks exchange their arenas' IPC handles
+    through ``torch.distributed`` (``group``, default the world group) and
+    from then on talk only over NVLink, inside the decode graph.  Every rank
+    must make the same calls in the same order.
+    """
+
+    def __init__(self, rank: int = 0, world: int = 1, group=None, **config):
         self.handle = None
         self.cfg = default_config(**config)
+        self.shard = shard_info(rank, world, **config)
         h = C.c_void_p()
-        _check(_lib.lib.abra_model_create(C.byref(self.cfg), C.byref(h)), "abra_model_create")
+        _check(_lib.lib.abra_model_create_tp(C.byref(self.cfg), rank, world, C.byref(h)),
+               "abra_model_create_tp")
         self.handle = h
+        if world > 1:
+            self._connect(group)
+
+    def _connect(self, group) -> None:
+        mine = C.create_string_buffer(IPC_HANDLE_BYTES)
+        _check(_lib.lib.abra_model_tp_handle(self.handle, mine, IPC_HANDLE_BYTES),
+               "abra_model_tp_handle")
+        allh = exchange_handles(bytes(mine.raw), self.shard.world, group)
+        buf = C.create_string_buffer(allh, len(allh))
+        _check(_lib.lib.abra_model_tp_connect(self.handle, buf, IPC_HANDLE_BYTES),
+               "abra_model_tp_connect")
+        import torch.distributed as dist
+
+        dist.barrier(group=group)  # every rank mapped its peers and recorded its step
 
     def close(self) -> None:
         if self.handle:
@@ -83,7 +140,8 @@ class DecodeModel:
         return out
 
     def logits(self) -> np.ndarray:
-        out = np.empty(self.cfg.vocab, dtype=np.float32)
+        """The last step's logits of this rank's vocab rows [vocab_lo, vocab_hi)."""
+        out = np.empty(self.shard.vocab_hi - self.shard.vocab_lo, dtype=np.float32)
         _check(_lib.lib.abra_model_read(self.handle, None, 0, out.ctypes.data, None), "abra_model_read")
         return out
 

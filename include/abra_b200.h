@@ -79,6 +79,19 @@ int abra_q4k_mmvq_combined(int32_t candidate, const void *w_q4k, const float *x,
 int abra_q4k_mmvq_combined_static(int32_t candidate, const void *w_q4k, const float *x,
                                   float *y, int64_t N, int64_t K, int32_t ncols, void *stream);
 
+/* Row-parallel (K-sharded) MMVQ: w holds columns [k0, k0 + K) of an
+ * N x K_full matrix, where [k0, k0 + K) are the canonical K-slices
+ * [sl_base, sl_base + sl_cnt) of K_full (slice i of a row of n = K_full/256
+ * superblocks starts at superblock i*(n/8) + min(i, n%8)); x holds the same
+ * K activations.  y gets this shard's partial sums, each a subtree of the
+ * unsharded sum, so adding the shards' partials in the fixed tree
+ * (2: p0+p1; 4: (p0+p1)+(p2+p3); 8: three levels) reproduces the unsharded
+ * y bit for bit.  The reference's tensor split sums its shards with an
+ * NCCL all-reduce instead (docs/research/1080ti-speed-results.md:76-81). */
+int abra_q4k_mmvq_kshard(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, int64_t K,
+                         int32_t ncols, int64_t K_full, int32_t sl_base, int32_t sl_cnt,
+                         int32_t candidate, void *stream);
+
 /* Full form: explicit output column stride ldy >= N, candidate (0 = tuned)
  * and ABRA_MMVQ_* flags. */
 int abra_q4k_mmvq_ex(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, int64_t K,
@@ -151,7 +164,7 @@ int abra_tune_get(int64_t N, int64_t K, int32_t ncols, int32_t nmat); /* candida
 int abra_tune_clear(void);
 
 /* ------------------------------------------------------ decode model --- */
-/* Qwen3-4B-shaped decode with every linear layer Q4_K (BASELINE config 3):
+/* Qwen3-4B-shaped decode with every linear layer Q4_K:
  * the native runtime that the reference delegates to llama.cpp.  Weights
  * are generated on the device from a seed (the same counter-based generator
  * as abra_gen_q4k; tensor ids: 1 embedding/output (tied), 2 output norm,
@@ -192,6 +205,43 @@ int abra_model_generate(void *model, const int32_t *prompt, int32_t n_prompt, in
 int abra_model_decode_streaming(void *model, int32_t n, int32_t *out);
 int abra_model_info(void *model, void **stream, uint64_t *weight_bytes, uint64_t *kv_bytes);
 const char *abra_model_last_error(void);
+
+/* ------------------------------------------- tensor-parallel decode --- */
+/* The same model split over world = 2, 4 or 8 GPUs of one node, one process
+ * (or thread) per GPU.  Replaces the reference's llama.cpp tensor split with
+ * an fp32 all-reduce after attn_output and ffn_down and its tied-output vocab
+ * split (tools/prepare-output-split.py:8-32, runtime argmax
+ * tests/runtime_logits.cpp:101).  Heads, FFN units and vocab rows are split;
+ * o and down are K-sharded on canonical K-slice boundaries and each rank
+ * pushes its fp32 partial sums straight from the MMVQ epilogue into every
+ * rank's exchange arena over NVLink (peer stores, then a release counter);
+ * the next kernel waits (bounded) for all ranks and adds the partials in the
+ * fixed slice tree, so logits and greedy tokens are bit-identical to the
+ * single-GPU model for every world size.  The argmax keys meet the same way.
+ * Every rank must run the same sequence of calls; destroy only after all
+ * ranks have finished stepping (a barrier), since peers write into each
+ * other's arenas. */
+typedef struct {
+    int32_t rank, world;
+    int32_t q_head_lo, q_heads, kv_head_lo, kv_heads; /* this rank's heads */
+    int32_t ffn_lo, ffn_hi;    /* rows of gate/up and columns of down */
+    int32_t sl_base, sl_cnt;   /* canonical K-slices of o and down held here */
+    int64_t vocab_lo, vocab_hi; /* rows of the tied output (logits held here) */
+} abra_tp_shard;
+
+/* The split a rank would hold (no GPU needed); ABRA_E_UNSUPPORTED when the
+ * configuration has no split at this world size. */
+int abra_tp_shard_info(const abra_model_config *cfg, int32_t rank, int32_t world,
+                       abra_tp_shard *out);
+/* Build this rank's shard on the current device (world == 1 is
+ * abra_model_create). */
+int abra_model_create_tp(const abra_model_config *cfg, int32_t rank, int32_t world,
+                         void **model);
+/* The 64-byte CUDA IPC handle of this rank's exchange arena. */
+int abra_model_tp_handle(void *model, void *handle, int32_t size);
+/* Map every other rank's arena (handles: world entries of size_each bytes,
+ * indexed by rank).  Required before the first step. */
+int abra_model_tp_connect(void *model, const void *handles, int32_t size_each);
 
 #ifdef __cplusplus
 }

@@ -354,3 +354,31 @@ def qk_norm_rope(qkv, q_norm, k_norm, eps, cs_row, n_heads, n_kv, hd):
 
 def argmax(x: np.ndarray) -> int:
     return int(lib.orc_argmax(np.ascontiguousarray(x, dtype=np.float32), x.size))
+
+
+# --------------------------------------------------- K-shard arithmetic ---
+def tree8(v: np.ndarray) -> np.ndarray:
+    """The canonical fp32 tree over the last axis (8 slice sums):
+    ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7))."""
+    v = np.asarray(v, dtype=np.float32)
+    a = (v[..., 0] + v[..., 1]) + (v[..., 2] + v[..., 3])
+    b = (v[..., 4] + v[..., 5]) + (v[..., 6] + v[..., 7])
+    return (a + b).astype(np.float32)
+
+
+def kshard_partial(slices: np.ndarray, sl_base: int, sl_cnt: int) -> np.ndarray:
+    """A K-shard's partial sum as the kernel forms it: its global slices
+    [sl_base, sl_base + sl_cnt) as local slices 0.., the rest +0.0, then the
+    canonical tree."""
+    local = np.zeros(slices.shape, dtype=np.float32)
+    local[..., :sl_cnt] = slices[..., sl_base:sl_base + sl_cnt]
+    return tree8(local)
+
+
+def delta_tree(parts) -> np.ndarray:
+    """Fixed tree over G partials: 1: p0; 2: p0+p1; 4: (p0+p1)+(p2+p3);
+    8: ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7))."""
+    p = [np.asarray(x, dtype=np.float32) for x in parts]
+    while len(p) > 1:
+        p = [(p[i] + p[i + 1]).astype(np.float32) for i in range(0, len(p), 2)]
+    return p[0]

@@ -5,7 +5,7 @@
 // timing comparison, never as part of libabra_b200.
 //
 // The reference's kernels/q4k/q4k_q8_mmvq.cu and q4k_family.cu are compiled
-// from /root/reference as they are (see oracle/Makefile).  They reference
+// from the reference tree as they are (see oracle/Makefile).  They reference
 // the upstream ggml adapter (kernels/q4k/upstream_adapter.cuh:12-26), whose
 // definition needs llama.cpp/ggml sources that are not available; the two
 // symbols are defined here to record the call and do nothing, so that only

@@ -1,6 +1,6 @@
 """GPU parity tests of the Q4_K x Q8_1 path, through the C ABI.
 
-Bar (BASELINE north star): per-sub-block int32 dot products bit-exact;
+Bar: per-sub-block int32 dot products bit-exact;
 fp32 outputs within 1e-5 of each row's |w|.|x| scale against the f64 oracle.
 The kernels follow the oracle's canonical fp32 order, so they are also
 checked bit-for-bit against the canonical fp32 oracle.
@@ -15,7 +15,7 @@ from conftest import to_dev, tol_check
 
 pytestmark = pytest.mark.gpu
 
-TOL = 1e-5  # of sum_k |w_k| |x_k|, per row
+TOL = 1e-5  # of sum_k |w_k| |x_k|, per row (the path's stated tolerance)
 
 
 def _case(N, K, ncols, seed=0, tid=0):

@@ -1,4 +1,4 @@
-"""GPU parity of the Qwen3-4B-shaped decode runtime (BASELINE config 3)
+"""GPU parity of the Qwen3-4B-shaped decode runtime
 against the CPU oracle model, through the C ABI.
 
 The runtime follows the oracle's operation order everywhere, so the bar is
