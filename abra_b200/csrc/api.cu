@@ -130,11 +130,11 @@ int abra_q4k_mmvq(const void *w, const void *x, float *y, int64_t N, int64_t K, 
 
 int abra_q4k_mmvq_kshard(const void *w, const void *x, float *y, int64_t N, int64_t K,
                          int32_t ncols, int64_t K_full, int32_t sl_base, int32_t sl_cnt,
-                         int32_t candidate, void *stream) {
+                         int32_t candidate, int32_t flags, void *stream) {
     int rc = check_mmvq_args(w, x, y, N, K, ncols, N);
     if (rc) return rc;
-    if (K_full <= 0 || K_full % 256 != 0 || K_full > 65536 || sl_base < 0 || sl_cnt < 1 ||
-        sl_base + sl_cnt > 8)
+    if (K_full <= 0 || K_full % 256 != 0 || K_full > 65536 || sl_base < 0 ||
+        !(sl_cnt == 1 || sl_cnt == 2 || sl_cnt == 4 || sl_cnt == 8) || sl_base + sl_cnt > 8)
         return fail(ABRA_E_INVALID, "bad K-shard (K_full=%lld sl_base=%d sl_cnt=%d)",
                     (long long)K_full, sl_base, sl_cnt);
     const int nsb_g = static_cast<int>(K_full / 256);
@@ -145,11 +145,12 @@ int abra_q4k_mmvq_kshard(const void *w, const void *x, float *y, int64_t N, int6
     if (id == 0) id = abra_tune_get(N, K, ncols, 1);
     const abra::MmvqConfig *cfg = abra::mmvq_candidate_by_id(id);
     if (!cfg) return fail(ABRA_E_INVALID, "unknown candidate id %d", id);
-    abra::MmvqTp tp;
+    abra::MmvqOpts tp;
     tp.sl_nsb = nsb_g;
     tp.sl_base = sl_base;
     tp.sl_cnt = sl_cnt;
-    cudaError_t e = abra::launch_mmvq_q4k(*cfg, w, nullptr, x, y, N, K, ncols, N, 0,
+    cudaError_t e = abra::launch_mmvq_q4k(*cfg, w, nullptr, x, y, N, K, ncols, N,
+                                          (flags & ABRA_MMVQ_PDL) ? abra::MMVQ_PDL : 0,
                                           static_cast<cudaStream_t>(stream), nullptr, &tp);
     if (e != cudaSuccess) return cuda_fail(e, "mmvq launch");
     return ABRA_OK;

@@ -26,8 +26,9 @@ enum : int {
     MMVQ_PDL = 1,  // launch with programmatic dependent launch (weights must be immutable)
 };
 
-// Tensor-parallel options of one MMVQ launch (all off by default).
-struct MmvqTp {
+// Options of one MMVQ launch (all off by default): tensor-parallel slicing,
+// push and wait, and an L2 prefetch of other weights.
+struct MmvqOpts {
     // K-shard slicing: the shard holds global canonical slices
     // [sl_base, sl_base + sl_cnt) of rows of sl_nsb superblocks (0: unsharded)
     int sl_nsb = 0, sl_base = 0, sl_cnt = 8;
@@ -45,6 +46,10 @@ struct MmvqTp {
     const unsigned long long *wait_cnt = nullptr;
     const unsigned long long *epoch = nullptr;
     unsigned long long wait_per_step = 0;
+    // L2 prefetch of up to two regions (the next kernels' weights), split
+    // evenly over the CTAs; 16-byte aligned, sizes multiples of 16
+    const void *pf_ptr[2] = {};
+    int64_t pf_bytes[2] = {};
 };
 
 // w2 != nullptr selects the fused gate/up form: y = (w2 x) * silu(w x).
@@ -53,10 +58,10 @@ struct MmvqTp {
 cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2,
                             const void *x_q8, float *y, int64_t N, int64_t K, int ncols,
                             int64_t ldy, int flags, cudaStream_t stream,
-                            unsigned long long *amax = nullptr, const MmvqTp *tp = nullptr);
+                            unsigned long long *amax = nullptr, const MmvqOpts *tp = nullptr);
 // Grid size the launch above would use (for arrival counts).
 int mmvq_grid(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, bool xin,
-              const MmvqTp *tp = nullptr);
+              const MmvqOpts *tp = nullptr);
 // Fused input of launch_mmvq_q4k_xin: x = h_in + tree(deltas) (written to
 // h_out when not null), quantized as Q8_1 of RMSNorm(x) * norm_w.
 struct MmvqXin {
@@ -71,7 +76,7 @@ struct MmvqXin {
 cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void *w2,
                                 const MmvqXin &xin, float *y, int64_t N, int64_t K, int flags,
                                 cudaStream_t stream, unsigned long long *amax = nullptr,
-                                const MmvqTp *tp = nullptr);
+                                const MmvqOpts *tp = nullptr);
 
 // Sets the kernel attributes a later launch of this candidate needs (done
 // outside stream capture).

@@ -102,30 +102,33 @@ struct MmvqPlan {
 
 // Slicing of a launch: unsharded unless tp names a K-shard.  Returns false
 // when the shard's slices do not add up to nsb superblocks.
-static bool shard_of(const MmvqTp *tp, int nsb, int &sl_nsb, int &sl_base, int &sl_cnt) {
+static bool shard_of(const MmvqOpts *tp, int nsb, int &sl_nsb, int &sl_base, int &sl_shift) {
     sl_nsb = nsb;
     sl_base = 0;
-    sl_cnt = 8;
+    int sl_cnt = 8;
     if (tp && tp->sl_nsb > 0) {
         sl_nsb = tp->sl_nsb;
         sl_base = tp->sl_base;
         sl_cnt = tp->sl_cnt;
     }
-    if (sl_base < 0 || sl_cnt < 1 || sl_base + sl_cnt > 8) return false;
-    return shard_slice(sl_nsb, sl_base, sl_cnt, 8) == nsb;
+    if (sl_base < 0 || !(sl_cnt == 1 || sl_cnt == 2 || sl_cnt == 4 || sl_cnt == 8) ||
+        sl_base + sl_cnt > 8)
+        return false;
+    sl_shift = sl_cnt == 8 ? 0 : sl_cnt == 4 ? 1 : sl_cnt == 2 ? 2 : 3;
+    return shard_slice(sl_nsb, sl_base, sl_shift, 8) == nsb;
 }
 
 static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int nmat,
-                      MmvqPlan &pl, bool xin = false, const MmvqTp *tp = nullptr) {
+                      MmvqPlan &pl, bool xin = false, const MmvqOpts *tp = nullptr) {
     const int ks = cfg.ks;
     const bool staged = cfg.mode != MODE_DIRECT;
     const int nsl = 8 / ks;
-    int sl_nsb, sl_base, sl_cnt;
-    if (!shard_of(tp, nsb, sl_nsb, sl_base, sl_cnt)) return false;
+    int sl_nsb, sl_base, sl_shift;
+    if (!shard_of(tp, nsb, sl_nsb, sl_base, sl_shift)) return false;
     int max_sb = 0;
     for (int j = 0; j < ks; ++j) {
-        const int w = shard_slice(sl_nsb, sl_base, sl_cnt, (j + 1) * nsl) -
-                      shard_slice(sl_nsb, sl_base, sl_cnt, j * nsl);
+        const int w = shard_slice(sl_nsb, sl_base, sl_shift, (j + 1) * nsl) -
+                      shard_slice(sl_nsb, sl_base, sl_shift, j * nsl);
         max_sb = w > max_sb ? w : max_sb;
     }
     const int max_part = max_sb * Q4K_BYTES;
@@ -169,8 +172,8 @@ static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int 
 }
 
 // Copies the tensor-parallel options into the kernel parameters.
-static bool apply_tp(MmvqParams &prm, const MmvqTp *tp) {
-    if (!shard_of(tp, prm.nsb, prm.sl_nsb, prm.sl_base, prm.sl_cnt)) return false;
+static bool apply_tp(MmvqParams &prm, const MmvqOpts *tp) {
+    if (!shard_of(tp, prm.nsb, prm.sl_nsb, prm.sl_base, prm.sl_shift)) return false;
     if (!tp) return true;
     if (tp->npeer < 0 || tp->npeer > 8) return false;
     prm.row_offset = tp->row_offset;
@@ -186,6 +189,12 @@ static bool apply_tp(MmvqParams &prm, const MmvqTp *tp) {
     prm.wait_cnt = tp->wait_cnt;
     prm.epoch = tp->epoch;
     prm.wait_per_step = tp->wait_per_step;
+    for (int r = 0; r < 2; ++r) {
+        if (tp->pf_bytes[r] <= 0) continue;
+        if ((reinterpret_cast<uintptr_t>(tp->pf_ptr[r]) & 15) || (tp->pf_bytes[r] & 15)) return false;
+        prm.pf_ptr[r] = static_cast<const uint8_t *>(tp->pf_ptr[r]);
+        prm.pf_bytes[r] = tp->pf_bytes[r];
+    }
     return !prm.wait_cnt || prm.epoch;
 }
 
@@ -212,7 +221,7 @@ static cudaError_t launch_plan(MmvqFn fn, const MmvqPlan &pl, bool pdl, MmvqPara
 cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2,
                             const void *x_q8, float *y, int64_t N, int64_t K, int ncols,
                             int64_t ldy, int flags, cudaStream_t stream,
-                            unsigned long long *amax, const MmvqTp *tp) {
+                            unsigned long long *amax, const MmvqOpts *tp) {
     const int nsb = static_cast<int>(K / QK_K);
     const int nmat = w2 ? 2 : 1;
     const MmvqTable *t = table_for(ncols);
@@ -236,7 +245,7 @@ cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2
 }
 
 int mmvq_grid(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, bool xin,
-              const MmvqTp *tp) {
+              const MmvqOpts *tp) {
     MmvqPlan pl;
     if (!plan_mmvq(cfg, N, static_cast<int>(K / QK_K), ncols, nmat, pl, xin, tp)) return -1;
     return pl.grid;
@@ -244,7 +253,7 @@ int mmvq_grid(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, 
 
 cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void *w2,
                                 const MmvqXin &xin, float *y, int64_t N, int64_t K, int flags,
-                                cudaStream_t stream, unsigned long long *amax, const MmvqTp *tp) {
+                                cudaStream_t stream, unsigned long long *amax, const MmvqOpts *tp) {
     const int nsb = static_cast<int>(K / QK_K);
     const int nmat = w2 ? 2 : 1;
     const int ki = ks_index(cfg.ks);

@@ -55,11 +55,13 @@ struct MmvqParams {
     DeltaSet deltas;
     const float *norm_w;
     float eps;
-    // K-shard slicing: local canonical slice i is global slice sl_base + i of
-    // a row of sl_nsb superblocks for i < sl_cnt, and empty after that, so a
-    // shard's sum is a subtree of the unsharded tree (sl_nsb == nsb,
+    // K-shard slicing (sl_cnt in 1, 2, 4, 8): the shard holds global canonical
+    // slices [sl_base, sl_base + sl_cnt) of rows of sl_nsb superblocks; they
+    // sit at local slices 0, s, 2s, .. (stride s = 8 / sl_cnt) and the other
+    // local slices are empty (+0.0), so the local tree is the shard's subtree
+    // of the unsharded tree and every k-part gets real work (sl_nsb == nsb,
     // sl_base == 0, sl_cnt == 8 when K is not sharded).
-    int sl_nsb, sl_base, sl_cnt;
+    int sl_nsb, sl_base, sl_shift;  // sl_shift = log2(8 / sl_cnt)
     int row_offset;  // added to row ids in argmax keys (vocab shards)
     // Tensor-parallel push (npeer > 0): output rows go to peer_y[q] for every
     // rank q; each CTA then counts itself on cta_cnt (GPU scope, acq_rel), and
@@ -76,11 +78,34 @@ struct MmvqParams {
     const unsigned long long *wait_cnt;
     const unsigned long long *epoch;
     unsigned long long wait_per_step;
+    // L2 prefetch of the next kernels' weights, split evenly over the CTAs
+    const uint8_t *pf_ptr[2];
+    int64_t pf_bytes[2];
 };
 
-// First superblock (relative to the shard) of local canonical slice i.
-__host__ __device__ __forceinline__ int shard_slice(int sl_nsb, int sl_base, int sl_cnt, int i) {
-    return slice_start(sl_nsb, sl_base + (i < sl_cnt ? i : sl_cnt)) - slice_start(sl_nsb, sl_base);
+// This CTA's share of the L2 prefetch regions, issued by one warp in 16 KB
+// pieces.
+__device__ __forceinline__ void prefetch_share(const MmvqParams &prm, int lane) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int64_t units = prm.pf_bytes[r] >> 4;  // 16-byte units
+        if (units <= 0) continue;
+        const int64_t u0 = units * blockIdx.x / gridDim.x;
+        const int64_t u1 = units * (blockIdx.x + 1) / gridDim.x;
+        constexpr int64_t PIECE = 1024;  // 16 KB
+        for (int64_t u = u0 + lane * PIECE; u < u1; u += 32 * PIECE) {
+            const int64_t n = u1 - u < PIECE ? u1 - u : PIECE;
+            prefetch_l2_bulk(prm.pf_ptr[r] + (u << 4), static_cast<uint32_t>(n << 4));
+        }
+    }
+}
+
+// First superblock (relative to the shard) of local canonical slice i
+// (0 <= i <= 8): the real slices before it are those at multiples of the
+// stride 2^sl_shift below i.
+__host__ __device__ __forceinline__ int shard_slice(int sl_nsb, int sl_base, int sl_shift, int i) {
+    return slice_start(sl_nsb, sl_base + ((i + (1 << sl_shift) - 1) >> sl_shift)) -
+           slice_start(sl_nsb, sl_base);
 }
 
 // Order-preserving 64-bit key of (value, row): the float's bits mapped to an
@@ -278,11 +303,12 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
             const uint64_t pol = policy_evict_first();
             const int U = nrg * KS;
             for (int u = 0; u < U; ++u) {
+                if (u == nstage) prefetch_share(prm, lane);  // after the first ring fill
                 const int s = u % nstage, k = u / nstage;
                 if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1, ERR_WAIT_EMPTY)) break;
                 const int rg = rg_begin + u / KS, j = u % KS;
-                const int sb_lo = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, j * NSL);
-                const int sb_hi = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, (j + 1) * NSL);
+                const int sb_lo = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_shift, j * NSL);
+                const int sb_hi = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_shift, (j + 1) * NSL);
                 const uint32_t part_bytes = static_cast<uint32_t>(sb_hi - sb_lo) * Q4K_BYTES;
                 const int row0 = rg * 8;
                 const int nvalid = min(8, N - row0);
@@ -306,6 +332,7 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
                     }
                 }
             }
+            if (U <= nstage) prefetch_share(prm, lane);
             return;
         }
     }
@@ -428,11 +455,19 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
     }
     if (threadIdx.x < NCOLS) s_amax[threadIdx.x] = 0ull;
     named_bar_sync(1, NCW * 32);
+    if constexpr (!STAGED) {
+        if (warp == NCW - 1) prefetch_share(prm, lane);
+    }
 
     const int grp = warp / KS, j = warp % KS;
     const int p = lane >> 3, g = lane & 7;
-    const int sb_part = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, j * NSL);
-    const int sb_part_end = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, (j + 1) * NSL);
+    // this warp's slice bounds, once: superblocks [bnd[i], bnd[i+1]) of local
+    // slice j*NSL + i, relative to the row (or shard) start
+    int bnd[NSL + 1];
+#pragma unroll
+    for (int i = 0; i <= NSL; ++i) bnd[i] = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_shift, j * NSL + i);
+    const int sb_part = bnd[0];
+    const int sb_part_end = bnd[NSL];
     bool poisoned = false;
     int round = 0;
     for (int r = grp; r < nrg; r += NGRP, ++round) {
@@ -459,8 +494,7 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
         }
 #pragma unroll
         for (int i = 0; i < NSL; ++i) {
-            const int b0 = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, j * NSL + i);
-            const int b1 = shard_slice(prm.sl_nsb, prm.sl_base, prm.sl_cnt, j * NSL + i + 1);
+            const int b0 = bnd[i], b1 = bnd[i + 1];
 #pragma unroll
             for (int m = 0; m < NMAT; ++m)
 #pragma unroll

@@ -19,6 +19,7 @@
 //   Q8_1 of the SwiGLU output
 //   MMVQ down
 // then residual + RMSNorm + Q8_1, the tied output MMVQ and argmax.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -287,18 +288,18 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
         for (int q = 0; q < W; ++q) d.p[q] = m.recv(q, slot);
         return d;
     };
-    MmvqTp kshard;  // slicing of this rank's o / down K-shard
+    MmvqOpts kshard;  // slicing of this rank's o / down K-shard
     kshard.sl_nsb = 0;
     if (tp) {
         kshard.sl_base = sh.sl_base;
         kshard.sl_cnt = sh.sl_cnt;
     }
-    MmvqTp proto_o = kshard, proto_down = kshard;
+    MmvqOpts proto_o = kshard, proto_down = kshard;
     proto_o.sl_nsb = static_cast<int>(c.n_heads * c.head_dim / QK_K);
     proto_down.sl_nsb = c.ffn / QK_K;
     // each rank's launch publishes once per step (its last CTA)
     const int64_t per_o = W, per_down = W, per_out = W;
-    auto push_to = [&](MmvqTp &t, int slot) {
+    auto push_to = [&](MmvqOpts &t, int slot) {
         t.npeer = W;
         t.cta_cnt = m.cta_cnt(slot);
         for (int q = 0; q < W; ++q) {
@@ -307,7 +308,7 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
             t.peer_cnt[q] = m.cnt_of(m.peer[q], slot);
         }
     };
-    auto wait_on = [&](MmvqTp &t, int slot, int64_t per_step) {
+    auto wait_on = [&](MmvqOpts &t, int slot, int64_t per_step) {
         t.wait_cnt = m.cnt_of(m.arena, slot);
         t.epoch = m.epoch();
         t.wait_per_step = static_cast<unsigned long long>(per_step);
@@ -318,7 +319,7 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
     int cur = 0;
     auto fused = [&](const void *w, const void *w2, const DeltaSet &ds, const float *norm,
                      float *y, const int64_t shp[4], unsigned long long *amax,
-                     const MmvqTp *t) -> cudaError_t {
+                     const MmvqOpts *t) -> cudaError_t {
         const MmvqConfig *cfg = tuned(shp);
         if (!cfg) return cudaErrorInvalidValue;
         MmvqXin xin = {h[cur], h[cur ^ 1], ds, norm, c.eps};
@@ -326,48 +327,76 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
         return launch_mmvq_q4k_xin(*cfg, w, w2, xin, y, shp[0], shp[1], pf, st, amax, t);
     };
     auto plain = [&](const void *w, const void *x, float *y, const int64_t shp[4],
-                     const MmvqTp *t) -> cudaError_t {
+                     const MmvqOpts *t) -> cudaError_t {
         const MmvqConfig *cfg = tuned(shp);
         if (!cfg) return cudaErrorInvalidValue;
         return launch_mmvq_q4k(*cfg, w, nullptr, x, y, shp[0], shp[1], 1, shp[0], pf, st, nullptr, t);
+    };
+    // Each MMVQ streams the next MMVQ's weights into L2 while it runs (it is
+    // latency-bound, so HBM has room): q|k|v -> o -> gate, up -> down -> the
+    // next layer's q|k|v (after the last layer: the head of this rank's output
+    // rows; after the output: layer 0's q|k|v of the next token).
+    const bool prefetch = (c.flags & ABRA_MODEL_NO_PREFETCH) == 0;
+    const size_t row_h = q4k_bytes(1, c.hidden);
+    auto bytes_of = [&](const int64_t shp[4]) {
+        return static_cast<int64_t>(q4k_bytes(shp[0], shp[1]));
+    };
+    const uint8_t *out_w = m.embd + static_cast<size_t>(sh.vocab_lo) * row_h;
+    const int64_t out_head = std::min<int64_t>(bytes_of(ss.out), int64_t(32) << 20) / 16 * 16;
+    auto next_of = [&](MmvqOpts &t, const void *a, int64_t na, const void *b = nullptr,
+                       int64_t nb = 0) {
+        if (!prefetch) return;
+        t.pf_ptr[0] = a;
+        t.pf_bytes[0] = na;
+        t.pf_ptr[1] = b;
+        t.pf_bytes[1] = nb;
     };
     TRY(launch_embed(m.embd, c.hidden, m.tokens, m.pos, h[cur], pdl, st));
     for (int l = 0; l < L; ++l) {
         const LayerW &y = m.layers[l];
         // residual + RMSNorm + Q8_1 fused into the q|k|v MMVQ
-        MmvqTp tq;
+        MmvqOpts tq;
         if (tp && l > 0) wait_on(tq, 2 * l - 1, per_down);
+        next_of(tq, y.wo, bytes_of(ss.o));
         TRY(fused(y.wqkv, nullptr, l == 0 ? none : (tp ? slot_deltas(2 * l - 1) : one), y.attn_norm,
-                  m.qkv, ss.qkv, nullptr, tp && l > 0 ? &tq : nullptr));
+                  m.qkv, ss.qkv, nullptr, &tq));
         TRY(launch_qk_norm_rope_kv(m.qkv, y.q_norm, y.k_norm, c.eps, m.rope, m.pos, m.q,
                                    m.kc + l * kv_layer, m.vc + l * kv_layer, sh.q_heads,
                                    sh.kv_heads, c.max_ctx, pdl, st));
         TRY(launch_attention(m.q, m.kc + l * kv_layer, m.vc + l * kv_layer, m.pos, scale,
                              sh.q_heads, sh.kv_heads, c.max_ctx, m.part_m, m.part_l, m.part_o,
                              m.att, m.oq, pdl, st));
-        MmvqTp to = proto_o;
+        MmvqOpts to = tp ? proto_o : MmvqOpts();
         if (tp) push_to(to, 2 * l);
-        TRY(plain(y.wo, m.oq, m.delta, ss.o, tp ? &to : nullptr));
+        next_of(to, y.wgate, bytes_of(ss.gate_up), y.wup, bytes_of(ss.gate_up));
+        TRY(plain(y.wo, m.oq, m.delta, ss.o, &to));
         // residual + RMSNorm + Q8_1 fused into the gate/up SwiGLU MMVQ
-        MmvqTp tg;
+        MmvqOpts tg;
         if (tp) wait_on(tg, 2 * l, per_o);
+        next_of(tg, y.wdown, bytes_of(ss.down));
         TRY(fused(y.wgate, y.wup, tp ? slot_deltas(2 * l) : one, y.ffn_norm, m.act, ss.gate_up,
-                  nullptr, tp ? &tg : nullptr));
+                  nullptr, &tg));
         TRY(launch_quantize_q8_1(m.act, m.aq, ss.gate_up[0], 1, st));
-        MmvqTp td = proto_down;
+        MmvqOpts td = tp ? proto_down : MmvqOpts();
         if (tp) push_to(td, 2 * l + 1);
-        TRY(plain(y.wdown, m.aq, m.delta, ss.down, tp ? &td : nullptr));
+        if (l + 1 < L)
+            next_of(td, m.layers[l + 1].wqkv, bytes_of(ss.qkv));
+        else
+            next_of(td, out_w, out_head);
+        TRY(plain(y.wdown, m.aq, m.delta, ss.down, &td));
     }
     // final residual + RMSNorm fused into the tied output MMVQ over this
     // rank's vocab rows, which also reduces the greedy argmax (ties to the
     // lowest id); with TP every rank's keys meet in every rank's key word
     if (!tp) {
-        TRY(fused(m.embd, nullptr, L > 0 ? one : none, m.out_norm, m.logits, ss.out, m.amax, nullptr));
+        MmvqOpts t1;
+        if (L > 0) next_of(t1, m.layers[0].wqkv, bytes_of(ss.qkv));
+        TRY(fused(m.embd, nullptr, L > 0 ? one : none, m.out_norm, m.logits, ss.out, m.amax, &t1));
         return launch_argmax_finish(m.amax, m.tokens, m.picks, m.pos, m.nprompt, c.max_ctx, pdl, st);
     }
     // this rank's CTAs reduce into the local key m.amax; the last one
     // forwards it to every rank's combined key
-    MmvqTp tout;
+    MmvqOpts tout;
     tout.row_offset = static_cast<int>(sh.vocab_lo);
     tout.npeer = W;
     tout.cta_cnt = m.cta_cnt(2 * L);
@@ -376,7 +405,7 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
         tout.peer_cnt[q] = m.cnt_of(m.peer[q], 2 * L);
     }
     if (L > 0) wait_on(tout, 2 * L - 1, per_down);
-    const uint8_t *out_w = m.embd + static_cast<size_t>(sh.vocab_lo) * q4k_bytes(1, c.hidden);
+    if (L > 0) next_of(tout, m.layers[0].wqkv, bytes_of(ss.qkv));
     TRY(fused(out_w, nullptr, L > 0 ? slot_deltas(2 * L - 1) : none, m.out_norm, m.logits, ss.out,
               m.amax, &tout));
     return launch_argmax_finish(m.key_of(m.arena), m.tokens, m.picks, m.pos, m.nprompt, c.max_ctx,

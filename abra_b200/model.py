@@ -36,6 +36,7 @@ class TpShard(C.Structure):
 
 EAGER = 1   # ABRA_MODEL_EAGER
 NO_PDL = 2  # ABRA_MODEL_NO_PDL
+NO_PREFETCH = 4  # ABRA_MODEL_NO_PREFETCH
 IPC_HANDLE_BYTES = 64
 
 

@@ -184,12 +184,12 @@ def mmvq_swiglu(d_w_gate, d_w_up, d_x, d_y, N: int, K: int, ncols: int = 1,
 
 
 def mmvq_kshard(d_w, d_x, d_y, N: int, K: int, K_full: int, sl_base: int, sl_cnt: int,
-                ncols: int = 1, candidate: int = 0, stream=None) -> None:
+                ncols: int = 1, candidate: int = 0, pdl: bool = False, stream=None) -> None:
     """Row-parallel MMVQ over canonical K-slices [sl_base, sl_base + sl_cnt)
     of K_full (see abra_q4k_mmvq_kshard): y gets this shard's partial sums."""
     _check_k(K)
     call("abra_q4k_mmvq_kshard", ptr(d_w), ptr(d_x), ptr(d_y), N, K, ncols, K_full, sl_base,
-         sl_cnt, candidate, stream_handle(stream))
+         sl_cnt, candidate, _lib.ABRA_MMVQ_PDL if pdl else 0, stream_handle(stream))
 
 
 def slice_start(nsb: int, i: int) -> int:

@@ -13,6 +13,7 @@ synthesize_tuning_table at :168-240) and its hand-copied table
 candidate id, mirroring the reference's tie-break rule (:200-206).
 
     python -m abra_b200.tune [--ncols 1 8] [--out PATH] [--quick]
+    python -m abra_b200.tune --tp --ncols 1 --merge   # tensor-parallel shard shapes
 """
 from __future__ import annotations
 
@@ -37,20 +38,47 @@ DECODE_SHAPES = [
 ]
 
 
+
+
+def tp_shapes(worlds=(2, 4, 8)):
+    """Per-rank shapes of the tensor-parallel decode: (N, K, nmat, K_full,
+    sl_base, sl_cnt); K_full > 0 marks a K-shard (o, down), timed through the
+    K-shard entry point with the shard's slicing."""
+    from .model import shard_info
+
+    out = []
+    for w in worlds:
+        for r in range(w):
+            s = shard_info(r, w)
+            qkv = (s.q_heads + 2 * s.kv_heads) * 128
+            ffn = s.ffn_hi - s.ffn_lo
+            for shp in ((qkv, 2560, 1, 0, 0, 8),
+                        (2560, s.q_heads * 128, 1, 4096, s.sl_base, s.sl_cnt),
+                        (ffn, 2560, 2, 0, 0, 8), (2560, ffn, 1, 9728, s.sl_base, s.sl_cnt),
+                        (int(s.vocab_hi - s.vocab_lo), 2560, 1, 0, 0, 8)):
+                if shp[:3] not in [o[:3] for o in out]:
+                    out.append(shp)
+    return out
+
+
 def q4k_bytes(N: int, K: int) -> int:
     return N * (K // 256) * 144
 
 
-def time_candidate(torch, plan, ncols, nmat, cid, reps=3, failures=None):
+def time_candidate(torch, plan, ncols, nmat, cid, reps=3, failures=None, kshard=(0, 0, 8)):
     from .q4k import device_error
 
     f_mm = _lib.lib.abra_q4k_mmvq_ex
     f_sw = _lib.lib.abra_q4k_mmvq_swiglu
+    f_ks = _lib.lib.abra_q4k_mmvq_kshard
+    K_full, sl_base, sl_cnt = kshard
 
     def run(items=plan):
         st = stream_handle(None)
         for w, w2, x, y, N, K in items:
-            if nmat == 1:
+            if K_full:
+                rc = f_ks(w, x, y, N, K, ncols, K_full, sl_base, sl_cnt, cid, _lib.ABRA_MMVQ_PDL, st)
+            elif nmat == 1:
                 rc = f_mm(w, x, y, N, K, ncols, N, cid, _lib.ABRA_MMVQ_PDL, st)
             else:
                 rc = f_sw(w, w2, x, y, N, K, ncols, N, cid, _lib.ABRA_MMVQ_PDL, st)
@@ -88,7 +116,7 @@ def time_candidate(torch, plan, ncols, nmat, cid, reps=3, failures=None):
     return best
 
 
-def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None) -> dict:
+def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None, merge: bool = False) -> dict:
     import torch
 
     import abra_b200 as A
@@ -97,7 +125,9 @@ def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None) -> dict:
     ids = ids or get_all_candidate_ids()
     entries = []
     failures = []
-    for (N, K, nmat) in shapes:
+    for shape in shapes:
+        N, K, nmat = shape[:3]
+        kshard = tuple(shape[3:6]) if len(shape) >= 6 else (0, 0, 8)
         per = q4k_bytes(N, K) * nmat
         copies = max(4, -(-4 * L2_BYTES // per))
         if quick:
@@ -121,7 +151,7 @@ def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None) -> dict:
             times = {}
             for cid in ids:
                 nf = len(failures)
-                us = time_candidate(torch, plan, ncols, nmat, cid, failures=failures)
+                us = time_candidate(torch, plan, ncols, nmat, cid, failures=failures, kshard=kshard)
                 if len(failures) > nf:
                     failures[-1].update({"N": N, "K": K, "ncols": ncols, "nmat": nmat})
                     print(json.dumps({"failure": failures[-1]}), flush=True)
@@ -132,6 +162,8 @@ def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None) -> dict:
             winner = min(c for c, t in times.items() if t <= fastest * 1.005)
             nbytes = per + ncols * (K // 32) * 36 + ncols * N * 4
             e = {"N": N, "K": K, "ncols": ncols, "nmat": nmat, "candidate": winner,
+                 **({"K_full": kshard[0], "sl_base": kshard[1], "sl_cnt": kshard[2]}
+                    if kshard[0] else {}),
                  "name": get_candidate_spec(winner).name, "us": round(times[winner], 3),
                  "GBps": round(nbytes / (times[winner] * 1e-6) / 1e9, 1), "copies": copies,
                  "all_us": {str(c): round(t, 3) for c, t in sorted(times.items())}}
@@ -140,6 +172,12 @@ def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None) -> dict:
                   flush=True)
         del bufs
         torch.cuda.empty_cache()
+    if merge and out.exists():
+        old = json.loads(out.read_text())
+        keys = {(e["N"], e["K"], e["ncols"], e["nmat"]) for e in entries}
+        entries = [e for e in old.get("entries", [])
+                   if (e["N"], e["K"], e["ncols"], e["nmat"]) not in keys] + entries
+        failures = old.get("failures", []) + failures
     data = {"arch": 100, "device": torch.cuda.get_device_name(0),
             "when": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime()),
             "method": "CUDA graph of back-to-back launches over >= 4 x L2 of weight copies, "
@@ -158,9 +196,12 @@ def main(argv=None) -> int:
     ap.add_argument("--shape", type=int, nargs=3, action="append", metavar=("N", "K", "NMAT"),
                     help="tune only these shapes (repeatable)")
     ap.add_argument("--ids", type=int, nargs="+", help="only these candidate ids")
+    ap.add_argument("--tp", action="store_true",
+                    help="the per-rank shapes of the 2/4/8-GPU tensor-parallel decode (batch 1)")
+    ap.add_argument("--merge", action="store_true", help="keep the other entries of --out")
     a = ap.parse_args(argv)
-    shapes = [tuple(s) for s in a.shape] if a.shape else DECODE_SHAPES
-    tune(shapes, a.ncols, Path(a.out), a.quick, a.ids)
+    shapes = [tuple(s) for s in a.shape] if a.shape else (tp_shapes() if a.tp else DECODE_SHAPES)
+    tune(shapes, a.ncols, Path(a.out), a.quick, a.ids, a.merge)
     return 0
 
 

@@ -81,7 +81,7 @@ int abra_q4k_mmvq_combined_static(int32_t candidate, const void *w_q4k, const fl
 
 /* Row-parallel (K-sharded) MMVQ: w holds columns [k0, k0 + K) of an
  * N x K_full matrix, where [k0, k0 + K) are the canonical K-slices
- * [sl_base, sl_base + sl_cnt) of K_full (slice i of a row of n = K_full/256
+ * [sl_base, sl_base + sl_cnt), sl_cnt in {1, 2, 4, 8}, of K_full (slice i of a row of n = K_full/256
  * superblocks starts at superblock i*(n/8) + min(i, n%8)); x holds the same
  * K activations.  y gets this shard's partial sums, each a subtree of the
  * unsharded sum, so adding the shards' partials in the fixed tree
@@ -90,7 +90,7 @@ int abra_q4k_mmvq_combined_static(int32_t candidate, const void *w_q4k, const fl
  * NCCL all-reduce instead (docs/research/1080ti-speed-results.md:76-81). */
 int abra_q4k_mmvq_kshard(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, int64_t K,
                          int32_t ncols, int64_t K_full, int32_t sl_base, int32_t sl_cnt,
-                         int32_t candidate, void *stream);
+                         int32_t candidate, int32_t flags, void *stream);
 
 /* Full form: explicit output column stride ldy >= N, candidate (0 = tuned)
  * and ABRA_MMVQ_* flags. */
@@ -182,6 +182,7 @@ typedef struct {
 
 #define ABRA_MODEL_EAGER 1  /* launch kernels per step instead of a CUDA graph */
 #define ABRA_MODEL_NO_PDL 2 /* no programmatic dependent launch */
+#define ABRA_MODEL_NO_PREFETCH 4 /* no L2 prefetch of the next kernel's weights */
 
 int abra_model_default_config(abra_model_config *cfg); /* Qwen3-4B, max_ctx 4096 */
 int abra_model_create(const abra_model_config *cfg, void **model);

@@ -368,10 +368,10 @@ def tree8(v: np.ndarray) -> np.ndarray:
 
 def kshard_partial(slices: np.ndarray, sl_base: int, sl_cnt: int) -> np.ndarray:
     """A K-shard's partial sum as the kernel forms it: its global slices
-    [sl_base, sl_base + sl_cnt) as local slices 0.., the rest +0.0, then the
-    canonical tree."""
+    [sl_base, sl_base + sl_cnt) at local slices 0, s, 2s, .. (s = 8 / sl_cnt),
+    the other local slices +0.0, then the canonical tree."""
     local = np.zeros(slices.shape, dtype=np.float32)
-    local[..., :sl_cnt] = slices[..., sl_base:sl_base + sl_cnt]
+    local[..., ::8 // sl_cnt] = slices[..., sl_base:sl_base + sl_cnt]
     return tree8(local)
 
 

@@ -50,13 +50,13 @@ def test_small_model_logits_bit_exact_across_chunks(centered):
     c.close()
 
 
-def test_graph_eager_and_no_pdl_agree():
-    from abra_b200.model import EAGER, NO_PDL, DecodeModel
+def test_graph_eager_no_pdl_and_no_prefetch_agree():
+    from abra_b200.model import EAGER, NO_PDL, NO_PREFETCH, DecodeModel
 
     cfg = dict(n_layers=3, vocab=2048, max_ctx=300, centered=1, seed=5)
     prompt = _prompt(7, 2048, 2)
     outs = []
-    for flags in (0, EAGER, NO_PDL, EAGER | NO_PDL):
+    for flags in (0, EAGER, NO_PDL, EAGER | NO_PDL, NO_PREFETCH):
         with DecodeModel(flags=flags, **cfg) as m:
             toks = m.generate(prompt, 280)
             outs.append((toks, m.logits()))
