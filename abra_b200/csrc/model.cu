@@ -592,6 +592,16 @@ int abra_model_step(void *model, int32_t n_steps) {
     return ABRA_OK;
 }
 
+int abra_model_invalidate(void *model) {
+    Model *m = static_cast<Model *>(model);
+    if (!m) return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "sync", e);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+    return ABRA_OK;
+}
+
 int abra_model_sync(void *model) {
     Model *m = static_cast<Model *>(model);
     if (!m) return ABRA_E_INVALID;

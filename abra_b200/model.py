@@ -132,6 +132,11 @@ class DecodeModel:
         """Queue n decode steps on the model's stream (asynchronous)."""
         _check(_lib.lib.abra_model_step(self.handle, n), "abra_model_step")
 
+    def invalidate(self) -> None:
+        """Drop the recorded step; the next step records it again (picks up
+        tuning-table changes)."""
+        _check(_lib.lib.abra_model_invalidate(self.handle), "abra_model_invalidate")
+
     def sync(self) -> None:
         _check(_lib.lib.abra_model_sync(self.handle), "abra_model_sync")
 

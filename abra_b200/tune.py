@@ -14,6 +14,7 @@ candidate id, mirroring the reference's tie-break rule (:200-206).
 
     python -m abra_b200.tune [--ncols 1 8] [--out PATH] [--quick]
     python -m abra_b200.tune --tp --ncols 1 --merge   # tensor-parallel shard shapes
+    python -m abra_b200.tune --decode                 # decode slots, by whole-token time
 """
 from __future__ import annotations
 
@@ -188,6 +189,81 @@ def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None, merge: bo
     return data
 
 
+def decode_slots():
+    """The MMVQ launch slots of one decode token (batch 1, one GPU):
+    (name, N, K, nmat)."""
+    return [("qkv", 6144, 2560, 1), ("o", 2560, 4096, 1), ("gate_up", 9728, 2560, 2),
+            ("down", 2560, 9728, 1), ("output", 151936, 2560, 1)]
+
+
+def tune_decode(out: Path, passes: int = 2, tokens: int = 48, ids=None) -> dict:
+    """In-situ tuning: the candidate of each MMVQ slot of the decode step is
+    chosen by the time of whole decode tokens (one CUDA graph per token, the
+    same graph the runtime replays), one slot at a time, ``passes`` rounds
+    of coordinate descent.  Kernel-alone timing misses how a kernel's
+    prologue and tail overlap its neighbours under programmatic dependent
+    launch; this measures exactly that."""
+    import torch
+
+    from .model import DecodeModel
+
+    ids = ids or get_all_candidate_ids()
+    m = DecodeModel(max_ctx=tokens + 64)
+    prompt = np.random.default_rng(0).integers(0, m.cfg.vocab, 16).astype(np.int32)
+    st = torch.cuda.ExternalStream(m.stream)
+
+    def token_ms() -> float:  # every measurement at the same positions
+        m.invalidate()
+        m.reset(prompt)
+        m.step(4)
+        m.sync()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(st)
+        m.step(tokens)
+        e.record(st)
+        e.synchronize()
+        return s.elapsed_time(e) / tokens
+
+    current = {name: _lib.lib.abra_tune_get(N, K, 1, nmat) for name, N, K, nmat in decode_slots()}
+    log = []
+    base = token_ms()
+    for p in range(passes):
+        for name, N, K, nmat in decode_slots():
+            times = {}
+            for cid in ids:
+                if _lib.lib.abra_tune_set(N, K, 1, nmat, cid) != 0:
+                    continue
+                try:
+                    times[cid] = token_ms()
+                except _lib.AbraError as exc:  # e.g. staging that does not fit
+                    log.append({"slot": name, "candidate": cid, "error": str(exc)})
+            best = min(times, key=times.get)
+            if times[best] > times.get(current[name], float("inf")) * 0.995:
+                best = current[name]  # keep the incumbent unless clearly beaten
+            current[name] = best
+            _lib.lib.abra_tune_set(N, K, 1, nmat, best)
+            log.append({"pass": p, "slot": name, "candidate": best, "ms_per_token": round(times[best], 4),
+                        "all_ms": {str(c): round(t, 4) for c, t in sorted(times.items())}})
+            print(json.dumps({k: log[-1][k] for k in ("pass", "slot", "candidate", "ms_per_token")}), flush=True)
+    final = token_ms()
+    m.close()
+    entries = [{"N": N, "K": K, "ncols": 1, "nmat": nmat, "candidate": current[name],
+                "name": get_candidate_spec(current[name]).name, "slot": name, "in_situ": True}
+               for name, N, K, nmat in decode_slots()]
+    data = json.loads(out.read_text()) if out.exists() else {"arch": 100, "entries": []}
+    keys = {(e["N"], e["K"], e["ncols"], e["nmat"]) for e in entries}
+    data["entries"] = [e for e in data.get("entries", [])
+                       if (e["N"], e["K"], e["ncols"], e["nmat"]) not in keys] + entries
+    data["decode_in_situ"] = {"when": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime()),
+                              "ms_per_token_before": round(base, 4),
+                              "ms_per_token_after": round(final, 4), "tokens": tokens,
+                              "passes": passes, "log": log}
+    out.parent.mkdir(parents=True, exist_ok=True)
+    out.write_text(json.dumps(data, indent=1) + "\n")
+    print(json.dumps({"before_ms": round(base, 4), "after_ms": round(final, 4)}), flush=True)
+    return data
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--ncols", type=int, nargs="+", default=[1, 8])
@@ -199,7 +275,12 @@ def main(argv=None) -> int:
     ap.add_argument("--tp", action="store_true",
                     help="the per-rank shapes of the 2/4/8-GPU tensor-parallel decode (batch 1)")
     ap.add_argument("--merge", action="store_true", help="keep the other entries of --out")
+    ap.add_argument("--decode", action="store_true",
+                    help="in-situ: pick each decode slot's candidate by whole-token time")
     a = ap.parse_args(argv)
+    if a.decode:
+        tune_decode(Path(a.out), ids=a.ids)
+        return 0
     shapes = [tuple(s) for s in a.shape] if a.shape else (tp_shapes() if a.tp else DECODE_SHAPES)
     tune(shapes, a.ncols, Path(a.out), a.quick, a.ids, a.merge)
     return 0

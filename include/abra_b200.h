@@ -193,6 +193,10 @@ int abra_model_reset(void *model, const int32_t *prompt, int32_t n_prompt);
  * tokens[pos], appends the greedy pick once past the prompt, pos += 1. */
 int abra_model_step(void *model, int32_t n_steps);
 int abra_model_sync(void *model);
+/* Drop the recorded step (after abra_tune_set, for example); the next step
+ * records it again.  Not for tensor-parallel models, whose ranks record
+ * together at connect. */
+int abra_model_invalidate(void *model);
 /* Synchronises, then copies tokens[0..n_tokens) (prompt then picks), the
  * last step's logits (vocab floats) and the position; NULL skips an item. */
 int abra_model_read(void *model, int32_t *tokens, int32_t n_tokens, float *logits,
