@@ -33,6 +33,7 @@ from .q4k import (
     mmvq_kshard,
     mmvq_partials,
     mmvq_swiglu,
+    mmvq_tc,
     q4k_nbytes,
     q8_1_nbytes,
     register_autotuned_table_entry,

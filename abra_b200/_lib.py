@@ -32,6 +32,7 @@ SIGNATURES: dict[str, tuple] = {
     "abra_q4k_mmvq_partials": (C.c_int, [_vp, _vp, _fp, _vp, _vp, _i64, _i64, _i32, _i32, _vp]),
     "launch_pinned_upstream_mmvq": (None, [_vp, _vp, _fp, _i64, _i64, _vp]),
     "abra_quantize_q8_1": (C.c_int, [_fp, _vp, _i64, _i32, _vp]),
+    "abra_q4k_mmvq_tc": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _fp, _i32, _vp]),
     "abra_q4k_mmvq_kshard": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _i32, _i32, _i32, _vp]),
     "abra_q4k_mmvq_combined": (C.c_int, [_i32, _vp, _fp, _vp, _fp, _i64, _i64, _i32, _vp]),
     "abra_q4k_mmvq_combined_static": (C.c_int, [_i32, _vp, _fp, _fp, _i64, _i64, _i32, _vp]),

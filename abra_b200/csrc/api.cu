@@ -156,6 +156,24 @@ int abra_q4k_mmvq_kshard(const void *w, const void *x, float *y, int64_t N, int6
     return ABRA_OK;
 }
 
+int abra_q4k_mmvq_tc(const void *w, const void *x, float *y, int64_t N, int64_t K,
+                     int32_t ncols, int64_t ldy, int32_t ks, float *workspace, int32_t flags,
+                     void *stream) {
+    if (ncols != 32) return fail(ABRA_E_UNSUPPORTED, "the tensor-core MMVQ takes 32 columns (got %d)", ncols);
+    if (!w || !x || !y) return fail(ABRA_E_INVALID, "null pointer");
+    if (N <= 0 || K <= 0 || K % 256 != 0) return fail(ABRA_E_INVALID, "K must be a positive multiple of QK_K=256 (K=%lld)", (long long)K);
+    if (K > 65536 || N > (int64_t)0x7fffffff - 128) return fail(ABRA_E_UNSUPPORTED, "shape too large");
+    if (ldy < N) return fail(ABRA_E_INVALID, "ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
+    if (!(ks == 1 || ks == 2 || ks == 4 || ks == 8)) return fail(ABRA_E_INVALID, "ks must be 1, 2, 4 or 8");
+    if (ks > 1 && !workspace) return fail(ABRA_E_INVALID, "ks > 1 needs a workspace of ks*32*N floats");
+    if (!aligned16(w) || (reinterpret_cast<uintptr_t>(x) & 3u)) return fail(ABRA_E_INVALID, "weights 16-byte and activations 4-byte aligned");
+    cudaError_t e = abra::launch_mmvq_tc(w, x, y, N, K, ldy, ks, workspace,
+                                         (flags & ABRA_MMVQ_PDL) ? abra::MMVQ_PDL : 0,
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core mmvq launch");
+    return ABRA_OK;
+}
+
 int abra_q4k_mmvq_combined(int32_t candidate, const void *w, const float *x, void *xq,
                            float *y, int64_t N, int64_t K, int32_t ncols, void *stream) {
     if (!x) return fail(ABRA_E_INVALID, "null pointer");

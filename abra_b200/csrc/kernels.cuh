@@ -88,6 +88,12 @@ cudaError_t launch_mmvq_q4k_partials(const void *w, const void *x_q8, float *y, 
                                      int32_t *M, int64_t N, int64_t K, int ncols, int ks,
                                      cudaStream_t stream);
 
+// Batch-32 MMVQ on the tensor cores (tcgen05 kind::i8): ncols = 32 Q8_1
+// columns, ks k-parts (1, 2, 4, 8) over the canonical slices; ks > 1 needs
+// part = ks * 32 * N floats of scratch and adds a combine launch.
+cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N, int64_t K,
+                           int64_t ldy, int ks, float *part, int flags, cudaStream_t stream);
+
 // ------------------------------------------------------------ quantize ---
 cudaError_t launch_quantize_q8_1(const float *x, void *y, int64_t K, int ncols,
                                  cudaStream_t stream);

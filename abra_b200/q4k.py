@@ -192,6 +192,16 @@ def mmvq_kshard(d_w, d_x, d_y, N: int, K: int, K_full: int, sl_base: int, sl_cnt
          sl_cnt, candidate, _lib.ABRA_MMVQ_PDL if pdl else 0, stream_handle(stream))
 
 
+def mmvq_tc(d_w, d_x, d_y, N: int, K: int, ks: int = 1, d_workspace=None, ldy: int | None = None,
+            pdl: bool = False, stream=None) -> None:
+    """Batch-32 MMVQ on the tcgen05 tensor cores (32 Q8_1 columns): bit-identical
+    to :func:`mmvq`; ks > 1 splits K over CTAs and needs ks*32*N floats of
+    workspace."""
+    _check_k(K)
+    call("abra_q4k_mmvq_tc", ptr(d_w), ptr(d_x), ptr(d_y), N, K, 32, N if ldy is None else ldy, ks,
+         ptr(d_workspace), _lib.ABRA_MMVQ_PDL if pdl else 0, stream_handle(stream))
+
+
 def slice_start(nsb: int, i: int) -> int:
     """First superblock of canonical K-slice i of a row of nsb superblocks."""
     return i * (nsb // 8) + min(i, nsb % 8)

@@ -92,6 +92,18 @@ int abra_q4k_mmvq_kshard(const void *w_q4k, const void *x_q8_1, float *y, int64_
                          int32_t ncols, int64_t K_full, int32_t sl_base, int32_t sl_cnt,
                          int32_t candidate, int32_t flags, void *stream);
 
+/* Batch-32 MMVQ on the 5th-generation tensor cores (tcgen05.mma kind::i8,
+ * TMEM accumulators): y = W x for ncols = 32 Q8_1 columns, bit-identical
+ * to abra_q4k_mmvq (the exact int32 sub-block dots come from the tensor
+ * core, the fp32 scaling follows the same canonical order).  ks in
+ * {1, 2, 4, 8} splits K over CTAs along the canonical slices; ks > 1 needs
+ * workspace = ks * 32 * N floats (one more launch combines the parts).  The
+ * reference has no tensor-core path: its batched decode runs its MMVQ
+ * family per column group (kernels/q4k/q4k_family.cu:12-110). */
+int abra_q4k_mmvq_tc(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, int64_t K,
+                     int32_t ncols, int64_t ldy, int32_t ks, float *workspace, int32_t flags,
+                     void *stream);
+
 /* Full form: explicit output column stride ldy >= N, candidate (0 = tuned)
  * and ABRA_MMVQ_* flags. */
 int abra_q4k_mmvq_ex(const void *w_q4k, const void *x_q8_1, float *y, int64_t N, int64_t K,

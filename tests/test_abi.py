@@ -78,3 +78,16 @@ def test_rejects_bad_arguments_without_gpu():
         A.launch_quantize_f32_to_q8_1(16, 16, 33)
     with pytest.raises(ValueError):
         A.launch_q4k_candidate(999999, 16, 16, 16, 8, 256)
+
+
+def test_tensor_core_mmvq_rejects_bad_arguments_without_gpu():
+    import abra_b200 as A
+    from abra_b200 import _lib
+
+    lib = _lib.lib
+    assert lib.abra_q4k_mmvq_tc(16, 16, 16, 128, 256, 8, 128, 1, None, 0, None) == _lib.ABRA_E_UNSUPPORTED
+    assert lib.abra_q4k_mmvq_tc(16, 16, 16, 128, 256, 32, 128, 2, None, 0, None) == _lib.ABRA_E_INVALID
+    assert "workspace" in _lib.last_error()
+    assert lib.abra_q4k_mmvq_tc(16, 16, 16, 128, 256, 32, 128, 3, None, 0, None) == _lib.ABRA_E_INVALID
+    with pytest.raises(ValueError):
+        A.mmvq_tc(16, 16, 16, 128, 300)
