@@ -6,19 +6,26 @@
 
 namespace abra {
 
+// Per-sequence element strides of a batch of sequences sharing one position
+// (batch 1: all zero).
+struct SeqStrides {
+    int batch = 1;
+    int64_t qkv = 0, q = 0, kv = 0;
+};
+
 cudaError_t launch_embed(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
-                         float *h, bool pdl, cudaStream_t s);
+                         float *h, bool pdl, cudaStream_t s, int batch = 1, int64_t tok_stride = 0);
 cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const float *w,
                                           float eps, void *y, int K, int ncols, bool pdl,
                                           cudaStream_t s);
 cudaError_t launch_qk_norm_rope_kv(const float *qkv, const float *q_norm, const float *k_norm,
                                    float eps, const float *rope, const int32_t *pos, float *q_out,
                                    void *kc, void *vc, int n_heads, int n_kv, int max_ctx,
-                                   bool pdl, cudaStream_t s);
+                                   bool pdl, cudaStream_t s, const SeqStrides &b = SeqStrides());
 cudaError_t launch_attention(const float *q, const void *kc, const void *vc, const int32_t *pos,
                              float scale, int n_heads, int n_kv, int max_ctx, float *part_m,
                              float *part_l, float *part_o, float *out_f32, void *out_q8,
-                             bool pdl, cudaStream_t s);
+                             bool pdl, cudaStream_t s, const SeqStrides &b = SeqStrides());
 // Reads the argmax key left by the output MMVQ, resets it, appends the pick.
 // Tensor parallel (epoch != nullptr): first waits until *wait_cnt >=
 // (*epoch + 1) * per_step (every rank's keys have arrived), then advances
@@ -31,6 +38,15 @@ cudaError_t launch_argmax_finish(unsigned long long *key, int32_t *tokens, int32
 cudaError_t launch_argmax_advance(const float *logits, int n, int32_t *tokens, int32_t *picks,
                                   int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
                                   cudaStream_t s);
+// Greedy picks of a batch of sequences (logits rows ldl apart, token rows
+// tok_stride apart), then one advance of the shared position.
+cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t *tokens,
+                                int32_t *picks, int64_t tok_stride, int32_t *pos,
+                                const int32_t *n_prompt, int max_ctx, int batch, bool pdl,
+                                cudaStream_t s);
+// y = Q8_1 of up * silu(gate), n values (a multiple of 32).
+cudaError_t launch_swiglu_quant(const float *g, const float *u, void *y, int64_t n, bool pdl,
+                                cudaStream_t s);
 
 // Generator variants (gen_quant.cu).
 cudaError_t launch_gen_q4k_ex(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,

@@ -25,12 +25,15 @@ __device__ __forceinline__ void scale_min_one(const uint8_t *q, int j, int &sc, 
 }
 
 // ---------------------------------------------------------------- embed ---
-// h = dequant(E[tokens[*pos]]): w = fmaf(d * sc, q, -(dmin * m)).
+// h = dequant(E[tokens[*pos]]): w = fmaf(d * sc, q, -(dmin * m)).  Sequence
+// blockIdx.y of a batch reads tokens + y * tok_stride and writes h + y * hidden.
 __global__ void embed_kernel(const uint8_t *__restrict__ E, int hidden,
                              const int32_t *__restrict__ tokens, const int32_t *__restrict__ pos,
-                             float *__restrict__ h) {
+                             float *__restrict__ h, int64_t tok_stride) {
     pdl_wait();
     pdl_launch_dependents();
+    tokens += blockIdx.y * tok_stride;
+    h += static_cast<int64_t>(blockIdx.y) * hidden;
     const int tok = tokens[*pos];
     const uint8_t *row = E + static_cast<int64_t>(tok) * (hidden / QK_K) * Q4K_BYTES;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += blockDim.x * gridDim.x) {
@@ -106,14 +109,21 @@ __global__ void __launch_bounds__(RES_THREADS)
 // four, xor butterfly 16..1), times the norm weight, then NEOX RoPE pairs
 // (i, i+64) with the host cos/sin table row of this position.  q stays fp32;
 // k and v are stored fp16 at kv[head][pos][128].
+// Sequence blockIdx.y of a batch: qkv, q_out and the KV cache advance by
+// their per-sequence strides.
 __global__ void __launch_bounds__(256)
     qk_norm_rope_kv_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
                            const float *__restrict__ k_norm, float eps,
                            const float *__restrict__ rope, const int32_t *__restrict__ pos_p,
                            float *__restrict__ q_out, __half *__restrict__ kc,
-                           __half *__restrict__ vc, int n_heads, int n_kv, int max_ctx) {
+                           __half *__restrict__ vc, int n_heads, int n_kv, int max_ctx,
+                           int64_t qkv_stride, int64_t q_stride, int64_t kv_stride) {
     pdl_wait();
     pdl_launch_dependents();
+    qkv += blockIdx.y * qkv_stride;
+    q_out += blockIdx.y * q_stride;
+    kc += blockIdx.y * kv_stride;
+    vc += blockIdx.y * kv_stride;
     const int lane = threadIdx.x & 31;
     const int hw = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (hw >= n_heads + 2 * n_kv) return;
@@ -170,13 +180,25 @@ __global__ void __launch_bounds__(256)
 constexpr int ATT_CHUNK = 256;
 constexpr int ATT_MAXG = 8;  // q heads per kv head supported
 
+// Sequence blockIdx.z of a batch: q and the KV cache advance by their strides,
+// the partials by (kv heads * GQ) * max_chunks per sequence.
 template <int GQ>
 __global__ void __launch_bounds__(256)
     attention_chunk_kernel(const float *__restrict__ q, const __half *__restrict__ kc,
                            const __half *__restrict__ vc, const int32_t *__restrict__ pos_p,
                            float scale, int max_ctx, int max_chunks,
                            float *__restrict__ part_m, float *__restrict__ part_l,
-                           float *__restrict__ part_o) {
+                           float *__restrict__ part_o, int64_t q_stride, int64_t kv_stride) {
+    {
+        const int64_t z = blockIdx.z;
+        const int64_t pstride = static_cast<int64_t>(gridDim.x) * GQ * max_chunks;
+        q += z * q_stride;
+        kc += z * kv_stride;
+        vc += z * kv_stride;
+        part_m += z * pstride;
+        part_l += z * pstride;
+        part_o += z * pstride * 128;
+    }
     __shared__ __align__(16) float s_q[GQ][128];
     __shared__ float s_e[GQ][ATT_CHUNK];
     __shared__ float s_red[GQ][8];
@@ -307,6 +329,14 @@ __global__ void __launch_bounds__(256)
                                  float *__restrict__ out_f32, block_q8_1 *__restrict__ out_q8) {
     pdl_wait();
     pdl_launch_dependents();
+    {  // sequence blockIdx.y of a batch
+        const int64_t y = blockIdx.y, pstride = static_cast<int64_t>(n_heads) * max_chunks;
+        part_m += y * pstride;
+        part_l += y * pstride;
+        part_o += y * pstride * 128;
+        if (out_f32) out_f32 += y * n_heads * 128;
+        out_q8 += y * n_heads * 4;
+    }
     const int lane = threadIdx.x & 31;
     const int hq = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (hq >= n_heads) return;
@@ -437,6 +467,82 @@ __global__ void argmax_finish_kernel(unsigned long long *__restrict__ key,
     }
 }
 
+// ------------------------------------------------------ batched decode ---
+// Greedy pick of sequence blockIdx.x of a batch: largest of its n logits
+// (row stride ldl), ties to the lowest index; records picks[seq][*pos] and,
+// past the prompt, tokens[seq][*pos + 1].  The shared position advances in
+// pos_advance_kernel once every sequence has read it.
+__global__ void __launch_bounds__(1024)
+    argmax_batch_kernel(const float *__restrict__ x, int n, int64_t ldl,
+                        int32_t *__restrict__ tokens, int32_t *__restrict__ picks,
+                        int64_t tok_stride, const int32_t *__restrict__ pos_p,
+                        const int32_t *__restrict__ n_prompt_p, int max_ctx) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    pdl_wait();
+    pdl_launch_dependents();
+    x += blockIdx.x * ldl;
+    tokens += blockIdx.x * tok_stride;
+    picks += blockIdx.x * tok_stride;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i];
+        if (v > bv) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        const int p = *pos_p;
+        if (bi == 0x7fffffff) bi = 0;
+        if (p < max_ctx) {  // the host never steps past max_ctx
+            picks[p] = bi;
+            if (p + 1 >= *n_prompt_p) tokens[p + 1] = bi;
+        }
+    }
+}
+
+__global__ void pos_advance_kernel(int32_t *__restrict__ pos_p, int max_ctx) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x == 0 && *pos_p < max_ctx) *pos_p += 1;
+}
+
+// act = up * silu(gate) (the fused gate/up MMVQ's epilogue, elementwise),
+// then its Q8_1 blocks; one warp per 32-block.
+__global__ void __launch_bounds__(256)
+    swiglu_quant_kernel(const float *__restrict__ g, const float *__restrict__ u,
+                        block_q8_1 *__restrict__ y, int64_t nblocks_total) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+    pdl_wait();
+    pdl_launch_dependents();
+    if (warp >= nblocks_total) return;
+    const int64_t i = warp * QK8_1 + lane;
+    quantize_block_warp(__fmul_rn(u[i], abra_silu(g[i])), y + warp, lane);
+}
+
 // ----------------------------------------------------------- launchers ---
 static cudaLaunchAttribute pdl_attr() {
     cudaLaunchAttribute a;
@@ -460,9 +566,9 @@ static cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t
 }
 
 cudaError_t launch_embed(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
-                         float *h, bool pdl, cudaStream_t s) {
-    return launch_pdl(embed_kernel, dim3((hidden + 255) / 256), dim3(256), 0, s, pdl,
-                      static_cast<const uint8_t *>(E), hidden, tokens, pos, h);
+                         float *h, bool pdl, cudaStream_t s, int batch, int64_t tok_stride) {
+    return launch_pdl(embed_kernel, dim3((hidden + 255) / 256, batch), dim3(256), 0, s, pdl,
+                      static_cast<const uint8_t *>(E), hidden, tokens, pos, h, tok_stride);
 }
 
 cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const float *w,
@@ -482,36 +588,59 @@ cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const fl
 cudaError_t launch_qk_norm_rope_kv(const float *qkv, const float *q_norm, const float *k_norm,
                                    float eps, const float *rope, const int32_t *pos, float *q_out,
                                    void *kc, void *vc, int n_heads, int n_kv, int max_ctx,
-                                   bool pdl, cudaStream_t s) {
+                                   bool pdl, cudaStream_t s, const SeqStrides &b) {
     const int heads = n_heads + 2 * n_kv;
-    return launch_pdl(qk_norm_rope_kv_kernel, dim3((heads + 7) / 8), dim3(256), 0, s, pdl, qkv,
-                      q_norm, k_norm, eps, rope, pos, q_out, static_cast<__half *>(kc),
-                      static_cast<__half *>(vc), n_heads, n_kv, max_ctx);
+    return launch_pdl(qk_norm_rope_kv_kernel, dim3((heads + 7) / 8, b.batch), dim3(256), 0, s, pdl,
+                      qkv, q_norm, k_norm, eps, rope, pos, q_out, static_cast<__half *>(kc),
+                      static_cast<__half *>(vc), n_heads, n_kv, max_ctx, b.qkv, b.q, b.kv);
 }
 
 cudaError_t launch_attention(const float *q, const void *kc, const void *vc, const int32_t *pos,
                              float scale, int n_heads, int n_kv, int max_ctx, float *part_m,
                              float *part_l, float *part_o, float *out_f32, void *out_q8,
-                             bool pdl, cudaStream_t s) {
+                             bool pdl, cudaStream_t s, const SeqStrides &b) {
     const int gq = n_heads / n_kv;
     if (gq > ATT_MAXG || n_heads % n_kv) return cudaErrorInvalidValue;
     const int max_chunks = (max_ctx + ATT_CHUNK - 1) / ATT_CHUNK;
-    const dim3 grid(n_kv, max_chunks);
+    const dim3 grid(n_kv, max_chunks, b.batch);
     const __half *k = static_cast<const __half *>(kc);
     const __half *v = static_cast<const __half *>(vc);
     cudaError_t e;
+#define ABRA_ATT(G)                                                                                  \
+    launch_pdl(attention_chunk_kernel<G>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, \
+               max_chunks, part_m, part_l, part_o, b.q, b.kv)
     switch (gq) {
-        case 1: e = launch_pdl(attention_chunk_kernel<1>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, max_chunks, part_m, part_l, part_o); break;
-        case 2: e = launch_pdl(attention_chunk_kernel<2>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, max_chunks, part_m, part_l, part_o); break;
-        case 4: e = launch_pdl(attention_chunk_kernel<4>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, max_chunks, part_m, part_l, part_o); break;
-        case 8: e = launch_pdl(attention_chunk_kernel<8>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, max_chunks, part_m, part_l, part_o); break;
+        case 1: e = ABRA_ATT(1); break;
+        case 2: e = ABRA_ATT(2); break;
+        case 4: e = ABRA_ATT(4); break;
+        case 8: e = ABRA_ATT(8); break;
         default: return cudaErrorInvalidValue;
     }
+#undef ABRA_ATT
     if (e != cudaSuccess) return e;
-    return launch_pdl(attention_merge_quant_kernel, dim3((n_heads + 7) / 8), dim3(256), 0, s, pdl,
-                      static_cast<const float *>(part_m), static_cast<const float *>(part_l),
+    return launch_pdl(attention_merge_quant_kernel, dim3((n_heads + 7) / 8, b.batch), dim3(256), 0, s,
+                      pdl, static_cast<const float *>(part_m), static_cast<const float *>(part_l),
                       static_cast<const float *>(part_o), pos, n_heads, max_chunks, out_f32,
                       static_cast<block_q8_1 *>(out_q8));
+}
+
+cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t *tokens,
+                                int32_t *picks, int64_t tok_stride, int32_t *pos,
+                                const int32_t *n_prompt, int max_ctx, int batch, bool pdl,
+                                cudaStream_t s) {
+    cudaError_t e = launch_pdl(argmax_batch_kernel, dim3(batch), dim3(1024), 0, s, pdl, logits, n,
+                               ldl, tokens, picks, tok_stride, static_cast<const int32_t *>(pos),
+                               n_prompt, max_ctx);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(pos_advance_kernel, dim3(1), dim3(32), 0, s, pdl, pos, max_ctx);
+}
+
+cudaError_t launch_swiglu_quant(const float *g, const float *u, void *y, int64_t n, bool pdl,
+                                cudaStream_t s) {
+    const int64_t nb = n / QK8_1;
+    const int64_t grid = (nb * 32 + 255) / 256;
+    return launch_pdl(swiglu_quant_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0, s, pdl, g, u,
+                      static_cast<block_q8_1 *>(y), nb);
 }
 
 cudaError_t launch_argmax_finish(unsigned long long *key, int32_t *tokens, int32_t *picks,

@@ -93,6 +93,8 @@ cudaError_t launch_mmvq_q4k_partials(const void *w, const void *x_q8, float *y, 
 // part = ks * 32 * N floats of scratch and adds a combine launch.
 cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N, int64_t K,
                            int64_t ldy, int ks, float *part, int flags, cudaStream_t stream);
+// Sets the tensor-core kernels' attributes (outside stream capture).
+cudaError_t prepare_mmvq_tc();
 
 // ------------------------------------------------------------ quantize ---
 cudaError_t launch_quantize_q8_1(const float *x, void *y, int64_t K, int ncols,

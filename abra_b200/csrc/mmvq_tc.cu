@@ -389,6 +389,21 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+cudaError_t prepare_mmvq_tc() {
+    constexpr int smem = tc_layout().bytes;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    void (*fns[4])(const TcParams, const CUtensorMap) = {mmvq_tc_kernel<1>, mmvq_tc_kernel<2>,
+                                                         mmvq_tc_kernel<4>, mmvq_tc_kernel<8>};
+    for (int ki = 0; ki < 4; ++ki) {
+        e = cudaFuncSetAttribute(fns[ki], cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+    }
+    return tensor_map_encoder() ? cudaSuccess : cudaErrorNotSupported;
+}
+
 cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N, int64_t K,
                            int64_t ldy, int ks, float *part, int flags, cudaStream_t stream) {
     if (K % QK_K || K <= 0 || N <= 0 || ldy < N || !(ks == 1 || ks == 2 || ks == 4 || ks == 8) ||

@@ -92,6 +92,11 @@ struct Model {
     uint8_t *xq, *oq, *aq;
     int32_t *tokens, *picks, *pos, *nprompt;
     unsigned long long *amax = nullptr;  // argmax key of the output MMVQ
+    // batched decode (batch > 1): sequences in lockstep at one shared
+    // position; activations, KV cache and tokens are per sequence
+    int batch = 1;
+    float *gbuf = nullptr, *ubuf = nullptr;  // gate and up outputs
+    float *tc_ws = nullptr;                  // k-part scratch of the tensor-core MMVQ
     int max_chunks = 0;
     cudaStream_t stream = nullptr;
     cudaGraphExec_t graph = nullptr;
@@ -190,7 +195,8 @@ static cudaError_t build(Model &m) {
         TRY(launch_gen_q4k_cols(y.wdown, c.hidden, nsb_f, sh.ffn_lo / QK_K, sh.ffn_hi / QK_K, s,
                                 tensor_id(l, 8), 0, flags, st));
     }
-    const size_t kv = static_cast<size_t>(c.n_layers) * sh.kv_heads * c.max_ctx * c.head_dim * 2;
+    const int B = m.batch;
+    const size_t kv = static_cast<size_t>(B) * c.n_layers * sh.kv_heads * c.max_ctx * c.head_dim * 2;
     TRY(alloc(m, &m.kc, kv));
     TRY(alloc(m, &m.vc, kv));
     TRY(cudaMemsetAsync(m.kc, 0, kv, st));
@@ -212,28 +218,36 @@ static cudaError_t build(Model &m) {
     m.max_chunks = (c.max_ctx + 255) / 256;
     int64_t mx = c.hidden > ffn_l ? c.hidden : ffn_l;
     if (qd_l > mx) mx = qd_l;
-    TRY(alloc(m, &m.h, c.hidden * 4));
-    TRY(alloc(m, &m.h2, c.hidden * 4));
-    TRY(alloc(m, &m.delta, c.hidden * 4));
-    TRY(alloc(m, &m.qkv, qkv_l * 4));
-    TRY(alloc(m, &m.q, qd_l * 4));
-    TRY(alloc(m, &m.att, qd_l * 4));
-    TRY(alloc(m, &m.part_m, static_cast<size_t>(sh.q_heads) * m.max_chunks * 4));
-    TRY(alloc(m, &m.part_l, static_cast<size_t>(sh.q_heads) * m.max_chunks * 4));
-    TRY(alloc(m, &m.part_o, static_cast<size_t>(sh.q_heads) * m.max_chunks * c.head_dim * 4));
-    TRY(alloc(m, &m.act, ffn_l * 4));
-    TRY(alloc(m, &m.logits, static_cast<size_t>(vocab_l) * 4));
-    TRY(alloc(m, &m.xq, (mx / QK8_1) * Q81_BYTES));
-    TRY(alloc(m, &m.oq, (qd_l / QK8_1) * Q81_BYTES));
-    TRY(alloc(m, &m.aq, (ffn_l / QK8_1) * Q81_BYTES));
-    TRY(alloc(m, &m.tokens, (c.max_ctx + 1) * 4));
-    TRY(alloc(m, &m.picks, (c.max_ctx + 1) * 4));
+    TRY(alloc(m, &m.h, static_cast<size_t>(B) * c.hidden * 4));
+    TRY(alloc(m, &m.h2, static_cast<size_t>(B) * c.hidden * 4));
+    TRY(alloc(m, &m.delta, static_cast<size_t>(B) * c.hidden * 4));
+    TRY(alloc(m, &m.qkv, B * qkv_l * 4));
+    TRY(alloc(m, &m.q, B * qd_l * 4));
+    TRY(alloc(m, &m.att, B * qd_l * 4));
+    TRY(alloc(m, &m.part_m, static_cast<size_t>(B) * sh.q_heads * m.max_chunks * 4));
+    TRY(alloc(m, &m.part_l, static_cast<size_t>(B) * sh.q_heads * m.max_chunks * 4));
+    TRY(alloc(m, &m.part_o, static_cast<size_t>(B) * sh.q_heads * m.max_chunks * c.head_dim * 4));
+    TRY(alloc(m, &m.act, B * ffn_l * 4));
+    TRY(alloc(m, &m.logits, static_cast<size_t>(B) * vocab_l * 4));
+    TRY(alloc(m, &m.xq, B * (mx / QK8_1) * Q81_BYTES));
+    TRY(alloc(m, &m.oq, B * (qd_l / QK8_1) * Q81_BYTES));
+    TRY(alloc(m, &m.aq, B * (ffn_l / QK8_1) * Q81_BYTES));
+    TRY(alloc(m, &m.tokens, static_cast<size_t>(B) * (c.max_ctx + 1) * 4));
+    TRY(alloc(m, &m.picks, static_cast<size_t>(B) * (c.max_ctx + 1) * 4));
+    if (B > 1) {
+        TRY(alloc(m, &m.gbuf, B * ffn_l * 4));
+        TRY(alloc(m, &m.ubuf, B * ffn_l * 4));
+        int64_t ws = 8 * c.hidden;  // k-parts x rows of the K-split launches
+        if (2 * ffn_l > ws) ws = 2 * ffn_l;
+        if (2 * qkv_l > ws) ws = 2 * qkv_l;
+        TRY(alloc(m, &m.tc_ws, static_cast<size_t>(B) * ws * 4));
+    }
     TRY(alloc(m, &m.pos, 4));
     TRY(alloc(m, &m.nprompt, 4));
     TRY(alloc(m, &m.amax, 8));
     TRY(cudaMemsetAsync(m.amax, 0, 8, st));
-    TRY(cudaMemsetAsync(m.tokens, 0, (c.max_ctx + 1) * 4, st));
-    TRY(cudaMemsetAsync(m.picks, 0, (c.max_ctx + 1) * 4, st));
+    TRY(cudaMemsetAsync(m.tokens, 0, static_cast<size_t>(B) * (c.max_ctx + 1) * 4, st));
+    TRY(cudaMemsetAsync(m.picks, 0, static_cast<size_t>(B) * (c.max_ctx + 1) * 4, st));
     TRY(cudaMemsetAsync(m.pos, 0, 4, st));
     TRY(cudaMemsetAsync(m.nprompt, 0, 4, st));
     if (sh.world > 1) {
@@ -264,8 +278,60 @@ static const MmvqConfig *tuned(const int64_t sh[4]) {
     return mmvq_candidate_by_id(abra_tune_get(sh[0], sh[1], 1, static_cast<int>(sh[2])));
 }
 
+// The batched step (batch 32): every GEMV on the tensor cores with all
+// sequences as its 32 columns; the column-wise kernels take the sequence as
+// a grid dimension.  Per sequence the arithmetic is the batch-1 step's,
+// kernel for kernel, so the logits are the same bits.
+static cudaError_t record_step_batched(const Model &m, cudaStream_t st) {
+    const abra_model_config &c = m.cfg;
+    const int B = m.batch, L = c.n_layers;
+    const bool pdl = (c.flags & ABRA_MODEL_NO_PDL) == 0;
+    const int pf = pdl ? MMVQ_PDL : 0;
+    const int64_t hd = c.head_dim, qd = c.n_heads * hd;
+    const int64_t qkv_rows = (c.n_heads + 2 * c.n_kv_heads) * hd;
+    const size_t kv_layer = static_cast<size_t>(c.n_kv_heads) * c.max_ctx * c.head_dim;
+    const int64_t tok_stride = c.max_ctx + 1;
+    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
+    SeqStrides sb;
+    sb.batch = B;
+    sb.qkv = qkv_rows;
+    sb.q = qd;
+    sb.kv = static_cast<int64_t>(L) * kv_layer;
+    DeltaSet none = {}, one = {};
+    one.p[0] = m.delta;
+    one.G = 1;
+    auto tc = [&](const void *w, const void *x, float *y, int64_t N, int64_t K, int ks) {
+        return launch_mmvq_tc(w, x, y, N, K, N, ks, m.tc_ws, pf, st);
+    };
+    TRY(launch_embed(m.embd, c.hidden, m.tokens, m.pos, m.h, pdl, st, B, tok_stride));
+    for (int l = 0; l < L; ++l) {
+        const LayerW &y = m.layers[l];
+        TRY(launch_residual_rmsnorm_quant(m.h, l == 0 ? none : one, y.attn_norm, c.eps, m.xq, c.hidden,
+                                          B, pdl, st));
+        TRY(tc(y.wqkv, m.xq, m.qkv, qkv_rows, c.hidden, 2));
+        TRY(launch_qk_norm_rope_kv(m.qkv, y.q_norm, y.k_norm, c.eps, m.rope, m.pos, m.q,
+                                   m.kc + l * kv_layer, m.vc + l * kv_layer, c.n_heads, c.n_kv_heads,
+                                   c.max_ctx, pdl, st, sb));
+        TRY(launch_attention(m.q, m.kc + l * kv_layer, m.vc + l * kv_layer, m.pos, scale, c.n_heads,
+                             c.n_kv_heads, c.max_ctx, m.part_m, m.part_l, m.part_o, m.att, m.oq, pdl,
+                             st, sb));
+        TRY(tc(y.wo, m.oq, m.delta, c.hidden, qd, 8));
+        TRY(launch_residual_rmsnorm_quant(m.h, one, y.ffn_norm, c.eps, m.xq, c.hidden, B, pdl, st));
+        TRY(tc(y.wgate, m.xq, m.gbuf, c.ffn, c.hidden, 2));
+        TRY(tc(y.wup, m.xq, m.ubuf, c.ffn, c.hidden, 2));
+        TRY(launch_swiglu_quant(m.gbuf, m.ubuf, m.aq, static_cast<int64_t>(B) * c.ffn, pdl, st));
+        TRY(tc(y.wdown, m.aq, m.delta, c.hidden, c.ffn, 8));
+    }
+    TRY(launch_residual_rmsnorm_quant(m.h, L > 0 ? one : none, m.out_norm, c.eps, m.xq, c.hidden, B,
+                                      pdl, st));
+    TRY(tc(m.embd, m.xq, m.logits, c.vocab, c.hidden, 1));
+    return launch_argmax_batch(m.logits, c.vocab, c.vocab, m.tokens, m.picks, tok_stride, m.pos,
+                               m.nprompt, c.max_ctx, B, pdl, st);
+}
+
 // The decode step for the token at tokens[*pos] (recorded into the graph).
 static cudaError_t record_step(const Model &m, cudaStream_t st) {
+    if (m.batch > 1) return record_step_batched(m, st);
     const abra_model_config &c = m.cfg;
     const abra_tp_shard &sh = m.sh;
     const int W = sh.world;
@@ -414,6 +480,7 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
 }
 
 static cudaError_t prepare(const Model &m) {
+    if (m.batch > 1) return prepare_mmvq_tc();
     const StepShapes ss = step_shapes(m.cfg, m.sh);
     for (const int64_t *sh : {ss.qkv, ss.o, ss.gate_up, ss.down, ss.out}) {
         const MmvqConfig *cfg = tuned(sh);
@@ -486,7 +553,20 @@ int abra_model_create(const abra_model_config *cfg, void **out) {
     return abra_model_create_tp(cfg, 0, 1, out);
 }
 
+static int create_model(const abra_model_config *cfg, int32_t rank, int32_t world, int32_t batch,
+                        void **out);
+
 int abra_model_create_tp(const abra_model_config *cfg, int32_t rank, int32_t world, void **out) {
+    return create_model(cfg, rank, world, 1, out);
+}
+
+int abra_model_create_batched(const abra_model_config *cfg, int32_t batch, void **out) {
+    if (batch != 1 && batch != 32) return model_fail(ABRA_E_UNSUPPORTED, "batch must be 1 or 32", cudaSuccess);
+    return create_model(cfg, 0, 1, batch, out);
+}
+
+static int create_model(const abra_model_config *cfg, int32_t rank, int32_t world, int32_t batch,
+                        void **out) {
     if (!cfg || !out) return model_fail(ABRA_E_INVALID, "null pointer", cudaSuccess);
     const abra_model_config &c = *cfg;
     if (c.head_dim != 128 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads ||
@@ -501,6 +581,7 @@ int abra_model_create_tp(const abra_model_config *cfg, int32_t rank, int32_t wor
     if (!m) return model_fail(ABRA_E_INVALID, "out of host memory", cudaSuccess);
     m->cfg = c;
     m->sh = shard;
+    m->batch = batch;
     m->connected = world == 1;
     cudaGetDevice(&m->device);
     cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
@@ -560,10 +641,47 @@ int abra_model_tp_connect(void *model, const void *handles, int32_t size_each) {
     return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "graph capture", e);
 }
 
+int abra_model_reset_batched(void *model, const int32_t *prompts, int32_t n_prompt) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || !prompts || n_prompt < 1 || n_prompt > m->cfg.max_ctx)
+        return model_fail(ABRA_E_INVALID, "bad prompt", cudaSuccess);
+    const int B = m->batch;
+    for (int64_t i = 0; i < static_cast<int64_t>(B) * n_prompt; ++i)
+        if (prompts[i] < 0 || prompts[i] >= m->cfg.vocab)
+            return model_fail(ABRA_E_INVALID, "token id out of range", cudaSuccess);
+    const int32_t zero = 0;
+    const size_t stride = static_cast<size_t>(m->cfg.max_ctx) + 1;
+    cudaError_t e = cudaSuccess;
+    for (int b = 0; b < B && e == cudaSuccess; ++b)
+        e = cudaMemcpyAsync(m->tokens + b * stride, prompts + static_cast<size_t>(b) * n_prompt,
+                            n_prompt * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, &zero, 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->nprompt, &n_prompt, 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e == cudaSuccess) m->host_pos = 0;
+    return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "reset", e);
+}
+
+int abra_model_read_batched(void *model, int32_t *tokens, int32_t n_tokens, float *logits) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || n_tokens < 0 || n_tokens > m->cfg.max_ctx + 1)
+        return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
+    const size_t stride = static_cast<size_t>(m->cfg.max_ctx) + 1;
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    for (int b = 0; b < m->batch && e == cudaSuccess && tokens && n_tokens; ++b)
+        e = cudaMemcpy(tokens + static_cast<size_t>(b) * n_tokens, m->tokens + b * stride, n_tokens * 4,
+                       cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && logits)
+        e = cudaMemcpy(logits, m->logits, static_cast<size_t>(m->batch) * (m->sh.vocab_hi - m->sh.vocab_lo) * 4,
+                       cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "read", e);
+}
+
 int abra_model_reset(void *model, const int32_t *prompt, int32_t n_prompt) {
     Model *m = static_cast<Model *>(model);
     if (!m || !prompt || n_prompt < 1 || n_prompt > m->cfg.max_ctx)
         return model_fail(ABRA_E_INVALID, "bad prompt", cudaSuccess);
+    if (m->batch > 1) return model_fail(ABRA_E_INVALID, "batched model: use abra_model_reset_batched", cudaSuccess);
     for (int i = 0; i < n_prompt; ++i)
         if (prompt[i] < 0 || prompt[i] >= m->cfg.vocab)
             return model_fail(ABRA_E_INVALID, "token id out of range", cudaSuccess);
@@ -643,6 +761,7 @@ int abra_model_generate(void *model, const int32_t *prompt, int32_t n_prompt, in
 int abra_model_decode_streaming(void *model, int32_t n, int32_t *out) {
     Model *m = static_cast<Model *>(model);
     if (!m || !out || n < 1) return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
+    if (m->batch > 1) return model_fail(ABRA_E_UNSUPPORTED, "streaming is for batch 1", cudaSuccess);
     if (static_cast<int64_t>(m->host_pos) + n > m->cfg.max_ctx)
         return model_fail(ABRA_E_INVALID, "steps would pass max_ctx", cudaSuccess);
     if (!m->connected) return model_fail(ABRA_E_INVALID, "tensor-parallel model not connected", cudaSuccess);

@@ -76,6 +76,68 @@ def _check(rc: int, what: str) -> None:
         raise _lib.AbraError(rc, what, msg.decode() if msg else "")
 
 
+class BatchedDecodeModel:
+    """32 sequences decoded in lockstep at one shared position, every GEMV on
+    the tcgen05 tensor cores (abra_model_create_batched); per sequence the
+    logits and tokens equal the batch-1 model's bit for bit."""
+
+    def __init__(self, batch: int = 32, **config):
+        self.handle = None
+        self.batch = batch
+        self.cfg = default_config(**config)
+        h = C.c_void_p()
+        _check(_lib.lib.abra_model_create_batched(C.byref(self.cfg), batch, C.byref(h)),
+               "abra_model_create_batched")
+        self.handle = h
+
+    def close(self) -> None:
+        if self.handle:
+            _lib.lib.abra_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def reset(self, prompts) -> None:
+        """prompts: (batch, n_prompt) token ids."""
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        if p.ndim != 2 or p.shape[0] != self.batch:
+            raise ValueError(f"prompts must be ({self.batch}, n_prompt)")
+        _check(_lib.lib.abra_model_reset_batched(self.handle, p.ctypes.data, p.shape[1]),
+               "abra_model_reset_batched")
+
+    def step(self, n: int = 1) -> None:
+        _check(_lib.lib.abra_model_step(self.handle, n), "abra_model_step")
+
+    def sync(self) -> None:
+        _check(_lib.lib.abra_model_sync(self.handle), "abra_model_sync")
+
+    def tokens(self, n: int) -> np.ndarray:
+        out = np.empty((self.batch, n), dtype=np.int32)
+        _check(_lib.lib.abra_model_read_batched(self.handle, out.ctypes.data, n, None),
+               "abra_model_read_batched")
+        return out
+
+    def logits(self) -> np.ndarray:
+        out = np.empty((self.batch, self.cfg.vocab), dtype=np.float32)
+        _check(_lib.lib.abra_model_read_batched(self.handle, None, 0, out.ctypes.data),
+               "abra_model_read_batched")
+        return out
+
+    @property
+    def stream(self) -> int:
+        st, wb, kb = C.c_void_p(), C.c_uint64(), C.c_uint64()
+        _check(_lib.lib.abra_model_info(self.handle, C.byref(st), C.byref(wb), C.byref(kb)),
+               "abra_model_info")
+        return st.value or 0
+
+
 class DecodeModel:
     """A seeded Qwen3-4B-shaped model resident on the current CUDA device.
 

@@ -223,6 +223,18 @@ int abra_model_decode_streaming(void *model, int32_t n, int32_t *out);
 int abra_model_info(void *model, void **stream, uint64_t *weight_bytes, uint64_t *kv_bytes);
 const char *abra_model_last_error(void);
 
+/* ------------------------------------------------- batched decode --- */
+/* batch = 32 sequences decoded in lockstep at one shared position, every
+ * GEMV on the tcgen05 tensor cores (abra_q4k_mmvq_tc) with the sequences as
+ * its 32 columns; the per-sequence logits and tokens are bit-identical to
+ * the batch-1 model's.  batch = 1 is abra_model_create.  Prompts of the
+ * batch share one length; tokens and logits are read per sequence. */
+int abra_model_create_batched(const abra_model_config *cfg, int32_t batch, void **model);
+/* prompts: batch x n_prompt token ids, sequence after sequence. */
+int abra_model_reset_batched(void *model, const int32_t *prompts, int32_t n_prompt);
+/* tokens: batch x n_tokens (prompt then picks), logits: batch x vocab. */
+int abra_model_read_batched(void *model, int32_t *tokens, int32_t n_tokens, float *logits);
+
 /* ------------------------------------------- tensor-parallel decode --- */
 /* The same model split over world = 2, 4 or 8 GPUs of one node, one process
  * (or thread) per GPU.  Replaces the reference's llama.cpp tensor split with
