@@ -225,6 +225,27 @@ def launch_ops(plan, ncols: int, pdl: bool, stream=None):
             _lib.check(rc, "abra_q4k_mmvq")
 
 
+def tc_ks(N: int) -> int:
+    """k-parts of the batch-32 tensor-core MMVQ: enough CTAs for 148 SMs."""
+    return 1 if N >= 16384 else 2 if N >= 4096 else 8
+
+
+def launch_ops_tc(plan, ws_ptr: int, pdl: bool, stream=None):
+    """The same decode weight set at batch 32 through the tcgen05 MMVQ
+    (abra_q4k_mmvq_tc); a fused gate/up op is its two matrices."""
+    from abra_b200 import _lib
+    from abra_b200.q4k import stream_handle
+
+    f = _lib.lib.abra_q4k_mmvq_tc
+    st = stream_handle(stream)
+    flags = _lib.ABRA_MMVQ_PDL if pdl else 0
+    for w, w2, x, y, N, K, nmat in plan:
+        for wm in ((w,) if nmat == 1 else (w, w2)):
+            rc = f(wm, x, y, N, K, 32, N, tc_ks(N), ws_ptr, flags, st)
+            if rc:
+                _lib.check(rc, "abra_q4k_mmvq_tc")
+
+
 class Sweep:
     def __init__(self, dev, batch: int, seed: int = 0):
         import torch
@@ -503,6 +524,31 @@ def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, se
             "tokens_head": toks[:8].tolist()}
 
 
+def decode_batched(torch, warmup: int, steps: int, batch: int = 32, seed: int = 0):
+    """Batch-32 decode (32 sequences in lockstep, tcgen05 GEMVs): aggregate
+    tok/s over ``steps`` graph replays after the 16-token prompts and
+    ``warmup`` untimed steps, CUDA events on the model's stream."""
+    from abra_b200.model import BatchedDecodeModel
+
+    m = BatchedDecodeModel(batch, max_ctx=PROMPT + warmup + steps, seed=seed)
+    prompts = np.random.default_rng(seed).integers(0, m.cfg.vocab, (batch, PROMPT)).astype(np.int32)
+    m.reset(prompts)
+    m.step(PROMPT - 1 + warmup)
+    m.sync()
+    st = torch.cuda.ExternalStream(m.stream)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(st)
+    m.step(steps)
+    e.record(st)
+    e.synchronize()
+    ms = s.elapsed_time(e) / steps
+    toks = m.tokens(PROMPT + warmup + steps)[:, PROMPT:]
+    m.close()
+    return {"batch": batch, "depth": 0, "ms_per_step": round(ms, 4),
+            "tok_s_aggregate": round(batch * 1000.0 / ms, 1), "tokens_head_seq0": toks[0, :8].tolist(),
+            "path": "abra_model_create_batched: every GEMV on tcgen05 kind::i8 (abra_q4k_mmvq_tc)"}
+
+
 def decode_main(a, dist):
     import torch
 
@@ -536,6 +582,24 @@ def decode_main(a, dist):
     extras["gemv_sweep"] = {"workload": WORKLOAD, "GBps": round(achieved, 1),
                             "ms_per_step": round(ms_sw, 4), "launches_per_step": sw.launches}
     cpu = None
+    if dist.world == 1:
+        # batch 32 on the tensor cores: the decode weight set as one graph, and
+        # the batched decode step
+        sw32 = Sweep(torch.device("cuda", dist.local), 32)
+        ws = torch.empty(8 * 32 * 20480, dtype=torch.float32, device=sw32.dev)
+        g32 = sw32.capture(lambda: launch_ops_tc(sw32.plan, ws.data_ptr(), True))
+        for _ in range(3):
+            g32.replay()
+        ms32 = sw32.timed(max(3, a.steps // 16), g32.replay)
+        del g32
+        extras["gemv_sweep_b32_tc"] = {
+            "workload": WORKLOAD, "batch": 32, "GBps": round(sw32.bytes / (ms32 * 1e-3) / 1e9, 1),
+            "weight_GBps": round(sw32.weight_bytes / (ms32 * 1e-3) / 1e9, 1),
+            "ms_per_step": round(ms32, 4), "launches_per_step": sw32.launches + LAYERS,
+            "kernel": "mmvq_tc_kernel (tcgen05.mma kind::i8, TMEM, 2-D TMA)"}
+        del sw32, ws
+        torch.cuda.empty_cache()
+        extras["decode_b32"] = decode_batched(torch, a.warmup, a.steps)
     if dist.rank == 0 and dist.world == 1:
         if not a.no_extras:
             extras["per_shape"] = shape_table(sw)
