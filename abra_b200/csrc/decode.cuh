@@ -35,9 +35,6 @@ cudaError_t launch_argmax_finish(unsigned long long *key, int32_t *tokens, int32
                                  cudaStream_t s, const unsigned long long *wait_cnt = nullptr,
                                  unsigned long long *epoch = nullptr,
                                  unsigned long long per_step = 0);
-cudaError_t launch_argmax_advance(const float *logits, int n, int32_t *tokens, int32_t *picks,
-                                  int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
-                                  cudaStream_t s);
 // Greedy picks of a batch of sequences (logits rows ldl apart, token rows
 // tok_stride apart), then one advance of the shared position.
 cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t *tokens,

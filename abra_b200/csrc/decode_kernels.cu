@@ -388,57 +388,6 @@ __global__ void __launch_bounds__(256)
 }
 
 // --------------------------------------------------------------- argmax ---
-// Greedy token: largest logit, ties to the lowest index.  Writes
-// tokens[*pos + 1] unless that slot still belongs to the prompt (first
-// *n_prompt_p tokens), records the pick in picks[*pos], then advances *pos.
-__global__ void __launch_bounds__(1024)
-    argmax_advance_kernel(const float *__restrict__ x, int n, int32_t *__restrict__ tokens,
-                          int32_t *__restrict__ picks, int32_t *__restrict__ pos_p,
-                          const int32_t *__restrict__ n_prompt_p, int max_ctx) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    pdl_wait();
-    pdl_launch_dependents();
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = x[i];
-        if (v > bv) {
-            bv = v;
-            bi = i;
-        }
-    }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
-        if (ov > bv || (ov == bv && oi < bi)) {
-            bv = ov;
-            bi = oi;
-        }
-    }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) {
-        sv[warp] = bv;
-        si[warp] = bi;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
-            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
-                bv = sv[w];
-                bi = si[w];
-            }
-        const int p = *pos_p;
-        if (bi == 0x7fffffff) bi = 0;
-        if (p < max_ctx) {  // the host never steps past max_ctx
-            picks[p] = bi;
-            if (p + 1 >= *n_prompt_p) tokens[p + 1] = bi;
-            *pos_p = p + 1;
-        }
-    }
-}
-
 // Finish of the argmax fused into the output MMVQ: decode the winning key
 // (ties already resolved to the lowest row), reset it for the next step,
 // record the pick, append it past the prompt, advance *pos.
@@ -649,13 +598,6 @@ cudaError_t launch_argmax_finish(unsigned long long *key, int32_t *tokens, int32
                                  unsigned long long *epoch, unsigned long long per_step) {
     return launch_pdl(argmax_finish_kernel, dim3(1), dim3(32), 0, s, pdl, key, tokens, picks, pos,
                       n_prompt, max_ctx, wait_cnt, epoch, per_step);
-}
-
-cudaError_t launch_argmax_advance(const float *logits, int n, int32_t *tokens, int32_t *picks,
-                                  int32_t *pos, const int32_t *n_prompt, int max_ctx, bool pdl,
-                                  cudaStream_t s) {
-    return launch_pdl(argmax_advance_kernel, dim3(1), dim3(1024), 0, s, pdl, logits, n, tokens,
-                      picks, pos, n_prompt, max_ctx);
 }
 
 }  // namespace abra

@@ -665,8 +665,10 @@ def reference_arm(a, dist):
     if a.workload == "decode":
         weight_bytes = sum(nmat * q4k_bytes(N, K) for _, N, K, nmat, _ in sweep_ops())
         val, unit, metric = gbs * 1e9 / weight_bytes, "tok/s", "Qwen3-4B-shape decode tok/s"
-        cfg = {"workload": DECODE_WORKLOAD, "model": "qwen3-4b-shape-q4k", "depth": 0,
-               "prompt": PROMPT, "gen": a.steps, "batch_per_gpu": 1}
+        cfg = {"workload": DECODE_WORKLOAD, "model": "qwen3-4b-shape-q4k", "global_batch": 1,
+               "batch_per_gpu": 1, "seq_len": PROMPT + a.warmup + a.steps, "depth": 0,
+               "prompt": PROMPT, "gen": a.steps,
+               "parallelism": f"CPU restatement on {threads} host threads"}
         sample += ", scaled to the 2.26 GB of Q4_K weights a token reads"
     else:
         val, unit, metric = gbs, "GB/s", "Q4_K GEMV HBM GB/s"
@@ -674,7 +676,8 @@ def reference_arm(a, dist):
     line = {
         "impl": "reference", "metric": metric, "value": round(val, 3),
         "unit": unit, "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(1000.0 / val, 3) if a.workload == "decode" else None,
+        "higher_is_better": True, "scaling": "strong" if a.workload == "decode" else "weak",
         "vs_baseline": None, "dtype": "u4 x s8 dot, fp32 scale", "data": "synthetic",
         "config": cfg,
         "cpu_baseline": {"value": round(val, 3), "unit": unit, "cores": threads, "kind": "port",
