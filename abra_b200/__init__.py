@@ -1,4 +1,4 @@
-"""abra_b200 -- B200-native (sm_100a) Q4_K x Q8_1 decode path.
+"""abra_b200 -- B200-native (sm_100a) Q4_K x Q8_1 decode path (with its Q6_K leg).
 
 The compute lives in libabra_b200.so (hand-written CUDA for sm_100a behind a
 C ABI, include/abra_b200.h).  This package binds it with ctypes and mirrors
@@ -39,6 +39,18 @@ from .q4k import (
     register_autotuned_table_entry,
     rmsnorm_quantize_q8_1,
     slice_start,
+)
+from .q6k import (
+    Q6K_BYTES,
+    Q6KCandidateSpec,
+    gen_q6k,
+    mmvq_q6k,
+    mmvq_q6k_kshard,
+    mmvq_q6k_partials,
+    q6k_candidates,
+    q6k_nbytes,
+    q6k_tune_get,
+    q6k_tune_set,
 )
 
 __version__ = _lib.lib.abra_version().decode()

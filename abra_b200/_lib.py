@@ -45,6 +45,16 @@ SIGNATURES: dict[str, tuple] = {
     "abra_tune_set": (C.c_int, [_i64, _i64, _i32, _i32, _i32]),
     "abra_tune_get": (C.c_int, [_i64, _i64, _i32, _i32]),
     "abra_tune_clear": (C.c_int, []),
+    # Q6_K
+    "abra_q6k_mmvq": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _vp]),
+    "abra_q6k_mmvq_ex": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _i32, _vp]),
+    "abra_q6k_mmvq_kshard": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _i32, _i32, _i32, _vp]),
+    "abra_q6k_mmvq_partials": (C.c_int, [_vp, _vp, _fp, _vp, _i64, _i64, _i32, _vp]),
+    "abra_gen_q6k": (C.c_int, [_vp, _i64, _u64, _u64, _i64, _vp]),
+    "abra_q6k_candidate_count": (C.c_int, []),
+    "abra_q6k_candidate_info": (C.c_int, [_i32] + [C.POINTER(C.c_int32)] * 5),
+    "abra_q6k_tune_set": (C.c_int, [_i64, _i64, _i32, _i32]),
+    "abra_q6k_tune_get": (C.c_int, [_i64, _i64, _i32]),
     # decode model
     "abra_model_default_config": (C.c_int, [_vp]),
     "abra_model_create": (C.c_int, [_vp, C.POINTER(C.c_void_p)]),

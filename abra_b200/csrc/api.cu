@@ -31,6 +31,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 std::mutex g_tune_mu;
 std::map<std::tuple<int64_t, int64_t, int, int>, int> g_tune;
+std::map<std::tuple<int64_t, int64_t, int>, int> g_tune_q6;
 
 // Default when the table has no entry: more k-parts for few rows or long K.
 int default_candidate(int64_t N, int64_t K, int ncols, int nmat) {
@@ -257,6 +258,115 @@ int abra_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_i
     return ABRA_OK;
 }
 
+// ------------------------------------------------------------- Q6_K ---
+static int q6k_common(const void *w, const void *x, float *y, int64_t N, int64_t K,
+                      int32_t ncols, int64_t ldy, int32_t candidate, int32_t flags,
+                      const abra::MmvqOpts *tp, void *stream) {
+    int id = candidate;
+    if (id == 0) id = abra_q6k_tune_get(N, K, ncols);
+    const abra::MmvqConfig *cfg = abra::q6k_candidate_by_id(id);
+    if (!cfg) return fail(ABRA_E_INVALID, "unknown Q6_K candidate id %d", id);
+    cudaError_t e = abra::launch_mmvq_q6k(*cfg, w, x, y, N, K, ncols, ldy,
+                                          (flags & ABRA_MMVQ_PDL) ? abra::MMVQ_PDL : 0,
+                                          static_cast<cudaStream_t>(stream), nullptr, tp);
+    if (e == cudaErrorInvalidConfiguration)
+        return fail(ABRA_E_UNSUPPORTED, "Q6_K candidate %d does not fit N=%lld K=%lld ncols=%d", id,
+                    (long long)N, (long long)K, ncols);
+    if (e != cudaSuccess) return cuda_fail(e, "q6k mmvq launch");
+    return ABRA_OK;
+}
+
+int abra_q6k_mmvq_ex(const void *w, const void *x, float *y, int64_t N, int64_t K, int32_t ncols,
+                     int64_t ldy, int32_t candidate, int32_t flags, void *stream) {
+    int rc = check_mmvq_args(w, x, y, N, K, ncols, ldy);
+    if (rc) return rc;
+    return q6k_common(w, x, y, N, K, ncols, ldy, candidate, flags, nullptr, stream);
+}
+
+int abra_q6k_mmvq(const void *w, const void *x, float *y, int64_t N, int64_t K, int32_t ncols,
+                  void *stream) {
+    return abra_q6k_mmvq_ex(w, x, y, N, K, ncols, N, 0, 0, stream);
+}
+
+int abra_q6k_mmvq_kshard(const void *w, const void *x, float *y, int64_t N, int64_t K,
+                         int32_t ncols, int64_t K_full, int32_t sl_base, int32_t sl_cnt,
+                         int32_t candidate, int32_t flags, void *stream) {
+    int rc = check_mmvq_args(w, x, y, N, K, ncols, N);
+    if (rc) return rc;
+    if (K_full <= 0 || K_full % 256 != 0 || K_full > 65536 || sl_base < 0 ||
+        !(sl_cnt == 1 || sl_cnt == 2 || sl_cnt == 4 || sl_cnt == 8) || sl_base + sl_cnt > 8)
+        return fail(ABRA_E_INVALID, "bad K-shard (K_full=%lld sl_base=%d sl_cnt=%d)",
+                    (long long)K_full, sl_base, sl_cnt);
+    const int nsb_g = static_cast<int>(K_full / 256);
+    if ((abra::slice_start(nsb_g, sl_base + sl_cnt) - abra::slice_start(nsb_g, sl_base)) * 256 != K)
+        return fail(ABRA_E_INVALID, "K=%lld is not the width of canonical slices [%d, %d) of K_full=%lld",
+                    (long long)K, sl_base, sl_base + sl_cnt, (long long)K_full);
+    abra::MmvqOpts tp;
+    tp.sl_nsb = nsb_g;
+    tp.sl_base = sl_base;
+    tp.sl_cnt = sl_cnt;
+    return q6k_common(w, x, y, N, K, ncols, N, candidate, flags, &tp, stream);
+}
+
+int abra_q6k_mmvq_partials(const void *w, const void *x, float *y, int32_t *P, int64_t N,
+                           int64_t K, int32_t ncols, void *stream) {
+    int rc = check_mmvq_args(w, x, y, N, K, ncols, N);
+    if (rc) return rc;
+    if (!P) return fail(ABRA_E_INVALID, "null partials pointer");
+    cudaError_t e = abra::launch_mmvq_q6k_partials(w, x, y, P, N, K, ncols,
+                                                   static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidConfiguration)
+        return fail(ABRA_E_UNSUPPORTED, "Q6_K partials do not fit N=%lld K=%lld ncols=%d",
+                    (long long)N, (long long)K, ncols);
+    if (e != cudaSuccess) return cuda_fail(e, "q6k partials launch");
+    return ABRA_OK;
+}
+
+int abra_gen_q6k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                 int64_t block_offset, void *stream) {
+    if (!dst || nblocks < 0 || block_offset < 0) return fail(ABRA_E_INVALID, "bad generator arguments");
+    if (reinterpret_cast<uintptr_t>(dst) & 1u) return fail(ABRA_E_INVALID, "dst must be 2-byte aligned");
+    cudaError_t e = abra::launch_gen_q6k(dst, nblocks, seed, tensor_id, block_offset,
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "gen_q6k launch");
+    return ABRA_OK;
+}
+
+int abra_q6k_candidate_count(void) {
+    int n = 0;
+    abra::q6k_candidates(&n);
+    return n;
+}
+
+int abra_q6k_candidate_info(int32_t index, int32_t *id, int32_t *mode, int32_t *ks,
+                            int32_t *ctas_per_sm, int32_t *stage_kb) {
+    int n = 0;
+    const abra::MmvqConfig *c = abra::q6k_candidates(&n);
+    if (index < 0 || index >= n) return fail(ABRA_E_INVALID, "candidate index %d out of range", index);
+    if (id) *id = c[index].id;
+    if (mode) *mode = c[index].mode;
+    if (ks) *ks = c[index].ks;
+    if (ctas_per_sm) *ctas_per_sm = c[index].ctas_per_sm;
+    if (stage_kb) *stage_kb = c[index].stage_kb;
+    return ABRA_OK;
+}
+
+int abra_q6k_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t candidate) {
+    if (!abra::q6k_candidate_by_id(candidate)) return fail(ABRA_E_INVALID, "unknown Q6_K candidate id %d", candidate);
+    std::lock_guard<std::mutex> lock(g_tune_mu);
+    g_tune_q6[std::make_tuple(N, K, static_cast<int>(ncols))] = candidate;
+    return ABRA_OK;
+}
+
+int abra_q6k_tune_get(int64_t N, int64_t K, int32_t ncols) {
+    {
+        std::lock_guard<std::mutex> lock(g_tune_mu);
+        auto it = g_tune_q6.find(std::make_tuple(N, K, static_cast<int>(ncols)));
+        if (it != g_tune_q6.end()) return it->second;
+    }
+    return abra::q6k_default_candidate(N, K, ncols);
+}
+
 int abra_candidate_count(void) {
     int n = 0;
     abra::mmvq_candidates(&n);
@@ -297,6 +407,7 @@ int abra_tune_get(int64_t N, int64_t K, int32_t ncols, int32_t nmat) {
 int abra_tune_clear(void) {
     std::lock_guard<std::mutex> lock(g_tune_mu);
     g_tune.clear();
+    g_tune_q6.clear();
     return ABRA_OK;
 }
 

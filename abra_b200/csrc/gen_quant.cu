@@ -150,6 +150,52 @@ cudaError_t launch_gen_q4k(void *dst, int64_t nblocks, uint64_t seed, uint64_t t
     return launch_gen_q4k_ex(dst, nblocks, seed, tensor_id, block_offset, 0, stream);
 }
 
+// Q6_K blocks (210 bytes): thread i writes word w = i % 27 of local block
+// i / 27 -- words 0..25 are bytes 8w..8w+7 (ql, qh, scales), word 26 gives
+// d ~ U(0.0001, 0.002) as fp16 at byte 208.  Stores are 16-bit: a block is
+// only 2-byte aligned.  Local block blk is global block block_offset +
+// (blk / width) * gstride + blk % width, as for Q4_K.
+__global__ void gen_q6k_kernel(uint16_t *__restrict__ dst, int64_t nblocks, uint64_t key,
+                               int64_t block_offset, int64_t width, int64_t gstride) {
+    const int64_t nwords = nblocks * 27;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nwords;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t blk = i / 27;
+        const int w = static_cast<int>(i - blk * 27);
+        const int64_t row = blk / width;
+        const int64_t gb = block_offset + row * gstride + (blk - row * width);
+        const uint64_t h = stream_word(key, static_cast<uint64_t>(gb) * 27u + static_cast<uint64_t>(w));
+        uint16_t *b = dst + blk * 105;  // 210 bytes = 105 halfwords
+        if (w < 26) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) b[4 * w + k] = static_cast<uint16_t>(h >> (16 * k));
+        } else {
+            const float d = __fmaf_rn(unit24(h >> 40), 0.0019f, 0.0001f);
+            b[104] = __half_as_ushort(__float2half_rn(d));
+        }
+    }
+}
+
+cudaError_t launch_gen_q6k_cols(void *dst, int64_t nblocks, int64_t width, int64_t gstride,
+                                uint64_t seed, uint64_t tensor_id, int64_t block_offset,
+                                cudaStream_t stream) {
+    if (nblocks <= 0) return cudaSuccess;
+    if (reinterpret_cast<uintptr_t>(dst) & 1) return cudaErrorInvalidValue;
+    const int64_t nwords = nblocks * 27;
+    const int threads = 256;
+    const int64_t want = (nwords + threads - 1) / threads;
+    const int grid = static_cast<int>(want < 148 * 32 ? want : 148 * 32);
+    gen_q6k_kernel<<<grid, threads, 0, stream>>>(static_cast<uint16_t *>(dst), nblocks,
+                                                 stream_key(seed, tensor_id), block_offset, width,
+                                                 gstride);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gen_q6k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                           int64_t block_offset, cudaStream_t stream) {
+    return launch_gen_q6k_cols(dst, nblocks, nblocks, 0, seed, tensor_id, block_offset, stream);
+}
+
 cudaError_t launch_gen_norm_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
                                 cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;

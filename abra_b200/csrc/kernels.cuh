@@ -112,6 +112,35 @@ cudaError_t launch_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_
 
 int device_sm_count();
 
+// Dynamic shared memory an MMVQ plan may use (the 227 KiB opt-in limit less
+// room for static shared memory), and the attribute that allows it, set once
+// per (kernel, device).
+constexpr int kMmvqMaxSmem = 227 * 1024 - 1024;
+cudaError_t ensure_smem_attr_ptr(const void *fn);
+// K-shard slicing of a launch (unsharded unless tp names a shard); false when
+// the shard's slices do not add up to nsb superblocks.
+bool mmvq_shard_of(const MmvqOpts *tp, int nsb, int &sl_nsb, int &sl_base, int &sl_shift);
+
+// --------------------------------------------------------- Q6_K MMVQ ---
+// Candidates of the Q6_K x Q8_1 MMVQ (MmvqConfig with mode 0 per-row
+// copies, 1 whole-unit copies, 2 direct loads).
+const MmvqConfig *q6k_candidates(int *count);
+const MmvqConfig *q6k_candidate_by_id(int id);
+// Default candidate for a shape.
+int q6k_default_candidate(int64_t N, int64_t K, int ncols);
+// y = W x for N x K Q6_K rows; amax and tp (slicing and row_offset only) as
+// for launch_mmvq_q4k.
+cudaError_t launch_mmvq_q6k(const MmvqConfig &cfg, const void *w, const void *x_q8, float *y,
+                            int64_t N, int64_t K, int ncols, int64_t ldy, int flags,
+                            cudaStream_t stream, unsigned long long *amax = nullptr,
+                            const MmvqOpts *tp = nullptr);
+// Debug: also stores the exact int32 16-weight dots P[c][r][b][16].
+cudaError_t launch_mmvq_q6k_partials(const void *w, const void *x_q8, float *y, int32_t *P,
+                                     int64_t N, int64_t K, int ncols, cudaStream_t stream);
+cudaError_t prepare_mmvq_q6k(const MmvqConfig &cfg, int ncols);
+cudaError_t launch_gen_q6k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                           int64_t block_offset, cudaStream_t stream);
+
 // Reads (and optionally clears) every translation unit's device error word.
 cudaError_t read_error_words(unsigned *value, bool clear);
 

@@ -68,9 +68,9 @@ static int ks_index(int ks) { return ks == 1 ? 0 : ks == 2 ? 1 : ks == 4 ? 2 : k
 // Dynamic shared memory a plan may use: the 227 KiB opt-in limit less room
 // for the kernel's static shared memory (a few bytes of argmax keys).
 constexpr int kOptinSmem = 227 * 1024;
-constexpr int kMaxSmem = kOptinSmem - 1024;
+constexpr int kMaxSmem = kMmvqMaxSmem;
 
-static cudaError_t ensure_smem_attr(MmvqFn fn) {
+cudaError_t ensure_smem_attr_ptr(const void *fn) {
     // Raise the dynamic shared-memory limit once per (kernel, device).
     static std::mutex mu;
     static const void *done[1024];
@@ -80,20 +80,23 @@ static cudaError_t ensure_smem_attr(MmvqFn fn) {
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < ndone; ++i)
-        if (done[i] == reinterpret_cast<const void *>(fn) && done_dev[i] == dev) return cudaSuccess;
+        if (done[i] == fn && done_dev[i] == dev) return cudaSuccess;
     cudaFuncAttributes fa;
-    cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(fn));
+    cudaError_t e = cudaFuncGetAttributes(&fa, fn);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(reinterpret_cast<const void *>(fn),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kOptinSmem - static_cast<int>(fa.sharedSizeBytes));
     if (e != cudaSuccess) return e;
     if (ndone < 1024) {
-        done[ndone] = reinterpret_cast<const void *>(fn);
+        done[ndone] = fn;
         done_dev[ndone] = dev;
         ++ndone;
     }
     return cudaSuccess;
+}
+
+static cudaError_t ensure_smem_attr(MmvqFn fn) {
+    return ensure_smem_attr_ptr(reinterpret_cast<const void *>(fn));
 }
 
 struct MmvqPlan {
@@ -102,7 +105,7 @@ struct MmvqPlan {
 
 // Slicing of a launch: unsharded unless tp names a K-shard.  Returns false
 // when the shard's slices do not add up to nsb superblocks.
-static bool shard_of(const MmvqOpts *tp, int nsb, int &sl_nsb, int &sl_base, int &sl_shift) {
+bool mmvq_shard_of(const MmvqOpts *tp, int nsb, int &sl_nsb, int &sl_base, int &sl_shift) {
     sl_nsb = nsb;
     sl_base = 0;
     int sl_cnt = 8;
@@ -124,7 +127,7 @@ static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int 
     const bool staged = cfg.mode != MODE_DIRECT;
     const int nsl = 8 / ks;
     int sl_nsb, sl_base, sl_shift;
-    if (!shard_of(tp, nsb, sl_nsb, sl_base, sl_shift)) return false;
+    if (!mmvq_shard_of(tp, nsb, sl_nsb, sl_base, sl_shift)) return false;
     int max_sb = 0;
     for (int j = 0; j < ks; ++j) {
         const int w = shard_slice(sl_nsb, sl_base, sl_shift, (j + 1) * nsl) -
@@ -173,7 +176,7 @@ static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int 
 
 // Copies the tensor-parallel options into the kernel parameters.
 static bool apply_tp(MmvqParams &prm, const MmvqOpts *tp) {
-    if (!shard_of(tp, prm.nsb, prm.sl_nsb, prm.sl_base, prm.sl_shift)) return false;
+    if (!mmvq_shard_of(tp, prm.nsb, prm.sl_nsb, prm.sl_base, prm.sl_shift)) return false;
     if (!tp) return true;
     if (tp->npeer < 0 || tp->npeer > 8) return false;
     prm.row_offset = tp->row_offset;

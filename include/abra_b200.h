@@ -173,7 +173,46 @@ int abra_candidate_info(int32_t index, int32_t *id, int32_t *mode, int32_t *ks, 
  * get_autotuned_candidate_for_shape (kernels/q4k/q4k_family.cuh:86-87). */
 int abra_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t nmat, int32_t candidate);
 int abra_tune_get(int64_t N, int64_t K, int32_t ncols, int32_t nmat); /* candidate id */
-int abra_tune_clear(void);
+int abra_tune_clear(void); /* clears the Q4_K and the Q6_K tables */
+
+/* ------------------------------------------------------------ Q6_K ----- */
+/* y[c][r] = sum_k W[r][k] x[c][k] for N x K Q6_K rows W (ggml's block_q6_K,
+ * 210 bytes per 256 weights: ql[128], qh[64], int8 scales[16], fp16 d;
+ * w = d * scales[e/16] * (q - 32)) and ncols (1..8) Q8_1 columns x.  The
+ * Q6_K leg of the reference's dispatch, abra_dispatch_mmvq<GGML_TYPE_Q6_K>
+ * (kernels/q4k/abra-mmvq.cuh:209-221, which runs ggml's vec_dot_q6_K_q8_1
+ * at :138-141; the reference's f64 oracle for it is
+ * tests/runtime_kernel_test.cu:82-106).  Exact int32 16-weight dots, fp32
+ * scaling in a fixed order, the canonical eight K-slices of the Q4_K path.
+ * w 16-byte aligned; x 16-byte aligned; ldy >= N; candidate 0 = tuned. */
+int abra_q6k_mmvq(const void *w_q6k, const void *x_q8_1, float *y, int64_t N, int64_t K,
+                  int32_t ncols, void *stream);
+int abra_q6k_mmvq_ex(const void *w_q6k, const void *x_q8_1, float *y, int64_t N, int64_t K,
+                     int32_t ncols, int64_t ldy, int32_t candidate, int32_t flags,
+                     void *stream);
+/* K-shard form (row-parallel tensor parallelism), as abra_q4k_mmvq_kshard:
+ * w holds canonical slices [sl_base, sl_base + sl_cnt) of rows K_full wide;
+ * y is that shard's subtree of the unsharded result. */
+int abra_q6k_mmvq_kshard(const void *w_q6k, const void *x_q8_1, float *y, int64_t N, int64_t K,
+                         int32_t ncols, int64_t K_full, int32_t sl_base, int32_t sl_cnt,
+                         int32_t candidate, int32_t flags, void *stream);
+/* Debug form: also stores the exact int32 dots P[c][r][b][j] of the 16
+ * sub-blocks j (16 weights each) of every superblock b. */
+int abra_q6k_mmvq_partials(const void *w_q6k, const void *x_q8_1, float *y, int32_t *P,
+                           int64_t N, int64_t K, int32_t ncols, void *stream);
+/* Seeded synthetic Q6_K blocks [block_offset, block_offset + nblocks) of
+ * tensor tensor_id: ql, qh, scales uniform over byte values, d ~
+ * U(0.0001, 0.002) fp16.  dst 2-byte aligned. */
+int abra_gen_q6k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
+                 int64_t block_offset, void *stream);
+/* Q6_K candidates (index 0..count-1 -> id, feed mode 0 per-row bulk copies,
+ * 1 whole-unit copy, 2 direct loads; k-split; CTAs per SM; stage KiB) and
+ * their tuning table keyed by (N, K, ncols). */
+int abra_q6k_candidate_count(void);
+int abra_q6k_candidate_info(int32_t index, int32_t *id, int32_t *mode, int32_t *ks,
+                            int32_t *ctas_per_sm, int32_t *stage_kb);
+int abra_q6k_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t candidate);
+int abra_q6k_tune_get(int64_t N, int64_t K, int32_t ncols);
 
 /* ------------------------------------------------------ decode model --- */
 /* Qwen3-4B-shaped decode with every linear layer Q4_K:

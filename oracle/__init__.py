@@ -8,7 +8,9 @@ library never imports it.
 block layouts kernels/q4k/q4k_q8_mmvq.cuh:42-57, scale unpack
 tests/q4k_q8_test.cu:44-52, the f64 oracle tests/q4k_q8_test.cu:54-107,
 vec_dot_q4_K_q8_1 kernels/q4k/q4k_vecdot.cuh:23-87 and the Q8_1 quantizer
-kernels/q4k/q4k_q8_mmvq.cu:223-255 (paths inside talystalys/abra).
+kernels/q4k/q4k_q8_mmvq.cu:223-255 (paths inside talystalys/abra);
+q6k_oracle.c the Q6_K leg of the dispatch (kernels/q4k/abra-mmvq.cuh:138-141)
+with the reference's f64 Q6_K oracle tests/runtime_kernel_test.cu:82-106.
 
 ``_ref/libq4k_ref.so`` is the reference's own kernel family compiled from its
 sources (see Makefile); ``ref`` binds it when present.
@@ -25,7 +27,7 @@ HERE = Path(__file__).resolve().parent
 ORC_PATH = HERE / "liborc.so"
 REF_PATH = HERE / "_ref" / "libq4k_ref.so"
 
-QK_K, QK8_1, Q4K_BYTES, Q81_BYTES = 256, 32, 144, 36
+QK_K, QK8_1, Q4K_BYTES, Q81_BYTES, Q6K_BYTES = 256, 32, 144, 36, 210
 
 _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
@@ -64,6 +66,13 @@ def _load() -> C.CDLL:
         "orc_expf": (C.c_float, [C.c_float]),
         "orc_silu": (C.c_float, [C.c_float]),
         "orc_swiglu": (None, [_f32p, _f32p, _f32p, _i64]),
+        "orc_gen_q6k": (None, [_u8p, _i64, _u64, _u64, _i64]),
+        "orc_q6k_partials": (None, [_u8p, _u8p, _i32p, _i64, _i64, _i32]),
+        "orc_q6k_gemv": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i32, _i32]),
+        "orc_q6k_gemv_slices": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i32]),
+        "orc_q6k_gemv_f64": (None, [_u8p, _u8p, _f64p, _i64, _i64, _i32]),
+        "orc_q6k_absdot_f64": (None, [_u8p, _u8p, _f64p, _i64, _i64, _i32]),
+        "orc_dequant_q6k": (None, [_u8p, _f32p, _i64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -196,6 +205,87 @@ def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
 
 def gemv_swiglu(w_gate, w_up, xq, K: int, nthreads: int = 1) -> np.ndarray:
     return swiglu(gemv(w_gate, xq, K, nthreads), gemv(w_up, xq, K, nthreads))
+
+
+# -------------------------------------------------------------- Q6_K ------
+def gen_q6k(N: int, K: int, seed: int, tensor_id: int, row_offset: int = 0) -> np.ndarray:
+    """Q6_K rows [row_offset, row_offset+N) of a K-wide tensor, uint8 (N, K/256*210)."""
+    nsb = K // QK_K
+    out = np.empty(N * nsb * Q6K_BYTES, dtype=np.uint8)
+    lib.orc_gen_q6k(out, N * nsb, seed, tensor_id, row_offset * nsb)
+    return out.reshape(N, nsb * Q6K_BYTES)
+
+
+def _shape6(w: np.ndarray, xq: np.ndarray, K: int):
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+    xq2 = np.ascontiguousarray(np.atleast_2d(xq), dtype=np.uint8)
+    ncols = xq2.shape[0]
+    N = w.size // ((K // QK_K) * Q6K_BYTES)
+    return w, xq2.reshape(-1), N, ncols
+
+
+def q6k_partials(w, xq, K: int) -> np.ndarray:
+    """Exact int32 sub-block dots (ncols, N, K/256, 16)."""
+    w, xq, N, ncols = _shape6(w, xq, K)
+    P = np.empty(ncols * N * (K // QK_K) * 16, dtype=np.int32)
+    lib.orc_q6k_partials(w, xq, P, N, K, ncols)
+    return P.reshape(ncols, N, K // QK_K, 16)
+
+
+def q6k_gemv(w, xq, K: int, nthreads: int = 1) -> np.ndarray:
+    """Canonical fp32 Q6_K GEMV, (ncols, N)."""
+    w, xq, N, ncols = _shape6(w, xq, K)
+    y = np.empty(ncols * N, dtype=np.float32)
+    lib.orc_q6k_gemv(w, xq, y, N, K, ncols, nthreads)
+    return y.reshape(ncols, N)
+
+
+def q6k_gemv_slices(w, xq, K: int) -> np.ndarray:
+    w, xq, N, ncols = _shape6(w, xq, K)
+    v = np.empty(ncols * N * 8, dtype=np.float32)
+    lib.orc_q6k_gemv_slices(w, xq, v, N, K, ncols)
+    return v.reshape(ncols, N, 8)
+
+
+def q6k_gemv_f64(w, xq, K: int) -> np.ndarray:
+    """The reference's f64 Q6_K oracle (tests/runtime_kernel_test.cu:82-106)."""
+    w, xq, N, ncols = _shape6(w, xq, K)
+    y = np.empty(ncols * N, dtype=np.float64)
+    lib.orc_q6k_gemv_f64(w, xq, y, N, K, ncols)
+    return y.reshape(ncols, N)
+
+
+def q6k_absdot_f64(w, xq, K: int) -> np.ndarray:
+    w, xq, N, ncols = _shape6(w, xq, K)
+    s = np.empty(ncols * N, dtype=np.float64)
+    lib.orc_q6k_absdot_f64(w, xq, s, N, K, ncols)
+    return s.reshape(ncols, N)
+
+
+def dequant_q6k(w: np.ndarray) -> np.ndarray:
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+    nb = w.size // Q6K_BYTES
+    out = np.empty(nb * QK_K, dtype=np.float32)
+    lib.orc_dequant_q6k(w, out, nb)
+    return out
+
+
+def dequant_q6k_numpy(w: np.ndarray) -> np.ndarray:
+    """Independent vectorised decode of block_q6_K (ggml layout: ql[128],
+    qh[64], int8 scales[16], fp16 d), used to cross-check the C decoder."""
+    b = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1, Q6K_BYTES)
+    ql, qh = b[:, :128].astype(np.int32), b[:, 128:192].astype(np.int32)
+    sc = b[:, 192:208].view(np.int8).astype(np.float32)
+    d = b[:, 208:210].copy().view(np.float16).astype(np.float32)[:, 0]
+    q = np.empty((b.shape[0], 256), dtype=np.int32)
+    for half in range(2):
+        for group in range(4):
+            qlb = ql[:, half * 64 + (group % 2) * 32: half * 64 + (group % 2) * 32 + 32]
+            low = (qlb & 15) if group < 2 else (qlb >> 4)
+            hi = (qh[:, half * 32: half * 32 + 32] >> (2 * group)) & 3
+            q[:, half * 128 + group * 32: half * 128 + group * 32 + 32] = low | (hi << 4)
+    scale = (d[:, None] * np.repeat(sc, 16, axis=1)).astype(np.float32)
+    return (scale * (q - 32).astype(np.float32)).reshape(-1)
 
 
 def expf(x: float) -> float:

@@ -100,6 +100,8 @@ static inline uint64_t stream_key(uint64_t seed, uint64_t tensor_id) {
 static inline uint64_t stream_word(uint64_t key, uint64_t i) {
     return mix64(key + (i + 1ull) * 0x9E3779B97F4A7C15ull);
 }
+uint64_t orc_stream_key(uint64_t seed, uint64_t tensor_id) { return stream_key(seed, tensor_id); }
+uint64_t orc_stream_word(uint64_t key, uint64_t i) { return stream_word(key, i); }
 static inline float unit24(uint64_t bits24) { /* exact: 24-bit int * 2^-24 */
     return (float)(uint32_t)bits24 * 5.9604644775390625e-08f;
 }

@@ -28,6 +28,10 @@ uint16_t orc_f32_to_f16(float f);
 float    orc_f16_to_f32(uint16_t h);
 
 /* ---- seeded synthetic generators (counter-based, splitmix64) ------------ */
+/* Word i of the stream of (seed, tensor_id): the i-th splitmix64 output
+ * from key = orc_stream_key(seed, tensor_id). */
+uint64_t orc_stream_key(uint64_t seed, uint64_t tensor_id);
+uint64_t orc_stream_word(uint64_t key, uint64_t i);
 /* Q4_K superblocks [block_offset, block_offset + nblocks) of tensor
  * `tensor_id`: d, dmin ~ U(0.001, 0.02) as fp16, 12 scale bytes (= sixteen
  * 6-bit sc/m values ~ U{0..63}) and 128 nibble bytes (nibbles ~ U{0..15}). */

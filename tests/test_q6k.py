@@ -1,0 +1,166 @@
+"""CPU tests of the Q6_K oracle (no GPU).
+
+Pins the canonical fp32 Q6_K GEMV three ways: against a loop-for-loop
+restatement of the reference's f64 oracle (tests/runtime_kernel_test.cu:82-106)
+on the reference test's shapes and input patterns (:119-123), against an
+independent numpy decode of ggml's block_q6_K, and through its exact int32
+sub-block dots.  Also checks the K-slice tree and the K-shard subtree
+property that tensor parallelism relies on, and the C-ABI argument checks.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+TOL = 1e-5  # of sum_k |w_k| |x_k| per row
+
+
+def _pattern(N, K, pattern, seed=0):
+    """The reference test's three input patterns: 0 all-zero weights and
+    input, 1 U(-1, 1) input, 2 weights scaled x100."""
+    w = O.gen_q6k(N, K, seed, 40 + pattern)
+    rng = np.random.default_rng(seed + 7)
+    if pattern == 0:
+        w = np.zeros_like(w)
+        x = np.zeros((1, K), dtype=np.float32)
+    else:
+        x = rng.uniform(-1, 1, (1, K)).astype(np.float32)
+    if pattern == 2:
+        blocks = w.reshape(-1, 210)
+        d = blocks[:, 208:210].copy().view(np.float16).astype(np.float32)[:, 0]
+        d16 = np.array([O.lib.orc_f32_to_f16(float(v) * 100.0) for v in d], dtype=np.uint16)
+        blocks[:, 208:210] = d16.view(np.uint8).reshape(-1, 2)
+    return w, O.quantize_q8_1(x)
+
+
+def _codes(w: np.ndarray) -> np.ndarray:
+    """6-bit codes (nblocks, 256), decoded with numpy from the block layout."""
+    b = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1, 210).astype(np.int32)
+    q = np.empty((b.shape[0], 256), dtype=np.int32)
+    for e in range(256):
+        half, r = divmod(e, 128)
+        group, lane = divmod(r, 32)
+        qlb = b[:, half * 64 + lane + (group % 2) * 32]
+        low = (qlb & 15) if group < 2 else (qlb >> 4)
+        q[:, e] = low | (((b[:, 128 + half * 32 + lane] >> (2 * group)) & 3) << 4)
+    return q
+
+
+def test_generator_layout():
+    w = O.gen_q6k(64, 2560, 3, 9)
+    assert w.shape == (64, 10 * 210)
+    b = w.reshape(-1, 210)
+    d = b[:, 208:210].copy().view(np.float16).astype(np.float32)[:, 0]
+    assert (d >= 0.0001 * 0.999).all() and (d <= 0.002 * 1.001).all()
+    sc = b[:, 192:208].view(np.int8)
+    assert sc.min() < -100 and sc.max() > 100  # full int8 range
+    q = _codes(w)
+    assert q.min() == 0 and q.max() == 63
+    # row offsets continue the same stream
+    assert np.array_equal(O.gen_q6k(10, 2560, 3, 9, row_offset=54), w[54:])
+
+
+def test_dequant_c_matches_numpy_decoder():
+    w = O.gen_q6k(33, 768, 1, 2)
+    assert np.array_equal(O.dequant_q6k(w), O.dequant_q6k_numpy(w))
+
+
+@pytest.mark.parametrize("pattern", [0, 1, 2])
+@pytest.mark.parametrize("N", [1, 33, 64])
+@pytest.mark.parametrize("K", [256, 768, 2048, 2560, 4096, 4864, 9728])
+def test_canonical_matches_reference_f64_oracle(N, K, pattern):
+    w, xq = _pattern(N, K, pattern)
+    y = O.q6k_gemv(w, xq, K)
+    y64 = O.q6k_gemv_f64(w, xq, K)
+    scale = O.q6k_absdot_f64(w, xq, K)
+    assert np.isfinite(y).all()
+    if pattern == 0:
+        assert not y.any() and not y64.any()
+        return
+    err = np.abs(y.astype(np.float64) - y64) / np.maximum(scale, 1e-30)
+    assert err.max() <= TOL, err.max()
+
+
+def test_f64_oracle_is_the_dequantized_dot():
+    K = 2560
+    w = O.gen_q6k(17, K, 5, 3)
+    xq = O.quantize_q8_1(O.gen_normal_f32((2, K), 4))
+    wd = O.dequant_q6k_numpy(w).astype(np.float64).reshape(17, K)
+    xb = xq.reshape(2, K // 32, 36)
+    d8 = xb[:, :, 0:2].copy().view(np.float16).astype(np.float64)[:, :, 0]
+    q8 = xb[:, :, 4:].copy().view(np.int8).astype(np.float64)
+    xd = (d8[:, :, None] * q8).reshape(2, K)
+    ref = xd @ wd.T
+    y64 = O.q6k_gemv_f64(w, xq, K)
+    assert np.allclose(y64, ref, rtol=1e-12, atol=1e-9)
+
+
+def test_partials_exact_against_numpy():
+    N, K = 9, 768
+    w = O.gen_q6k(N, K, 2, 6)
+    xq = O.quantize_q8_1(O.gen_normal_f32((2, K), 5))
+    P = O.q6k_partials(w, xq, K)
+    q = _codes(w).reshape(N, K // 256, 256) - 32
+    q8 = xq.reshape(2, K // 32, 36)[:, :, 4:].copy().view(np.int8).astype(np.int64).reshape(2, K // 256, 256)
+    ref = np.einsum("rbe,cbe->crbe", q.astype(np.int64), q8).reshape(2, N, K // 256, 16, 16).sum(-1)
+    assert np.array_equal(P, ref)
+
+
+@pytest.mark.parametrize("nsb", [1, 3, 8, 10, 19, 38])
+def test_slices_and_tree(nsb):
+    K = nsb * 256
+    w = O.gen_q6k(7, K, 1, 8)
+    xq = O.quantize_q8_1(O.gen_normal_f32((3, K), 9))
+    v = O.q6k_gemv_slices(w, xq, K)
+    assert np.array_equal(O.tree8(v), O.q6k_gemv(w, xq, K))
+    assert np.array_equal(O.q6k_gemv(w, xq, K, nthreads=4), O.q6k_gemv(w, xq, K))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_kshard_partials_recombine_bit_exact(world):
+    """Row-parallel shards of a Q6_K ffn_down (K = 9728) recombine exactly."""
+    N, K = 40, 9728
+    w = O.gen_q6k(N, K, 4, 21)
+    xq = O.quantize_q8_1(O.gen_normal_f32((1, K), 8))
+    slices = O.q6k_gemv_slices(w, xq, K)
+    full = O.q6k_gemv(w, xq, K)
+    per = 8 // world
+    parts = [O.kshard_partial(slices, r * per, per) for r in range(world)]
+    assert np.array_equal(O.delta_tree(parts), full)
+
+
+def test_q6k_entry_points_reject_bad_arguments_without_gpu():
+    import abra_b200 as A
+    from abra_b200 import _lib
+
+    lib = _lib.lib
+    assert lib.abra_q6k_mmvq(0, 16, 16, 8, 256, 1, None) == _lib.ABRA_E_INVALID  # null
+    assert lib.abra_q6k_mmvq(16, 16, 16, 8, 300, 1, None) == _lib.ABRA_E_INVALID  # K
+    assert lib.abra_q6k_mmvq(16, 16, 16, 8, 256, 9, None) == _lib.ABRA_E_UNSUPPORTED  # ncols
+    assert lib.abra_q6k_mmvq(18, 16, 16, 8, 256, 1, None) == _lib.ABRA_E_INVALID  # align
+    assert lib.abra_q6k_mmvq_ex(16, 16, 16, 8, 256, 1, 4, 0, 0, None) == _lib.ABRA_E_INVALID  # ldy
+    assert lib.abra_q6k_mmvq_ex(16, 16, 16, 8, 256, 1, 8, 4242, 0, None) == _lib.ABRA_E_INVALID
+    assert "candidate" in _lib.last_error()
+    # a K-shard whose width is not that of its canonical slices
+    assert lib.abra_q6k_mmvq_kshard(16, 16, 16, 8, 512, 1, 9728, 0, 2, 0, 0, None) == _lib.ABRA_E_INVALID
+    assert lib.abra_q6k_mmvq_kshard(16, 16, 16, 8, 256, 1, 9728, 0, 3, 0, 0, None) == _lib.ABRA_E_INVALID
+    assert lib.abra_q6k_mmvq_partials(16, 16, 16, None, 8, 256, 1, None) == _lib.ABRA_E_INVALID
+    assert lib.abra_gen_q6k(17, 4, 0, 0, 0, None) == _lib.ABRA_E_INVALID
+    with pytest.raises(ValueError):
+        A.mmvq_q6k(16, 16, 16, 8, 300)
+
+
+def test_q6k_candidates_and_tuning():
+    import abra_b200 as A
+
+    c = A.q6k_candidates()
+    assert len(c) >= 10
+    for cid, s in c.items():
+        assert s.ks in (1, 2, 4, 8) and s.mode in (0, 1, 2) and (s.mode != 1 or s.ks == 1)
+    assert A.q6k_tune_get(151936, 2560) in c
+    A.q6k_tune_set(777, 2560, 1, 1042)
+    assert A.q6k_tune_get(777, 2560, 1) == 1042
+    with pytest.raises(ValueError):
+        A.q6k_tune_set(777, 2560, 1, 999999)
