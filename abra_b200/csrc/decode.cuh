@@ -15,6 +15,10 @@ struct SeqStrides {
 
 cudaError_t launch_embed(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
                          float *h, bool pdl, cudaStream_t s, int batch = 1, int64_t tok_stride = 0);
+// The same lookup from a Q6_K table (210-byte blocks).
+cudaError_t launch_embed_q6k(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
+                             float *h, bool pdl, cudaStream_t s, int batch = 1,
+                             int64_t tok_stride = 0);
 cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const float *w,
                                           float eps, void *y, int K, int ncols, bool pdl,
                                           cudaStream_t s);
@@ -56,5 +60,11 @@ cudaError_t launch_gen_norm_f32(float *dst, int64_t n, uint64_t seed, uint64_t t
 cudaError_t launch_gen_q4k_cols(void *dst, int64_t rows, int64_t nsb_g, int64_t sb_lo,
                                 int64_t sb_hi, uint64_t seed, uint64_t tensor_id, int64_t row0,
                                 int flags, cudaStream_t stream);
+// Q6_K blocks: local block i is global block block_offset + (i / width) *
+// gstride + i % width of the tensor's stream (width = nblocks, gstride = 0:
+// a contiguous run), bytes identical to abra_gen_q6k's.
+cudaError_t launch_gen_q6k_cols(void *dst, int64_t nblocks, int64_t width, int64_t gstride,
+                                uint64_t seed, uint64_t tensor_id, int64_t block_offset,
+                                cudaStream_t stream);
 
 }  // namespace abra

@@ -51,6 +51,31 @@ __global__ void embed_kernel(const uint8_t *__restrict__ E, int hidden,
     }
 }
 
+// Q6_K rows of the tied table (the Q4_K_M type map): element e of a 256-block
+// is (d * scales[e / 16]) * (q - 32), q the 6-bit code in ggml's block_q6_K
+// order (low nibble of ql[64 half + lane + 32 (group % 2)] for groups 0, 1,
+// high nibble for 2, 3; bits 2 group of qh[32 half + lane]).
+__global__ void embed_q6k_kernel(const uint8_t *__restrict__ E, int hidden,
+                                 const int32_t *__restrict__ tokens, const int32_t *__restrict__ pos,
+                                 float *__restrict__ h, int64_t tok_stride) {
+    pdl_wait();
+    pdl_launch_dependents();
+    tokens += blockIdx.y * tok_stride;
+    h += static_cast<int64_t>(blockIdx.y) * hidden;
+    const int tok = tokens[*pos];
+    const uint8_t *row = E + static_cast<int64_t>(tok) * (hidden / QK_K) * 210;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += blockDim.x * gridDim.x) {
+        const int e = i & 255, half = e >> 7, group = (e >> 5) & 3, lane = e & 31;
+        const uint8_t *blk = row + static_cast<int64_t>(i >> 8) * 210;
+        const int qlb = blk[half * 64 + lane + (group & 1) * 32];
+        const int low = group < 2 ? (qlb & 15) : (qlb >> 4);
+        const int q = low | (((blk[128 + half * 32 + lane] >> (2 * group)) & 3) << 4);
+        const int sc = static_cast<int8_t>(blk[192 + (e >> 4)]);
+        const float d = __half2float(*reinterpret_cast<const __half *>(blk + 208));
+        h[i] = __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q - 32));
+    }
+}
+
 // ------------------------------------------ residual + RMSNorm + Q8_1 ---
 // h = h + D (D = fixed-order tree of G partial deltas, G in {0,1,2,4,8}),
 // then Q8_1 of (h * r) * w, r = 1/sqrt(mean(h^2) + eps).  One CTA per column.
@@ -517,6 +542,12 @@ static cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t
 cudaError_t launch_embed(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
                          float *h, bool pdl, cudaStream_t s, int batch, int64_t tok_stride) {
     return launch_pdl(embed_kernel, dim3((hidden + 255) / 256, batch), dim3(256), 0, s, pdl,
+                      static_cast<const uint8_t *>(E), hidden, tokens, pos, h, tok_stride);
+}
+
+cudaError_t launch_embed_q6k(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
+                             float *h, bool pdl, cudaStream_t s, int batch, int64_t tok_stride) {
+    return launch_pdl(embed_q6k_kernel, dim3((hidden + 255) / 256, batch), dim3(256), 0, s, pdl,
                       static_cast<const uint8_t *>(E), hidden, tokens, pos, h, tok_stride);
 }
 

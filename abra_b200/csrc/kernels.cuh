@@ -70,6 +70,9 @@ struct MmvqXin {
     DeltaSet deltas;
     const float *norm_w;
     float eps;
+    // when set (4-byte aligned): CTA 0 also stores the Q8_1 activation
+    // (K/32 blocks), for another MMVQ on the same normalized input
+    uint8_t *x_out = nullptr;
 };
 // Batch-1 MMVQ whose activation is built in each CTA from the fp32 residual
 // stream (residual add + RMSNorm + Q8_1 fused into the prologue).
@@ -128,8 +131,8 @@ const MmvqConfig *q6k_candidates(int *count);
 const MmvqConfig *q6k_candidate_by_id(int id);
 // Default candidate for a shape.
 int q6k_default_candidate(int64_t N, int64_t K, int ncols);
-// y = W x for N x K Q6_K rows; amax and tp (slicing and row_offset only) as
-// for launch_mmvq_q4k.
+// y = W x for N x K Q6_K rows; amax and tp (slicing, row_offset and the L2
+// prefetch regions; no push or wait) as for launch_mmvq_q4k.
 cudaError_t launch_mmvq_q6k(const MmvqConfig &cfg, const void *w, const void *x_q8, float *y,
                             int64_t N, int64_t K, int ncols, int64_t ldy, int flags,
                             cudaStream_t stream, unsigned long long *amax = nullptr,

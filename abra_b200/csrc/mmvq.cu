@@ -264,6 +264,7 @@ cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void
     MmvqFn fn = mmvq_table_c1().xin[cfg.mode][ki][nmat - 1];
     if (!fn || !xin.h_in || !xin.norm_w) return cudaErrorInvalidValue;
     if (reinterpret_cast<uintptr_t>(xin.norm_w) & 15) return cudaErrorInvalidValue;  // float4 loads
+    if (reinterpret_cast<uintptr_t>(xin.x_out) & 3) return cudaErrorInvalidValue;
     MmvqPlan pl;
     if (!plan_mmvq(cfg, N, nsb, 1, nmat, pl, true, tp)) return cudaErrorInvalidConfiguration;
     MmvqParams prm = {};
@@ -279,6 +280,7 @@ cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void
     prm.deltas = xin.deltas;
     prm.norm_w = xin.norm_w;
     prm.eps = xin.eps;
+    prm.x_out = xin.x_out;
     if (!apply_tp(prm, tp)) return cudaErrorInvalidValue;
     return launch_plan(fn, pl, (flags & MMVQ_PDL) != 0, prm, stream);
 }

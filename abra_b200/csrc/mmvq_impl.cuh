@@ -81,23 +81,32 @@ struct MmvqParams {
     // L2 prefetch of the next kernels' weights, split evenly over the CTAs
     const uint8_t *pf_ptr[2];
     int64_t pf_bytes[2];
+    // fused input only: CTA 0 also stores the Q8_1 blocks it built (the
+    // bytes the standalone quantizer would write), for a later MMVQ of
+    // another weight type on the same activation
+    uint8_t *x_out;
 };
 
-// This CTA's share of the L2 prefetch regions, issued by one warp in 16 KB
-// pieces.
-__device__ __forceinline__ void prefetch_share(const MmvqParams &prm, int lane) {
+// This CTA's share of up to two L2 prefetch regions, issued by one warp in
+// 16 KB pieces.
+__device__ __forceinline__ void prefetch_regions(const uint8_t *const (&ptr)[2],
+                                                 const int64_t (&bytes)[2], int lane) {
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-        const int64_t units = prm.pf_bytes[r] >> 4;  // 16-byte units
+        const int64_t units = bytes[r] >> 4;  // 16-byte units
         if (units <= 0) continue;
         const int64_t u0 = units * blockIdx.x / gridDim.x;
         const int64_t u1 = units * (blockIdx.x + 1) / gridDim.x;
         constexpr int64_t PIECE = 1024;  // 16 KB
         for (int64_t u = u0 + lane * PIECE; u < u1; u += 32 * PIECE) {
             const int64_t n = u1 - u < PIECE ? u1 - u : PIECE;
-            prefetch_l2_bulk(prm.pf_ptr[r] + (u << 4), static_cast<uint32_t>(n << 4));
+            prefetch_l2_bulk(ptr[r] + (u << 4), static_cast<uint32_t>(n << 4));
         }
     }
+}
+
+__device__ __forceinline__ void prefetch_share(const MmvqParams &prm, int lane) {
+    prefetch_regions(prm.pf_ptr, prm.pf_bytes, lane);
 }
 
 // First superblock (relative to the shard) of local canonical slice i
@@ -422,13 +431,24 @@ __global__ void __launch_bounds__((NCW + (MODE == MODE_DIRECT ? 0 : 1)) * 32, MO
             int sum = (q0 + q1) + (q2 + q3);
 #pragma unroll
             for (int m = 4; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-            *reinterpret_cast<uint32_t *>(aq + i * 32 + sub * 4) =
-                (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
-                ((static_cast<uint32_t>(q2) & 0xffu) << 16) | (static_cast<uint32_t>(q3) << 24);
+            const uint32_t packed = (static_cast<uint32_t>(q0) & 0xffu) |
+                                    ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
+                                    ((static_cast<uint32_t>(q2) & 0xffu) << 16) |
+                                    (static_cast<uint32_t>(q3) << 24);
+            *reinterpret_cast<uint32_t *>(aq + i * 32 + sub * 4) = packed;
             if (sub == 0) {
                 const float d8 = __half2float(__float2half_rn(d));
                 ad8[i] = d8;
                 aA[i] = __fmul_rn(d8, __int2float_rn(sum));
+            }
+            if (blockIdx.x == 0 && prm.x_out) {  // d, s = d * sum as fp16, then the 32 int8
+                uint8_t *blk = prm.x_out + static_cast<int64_t>(i) * Q81_BYTES;
+                *reinterpret_cast<uint32_t *>(blk + 4 + sub * 4) = packed;
+                if (sub == 0)
+                    *reinterpret_cast<uint32_t *>(blk) =
+                        static_cast<uint32_t>(__half_as_ushort(__float2half_rn(d))) |
+                        (static_cast<uint32_t>(__half_as_ushort(
+                             __float2half_rn(__fmul_rn(d, __int2float_rn(sum))))) << 16);
             }
         }
     }

@@ -150,7 +150,14 @@ static bool q6_params(Q6Params &prm, const void *w, const void *x_q8, float *y, 
     prm.w_bytes = N * nsb * Q6K_BYTES;
     if (!mmvq_shard_of(tp, nsb, prm.sl_nsb, prm.sl_base, prm.sl_shift)) return false;
     prm.row_offset = tp ? tp->row_offset : 0;
-    return !tp || tp->npeer == 0;  // no tensor-parallel push on this path
+    if (!tp) return true;
+    for (int r = 0; r < 2; ++r) {
+        if (tp->pf_bytes[r] <= 0) continue;
+        if ((reinterpret_cast<uintptr_t>(tp->pf_ptr[r]) & 15) || (tp->pf_bytes[r] & 15)) return false;
+        prm.pf_ptr[r] = static_cast<const uint8_t *>(tp->pf_ptr[r]);
+        prm.pf_bytes[r] = tp->pf_bytes[r];
+    }
+    return tp->npeer == 0 && !tp->wait_cnt;  // no tensor-parallel push or wait on this path
 }
 
 cudaError_t launch_mmvq_q6k(const MmvqConfig &cfg, const void *w, const void *x_q8, float *y,

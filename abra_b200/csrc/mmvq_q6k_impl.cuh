@@ -54,6 +54,8 @@ struct Q6Params {
     unsigned long long *amax;  // optional per-column argmax keys
     int row_offset;            // added to row ids in argmax keys
     int sl_nsb, sl_base, sl_shift;  // K-shard slicing, as MmvqParams
+    const uint8_t *pf_ptr[2];        // L2 prefetch of the next kernels' weights
+    int64_t pf_bytes[2];
 };
 
 struct Q6Layout {
@@ -257,6 +259,7 @@ __global__ void __launch_bounds__((NCW + (MODE == Q6_DIRECT ? 0 : 1)) * 32, MODE
             const uint64_t pol = policy_evict_first();
             const int U = nrg * KS;
             for (int u = 0; u < U; ++u) {
+                if (u == nstage) prefetch_regions(prm.pf_ptr, prm.pf_bytes, lane);  // after the first ring fill
                 const int s = u % nstage, k = u / nstage;
                 if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1, ERR_WAIT_EMPTY)) break;
                 const int rg = rg_begin + u / KS, j = u % KS;
@@ -289,6 +292,7 @@ __global__ void __launch_bounds__((NCW + (MODE == Q6_DIRECT ? 0 : 1)) * 32, MODE
                     bulk_g2s(d, prm.W + (start & ~int64_t(15)), bulk, &full[s], pol);
                 }
             }
+            if (U <= nstage) prefetch_regions(prm.pf_ptr, prm.pf_bytes, lane);
             return;
         }
     }
@@ -316,6 +320,9 @@ __global__ void __launch_bounds__((NCW + (MODE == Q6_DIRECT ? 0 : 1)) * 32, MODE
     }
     if (threadIdx.x < NCOLS) s_amax[threadIdx.x] = 0ull;
     named_bar_sync(1, NCW * 32);
+    if constexpr (!STAGED) {
+        if (warp == NCW - 1) prefetch_regions(prm.pf_ptr, prm.pf_bytes, lane);
+    }
 
     const int grp = warp / KS, j = warp % KS;
     const int p = lane >> 3, g = lane & 7, h = p >> 1, s = p & 1;

@@ -19,6 +19,13 @@
 //   Q8_1 of the SwiGLU output
 //   MMVQ down
 // then residual + RMSNorm + Q8_1, the tied output MMVQ and argmax.
+//
+// With ABRA_MODEL_Q4_K_M the weights follow the real Qwen3-4B-Q4_K_M type
+// map: the tied table is Q6_K, and layers with q6k_layer() keep attn_v and
+// ffn_down in Q6_K.  There the fused MMVQ covers q|k only and also exports
+// its Q8_1 activation, which the Q6_K V MMVQ reads; ffn_down runs the Q6_K
+// MMVQ on the SwiGLU's Q8_1; the output is a residual + RMSNorm + Q8_1
+// kernel followed by the Q6_K MMVQ with the argmax keys.
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -36,7 +43,18 @@ namespace abra {
 struct LayerW {
     float *attn_norm, *q_norm, *k_norm, *ffn_norm;
     uint8_t *wqkv, *wo, *wgate, *wup, *wdown;
+    uint8_t *wv = nullptr;  // Q6_K V rows (q6 layers; wqkv then holds q|k only)
+    bool q6 = false;        // attn_v and ffn_down in Q6_K
 };
+
+// Q4_K_M type map (llama.cpp's use_more_bits rule): attn_v and ffn_down stay
+// Q6_K in layer l of n when l < n/8, l >= 7n/8 or (l - n/8) % 3 == 2 -- for
+// 36 layers: 0-3, 6, 9, ..., 30 and 31-35, as in the Qwen3-4B-Q4_K_M census
+// the reference records (bench/results/m3/qwen3-q4k-tensor-map.json).
+static bool q6k_layer(int l, int n) {
+    const int a = n / 8, b = 7 * n / 8;
+    return l < a || l >= b || (l - a) % 3 == 2;
+}
 
 // What one rank of a tensor-parallel group holds (world == 1: everything).
 // K-sharded layers (o, down) are cut on canonical K-slice boundaries, so the
@@ -83,6 +101,7 @@ struct Model {
     bool connected = false;
     std::vector<void *> allocs;
     uint8_t *embd = nullptr;
+    bool mix = false;  // the Q4_K_M type map (embd is Q6_K)
     float *out_norm = nullptr;
     std::vector<LayerW> layers;
     __half *kc = nullptr, *vc = nullptr;
@@ -138,6 +157,10 @@ static size_t q4k_bytes(int64_t rows, int64_t cols) {
     return static_cast<size_t>(rows) * (cols / QK_K) * Q4K_BYTES;
 }
 
+static size_t q6k_bytes(int64_t rows, int64_t cols) {
+    return static_cast<size_t>(rows) * (cols / QK_K) * 210;
+}
+
 static cudaError_t build(Model &m) {
     const abra_model_config &c = m.cfg;
     const abra_tp_shard &sh = m.sh;
@@ -149,11 +172,16 @@ static cudaError_t build(Model &m) {
     const int64_t ffn_l = sh.ffn_hi - sh.ffn_lo, vocab_l = sh.vocab_hi - sh.vocab_lo;
     const int64_t nsb_h = c.hidden / QK_K, nsb_o = qd / QK_K, nsb_f = c.ffn / QK_K;
     cudaStream_t st = m.stream;
-    auto walloc = [&](uint8_t **p, int64_t rows, int64_t cols) -> cudaError_t {
-        const size_t b = q4k_bytes(rows, cols);
+    auto walloc = [&](uint8_t **p, int64_t rows, int64_t cols, bool q6 = false) -> cudaError_t {
+        const size_t b = q6 ? q6k_bytes(rows, cols) : q4k_bytes(rows, cols);
         TRY(alloc(m, p, b));
         m.weight_bytes += b;
         return cudaSuccess;
+    };
+    // Q6_K rows [row0, row0 + n) of a tensor `cols` wide, at dst
+    auto rows6 = [&](uint8_t *dst, int64_t row0, int64_t n, int64_t cols, uint64_t tid) -> cudaError_t {
+        const int64_t nb = n * (cols / QK_K);
+        return launch_gen_q6k_cols(dst, nb, nb, 0, s, tid, row0 * (cols / QK_K), st);
     };
     // full-K rows [row0, row0 + n) of a tensor, at dst
     auto rows = [&](uint8_t *dst, int64_t row0, int64_t n, uint64_t tid) -> cudaError_t {
@@ -165,19 +193,30 @@ static cudaError_t build(Model &m) {
     };
     // the whole tied table on every rank: embedding lookups need any row;
     // the output MMVQ reads this rank's vocab rows of it
-    TRY(walloc(&m.embd, c.vocab, c.hidden));
-    TRY(rows(m.embd, 0, c.vocab, tensor_id(-1, 1)));
+    m.mix = (c.flags & ABRA_MODEL_Q4_K_M) != 0;
+    TRY(walloc(&m.embd, c.vocab, c.hidden, m.mix));
+    if (m.mix)
+        TRY(rows6(m.embd, 0, c.vocab, c.hidden, tensor_id(-1, 1)));
+    else
+        TRY(rows(m.embd, 0, c.vocab, tensor_id(-1, 1)));
     TRY(norm(&m.out_norm, c.hidden, tensor_id(-1, 2)));
     m.layers.resize(c.n_layers);
     for (int l = 0; l < c.n_layers; ++l) {
         LayerW &y = m.layers[l];
         TRY(norm(&y.attn_norm, c.hidden, tensor_id(l, 0)));
         // q|k|v rows of this rank's heads, fused: [q heads | k heads | v heads]
-        TRY(walloc(&y.wqkv, qkv_l, c.hidden));
+        // (q6 layers: q|k here, the V rows as Q6_K in wv)
+        y.q6 = m.mix && q6k_layer(l, c.n_layers);
+        TRY(walloc(&y.wqkv, y.q6 ? qd_l + kvd_l : qkv_l, c.hidden));
         const size_t rb = q4k_bytes(1, c.hidden);
         TRY(rows(y.wqkv, sh.q_head_lo * hd, qd_l, tensor_id(l, 1)));
         TRY(rows(y.wqkv + qd_l * rb, qd + sh.kv_head_lo * hd, kvd_l, tensor_id(l, 1)));
-        TRY(rows(y.wqkv + (qd_l + kvd_l) * rb, qd + kvd + sh.kv_head_lo * hd, kvd_l, tensor_id(l, 1)));
+        if (y.q6) {
+            TRY(walloc(&y.wv, kvd_l, c.hidden, true));
+            TRY(rows6(y.wv, qd + kvd + sh.kv_head_lo * hd, kvd_l, c.hidden, tensor_id(l, 1)));
+        } else {
+            TRY(rows(y.wqkv + (qd_l + kvd_l) * rb, qd + kvd + sh.kv_head_lo * hd, kvd_l, tensor_id(l, 1)));
+        }
         TRY(norm(&y.q_norm, c.head_dim, tensor_id(l, 2)));
         TRY(norm(&y.k_norm, c.head_dim, tensor_id(l, 3)));
         // o: K-shard = this rank's canonical slices = its heads' columns
@@ -190,10 +229,13 @@ static cudaError_t build(Model &m) {
         TRY(rows(y.wgate, sh.ffn_lo, ffn_l, tensor_id(l, 6)));
         TRY(walloc(&y.wup, ffn_l, c.hidden));
         TRY(rows(y.wup, sh.ffn_lo, ffn_l, tensor_id(l, 7)));
-        // down: K-shard = this rank's FFN units
-        TRY(walloc(&y.wdown, c.hidden, ffn_l));
-        TRY(launch_gen_q4k_cols(y.wdown, c.hidden, nsb_f, sh.ffn_lo / QK_K, sh.ffn_hi / QK_K, s,
-                                tensor_id(l, 8), 0, flags, st));
+        // down: K-shard = this rank's FFN units (Q6_K only unsharded)
+        TRY(walloc(&y.wdown, c.hidden, ffn_l, y.q6));
+        if (y.q6)
+            TRY(rows6(y.wdown, 0, c.hidden, c.ffn, tensor_id(l, 8)));
+        else
+            TRY(launch_gen_q4k_cols(y.wdown, c.hidden, nsb_f, sh.ffn_lo / QK_K, sh.ffn_hi / QK_K, s,
+                                    tensor_id(l, 8), 0, flags, st));
     }
     const int B = m.batch;
     const size_t kv = static_cast<size_t>(B) * c.n_layers * sh.kv_heads * c.max_ctx * c.head_dim * 2;
@@ -261,21 +303,28 @@ static cudaError_t build(Model &m) {
     return cudaStreamSynchronize(st);
 }
 
-// Local MMVQ shapes of one rank: {N, K, nmat, fused RMSNorm input}.
+// Local MMVQ shapes of one rank: {N, K, nmat, fused RMSNorm input}; qk is
+// the q|k-only fused MMVQ of a Q6_K-V layer, v its Q6_K V rows.
 struct StepShapes {
-    int64_t qkv[4], o[4], gate_up[4], down[4], out[4];
+    int64_t qkv[4], o[4], gate_up[4], down[4], out[4], qk[4], v[4];
 };
 
 static StepShapes step_shapes(const abra_model_config &c, const abra_tp_shard &sh) {
     const int64_t hd = c.head_dim;
     const int64_t qkv_l = (sh.q_heads + 2 * sh.kv_heads) * hd, qd_l = sh.q_heads * hd;
     const int64_t ffn_l = sh.ffn_hi - sh.ffn_lo, vocab_l = sh.vocab_hi - sh.vocab_lo;
+    const int64_t kvd_l = sh.kv_heads * hd;
     return {{qkv_l, c.hidden, 1, 1}, {c.hidden, qd_l, 1, 0}, {ffn_l, c.hidden, 2, 1},
-            {c.hidden, ffn_l, 1, 0}, {vocab_l, c.hidden, 1, 1}};
+            {c.hidden, ffn_l, 1, 0}, {vocab_l, c.hidden, 1, 1}, {qkv_l - kvd_l, c.hidden, 1, 1},
+            {kvd_l, c.hidden, 1, 0}};
 }
 
 static const MmvqConfig *tuned(const int64_t sh[4]) {
     return mmvq_candidate_by_id(abra_tune_get(sh[0], sh[1], 1, static_cast<int>(sh[2])));
+}
+
+static const MmvqConfig *tuned6(const int64_t sh[4]) {
+    return q6k_candidate_by_id(abra_q6k_tune_get(sh[0], sh[1], 1));
 }
 
 // The batched step (batch 32): every GEMV on the tensor cores with all
@@ -385,12 +434,19 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
     int cur = 0;
     auto fused = [&](const void *w, const void *w2, const DeltaSet &ds, const float *norm,
                      float *y, const int64_t shp[4], unsigned long long *amax,
-                     const MmvqOpts *t) -> cudaError_t {
+                     const MmvqOpts *t, uint8_t *x_out = nullptr) -> cudaError_t {
         const MmvqConfig *cfg = tuned(shp);
         if (!cfg) return cudaErrorInvalidValue;
-        MmvqXin xin = {h[cur], h[cur ^ 1], ds, norm, c.eps};
+        MmvqXin xin = {h[cur], h[cur ^ 1], ds, norm, c.eps, x_out};
         cur ^= 1;
         return launch_mmvq_q4k_xin(*cfg, w, w2, xin, y, shp[0], shp[1], pf, st, amax, t);
+    };
+    // Q6_K MMVQ (the Q4_K_M type map; unsharded)
+    auto plain6 = [&](const void *w, const void *x, float *y, const int64_t shp[4],
+                      unsigned long long *amax, const MmvqOpts *t) -> cudaError_t {
+        const MmvqConfig *cfg = tuned6(shp);
+        if (!cfg) return cudaErrorInvalidValue;
+        return launch_mmvq_q6k(*cfg, w, x, y, shp[0], shp[1], 1, shp[0], pf, st, amax, t);
     };
     auto plain = [&](const void *w, const void *x, float *y, const int64_t shp[4],
                      const MmvqOpts *t) -> cudaError_t {
@@ -403,12 +459,13 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
     // next layer's q|k|v (after the last layer: the head of this rank's output
     // rows; after the output: layer 0's q|k|v of the next token).
     const bool prefetch = (c.flags & ABRA_MODEL_NO_PREFETCH) == 0;
-    const size_t row_h = q4k_bytes(1, c.hidden);
-    auto bytes_of = [&](const int64_t shp[4]) {
-        return static_cast<int64_t>(q4k_bytes(shp[0], shp[1]));
+    const size_t row_h = m.mix ? q6k_bytes(1, c.hidden) : q4k_bytes(1, c.hidden);
+    auto bytes_of = [&](const int64_t shp[4], bool q6 = false) {
+        return static_cast<int64_t>(q6 ? q6k_bytes(shp[0], shp[1]) : q4k_bytes(shp[0], shp[1]));
     };
+    const int64_t qkv_bytes0 = L > 0 ? bytes_of(m.layers[0].q6 ? ss.qk : ss.qkv) : 0;
     const uint8_t *out_w = m.embd + static_cast<size_t>(sh.vocab_lo) * row_h;
-    const int64_t out_head = std::min<int64_t>(bytes_of(ss.out), int64_t(32) << 20) / 16 * 16;
+    const int64_t out_head = std::min<int64_t>(bytes_of(ss.out, m.mix), int64_t(32) << 20) / 16 * 16;
     auto next_of = [&](MmvqOpts &t, const void *a, int64_t na, const void *b = nullptr,
                        int64_t nb = 0) {
         if (!prefetch) return;
@@ -417,15 +474,23 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
         t.pf_ptr[1] = b;
         t.pf_bytes[1] = nb;
     };
-    TRY(launch_embed(m.embd, c.hidden, m.tokens, m.pos, h[cur], pdl, st));
+    if (m.mix)
+        TRY(launch_embed_q6k(m.embd, c.hidden, m.tokens, m.pos, h[cur], pdl, st));
+    else
+        TRY(launch_embed(m.embd, c.hidden, m.tokens, m.pos, h[cur], pdl, st));
     for (int l = 0; l < L; ++l) {
         const LayerW &y = m.layers[l];
         // residual + RMSNorm + Q8_1 fused into the q|k|v MMVQ
         MmvqOpts tq;
         if (tp && l > 0) wait_on(tq, 2 * l - 1, per_down);
         next_of(tq, y.wo, bytes_of(ss.o));
-        TRY(fused(y.wqkv, nullptr, l == 0 ? none : (tp ? slot_deltas(2 * l - 1) : one), y.attn_norm,
-                  m.qkv, ss.qkv, nullptr, &tq));
+        const DeltaSet &dq = l == 0 ? none : (tp ? slot_deltas(2 * l - 1) : one);
+        if (y.q6) {  // q|k, exporting the Q8_1 activation, then the Q6_K V rows
+            TRY(fused(y.wqkv, nullptr, dq, y.attn_norm, m.qkv, ss.qk, nullptr, &tq, m.xq));
+            TRY(plain6(y.wv, m.xq, m.qkv + ss.qk[0], ss.v, nullptr, nullptr));
+        } else {
+            TRY(fused(y.wqkv, nullptr, dq, y.attn_norm, m.qkv, ss.qkv, nullptr, &tq));
+        }
         TRY(launch_qk_norm_rope_kv(m.qkv, y.q_norm, y.k_norm, c.eps, m.rope, m.pos, m.q,
                                    m.kc + l * kv_layer, m.vc + l * kv_layer, sh.q_heads,
                                    sh.kv_heads, c.max_ctx, pdl, st));
@@ -439,25 +504,34 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
         // residual + RMSNorm + Q8_1 fused into the gate/up SwiGLU MMVQ
         MmvqOpts tg;
         if (tp) wait_on(tg, 2 * l, per_o);
-        next_of(tg, y.wdown, bytes_of(ss.down));
+        next_of(tg, y.wdown, bytes_of(ss.down, y.q6));
         TRY(fused(y.wgate, y.wup, tp ? slot_deltas(2 * l) : one, y.ffn_norm, m.act, ss.gate_up,
                   nullptr, &tg));
         TRY(launch_quantize_q8_1(m.act, m.aq, ss.gate_up[0], 1, st));
         MmvqOpts td = tp ? proto_down : MmvqOpts();
         if (tp) push_to(td, 2 * l + 1);
         if (l + 1 < L)
-            next_of(td, m.layers[l + 1].wqkv, bytes_of(ss.qkv));
+            next_of(td, m.layers[l + 1].wqkv, bytes_of(m.layers[l + 1].q6 ? ss.qk : ss.qkv));
         else
             next_of(td, out_w, out_head);
-        TRY(plain(y.wdown, m.aq, m.delta, ss.down, &td));
+        if (y.q6)
+            TRY(plain6(y.wdown, m.aq, m.delta, ss.down, nullptr, &td));
+        else
+            TRY(plain(y.wdown, m.aq, m.delta, ss.down, &td));
     }
     // final residual + RMSNorm fused into the tied output MMVQ over this
     // rank's vocab rows, which also reduces the greedy argmax (ties to the
     // lowest id); with TP every rank's keys meet in every rank's key word
     if (!tp) {
         MmvqOpts t1;
-        if (L > 0) next_of(t1, m.layers[0].wqkv, bytes_of(ss.qkv));
-        TRY(fused(m.embd, nullptr, L > 0 ? one : none, m.out_norm, m.logits, ss.out, m.amax, &t1));
+        if (L > 0) next_of(t1, m.layers[0].wqkv, qkv_bytes0);
+        if (m.mix) {  // Q6_K table: standalone residual + RMSNorm + Q8_1, then the MMVQ
+            TRY(launch_residual_rmsnorm_quant(h[cur], L > 0 ? one : none, m.out_norm, c.eps, m.xq,
+                                              c.hidden, 1, pdl, st));
+            TRY(plain6(m.embd, m.xq, m.logits, ss.out, m.amax, &t1));
+        } else {
+            TRY(fused(m.embd, nullptr, L > 0 ? one : none, m.out_norm, m.logits, ss.out, m.amax, &t1));
+        }
         return launch_argmax_finish(m.amax, m.tokens, m.picks, m.pos, m.nprompt, c.max_ctx, pdl, st);
     }
     // this rank's CTAs reduce into the local key m.amax; the last one
@@ -471,7 +545,7 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
         tout.peer_cnt[q] = m.cnt_of(m.peer[q], 2 * L);
     }
     if (L > 0) wait_on(tout, 2 * L - 1, per_down);
-    if (L > 0) next_of(tout, m.layers[0].wqkv, bytes_of(ss.qkv));
+    if (L > 0) next_of(tout, m.layers[0].wqkv, qkv_bytes0);
     TRY(fused(out_w, nullptr, L > 0 ? slot_deltas(2 * L - 1) : none, m.out_norm, m.logits, ss.out,
               m.amax, &tout));
     return launch_argmax_finish(m.key_of(m.arena), m.tokens, m.picks, m.pos, m.nprompt, c.max_ctx,
@@ -482,10 +556,17 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
 static cudaError_t prepare(const Model &m) {
     if (m.batch > 1) return prepare_mmvq_tc();
     const StepShapes ss = step_shapes(m.cfg, m.sh);
-    for (const int64_t *sh : {ss.qkv, ss.o, ss.gate_up, ss.down, ss.out}) {
+    for (const int64_t *sh : {ss.qkv, ss.o, ss.gate_up, ss.down, ss.out, ss.qk}) {
         const MmvqConfig *cfg = tuned(sh);
         if (!cfg) return cudaErrorInvalidValue;
         TRY(prepare_mmvq(*cfg, 1, static_cast<int>(sh[2]), sh[3] != 0));
+    }
+    if (m.mix) {
+        for (const int64_t *sh : {ss.v, ss.down, ss.out}) {
+            const MmvqConfig *cfg = tuned6(sh);
+            if (!cfg) return cudaErrorInvalidValue;
+            TRY(prepare_mmvq_q6k(*cfg, 1));
+        }
     }
     return cudaSuccess;
 }
@@ -574,6 +655,8 @@ static int create_model(const abra_model_config *cfg, int32_t rank, int32_t worl
         (c.n_heads * c.head_dim) % 256 || c.vocab <= 0 || c.max_ctx <= 0 || c.n_layers < 0 ||
         c.hidden > 16384)
         return model_fail(ABRA_E_UNSUPPORTED, "unsupported model configuration", cudaSuccess);
+    if ((c.flags & ABRA_MODEL_Q4_K_M) && (world > 1 || batch > 1))
+        return model_fail(ABRA_E_UNSUPPORTED, "the Q4_K_M type map runs on one GPU at batch 1", cudaSuccess);
     abra_tp_shard shard = {};
     const int src = abra::tp_shard(c, rank, world, shard);
     if (src != ABRA_OK) return model_fail(src, "no tensor-parallel split of this configuration", cudaSuccess);

@@ -37,6 +37,14 @@ class TpShard(C.Structure):
 EAGER = 1   # ABRA_MODEL_EAGER
 NO_PDL = 2  # ABRA_MODEL_NO_PDL
 NO_PREFETCH = 4  # ABRA_MODEL_NO_PREFETCH
+Q4_K_M = 8  # ABRA_MODEL_Q4_K_M: the real Qwen3-4B-Q4_K_M type map (Q6_K attn_v/ffn_down/output)
+
+
+def q6k_layers(n_layers: int) -> list[int]:
+    """Layers whose attn_v and ffn_down are Q6_K under the Q4_K_M type map
+    (llama.cpp's use_more_bits: l < n/8, l >= 7n/8 or (l - n/8) % 3 == 2)."""
+    a, b = n_layers // 8, 7 * n_layers // 8
+    return [l for l in range(n_layers) if l < a or l >= b or (l - a) % 3 == 2]
 IPC_HANDLE_BYTES = 64
 
 

@@ -394,6 +394,47 @@ def shape_table(sw: Sweep, reps: int = 3):
     return out
 
 
+Q6K_SHAPES = [("attn_v", 1024, 2560), ("ffn_down", 2560, 9728), ("output", 151936, 2560)]
+
+
+def shape_table_q6k(sw: Sweep, reps: int = 3):
+    """The real model's Q6_K tensors (abra_q6k_mmvq, tuned candidate) alone,
+    timed like shape_table: one graph over >= 4 x L2 of distinct weight copies."""
+    torch, A = sw.torch, sw.A
+    from abra_b200 import _lib
+    from abra_b200.q4k import stream_handle
+
+    out = {}
+    for name, N, K in Q6K_SHAPES:
+        per = N * K // 256 * 210
+        copies = max(8, -(-4 * L2_BYTES // per))
+        nb = N * K // 256
+        bufs = []
+        for i in range(copies):
+            t = torch.empty(nb * 210, dtype=torch.uint8, device=sw.dev)
+            A.gen_q6k(t, nb, 0, 9500 + i)
+            bufs.append(t)
+        xq, y = sw.xq[K].data_ptr(), sw.y.data_ptr()
+        fn = _lib.lib.abra_q6k_mmvq_ex
+
+        def run():
+            st = stream_handle(None)
+            for b in bufs:
+                rc = fn(b.data_ptr(), xq, y, N, K, 1, N, 0, _lib.ABRA_MMVQ_PDL, st)
+                if rc:
+                    _lib.check(rc, "abra_q6k_mmvq_ex")
+
+        g = sw.capture(run)
+        ms = min(sw.timed(1, g.replay) for _ in range(reps))
+        us = ms * 1e3 / copies
+        alg = per + K // 32 * 36 + N * 4
+        out[name] = {"N": N, "K": K, "us": round(us, 3), "GBps": round(alg / (us * 1e-6) / 1e9, 1),
+                     "copies": copies, "candidate": A.q6k_tune_get(N, K, 1)}
+        del g, bufs
+        torch.cuda.empty_cache()
+    return out
+
+
 def ref_gpu_sweep(sw: Sweep, steps: int):
     """The reference's own kernel family (oracle/_ref) on the same weights,
     unfused (q, k, v, gate, up as separate launches -- it has no fused forms),
@@ -484,7 +525,7 @@ LAUNCHES_PER_TOKEN = 1 + 36 * 8 + 2
 
 
 def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, seed: int = 0,
-                 dist=None):
+                 dist=None, flags: int = 0):
     """One decode measurement: a model sized for the prompt + depth prefix +
     warm-up + timed tokens; the prefix is fed untimed (token by token through
     the same step), then ``warmup`` untimed tokens, then ``steps`` timed
@@ -496,7 +537,8 @@ def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, se
 
     n_prompt = PROMPT + depth
     rank, world = (dist.rank, dist.world) if dist else (0, 1)
-    m = DecodeModel(rank=rank, world=world, max_ctx=n_prompt + warmup + steps, seed=seed)
+    m = DecodeModel(rank=rank, world=world, max_ctx=n_prompt + warmup + steps, seed=seed,
+                    flags=flags)
     prompt = np.random.default_rng(seed + depth).integers(0, m.cfg.vocab, n_prompt).astype(np.int32)
     m.reset(prompt)
     m.step(n_prompt - 1 + warmup)
@@ -600,9 +642,16 @@ def decode_main(a, dist):
         del sw32, ws
         torch.cuda.empty_cache()
         extras["decode_b32"] = decode_batched(torch, a.warmup, a.steps)
+        # the real Qwen3-4B-Q4_K_M type map: Q6_K attn_v/ffn_down in 18 layers
+        # and a Q6_K tied table
+        from abra_b200.model import Q4_K_M
+        r = decode_depth(torch, 0, a.warmup, a.steps, streaming=False, flags=Q4_K_M)
+        r["type_map"] = "Q4_K_M (Q6_K attn_v, ffn_down in 18 of 36 layers; Q6_K tied output)"
+        extras["decode_q4_k_m"] = r
     if dist.rank == 0 and dist.world == 1:
         if not a.no_extras:
             extras["per_shape"] = shape_table(sw)
+            extras["per_shape_q6k"] = shape_table_q6k(sw)
             r = ref_gpu_sweep(sw, 5)
             if r:
                 extras["reference_kernels_on_b200"] = r

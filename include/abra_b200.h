@@ -234,6 +234,13 @@ typedef struct {
 #define ABRA_MODEL_EAGER 1  /* launch kernels per step instead of a CUDA graph */
 #define ABRA_MODEL_NO_PDL 2 /* no programmatic dependent launch */
 #define ABRA_MODEL_NO_PREFETCH 4 /* no L2 prefetch of the next kernel's weights */
+/* The real Qwen3-4B-Q4_K_M type map instead of all-Q4_K: the tied
+ * embedding/output is Q6_K, and attn_v and ffn_down are Q6_K in layers l
+ * with l < n/8, l >= 7n/8 or (l - n/8) % 3 == 2 (layers 0-3, 6, 9, ..., 30,
+ * 31-35 of 36, the reference's census bench/results/m3/qwen3-q4k-tensor-map.json);
+ * Q6_K tensors are generated like abra_gen_q6k from the same tensor ids (V
+ * rows keep their row index in tensor 1).  One GPU, batch 1. */
+#define ABRA_MODEL_Q4_K_M 8
 
 int abra_model_default_config(abra_model_config *cfg); /* Qwen3-4B, max_ctx 4096 */
 int abra_model_create(const abra_model_config *cfg, void **model);

@@ -340,7 +340,7 @@ class OrcModelConfig(C.Structure):
                 ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("ffn", C.c_int32),
                 ("vocab", C.c_int32), ("max_ctx", C.c_int32), ("rope_theta", C.c_float),
                 ("eps", C.c_float), ("seed", C.c_uint64), ("centered", C.c_int32),
-                ("reserved", C.c_int32)]
+                ("mix", C.c_int32)]
 
 
 def _bind_model():
@@ -348,6 +348,7 @@ def _bind_model():
     sig = {
         "orc_model_default_config": (None, [C.POINTER(OrcModelConfig)]),
         "orc_tensor_id": (C.c_uint64, [C.c_int32, C.c_int32]),
+        "orc_q6k_layer": (C.c_int32, [C.c_int32, C.c_int32]),
         "orc_rope_table": (None, [_f32p, C.c_int32, C.c_int32, C.c_float]),
         "orc_model_create": (vp, [C.POINTER(OrcModelConfig)]),
         "orc_model_destroy": (None, [vp]),

@@ -1,5 +1,5 @@
 /*
- * model_oracle.c -- CPU oracle of the Qwen3-4B-shaped Q4_K decode step.
+ * model_oracle.c -- CPU oracle of the Qwen3-4B-shaped Q4_K (or Q4_K_M) decode step.
  *
  * TEST INFRASTRUCTURE ONLY (checker for tests/ and the smoke entry).  It
  * evaluates the same random-init model as abra_b200's decode runtime, every
@@ -19,18 +19,22 @@
 
 #include "model_oracle.h"
 #include "q4k_oracle.h"
+#include "q6k_oracle.h"
 
 #define Q4K_BYTES 144
 #define Q81_BYTES 36
+/* Q6K_BYTES (210) comes from q6k_oracle.h */
 #define ATT_CHUNK 256
 
 struct orc_model {
     orc_model_config cfg;
-    uint8_t *embd;  /* vocab x hidden Q4_K, tied with the output */
+    uint8_t *embd;  /* vocab x hidden Q4_K (Q6_K with the Q4_K_M map), tied with the output */
     float *out_norm;
     struct layer {
         float *attn_norm, *q_norm, *k_norm, *ffn_norm;
         uint8_t *wqkv, *wo, *wgate, *wup, *wdown;
+        uint8_t *wv6; /* Q6_K V rows (q6 layers; wqkv then holds q|k only) */
+        int q6;       /* attn_v and ffn_down in Q6_K */
     } *L;
     uint16_t *kcache, *vcache; /* [layer][kv head][ctx][head_dim] fp16 */
     float *rope;               /* [ctx][head_dim/2][2] cos, sin */
@@ -54,7 +58,12 @@ void orc_model_default_config(orc_model_config *c) {
     c->eps = 1e-6f;
     c->seed = 0;
     c->centered = 0;
-    c->reserved = 0;
+    c->mix = 0;
+}
+
+int32_t orc_q6k_layer(int32_t layer, int32_t n_layers) {
+    const int32_t a = n_layers / 8, b = 7 * n_layers / 8;
+    return layer < a || layer >= b || (layer - a) % 3 == 2;
 }
 
 uint64_t orc_tensor_id(int32_t layer, int32_t which) {
@@ -71,6 +80,20 @@ static uint8_t *gen_q4k_tensor(int64_t rows, int64_t cols, uint64_t seed, uint64
     for (int64_t b = 0; b < nb; b += chunk) {
         const int64_t n = nb - b < chunk ? nb - b : chunk;
         orc_gen_q4k_ex(p + b * Q4K_BYTES, n, seed, tid, b, flags);
+    }
+    return p;
+}
+
+/* rows [row0, row0 + rows) of a Q6_K tensor of `cols` columns */
+static uint8_t *gen_q6k_tensor(int64_t row0, int64_t rows, int64_t cols, uint64_t seed,
+                               uint64_t tid) {
+    const int64_t nsb = cols / 256, nb = rows * nsb;
+    uint8_t *p = (uint8_t *)malloc((size_t)nb * Q6K_BYTES);
+    const int64_t chunk = 1 << 16;
+#pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nb; b += chunk) {
+        const int64_t n = nb - b < chunk ? nb - b : chunk;
+        orc_gen_q6k(p + b * Q6K_BYTES, n, seed, tid, row0 * nsb + b);
     }
     return p;
 }
@@ -99,20 +122,26 @@ orc_model *orc_model_create(const orc_model_config *cfg) {
     const orc_model_config *c = &m->cfg;
     const uint64_t s = c->seed;
     const int64_t qkv_rows = (int64_t)(c->n_heads + 2 * c->n_kv_heads) * c->head_dim;
-    m->embd = gen_q4k_tensor(c->vocab, c->hidden, s, orc_tensor_id(-1, 1), c->centered);
+    const int64_t qk_rows = (int64_t)(c->n_heads + c->n_kv_heads) * c->head_dim;
+    const int64_t kvd = (int64_t)c->n_kv_heads * c->head_dim;
+    m->embd = c->mix ? gen_q6k_tensor(0, c->vocab, c->hidden, s, orc_tensor_id(-1, 1))
+                     : gen_q4k_tensor(c->vocab, c->hidden, s, orc_tensor_id(-1, 1), c->centered);
     m->out_norm = gen_norm(c->hidden, s, orc_tensor_id(-1, 2));
     m->L = calloc((size_t)c->n_layers, sizeof *m->L);
     for (int l = 0; l < c->n_layers; ++l) {
         struct layer *y = &m->L[l];
         y->attn_norm = gen_norm(c->hidden, s, orc_tensor_id(l, 0));
-        y->wqkv = gen_q4k_tensor(qkv_rows, c->hidden, s, orc_tensor_id(l, 1), c->centered);
+        y->q6 = c->mix && orc_q6k_layer(l, c->n_layers);
+        y->wqkv = gen_q4k_tensor(y->q6 ? qk_rows : qkv_rows, c->hidden, s, orc_tensor_id(l, 1), c->centered);
+        if (y->q6) y->wv6 = gen_q6k_tensor(qk_rows, kvd, c->hidden, s, orc_tensor_id(l, 1));
         y->q_norm = gen_norm(c->head_dim, s, orc_tensor_id(l, 2));
         y->k_norm = gen_norm(c->head_dim, s, orc_tensor_id(l, 3));
         y->wo = gen_q4k_tensor(c->hidden, (int64_t)c->n_heads * c->head_dim, s, orc_tensor_id(l, 4), c->centered);
         y->ffn_norm = gen_norm(c->hidden, s, orc_tensor_id(l, 5));
         y->wgate = gen_q4k_tensor(c->ffn, c->hidden, s, orc_tensor_id(l, 6), c->centered);
         y->wup = gen_q4k_tensor(c->ffn, c->hidden, s, orc_tensor_id(l, 7), c->centered);
-        y->wdown = gen_q4k_tensor(c->hidden, c->ffn, s, orc_tensor_id(l, 8), c->centered);
+        y->wdown = y->q6 ? gen_q6k_tensor(0, c->hidden, c->ffn, s, orc_tensor_id(l, 8))
+                         : gen_q4k_tensor(c->hidden, c->ffn, s, orc_tensor_id(l, 8), c->centered);
     }
     const size_t kv = (size_t)c->n_layers * c->n_kv_heads * c->max_ctx * c->head_dim;
     m->kcache = (uint16_t *)calloc(kv, 2);
@@ -140,7 +169,7 @@ void orc_model_destroy(orc_model *m) {
     for (int l = 0; l < m->cfg.n_layers; ++l) {
         struct layer *y = &m->L[l];
         free(y->attn_norm); free(y->wqkv); free(y->q_norm); free(y->k_norm); free(y->wo);
-        free(y->ffn_norm); free(y->wgate); free(y->wup); free(y->wdown);
+        free(y->ffn_norm); free(y->wgate); free(y->wup); free(y->wdown); free(y->wv6);
     }
     free(m->L); free(m->embd); free(m->out_norm); free(m->kcache); free(m->vcache);
     free(m->rope); free(m->h); free(m->delta); free(m->qkv); free(m->q); free(m->att);
@@ -285,12 +314,21 @@ int32_t orc_model_step(orc_model *m, int32_t token, int32_t pos, float *logits_o
     const int64_t qkv_rows = (int64_t)(c->n_heads + 2 * c->n_kv_heads) * hd;
     const float scale = (float)(1.0 / sqrt((double)hd));
     const int64_t kvstride = (int64_t)c->max_ctx * hd; /* per (layer, kv head) */
-    orc_dequant_q4k(m->embd + (int64_t)token * (H / 256) * Q4K_BYTES, m->h, H / 256);
+    if (c->mix)
+        orc_dequant_q6k(m->embd + (int64_t)token * (H / 256) * Q6K_BYTES, m->h, H / 256);
+    else
+        orc_dequant_q4k(m->embd + (int64_t)token * (H / 256) * Q4K_BYTES, m->h, H / 256);
     int have_delta = 0;
     for (int l = 0; l < c->n_layers; ++l) {
         struct layer *y = &m->L[l];
         orc_add_rmsnorm_quantize(m->h, have_delta ? m->delta : NULL, y->attn_norm, c->eps, m->xq, H);
-        orc_q4k_gemv(y->wqkv, m->xq, m->qkv, qkv_rows, H, 1, nthreads);
+        if (y->q6) { /* q|k Q4_K, then v Q6_K on the same Q8_1 activation */
+            const int64_t qk_rows = qkv_rows - (int64_t)c->n_kv_heads * hd;
+            orc_q4k_gemv(y->wqkv, m->xq, m->qkv, qk_rows, H, 1, nthreads);
+            orc_q6k_gemv(y->wv6, m->xq, m->qkv + qk_rows, qkv_rows - qk_rows, H, 1, nthreads);
+        } else {
+            orc_q4k_gemv(y->wqkv, m->xq, m->qkv, qkv_rows, H, 1, nthreads);
+        }
         uint16_t kt[8 * 256], vt[8 * 256];
         orc_qk_norm_rope(m->qkv, y->q_norm, y->k_norm, c->eps, m->rope + (int64_t)pos * hd,
                          c->n_heads, c->n_kv_heads, hd, m->q, kt, vt);
@@ -314,11 +352,17 @@ int32_t orc_model_step(orc_model *m, int32_t token, int32_t pos, float *logits_o
         orc_q4k_gemv(y->wup, m->xq, m->tmp + c->ffn, c->ffn, H, 1, nthreads);
         orc_swiglu(m->tmp, m->tmp + c->ffn, m->act, c->ffn);
         orc_quantize_q8_1(m->act, m->aq, c->ffn, 1);
-        orc_q4k_gemv(y->wdown, m->aq, m->delta, H, c->ffn, 1, nthreads);
+        if (y->q6)
+            orc_q6k_gemv(y->wdown, m->aq, m->delta, H, c->ffn, 1, nthreads);
+        else
+            orc_q4k_gemv(y->wdown, m->aq, m->delta, H, c->ffn, 1, nthreads);
         have_delta = 1;
     }
     orc_add_rmsnorm_quantize(m->h, have_delta ? m->delta : NULL, m->out_norm, c->eps, m->xq, H);
-    orc_q4k_gemv(m->embd, m->xq, m->logits, c->vocab, H, 1, nthreads);
+    if (c->mix)
+        orc_q6k_gemv(m->embd, m->xq, m->logits, c->vocab, H, 1, nthreads);
+    else
+        orc_q4k_gemv(m->embd, m->xq, m->logits, c->vocab, H, 1, nthreads);
     if (logits_out) memcpy(logits_out, m->logits, (size_t)c->vocab * 4);
     return orc_argmax(m->logits, c->vocab);
 }

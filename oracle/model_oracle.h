@@ -1,5 +1,5 @@
 /*
- * model_oracle.h -- CPU oracle of the Qwen3-4B-shaped Q4_K decode step.
+ * model_oracle.h -- CPU oracle of the Qwen3-4B-shaped Q4_K (or Q4_K_M) decode step.
  * TEST INFRASTRUCTURE ONLY; see model_oracle.c.
  */
 #ifndef ABRA_MODEL_ORACLE_H
@@ -16,7 +16,7 @@ typedef struct {
     float rope_theta, eps;
     uint64_t seed;
     int32_t centered; /* 1: centred Q4_K variant (orc_gen_q4k_ex flag 1) */
-    int32_t reserved;
+    int32_t mix;      /* 1: the Q4_K_M type map (orc_q6k_layer), 0: all Q4_K */
 } orc_model_config;
 
 typedef struct orc_model orc_model;
@@ -26,6 +26,14 @@ void orc_model_default_config(orc_model_config *c);
  * layer l -> 100 + 16 l + which (0 attn_norm, 1 wqkv, 2 q_norm, 3 k_norm,
  * 4 wo, 5 ffn_norm, 6 wgate, 7 wup, 8 wdown). */
 uint64_t orc_tensor_id(int32_t layer, int32_t which);
+/* Q4_K_M type map: layer l of n keeps attn_v and ffn_down in Q6_K when
+ * l < n/8, l >= 7n/8 or (l - n/8) % 3 == 2 (llama.cpp's use_more_bits; for
+ * Qwen3-4B-Q4_K_M that is layers 0-3, 6, 9, ..., 30, 31-35, the census in
+ * the reference's bench/results/m3/qwen3-q4k-tensor-map.json); the tied
+ * embedding/output is Q6_K, every other linear weight Q4_K.  With the map
+ * the V rows of layer l come from tensor 1 as Q6_K rows (same row indices)
+ * and ffn_down from tensor 8 as Q6_K. */
+int32_t orc_q6k_layer(int32_t layer, int32_t n_layers);
 void orc_rope_table(float *out, int32_t ctx, int32_t head_dim, float theta);
 
 orc_model *orc_model_create(const orc_model_config *cfg);

@@ -104,3 +104,58 @@ def test_full_qwen3_4b_shape_greedy_bit_exact(centered):
         assert len(set(picks)) > 4, "centred model should not collapse to one token"
     g.close()
     c.close()
+
+
+def _mix_pair(**cfg):
+    from abra_b200.model import Q4_K_M, DecodeModel
+
+    return DecodeModel(flags=Q4_K_M, **cfg), O.OrcModel(mix=1, **cfg)
+
+
+def test_q4_k_m_type_map_small_model_bit_exact():
+    """9 layers under the Q4_K_M type map (Q6_K attn_v/ffn_down in layers 0,
+    3, 6, 7, 8, Q6_K tied table): logits bit-identical to the oracle."""
+    cfg = dict(n_layers=9, vocab=4096, max_ctx=300, centered=1, seed=13)
+    g, c = _mix_pair(**cfg)
+    prompt = _prompt(6, 4096, 5)
+    g.reset(prompt)
+    tok = None
+    for pos in range(40):
+        feed = int(prompt[pos]) if pos < len(prompt) else tok
+        tok, want = c.step(feed, pos, logits=True)
+        g.step(1)
+        got = g.logits()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"logits differ at pos {pos}"
+    g.close()
+    c.close()
+
+
+def test_q4_k_m_graph_eager_no_pdl_no_prefetch_agree():
+    from abra_b200.model import EAGER, NO_PDL, NO_PREFETCH, Q4_K_M, DecodeModel
+
+    cfg = dict(n_layers=5, vocab=2048, max_ctx=200, centered=1, seed=17)
+    prompt = _prompt(4, 2048, 6)
+    outs = []
+    for flags in (0, EAGER, NO_PDL, NO_PREFETCH):
+        with DecodeModel(flags=flags | Q4_K_M, **cfg) as m:
+            outs.append((m.generate(prompt, 150), m.logits()))
+    for toks, lg in outs[1:]:
+        assert np.array_equal(toks, outs[0][0])
+        assert np.array_equal(lg.view(np.uint32), outs[0][1].view(np.uint32))
+
+
+def test_full_qwen3_4b_q4_k_m_greedy_bit_exact():
+    """The full 36-layer shape with the real Q4_K_M type map (18 Q6_K layers,
+    Q6_K tied 151936 x 2560 table): logits bit-identical at every step."""
+    cfg = dict(max_ctx=64, centered=1, seed=0)
+    g, c = _mix_pair(**cfg)
+    prompt = _prompt(16, 151936, 8)
+    g.reset(prompt)
+    tok = None
+    for pos in range(24):
+        feed = int(prompt[pos]) if pos < 16 else tok
+        tok, want = c.step(feed, pos, logits=True)
+        g.step(1)
+        assert np.array_equal(g.logits().view(np.uint32), want.view(np.uint32)), f"pos {pos}"
+    g.close()
+    c.close()

@@ -164,3 +164,44 @@ def test_q6k_candidates_and_tuning():
     assert A.q6k_tune_get(777, 2560, 1) == 1042
     with pytest.raises(ValueError):
         A.q6k_tune_set(777, 2560, 1, 999999)
+
+
+# Layers with Q6_K attn_v and ffn_down in Qwen3-4B-Q4_K_M, from the
+# reference's GGUF census (bench/results/m3/qwen3-q4k-tensor-map.json).
+CENSUS_Q6K_LAYERS = [0, 1, 2, 3, 6, 9, 12, 15, 18, 21, 24, 27, 30, 31, 32, 33, 34, 35]
+
+
+def test_q4_k_m_type_map_matches_the_census():
+    from abra_b200.model import q6k_layers
+
+    assert q6k_layers(36) == CENSUS_Q6K_LAYERS
+    assert [l for l in range(36) if O.lib.orc_q6k_layer(l, 36)] == CENSUS_Q6K_LAYERS
+    for n in (2, 5, 9, 16):
+        assert q6k_layers(n) == [l for l in range(n) if O.lib.orc_q6k_layer(l, n)]
+
+
+def test_q4_k_m_model_is_single_gpu_batch_1_without_gpu():
+    """Refused on the host, before any CUDA call."""
+    import ctypes as C
+
+    from abra_b200 import _lib
+    from abra_b200.model import Q4_K_M, default_config
+
+    cfg = default_config(flags=Q4_K_M)
+    h = C.c_void_p()
+    assert _lib.lib.abra_model_create_tp(C.byref(cfg), 0, 2, C.byref(h)) == _lib.ABRA_E_UNSUPPORTED
+    assert _lib.lib.abra_model_create_batched(C.byref(cfg), 32, C.byref(h)) == _lib.ABRA_E_UNSUPPORTED
+    assert b"Q4_K_M" in _lib.lib.abra_model_last_error()
+
+
+def test_oracle_q4_k_m_model_differs_from_q4k_model():
+    """A 2-layer oracle model under the type map (layer 1 Q6_K for n = 2,
+    Q6_K tied table) gives other logits than the all-Q4_K model of the same
+    seed."""
+    cfg = dict(n_layers=2, hidden=512, n_heads=4, n_kv_heads=2, ffn=1024, vocab=300, max_ctx=8, seed=1)
+    a, b = O.OrcModel(**cfg), O.OrcModel(mix=1, **cfg)
+    _, la = a.step(5, 0, logits=True)
+    _, lb = b.step(5, 0, logits=True)
+    assert np.isfinite(lb).all() and not np.array_equal(la, lb)
+    a.close()
+    b.close()
