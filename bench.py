@@ -483,6 +483,8 @@ def run_case(a):
 
     table = {n: (N, K, 1) for n, N, K in CONFIG1_SHAPES}
     table.update({"qkv": (6144, 2560, 1), "gate_up": (9728, 2560, 2)})
+    if a.case.startswith("q6k_"):
+        return run_case_q6k(a)
     N, K, nmat = table[a.case]
     dev = torch.device("cuda:0")
     nb = N * K // 256
@@ -513,6 +515,51 @@ def run_case(a):
                       "GBps_eager": round(alg_bytes(N, K, a.batch, nmat) / (us * 1e-6) / 1e9, 1),
                       "candidate": A.get_autotuned_candidate_for_shape(N, K, ncols=a.batch,
                                                                        nmat=nmat),
+                      "device_error": A.device_error()}), flush=True)
+    return 0
+
+
+def run_case_q6k(a):
+    """Profiling case for a Q6_K tensor of the real model (q6k_<name> of
+    Q6K_SHAPES): ``--copies`` weight copies, eager tuned launches."""
+    import torch
+
+    import abra_b200 as A
+    import oracle as O
+
+    N, K = {f"q6k_{n}": (N, K) for n, N, K in Q6K_SHAPES}[a.case]
+    dev = torch.device("cuda:0")
+    nb = N * K // 256
+    bufs = []
+    for i in range(a.copies):
+        t = torch.empty(nb * 210, dtype=torch.uint8, device=dev)
+        A.gen_q6k(t, nb, 0, 700 + i)
+        bufs.append(t)
+    xq = torch.empty(a.batch * (K // 32) * 36, dtype=torch.uint8, device=dev)
+    A.launch_quantize_f32_to_q8_1(
+        torch.from_numpy(O.gen_normal_f32((a.batch, K), 1).reshape(-1)).to(dev), xq, K,
+        ncols=a.batch)
+    y = torch.empty(a.batch * N, dtype=torch.float32, device=dev)
+
+    def run():
+        for b in bufs:
+            A.mmvq_q6k(b, xq, y, N, K, ncols=a.batch, pdl=True)
+
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(a.steps):
+        run()
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1e3 / (a.steps * len(bufs))
+    alg = N * K // 256 * 210 + a.batch * (K // 32 * 36 + N * 4)
+    print(json.dumps({"case": a.case, "N": N, "K": K, "batch": a.batch, "copies": a.copies,
+                      "us_per_launch_eager": round(us, 3),
+                      "GBps_eager": round(alg / (us * 1e-6) / 1e9, 1),
+                      "candidate": A.q6k_tune_get(N, K, a.batch),
                       "device_error": A.device_error()}), flush=True)
     return 0
 
@@ -753,7 +800,8 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the per-shape table and the reference kernel family")
     ap.add_argument("--quick", action="store_true", help="decode: depth 0 only")
-    ap.add_argument("--case", choices=[n for n, _, _ in CONFIG1_SHAPES] + ["qkv", "gate_up"],
+    ap.add_argument("--case", choices=[n for n, _, _ in CONFIG1_SHAPES] + ["qkv", "gate_up"]
+                    + [f"q6k_{n}" for n, _, _ in Q6K_SHAPES],
                     help="profiling mode: one operator, eager launches")
     ap.add_argument("--copies", type=int, default=2, help="weight copies in --case mode")
     a = ap.parse_args()
