@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple] = {
     "abra_model_create_tp": (C.c_int, [_vp, _i32, _i32, C.POINTER(C.c_void_p)]),
     "abra_model_tp_handle": (C.c_int, [_vp, _vp, _i32]),
     "abra_model_tp_connect": (C.c_int, [_vp, _vp, _i32]),
+    "abra_model_load_tensor": (C.c_int, [_vp, _i32, _i32, _i32, _vp, C.c_uint64]),
 }
 
 

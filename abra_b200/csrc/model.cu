@@ -874,6 +874,106 @@ int abra_model_decode_streaming(void *model, int32_t n, int32_t *out) {
     return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "streaming decode", e);
 }
 
+// One tensor of a GGUF file (ggml layout: rows of K/256 blocks, row-major)
+// into the model's buffers: whole tensors on one GPU; on a tensor-parallel
+// rank, its rows (q, k, v, gate, up) or its canonical K-slices of every row
+// (o, down).  The tied table is whole on every rank.
+int abra_model_load_tensor(void *model, int32_t layer, int32_t slot, int32_t ggml_type,
+                           const void *host, uint64_t bytes) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || !host) return model_fail(ABRA_E_INVALID, "null pointer", cudaSuccess);
+    if (m->batch > 1) return model_fail(ABRA_E_UNSUPPORTED, "load into a batch-1 model", cudaSuccess);
+    const abra_model_config &c = m->cfg;
+    const abra_tp_shard &sh = m->sh;
+    const int64_t hd = c.head_dim, qd = static_cast<int64_t>(c.n_heads) * hd;
+    const int64_t kvd = static_cast<int64_t>(c.n_kv_heads) * hd;
+    const int64_t qd_l = sh.q_heads * hd, kvd_l = sh.kv_heads * hd;
+    const int64_t nsb_o = qd / abra::QK_K, nsb_f = c.ffn / abra::QK_K;
+    const int64_t row_h = static_cast<int64_t>(abra::q4k_bytes(1, c.hidden));
+    // the destination: dst <- rows [r0, r0 + nr) of an N x K tensor of type t
+    // (row bytes rb), each row's bytes [b0, b0 + nb) (nb == rb: whole rows)
+    void *dst = nullptr;
+    int want_type = ABRA_GGML_Q4_K;
+    int64_t N = 0, K = 0, r0 = 0, nr = 0, b0 = 0, nb = 0, rb = 0;
+    auto block = [&](int type) { return type == ABRA_GGML_Q6_K ? 210 : abra::Q4K_BYTES; };
+    auto rows = [&](void *d, int type, int64_t n, int64_t k, int64_t lo, int64_t cnt) {
+        dst = d;
+        want_type = type;
+        N = n;
+        K = k;
+        rb = k / abra::QK_K * block(type);
+        r0 = lo;
+        nr = cnt;
+        b0 = 0;
+        nb = rb;
+    };
+    auto f32 = [&](float *d, int64_t n) {
+        dst = d;
+        want_type = ABRA_GGML_F32;
+        N = 1;
+        K = n;
+        rb = nb = n * 4;
+        r0 = b0 = 0;
+        nr = 1;
+    };
+    const bool in_layer = layer >= 0 && layer < c.n_layers;
+    if (layer == -1 && slot == ABRA_TENSOR_TOKEN_EMBD) {
+        rows(m->embd, m->mix ? ABRA_GGML_Q6_K : ABRA_GGML_Q4_K, c.vocab, c.hidden, 0, c.vocab);
+    } else if (layer == -1 && slot == ABRA_TENSOR_OUTPUT_NORM) {
+        f32(m->out_norm, c.hidden);
+    } else if (in_layer) {
+        abra::LayerW &y = m->layers[layer];
+        switch (slot) {
+            case ABRA_TENSOR_ATTN_NORM: f32(y.attn_norm, c.hidden); break;
+            case ABRA_TENSOR_FFN_NORM: f32(y.ffn_norm, c.hidden); break;
+            case ABRA_TENSOR_ATTN_Q_NORM: f32(y.q_norm, hd); break;
+            case ABRA_TENSOR_ATTN_K_NORM: f32(y.k_norm, hd); break;
+            case ABRA_TENSOR_ATTN_Q:
+                rows(y.wqkv, ABRA_GGML_Q4_K, qd, c.hidden, sh.q_head_lo * hd, qd_l);
+                break;
+            case ABRA_TENSOR_ATTN_K:
+                rows(y.wqkv + qd_l * row_h, ABRA_GGML_Q4_K, kvd, c.hidden, sh.kv_head_lo * hd, kvd_l);
+                break;
+            case ABRA_TENSOR_ATTN_V:
+                if (y.q6)
+                    rows(y.wv, ABRA_GGML_Q6_K, kvd, c.hidden, sh.kv_head_lo * hd, kvd_l);
+                else
+                    rows(y.wqkv + (qd_l + kvd_l) * row_h, ABRA_GGML_Q4_K, kvd, c.hidden,
+                         sh.kv_head_lo * hd, kvd_l);
+                break;
+            case ABRA_TENSOR_ATTN_OUTPUT:  // this rank's canonical K-slices of every row
+                rows(y.wo, ABRA_GGML_Q4_K, c.hidden, qd, 0, c.hidden);
+                b0 = abra::slice_start(static_cast<int>(nsb_o), sh.sl_base) * abra::Q4K_BYTES;
+                nb = abra::slice_start(static_cast<int>(nsb_o), sh.sl_base + sh.sl_cnt) * abra::Q4K_BYTES - b0;
+                break;
+            case ABRA_TENSOR_FFN_GATE:
+            case ABRA_TENSOR_FFN_UP:
+                rows(slot == ABRA_TENSOR_FFN_GATE ? y.wgate : y.wup, ABRA_GGML_Q4_K, c.ffn, c.hidden,
+                     sh.ffn_lo, sh.ffn_hi - sh.ffn_lo);
+                break;
+            case ABRA_TENSOR_FFN_DOWN: {
+                const int t = y.q6 ? ABRA_GGML_Q6_K : ABRA_GGML_Q4_K;
+                rows(y.wdown, t, c.hidden, c.ffn, 0, c.hidden);
+                b0 = sh.ffn_lo / abra::QK_K * block(t);
+                nb = (sh.ffn_hi - sh.ffn_lo) / abra::QK_K * block(t);
+                (void)nsb_f;
+                break;
+            }
+            default: return model_fail(ABRA_E_INVALID, "unknown tensor slot", cudaSuccess);
+        }
+    } else {
+        return model_fail(ABRA_E_INVALID, "unknown tensor (layer, slot)", cudaSuccess);
+    }
+    if (ggml_type != want_type)
+        return model_fail(ABRA_E_INVALID, "tensor type differs from the model's type for this slot", cudaSuccess);
+    if (bytes != static_cast<uint64_t>(N * rb))
+        return model_fail(ABRA_E_INVALID, "tensor size differs from the model's shape", cudaSuccess);
+    const uint8_t *src = static_cast<const uint8_t *>(host) + r0 * rb + b0;
+    cudaError_t e = cudaMemcpy2DAsync(dst, nb, src, rb, nb, nr, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "tensor upload", e);
+}
+
 int abra_model_info(void *model, void **stream, uint64_t *weight_bytes, uint64_t *kv_bytes) {
     Model *m = static_cast<Model *>(model);
     if (!m) return ABRA_E_INVALID;

@@ -156,6 +156,25 @@ class DecodeModel:
     must make the same calls in the same order.
     """
 
+    @classmethod
+    def from_gguf(cls, path, rank: int = 0, world: int = 1, group=None, max_ctx: int = 4096,
+                  flags: int = 0) -> "DecodeModel":
+        """A model whose shape, type map and weights come from a Qwen3 GGUF
+        file (abra_b200.gguf): created seeded, then every tensor copied in."""
+        from . import gguf
+
+        with gguf.read_gguf(path) as g:
+            cfg = gguf.model_config(g)
+            tflags = gguf.type_flags(g, cfg["n_layers"])
+            m = cls(rank=rank, world=world, group=group, max_ctx=max_ctx,
+                    flags=flags | tflags, **cfg)
+            try:
+                gguf.load_into(m, g)
+            except Exception:
+                m.close()
+                raise
+        return m
+
     def __init__(self, rank: int = 0, world: int = 1, group=None, **config):
         self.handle = None
         self.cfg = default_config(**config)

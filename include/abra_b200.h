@@ -267,6 +267,36 @@ int abra_model_generate(void *model, const int32_t *prompt, int32_t n_prompt, in
  * back and wait for it (the host sees every token as it is produced). */
 int abra_model_decode_streaming(void *model, int32_t n, int32_t *out);
 int abra_model_info(void *model, void **stream, uint64_t *weight_bytes, uint64_t *kv_bytes);
+
+/* Weights from a GGUF file.  Slots of layer -1: token_embd (1, tied with
+ * the output), output_norm (2); of layer l: the GGUF names blk.l.<name>. */
+#define ABRA_TENSOR_ATTN_NORM 0
+#define ABRA_TENSOR_ATTN_Q 1
+#define ABRA_TENSOR_ATTN_Q_NORM 2
+#define ABRA_TENSOR_ATTN_K_NORM 3
+#define ABRA_TENSOR_ATTN_OUTPUT 4
+#define ABRA_TENSOR_FFN_NORM 5
+#define ABRA_TENSOR_FFN_GATE 6
+#define ABRA_TENSOR_FFN_UP 7
+#define ABRA_TENSOR_FFN_DOWN 8
+#define ABRA_TENSOR_ATTN_K 9
+#define ABRA_TENSOR_ATTN_V 10
+#define ABRA_TENSOR_TOKEN_EMBD 1  /* layer -1 */
+#define ABRA_TENSOR_OUTPUT_NORM 2 /* layer -1 */
+/* ggml tensor types a slot can hold */
+#define ABRA_GGML_F32 0
+#define ABRA_GGML_Q4_K 12
+#define ABRA_GGML_Q6_K 14
+/* Copy one tensor's data, as stored in a GGUF file (ggml layout: N rows of
+ * K/256 blocks for a [K, N] weight; fp32 vectors for norms), from host
+ * memory into the model, overwriting the seeded weights.  ggml_type and
+ * bytes must match the model's slot exactly (whole, unsharded tensor); a
+ * tensor-parallel rank keeps its own rows or canonical K-slices.  The
+ * reference reads these files through llama.cpp; its census of the real
+ * Qwen3-4B-Q4_K_M tensors is bench/results/m3/qwen3-q4k-tensor-map.json
+ * (parser: tools/extract-qwen3-tensor-map.py:15-141).  Batch-1 models. */
+int abra_model_load_tensor(void *model, int32_t layer, int32_t slot, int32_t ggml_type,
+                           const void *host, uint64_t bytes);
 const char *abra_model_last_error(void);
 
 /* ------------------------------------------------- batched decode --- */
