@@ -61,6 +61,7 @@ SIGNATURES: dict[str, tuple] = {
     "abra_model_destroy": (C.c_int, [_vp]),
     "abra_model_reset": (C.c_int, [_vp, _vp, _i32]),
     "abra_model_step": (C.c_int, [_vp, _i32]),
+    "abra_model_prefill": (C.c_int, [_vp, _i32]),
     "abra_model_sync": (C.c_int, [_vp]),
     "abra_model_invalidate": (C.c_int, [_vp]),
     "abra_model_read": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),

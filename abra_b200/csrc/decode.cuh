@@ -11,6 +11,10 @@ namespace abra {
 struct SeqStrides {
     int batch = 1;
     int64_t qkv = 0, q = 0, kv = 0;
+    // position step per sequence: 0 when every sequence is at *pos (batched
+    // decode), 1 for a prefill chunk, whose column b is the token at *pos + b
+    // of one sequence (kv = 0: the columns share one cache)
+    int pos = 0;
 };
 
 cudaError_t launch_embed(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
@@ -45,6 +49,8 @@ cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t
                                 int32_t *picks, int64_t tok_stride, int32_t *pos,
                                 const int32_t *n_prompt, int max_ctx, int batch, bool pdl,
                                 cudaStream_t s);
+// *pos = min(*pos + n, max_ctx).
+cudaError_t launch_pos_advance(int32_t *pos, int n, int max_ctx, bool pdl, cudaStream_t s);
 // y = Q8_1 of up * silu(gate), n values (a multiple of 32).
 cudaError_t launch_swiglu_quant(const float *g, const float *u, void *y, int64_t n, bool pdl,
                                 cudaStream_t s);

@@ -135,14 +135,16 @@ __global__ void __launch_bounds__(RES_THREADS)
 // (i, i+64) with the host cos/sin table row of this position.  q stays fp32;
 // k and v are stored fp16 at kv[head][pos][128].
 // Sequence blockIdx.y of a batch: qkv, q_out and the KV cache advance by
-// their per-sequence strides.
+// their per-sequence strides, the position by pos_stride (a prefill chunk:
+// column b is position *pos + b of one cache).
 __global__ void __launch_bounds__(256)
     qk_norm_rope_kv_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
                            const float *__restrict__ k_norm, float eps,
                            const float *__restrict__ rope, const int32_t *__restrict__ pos_p,
                            float *__restrict__ q_out, __half *__restrict__ kc,
                            __half *__restrict__ vc, int n_heads, int n_kv, int max_ctx,
-                           int64_t qkv_stride, int64_t q_stride, int64_t kv_stride) {
+                           int64_t qkv_stride, int64_t q_stride, int64_t kv_stride,
+                           int pos_stride) {
     pdl_wait();
     pdl_launch_dependents();
     qkv += blockIdx.y * qkv_stride;
@@ -152,7 +154,7 @@ __global__ void __launch_bounds__(256)
     const int lane = threadIdx.x & 31;
     const int hw = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (hw >= n_heads + 2 * n_kv) return;
-    const int pos = *pos_p;
+    const int pos = *pos_p + static_cast<int>(blockIdx.y) * pos_stride;
     if (pos >= max_ctx) return;  // the host never steps past max_ctx; no write out of range
     const float4 xv = *reinterpret_cast<const float4 *>(qkv + static_cast<int64_t>(hw) * 128 + 4 * lane);
     const float x[4] = {xv.x, xv.y, xv.z, xv.w};
@@ -213,7 +215,8 @@ __global__ void __launch_bounds__(256)
                            const __half *__restrict__ vc, const int32_t *__restrict__ pos_p,
                            float scale, int max_ctx, int max_chunks,
                            float *__restrict__ part_m, float *__restrict__ part_l,
-                           float *__restrict__ part_o, int64_t q_stride, int64_t kv_stride) {
+                           float *__restrict__ part_o, int64_t q_stride, int64_t kv_stride,
+                           int pos_stride) {
     {
         const int64_t z = blockIdx.z;
         const int64_t pstride = static_cast<int64_t>(gridDim.x) * GQ * max_chunks;
@@ -230,7 +233,7 @@ __global__ void __launch_bounds__(256)
     __shared__ __align__(16) float s_o[8][GQ][128];
     pdl_wait();
     pdl_launch_dependents();
-    const int L = min(*pos_p + 1, max_ctx);
+    const int L = min(*pos_p + static_cast<int>(blockIdx.z) * pos_stride + 1, max_ctx);
     const int c = blockIdx.y, g = blockIdx.x;
     if (c * ATT_CHUNK >= L) return;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -351,7 +354,8 @@ __global__ void __launch_bounds__(256)
                                  const float *__restrict__ part_l,
                                  const float *__restrict__ part_o,
                                  const int32_t *__restrict__ pos_p, int n_heads, int max_chunks,
-                                 float *__restrict__ out_f32, block_q8_1 *__restrict__ out_q8) {
+                                 float *__restrict__ out_f32, block_q8_1 *__restrict__ out_q8,
+                                 int pos_stride) {
     pdl_wait();
     pdl_launch_dependents();
     {  // sequence blockIdx.y of a batch
@@ -365,7 +369,7 @@ __global__ void __launch_bounds__(256)
     const int lane = threadIdx.x & 31;
     const int hq = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (hq >= n_heads) return;
-    const int L = min(*pos_p + 1, max_chunks * ATT_CHUNK);
+    const int L = min(*pos_p + static_cast<int>(blockIdx.y) * pos_stride + 1, max_chunks * ATT_CHUNK);
     const int nch = (L + ATT_CHUNK - 1) / ATT_CHUNK;
     const float *pm = part_m + static_cast<int64_t>(hq) * max_chunks;
     const float *pl = part_l + static_cast<int64_t>(hq) * max_chunks;
@@ -497,10 +501,10 @@ __global__ void __launch_bounds__(1024)
     }
 }
 
-__global__ void pos_advance_kernel(int32_t *__restrict__ pos_p, int max_ctx) {
+__global__ void pos_advance_kernel(int32_t *__restrict__ pos_p, int n, int max_ctx) {
     pdl_wait();
     pdl_launch_dependents();
-    if (threadIdx.x == 0 && *pos_p < max_ctx) *pos_p += 1;
+    if (threadIdx.x == 0) *pos_p = min(*pos_p + n, max_ctx);
 }
 
 // act = up * silu(gate) (the fused gate/up MMVQ's epilogue, elementwise),
@@ -572,7 +576,7 @@ cudaError_t launch_qk_norm_rope_kv(const float *qkv, const float *q_norm, const 
     const int heads = n_heads + 2 * n_kv;
     return launch_pdl(qk_norm_rope_kv_kernel, dim3((heads + 7) / 8, b.batch), dim3(256), 0, s, pdl,
                       qkv, q_norm, k_norm, eps, rope, pos, q_out, static_cast<__half *>(kc),
-                      static_cast<__half *>(vc), n_heads, n_kv, max_ctx, b.qkv, b.q, b.kv);
+                      static_cast<__half *>(vc), n_heads, n_kv, max_ctx, b.qkv, b.q, b.kv, b.pos);
 }
 
 cudaError_t launch_attention(const float *q, const void *kc, const void *vc, const int32_t *pos,
@@ -588,7 +592,7 @@ cudaError_t launch_attention(const float *q, const void *kc, const void *vc, con
     cudaError_t e;
 #define ABRA_ATT(G)                                                                                  \
     launch_pdl(attention_chunk_kernel<G>, grid, dim3(256), 0, s, pdl, q, k, v, pos, scale, max_ctx, \
-               max_chunks, part_m, part_l, part_o, b.q, b.kv)
+               max_chunks, part_m, part_l, part_o, b.q, b.kv, b.pos)
     switch (gq) {
         case 1: e = ABRA_ATT(1); break;
         case 2: e = ABRA_ATT(2); break;
@@ -601,7 +605,7 @@ cudaError_t launch_attention(const float *q, const void *kc, const void *vc, con
     return launch_pdl(attention_merge_quant_kernel, dim3((n_heads + 7) / 8, b.batch), dim3(256), 0, s,
                       pdl, static_cast<const float *>(part_m), static_cast<const float *>(part_l),
                       static_cast<const float *>(part_o), pos, n_heads, max_chunks, out_f32,
-                      static_cast<block_q8_1 *>(out_q8));
+                      static_cast<block_q8_1 *>(out_q8), b.pos);
 }
 
 cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t *tokens,
@@ -612,7 +616,11 @@ cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t
                                ldl, tokens, picks, tok_stride, static_cast<const int32_t *>(pos),
                                n_prompt, max_ctx);
     if (e != cudaSuccess) return e;
-    return launch_pdl(pos_advance_kernel, dim3(1), dim3(32), 0, s, pdl, pos, max_ctx);
+    return launch_pdl(pos_advance_kernel, dim3(1), dim3(32), 0, s, pdl, pos, 1, max_ctx);
+}
+
+cudaError_t launch_pos_advance(int32_t *pos, int n, int max_ctx, bool pdl, cudaStream_t s) {
+    return launch_pdl(pos_advance_kernel, dim3(1), dim3(32), 0, s, pdl, pos, n, max_ctx);
 }
 
 cudaError_t launch_swiglu_quant(const float *g, const float *u, void *y, int64_t n, bool pdl,

@@ -119,6 +119,14 @@ struct Model {
     int max_chunks = 0;
     cudaStream_t stream = nullptr;
     cudaGraphExec_t graph = nullptr;
+    // prefill (batch-1 model): up to kPrefillMax prompt tokens of one
+    // sequence per step as the columns of the tensor-core GEMVs; buffers
+    // allocated on first use, one graph per chunk size (a multiple of 32)
+    float *ph = nullptr, *pdelta = nullptr, *pqkv = nullptr, *pq = nullptr, *pg = nullptr, *pu = nullptr;
+    float *ppart_m = nullptr, *ppart_l = nullptr, *ppart_o = nullptr, *pws = nullptr;
+    uint8_t *pxq = nullptr, *poq = nullptr, *paq = nullptr;
+    cudaGraphExec_t pgraph[8] = {};  // chunk size 32 (i + 1)
+    int32_t host_nprompt = 0;
     size_t weight_bytes = 0, kv_bytes = 0;
     int32_t host_pos = 0;      // position after the queued steps (mirrors *pos)
     int32_t *pinned = nullptr; // 2 pinned ints for the streaming loop
@@ -376,6 +384,89 @@ static cudaError_t record_step_batched(const Model &m, cudaStream_t st) {
     TRY(tc(m.embd, m.xq, m.logits, c.vocab, c.hidden, 1));
     return launch_argmax_batch(m.logits, c.vocab, c.vocab, m.tokens, m.picks, tok_stride, m.pos,
                                m.nprompt, c.max_ctx, B, pdl, st);
+}
+
+// Prefill: the P prompt tokens at tokens[*pos .. *pos + P) of the batch-1
+// model as P columns -- every GEMV on the tensor cores (32 columns per
+// launch), RoPE, the KV append and attention with column b at position
+// *pos + b of the model's one KV cache (causal: column b attends to positions
+// <= *pos + b, all written by the same RoPE/KV launch before the attention
+// launch).  Per column the arithmetic is the decode step's, kernel for
+// kernel, so the cache holds the bits token-by-token decoding writes.  No
+// logits: the last prompt token goes through the decode step.
+constexpr int kPrefillMax = 256;
+
+static cudaError_t record_prefill(const Model &m, int P, cudaStream_t st) {
+    const abra_model_config &c = m.cfg;
+    const int L = c.n_layers;
+    const bool pdl = (c.flags & ABRA_MODEL_NO_PDL) == 0;
+    const int pf = pdl ? MMVQ_PDL : 0;
+    const int64_t hd = c.head_dim, qd = c.n_heads * hd;
+    const int64_t qkv_rows = (c.n_heads + 2 * c.n_kv_heads) * hd;
+    const size_t kv_layer = static_cast<size_t>(c.n_kv_heads) * c.max_ctx * c.head_dim;
+    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
+    SeqStrides sb;
+    sb.batch = P;
+    sb.qkv = qkv_rows;
+    sb.q = qd;
+    sb.kv = 0;
+    sb.pos = 1;
+    DeltaSet none = {}, one = {};
+    one.p[0] = m.pdelta;
+    one.G = 1;
+    // y[c][n] = W x[c] for the P columns, 32 at a time
+    auto tc = [&](const void *w, const uint8_t *x, float *y, int64_t N, int64_t K, int ks) -> cudaError_t {
+        const int64_t xcol = K / QK8_1 * Q81_BYTES;
+        for (int t = 0; t < P / 32; ++t)
+            TRY(launch_mmvq_tc(w, x + t * 32 * xcol, y + t * 32 * N, N, K, N, ks, m.pws, pf, st));
+        return cudaSuccess;
+    };
+    TRY(launch_embed(m.embd, c.hidden, m.tokens, m.pos, m.ph, pdl, st, P, 1));
+    for (int l = 0; l < L; ++l) {
+        const LayerW &y = m.layers[l];
+        TRY(launch_residual_rmsnorm_quant(m.ph, l == 0 ? none : one, y.attn_norm, c.eps, m.pxq, c.hidden,
+                                          P, pdl, st));
+        TRY(tc(y.wqkv, m.pxq, m.pqkv, qkv_rows, c.hidden, 2));
+        TRY(launch_qk_norm_rope_kv(m.pqkv, y.q_norm, y.k_norm, c.eps, m.rope, m.pos, m.pq,
+                                   m.kc + l * kv_layer, m.vc + l * kv_layer, c.n_heads, c.n_kv_heads,
+                                   c.max_ctx, pdl, st, sb));
+        TRY(launch_attention(m.pq, m.kc + l * kv_layer, m.vc + l * kv_layer, m.pos, scale, c.n_heads,
+                             c.n_kv_heads, c.max_ctx, m.ppart_m, m.ppart_l, m.ppart_o, nullptr, m.poq,
+                             pdl, st, sb));
+        TRY(tc(y.wo, m.poq, m.pdelta, c.hidden, qd, 8));
+        TRY(launch_residual_rmsnorm_quant(m.ph, one, y.ffn_norm, c.eps, m.pxq, c.hidden, P, pdl, st));
+        TRY(tc(y.wgate, m.pxq, m.pg, c.ffn, c.hidden, 2));
+        TRY(tc(y.wup, m.pxq, m.pu, c.ffn, c.hidden, 2));
+        TRY(launch_swiglu_quant(m.pg, m.pu, m.paq, static_cast<int64_t>(P) * c.ffn, pdl, st));
+        TRY(tc(y.wdown, m.paq, m.pdelta, c.hidden, c.ffn, 8));
+    }
+    return launch_pos_advance(m.pos, P, c.max_ctx, pdl, st);
+}
+
+static cudaError_t prefill_buffers(Model &m) {
+    if (m.ph) return cudaSuccess;
+    const abra_model_config &c = m.cfg;
+    const int64_t P = kPrefillMax, hd = c.head_dim, qd = c.n_heads * hd;
+    const int64_t qkv_rows = (c.n_heads + 2 * c.n_kv_heads) * hd;
+    int64_t mx = c.hidden > c.ffn ? c.hidden : c.ffn;
+    if (qd > mx) mx = qd;
+    TRY(alloc(m, &m.ph, P * c.hidden * 4));
+    TRY(alloc(m, &m.pdelta, P * c.hidden * 4));
+    TRY(alloc(m, &m.pqkv, P * qkv_rows * 4));
+    TRY(alloc(m, &m.pq, P * qd * 4));
+    TRY(alloc(m, &m.pg, P * c.ffn * 4));
+    TRY(alloc(m, &m.pu, P * c.ffn * 4));
+    TRY(alloc(m, &m.ppart_m, P * c.n_heads * m.max_chunks * 4));
+    TRY(alloc(m, &m.ppart_l, P * c.n_heads * m.max_chunks * 4));
+    TRY(alloc(m, &m.ppart_o, P * c.n_heads * m.max_chunks * c.head_dim * 4));
+    TRY(alloc(m, &m.pxq, P * (mx / QK8_1) * Q81_BYTES));
+    TRY(alloc(m, &m.poq, P * (qd / QK8_1) * Q81_BYTES));
+    TRY(alloc(m, &m.paq, P * (c.ffn / QK8_1) * Q81_BYTES));
+    int64_t ws = 8 * c.hidden;  // k-parts x rows of the K-split launches
+    if (2 * c.ffn > ws) ws = 2 * c.ffn;
+    if (2 * qkv_rows > ws) ws = 2 * qkv_rows;
+    TRY(alloc(m, &m.pws, 32 * ws * 4));
+    return prepare_mmvq_tc();
 }
 
 // The decode step for the token at tokens[*pos] (recorded into the graph).
@@ -682,6 +773,8 @@ int abra_model_destroy(void *model) {
     if (!m) return ABRA_OK;
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    for (cudaGraphExec_t g : m->pgraph)
+        if (g) cudaGraphExecDestroy(g);
     if (m->pinned) cudaFreeHost(m->pinned);
     for (int q = 0; q < m->sh.world; ++q)
         if (m->peer[q] && m->peer[q] != m->arena) cudaIpcCloseMemHandle(m->peer[q]);
@@ -773,8 +866,43 @@ int abra_model_reset(void *model, const int32_t *prompt, int32_t n_prompt) {
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, &zero, 4, cudaMemcpyHostToDevice, m->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->nprompt, &n_prompt, 4, cudaMemcpyHostToDevice, m->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
-    if (e == cudaSuccess) m->host_pos = 0;
+    if (e == cudaSuccess) {
+        m->host_pos = 0;
+        m->host_nprompt = n_prompt;
+    }
     return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "reset", e);
+}
+
+int abra_model_prefill(void *model, int32_t n_tokens) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || n_tokens < 0 || n_tokens % 32)
+        return model_fail(ABRA_E_INVALID, "n_tokens must be a multiple of 32", cudaSuccess);
+    if (m->batch > 1 || m->sh.world > 1 || m->mix)
+        return model_fail(ABRA_E_UNSUPPORTED, "prefill runs on a one-GPU batch-1 all-Q4_K model", cudaSuccess);
+    if (static_cast<int64_t>(m->host_pos) + n_tokens > static_cast<int64_t>(m->host_nprompt) - 1)
+        return model_fail(ABRA_E_INVALID, "prefill must leave the last prompt token to a decode step", cudaSuccess);
+    cudaError_t e = abra::prefill_buffers(*m);
+    if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "prefill buffers", e);
+    for (int done = 0; done < n_tokens;) {
+        const int P = std::min(n_tokens - done, abra::kPrefillMax);
+        cudaGraphExec_t &g = m->pgraph[P / 32 - 1];
+        if (!g && !(m->cfg.flags & ABRA_MODEL_EAGER)) {
+            cudaGraph_t gr = nullptr;
+            e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+            if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "prefill capture", e);
+            const cudaError_t e1 = abra::record_prefill(*m, P, m->stream);
+            e = cudaStreamEndCapture(m->stream, &gr);
+            if (e1 == cudaSuccess && e == cudaSuccess) e = cudaGraphInstantiate(&g, gr, 0);
+            if (gr) cudaGraphDestroy(gr);
+            if (e1 != cudaSuccess) e = e1;
+            if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "prefill capture", e);
+        }
+        e = g ? cudaGraphLaunch(g, m->stream) : abra::record_prefill(*m, P, m->stream);
+        if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "prefill launch", e);
+        m->host_pos += P;
+        done += P;
+    }
+    return ABRA_OK;
 }
 
 int abra_model_step(void *model, int32_t n_steps) {

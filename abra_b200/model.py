@@ -221,6 +221,23 @@ class DecodeModel:
         """Queue n decode steps on the model's stream (asynchronous)."""
         _check(_lib.lib.abra_model_step(self.handle, n), "abra_model_step")
 
+    def prefill(self, n: int) -> None:
+        """Process the next n prompt tokens (a multiple of 32) as tensor-core
+        GEMV columns, chunks of up to 256 (asynchronous): the KV cache ends
+        up as after n decode steps; the last prompt token is left to step()."""
+        _check(_lib.lib.abra_model_prefill(self.handle, n), "abra_model_prefill")
+
+    def feed_prompt(self, prompt) -> None:
+        """reset(prompt), then prefill every whole 32-token tile of the
+        first len(prompt) - 1 tokens and step through the rest; afterwards the
+        model has picked the first generated token."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        self.reset(p)
+        n = (p.size - 1) // 32 * 32
+        if n:
+            self.prefill(n)
+        self.step(p.size - n)
+
     def invalidate(self) -> None:
         """Drop the recorded step; the next step records it again (picks up
         tuning-table changes)."""

@@ -613,6 +613,36 @@ def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, se
             "tokens_head": toks[:8].tolist()}
 
 
+def prompt_processing(torch, n: int = 512, reps: int = 3, seed: int = 0):
+    """pp<n>: an n+1-token prompt: n tokens through abra_model_prefill (the
+    tensor-core tiles) and the last through one decode step, which picks the
+    first generated token; CUDA events on the model's stream around both,
+    best of ``reps`` after one untimed pass (graph capture)."""
+    from abra_b200.model import DecodeModel
+
+    m = DecodeModel(max_ctx=n + 8, seed=seed)
+    prompt = np.random.default_rng(seed + 1).integers(0, m.cfg.vocab, n + 1).astype(np.int32)
+    st = torch.cuda.ExternalStream(m.stream)
+    best = None
+    for r in range(reps + 1):
+        m.reset(prompt)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(st)
+        m.prefill(n)
+        m.step(1)
+        e.record(st)
+        e.synchronize()
+        if r > 0:
+            ms = s.elapsed_time(e)
+            best = ms if best is None else min(best, ms)
+    first = int(m.tokens(n + 2)[n + 1])
+    m.close()
+    return {"prompt_tokens": n + 1, "ms": round(best, 3), "tok_s": round((n + 1) * 1000.0 / best, 1),
+            "first_token": first,
+            "path": f"abra_model_prefill({n}): 32-column tcgen05 GEMV tiles, chunks of 256; "
+                    "then one decode step"}
+
+
 def decode_batched(torch, warmup: int, steps: int, batch: int = 32, seed: int = 0):
     """Batch-32 decode (32 sequences in lockstep, tcgen05 GEMVs): aggregate
     tok/s over ``steps`` graph replays after the 16-token prompts and
@@ -695,6 +725,7 @@ def decode_main(a, dist):
         r = decode_depth(torch, 0, a.warmup, a.steps, streaming=False, flags=Q4_K_M)
         r["type_map"] = "Q4_K_M (Q6_K attn_v, ffn_down in 18 of 36 layers; Q6_K tied output)"
         extras["decode_q4_k_m"] = r
+        extras["prompt_pp512"] = prompt_processing(torch, 512)
     if dist.rank == 0 and dist.world == 1:
         if not a.no_extras:
             extras["per_shape"] = shape_table(sw)

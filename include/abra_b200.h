@@ -250,6 +250,16 @@ int abra_model_reset(void *model, const int32_t *prompt, int32_t n_prompt);
 /* Run n decode steps (asynchronous on the model's stream): each consumes
  * tokens[pos], appends the greedy pick once past the prompt, pos += 1. */
 int abra_model_step(void *model, int32_t n_steps);
+/* Prompt processing: the next n_tokens prompt tokens (a multiple of 32) in
+ * chunks of up to 256 tokens, each chunk one pass of the layers with the
+ * tokens as the 32-column tiles of the tcgen05 GEMVs and causal attention
+ * over the shared KV cache.  It writes the KV cache bit-identically to
+ * n_tokens decode steps, without logits; at least the last prompt token is
+ * left to abra_model_step.  Asynchronous on the model's stream; one GPU,
+ * batch 1, all-Q4_K models.  Counterpart of llama.cpp's batched prompt
+ * evaluation, which the reference measures as pp512
+ * (docs/research/1080ti-speed-results.md:84-91). */
+int abra_model_prefill(void *model, int32_t n_tokens);
 int abra_model_sync(void *model);
 /* Drop the recorded step (after abra_tune_set, for example); the next step
  * records it again.  Not for tensor-parallel models, whose ranks record

@@ -159,3 +159,49 @@ def test_full_qwen3_4b_q4_k_m_greedy_bit_exact():
         assert np.array_equal(g.logits().view(np.uint32), want.view(np.uint32)), f"pos {pos}"
     g.close()
     c.close()
+
+
+def test_prefill_matches_token_by_token_decode():
+    """Prompt processing on the tensor cores leaves the KV cache bit-identical
+    to decoding the prompt token by token: the logits of every following step
+    are equal (2 layers; 300 prompt tokens cross a 256-position attention
+    chunk; chunks of 256 + 32, then a second prefill from a later position)."""
+    from abra_b200.model import DecodeModel
+
+    cfg = dict(n_layers=2, vocab=4096, max_ctx=400, centered=1, seed=21)
+    prompt = _prompt(330, 4096, 9)
+    with DecodeModel(**cfg) as a, DecodeModel(**cfg) as b:
+        a.reset(prompt)
+        b.reset(prompt)
+        b.step(5)
+        b.prefill(288)    # positions 5..292: one 256 chunk and one 32 chunk
+        b.prefill(32)     # positions 293..324
+        a.step(325)
+        assert b.position() == a.position() == 325
+        for pos in range(325, 340):
+            a.step(1)
+            b.step(1)
+            assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32)), f"pos {pos}"
+        assert np.array_equal(a.tokens(341), b.tokens(341))
+
+
+def test_prefill_full_shape_matches_decode_and_refuses_bad_calls():
+    from abra_b200.model import DecodeModel, Q4_K_M
+    from abra_b200._lib import AbraError
+
+    cfg = dict(max_ctx=160, centered=1, seed=2)
+    prompt = _prompt(129, 151936, 10)
+    with DecodeModel(**cfg) as a, DecodeModel(**cfg) as b:
+        a.feed_prompt(prompt)   # prefill 128, then the last prompt token
+        b.reset(prompt)
+        b.step(129)
+        for pos in range(129, 137):
+            assert np.array_equal(a.logits().view(np.uint32), b.logits().view(np.uint32)), f"pos {pos}"
+            a.step(1)
+            b.step(1)
+        with pytest.raises(Exception):
+            a.prefill(32)  # past the prompt
+    with DecodeModel(max_ctx=64, n_layers=2, vocab=512, flags=Q4_K_M) as m:
+        m.reset(_prompt(40, 512, 1))
+        with pytest.raises(AbraError):
+            m.prefill(32)  # the Q4_K_M map has no tensor-core path
