@@ -62,6 +62,9 @@ SIGNATURES: dict[str, tuple] = {
     "abra_model_reset": (C.c_int, [_vp, _vp, _i32]),
     "abra_model_step": (C.c_int, [_vp, _i32]),
     "abra_model_prefill": (C.c_int, [_vp, _i32]),
+    "abra_lookup_draft": (C.c_int, [_vp, _i32, _i32, _i32, _vp]),
+    "abra_model_verify": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),
+    "abra_model_generate_lookup": (C.c_int, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
     "abra_model_sync": (C.c_int, [_vp]),
     "abra_model_invalidate": (C.c_int, [_vp]),
     "abra_model_read": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),

@@ -49,6 +49,9 @@ cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t
                                 int32_t *picks, int64_t tok_stride, int32_t *pos,
                                 const int32_t *n_prompt, int max_ctx, int batch, bool pdl,
                                 cudaStream_t s);
+// out[c] = argmax of column c of logits (ldl floats apart), c < ncols.
+cudaError_t launch_argmax_cols(const float *logits, int n, int64_t ldl, int32_t *out, int ncols,
+                               bool pdl, cudaStream_t s);
 // *pos = min(*pos + n, max_ctx).
 cudaError_t launch_pos_advance(int32_t *pos, int n, int max_ctx, bool pdl, cudaStream_t s);
 // y = Q8_1 of up * silu(gate), n values (a multiple of 32).

@@ -501,6 +501,49 @@ __global__ void __launch_bounds__(1024)
     }
 }
 
+// out[c] = argmax of logits column c (ties to the lowest index, the order of
+// argmax_batch_kernel); one CTA of 1024 threads per column.
+__global__ void argmax_cols_kernel(const float *__restrict__ x, int n, int64_t ldl,
+                                   int32_t *__restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    pdl_wait();
+    pdl_launch_dependents();
+    x += blockIdx.x * ldl;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i];
+        if (v > bv) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
 __global__ void pos_advance_kernel(int32_t *__restrict__ pos_p, int n, int max_ctx) {
     pdl_wait();
     pdl_launch_dependents();
@@ -617,6 +660,11 @@ cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t
                                n_prompt, max_ctx);
     if (e != cudaSuccess) return e;
     return launch_pdl(pos_advance_kernel, dim3(1), dim3(32), 0, s, pdl, pos, 1, max_ctx);
+}
+
+cudaError_t launch_argmax_cols(const float *logits, int n, int64_t ldl, int32_t *out, int ncols,
+                               bool pdl, cudaStream_t s) {
+    return launch_pdl(argmax_cols_kernel, dim3(ncols), dim3(1024), 0, s, pdl, logits, n, ldl, out);
 }
 
 cudaError_t launch_pos_advance(int32_t *pos, int n, int max_ctx, bool pdl, cudaStream_t s) {

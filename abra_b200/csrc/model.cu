@@ -127,6 +127,11 @@ struct Model {
     uint8_t *pxq = nullptr, *poq = nullptr, *paq = nullptr;
     cudaGraphExec_t pgraph[8] = {};  // chunk size 32 (i + 1)
     int32_t host_nprompt = 0;
+    // draft verification: 32 columns with logits and per-column greedy picks
+    float *plogits = nullptr;
+    int32_t *vpick = nullptr;   // device, 32
+    int32_t *vhost = nullptr;   // pinned, 64
+    cudaGraphExec_t vgraph = nullptr;
     size_t weight_bytes = 0, kv_bytes = 0;
     int32_t host_pos = 0;      // position after the queued steps (mirrors *pos)
     int32_t *pinned = nullptr; // 2 pinned ints for the streaming loop
@@ -396,7 +401,7 @@ static cudaError_t record_step_batched(const Model &m, cudaStream_t st) {
 // logits: the last prompt token goes through the decode step.
 constexpr int kPrefillMax = 256;
 
-static cudaError_t record_prefill(const Model &m, int P, cudaStream_t st) {
+static cudaError_t record_layers(const Model &m, int P, cudaStream_t st) {
     const abra_model_config &c = m.cfg;
     const int L = c.n_layers;
     const bool pdl = (c.flags & ABRA_MODEL_NO_PDL) == 0;
@@ -440,7 +445,32 @@ static cudaError_t record_prefill(const Model &m, int P, cudaStream_t st) {
         TRY(launch_swiglu_quant(m.pg, m.pu, m.paq, static_cast<int64_t>(P) * c.ffn, pdl, st));
         TRY(tc(y.wdown, m.paq, m.pdelta, c.hidden, c.ffn, 8));
     }
-    return launch_pos_advance(m.pos, P, c.max_ctx, pdl, st);
+    return cudaSuccess;
+}
+
+static cudaError_t record_prefill(const Model &m, int P, cudaStream_t st) {
+    TRY(record_layers(m, P, st));
+    return launch_pos_advance(m.pos, P, m.cfg.max_ctx, (m.cfg.flags & ABRA_MODEL_NO_PDL) == 0, st);
+}
+
+// Verification of draft tokens (prompt-lookup decoding): the 32 tokens at
+// tokens[*pos .. *pos + 32) as one prefill chunk, then the final residual +
+// RMSNorm + Q8_1, the tied output GEMV for all 32 columns on the tensor
+// cores and each column's greedy pick into vpick.  Position and history are
+// committed by the host (abra_model_verify), which knows how many drafts
+// held.  Per column the logits are the decode step's bits.
+static cudaError_t record_verify(const Model &m, cudaStream_t st) {
+    const abra_model_config &c = m.cfg;
+    const bool pdl = (c.flags & ABRA_MODEL_NO_PDL) == 0;
+    TRY(record_layers(m, 32, st));
+    DeltaSet none = {}, one = {};
+    one.p[0] = m.pdelta;
+    one.G = 1;
+    TRY(launch_residual_rmsnorm_quant(m.ph, c.n_layers > 0 ? one : none, m.out_norm, c.eps, m.pxq,
+                                      c.hidden, 32, pdl, st));
+    TRY(launch_mmvq_tc(m.embd, m.pxq, m.plogits, c.vocab, c.hidden, c.vocab, 1, nullptr,
+                       pdl ? MMVQ_PDL : 0, st));
+    return launch_argmax_cols(m.plogits, c.vocab, c.vocab, m.vpick, 32, pdl, st);
 }
 
 static cudaError_t prefill_buffers(Model &m) {
@@ -466,7 +496,27 @@ static cudaError_t prefill_buffers(Model &m) {
     if (2 * c.ffn > ws) ws = 2 * c.ffn;
     if (2 * qkv_rows > ws) ws = 2 * qkv_rows;
     TRY(alloc(m, &m.pws, 32 * ws * 4));
+    TRY(alloc(m, &m.plogits, static_cast<size_t>(32) * c.vocab * 4));
+    TRY(alloc(m, &m.vpick, 32 * 4));
+    TRY(cudaHostAlloc(reinterpret_cast<void **>(&m.vhost), 64 * sizeof(int32_t), cudaHostAllocDefault));
     return prepare_mmvq_tc();
+}
+
+// Prompt-lookup draft (the reference's draft(), tests/lookup_decode.cpp:39-51):
+// the most recent earlier occurrence of the last `key` tokens of the history,
+// scanning back from history.size() - 2 key, proposes the up to `limit`
+// tokens that followed it.
+static int lookup_draft(const int32_t *h, int n, int key, int limit, int32_t *out) {
+    if (limit <= 0 || key < 1 || n < 2 * key) return 0;
+    const int suffix = n - key;
+    for (int pos = suffix - key; pos >= 0; --pos) {
+        if (std::equal(h + pos, h + pos + key, h + suffix)) {
+            const int cnt = std::min(limit, suffix - pos - key);
+            for (int j = 0; j < cnt; ++j) out[j] = h[pos + key + j];
+            return cnt > 0 ? cnt : 0;
+        }
+    }
+    return 0;
 }
 
 // The decode step for the token at tokens[*pos] (recorded into the graph).
@@ -775,6 +825,8 @@ int abra_model_destroy(void *model) {
     if (m->graph) cudaGraphExecDestroy(m->graph);
     for (cudaGraphExec_t g : m->pgraph)
         if (g) cudaGraphExecDestroy(g);
+    if (m->vgraph) cudaGraphExecDestroy(m->vgraph);
+    if (m->vhost) cudaFreeHost(m->vhost);
     if (m->pinned) cudaFreeHost(m->pinned);
     for (int q = 0; q < m->sh.world; ++q)
         if (m->peer[q] && m->peer[q] != m->arena) cudaIpcCloseMemHandle(m->peer[q]);
@@ -901,6 +953,131 @@ int abra_model_prefill(void *model, int32_t n_tokens) {
         if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "prefill launch", e);
         m->host_pos += P;
         done += P;
+    }
+    return ABRA_OK;
+}
+
+int abra_model_verify(void *model, const int32_t *draft, int32_t n_draft, int32_t *picks_out,
+                      int32_t *kept_out) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || n_draft < 0 || n_draft > 31 || (n_draft > 0 && !draft))
+        return model_fail(ABRA_E_INVALID, "n_draft must be in 0..31", cudaSuccess);
+    if (m->batch > 1 || m->sh.world > 1 || m->mix)
+        return model_fail(ABRA_E_UNSUPPORTED, "verification runs on a one-GPU batch-1 all-Q4_K model", cudaSuccess);
+    const int32_t p = m->host_pos;
+    if (p < m->host_nprompt)
+        return model_fail(ABRA_E_INVALID, "verify after the prompt: the current token must be a pick", cudaSuccess);
+    if (static_cast<int64_t>(p) + 32 > m->cfg.max_ctx)
+        return model_fail(ABRA_E_INVALID, "verification needs 32 positions below max_ctx", cudaSuccess);
+    for (int j = 0; j < n_draft; ++j)
+        if (draft[j] < 0 || draft[j] >= m->cfg.vocab)
+            return model_fail(ABRA_E_INVALID, "token id out of range", cudaSuccess);
+    cudaError_t e = abra::prefill_buffers(*m);
+    if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "verify buffers", e);
+    if (!m->vgraph && !(m->cfg.flags & ABRA_MODEL_EAGER)) {
+        cudaGraph_t gr = nullptr;
+        e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "verify capture", e);
+        const cudaError_t e1 = abra::record_verify(*m, m->stream);
+        e = cudaStreamEndCapture(m->stream, &gr);
+        if (e1 == cudaSuccess && e == cudaSuccess) e = cudaGraphInstantiate(&m->vgraph, gr, 0);
+        if (gr) cudaGraphDestroy(gr);
+        if (e1 != cudaSuccess) e = e1;
+        if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "verify capture", e);
+    }
+    int32_t *hp = m->vhost;  // [0, 32) picks, [32, 64) staging
+    for (int j = 0; j < n_draft; ++j) hp[32 + j] = draft[j];
+    if (n_draft > 0)
+        e = cudaMemcpyAsync(m->tokens + p + 1, hp + 32, n_draft * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = m->vgraph ? cudaGraphLaunch(m->vgraph, m->stream) : abra::record_verify(*m, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(hp, m->vpick, 32 * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "verify", e);
+    // keep the current token and every draft that equals the pick before it
+    int kept = 1;
+    while (kept - 1 < n_draft && hp[kept - 1] == draft[kept - 1]) ++kept;
+    if (picks_out)
+        for (int j = 0; j <= n_draft; ++j) picks_out[j] = hp[j];
+    // commit as kept decode steps would: picks[p + j], the next token, *pos
+    hp[32] = hp[kept - 1];
+    hp[33] = p + kept;
+    e = cudaMemcpyAsync(m->picks + p, hp, kept * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->tokens + p + kept, hp + 32, 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, hp + 33, 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "verify commit", e);
+    m->host_pos = p + kept;
+    if (kept_out) *kept_out = kept;
+    return ABRA_OK;
+}
+
+int abra_lookup_draft(const int32_t *history, int32_t n, int32_t key, int32_t limit, int32_t *out) {
+    if ((n > 0 && !history) || n < 0 || (limit > 0 && !out)) return ABRA_E_INVALID;
+    return abra::lookup_draft(history, n, key, limit, out);
+}
+
+int abra_model_generate_lookup(void *model, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
+                               int32_t key, int32_t draft_max, int32_t *out, int32_t *stats) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || !prompt || !out || n_prompt < 1 || n_gen < 1 || key < 1 || draft_max < 0 || draft_max > 31 ||
+        static_cast<int64_t>(n_prompt) + n_gen > m->cfg.max_ctx + 1)
+        return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
+    if (m->batch > 1 || m->sh.world > 1 || m->mix)
+        return model_fail(ABRA_E_UNSUPPORTED, "lookup decoding runs on a one-GPU batch-1 all-Q4_K model", cudaSuccess);
+    int rc = abra_model_reset(model, prompt, n_prompt);
+    const int n_pf = (n_prompt - 1) / 32 * 32;
+    if (!rc && n_pf) rc = abra_model_prefill(model, n_pf);
+    if (!rc) rc = abra_model_step(model, n_prompt - n_pf);
+    if (rc) return rc;
+    // the pick at the model's position, after the queued work on its stream
+    auto read_current = [&](int32_t *v) {
+        cudaError_t e = cudaMemcpyAsync(m->vhost ? m->vhost + 63 : v, m->tokens + m->host_pos, 4,
+                                        cudaMemcpyDeviceToHost, m->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+        if (e == cudaSuccess && m->vhost) *v = m->vhost[63];
+        return e;
+    };
+    int32_t current = 0;
+    cudaError_t e = abra::prefill_buffers(*m);  // also the pinned staging words
+    if (e == cudaSuccess) e = read_current(&current);
+    if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "read pick", e);
+    std::vector<int32_t> history(prompt, prompt + n_prompt), gen;
+    int32_t cand[32], proposed = 0, accepted = 0, blocks = 0;
+    while (static_cast<int>(gen.size()) < n_gen) {
+        if (static_cast<int>(gen.size()) == n_gen - 1) {  // the last token is already picked
+            gen.push_back(current);
+            break;
+        }
+        history.push_back(current);
+        const int limit = std::min(draft_max, n_gen - static_cast<int>(gen.size()) - 1);
+        const int nc = abra::lookup_draft(history.data(), static_cast<int>(history.size()), key, limit, cand);
+        ++blocks;
+        if (nc == 0 || static_cast<int64_t>(m->host_pos) + 32 > m->cfg.max_ctx) {
+            rc = abra_model_step(model, 1);  // no draft: one decode step
+            if (rc) return rc;
+            gen.push_back(current);
+            e = read_current(&current);
+            if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "read pick", e);
+            continue;
+        }
+        int32_t picks[32], kept = 0;
+        rc = abra_model_verify(model, cand, nc, picks, &kept);
+        if (rc) return rc;
+        proposed += nc;
+        accepted += kept - 1;
+        gen.push_back(current);
+        for (int j = 0; j + 1 < kept; ++j) {
+            gen.push_back(cand[j]);
+            history.push_back(cand[j]);
+        }
+        current = picks[kept - 1];
+    }
+    std::copy(gen.begin(), gen.begin() + n_gen, out);
+    if (stats) {
+        stats[0] = proposed;
+        stats[1] = accepted;
+        stats[2] = blocks;
     }
     return ABRA_OK;
 }

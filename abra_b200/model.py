@@ -40,6 +40,18 @@ NO_PREFETCH = 4  # ABRA_MODEL_NO_PREFETCH
 Q4_K_M = 8  # ABRA_MODEL_Q4_K_M: the real Qwen3-4B-Q4_K_M type map (Q6_K attn_v/ffn_down/output)
 
 
+def lookup_draft(history, key: int, limit: int) -> np.ndarray:
+    """Prompt-lookup draft of the native loop (abra_lookup_draft): the
+    tokens after the most recent earlier occurrence of the last ``key``."""
+    h = np.ascontiguousarray(history, dtype=np.int32)
+    out = np.empty(max(limit, 1), dtype=np.int32)
+    n = _lib.lib.abra_lookup_draft(h.ctypes.data if h.size else None, h.size, key, limit,
+                                   out.ctypes.data)
+    if n < 0:
+        raise ValueError("abra_lookup_draft: bad arguments")
+    return out[:n]
+
+
 def q6k_layers(n_layers: int) -> list[int]:
     """Layers whose attn_v and ffn_down are Q6_K under the Q4_K_M type map
     (llama.cpp's use_more_bits: l < n/8, l >= 7n/8 or (l - n/8) % 3 == 2)."""
@@ -237,6 +249,28 @@ class DecodeModel:
         if n:
             self.prefill(n)
         self.step(p.size - n)
+
+    def verify(self, draft) -> tuple[int, np.ndarray]:
+        """Prompt-lookup verification of up to 31 draft tokens after the
+        current token (abra_model_verify): (kept, the greedy picks)."""
+        d = np.ascontiguousarray(draft, dtype=np.int32)
+        picks = np.empty(d.size + 1, dtype=np.int32)
+        kept = C.c_int32()
+        _check(_lib.lib.abra_model_verify(self.handle, d.ctypes.data if d.size else None, d.size,
+                                          picks.ctypes.data, C.byref(kept)), "abra_model_verify")
+        return kept.value, picks
+
+    def generate_lookup(self, prompt, n_gen: int, key: int = 2, draft_max: int = 16):
+        """Greedy generation with prompt-lookup speculation (the reference's
+        lookup_decode loop): the same tokens as generate(), plus the stats
+        {proposed, accepted, blocks}."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(n_gen, dtype=np.int32)
+        st = np.zeros(3, dtype=np.int32)
+        _check(_lib.lib.abra_model_generate_lookup(self.handle, p.ctypes.data, p.size, n_gen, key,
+                                                   draft_max, out.ctypes.data, st.ctypes.data),
+               "abra_model_generate_lookup")
+        return out, {"proposed": int(st[0]), "accepted": int(st[1]), "blocks": int(st[2])}
 
     def invalidate(self) -> None:
         """Drop the recorded step; the next step records it again (picks up

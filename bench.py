@@ -643,6 +643,42 @@ def prompt_processing(torch, n: int = 512, reps: int = 3, seed: int = 0):
                     "then one decode step"}
 
 
+def lookup_verification(torch, n_prompt: int = 16, blocks: int = 12, seed: int = 0):
+    """Prompt-lookup speculation's verification pass (abra_model_verify):
+    per block 1 current + 15 drafted tokens, the drafts being the true greedy
+    continuation (every draft accepted: the best case of the reference's
+    lookup_decode loop), host round trip included; against plain decode
+    steps.  The break-even point is decode_ms -> verify_ms / decode_ms
+    accepted tokens per block."""
+    from abra_b200.model import DecodeModel
+
+    n_gen = blocks * 16 + 8
+    m = DecodeModel(max_ctx=n_prompt + n_gen + 40, seed=seed)
+    prompt = np.random.default_rng(seed + 2).integers(0, m.cfg.vocab, n_prompt).astype(np.int32)
+    greedy = m.generate(prompt, n_gen)
+    st = torch.cuda.ExternalStream(m.stream)
+    m.reset(prompt)
+    m.step(n_prompt)  # current = greedy[0]
+    m.verify(greedy[1:16])  # warm-up: graph capture
+    i = 16
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(st)
+    kept_total = 0
+    for _ in range(blocks - 1):
+        kept, _ = m.verify(greedy[i + 1:i + 16])
+        kept_total += kept
+        i += kept
+    e.record(st)
+    e.synchronize()
+    ms = s.elapsed_time(e) / (blocks - 1)
+    ok = bool(np.array_equal(m.tokens(n_prompt + i + 1)[n_prompt:n_prompt + i + 1], greedy[:i + 1]))
+    m.close()
+    return {"verify_ms": round(ms, 3), "tokens_per_verify": kept_total / (blocks - 1),
+            "tok_s_all_accepted": round(kept_total / (blocks - 1) * 1000.0 / ms, 1),
+            "tokens_equal_greedy": ok,
+            "path": "abra_model_verify: 32-column tcgen05 pass with logits, host commit"}
+
+
 def decode_batched(torch, warmup: int, steps: int, batch: int = 32, seed: int = 0):
     """Batch-32 decode (32 sequences in lockstep, tcgen05 GEMVs): aggregate
     tok/s over ``steps`` graph replays after the 16-token prompts and
@@ -725,7 +761,12 @@ def decode_main(a, dist):
         r = decode_depth(torch, 0, a.warmup, a.steps, streaming=False, flags=Q4_K_M)
         r["type_map"] = "Q4_K_M (Q6_K attn_v, ffn_down in 18 of 36 layers; Q6_K tied output)"
         extras["decode_q4_k_m"] = r
-        extras["prompt_pp512"] = prompt_processing(torch, 512)
+        for name, fn in (("prompt_pp512", lambda: prompt_processing(torch, 512)),
+                         ("lookup_verify", lambda: lookup_verification(torch))):
+            try:
+                extras[name] = fn()
+            except Exception as exc:  # an extra must not cost the main line
+                extras[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     if dist.rank == 0 and dist.world == 1:
         if not a.no_extras:
             extras["per_shape"] = shape_table(sw)

@@ -260,6 +260,29 @@ int abra_model_step(void *model, int32_t n_steps);
  * evaluation, which the reference measures as pp512
  * (docs/research/1080ti-speed-results.md:84-91). */
 int abra_model_prefill(void *model, int32_t n_tokens);
+/* Prompt-lookup speculative decoding (the reference's tests/lookup_decode.cpp:
+ * draft :39-51, verification and rollback :107-131).
+ * abra_lookup_draft: the most recent earlier occurrence of the last `key`
+ * tokens of history[0, n) proposes the up to `limit` tokens that followed
+ * it; returns their count (written to out).  Host only.
+ * abra_model_verify: after the prompt, with the current token (the last
+ * pick) at the model's position p, evaluates [current, draft[0..n_draft))
+ * (n_draft <= 31) as one 32-column pass with logits -- the same bits as
+ * decode steps -- keeps the current token and every draft that equals the
+ * greedy pick before it (*kept_out = 1 + accepted), and commits: the picks,
+ * the next token at p + kept and the position p + kept (the KV rows past it
+ * are rewritten before they are read).  picks_out receives the n_draft + 1
+ * greedy picks.  Needs p + 32 <= max_ctx.
+ * abra_model_generate_lookup: the reference's loop -- prompt (prefill and a
+ * decode step), then per block a draft from the history and its
+ * verification (a plain decode step when there is no draft); the n_gen
+ * tokens equal greedy decoding's.  stats (optional): proposed, accepted,
+ * blocks.  One GPU, batch 1, all-Q4_K models. */
+int abra_lookup_draft(const int32_t *history, int32_t n, int32_t key, int32_t limit, int32_t *out);
+int abra_model_verify(void *model, const int32_t *draft, int32_t n_draft, int32_t *picks_out,
+                      int32_t *kept_out);
+int abra_model_generate_lookup(void *model, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
+                               int32_t key, int32_t draft_max, int32_t *out, int32_t *stats);
 int abra_model_sync(void *model);
 /* Drop the recorded step (after abra_tune_set, for example); the next step
  * records it again.  Not for tensor-parallel models, whose ranks record

@@ -205,3 +205,43 @@ def test_prefill_full_shape_matches_decode_and_refuses_bad_calls():
         m.reset(_prompt(40, 512, 1))
         with pytest.raises(AbraError):
             m.prefill(32)  # the Q4_K_M map has no tensor-core path
+
+
+@pytest.mark.parametrize("centered", [0, 1])
+def test_lookup_decoding_equals_greedy(centered):
+    """Prompt-lookup speculation (drafts verified in 32-column passes) gives
+    exactly the greedy tokens, whatever the drafts' fate (the prompt repeats
+    itself, so drafts are proposed)."""
+    from abra_b200.model import DecodeModel
+
+    cfg = dict(n_layers=2, vocab=4096, max_ctx=400, centered=centered, seed=31)
+    base = _prompt(20, 4096, 12)
+    prompt = np.concatenate([base, base[:12], base]).astype(np.int32)  # repeats to look up
+    with DecodeModel(**cfg) as m:
+        want = m.generate(prompt, 120)
+        got, stats = m.generate_lookup(prompt, 120, key=2, draft_max=16)
+        assert np.array_equal(got, want)
+        assert stats["blocks"] >= 1 and stats["accepted"] <= stats["proposed"]
+        assert stats["proposed"] > 0, stats
+        # the state after lookup decoding continues like greedy decoding
+        m.step(1)
+        after = m.tokens(len(prompt) + 121)[len(prompt) + 120]
+    with DecodeModel(**cfg) as g:
+        assert g.generate(prompt, 121)[120] == after
+
+
+def test_verify_picks_are_the_decode_steps_picks():
+    from abra_b200.model import DecodeModel
+
+    cfg = dict(n_layers=2, vocab=4096, max_ctx=200, centered=1, seed=33)
+    prompt = _prompt(9, 4096, 13)
+    with DecodeModel(**cfg) as a, DecodeModel(**cfg) as b:
+        greedy = a.generate(prompt, 20)
+        b.reset(prompt)
+        b.step(9)                   # current = greedy[0] at position 9
+        draft = np.array(list(greedy[1:6]) + [7, 8], dtype=np.int32)  # 5 right, then wrong
+        kept, picks = b.verify(draft)
+        assert kept == 6 and np.array_equal(picks[:6], greedy[1:7])
+        assert b.position() == 15
+        b.step(4)
+        assert np.array_equal(b.tokens(20)[9:20], greedy[:11])
