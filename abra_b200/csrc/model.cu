@@ -1193,7 +1193,7 @@ int abra_model_load_tensor(void *model, int32_t layer, int32_t slot, int32_t ggm
     const int64_t hd = c.head_dim, qd = static_cast<int64_t>(c.n_heads) * hd;
     const int64_t kvd = static_cast<int64_t>(c.n_kv_heads) * hd;
     const int64_t qd_l = sh.q_heads * hd, kvd_l = sh.kv_heads * hd;
-    const int64_t nsb_o = qd / abra::QK_K, nsb_f = c.ffn / abra::QK_K;
+    const int64_t nsb_o = qd / abra::QK_K;
     const int64_t row_h = static_cast<int64_t>(abra::q4k_bytes(1, c.hidden));
     // the destination: dst <- rows [r0, r0 + nr) of an N x K tensor of type t
     // (row bytes rb), each row's bytes [b0, b0 + nb) (nb == rb: whole rows)
@@ -1261,7 +1261,6 @@ int abra_model_load_tensor(void *model, int32_t layer, int32_t slot, int32_t ggm
                 rows(y.wdown, t, c.hidden, c.ffn, 0, c.hidden);
                 b0 = sh.ffn_lo / abra::QK_K * block(t);
                 nb = (sh.ffn_hi - sh.ffn_lo) / abra::QK_K * block(t);
-                (void)nsb_f;
                 break;
             }
             default: return model_fail(ABRA_E_INVALID, "unknown tensor slot", cudaSuccess);
