@@ -139,6 +139,10 @@ def load_tuning_table(path: Path | str = TUNING_FILE) -> int:
         call("abra_tune_set", int(e["N"]), int(e["K"]), int(e.get("ncols", 1)),
              int(e.get("nmat", 1)), int(e["candidate"]))
         n += 1
+    for e in data.get("q6k_entries", []):  # the Q6_K MMVQ's table
+        call("abra_q6k_tune_set", int(e["N"]), int(e["K"]), int(e.get("ncols", 1)),
+             int(e["candidate"]))
+        n += 1
     return n
 
 

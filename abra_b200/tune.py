@@ -96,6 +96,12 @@ def time_candidate(torch, plan, ncols, nmat, cid, reps=3, failures=None, kshard=
             if failures is not None and err:
                 failures.append({"candidate": cid, "device_error": err, "launches": len(items)})
             return None
+    return graph_time(torch, run, len(plan), reps)
+
+
+def graph_time(torch, run, launches: int, reps: int = 3) -> float:
+    """Microseconds per launch of ``run`` (``launches`` launches) captured in
+    one CUDA graph, best of ``reps`` replays."""
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
@@ -112,9 +118,76 @@ def time_candidate(torch, plan, ncols, nmat, cid, reps=3, failures=None, kshard=
         g.replay()
         e.record()
         torch.cuda.synchronize()
-        best = min(best, s.elapsed_time(e) * 1e3 / len(plan))
+        best = min(best, s.elapsed_time(e) * 1e3 / launches)
     del g
     return best
+
+
+# the real Qwen3-4B-Q4_K_M Q6_K tensors: attn_v, ffn_down, tied output
+Q6K_SHAPES = [(1024, 2560), (2560, 9728), (151936, 2560)]
+
+
+def tune_q6k(shapes, ncols_list, out: Path, reps: int = 3) -> dict:
+    """Time every Q6_K candidate (abra_q6k_mmvq_ex) per shape and batch
+    width, as tune() does for Q4_K, and store the winners under
+    ``q6k_entries`` of ``out`` (other keys kept)."""
+    import torch
+
+    import abra_b200 as A
+    from .q4k import device_error
+
+    dev = torch.device("cuda:0")
+    ids = sorted(A.q6k_candidates())
+    f = _lib.lib.abra_q6k_mmvq_ex
+    entries = []
+    for N, K in shapes:
+        per = N * (K // 256) * 210
+        copies = max(4, -(-4 * L2_BYTES // per))
+        nb = N * K // 256
+        bufs = []
+        for i in range(copies):
+            t = torch.empty(nb * 210, dtype=torch.uint8, device=dev)
+            A.gen_q6k(t, nb, 0, 7500 + i)
+            bufs.append(t)
+        for ncols in ncols_list:
+            x = torch.from_numpy(np.random.default_rng(K).standard_normal(ncols * K, dtype=np.float32)).to(dev)
+            xq = torch.empty(ncols * (K // 32) * 36, dtype=torch.uint8, device=dev)
+            A.launch_quantize_f32_to_q8_1(x, xq, K, ncols=ncols)
+            y = torch.empty(ncols * N, dtype=torch.float32, device=dev)
+            times = {}
+            for cid in ids:
+                def run(n=copies, cid=cid):
+                    st = stream_handle(None)
+                    for b in bufs[:n]:
+                        rc = f(b.data_ptr(), xq.data_ptr(), y.data_ptr(), N, K, ncols, N, cid,
+                               _lib.ABRA_MMVQ_PDL, st)
+                        if rc:
+                            return rc
+                    return 0
+                if run(1) or run(2):  # shape does not fit this candidate
+                    continue
+                torch.cuda.synchronize()
+                if device_error(clear=True):
+                    continue
+                times[cid] = graph_time(torch, run, copies, reps)
+            assert times, f"no Q6_K candidate ran for {(N, K, ncols)}"
+            fastest = min(times.values())
+            winner = min(c for c, t in times.items() if t <= fastest * 1.005)
+            nbytes = per + ncols * (K // 32) * 36 + ncols * N * 4
+            e = {"N": N, "K": K, "ncols": ncols, "candidate": winner, "us": round(times[winner], 3),
+                 "GBps": round(nbytes / (times[winner] * 1e-6) / 1e9, 1), "copies": copies,
+                 "all_us": {str(c): round(t, 3) for c, t in sorted(times.items())}}
+            entries.append(e)
+            print(json.dumps({k: e[k] for k in ("N", "K", "ncols", "candidate", "us", "GBps")}), flush=True)
+        del bufs
+        torch.cuda.empty_cache()
+    data = json.loads(out.read_text()) if out.exists() else {"arch": 100, "entries": []}
+    keys = {(e["N"], e["K"], e["ncols"]) for e in entries}
+    data["q6k_entries"] = [e for e in data.get("q6k_entries", [])
+                           if (e["N"], e["K"], e["ncols"]) not in keys] + entries
+    out.parent.mkdir(parents=True, exist_ok=True)
+    out.write_text(json.dumps(data, indent=1) + "\n")
+    return data
 
 
 def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None, merge: bool = False) -> dict:
@@ -275,11 +348,17 @@ def main(argv=None) -> int:
     ap.add_argument("--tp", action="store_true",
                     help="the per-rank shapes of the 2/4/8-GPU tensor-parallel decode (batch 1)")
     ap.add_argument("--merge", action="store_true", help="keep the other entries of --out")
+    ap.add_argument("--q6k", action="store_true",
+                    help="tune the Q6_K MMVQ on the real Qwen3-4B-Q4_K_M Q6_K shapes (q6k_entries)")
     ap.add_argument("--decode", action="store_true",
                     help="in-situ: pick each decode slot's candidate by whole-token time")
     a = ap.parse_args(argv)
     if a.decode:
         tune_decode(Path(a.out), ids=a.ids)
+        return 0
+    if a.q6k:
+        shapes = [tuple(s[:2]) for s in a.shape] if a.shape else Q6K_SHAPES
+        tune_q6k(shapes, a.ncols, Path(a.out))
         return 0
     shapes = [tuple(s) for s in a.shape] if a.shape else (tp_shapes() if a.tp else DECODE_SHAPES)
     tune(shapes, a.ncols, Path(a.out), a.quick, a.ids, a.merge)

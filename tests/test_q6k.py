@@ -205,3 +205,21 @@ def test_oracle_q4_k_m_model_differs_from_q4k_model():
     assert np.isfinite(lb).all() and not np.array_equal(la, lb)
     a.close()
     b.close()
+
+
+def test_tuning_file_q6k_entries(tmp_path):
+    """q6k_entries of a tuning file feed the Q6_K table; the shipped file
+    holds the measured winners of the real model's three Q6_K shapes."""
+    import json
+
+    import abra_b200 as A
+    from abra_b200.q4k import TUNING_FILE, load_tuning_table
+
+    p = tmp_path / "t.json"
+    p.write_text(json.dumps({"entries": [], "q6k_entries": [{"N": 640, "K": 768, "ncols": 2, "candidate": 3082}]}))
+    assert load_tuning_table(p) == 1
+    assert A.q6k_tune_get(640, 768, 2) == 3082
+    shipped = json.loads(TUNING_FILE.read_text())["q6k_entries"]
+    assert {(e["N"], e["K"]) for e in shipped} == {(1024, 2560), (2560, 9728), (151936, 2560)}
+    for e in shipped:
+        assert A.q6k_tune_get(e["N"], e["K"], 1) == e["candidate"] == int(min(e["all_us"], key=e["all_us"].get))
