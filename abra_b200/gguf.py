@@ -99,7 +99,10 @@ class GGUFFile:
 
     def close(self) -> None:
         if self._mm is not None:
-            self._mm.close()
+            try:
+                self._mm.close()
+            except BufferError:  # a tensor view is still alive: the map closes with it
+                pass
             self._mm = None
 
     def __enter__(self):
@@ -147,6 +150,8 @@ class _Cursor:
 def read_gguf(path) -> GGUFFile:
     """Parse the header, metadata and tensor infos; map the file."""
     path = Path(path)
+    if path.stat().st_size < 24:
+        raise GGUFError(f"{path}: not a GGUF file")
     f = open(path, "rb")
     try:
         mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)

@@ -88,6 +88,9 @@ def test_slot_names():
 
 def test_malformed_files_refused(tmp_path):
     p = tmp_path / "m.gguf"
+    p.write_bytes(b"")
+    with pytest.raises(G.GGUFError, match="not a GGUF"):
+        G.read_gguf(p)
     p.write_bytes(b"GGML" + b"\0" * 40)
     with pytest.raises(G.GGUFError, match="not a GGUF"):
         G.read_gguf(p)
@@ -106,3 +109,12 @@ def test_load_tensor_refuses_without_a_model():
     from abra_b200 import _lib
 
     assert _lib.lib.abra_model_load_tensor(None, -1, 1, 12, 16, 144) == _lib.ABRA_E_INVALID
+
+
+def test_close_with_a_live_tensor_view(tmp_path):
+    p = tmp_path / "v.gguf"
+    G.write_gguf(p, {}, [("t", (256, 1), G.GGML_Q4_K, np.arange(144, dtype=np.uint8))])
+    g = G.read_gguf(p)
+    view = g.data("t")
+    g.close()  # does not raise while `view` is alive
+    assert view[5] == 5
