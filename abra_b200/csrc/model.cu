@@ -474,7 +474,7 @@ static cudaError_t record_verify(const Model &m, cudaStream_t st) {
 }
 
 static cudaError_t prefill_buffers(Model &m) {
-    if (m.ph) return cudaSuccess;
+    if (m.vhost) return cudaSuccess;  // the last allocation: all of them are in place
     const abra_model_config &c = m.cfg;
     const int64_t P = kPrefillMax, hd = c.head_dim, qd = c.n_heads * hd;
     const int64_t qkv_rows = (c.n_heads + 2 * c.n_kv_heads) * hd;
@@ -498,8 +498,8 @@ static cudaError_t prefill_buffers(Model &m) {
     TRY(alloc(m, &m.pws, 32 * ws * 4));
     TRY(alloc(m, &m.plogits, static_cast<size_t>(32) * c.vocab * 4));
     TRY(alloc(m, &m.vpick, 32 * 4));
-    TRY(cudaHostAlloc(reinterpret_cast<void **>(&m.vhost), 64 * sizeof(int32_t), cudaHostAllocDefault));
-    return prepare_mmvq_tc();
+    TRY(prepare_mmvq_tc());
+    return cudaHostAlloc(reinterpret_cast<void **>(&m.vhost), 64 * sizeof(int32_t), cudaHostAllocDefault);
 }
 
 // Prompt-lookup draft (the reference's draft(), tests/lookup_decode.cpp:39-51):
