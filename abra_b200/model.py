@@ -241,11 +241,14 @@ class DecodeModel:
 
     def feed_prompt(self, prompt) -> None:
         """reset(prompt), then prefill every whole 32-token tile of the
-        first len(prompt) - 1 tokens and step through the rest; afterwards the
-        model has picked the first generated token."""
+        first len(prompt) - 1 tokens (models the prefill supports) and step
+        through the rest; afterwards the model has picked the first generated
+        token."""
         p = np.ascontiguousarray(prompt, dtype=np.int32)
         self.reset(p)
-        n = (p.size - 1) // 32 * 32
+        # the tensor-core prefill covers one-GPU all-Q4_K models; the rest step
+        can = self.shard.world == 1 and not (self.cfg.flags & Q4_K_M)
+        n = (p.size - 1) // 32 * 32 if can else 0
         if n:
             self.prefill(n)
         self.step(p.size - n)

@@ -272,7 +272,8 @@ int abra_model_prefill(void *model, int32_t n_tokens);
  * greedy pick before it (*kept_out = 1 + accepted), and commits: the picks,
  * the next token at p + kept and the position p + kept (the KV rows past it
  * are rewritten before they are read).  picks_out receives the n_draft + 1
- * greedy picks.  Needs p + 32 <= max_ctx.
+ * greedy picks.  Needs p + 32 <= max_ctx.  abra_model_read's logits stay
+ * those of the last decode step.
  * abra_model_generate_lookup: the reference's loop -- prompt (prefill and a
  * decode step), then per block a draft from the history and its
  * verification (a plain decode step when there is no draft); the n_gen
