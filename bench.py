@@ -177,8 +177,15 @@ class Dist:
 
 
 # --------------------------------------------------------------- CPU arm ---
+def simd_level() -> int:
+    import oracle as O
+
+    return int(O.lib.orc_simd_level())
+
+
 def cpu_sample_rate(batch: int, budget_s: float, seed: int = 0):
-    """CPU restatement of vec_dot_q4_K_q8_1 (OpenMP, all host cores) on a
+    """CPU restatement of vec_dot_q4_K_q8_1 (OpenMP, all host cores; integer
+    sub-block dots on the host's AVX-512 VNNI or AVX2 when present) on a
     sample of the workload: the first 512 rows of every config-1 matrix,
     repeated until ``budget_s`` seconds elapse.  Returns GB/s by the same
     byte formula."""
@@ -780,7 +787,9 @@ def decode_main(a, dist):
         cpu = {"value": round(cpu_tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
                "sample": f"first 512 rows of every config-1 matrix, {reps} reps in {el:.1f}s "
                          f"({gbs:.2f} GB/s), scaled to the 2.26 GB of Q4_K weights a token "
-                         "reads; CPU restatement of vec_dot_q4_K_q8_1 (ggml CPU path not available)"}
+                         "reads; CPU restatement of vec_dot_q4_K_q8_1, integer dots at SIMD level "
+                         f"{simd_level()} (0 scalar, 1 AVX2, 2 AVX-512 VNNI); ggml CPU path "
+                         "not available"}
     traffic = None
     tp = ROOT / "profiles" / f"traffic_{WORKLOAD}_b1.json"
     if tp.exists():
@@ -829,7 +838,8 @@ def reference_arm(a, dist):
     gbs = statistics.median(r[0] for r in rates)
     threads = rates[0][1]
     sample = (f"first 512 rows of every config-1 matrix, batch {a.batch}, {per:.1f}s per step; "
-              "CPU restatement of vec_dot_q4_K_q8_1 (the ggml CPU path is not available)")
+              f"CPU restatement of vec_dot_q4_K_q8_1, integer dots at SIMD level {simd_level()} "
+              "(0 scalar, 1 AVX2, 2 AVX-512 VNNI); the ggml CPU path is not available")
     if a.workload == "decode":
         weight_bytes = sum(nmat * q4k_bytes(N, K) for _, N, K, nmat, _ in sweep_ops())
         val, unit, metric = gbs * 1e9 / weight_bytes, "tok/s", "Qwen3-4B-shape decode tok/s"
@@ -929,8 +939,9 @@ def main():
         gbs, threads, reps, el = cpu_sample_rate(a.batch, a.cpu_budget)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"first 512 rows of every config-1 matrix, batch {a.batch}, {reps} reps "
-                         f"in {el:.1f}s; CPU restatement of vec_dot_q4_K_q8_1 (the ggml CPU "
-                         "path is not available)"}
+                         f"in {el:.1f}s; CPU restatement of vec_dot_q4_K_q8_1, integer dots at "
+                         f"SIMD level {simd_level()} (0 scalar, 1 AVX2, 2 AVX-512 VNNI); the ggml "
+                         "CPU path is not available"}
 
     traffic = None
     tp = ROOT / "profiles" / f"traffic_{WORKLOAD}_b{a.batch}.json"

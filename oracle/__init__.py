@@ -63,6 +63,8 @@ def _load() -> C.CDLL:
         "orc_dequant_q4k": (None, [_u8p, _f32p, _i64]),
         "orc_slice_starts": (None, [_i32, _i32p]),
         "orc_max_threads": (C.c_int32, []),
+        "orc_simd_level": (C.c_int32, []),
+        "orc_set_simd_level": (None, [C.c_int32]),
         "orc_expf": (C.c_float, [C.c_float]),
         "orc_silu": (C.c_float, [C.c_float]),
         "orc_swiglu": (None, [_f32p, _f32p, _f32p, _i64]),

@@ -385,18 +385,141 @@ static inline float tree8(const float v[8]) {
     return ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
 }
 
+/* ---- the integer sub-block dots, vectorised ------------------------------
+ * P[s] = sum_l q4 * q8 over sub-block s is an exact integer in any order, so
+ * the GEMVs compute it with the widest integer dot the host has (AVX-512
+ * VNNI vpdpbusd, AVX2 vpmaddubsw + vpmaddwd, or the scalar loop of
+ * sb_partials) on activations staged once per column as contiguous int8;
+ * the fp32 part (sb_value) is unchanged.  Sub-block 2p is the low nibbles of
+ * qs[32p..32p+31] against x[64p..64p+31], sub-block 2p+1 the high nibbles
+ * against x[64p+32..64p+63], so one 64-byte step covers a pair. */
+typedef void (*sb_dots_fn)(const uint8_t *qs, const int8_t *x, int32_t P[8]);
+
+static void sb_dots_scalar(const uint8_t *qs, const int8_t *x, int32_t P[8]) {
+    for (int p = 0; p < 4; ++p) {
+        int32_t lo = 0, hi = 0;
+        for (int l = 0; l < 32; ++l) {
+            lo += (qs[32 * p + l] & 0xF) * x[64 * p + l];
+            hi += (qs[32 * p + l] >> 4) * x[64 * p + 32 + l];
+        }
+        P[2 * p] = lo;
+        P[2 * p + 1] = hi;
+    }
+}
+
+#if defined(__x86_64__) && defined(__GNUC__)
+#include <immintrin.h>
+
+__attribute__((target("avx2"))) static inline int32_t hsum8_avx2(__m256i v) {
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0x4E));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0xB1));
+    return _mm_cvtsi128_si32(s);
+}
+
+__attribute__((target("avx2"))) static void sb_dots_avx2(const uint8_t *qs, const int8_t *x,
+                                                        int32_t P[8]) {
+    const __m256i m4 = _mm256_set1_epi8(0x0F), ones = _mm256_set1_epi16(1);
+    for (int p = 0; p < 4; ++p) {
+        const __m256i b = _mm256_loadu_si256((const __m256i *)(qs + 32 * p));
+        const __m256i lo = _mm256_and_si256(b, m4);
+        const __m256i hi = _mm256_and_si256(_mm256_srli_epi16(b, 4), m4);
+        const __m256i xl = _mm256_loadu_si256((const __m256i *)(x + 64 * p));
+        const __m256i xh = _mm256_loadu_si256((const __m256i *)(x + 64 * p + 32));
+        /* u4 x s8 pair sums stay within int16 (|15 * 127 * 2| < 2^15) */
+        P[2 * p] = hsum8_avx2(_mm256_madd_epi16(_mm256_maddubs_epi16(lo, xl), ones));
+        P[2 * p + 1] = hsum8_avx2(_mm256_madd_epi16(_mm256_maddubs_epi16(hi, xh), ones));
+    }
+}
+
+__attribute__((target("avx512f,avx512bw,avx512vnni,avx2"))) static void sb_dots_vnni(
+    const uint8_t *qs, const int8_t *x, int32_t P[8]) {
+    const __m256i m4 = _mm256_set1_epi8(0x0F);
+    for (int p = 0; p < 4; ++p) {
+        const __m256i b = _mm256_loadu_si256((const __m256i *)(qs + 32 * p));
+        const __m256i lo = _mm256_and_si256(b, m4);
+        const __m256i hi = _mm256_and_si256(_mm256_srli_epi16(b, 4), m4);
+        const __m512i wv = _mm512_inserti64x4(_mm512_castsi256_si512(lo), hi, 1);
+        const __m512i xv = _mm512_loadu_si512((const void *)(x + 64 * p));
+        const __m512i acc = _mm512_dpbusd_epi32(_mm512_setzero_si512(), wv, xv);
+        P[2 * p] = hsum8_avx2(_mm512_castsi512_si256(acc));
+        P[2 * p + 1] = hsum8_avx2(_mm512_extracti64x4_epi64(acc, 1));
+    }
+}
+#endif
+
+static int32_t g_simd = -1; /* -1: not chosen yet; 0 scalar, 1 AVX2, 2 AVX-512 VNNI */
+
+int32_t orc_simd_level(void) {
+    if (g_simd < 0) {
+        g_simd = 0;
+#if defined(__x86_64__) && defined(__GNUC__)
+        __builtin_cpu_init();
+        if (__builtin_cpu_supports("avx2")) g_simd = 1;
+        if (__builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
+            __builtin_cpu_supports("avx512vnni"))
+            g_simd = 2;
+#endif
+    }
+    return g_simd;
+}
+
+void orc_set_simd_level(int32_t level) {
+    const int32_t best = (g_simd = -1, orc_simd_level());
+    g_simd = level < 0 ? best : (level < best ? level : best);
+}
+
+static sb_dots_fn sb_dots(void) {
+#if defined(__x86_64__) && defined(__GNUC__)
+    switch (orc_simd_level()) {
+        case 2: return sb_dots_vnni;
+        case 1: return sb_dots_avx2;
+        default: break;
+    }
+#endif
+    return sb_dots_scalar;
+}
+
+/* One activation column staged for the vectorised dots: the K int8 values
+ * contiguous and M[s] = sum of each 32-block. */
+typedef struct {
+    int8_t *x8;
+    int32_t *M;
+} xstage;
+
+static xstage stage_column(const uint8_t *xcol, int64_t K) {
+    xstage st;
+    st.x8 = (int8_t *)malloc((size_t)K);
+    st.M = (int32_t *)malloc((size_t)(K / QK8_1) * sizeof(int32_t));
+    for (int64_t i = 0; i < K / QK8_1; ++i) {
+        const int8_t *q = (const int8_t *)(xcol + i * Q81_BYTES + 4);
+        int32_t m = 0;
+        for (int l = 0; l < QK8_1; ++l) {
+            st.x8[i * QK8_1 + l] = q[l];
+            m += q[l];
+        }
+        st.M[i] = m;
+    }
+    return st;
+}
+
+static void free_stage(xstage *st) {
+    free(st->x8);
+    free(st->M);
+}
+
 /* Slice sums of one row against one column: sequential within a slice,
  * +0.0f for an empty slice. */
-static void row_slices(const uint8_t *wrow, const uint8_t *xcol, int32_t nsb,
-                       const int32_t start9[9], float v[8]) {
+static void row_slices(const uint8_t *wrow, const uint8_t *xcol, const xstage *st,
+                       sb_dots_fn dots, const int32_t start9[9], float v[8]) {
     for (int i = 0; i < 8; ++i) {
         float acc = 0.0f;
         for (int b = start9[i]; b < start9[i + 1]; ++b) {
-            int32_t P[8], M[8];
+            int32_t P[8];
             const uint8_t *blk = wrow + (int64_t)b * Q4K_BYTES;
             const uint8_t *xb = xcol + (int64_t)b * 8 * Q81_BYTES;
-            sb_partials(blk, xb, P, M);
-            const float c = sb_value(blk, xb, P, M);
+            dots(blk + 16, st->x8 + (int64_t)b * QK_K, P);
+            const float c = sb_value(blk, xb, P, st->M + (int64_t)b * 8);
             acc = (b == start9[i]) ? c : acc + c;
         }
         v[i] = acc;
@@ -424,15 +547,20 @@ void orc_q4k_gemv(const uint8_t *w, const uint8_t *xq, float *y, int64_t N, int6
     int32_t start9[9];
     orc_slice_starts(nsb, start9);
     if (nthreads < 1) nthreads = 1;
+    const sb_dots_fn dots = sb_dots();
+    xstage *st = (xstage *)malloc((size_t)ncols * sizeof(xstage));
+    for (int32_t c = 0; c < ncols; ++c) st[c] = stage_column(xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, K);
 #pragma omp parallel for num_threads(nthreads) schedule(static)
     for (int64_t r = 0; r < N; ++r) {
         for (int32_t c = 0; c < ncols; ++c) {
             float v[8];
-            row_slices(w + r * nsb * Q4K_BYTES, xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, nsb,
-                       start9, v);
+            row_slices(w + r * nsb * Q4K_BYTES, xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, &st[c],
+                       dots, start9, v);
             y[(int64_t)c * N + r] = tree8(v);
         }
     }
+    for (int32_t c = 0; c < ncols; ++c) free_stage(&st[c]);
+    free(st);
 }
 
 void orc_q4k_gemv_slices(const uint8_t *w, const uint8_t *xq, float *v, int64_t N,
@@ -440,10 +568,14 @@ void orc_q4k_gemv_slices(const uint8_t *w, const uint8_t *xq, float *v, int64_t 
     const int32_t nsb = (int32_t)(K / QK_K);
     int32_t start9[9];
     orc_slice_starts(nsb, start9);
-    for (int32_t c = 0; c < ncols; ++c)
+    const sb_dots_fn dots = sb_dots();
+    for (int32_t c = 0; c < ncols; ++c) {
+        xstage st = stage_column(xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, K);
         for (int64_t r = 0; r < N; ++r)
-            row_slices(w + r * nsb * Q4K_BYTES, xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, nsb,
+            row_slices(w + r * nsb * Q4K_BYTES, xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, &st, dots,
                        start9, v + ((int64_t)c * N + r) * 8);
+        free_stage(&st);
+    }
 }
 
 /* Independent f64 oracle, restating tests/q4k_q8_test.cu:54-107. */

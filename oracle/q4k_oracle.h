@@ -90,6 +90,11 @@ void orc_slice_starts(int32_t nsb, int32_t *start9);
 
 int32_t orc_max_threads(void);
 
+/* Integer-dot implementation of the GEMVs: 0 scalar, 1 AVX2, 2 AVX-512 VNNI
+ * (the best the host has, unless lowered; the results are the same bits). */
+int32_t orc_simd_level(void);
+void orc_set_simd_level(int32_t level); /* < 0: the best again */
+
 #ifdef __cplusplus
 }
 #endif

@@ -184,3 +184,22 @@ def test_oracle_matches_reference_kernels(path):
             tol_check(g[key].reshape(1, -1), y64, scale, rel=1e-5)
     # and the canonical fp32 oracle sits at least as close to f64
     tol_check(O.gemv(w, xq, K), y64, scale, rel=1e-6)
+
+
+def test_vectorised_integer_dots_give_the_same_bits():
+    """The oracle GEMV's integer sub-block dots run on the host's widest
+    integer dot (AVX-512 VNNI / AVX2) or the scalar loop: identical outputs."""
+    K = 2560
+    w = O.gen_q4k(200, K, 2, 71)
+    xq = O.quantize_q8_1(O.gen_normal_f32((3, K), 72))
+    best = O.lib.orc_simd_level()
+    try:
+        outs = []
+        for lvl in range(best + 1):
+            O.lib.orc_set_simd_level(lvl)
+            outs.append((O.gemv(w, xq, K, nthreads=4), O.gemv_slices(w, xq, K)))
+    finally:
+        O.lib.orc_set_simd_level(-1)
+    for y, v in outs[1:]:
+        assert np.array_equal(y, outs[0][0]) and np.array_equal(v, outs[0][1])
+    assert np.array_equal(O.tree8(outs[-1][1]), outs[-1][0])
