@@ -620,6 +620,33 @@ def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, se
             "tokens_head": toks[:8].tolist()}
 
 
+def decode_samples(torch, warmup: int, steps: int, seed: int = 0):
+    """Per-token decode times at depth 0 (a second pass after the headline
+    measurement): one CUDA event pair per token on the model's stream,
+    giving the median / min / max / spread / stddev and the raw samples the
+    reference's methodology reports (docs/benchmark-methodology.md:41-62)."""
+    from abra_b200.model import DecodeModel
+
+    m = DecodeModel(max_ctx=PROMPT + warmup + steps + 1, seed=seed)
+    prompt = np.random.default_rng(seed).integers(0, m.cfg.vocab, PROMPT).astype(np.int32)
+    m.reset(prompt)
+    m.step(PROMPT - 1 + warmup)
+    m.sync()
+    st = torch.cuda.ExternalStream(m.stream)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record(st)
+    for i in range(steps):
+        m.step(1)
+        ev[i + 1].record(st)
+    ev[-1].synchronize()
+    ms = np.array([ev[i].elapsed_time(ev[i + 1]) for i in range(steps)])
+    m.close()
+    return {"unit": "ms/token", "n": steps, "median": round(float(np.median(ms)), 4),
+            "min": round(float(ms.min()), 4), "max": round(float(ms.max()), 4),
+            "spread": round(float(ms.max() - ms.min()), 4), "stddev": round(float(ms.std()), 4),
+            "raw": [round(float(v), 4) for v in ms]}
+
+
 def prompt_processing(torch, n: int = 512, reps: int = 3, seed: int = 0):
     """pp<n>: an n+1-token prompt: n tokens through abra_model_prefill (the
     tensor-core tiles) and the last through one decode step, which picks the
@@ -769,7 +796,8 @@ def decode_main(a, dist):
         r["type_map"] = "Q4_K_M (Q6_K attn_v, ffn_down in 18 of 36 layers; Q6_K tied output)"
         extras["decode_q4_k_m"] = r
         for name, fn in (("prompt_pp512", lambda: prompt_processing(torch, 512)),
-                         ("lookup_verify", lambda: lookup_verification(torch))):
+                         ("lookup_verify", lambda: lookup_verification(torch)),
+                         ("decode_samples", lambda: decode_samples(torch, a.warmup, a.steps))):
             try:
                 extras[name] = fn()
             except Exception as exc:  # an extra must not cost the main line
