@@ -485,12 +485,14 @@ static sb_dots_fn sb_dots(void) {
 typedef struct {
     int8_t *x8;
     int32_t *M;
+    float *d8; /* the blocks' fp16 scales as fp32 (the values half_at gives) */
 } xstage;
 
 static xstage stage_column(const uint8_t *xcol, int64_t K) {
     xstage st;
     st.x8 = (int8_t *)malloc((size_t)K);
     st.M = (int32_t *)malloc((size_t)(K / QK8_1) * sizeof(int32_t));
+    st.d8 = (float *)malloc((size_t)(K / QK8_1) * sizeof(float));
     for (int64_t i = 0; i < K / QK8_1; ++i) {
         const int8_t *q = (const int8_t *)(xcol + i * Q81_BYTES + 4);
         int32_t m = 0;
@@ -499,6 +501,7 @@ static xstage stage_column(const uint8_t *xcol, int64_t K) {
             m += q[l];
         }
         st.M[i] = m;
+        st.d8[i] = half_at(xcol + i * Q81_BYTES);
     }
     return st;
 }
@@ -506,20 +509,44 @@ static xstage stage_column(const uint8_t *xcol, int64_t K) {
 static void free_stage(xstage *st) {
     free(st->x8);
     free(st->M);
+    free(st->d8);
+}
+
+/* sb_value with the column's staged d8: the same operations on the same
+ * values, so the same bits. */
+static inline float sb_value_staged(const uint8_t *blk, const float *d8, const int32_t P[8],
+                                    const int32_t M[8]) {
+    const float d = half_at(blk), dmin = half_at(blk + 2);
+    float tp[4], up[4];
+    for (int p = 0; p < 4; ++p) {
+        float t[2], u[2];
+        for (int i = 0; i < 2; ++i) {
+            const int s = 2 * p + i;
+            int sc, m;
+            scale_min(blk + 4, s, &sc, &m);
+            t[i] = d8[s] * (float)(P[s] * sc);
+            const float A = d8[s] * (float)M[s];
+            u[i] = A * (float)m;
+        }
+        tp[p] = t[0] + t[1];
+        up[p] = u[0] + u[1];
+    }
+    const float Sd = (tp[0] + tp[1]) + (tp[2] + tp[3]);
+    const float Sm = (up[0] + up[1]) + (up[2] + up[3]);
+    return fmaf(d, Sd, -(dmin * Sm));
 }
 
 /* Slice sums of one row against one column: sequential within a slice,
  * +0.0f for an empty slice. */
-static void row_slices(const uint8_t *wrow, const uint8_t *xcol, const xstage *st,
-                       sb_dots_fn dots, const int32_t start9[9], float v[8]) {
+static void row_slices(const uint8_t *wrow, const xstage *st, sb_dots_fn dots,
+                       const int32_t start9[9], float v[8]) {
     for (int i = 0; i < 8; ++i) {
         float acc = 0.0f;
         for (int b = start9[i]; b < start9[i + 1]; ++b) {
             int32_t P[8];
             const uint8_t *blk = wrow + (int64_t)b * Q4K_BYTES;
-            const uint8_t *xb = xcol + (int64_t)b * 8 * Q81_BYTES;
             dots(blk + 16, st->x8 + (int64_t)b * QK_K, P);
-            const float c = sb_value(blk, xb, P, st->M + (int64_t)b * 8);
+            const float c = sb_value_staged(blk, st->d8 + (int64_t)b * 8, P, st->M + (int64_t)b * 8);
             acc = (b == start9[i]) ? c : acc + c;
         }
         v[i] = acc;
@@ -554,8 +581,7 @@ void orc_q4k_gemv(const uint8_t *w, const uint8_t *xq, float *y, int64_t N, int6
     for (int64_t r = 0; r < N; ++r) {
         for (int32_t c = 0; c < ncols; ++c) {
             float v[8];
-            row_slices(w + r * nsb * Q4K_BYTES, xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, &st[c],
-                       dots, start9, v);
+            row_slices(w + r * nsb * Q4K_BYTES, &st[c], dots, start9, v);
             y[(int64_t)c * N + r] = tree8(v);
         }
     }
@@ -572,8 +598,7 @@ void orc_q4k_gemv_slices(const uint8_t *w, const uint8_t *xq, float *v, int64_t 
     for (int32_t c = 0; c < ncols; ++c) {
         xstage st = stage_column(xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, K);
         for (int64_t r = 0; r < N; ++r)
-            row_slices(w + r * nsb * Q4K_BYTES, xq + (int64_t)c * (K / QK8_1) * Q81_BYTES, &st, dots,
-                       start9, v + ((int64_t)c * N + r) * 8);
+            row_slices(w + r * nsb * Q4K_BYTES, &st, dots, start9, v + ((int64_t)c * N + r) * 8);
         free_stage(&st);
     }
 }
