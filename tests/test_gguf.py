@@ -118,3 +118,23 @@ def test_close_with_a_live_tensor_view(tmp_path):
     view = g.data("t")
     g.close()  # does not raise while `view` is alive
     assert view[5] == 5
+
+
+def test_from_gguf_refuses_before_creating_a_model(tmp_path):
+    """An unsupported file is refused while reading the header: no model (and
+    no CUDA call) is made."""
+    from abra_b200.model import DecodeModel
+    from gguf_fixture import qwen3_tensors
+
+    shape = {k: SMALL[k] for k in SMALL}
+    t = qwen3_tensors(**shape, seed=1) + [("output.weight", (512, 300), G.GGML_Q4_K,
+                                           np.zeros(300 * 2 * 144, np.uint8))]
+    p = tmp_path / "untied.gguf"
+    G.write_gguf(p, qwen3_metadata(**shape), t)
+    with pytest.raises(G.GGUFError, match="untied"):
+        DecodeModel.from_gguf(p)
+    meta = qwen3_metadata(**shape)
+    meta["general.architecture"] = "llama"
+    G.write_gguf(p, meta, qwen3_tensors(**shape, seed=1))
+    with pytest.raises(G.GGUFError, match="qwen3"):
+        DecodeModel.from_gguf(p)
