@@ -91,3 +91,15 @@ def test_tensor_core_mmvq_rejects_bad_arguments_without_gpu():
     assert lib.abra_q4k_mmvq_tc(16, 16, 16, 128, 256, 32, 128, 3, None, 0, None) == _lib.ABRA_E_INVALID
     with pytest.raises(ValueError):
         A.mmvq_tc(16, 16, 16, 128, 300)
+
+
+def test_new_model_entry_points_refuse_a_null_model():
+    from abra_b200 import _lib
+
+    lib = _lib.lib
+    assert lib.abra_model_prefill(None, 32) == _lib.ABRA_E_INVALID
+    assert lib.abra_model_prefill(None, 33) == _lib.ABRA_E_INVALID
+    assert lib.abra_model_verify(None, None, 0, None, None) == _lib.ABRA_E_INVALID
+    assert lib.abra_model_load_tensor(None, -1, 1, 12, None, 0) == _lib.ABRA_E_INVALID
+    assert lib.abra_lookup_draft(None, -1, 2, 4, None) == _lib.ABRA_E_INVALID
+    assert lib.abra_lookup_draft(None, 0, 2, 4, None) == _lib.ABRA_E_INVALID  # limit > 0, no out
