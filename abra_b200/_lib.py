@@ -81,6 +81,7 @@ SIGNATURES: dict[str, tuple] = {
     "abra_model_tp_handle": (C.c_int, [_vp, _vp, _i32]),
     "abra_model_tp_connect": (C.c_int, [_vp, _vp, _i32]),
     "abra_model_load_tensor": (C.c_int, [_vp, _i32, _i32, _i32, _vp, C.c_uint64]),
+    "abra_tp_tensor_slice": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _vp]),
 }
 
 

@@ -316,6 +316,102 @@ static cudaError_t build(Model &m) {
     return cudaStreamSynchronize(st);
 }
 
+// One tensor of a GGUF file as a rank holds it: the ggml type of the slot,
+// the whole tensor's N rows of K (rb bytes each), the rank's rows
+// [r0, r0 + nr) and bytes [b0, b0 + nb) of each (nb == rb: whole rows), and
+// where they go: buffer buf, after dst_row rows of nb bytes (the q|k|v rows
+// share one buffer).  Row-split tensors (q, k, v, gate, up) keep the rank's
+// heads or FFN units; K-split ones (o, down) its canonical K-slices of every
+// row; the tied table and the norms are whole on every rank -- the placement
+// build() gives the seeded weights.
+enum : int {
+    BUF_EMBD, BUF_OUT_NORM, BUF_ATTN_NORM, BUF_FFN_NORM, BUF_Q_NORM, BUF_K_NORM, BUF_WQKV, BUF_WV,
+    BUF_WO, BUF_WGATE, BUF_WUP, BUF_WDOWN
+};
+
+struct TensorSlice {
+    int type, buf;
+    int64_t N, K, rb, r0, nr, b0, nb, dst_row;
+};
+
+static int tensor_slice(const abra_model_config &c, const abra_tp_shard &sh, bool mix, int layer,
+                        int slot, TensorSlice &t) {
+    const int64_t hd = c.head_dim, qd = static_cast<int64_t>(c.n_heads) * hd;
+    const int64_t kvd = static_cast<int64_t>(c.n_kv_heads) * hd;
+    const int64_t qd_l = sh.q_heads * hd, kvd_l = sh.kv_heads * hd;
+    const int nsb_o = static_cast<int>(qd / QK_K);
+    auto block = [](int type) -> int64_t { return type == ABRA_GGML_Q6_K ? 210 : Q4K_BYTES; };
+    auto rows = [&](int buf, int type, int64_t n, int64_t k, int64_t lo, int64_t cnt, int64_t at) {
+        t.buf = buf;
+        t.type = type;
+        t.N = n;
+        t.K = k;
+        t.rb = k / QK_K * block(type);
+        t.r0 = lo;
+        t.nr = cnt;
+        t.b0 = 0;
+        t.nb = t.rb;
+        t.dst_row = at;
+    };
+    auto f32 = [&](int buf, int64_t n) {
+        t.buf = buf;
+        t.type = ABRA_GGML_F32;
+        t.N = 1;
+        t.K = n;
+        t.rb = t.nb = n * 4;
+        t.r0 = t.b0 = t.dst_row = 0;
+        t.nr = 1;
+    };
+    if (layer == -1) {
+        if (slot == ABRA_TENSOR_TOKEN_EMBD)
+            rows(BUF_EMBD, mix ? ABRA_GGML_Q6_K : ABRA_GGML_Q4_K, c.vocab, c.hidden, 0, c.vocab, 0);
+        else if (slot == ABRA_TENSOR_OUTPUT_NORM)
+            f32(BUF_OUT_NORM, c.hidden);
+        else
+            return ABRA_E_INVALID;
+        return ABRA_OK;
+    }
+    if (layer < 0 || layer >= c.n_layers) return ABRA_E_INVALID;
+    const bool q6 = mix && q6k_layer(layer, c.n_layers);
+    switch (slot) {
+        case ABRA_TENSOR_ATTN_NORM: f32(BUF_ATTN_NORM, c.hidden); break;
+        case ABRA_TENSOR_FFN_NORM: f32(BUF_FFN_NORM, c.hidden); break;
+        case ABRA_TENSOR_ATTN_Q_NORM: f32(BUF_Q_NORM, hd); break;
+        case ABRA_TENSOR_ATTN_K_NORM: f32(BUF_K_NORM, hd); break;
+        case ABRA_TENSOR_ATTN_Q:
+            rows(BUF_WQKV, ABRA_GGML_Q4_K, qd, c.hidden, sh.q_head_lo * hd, qd_l, 0);
+            break;
+        case ABRA_TENSOR_ATTN_K:
+            rows(BUF_WQKV, ABRA_GGML_Q4_K, kvd, c.hidden, sh.kv_head_lo * hd, kvd_l, qd_l);
+            break;
+        case ABRA_TENSOR_ATTN_V:
+            if (q6)
+                rows(BUF_WV, ABRA_GGML_Q6_K, kvd, c.hidden, sh.kv_head_lo * hd, kvd_l, 0);
+            else
+                rows(BUF_WQKV, ABRA_GGML_Q4_K, kvd, c.hidden, sh.kv_head_lo * hd, kvd_l, qd_l + kvd_l);
+            break;
+        case ABRA_TENSOR_ATTN_OUTPUT:  // this rank's canonical K-slices of every row
+            rows(BUF_WO, ABRA_GGML_Q4_K, c.hidden, qd, 0, c.hidden, 0);
+            t.b0 = slice_start(nsb_o, sh.sl_base) * Q4K_BYTES;
+            t.nb = slice_start(nsb_o, sh.sl_base + sh.sl_cnt) * Q4K_BYTES - t.b0;
+            break;
+        case ABRA_TENSOR_FFN_GATE:
+        case ABRA_TENSOR_FFN_UP:
+            rows(slot == ABRA_TENSOR_FFN_GATE ? BUF_WGATE : BUF_WUP, ABRA_GGML_Q4_K, c.ffn, c.hidden,
+                 sh.ffn_lo, sh.ffn_hi - sh.ffn_lo, 0);
+            break;
+        case ABRA_TENSOR_FFN_DOWN: {
+            const int type = q6 ? ABRA_GGML_Q6_K : ABRA_GGML_Q4_K;
+            rows(BUF_WDOWN, type, c.hidden, c.ffn, 0, c.hidden, 0);
+            t.b0 = sh.ffn_lo / QK_K * block(type);
+            t.nb = (sh.ffn_hi - sh.ffn_lo) / QK_K * block(type);
+            break;
+        }
+        default: return ABRA_E_INVALID;
+    }
+    return ABRA_OK;
+}
+
 // Local MMVQ shapes of one rank: {N, K, nmat, fused RMSNorm input}; qk is
 // the q|k-only fused MMVQ of a Q6_K-V layer, v its Q6_K V rows.
 struct StepShapes {
@@ -1188,94 +1284,51 @@ int abra_model_load_tensor(void *model, int32_t layer, int32_t slot, int32_t ggm
     Model *m = static_cast<Model *>(model);
     if (!m || !host) return model_fail(ABRA_E_INVALID, "null pointer", cudaSuccess);
     if (m->batch > 1) return model_fail(ABRA_E_UNSUPPORTED, "load into a batch-1 model", cudaSuccess);
-    const abra_model_config &c = m->cfg;
-    const abra_tp_shard &sh = m->sh;
-    const int64_t hd = c.head_dim, qd = static_cast<int64_t>(c.n_heads) * hd;
-    const int64_t kvd = static_cast<int64_t>(c.n_kv_heads) * hd;
-    const int64_t qd_l = sh.q_heads * hd, kvd_l = sh.kv_heads * hd;
-    const int64_t nsb_o = qd / abra::QK_K;
-    const int64_t row_h = static_cast<int64_t>(abra::q4k_bytes(1, c.hidden));
-    // the destination: dst <- rows [r0, r0 + nr) of an N x K tensor of type t
-    // (row bytes rb), each row's bytes [b0, b0 + nb) (nb == rb: whole rows)
-    void *dst = nullptr;
-    int want_type = ABRA_GGML_Q4_K;
-    int64_t N = 0, K = 0, r0 = 0, nr = 0, b0 = 0, nb = 0, rb = 0;
-    auto block = [&](int type) { return type == ABRA_GGML_Q6_K ? 210 : abra::Q4K_BYTES; };
-    auto rows = [&](void *d, int type, int64_t n, int64_t k, int64_t lo, int64_t cnt) {
-        dst = d;
-        want_type = type;
-        N = n;
-        K = k;
-        rb = k / abra::QK_K * block(type);
-        r0 = lo;
-        nr = cnt;
-        b0 = 0;
-        nb = rb;
-    };
-    auto f32 = [&](float *d, int64_t n) {
-        dst = d;
-        want_type = ABRA_GGML_F32;
-        N = 1;
-        K = n;
-        rb = nb = n * 4;
-        r0 = b0 = 0;
-        nr = 1;
-    };
-    const bool in_layer = layer >= 0 && layer < c.n_layers;
-    if (layer == -1 && slot == ABRA_TENSOR_TOKEN_EMBD) {
-        rows(m->embd, m->mix ? ABRA_GGML_Q6_K : ABRA_GGML_Q4_K, c.vocab, c.hidden, 0, c.vocab);
-    } else if (layer == -1 && slot == ABRA_TENSOR_OUTPUT_NORM) {
-        f32(m->out_norm, c.hidden);
-    } else if (in_layer) {
+    abra::TensorSlice t;
+    if (abra::tensor_slice(m->cfg, m->sh, m->mix, layer, slot, t) != ABRA_OK)
+        return model_fail(ABRA_E_INVALID, "unknown tensor (layer, slot)", cudaSuccess);
+    if (ggml_type != t.type)
+        return model_fail(ABRA_E_INVALID, "tensor type differs from the model's type for this slot", cudaSuccess);
+    if (bytes != static_cast<uint64_t>(t.N * t.rb))
+        return model_fail(ABRA_E_INVALID, "tensor size differs from the model's shape", cudaSuccess);
+    uint8_t *dst = nullptr;
+    if (layer == -1) {
+        dst = t.buf == abra::BUF_EMBD ? m->embd : reinterpret_cast<uint8_t *>(m->out_norm);
+    } else {
         abra::LayerW &y = m->layers[layer];
-        switch (slot) {
-            case ABRA_TENSOR_ATTN_NORM: f32(y.attn_norm, c.hidden); break;
-            case ABRA_TENSOR_FFN_NORM: f32(y.ffn_norm, c.hidden); break;
-            case ABRA_TENSOR_ATTN_Q_NORM: f32(y.q_norm, hd); break;
-            case ABRA_TENSOR_ATTN_K_NORM: f32(y.k_norm, hd); break;
-            case ABRA_TENSOR_ATTN_Q:
-                rows(y.wqkv, ABRA_GGML_Q4_K, qd, c.hidden, sh.q_head_lo * hd, qd_l);
-                break;
-            case ABRA_TENSOR_ATTN_K:
-                rows(y.wqkv + qd_l * row_h, ABRA_GGML_Q4_K, kvd, c.hidden, sh.kv_head_lo * hd, kvd_l);
-                break;
-            case ABRA_TENSOR_ATTN_V:
-                if (y.q6)
-                    rows(y.wv, ABRA_GGML_Q6_K, kvd, c.hidden, sh.kv_head_lo * hd, kvd_l);
-                else
-                    rows(y.wqkv + (qd_l + kvd_l) * row_h, ABRA_GGML_Q4_K, kvd, c.hidden,
-                         sh.kv_head_lo * hd, kvd_l);
-                break;
-            case ABRA_TENSOR_ATTN_OUTPUT:  // this rank's canonical K-slices of every row
-                rows(y.wo, ABRA_GGML_Q4_K, c.hidden, qd, 0, c.hidden);
-                b0 = abra::slice_start(static_cast<int>(nsb_o), sh.sl_base) * abra::Q4K_BYTES;
-                nb = abra::slice_start(static_cast<int>(nsb_o), sh.sl_base + sh.sl_cnt) * abra::Q4K_BYTES - b0;
-                break;
-            case ABRA_TENSOR_FFN_GATE:
-            case ABRA_TENSOR_FFN_UP:
-                rows(slot == ABRA_TENSOR_FFN_GATE ? y.wgate : y.wup, ABRA_GGML_Q4_K, c.ffn, c.hidden,
-                     sh.ffn_lo, sh.ffn_hi - sh.ffn_lo);
-                break;
-            case ABRA_TENSOR_FFN_DOWN: {
-                const int t = y.q6 ? ABRA_GGML_Q6_K : ABRA_GGML_Q4_K;
-                rows(y.wdown, t, c.hidden, c.ffn, 0, c.hidden);
-                b0 = sh.ffn_lo / abra::QK_K * block(t);
-                nb = (sh.ffn_hi - sh.ffn_lo) / abra::QK_K * block(t);
-                break;
-            }
+        switch (t.buf) {
+            case abra::BUF_ATTN_NORM: dst = reinterpret_cast<uint8_t *>(y.attn_norm); break;
+            case abra::BUF_FFN_NORM: dst = reinterpret_cast<uint8_t *>(y.ffn_norm); break;
+            case abra::BUF_Q_NORM: dst = reinterpret_cast<uint8_t *>(y.q_norm); break;
+            case abra::BUF_K_NORM: dst = reinterpret_cast<uint8_t *>(y.k_norm); break;
+            case abra::BUF_WQKV: dst = y.wqkv; break;
+            case abra::BUF_WV: dst = y.wv; break;
+            case abra::BUF_WO: dst = y.wo; break;
+            case abra::BUF_WGATE: dst = y.wgate; break;
+            case abra::BUF_WUP: dst = y.wup; break;
+            case abra::BUF_WDOWN: dst = y.wdown; break;
             default: return model_fail(ABRA_E_INVALID, "unknown tensor slot", cudaSuccess);
         }
-    } else {
-        return model_fail(ABRA_E_INVALID, "unknown tensor (layer, slot)", cudaSuccess);
     }
-    if (ggml_type != want_type)
-        return model_fail(ABRA_E_INVALID, "tensor type differs from the model's type for this slot", cudaSuccess);
-    if (bytes != static_cast<uint64_t>(N * rb))
-        return model_fail(ABRA_E_INVALID, "tensor size differs from the model's shape", cudaSuccess);
-    const uint8_t *src = static_cast<const uint8_t *>(host) + r0 * rb + b0;
-    cudaError_t e = cudaMemcpy2DAsync(dst, nb, src, rb, nb, nr, cudaMemcpyHostToDevice, m->stream);
+    dst += t.dst_row * t.nb;  // the rank's rows of the slot sit after dst_row others
+    const uint8_t *src = static_cast<const uint8_t *>(host) + t.r0 * t.rb + t.b0;
+    cudaError_t e = cudaMemcpy2DAsync(dst, t.nb, src, t.rb, t.nb, t.nr, cudaMemcpyHostToDevice, m->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
     return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "tensor upload", e);
+}
+
+int abra_tp_tensor_slice(const abra_model_config *cfg, int32_t rank, int32_t world, int32_t layer,
+                         int32_t slot, int64_t *out) {
+    if (!cfg || !out) return model_fail(ABRA_E_INVALID, "null pointer", cudaSuccess);
+    abra_tp_shard sh = {};
+    const int rc = abra::tp_shard(*cfg, rank, world, sh);
+    if (rc != ABRA_OK) return model_fail(rc, "no tensor-parallel split of this configuration", cudaSuccess);
+    abra::TensorSlice t;
+    if (abra::tensor_slice(*cfg, sh, (cfg->flags & ABRA_MODEL_Q4_K_M) != 0, layer, slot, t) != ABRA_OK)
+        return model_fail(ABRA_E_INVALID, "unknown tensor (layer, slot)", cudaSuccess);
+    const int64_t v[8] = {t.type, t.N, t.K, t.rb, t.r0, t.nr, t.b0, t.nb};
+    std::memcpy(out, v, sizeof v);
+    return ABRA_OK;
 }
 
 int abra_model_info(void *model, void **stream, uint64_t *weight_bytes, uint64_t *kv_bytes) {

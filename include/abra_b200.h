@@ -331,6 +331,12 @@ int abra_model_info(void *model, void **stream, uint64_t *weight_bytes, uint64_t
  * (parser: tools/extract-qwen3-tensor-map.py:15-141).  Batch-1 models. */
 int abra_model_load_tensor(void *model, int32_t layer, int32_t slot, int32_t ggml_type,
                            const void *host, uint64_t bytes);
+/* What rank `rank` of `world` keeps of a slot's tensor (host only):
+ * out[8] = {ggml type, N rows, K, bytes per row, first row, rows, first byte
+ * of each row, bytes of each row} -- whole rows of its heads / FFN units, or
+ * its canonical K-slices of every row (o, down). */
+int abra_tp_tensor_slice(const abra_model_config *cfg, int32_t rank, int32_t world, int32_t layer,
+                         int32_t slot, int64_t *out);
 const char *abra_model_last_error(void);
 
 /* ------------------------------------------------- batched decode --- */

@@ -103,3 +103,72 @@ def test_handle_exchange_gloo_two_ranks(tmp_path):
         d = np.load(tmp_path / f"rank{r}.npz")
         assert d["handles"].tobytes() == want
         assert d["vocab"].tolist() == [[0, 75968], [75968, 151936]]
+
+
+def _slice(cfg, rank, world, layer, slot):
+    import ctypes as C
+
+    from abra_b200 import _lib
+
+    out = (C.c_int64 * 8)()
+    rc = _lib.lib.abra_tp_tensor_slice(C.byref(cfg), rank, world, layer, slot, out)
+    assert rc == _lib.ABRA_OK, _lib.lib.abra_model_last_error()
+    return dict(zip(("type", "N", "K", "rb", "r0", "nr", "b0", "nb"), list(out)))
+
+
+ROW_SPLIT = {1: "q", 9: "k", 10: "v", 6: "gate", 7: "up"}
+K_SPLIT = {4: "o", 8: "down"}
+WHOLE = {0: "attn_norm", 2: "q_norm", 3: "k_norm", 5: "ffn_norm"}
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_gguf_tensor_slices_tile_every_tensor(world):
+    """What each rank keeps of a GGUF tensor (abra_model_load_tensor's cut):
+    row-split tensors partition the rows, K-split ones each row's bytes
+    along the canonical slices, the rest are whole on every rank -- the same
+    placement as the seeded weights (heads, FFN units, K-slices)."""
+    from abra_b200.model import default_config, shard_info
+
+    cfg = default_config()
+    for layer, slots in ((-1, {1: "embd", 2: "out_norm"}), (0, {**ROW_SPLIT, **K_SPLIT, **WHOLE}),
+                         (35, {**ROW_SPLIT, **K_SPLIT})):
+        for slot, name in slots.items():
+            sl = [_slice(cfg, r, world, layer, slot) for r in range(world)]
+            assert len({(s["type"], s["N"], s["K"], s["rb"]) for s in sl}) == 1, name
+            N, rb = sl[0]["N"], sl[0]["rb"]
+            if slot in ROW_SPLIT and layer >= 0:
+                spans = sorted((s["r0"], s["r0"] + s["nr"]) for s in sl)
+                assert spans[0][0] == 0 and spans[-1][1] == N, name
+                assert all(a[1] == b[0] for a, b in zip(spans, spans[1:])), name
+                assert all(s["b0"] == 0 and s["nb"] == rb for s in sl)
+            elif slot in K_SPLIT and layer >= 0:
+                spans = sorted((s["b0"], s["b0"] + s["nb"]) for s in sl)
+                assert spans[0][0] == 0 and spans[-1][1] == rb, name
+                assert all(a[1] == b[0] for a, b in zip(spans, spans[1:])), name
+                assert all(s["r0"] == 0 and s["nr"] == N for s in sl)
+            else:
+                assert all((s["r0"], s["nr"], s["b0"], s["nb"]) == (0, N, 0, rb) for s in sl), name
+        for r in range(world):
+            sh = shard_info(r, world)
+            q = _slice(cfg, r, world, 0, 1)
+            assert (q["r0"], q["nr"]) == (sh.q_head_lo * 128, sh.q_heads * 128)
+            g = _slice(cfg, r, world, 0, 6)
+            assert (g["r0"], g["r0"] + g["nr"]) == (sh.ffn_lo, sh.ffn_hi)
+            d = _slice(cfg, r, world, 0, 8)
+            assert (d["b0"] // 144 * 256, (d["b0"] + d["nb"]) // 144 * 256) == (sh.ffn_lo, sh.ffn_hi)
+            o = _slice(cfg, r, world, 0, 4)
+            nsb_o = 4096 // 256
+            assert o["b0"] // 144 == O.slice_starts(nsb_o)[sh.sl_base]
+
+
+def test_gguf_tensor_slices_of_the_q4_k_m_map():
+    from abra_b200.model import Q4_K_M, default_config, q6k_layers
+
+    cfg = default_config(flags=Q4_K_M)
+    q6 = set(q6k_layers(36))
+    assert _slice(cfg, 0, 1, -1, 1)["type"] == 14
+    for layer in range(36):
+        assert _slice(cfg, 0, 1, layer, 10)["type"] == (14 if layer in q6 else 12)
+        assert _slice(cfg, 0, 1, layer, 8)["type"] == (14 if layer in q6 else 12)
+        assert _slice(cfg, 0, 1, layer, 1)["type"] == 12
+    assert _slice(cfg, 0, 1, 0, 8)["rb"] == 9728 // 256 * 210
