@@ -1,7 +1,7 @@
 """CPU oracle of the Q4_K x Q8_1 decode path -- TEST INFRASTRUCTURE ONLY.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
-package, and only as the checker (or the timed CPU restatement); the product
+package, and only as the reference result (or the timed CPU restatement); the product
 library never imports it.
 
 ``liborc.so`` (q4k_oracle.c) restates the reference's arithmetic in C:

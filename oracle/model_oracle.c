@@ -1,7 +1,7 @@
 /*
  * model_oracle.c -- CPU oracle of the Qwen3-4B-shaped Q4_K (or Q4_K_M) decode step.
  *
- * TEST INFRASTRUCTURE ONLY (checker for tests/ and the smoke entry).  It
+ * TEST INFRASTRUCTURE ONLY (the reference result for tests/ and the smoke entry).  It
  * evaluates the same random-init model as abra_b200's decode runtime, every
  * operation in the same fp32 order as the CUDA kernels, so greedy tokens and
  * logits can be compared bit for bit.  Compiled with -ffp-contract=off.

@@ -1,7 +1,7 @@
 /*
  * q4k_oracle.h -- CPU oracle for the Q4_K x Q8_1 decode path.
  *
- * TEST INFRASTRUCTURE ONLY.  This is the checker: tests/, the smoke entry
+ * TEST INFRASTRUCTURE ONLY.  This is the test oracle: tests/, the smoke entry
  * and the CPU-baseline leg of bench.py call it; the product library never
  * links or calls it.  It restates, in plain C, the arithmetic of the
  * reference (talystalys/abra):

@@ -2,7 +2,7 @@
  * q6k_oracle.h -- CPU oracle for the Q6_K x Q8_1 MMVQ.
  *
  * TEST INFRASTRUCTURE ONLY: tests/ and bench.py's CPU leg call it as the
- * checker; the product library never links or calls it.  Restates the
+ * reference result; the product library never links or calls it.  Restates the
  * reference (talystalys/abra):
  *   - Q6_K leg of the MMVQ dispatch   kernels/q4k/abra-mmvq.cuh:138-141
  *   - f64 Q6_K oracle                 tests/runtime_kernel_test.cu:82-106

@@ -1,7 +1,7 @@
 // ref_shim.cu -- glue that lets the reference's own Q4_K kernel family be
 // compiled here, unmodified, into oracle/_ref/libq4k_ref.so.
 //
-// TEST INFRASTRUCTURE ONLY: the reference's kernels run as a checker and as a
+// TEST INFRASTRUCTURE ONLY: the reference's kernels run as a reference result and as a
 // timing comparison, never as part of libabra_b200.
 //
 // The reference's kernels/q4k/q4k_q8_mmvq.cu and q4k_family.cu are compiled
