@@ -44,6 +44,12 @@ const char *abra_last_error(void);
  * mbarrier wait, bit 1: a cross-rank flag wait).  clear != 0 resets it.
  * Synchronises the current device. */
 int abra_device_error(uint32_t *out, int32_t clear);
+/* Failure detection without a fault: waits on a device counter that nothing
+ * increments with the bounded cross-rank wait of the tensor-parallel kernels;
+ * returns the error bits it raised (bit 1: a flag wait gave up; then cleared)
+ * and how long the wait ran (about one second).  The context stays usable.
+ * Synchronous; allocates 16 bytes of device memory. */
+int abra_test_flag_timeout(uint32_t *error_bits, uint64_t *waited_ns);
 
 /* ------------------------------------------------------------- MMVQ ---- */
 /* y = W x for Q4_K W (N x K) and ncols Q8_1 columns, 1 <= ncols <= 8,
