@@ -233,6 +233,9 @@ int abra_rmsnorm_quantize_q8_1(const float *x, const float *w, float eps, void *
     if (K <= 0 || K % 32 != 0 || K > 16384)
         return fail(ABRA_E_INVALID, "K must be a multiple of 32 in 32..16384 (K=%lld)", (long long)K);
     if (ncols < 1) return fail(ABRA_E_INVALID, "ncols must be >= 1");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+         reinterpret_cast<uintptr_t>(xq) | reinterpret_cast<uintptr_t>(xn_out)) & 3u)
+        return fail(ABRA_E_INVALID, "x, w, x_q8_1 and xn_out must be 4-byte aligned");
     cudaError_t e = abra::launch_rmsnorm_quantize_q8_1(x, w, eps, xq, xn_out, K, ncols,
                                                        static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
@@ -252,6 +255,7 @@ int abra_gen_q4k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
 int abra_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_t tensor_id,
                          int64_t offset_index, float scale, float offset, void *stream) {
     if (!dst || n < 0 || offset_index < 0) return fail(ABRA_E_INVALID, "bad generator arguments");
+    if (reinterpret_cast<uintptr_t>(dst) & 3u) return fail(ABRA_E_INVALID, "dst must be 4-byte aligned");
     cudaError_t e = abra::launch_gen_uniform_f32(dst, n, seed, tensor_id, offset_index, scale,
                                                  offset, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "gen_uniform launch");

@@ -982,7 +982,10 @@ int abra_model_reset_batched(void *model, const int32_t *prompts, int32_t n_prom
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, &zero, 4, cudaMemcpyHostToDevice, m->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->nprompt, &n_prompt, 4, cudaMemcpyHostToDevice, m->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
-    if (e == cudaSuccess) m->host_pos = 0;
+    if (e == cudaSuccess) {
+        m->host_pos = 0;
+        m->host_nprompt = n_prompt;
+    }
     return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "reset", e);
 }
 

@@ -74,6 +74,11 @@ def test_rejects_bad_arguments_without_gpu():
     assert lib.abra_q4k_mmvq_combined(0, 16, None, 16, 16, 8, 256, 1, None) == _lib.ABRA_E_INVALID
     assert lib.abra_q4k_mmvq_combined(0, 16, 16, 16, 16, 8, 300, 1, None) == _lib.ABRA_E_INVALID
     assert lib.abra_rmsnorm_quantize_q8_1(16, 16, 1e-6, 16, None, 32768, 1, None) == _lib.ABRA_E_INVALID
+    assert lib.abra_rmsnorm_quantize_q8_1(16, 18, 1e-6, 16, None, 2560, 1, None) == _lib.ABRA_E_INVALID
+    assert "4-byte" in _lib.last_error()
+    assert lib.abra_rmsnorm_quantize_q8_1(16, 16, 1e-6, 16, 34, 2560, 1, None) == _lib.ABRA_E_INVALID
+    assert lib.abra_gen_uniform_f32(18, 8, 0, 0, 0, 1.0, 0.0, None) == _lib.ABRA_E_INVALID
+    assert "4-byte" in _lib.last_error()
     with pytest.raises(ValueError):
         A.launch_quantize_f32_to_q8_1(16, 16, 33)
     with pytest.raises(ValueError):
