@@ -57,6 +57,8 @@ def q6k_layers(n_layers: int) -> list[int]:
     (llama.cpp's use_more_bits: l < n/8, l >= 7n/8 or (l - n/8) % 3 == 2)."""
     a, b = n_layers // 8, 7 * n_layers // 8
     return [l for l in range(n_layers) if l < a or l >= b or (l - a) % 3 == 2]
+
+
 IPC_HANDLE_BYTES = 64
 
 
