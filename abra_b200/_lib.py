@@ -56,6 +56,8 @@ SIGNATURES: dict[str, tuple] = {
     "abra_q6k_candidate_info": (C.c_int, [_i32] + [C.POINTER(C.c_int32)] * 5),
     "abra_q6k_tune_set": (C.c_int, [_i64, _i64, _i32, _i32]),
     "abra_q6k_tune_get": (C.c_int, [_i64, _i64, _i32]),
+    "abra_mmvq_plan_info": (C.c_int, [_i32, _i32, _i64, _i64, _i32, _i32, _i32, _i64, _i32, _i32,
+                                      _i32, _vp]),
     # decode model
     "abra_model_default_config": (C.c_int, [_vp]),
     "abra_model_create": (C.c_int, [_vp, C.POINTER(C.c_void_p)]),

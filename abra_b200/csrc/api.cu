@@ -371,6 +371,45 @@ int abra_q6k_tune_get(int64_t N, int64_t K, int32_t ncols) {
     return abra::q6k_default_candidate(N, K, ncols);
 }
 
+int abra_mmvq_plan_info(int32_t ggml_type, int32_t candidate, int64_t N, int64_t K, int32_t ncols,
+                        int32_t nmat, int32_t xin, int64_t K_full, int32_t sl_base, int32_t sl_cnt,
+                        int32_t sm_count, int64_t *out) {
+    if (!out) return fail(ABRA_E_INVALID, "null pointer");
+    if (ggml_type != ABRA_GGML_Q4_K && ggml_type != ABRA_GGML_Q6_K)
+        return fail(ABRA_E_INVALID, "ggml_type must be Q4_K (12) or Q6_K (14)");
+    if (N <= 0 || K <= 0 || K % 256 != 0 || K > 65536 || N > (int64_t)0x7fffffff - 8)
+        return fail(ABRA_E_INVALID, "bad shape N=%lld K=%lld", (long long)N, (long long)K);
+    if (ncols < 1 || ncols > 8) return fail(ABRA_E_UNSUPPORTED, "ncols must be in 1..8 (got %d)", ncols);
+    if (nmat != 1 && !(nmat == 2 && ggml_type == ABRA_GGML_Q4_K))
+        return fail(ABRA_E_INVALID, "nmat must be 1 (or 2 for the Q4_K gate/up form)");
+    if (xin && (ggml_type != ABRA_GGML_Q4_K || ncols != 1))
+        return fail(ABRA_E_INVALID, "the fused RMSNorm prologue is Q4_K at batch 1");
+    if (sm_count < 0) return fail(ABRA_E_INVALID, "sm_count must be >= 0");
+    abra::MmvqOpts tp;
+    const abra::MmvqOpts *ptp = nullptr;
+    if (K_full > 0) {
+        if (K_full % 256 != 0 || K_full > 65536 || sl_base < 0 ||
+            !(sl_cnt == 1 || sl_cnt == 2 || sl_cnt == 4 || sl_cnt == 8) || sl_base + sl_cnt > 8)
+            return fail(ABRA_E_INVALID, "bad K-shard (K_full=%lld sl_base=%d sl_cnt=%d)",
+                        (long long)K_full, sl_base, sl_cnt);
+        tp.sl_nsb = static_cast<int>(K_full / 256);
+        tp.sl_base = sl_base;
+        tp.sl_cnt = sl_cnt;
+        ptp = &tp;
+    }
+    const bool q6 = ggml_type == ABRA_GGML_Q6_K;
+    int id = candidate;
+    if (id == 0) id = q6 ? abra_q6k_tune_get(N, K, ncols) : abra_tune_get(N, K, ncols, nmat);
+    const abra::MmvqConfig *cfg = q6 ? abra::q6k_candidate_by_id(id) : abra::mmvq_candidate_by_id(id);
+    if (!cfg) return fail(ABRA_E_INVALID, "unknown candidate id %d", id);
+    const bool ok = q6 ? abra::q6k_plan_info(*cfg, N, K, ncols, ptp, sm_count, out)
+                       : abra::mmvq_plan_info(*cfg, N, K, ncols, nmat, xin != 0, ptp, sm_count, out);
+    if (!ok)
+        return fail(ABRA_E_UNSUPPORTED, "candidate %d has no plan for N=%lld K=%lld ncols=%d", id,
+                    (long long)N, (long long)K, ncols);
+    return ABRA_OK;
+}
+
 int abra_candidate_count(void) {
     int n = 0;
     abra::mmvq_candidates(&n);

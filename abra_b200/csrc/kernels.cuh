@@ -115,6 +115,15 @@ cudaError_t launch_gen_uniform_f32(float *dst, int64_t n, uint64_t seed, uint64_
 
 int device_sm_count();
 
+// Launch plan of a Q4_K or Q6_K MMVQ on a GPU with `sms` SMs (0: this
+// device's), for host-side checks of what the kernel will address: out =
+// {grid, block, nstage, pitch, stage bytes, dynamic shared memory, row
+// groups, offset of the stage ring in shared memory}.  False when no plan fits.
+bool mmvq_plan_info(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, bool xin,
+                    const MmvqOpts *tp, int sms, int64_t out[8]);
+bool q6k_plan_info(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, const MmvqOpts *tp,
+                   int sms, int64_t out[8]);
+
 // Dynamic shared memory an MMVQ plan may use (the 227 KiB opt-in limit less
 // room for static shared memory), and the attribute that allows it, set once
 // per (kernel, device).

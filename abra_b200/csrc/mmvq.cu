@@ -121,8 +121,9 @@ bool mmvq_shard_of(const MmvqOpts *tp, int nsb, int &sl_nsb, int &sl_base, int &
     return shard_slice(sl_nsb, sl_base, sl_shift, 8) == nsb;
 }
 
+// sms: the SM count to plan for (0: this device's).
 static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int nmat,
-                      MmvqPlan &pl, bool xin = false, const MmvqOpts *tp = nullptr) {
+                      MmvqPlan &pl, bool xin = false, const MmvqOpts *tp = nullptr, int sms = 0) {
     const int ks = cfg.ks;
     const bool staged = cfg.mode != MODE_DIRECT;
     const int nsl = 8 / ks;
@@ -139,7 +140,7 @@ static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int 
     if (cfg.mode == MODE_TMA_ROWS && ((pitch / 16) & 1) == 0) pitch += 16;
     pl.pitch = pitch;
     pl.rg_total = static_cast<int>((N + 7) / 8);
-    const int sms = device_sm_count();
+    if (sms <= 0) sms = device_sm_count();
     pl.grid = pl.rg_total < sms * cfg.ctas_per_sm ? pl.rg_total : sms * cfg.ctas_per_sm;
     pl.block = (ABRA_MMVQ_NCW + (staged ? 1 : 0)) * 32;
     // Ring depth.  Unit u is consumed by warp u % NCW and lands in stage
@@ -252,6 +253,20 @@ int mmvq_grid(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, 
     MmvqPlan pl;
     if (!plan_mmvq(cfg, N, static_cast<int>(K / QK_K), ncols, nmat, pl, xin, tp)) return -1;
     return pl.grid;
+}
+
+bool mmvq_plan_info(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, bool xin,
+                    const MmvqOpts *tp, int sms, int64_t out[8]) {
+    MmvqPlan pl;
+    const int nsb = static_cast<int>(K / QK_K);
+    if (!plan_mmvq(cfg, N, nsb, ncols, nmat, pl, xin, tp, sms)) return false;
+    const bool staged = cfg.mode != MODE_DIRECT;
+    const MmvqLayout L = mmvq_layout(ncols, cfg.ks, ABRA_MMVQ_NCW, nsb, pl.nstage, pl.pitch, nmat,
+                                     staged, xin);
+    const int64_t v[8] = {pl.grid, pl.block, pl.nstage, pl.pitch, staged ? 8 * nmat * pl.pitch : 0,
+                          pl.smem, pl.rg_total, L.off_stage};
+    for (int i = 0; i < 8; ++i) out[i] = v[i];
+    return true;
 }
 
 cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void *w2,

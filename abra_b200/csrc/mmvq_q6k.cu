@@ -65,8 +65,9 @@ struct Q6Plan {
     int grid, block, nstage, pitch, stage_bytes, smem, rg_total;
 };
 
+// sms: the SM count to plan for (0: this device's).
 static bool plan_q6(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, const MmvqOpts *tp,
-                    Q6Plan &pl) {
+                    Q6Plan &pl, int sms = 0) {
     const int ks = cfg.ks;
     const bool staged = cfg.mode != Q6_DIRECT;
     if (cfg.mode == Q6_WHOLE && ks != 1) return false;
@@ -88,7 +89,7 @@ static bool plan_q6(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, const 
     pl.pitch = pitch;
     pl.stage_bytes = stage_bytes;
     pl.rg_total = static_cast<int>((N + 7) / 8);
-    const int sms = device_sm_count();
+    if (sms <= 0) sms = device_sm_count();
     pl.grid = pl.rg_total < sms * cfg.ctas_per_sm ? pl.rg_total : sms * cfg.ctas_per_sm;
     pl.block = (ABRA_Q6_NCW + (staged ? 1 : 0)) * 32;
     // Ring depth: every unit of a CTA has its own stage, or nstage is a
@@ -116,6 +117,19 @@ static bool plan_q6(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, const 
         if (next < W) return false;
         nstage = next;
     }
+}
+
+bool q6k_plan_info(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, const MmvqOpts *tp,
+                   int sms, int64_t out[8]) {
+    Q6Plan pl;
+    const int nsb = static_cast<int>(K / QK_K);
+    if (!plan_q6(cfg, N, nsb, ncols, tp, pl, sms)) return false;
+    const bool staged = cfg.mode != Q6_DIRECT;
+    const Q6Layout L = q6_layout(ncols, cfg.ks, ABRA_Q6_NCW, nsb, pl.nstage, pl.stage_bytes, staged);
+    const int64_t v[8] = {pl.grid, pl.block, pl.nstage, pl.pitch, staged ? pl.stage_bytes : 0,
+                          pl.smem, pl.rg_total, L.off_stage};
+    for (int i = 0; i < 8; ++i) out[i] = v[i];
+    return true;
 }
 
 static cudaError_t launch_q6_plan(Q6Fn fn, const Q6Plan &pl, bool pdl, Q6Params prm,

@@ -220,6 +220,21 @@ int abra_q6k_candidate_info(int32_t index, int32_t *id, int32_t *mode, int32_t *
 int abra_q6k_tune_set(int64_t N, int64_t K, int32_t ncols, int32_t candidate);
 int abra_q6k_tune_get(int64_t N, int64_t K, int32_t ncols);
 
+/* Launch plan of one MMVQ call, computed on the host exactly as the dispatch
+ * computes it, for a GPU with sm_count SMs (0: the current device's): no
+ * device call when sm_count > 0.  ggml_type ABRA_GGML_Q4_K (nmat 1, or 2 for
+ * the fused gate/up form; xin 1 for the fused RMSNorm prologue of the decode
+ * runtime, batch 1) or ABRA_GGML_Q6_K (nmat 1, xin 0); candidate 0 = tuned;
+ * K_full > 0 names a K-shard as in the _kshard calls.  out[8] = grid, threads
+ * per CTA, ring depth, per-row stage pitch, bytes per stage, dynamic shared
+ * memory, row groups of 8, offset of the stage ring in shared memory: what a
+ * host-side check needs to follow every address the kernel's copies form.
+ * The reference has no counterpart (its launch geometry is fixed per
+ * candidate, kernels/q4k/q4k_family.cu:12-110). */
+int abra_mmvq_plan_info(int32_t ggml_type, int32_t candidate, int64_t N, int64_t K, int32_t ncols,
+                        int32_t nmat, int32_t xin, int64_t K_full, int32_t sl_base, int32_t sl_cnt,
+                        int32_t sm_count, int64_t *out);
+
 /* ------------------------------------------------------ decode model --- */
 /* Qwen3-4B-shaped decode with every linear layer Q4_K:
  * the native runtime that the reference delegates to llama.cpp.  Weights
