@@ -106,6 +106,31 @@ def test_full_qwen3_4b_shape_greedy_bit_exact(centered):
     c.close()
 
 
+def test_full_qwen3_4b_tg128_greedy_tokens_identical():
+    """The decode bar at the benchmark's length: the full 36-layer shape, a
+    16-token prompt, tg128 -- the 128 greedy token ids equal the CPU oracle's,
+    and the logits of the last step are bit-identical."""
+    cfg = dict(max_ctx=160, centered=1, seed=0)
+    g, c = _pair(**cfg)
+    prompt = _prompt(16, 151936, 9)
+    got = g.generate(prompt, 128)
+    last = g.logits()
+    want, tok = [], None
+    for pos in range(16 + 127):
+        feed = int(prompt[pos]) if pos < 16 else tok
+        if pos == 16 + 126:
+            tok, want_logits = c.step(feed, pos, logits=True)
+        else:
+            tok = c.step(feed, pos)
+        if pos >= 15:
+            want.append(tok)
+    assert np.array_equal(got, np.array(want, dtype=np.int32))
+    assert np.array_equal(last.view(np.uint32), want_logits.view(np.uint32))
+    assert len(set(want)) > 8, "the centred model should not collapse to a few tokens"
+    g.close()
+    c.close()
+
+
 def _mix_pair(**cfg):
     from abra_b200.model import Q4_K_M, DecodeModel
 
