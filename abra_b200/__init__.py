@@ -32,6 +32,7 @@ from .q4k import (
     mmvq,
     mmvq_kshard,
     mmvq_partials,
+    mmvq_rmsnorm,
     mmvq_swiglu,
     mmvq_tc,
     q4k_nbytes,

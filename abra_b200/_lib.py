@@ -56,6 +56,8 @@ SIGNATURES: dict[str, tuple] = {
     "abra_q6k_candidate_info": (C.c_int, [_i32] + [C.POINTER(C.c_int32)] * 5),
     "abra_q6k_tune_set": (C.c_int, [_i64, _i64, _i32, _i32]),
     "abra_q6k_tune_get": (C.c_int, [_i64, _i64, _i32]),
+    "abra_q4k_mmvq_rmsnorm": (C.c_int, [_vp, _vp, _fp, _fp, _f32, _fp, _vp, _i64, _i64, _i32, _i32,
+                                        _vp]),
     "abra_mmvq_plan_info": (C.c_int, [_i32, _i32, _i64, _i64, _i32, _i32, _i32, _i64, _i32, _i32,
                                       _i32, _vp]),
     # decode model

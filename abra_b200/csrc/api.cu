@@ -242,6 +242,39 @@ int abra_rmsnorm_quantize_q8_1(const float *x, const float *w, float eps, void *
     return ABRA_OK;
 }
 
+int abra_q4k_mmvq_rmsnorm(const void *w, const void *w_up, const float *x, const float *norm_w,
+                          float eps, float *y, void *x_q8_out, int64_t N, int64_t K,
+                          int32_t candidate, int32_t flags, void *stream) {
+    if (!w || !x || !norm_w || !y) return fail(ABRA_E_INVALID, "null pointer");
+    if (N <= 0 || K <= 0) return fail(ABRA_E_INVALID, "N and K must be positive (N=%lld K=%lld)", (long long)N, (long long)K);
+    if (K % 256 != 0) return fail(ABRA_E_INVALID, "K must be a multiple of QK_K=256 (K=%lld)", (long long)K);
+    if (K > 16384) return fail(ABRA_E_UNSUPPORTED, "K=%lld too large for the fused RMSNorm (max 16384)", (long long)K);
+    if (N > (int64_t)0x7fffffff - 8) return fail(ABRA_E_UNSUPPORTED, "N=%lld too large", (long long)N);
+    if (!aligned16(w) || (w_up && !aligned16(w_up)) || !aligned16(norm_w))
+        return fail(ABRA_E_INVALID, "weights and norm weights must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+         reinterpret_cast<uintptr_t>(x_q8_out)) & 3u)
+        return fail(ABRA_E_INVALID, "x, y and x_q8_out must be 4-byte aligned");
+    const int nmat = w_up ? 2 : 1;
+    int id = candidate;
+    if (id == 0) id = abra_tune_get(N, K, 1, nmat);
+    const abra::MmvqConfig *cfg = abra::mmvq_candidate_by_id(id);
+    if (!cfg) return fail(ABRA_E_INVALID, "unknown candidate id %d", id);
+    abra::MmvqXin xin = {};
+    xin.h_in = x;
+    xin.norm_w = norm_w;
+    xin.eps = eps;
+    xin.x_out = static_cast<uint8_t *>(x_q8_out);
+    cudaError_t e = abra::launch_mmvq_q4k_xin(*cfg, w, w_up, xin, y, N, K,
+                                              (flags & ABRA_MMVQ_PDL) ? abra::MMVQ_PDL : 0,
+                                              static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidConfiguration)
+        return fail(ABRA_E_UNSUPPORTED, "candidate %d has no fused-RMSNorm plan for N=%lld K=%lld", id,
+                    (long long)N, (long long)K);
+    if (e != cudaSuccess) return cuda_fail(e, "fused rmsnorm mmvq launch");
+    return ABRA_OK;
+}
+
 int abra_gen_q4k(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
                  int64_t block_offset, void *stream) {
     if (!dst || nblocks < 0 || block_offset < 0) return fail(ABRA_E_INVALID, "bad generator arguments");

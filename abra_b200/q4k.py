@@ -187,6 +187,17 @@ def mmvq_swiglu(d_w_gate, d_w_up, d_x, d_y, N: int, K: int, ncols: int = 1,
          stream_handle(stream))
 
 
+def mmvq_rmsnorm(d_w, d_x, d_norm_w, eps: float, d_y, N: int, K: int, d_w_up=None,
+                 d_x_q8_out=None, candidate: int = 0, pdl: bool = False, stream=None) -> None:
+    """y = W Q8_1(RMSNorm(x) * norm_w) at batch 1 with the normalization and
+    the quantization in each CTA's prologue (abra_q4k_mmvq_rmsnorm); with
+    d_w_up the fused gate/up SwiGLU.  Bit-identical to rmsnorm_quantize_q8_1
+    followed by mmvq / mmvq_swiglu."""
+    _check_k(K)
+    call("abra_q4k_mmvq_rmsnorm", ptr(d_w), ptr(d_w_up), ptr(d_x), ptr(d_norm_w), eps, ptr(d_y),
+         ptr(d_x_q8_out), N, K, candidate, _lib.ABRA_MMVQ_PDL if pdl else 0, stream_handle(stream))
+
+
 def mmvq_kshard(d_w, d_x, d_y, N: int, K: int, K_full: int, sl_base: int, sl_cnt: int,
                 ncols: int = 1, candidate: int = 0, pdl: bool = False, stream=None) -> None:
     """Row-parallel MMVQ over canonical K-slices [sl_base, sl_base + sl_cnt)

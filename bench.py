@@ -17,6 +17,7 @@ the full set on its own GPU: weak scaling, no collective).
 Also reported: every config-1 shape separately (q, k, v, o, gate, up, down,
 output), the reference's own kernel family on the same GPU over the
 unfused sweep, the sweep end to end through the C ABI with host buffers,
+the quantize-once RMSNorm -> Q8_1 block in three forms (fused_rmsnorm_block),
 and the CPU restatement of vec_dot_q4_K_q8_1 (oracle/, all host cores).
 
 ``--impl reference`` times that CPU restatement alone on a bounded sample of
@@ -713,6 +714,161 @@ def lookup_verification(torch, n_prompt: int = 16, blocks: int = 12, seed: int =
             "path": "abra_model_verify: 32-column tcgen05 pass with logits, host commit"}
 
 
+def _span(t, off: int, nbytes: int) -> int:
+    """Device address of bytes [off, off + nbytes) of tensor t, checked to lie
+    inside it (every pointer handed to a kernel below goes through here)."""
+    size = t.numel() * t.element_size()
+    assert 0 <= off and off + nbytes <= size, (off, nbytes, size)
+    return t.data_ptr() + off
+
+
+FB_K, FB_HQ, FB_HKV, FB_F = 2560, 4096, 1024, 9728
+FB_NQKV = FB_HQ + 2 * FB_HKV
+FB_EPS = 1e-6
+
+
+def fused_block_buffers(torch, dev, copies: int) -> dict:
+    """Buffers of the quantize-once block (weights uninitialised)."""
+    K, NQKV, F = FB_K, FB_NQKV, FB_F
+    q8 = K // 32 * 36
+
+    def u8(n):
+        return torch.empty(n, dtype=torch.uint8, device=dev)
+
+    def f32(n):
+        return torch.empty(n, dtype=torch.float32, device=dev)
+
+    return {"wqkv": [u8(NQKV * (K // 256) * 144) for _ in range(copies)],
+            "wg": [u8(F * (K // 256) * 144) for _ in range(copies)],
+            "wu": [u8(F * (K // 256) * 144) for _ in range(copies)],
+            "x": f32(K), "g": f32(K), "xn": f32(K),
+            "xq": u8(6 * q8),  # [0]: the shared copy; [1..5]: one per consumer
+            "y_sep": f32(NQKV + 2 * F), "y_once": f32(NQKV + F), "y_fused": f32(NQKV + F)}
+
+
+def fused_block_forms(A, b: dict) -> dict:
+    """The three forms of the block over buffers ``b``: name -> (fn(copy),
+    launches, Q8_1 bytes written, Q8_1 bytes read, fp32 activation bytes).
+    Every pointer goes through _span, checked against its tensor."""
+    K, HQ, HKV, F, NQKV, eps = FB_K, FB_HQ, FB_HKV, FB_F, FB_NQKV, FB_EPS
+    q8 = K // 32 * 36
+    wq_bytes, wf_bytes = A.q4k_nbytes(NQKV, K), A.q4k_nbytes(F, K)
+    x, g, xn, xq = b["x"], b["g"], b["xn"], b["xq"]
+    rows = ((0, HQ), (HQ, HKV), (HQ + HKV, HKV))  # q, k, v: row ranges of q|k|v
+
+    def per_consumer(r):
+        A.rmsnorm_quantize_q8_1(_span(x, 0, K * 4), _span(g, 0, K * 4), eps, _span(xq, 0, q8), K,
+                                d_xn_out=_span(xn, 0, K * 4))
+        for i in range(5):
+            A.launch_quantize_f32_to_q8_1(_span(xn, 0, K * 4), _span(xq, (i + 1) * q8, q8), K)
+        yo = 0
+        for i, (r0, n) in enumerate(rows):
+            A.mmvq(_span(b["wqkv"][r], A.q4k_nbytes(r0, K), A.q4k_nbytes(n, K)),
+                   _span(xq, (i + 1) * q8, q8), _span(b["y_sep"], yo * 4, n * 4), n, K)
+            yo += n
+        for i, w in ((3, b["wg"][r]), (4, b["wu"][r])):
+            A.mmvq(_span(w, 0, wf_bytes), _span(xq, (i + 1) * q8, q8),
+                   _span(b["y_sep"], yo * 4, F * 4), F, K)
+            yo += F
+
+    def quantize_once(r):
+        A.rmsnorm_quantize_q8_1(_span(x, 0, K * 4), _span(g, 0, K * 4), eps, _span(xq, 0, q8), K)
+        A.mmvq(_span(b["wqkv"][r], 0, wq_bytes), _span(xq, 0, q8),
+               _span(b["y_once"], 0, NQKV * 4), NQKV, K)
+        A.mmvq_swiglu(_span(b["wg"][r], 0, wf_bytes), _span(b["wu"][r], 0, wf_bytes),
+                      _span(xq, 0, q8), _span(b["y_once"], NQKV * 4, F * 4), F, K)
+
+    def fused_prologue(r):
+        A.mmvq_rmsnorm(_span(b["wqkv"][r], 0, wq_bytes), _span(x, 0, K * 4), _span(g, 0, K * 4),
+                       eps, _span(b["y_fused"], 0, NQKV * 4), NQKV, K)
+        A.mmvq_rmsnorm(_span(b["wg"][r], 0, wf_bytes), _span(x, 0, K * 4), _span(g, 0, K * 4),
+                       eps, _span(b["y_fused"], NQKV * 4, F * 4), F, K,
+                       d_w_up=_span(b["wu"][r], 0, wf_bytes))
+
+    act = 2 * K * 4  # x and the norm weight
+    return {
+        # the norm's fp32 output written once and read by 5 quantizations
+        "per_consumer": (per_consumer, 11, 6 * q8, 5 * q8, act + K * 4 + 5 * K * 4),
+        "quantize_once": (quantize_once, 3, q8, 2 * q8, act),
+        "fused_prologue": (fused_prologue, 2, 0, 0, act),
+    }
+
+
+def fused_rmsnorm_block(torch, steps: int, copies: int = 8, seed: int = 0):
+    """The quantize-once block on hidden 2560: x ~ N(0,1) fp32 and a norm
+    weight ~ U(0.8, 1.2) (eps 1e-6); the normalized, Q8_1-quantized
+    activation feeds q (4096), k, v (1024 each), gate and up (9728 each).
+    Three forms of the same block, each as a CUDA graph over ``copies``
+    copies of the layer's weights (36.9 MB a copy, 295 MB in all: every block
+    reads its weights from HBM):
+
+    * per_consumer -- RMSNorm to fp32, then one Q8_1 quantization and one
+      MMVQ per consumer (the reference without its reuse cache: 5 Q8_1
+      writes and 5 reads);
+    * quantize_once -- abra_rmsnorm_quantize_q8_1 writes one Q8_1 copy that
+      the fused q|k|v MMVQ and the gate/up SwiGLU MMVQ read (the reference's
+      Q8 reuse, kernels/q4k/abra-q8-reuse.cuh:3-71);
+    * fused_prologue -- abra_q4k_mmvq_rmsnorm: each CTA of the two MMVQs
+      normalizes and quantizes in shared memory; no Q8_1 in HBM (the decode
+      runtime's form).
+
+    Reports time per block, launches, Q8_1 bytes through HBM and the bytes
+    saved, and whether the three forms give the same outputs."""
+    import abra_b200 as A
+    import oracle as O
+
+    K, NQKV, F = FB_K, FB_NQKV, FB_F
+    dev = torch.device("cuda", torch.cuda.current_device())
+    b = fused_block_buffers(torch, dev, copies)
+    for r in range(copies):
+        for name, tid in (("wqkv", 900), ("wg", 901), ("wu", 902)):
+            t = b[name][r]
+            A.gen_q4k(t, t.numel() // 144, seed, tid + 10 * r)
+    b["x"].copy_(torch.from_numpy(O.gen_normal_f32((1, K), seed + 77).reshape(-1)))
+    b["g"].copy_(torch.from_numpy(O.gen_uniform_f32(K, seed, 78, 0.4, 0.8)))  # U(0.8, 1.2)
+    out = {"workload": "fused_rmsnorm_q8_1_block_2560", "copies": copies,
+           "consumers": "q 4096, k 1024, v 1024, gate 9728, up 9728 (x 2560)", "forms": {}}
+    for name, (fn, launches, qw, qr, fp32_bytes) in fused_block_forms(A, b).items():
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for r in range(copies):
+                fn(r)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for r in range(copies):
+                fn(r)
+        for _ in range(3):
+            graph.replay()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(5, steps // 8)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(n):
+            graph.replay()
+        e.record()
+        torch.cuda.synchronize()
+        del graph
+        out["forms"][name] = {"us_per_block": round(s.elapsed_time(e) / n / copies * 1000.0, 2),
+                              "launches": launches, "q8_1_bytes_written": qw,
+                              "q8_1_bytes_read": qr, "fp32_activation_bytes": fp32_bytes}
+    base = out["forms"]["per_consumer"]
+    for name in ("quantize_once", "fused_prologue"):
+        f = out["forms"][name]
+        f["q8_1_bytes_saved"] = (base["q8_1_bytes_written"] + base["q8_1_bytes_read"]
+                                 - f["q8_1_bytes_written"] - f["q8_1_bytes_read"])
+    ys = b["y_sep"][:NQKV].cpu().numpy()
+    out["qkv_outputs_identical"] = bool(
+        np.array_equal(ys, b["y_once"][:NQKV].cpu().numpy())
+        and np.array_equal(ys, b["y_fused"][:NQKV].cpu().numpy()))
+    out["ffn_outputs_identical"] = bool(np.array_equal(b["y_once"][NQKV:].cpu().numpy(),
+                                                       b["y_fused"][NQKV:].cpu().numpy()))
+    del b
+    torch.cuda.empty_cache()
+    return out
+
+
 def decode_batched(torch, warmup: int, steps: int, batch: int = 32, seed: int = 0):
     """Batch-32 decode (32 sequences in lockstep, tcgen05 GEMVs): aggregate
     tok/s over ``steps`` graph replays after the 16-token prompts and
@@ -797,7 +953,8 @@ def decode_main(a, dist):
         extras["decode_q4_k_m"] = r
         for name, fn in (("prompt_pp512", lambda: prompt_processing(torch, 512)),
                          ("lookup_verify", lambda: lookup_verification(torch)),
-                         ("decode_samples", lambda: decode_samples(torch, a.warmup, a.steps))):
+                         ("decode_samples", lambda: decode_samples(torch, a.warmup, a.steps)),
+                         ("fused_rmsnorm_block", lambda: fused_rmsnorm_block(torch, a.steps))):
             try:
                 extras[name] = fn()
             except Exception as exc:  # an extra must not cost the main line

@@ -156,6 +156,23 @@ void launch_pinned_upstream_q8_1_quantize(const float *d_x_f32, void *d_x_q8, in
 int abra_rmsnorm_quantize_q8_1(const float *x, const float *w, float eps, void *x_q8_1,
                                float *xn_out, int64_t K, int32_t ncols, void *stream);
 
+/* RMSNorm -> Q8_1 -> MMVQ in one kernel, batch 1: every CTA normalizes the
+ * fp32 input x (K values) with the norm weights and quantizes it to Q8_1 in
+ * its own shared memory, in the order of abra_rmsnorm_quantize_q8_1, then
+ * runs the MMVQ on it, so the activation never makes a round trip through
+ * HBM and the result is bit-identical to abra_rmsnorm_quantize_q8_1 followed
+ * by abra_q4k_mmvq (w_up == NULL) or abra_q4k_mmvq_swiglu (w_up != NULL: y =
+ * (W_up xq) * silu(W_gate xq) with W_gate = w).  x_q8_out, when not NULL,
+ * receives the K/32 Q8_1 blocks (written by one CTA) for another consumer of
+ * the same activation.  This is the decode runtime's form of the reference's
+ * quantize-once reuse (kernels/q4k/abra-q8-reuse.cuh:3-71), where the
+ * consumers of one normalized activation share a single Q8_1 copy.
+ * w, w_up and norm_w 16-byte aligned; x, y, x_q8_out 4-byte aligned;
+ * candidate 0 = tuned; flags ABRA_MMVQ_PDL. */
+int abra_q4k_mmvq_rmsnorm(const void *w_q4k, const void *w_up, const float *x,
+                          const float *norm_w, float eps, float *y, void *x_q8_out, int64_t N,
+                          int64_t K, int32_t candidate, int32_t flags, void *stream);
+
 /* ------------------------------------------------------- generators ---- */
 /* Seeded synthetic Q4_K superblocks [block_offset, block_offset+nblocks) of
  * tensor tensor_id: d, dmin ~ U(0.001, 0.02) fp16, scales/mins ~ U{0..63},

@@ -79,6 +79,17 @@ def test_rejects_bad_arguments_without_gpu():
     assert lib.abra_rmsnorm_quantize_q8_1(16, 16, 1e-6, 16, 34, 2560, 1, None) == _lib.ABRA_E_INVALID
     assert lib.abra_gen_uniform_f32(18, 8, 0, 0, 0, 1.0, 0.0, None) == _lib.ABRA_E_INVALID
     assert "4-byte" in _lib.last_error()
+    # fused RMSNorm MMVQ (w, w_up, x, norm_w, eps, y, x_q8_out, N, K, candidate, flags,
+    # stream): every call below fails its argument checks before any launch
+    rms = lib.abra_q4k_mmvq_rmsnorm
+    assert rms(None, None, 16, 16, 1e-6, 16, None, 64, 2560, 0, 0, None) == _lib.ABRA_E_INVALID
+    assert rms(16, None, 16, 16, 1e-6, 16, None, 64, 2000, 0, 0, None) == _lib.ABRA_E_INVALID
+    assert rms(16, None, 16, 16, 1e-6, 16, None, 64, 32768, 0, 0, None) == _lib.ABRA_E_UNSUPPORTED
+    assert rms(16, 24, 16, 16, 1e-6, 16, None, 64, 2560, 0, 0, None) == _lib.ABRA_E_INVALID
+    assert rms(16, None, 16, 20, 1e-6, 16, None, 64, 2560, 0, 0, None) == _lib.ABRA_E_INVALID
+    assert rms(16, None, 18, 16, 1e-6, 16, None, 64, 2560, 0, 0, None) == _lib.ABRA_E_INVALID
+    assert rms(16, None, 16, 16, 1e-6, 16, 34, 64, 2560, 0, 0, None) == _lib.ABRA_E_INVALID
+    assert rms(16, None, 16, 16, 1e-6, 16, None, 64, 2560, 4242, 0, None) == _lib.ABRA_E_INVALID
     with pytest.raises(ValueError):
         A.launch_quantize_f32_to_q8_1(16, 16, 33)
     with pytest.raises(ValueError):

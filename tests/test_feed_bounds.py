@@ -254,6 +254,9 @@ def test_q4k_edge_shapes_every_candidate(K):
         for N in N_EDGES:
             for ncols in (1, 8):
                 check_q4k(cid, mode, ks, cps, N, K, ncols)
+            # the fused RMSNorm prologue (abra_q4k_mmvq_rmsnorm), MMVQ and gate/up
+            check_q4k(cid, mode, ks, cps, N, K, 1, xin=1)
+            check_q4k(cid, mode, ks, cps, N, K, 1, nmat=2, xin=1)
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])

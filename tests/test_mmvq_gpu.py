@@ -217,6 +217,48 @@ def test_swiglu_every_candidate(dev):
         assert np.array_equal(_run_swiglu(dev, wg, wu, xq, N, K, ncols, cid), ref), cid
 
 
+@pytest.mark.parametrize("N,K,nmat", [(6144, 2560, 1), (9728, 2560, 2), (300, 4096, 1),
+                                      (77, 256, 2)])
+def test_fused_rmsnorm_mmvq_bit_exact(dev, N, K, nmat):
+    """abra_q4k_mmvq_rmsnorm (RMSNorm and Q8_1 in every CTA's prologue, then
+    the MMVQ; nmat 2: the gate/up SwiGLU) equals the oracle's
+    rmsnorm_quantize_q8_1 followed by its GEMV, and the exported Q8_1 copy
+    equals the oracle's bytes."""
+    import torch
+    import abra_b200 as A
+    from abra_b200 import AbraError, _lib
+
+    x = O.gen_normal_f32((1, K), 17) * 3.0
+    g = O.gen_uniform_f32(K, 0, 93, 0.4, 0.8)
+    q_ref, _ = O.rmsnorm_quantize_q8_1(x, g, 1e-6)
+    w = O.gen_q4k(N, K, 2, 61)
+    wu = O.gen_q4k(N, K, 2, 62) if nmat == 2 else None
+    if nmat == 2:
+        ref = O.gemv_swiglu(w, wu, q_ref, K, nthreads=8)
+    else:
+        ref = O.gemv(w, q_ref, K, nthreads=8)
+    dx, dg = to_dev(x.reshape(-1), dev), to_dev(g, dev)
+    dw = to_dev(w.reshape(-1), dev)
+    dwu = to_dev(wu.reshape(-1), dev) if nmat == 2 else None
+    dq = torch.zeros(K // 32 * 36, dtype=torch.uint8, device=dev)
+    cands = [0] + A.get_all_candidate_ids() if N < 1000 else [0, 1011, 1021, 2011, 3012, 3082]
+    ran = 0
+    for cid in cands:
+        dy = torch.full((N,), float("nan"), dtype=torch.float32, device=dev)
+        dq.zero_()
+        try:
+            A.mmvq_rmsnorm(dw, dx, dg, 1e-6, dy, N, K, d_w_up=dwu, d_x_q8_out=dq, candidate=cid)
+        except AbraError as e:  # no fused plan for this candidate and shape
+            assert e.code == _lib.ABRA_E_UNSUPPORTED, str(e)
+            continue
+        torch.cuda.synchronize()
+        assert A.device_error() == 0
+        assert np.array_equal(dy.cpu().numpy(), ref[0]), f"candidate {cid}"
+        assert np.array_equal(dq.cpu().numpy(), q_ref.reshape(-1)), f"candidate {cid}: Q8_1 copy"
+        ran += 1
+    assert ran >= 2
+
+
 def test_expf_matches_oracle(dev):
     """silu's exp: the device copy returns the oracle's bits on a dense sweep."""
     import torch
