@@ -39,8 +39,6 @@ DECODE_SHAPES = [
 ]
 
 
-
-
 def tp_shapes(worlds=(2, 4, 8)):
     """Per-rank shapes of the tensor-parallel decode: (N, K, nmat, K_full,
     sl_base, sl_cnt); K_full > 0 marks a K-shard (o, down), timed through the
