@@ -64,6 +64,17 @@ def q4k_bytes(N: int, K: int) -> int:
     return N * (K // 256) * 144
 
 
+def pick_winner(times: dict) -> int:
+    """The candidate a shape's entry names: among those within 0.5 % of the
+    fastest, the lowest id.  The reference keeps the same 0.5 % band and
+    breaks ties by its own geometry order, then the id
+    (tools/run-m4-autotune.py:196-206); the id is this family's order."""
+    if not times:
+        raise ValueError("no candidate times")
+    fastest = min(times.values())
+    return min(c for c, t in times.items() if t <= fastest * 1.005)
+
+
 def time_candidate(torch, plan, ncols, nmat, cid, reps=3, failures=None, kshard=(0, 0, 8)):
     from .q4k import device_error
 
@@ -169,8 +180,7 @@ def tune_q6k(shapes, ncols_list, out: Path, reps: int = 3) -> dict:
                     continue
                 times[cid] = graph_time(torch, run, copies, reps)
             assert times, f"no Q6_K candidate ran for {(N, K, ncols)}"
-            fastest = min(times.values())
-            winner = min(c for c, t in times.items() if t <= fastest * 1.005)
+            winner = pick_winner(times)
             nbytes = per + ncols * (K // 32) * 36 + ncols * N * 4
             e = {"N": N, "K": K, "ncols": ncols, "candidate": winner, "us": round(times[winner], 3),
                  "GBps": round(nbytes / (times[winner] * 1e-6) / 1e9, 1), "copies": copies,
@@ -230,8 +240,7 @@ def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None, merge: bo
                 if us is not None:
                     times[cid] = us
             assert times, f"no candidate ran for {(N, K, ncols, nmat)}"
-            fastest = min(times.values())
-            winner = min(c for c, t in times.items() if t <= fastest * 1.005)
+            winner = pick_winner(times)
             nbytes = per + ncols * (K // 32) * 36 + ncols * N * 4
             e = {"N": N, "K": K, "ncols": ncols, "nmat": nmat, "candidate": winner,
                  **({"K_full": kshard[0], "sl_base": kshard[1], "sl_cnt": kshard[2]}

@@ -119,3 +119,15 @@ def test_new_model_entry_points_refuse_a_null_model():
     assert lib.abra_model_load_tensor(None, -1, 1, 12, None, 0) == _lib.ABRA_E_INVALID
     assert lib.abra_lookup_draft(None, -1, 2, 4, None) == _lib.ABRA_E_INVALID
     assert lib.abra_lookup_draft(None, 0, 2, 4, None) == _lib.ABRA_E_INVALID  # limit > 0, no out
+
+
+def test_tuner_tie_break():
+    """Within 0.5 % of the fastest the lowest candidate id wins (the band of
+    the reference's table synthesis, tools/run-m4-autotune.py:196-206)."""
+    from abra_b200.tune import pick_winner
+
+    assert pick_winner({3012: 10.0, 1011: 10.04, 2011: 9.99}) == 1011
+    assert pick_winner({3012: 10.0, 1011: 10.2, 2011: 9.99}) == 2011
+    assert pick_winner({1042: 5.0}) == 1042
+    with pytest.raises(ValueError):
+        pick_winner({})
