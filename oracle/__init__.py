@@ -397,10 +397,11 @@ class OrcModel:
         self.cfg = model_config(**cfg)
         self.ptr = lib.orc_model_create(C.byref(self.cfg))
         self.threads = max_threads()
+        self._destroy = lib.orc_model_destroy  # still bound when module globals are gone
 
     def close(self):
         if self.ptr:
-            lib.orc_model_destroy(self.ptr)
+            self._destroy(self.ptr)
             self.ptr = None
 
     def __del__(self):
