@@ -119,3 +119,41 @@ def test_oracle_model_agrees_with_transformers_qwen3(cfg, min_cos):
 def test_a_wrong_rotation_is_told_apart():
     cos, _, _ = _compare(CASES[0][0], theta=1e4)
     assert cos.min() < 0.95, cos.min()
+
+
+@pytest.mark.parametrize("mix", [False, True], ids=["q4_k", "q4_k_m"])
+def test_gguf_file_read_by_transformers_decodes_like_the_oracle(tmp_path, mix):
+    """A GGUF file written by abra_b200.gguf (the seeded tensors under the
+    Qwen3 names and metadata) read by transformers' own GGUF loader, which
+    dequantizes through the gguf package, gives a model whose logits agree
+    with the oracle model of that seed: an independent reader takes our
+    names, shapes, types and metadata for the model we mean."""
+    gguf_utils = pytest.importorskip("transformers.modeling_gguf_pytorch_utils")
+    pytest.importorskip("gguf")
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    from gguf_fixture import write_qwen3
+
+    shape = dict(n_layers=8 if mix else 2, hidden=256 if mix else 512, n_heads=2 if mix else 4,
+                 n_kv_heads=1 if mix else 2, head_dim=128, ffn=512 if mix else 768, vocab=1024)
+    path = tmp_path / "m.gguf"
+    write_qwen3(path, shape, seed=5, mix=mix)
+    meta = gguf_utils.load_gguf_checkpoint(str(path), return_tensors=False)["config"]
+    assert meta["model_type"] == "qwen3" and meta["num_key_value_heads"] == shape["n_kv_heads"]
+    qc = Qwen3Config(**{k: v for k, v in meta.items() if k not in ("model_type", "_model_name_or_path")})
+    qc._attn_implementation = "eager"
+    m = Qwen3ForCausalLM(qc).float().eval()
+    tensors = gguf_utils.load_gguf_checkpoint(str(path), return_tensors=True, model_to_load=m)["tensors"]
+    res = m.load_state_dict(tensors, strict=False)
+    assert not res.unexpected_keys and set(res.missing_keys) <= {"lm_head.weight"}  # tied
+    assert m.lm_head.weight.data_ptr() == m.model.embed_tokens.weight.data_ptr()
+
+    cfg = {k: shape[k] for k in ("n_layers", "hidden", "n_heads", "n_kv_heads", "ffn", "vocab")}
+    toks = np.random.default_rng(6).integers(0, shape["vocab"], 40).astype(np.int32)
+    c = O.OrcModel(**cfg, max_ctx=64, centered=1, seed=5, mix=int(mix))
+    ours = np.stack([c.step(int(t), p, logits=True)[1] for p, t in enumerate(toks)])
+    c.close()
+    with torch.no_grad():
+        ref = m(torch.from_numpy(toks.astype(np.int64))[None]).logits[0].numpy()
+    cos = (ours * ref).sum(1) / np.linalg.norm(ours, axis=1) / np.linalg.norm(ref, axis=1)
+    assert cos.min() > 0.98 and np.median(cos) > 0.998, (cos.min(), np.median(cos))
