@@ -493,6 +493,11 @@ def run_case(a):
     table.update({"qkv": (6144, 2560, 1), "gate_up": (9728, 2560, 2)})
     if a.case.startswith("q6k_"):
         return run_case_q6k(a)
+    if a.case == "fused_rmsnorm_block":
+        torch.cuda.set_device(0)
+        print(json.dumps({"case": a.case, **fused_rmsnorm_block(torch, a.steps, copies=max(8, a.copies))}),
+              flush=True)
+        return 0
     N, K, nmat = table[a.case]
     dev = torch.device("cuda:0")
     nb = N * K // 256
@@ -1071,7 +1076,7 @@ def main():
                     help="skip the per-shape table and the reference kernel family")
     ap.add_argument("--quick", action="store_true", help="decode: depth 0 only")
     ap.add_argument("--case", choices=[n for n, _, _ in CONFIG1_SHAPES] + ["qkv", "gate_up"]
-                    + [f"q6k_{n}" for n, _, _ in Q6K_SHAPES],
+                    + [f"q6k_{n}" for n, _, _ in Q6K_SHAPES] + ["fused_rmsnorm_block"],
                     help="profiling mode: one operator, eager launches")
     ap.add_argument("--copies", type=int, default=2, help="weight copies in --case mode")
     a = ap.parse_args()
