@@ -107,6 +107,7 @@ class BatchedDecodeModel:
         self.handle = None
         self.batch = batch
         self.cfg = default_config(**config)
+        self._destroy = _lib.lib.abra_model_destroy  # still bound at interpreter exit
         h = C.c_void_p()
         _check(_lib.lib.abra_model_create_batched(C.byref(self.cfg), batch, C.byref(h)),
                "abra_model_create_batched")
@@ -114,7 +115,7 @@ class BatchedDecodeModel:
 
     def close(self) -> None:
         if self.handle:
-            _lib.lib.abra_model_destroy(self.handle)
+            self._destroy(self.handle)
             self.handle = None
 
     def __del__(self):
@@ -193,6 +194,7 @@ class DecodeModel:
         self.handle = None
         self.cfg = default_config(**config)
         self.shard = shard_info(rank, world, **config)
+        self._destroy = _lib.lib.abra_model_destroy  # still bound at interpreter exit
         h = C.c_void_p()
         _check(_lib.lib.abra_model_create_tp(C.byref(self.cfg), rank, world, C.byref(h)),
                "abra_model_create_tp")
@@ -214,7 +216,7 @@ class DecodeModel:
 
     def close(self) -> None:
         if self.handle:
-            _lib.lib.abra_model_destroy(self.handle)
+            self._destroy(self.handle)
             self.handle = None
 
     def __del__(self):
