@@ -903,8 +903,8 @@ static int create_model(const abra_model_config *cfg, int32_t rank, int32_t worl
     m->sh = shard;
     m->batch = batch;
     m->connected = world == 1;
-    cudaGetDevice(&m->device);
-    cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    cudaError_t e = cudaGetDevice(&m->device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = abra::build(*m);
     if (e != cudaSuccess) {
         abra_model_destroy(m);
