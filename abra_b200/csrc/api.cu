@@ -57,6 +57,23 @@ int check_mmvq_args(const void *w, const void *x, const float *y, int64_t N, int
     return ABRA_OK;
 }
 
+// A K-shard: canonical slices [sl_base, sl_base + sl_cnt) of rows K_full wide,
+// whose width must be K.  Fills the slicing options on success.
+int check_kshard(int64_t K, int64_t K_full, int32_t sl_base, int32_t sl_cnt, abra::MmvqOpts &tp) {
+    if (K_full <= 0 || K_full % 256 != 0 || K_full > 65536 || sl_base < 0 ||
+        !(sl_cnt == 1 || sl_cnt == 2 || sl_cnt == 4 || sl_cnt == 8) || sl_base + sl_cnt > 8)
+        return fail(ABRA_E_INVALID, "bad K-shard (K_full=%lld sl_base=%d sl_cnt=%d)",
+                    (long long)K_full, sl_base, sl_cnt);
+    const int nsb_g = static_cast<int>(K_full / 256);
+    if ((abra::slice_start(nsb_g, sl_base + sl_cnt) - abra::slice_start(nsb_g, sl_base)) * 256 != K)
+        return fail(ABRA_E_INVALID, "K=%lld is not the width of canonical slices [%d, %d) of K_full=%lld",
+                    (long long)K, sl_base, sl_base + sl_cnt, (long long)K_full);
+    tp.sl_nsb = nsb_g;
+    tp.sl_base = sl_base;
+    tp.sl_cnt = sl_cnt;
+    return ABRA_OK;
+}
+
 }  // namespace
 
 int abra::record_failure(int code, const char *msg) { return fail(code, "%s", msg); }
@@ -134,22 +151,13 @@ int abra_q4k_mmvq_kshard(const void *w, const void *x, float *y, int64_t N, int6
                          int32_t candidate, int32_t flags, void *stream) {
     int rc = check_mmvq_args(w, x, y, N, K, ncols, N);
     if (rc) return rc;
-    if (K_full <= 0 || K_full % 256 != 0 || K_full > 65536 || sl_base < 0 ||
-        !(sl_cnt == 1 || sl_cnt == 2 || sl_cnt == 4 || sl_cnt == 8) || sl_base + sl_cnt > 8)
-        return fail(ABRA_E_INVALID, "bad K-shard (K_full=%lld sl_base=%d sl_cnt=%d)",
-                    (long long)K_full, sl_base, sl_cnt);
-    const int nsb_g = static_cast<int>(K_full / 256);
-    if ((abra::slice_start(nsb_g, sl_base + sl_cnt) - abra::slice_start(nsb_g, sl_base)) * 256 != K)
-        return fail(ABRA_E_INVALID, "K=%lld is not the width of canonical slices [%d, %d) of K_full=%lld",
-                    (long long)K, sl_base, sl_base + sl_cnt, (long long)K_full);
+    abra::MmvqOpts tp;
+    rc = check_kshard(K, K_full, sl_base, sl_cnt, tp);
+    if (rc) return rc;
     int id = candidate;
     if (id == 0) id = abra_tune_get(N, K, ncols, 1);
     const abra::MmvqConfig *cfg = abra::mmvq_candidate_by_id(id);
     if (!cfg) return fail(ABRA_E_INVALID, "unknown candidate id %d", id);
-    abra::MmvqOpts tp;
-    tp.sl_nsb = nsb_g;
-    tp.sl_base = sl_base;
-    tp.sl_cnt = sl_cnt;
     cudaError_t e = abra::launch_mmvq_q4k(*cfg, w, nullptr, x, y, N, K, ncols, N,
                                           (flags & ABRA_MMVQ_PDL) ? abra::MMVQ_PDL : 0,
                                           static_cast<cudaStream_t>(stream), nullptr, &tp);
@@ -330,18 +338,9 @@ int abra_q6k_mmvq_kshard(const void *w, const void *x, float *y, int64_t N, int6
                          int32_t candidate, int32_t flags, void *stream) {
     int rc = check_mmvq_args(w, x, y, N, K, ncols, N);
     if (rc) return rc;
-    if (K_full <= 0 || K_full % 256 != 0 || K_full > 65536 || sl_base < 0 ||
-        !(sl_cnt == 1 || sl_cnt == 2 || sl_cnt == 4 || sl_cnt == 8) || sl_base + sl_cnt > 8)
-        return fail(ABRA_E_INVALID, "bad K-shard (K_full=%lld sl_base=%d sl_cnt=%d)",
-                    (long long)K_full, sl_base, sl_cnt);
-    const int nsb_g = static_cast<int>(K_full / 256);
-    if ((abra::slice_start(nsb_g, sl_base + sl_cnt) - abra::slice_start(nsb_g, sl_base)) * 256 != K)
-        return fail(ABRA_E_INVALID, "K=%lld is not the width of canonical slices [%d, %d) of K_full=%lld",
-                    (long long)K, sl_base, sl_base + sl_cnt, (long long)K_full);
     abra::MmvqOpts tp;
-    tp.sl_nsb = nsb_g;
-    tp.sl_base = sl_base;
-    tp.sl_cnt = sl_cnt;
+    rc = check_kshard(K, K_full, sl_base, sl_cnt, tp);
+    if (rc) return rc;
     return q6k_common(w, x, y, N, K, ncols, N, candidate, flags, &tp, stream);
 }
 
@@ -421,13 +420,8 @@ int abra_mmvq_plan_info(int32_t ggml_type, int32_t candidate, int64_t N, int64_t
     abra::MmvqOpts tp;
     const abra::MmvqOpts *ptp = nullptr;
     if (K_full > 0) {
-        if (K_full % 256 != 0 || K_full > 65536 || sl_base < 0 ||
-            !(sl_cnt == 1 || sl_cnt == 2 || sl_cnt == 4 || sl_cnt == 8) || sl_base + sl_cnt > 8)
-            return fail(ABRA_E_INVALID, "bad K-shard (K_full=%lld sl_base=%d sl_cnt=%d)",
-                        (long long)K_full, sl_base, sl_cnt);
-        tp.sl_nsb = static_cast<int>(K_full / 256);
-        tp.sl_base = sl_base;
-        tp.sl_cnt = sl_cnt;
+        const int rc = check_kshard(K, K_full, sl_base, sl_cnt, tp);
+        if (rc) return rc;
         ptp = &tp;
     }
     const bool q6 = ggml_type == ABRA_GGML_Q6_K;
