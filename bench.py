@@ -1,7 +1,14 @@
 #!/usr/bin/env python
 """Benchmark of the Q4_K x Q8_1 MMVQ path on B200.
 
-Workload ("qwen3_4b_decode_weight_sweep"): one step is one pass of MMVQ over
+Default workload ("qwen3_4b_q4k_decode_tg"): greedy decode of the seeded
+Qwen3-4B-shaped model, all linear weights Q4_K, after a 16-token prompt; one
+step is one token (one CUDA graph of 291 kernels), ``value`` is tok/s at
+depth 0, ``e2e`` the same through the per-token host call, and ``roofline``
+the decode step's MMVQ launches (the weight sweep below) against measured
+HBM bandwidth.  Under torchrun the model is tensor parallel over the ranks.
+
+GEMV workload (``--workload gemv``, "qwen3_4b_decode_weight_sweep"): one step is one pass of MMVQ over
 the full Qwen3-4B-shaped decode weight set, in the operators a decode step
 runs: per layer the fused q|k|v projection (6144 x 2560), o (2560 x 4096),
 the fused gate/up SwiGLU (2 x 9728 x 2560) and down (2560 x 9728), for 36
