@@ -500,6 +500,8 @@ def run_case(a):
     table.update({"qkv": (6144, 2560, 1), "gate_up": (9728, 2560, 2)})
     if a.case.startswith("q6k_"):
         return run_case_q6k(a)
+    if a.case == "tc_b32_16384":
+        return run_case_tc(a)
     if a.case == "fused_rmsnorm_block":
         torch.cuda.set_device(0)
         print(json.dumps({"case": a.case, **fused_rmsnorm_block(torch, a.steps, copies=max(8, a.copies))}),
@@ -580,6 +582,53 @@ def run_case_q6k(a):
                       "us_per_launch_eager": round(us, 3),
                       "GBps_eager": round(alg / (us * 1e-6) / 1e9, 1),
                       "candidate": A.q6k_tune_get(N, K, a.batch),
+                      "device_error": A.device_error()}), flush=True)
+    return 0
+
+
+TC_CASE_SHAPE = (16384, 2560)
+
+
+def run_case_tc(a):
+    """Profiling case for the batch-32 tensor-core MMVQ: ``--copies`` (at
+    least 3) copies of a 16384 x 2560 Q4_K matrix (23.6 MB each), 32 N(0,1)
+    columns quantized to Q8_1, mmvq_tc (ks 1) on each copy, eager launches."""
+    import torch
+
+    import abra_b200 as A
+    import oracle as O
+
+    N, K = TC_CASE_SHAPE
+    dev = torch.device("cuda:0")
+    nb = N * K // 256
+    bufs = []
+    for i in range(max(3, a.copies)):
+        t = torch.empty(nb * 144, dtype=torch.uint8, device=dev)
+        A.gen_q4k(t, nb, 0, 40 + i)
+        bufs.append(t)
+    xq = torch.empty(32 * (K // 32) * 36, dtype=torch.uint8, device=dev)
+    A.launch_quantize_f32_to_q8_1(
+        torch.from_numpy(O.gen_normal_f32((32, K), 1).reshape(-1)).to(dev), xq, K, ncols=32)
+    y = torch.empty(32 * N, dtype=torch.float32, device=dev)
+
+    def run():
+        for b in bufs:
+            A.mmvq_tc(b, xq, y, N, K, ks=1)
+
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(a.steps):
+        run()
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1e3 / (a.steps * len(bufs))
+    alg = nb * 144 + 32 * (K // 32 * 36 + N * 4)
+    print(json.dumps({"case": a.case, "N": N, "K": K, "batch": 32, "copies": len(bufs),
+                      "us_per_launch_eager": round(us, 3),
+                      "GBps_eager": round(alg / (us * 1e-6) / 1e9, 1),
                       "device_error": A.device_error()}), flush=True)
     return 0
 
@@ -1083,7 +1132,7 @@ def main():
                     help="skip the per-shape table and the reference kernel family")
     ap.add_argument("--quick", action="store_true", help="decode: depth 0 only")
     ap.add_argument("--case", choices=[n for n, _, _ in CONFIG1_SHAPES] + ["qkv", "gate_up"]
-                    + [f"q6k_{n}" for n, _, _ in Q6K_SHAPES] + ["fused_rmsnorm_block"],
+                    + [f"q6k_{n}" for n, _, _ in Q6K_SHAPES] + ["tc_b32_16384", "fused_rmsnorm_block"],
                     help="profiling mode: one operator, eager launches")
     ap.add_argument("--copies", type=int, default=2, help="weight copies in --case mode")
     a = ap.parse_args()
