@@ -35,6 +35,7 @@ from .q4k import (
     mmvq_rmsnorm,
     mmvq_swiglu,
     mmvq_tc,
+    plan_info,
     q4k_nbytes,
     q8_1_nbytes,
     register_autotuned_table_entry,

@@ -103,6 +103,28 @@ def get_all_candidate_ids() -> list[int]:
     return sorted(_CANDIDATES)
 
 
+PLAN_FIELDS = ("grid", "threads", "nstage", "pitch", "stage_bytes", "smem", "row_groups",
+               "stage_offset")
+
+
+def plan_info(N: int, K: int, ncols: int = 1, candidate: int = 0, nmat: int = 1,
+              fused_rmsnorm: bool = False, q6k: bool = False, K_full: int = 0, sl_base: int = 0,
+              sl_cnt: int = 8, sm_count: int = 148) -> dict | None:
+    """The launch plan the dispatch makes for one MMVQ call
+    (abra_mmvq_plan_info), computed on the host: no GPU is needed when
+    sm_count > 0.  None when the candidate has no plan for the shape."""
+    import numpy as np
+
+    out = np.zeros(8, dtype=np.int64)
+    rc = lib.abra_mmvq_plan_info(14 if q6k else 12, candidate, N, K, ncols, nmat,
+                                 1 if fused_rmsnorm else 0, K_full, sl_base, sl_cnt, sm_count,
+                                 out.ctypes.data)
+    if rc == _lib.ABRA_E_UNSUPPORTED:
+        return None
+    _lib.check(rc, "abra_mmvq_plan_info")
+    return dict(zip(PLAN_FIELDS, (int(v) for v in out)))
+
+
 def get_candidate_spec(cid: int) -> Q4KCandidateSpec:
     if cid not in _CANDIDATES:
         raise ValueError(f"Unknown Q4KCandidateID {cid}")

@@ -322,3 +322,17 @@ def test_plan_info_rejects_bad_arguments():
     assert lib.abra_mmvq_plan_info(12, 12345, 64, 256, 1, 1, 0, 0, 0, 8, SMS, out.ctypes.data) == _lib.ABRA_E_INVALID
     assert lib.abra_mmvq_plan_info(12, 0, 64, 256, 1, 1, 0, 9728, 0, 3, SMS, out.ctypes.data) == _lib.ABRA_E_INVALID
     assert lib.abra_mmvq_plan_info(12, 0, 64, 256, 1, 1, 0, 0, 0, 8, SMS, None) == _lib.ABRA_E_INVALID
+
+
+def test_python_plan_info():
+    import abra_b200 as A
+
+    p = A.plan_info(9728, 2560)
+    from abra_b200.q4k import PLAN_FIELDS
+
+    assert tuple(p) == PLAN_FIELDS
+    assert p["row_groups"] == 1216 and p["threads"] in (256, 288) and p["smem"] <= MAX_SMEM
+    assert A.plan_info(151936, 2560, q6k=True)["row_groups"] == 18992
+    assert A.plan_info(2560, 9728, ncols=8, candidate=1021, q6k=True) is None  # does not fit
+    with pytest.raises(ValueError):
+        A.plan_info(64, 300)
