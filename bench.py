@@ -21,7 +21,7 @@ activations + fp32 outputs, the reference's formula,
 bench/micro/q4k_q8_bench.cu:330-333), aggregated over ranks (each rank runs
 the full set on its own GPU: weak scaling, no collective).
 
-Also reported: every config-1 shape separately (q, k, v, o, gate, up, down,
+Also reported: every decode matrix separately (q, k, v, o, gate, up, down,
 output), the reference's own kernel family on the same GPU over the
 unfused sweep, the sweep end to end through the C ABI with host buffers,
 the quantize-once RMSNorm -> Q8_1 block in three forms (fused_rmsnorm_block),
@@ -54,8 +54,8 @@ LAYERS = 36
 LAYER_OPS = [("qkv", 6144, 2560, 1), ("o", 2560, 4096, 1), ("gate_up", 9728, 2560, 2),
              ("down", 2560, 9728, 1)]
 OUTPUT_OP = ("output", 151936, 2560, 1)
-# config 1: every decode matrix separately
-CONFIG1_SHAPES = [("q", 4096, 2560), ("k", 1024, 2560), ("v", 1024, 2560), ("o", 2560, 4096),
+# every decode matrix of the Qwen3-4B shape, separately
+DECODE_MATRICES = [("q", 4096, 2560), ("k", 1024, 2560), ("v", 1024, 2560), ("o", 2560, 4096),
                   ("gate", 9728, 2560), ("up", 9728, 2560), ("down", 2560, 9728),
                   ("output", 151936, 2560)]
 WORKLOAD = "qwen3_4b_decode_weight_sweep"
@@ -194,7 +194,7 @@ def simd_level() -> int:
 def cpu_sample_rate(batch: int, budget_s: float, seed: int = 0):
     """CPU restatement of vec_dot_q4_K_q8_1 (OpenMP, all host cores; integer
     sub-block dots on the host's AVX-512 VNNI or AVX2 when present) on a
-    sample of the workload: the first 512 rows of every config-1 matrix,
+    sample of the workload: the first 512 rows of every decode matrix,
     repeated until ``budget_s`` seconds elapse.  Returns GB/s by the same
     byte formula."""
     import oracle as O
@@ -202,7 +202,7 @@ def cpu_sample_rate(batch: int, budget_s: float, seed: int = 0):
     threads = os.cpu_count() or 1
     rows = 512
     sample = []
-    for i, (name, N, K) in enumerate(CONFIG1_SHAPES):
+    for i, (name, N, K) in enumerate(DECODE_MATRICES):
         w = O.gen_q4k(min(rows, N), K, seed, i + 1)
         xq = O.quantize_q8_1(O.gen_normal_f32((batch, K), seed + 1000 + K))
         sample.append((w, xq, min(rows, N), K))
@@ -379,12 +379,12 @@ class E2E:
 
 
 def shape_table(sw: Sweep, reps: int = 3):
-    """Each config-1 shape (and the fused operators) alone: one CUDA graph of
+    """Each decode matrix (and the fused operators) alone: one CUDA graph of
     back-to-back launches over >= 4 x L2 (at least 8) distinct weight copies,
     best of ``reps`` replays."""
     torch, A = sw.torch, sw.A
     out = {}
-    shapes = [(n, N, K, 1) for n, N, K in CONFIG1_SHAPES] + [
+    shapes = [(n, N, K, 1) for n, N, K in DECODE_MATRICES] + [
         ("qkv_fused", 6144, 2560, 1), ("gate_up_swiglu", 9728, 2560, 2)]
     for name, N, K, nmat in shapes:
         per = nmat * q4k_bytes(N, K)
@@ -496,7 +496,7 @@ def run_case(a):
     import abra_b200 as A
     import oracle as O
 
-    table = {n: (N, K, 1) for n, N, K in CONFIG1_SHAPES}
+    table = {n: (N, K, 1) for n, N, K in DECODE_MATRICES}
     table.update({"qkv": (6144, 2560, 1), "gate_up": (9728, 2560, 2)})
     if a.case.startswith("q6k_"):
         return run_case_q6k(a)
@@ -1034,7 +1034,7 @@ def decode_main(a, dist):
         # the CPU restatement's decode rate: weight bytes per token at its GEMV rate
         cpu_tok_s = gbs * 1e9 / res["weight_bytes"]
         cpu = {"value": round(cpu_tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"first 512 rows of every config-1 matrix, {reps} reps in {el:.1f}s "
+               "sample": f"first 512 rows of every decode matrix, {reps} reps in {el:.1f}s "
                          f"({gbs:.2f} GB/s), scaled to the 2.26 GB of Q4_K weights a token "
                          "reads; CPU restatement of vec_dot_q4_K_q8_1, integer dots at SIMD level "
                          f"{simd_level()} (0 scalar, 1 AVX2, 2 AVX-512 VNNI); ggml CPU path "
@@ -1086,7 +1086,7 @@ def reference_arm(a, dist):
     rates = [cpu_sample_rate(a.batch, budget_s=per) for _ in range(a.steps)]
     gbs = statistics.median(r[0] for r in rates)
     threads = rates[0][1]
-    sample = (f"first 512 rows of every config-1 matrix, batch {a.batch}, {per:.1f}s per step; "
+    sample = (f"first 512 rows of every decode matrix, batch {a.batch}, {per:.1f}s per step; "
               f"CPU restatement of vec_dot_q4_K_q8_1, integer dots at SIMD level {simd_level()} "
               "(0 scalar, 1 AVX2, 2 AVX-512 VNNI); the ggml CPU path is not available")
     if a.workload == "decode":
@@ -1131,7 +1131,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the per-shape table and the reference kernel family")
     ap.add_argument("--quick", action="store_true", help="decode: depth 0 only")
-    ap.add_argument("--case", choices=[n for n, _, _ in CONFIG1_SHAPES] + ["qkv", "gate_up"]
+    ap.add_argument("--case", choices=[n for n, _, _ in DECODE_MATRICES] + ["qkv", "gate_up"]
                     + [f"q6k_{n}" for n, _, _ in Q6K_SHAPES] + ["tc_b32_16384", "fused_rmsnorm_block"],
                     help="profiling mode: one operator, eager launches")
     ap.add_argument("--copies", type=int, default=2, help="weight copies in --case mode")
@@ -1187,7 +1187,7 @@ def main():
     if dist.rank == 0 and dist.world == 1:
         gbs, threads, reps, el = cpu_sample_rate(a.batch, a.cpu_budget)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"first 512 rows of every config-1 matrix, batch {a.batch}, {reps} reps "
+               "sample": f"first 512 rows of every decode matrix, batch {a.batch}, {reps} reps "
                          f"in {el:.1f}s; CPU restatement of vec_dot_q4_K_q8_1, integer dots at "
                          f"SIMD level {simd_level()} (0 scalar, 1 AVX2, 2 AVX-512 VNNI); the ggml "
                          "CPU path is not available"}
