@@ -124,9 +124,11 @@ def test_full_qwen3_4b_tg128_greedy_tokens_identical():
             tok = c.step(feed, pos)
         if pos >= 15:
             want.append(tok)
-    assert np.array_equal(got, np.array(want, dtype=np.int32))
+    want = np.array(want, dtype=np.int32)
+    bad = np.flatnonzero(got != want)
+    assert bad.size == 0, f"tokens first differ at step {bad[:1]}: {got[bad[:4]]} vs {want[bad[:4]]}"
     assert np.array_equal(last.view(np.uint32), want_logits.view(np.uint32))
-    assert len(set(want)) > 8, "the centred model should not collapse to a few tokens"
+    assert len(set(want.tolist())) > 8, "the centred model should not collapse to a few tokens"
     g.close()
     c.close()
 
