@@ -336,3 +336,33 @@ def test_python_plan_info():
     assert A.plan_info(2560, 9728, ncols=8, candidate=1021, q6k=True) is None  # does not fit
     with pytest.raises(ValueError):
         A.plan_info(64, 300)
+
+
+def test_random_shapes_keep_every_feed_rule():
+    """Random shapes, batch widths, k-splits and K-shards (hypothesis): every
+    plan the dispatch makes keeps the rules above, for both weight types."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    q4, q6 = _cands("q4k"), _cands("q6k")
+
+    @settings(max_examples=60, deadline=None)
+    @given(kind=st.sampled_from(["q4k", "q6k"]), N=st.integers(1, 40000), nsb=st.integers(1, 48),
+           ncols=st.integers(1, 8), pick=st.integers(0, 10**6), nmat=st.integers(1, 2),
+           xin=st.booleans(), world=st.sampled_from([1, 2, 4, 8]), rank=st.integers(0, 7))
+    def run(kind, N, nsb, ncols, pick, nmat, xin, world, rank):
+        shard = None
+        K = nsb * 256
+        if world > 1 and nsb >= 8:  # a K-shard of a row nsb superblocks wide
+            per, r = 8 // world, rank % world
+            lo, hi = slice_start(nsb, r * per), slice_start(nsb, (r + 1) * per)
+            shard, K = (nsb, r * per, per), (hi - lo) * 256
+        if kind == "q4k":
+            cid, mode, ks, cps = q4[pick % len(q4)]
+            fused = xin and ncols == 1 and shard is None
+            check_q4k(cid, mode, ks, cps, N, K, ncols, nmat=nmat, xin=int(fused), shard=shard)
+        else:
+            cid, mode, ks, cps = q6[pick % len(q6)]
+            check_q6k(cid, mode, ks, cps, N, K, ncols, shard=shard)
+
+    run()
