@@ -25,10 +25,12 @@ Also reported: every decode matrix separately (q, k, v, o, gate, up, down,
 output), the reference's own kernel family on the same GPU over the
 unfused sweep, the sweep end to end through the C ABI with host buffers,
 the quantize-once RMSNorm -> Q8_1 block in three forms (fused_rmsnorm_block),
-and the CPU restatement of vec_dot_q4_K_q8_1 (oracle/, all host cores).
+and the CPU baseline on all host cores: llama.cpp's CPU Q4_K path restated in
+oracle/ (activations quantized to Q8_K, the Q4_K x Q8_K dot; llama.cpp itself
+is not in the image), beside the restatement of vec_dot_q4_K_q8_1.
 
-``--impl reference`` times that CPU restatement alone on a bounded sample of
-the same workload; the reference's ggml CPU path is not available.
+``--impl reference`` times that CPU path alone on a bounded sample of the
+same workload.
 
 Run: python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
 """
@@ -191,28 +193,37 @@ def simd_level() -> int:
     return int(O.lib.orc_simd_level())
 
 
-def cpu_sample_rate(batch: int, budget_s: float, seed: int = 0):
-    """CPU restatement of vec_dot_q4_K_q8_1 (OpenMP, all host cores; integer
-    sub-block dots on the host's AVX-512 VNNI or AVX2 when present) on a
-    sample of the workload: the first 512 rows of every decode matrix,
-    repeated until ``budget_s`` seconds elapse.  Returns GB/s by the same
-    byte formula."""
+CPU_PATHS = {
+    "ggml": "llama.cpp's CPU Q4_K path restated (activations in Q8_K, vec_dot_q4_K_q8_K)",
+    "q8_1": "the restatement of vec_dot_q4_K_q8_1 (the GPU path's formula)",
+}
+
+
+def cpu_sample_rate(batch: int, budget_s: float, seed: int = 0, path: str = "ggml"):
+    """A CPU Q4_K GEMV (OpenMP, all host cores; integer sub-block dots on the
+    host's AVX-512 VNNI or AVX2 when present) on a sample of the workload:
+    the first 512 rows of every decode matrix, repeated until ``budget_s``
+    seconds elapse.  ``path`` "ggml": llama.cpp's CPU path restated
+    (activations quantized to Q8_K, the Q4_K x Q8_K dot), the CPU path the
+    reference runs on the host; "q8_1": the restatement of
+    vec_dot_q4_K_q8_1.  Returns GB/s by the reference's byte formula."""
     import oracle as O
 
     threads = os.cpu_count() or 1
     rows = 512
+    quant, gemv = (O.quantize_q8_K, O.gemv_q8k) if path == "ggml" else (O.quantize_q8_1, O.gemv)
     sample = []
     for i, (name, N, K) in enumerate(DECODE_MATRICES):
         w = O.gen_q4k(min(rows, N), K, seed, i + 1)
-        xq = O.quantize_q8_1(O.gen_normal_f32((batch, K), seed + 1000 + K))
+        xq = quant(O.gen_normal_f32((batch, K), seed + 1000 + K))
         sample.append((w, xq, min(rows, N), K))
     nbytes = sum(alg_bytes(n, k, batch) for _, _, n, k in sample)
-    O.gemv(sample[0][0], sample[0][1], sample[0][3], threads)  # warm
+    gemv(sample[0][0], sample[0][1], sample[0][3], threads)  # warm
     t0 = time.perf_counter()
     reps = 0
     while True:
         for w, xq, n, k in sample:
-            O.gemv(w, xq, k, threads)
+            gemv(w, xq, k, threads)
         reps += 1
         el = time.perf_counter() - t0
         if el >= budget_s:
@@ -1031,14 +1042,18 @@ def decode_main(a, dist):
             except Exception as exc:
                 extras["fused_rmsnorm_block"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         gbs, threads, reps, el = cpu_sample_rate(1, a.cpu_budget)
-        # the CPU restatement's decode rate: weight bytes per token at its GEMV rate
+        # the CPU path's decode rate: weight bytes per token at its GEMV rate
         cpu_tok_s = gbs * 1e9 / res["weight_bytes"]
         cpu = {"value": round(cpu_tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
                "sample": f"first 512 rows of every decode matrix, {reps} reps in {el:.1f}s "
                          f"({gbs:.2f} GB/s), scaled to the 2.26 GB of Q4_K weights a token "
-                         "reads; CPU restatement of vec_dot_q4_K_q8_1, integer dots at SIMD level "
-                         f"{simd_level()} (0 scalar, 1 AVX2, 2 AVX-512 VNNI); ggml CPU path "
-                         "not available"}
+                         f"reads; {CPU_PATHS['ggml']}, integer dots at SIMD level "
+                         f"{simd_level()} (0 scalar, 1 AVX2, 2 AVX-512 VNNI)"}
+        g2, t2, r2, e2 = cpu_sample_rate(1, max(1.0, a.cpu_budget / 4), path="q8_1")
+        extras["cpu_baseline_q8_1"] = {"value": round(g2 * 1e9 / res["weight_bytes"], 3),
+                                       "unit": "tok/s", "cores": t2, "GBps": round(g2, 2),
+                                       "sample": f"the same sample, {r2} reps in {e2:.1f}s; "
+                                                 f"{CPU_PATHS['q8_1']}"}
     traffic = None
     tp = ROOT / "profiles" / f"traffic_{WORKLOAD}_b1.json"
     if tp.exists():
@@ -1087,8 +1102,8 @@ def reference_arm(a, dist):
     gbs = statistics.median(r[0] for r in rates)
     threads = rates[0][1]
     sample = (f"first 512 rows of every decode matrix, batch {a.batch}, {per:.1f}s per step; "
-              f"CPU restatement of vec_dot_q4_K_q8_1, integer dots at SIMD level {simd_level()} "
-              "(0 scalar, 1 AVX2, 2 AVX-512 VNNI); the ggml CPU path is not available")
+              f"{CPU_PATHS['ggml']}, integer dots at SIMD level {simd_level()} "
+              "(0 scalar, 1 AVX2, 2 AVX-512 VNNI)")
     if a.workload == "decode":
         weight_bytes = sum(nmat * q4k_bytes(N, K) for _, N, K, nmat, _ in sweep_ops())
         val, unit, metric = gbs * 1e9 / weight_bytes, "tok/s", "Qwen3-4B-shape decode tok/s"
@@ -1188,9 +1203,8 @@ def main():
         gbs, threads, reps, el = cpu_sample_rate(a.batch, a.cpu_budget)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"first 512 rows of every decode matrix, batch {a.batch}, {reps} reps "
-                         f"in {el:.1f}s; CPU restatement of vec_dot_q4_K_q8_1, integer dots at "
-                         f"SIMD level {simd_level()} (0 scalar, 1 AVX2, 2 AVX-512 VNNI); the ggml "
-                         "CPU path is not available"}
+                         f"in {el:.1f}s; {CPU_PATHS['ggml']}, integer dots at SIMD level "
+                         f"{simd_level()} (0 scalar, 1 AVX2, 2 AVX-512 VNNI)"}
 
     traffic = None
     tp = ROOT / "profiles" / f"traffic_{WORKLOAD}_b{a.batch}.json"

@@ -75,6 +75,8 @@ def _load() -> C.CDLL:
         "orc_q6k_gemv_f64": (None, [_u8p, _u8p, _f64p, _i64, _i64, _i32]),
         "orc_q6k_absdot_f64": (None, [_u8p, _u8p, _f64p, _i64, _i64, _i32]),
         "orc_dequant_q6k": (None, [_u8p, _f32p, _i64]),
+        "orc_quantize_q8_K": (None, [_f32p, _u8p, _i64, _i32]),
+        "orc_q4k_q8k_gemv": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i32, _i32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -158,6 +160,30 @@ def gemv(w, xq, K: int, nthreads: int = 1) -> np.ndarray:
     w, xq, N, ncols = _shape(w, xq, K)
     y = np.empty(ncols * N, dtype=np.float32)
     lib.orc_q4k_gemv(w, xq, y, N, K, ncols, nthreads)
+    return y.reshape(ncols, N)
+
+
+Q8K_BYTES = 292  # block_q8_K: fp32 d, 256 int8, 16 int16 sums
+
+
+def quantize_q8_K(x: np.ndarray) -> np.ndarray:
+    """llama.cpp's CPU activation format, restated: x (ncols, K) fp32 ->
+    uint8 (ncols, K/256*292)."""
+    x2 = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    ncols, K = x2.shape
+    out = np.empty(ncols * (K // QK_K) * Q8K_BYTES, dtype=np.uint8)
+    lib.orc_quantize_q8_K(x2, out, K, ncols)
+    return out.reshape(ncols, -1)
+
+
+def gemv_q8k(w, yk, K: int, nthreads: int = 1) -> np.ndarray:
+    """llama.cpp's CPU Q4_K x Q8_K dot, restated (the timed CPU baseline, not
+    a parity target), (ncols, N)."""
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+    yk2 = np.ascontiguousarray(np.atleast_2d(yk), dtype=np.uint8)
+    ncols, N = yk2.shape[0], w.size // ((K // QK_K) * Q4K_BYTES)
+    y = np.empty(ncols * N, dtype=np.float32)
+    lib.orc_q4k_q8k_gemv(w, yk2.reshape(-1), y, N, K, ncols, nthreads)
     return y.reshape(ncols, N)
 
 

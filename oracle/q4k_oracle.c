@@ -589,6 +589,94 @@ void orc_q4k_gemv(const uint8_t *w, const uint8_t *xq, float *y, int64_t N, int6
     free(st);
 }
 
+/* ------------------------------------------------------------------------ */
+/* llama.cpp's CPU Q4_K path, restated: the timed CPU baseline              */
+/* ------------------------------------------------------------------------ */
+/* On the CPU, ggml multiplies Q4_K rows by activations quantized to Q8_K
+ * rather than Q8_1: blocks of 256 int8 values with one fp32 scale and the
+ * sixteen sums of 16 values (block_q8_K: float d; int8 qs[256];
+ * int16 bsums[16], 292 bytes).  Restated here from the published algorithm
+ * of ggml's quantize_row_q8_K and generic vec_dot_q4_K_q8_K (llama.cpp
+ * commit 169e4a7f, which the reference pins in tools/setup-llama-cpp.sh),
+ * with the integer dots on the same vectorised helpers as above.  It times
+ * the CPU path the reference itself runs on the host; it is not a parity
+ * target. */
+#define Q8K_BYTES 292
+
+void orc_quantize_q8_K(const float *x, uint8_t *y, int64_t K, int32_t ncols) {
+    const int64_t nb = K / QK_K;
+    for (int32_t c = 0; c < ncols; ++c)
+        for (int64_t b = 0; b < nb; ++b) {
+            const float *xb = x + (int64_t)c * K + b * QK_K;
+            uint8_t *out = y + ((int64_t)c * nb + b) * Q8K_BYTES;
+            float amax = 0.0f, mx = 0.0f; /* the value of largest magnitude, with its sign */
+            for (int j = 0; j < QK_K; ++j)
+                if (fabsf(xb[j]) > amax) {
+                    amax = fabsf(xb[j]);
+                    mx = xb[j];
+                }
+            int8_t q[QK_K];
+            int16_t bs[16];
+            float d = 0.0f;
+            if (amax == 0.0f) {
+                memset(q, 0, sizeof q);
+            } else {
+                /* that value maps to -127; the far side may reach +128,
+                 * which is clipped to 127 */
+                const float iscale = -127.0f / mx;
+                for (int j = 0; j < QK_K; ++j) {
+                    const int v = (int)nearbyintf(iscale * xb[j]);
+                    q[j] = (int8_t)(v < 127 ? v : 127);
+                }
+                d = 1.0f / iscale;
+            }
+            for (int g = 0; g < 16; ++g) {
+                int s = 0;
+                for (int l = 0; l < 16; ++l) s += q[16 * g + l];
+                bs[g] = (int16_t)s;
+            }
+            memcpy(out, &d, 4);
+            memcpy(out + 4, q, QK_K);
+            memcpy(out + 4 + QK_K, bs, sizeof bs);
+        }
+}
+
+/* y[c][r] = sum over superblocks of d_x d_y sum_s sc_s P_s
+ *                                 - dmin_x d_y sum_s m_s (bsums_2s + bsums_2s+1),
+ * with P_s the exact int32 dot of sub-block s (ggml's vec_dot_q4_K_q8_K). */
+void orc_q4k_q8k_gemv(const uint8_t *w, const uint8_t *yq, float *y, int64_t N, int64_t K,
+                      int32_t ncols, int32_t nthreads) {
+    const int64_t nsb = K / QK_K;
+    if (nthreads < 1) nthreads = 1;
+    const sb_dots_fn dots = sb_dots();
+#pragma omp parallel for num_threads(nthreads) schedule(static)
+    for (int64_t r = 0; r < N; ++r) {
+        for (int32_t c = 0; c < ncols; ++c) {
+            const uint8_t *ycol = yq + (int64_t)c * nsb * Q8K_BYTES;
+            float sumf = 0.0f;
+            for (int64_t b = 0; b < nsb; ++b) {
+                const uint8_t *blk = w + (r * nsb + b) * Q4K_BYTES;
+                const uint8_t *yb = ycol + b * Q8K_BYTES;
+                float yd;
+                int16_t bs[16];
+                memcpy(&yd, yb, 4);
+                memcpy(bs, yb + 4 + QK_K, sizeof bs);
+                int32_t P[8];
+                dots(blk + 16, (const int8_t *)(yb + 4), P);
+                int32_t sumi = 0, summ = 0;
+                for (int s = 0; s < 8; ++s) {
+                    int sc, m;
+                    scale_min(blk + 4, s, &sc, &m);
+                    sumi += P[s] * sc;
+                    summ += (bs[2 * s] + bs[2 * s + 1]) * m;
+                }
+                sumf += (half_at(blk) * yd) * (float)sumi - (half_at(blk + 2) * yd) * (float)summ;
+            }
+            y[(int64_t)c * N + r] = sumf;
+        }
+    }
+}
+
 void orc_q4k_gemv_slices(const uint8_t *w, const uint8_t *xq, float *v, int64_t N,
                          int64_t K, int32_t ncols) {
     const int32_t nsb = (int32_t)(K / QK_K);

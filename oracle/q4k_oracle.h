@@ -70,6 +70,12 @@ void orc_swiglu(const float *gate, const float *up, float *y, int64_t n);
 void orc_q4k_partials(const uint8_t *w, const uint8_t *xq, int32_t *P, int32_t *M,
                       int64_t N, int64_t K, int32_t ncols);
 /* Canonical fp32 GEMV, y[c][r].  nthreads > 1 uses OpenMP over rows. */
+/* llama.cpp's CPU Q4_K path restated (the timed CPU baseline, not a parity
+ * target): Q8_K activation blocks (fp32 d, 256 int8, 16 int16 sums; 292 B)
+ * and the Q4_K x Q8_K dot; nthreads > 1 uses OpenMP over rows. */
+void orc_quantize_q8_K(const float *x, uint8_t *y, int64_t K, int32_t ncols);
+void orc_q4k_q8k_gemv(const uint8_t *w, const uint8_t *yq, float *y, int64_t N, int64_t K,
+                      int32_t ncols, int32_t nthreads);
 void orc_q4k_gemv(const uint8_t *w, const uint8_t *xq, float *y, int64_t N, int64_t K,
                   int32_t ncols, int32_t nthreads);
 /* Canonical per-slice values v[c][r][8] (the eight K-slice sums before the

@@ -203,3 +203,32 @@ def test_vectorised_integer_dots_give_the_same_bits():
     for y, v in outs[1:]:
         assert np.array_equal(y, outs[0][0]) and np.array_equal(v, outs[0][1])
     assert np.array_equal(O.tree8(outs[-1][1]), outs[-1][0])
+
+
+def test_cpu_baseline_q8k_path():
+    """The restated llama.cpp CPU path that bench.py times (not a parity
+    target): Q8_K blocks hold the block sums of 16 and map each block's
+    largest-magnitude value to -127; the Q4_K x Q8_K dot equals the f64 dot
+    of the dequantized operands to fp32 accuracy and stays within the
+    activation quantization of the fp32 product."""
+    N, K, ncols = 300, 2560, 3
+    w = O.gen_q4k(N, K, 4, 9)
+    x = O.gen_normal_f32((ncols, K), 12)
+    x[1, :256] = 0.0  # an all-zero block
+    yk = O.quantize_q8_K(x)
+    b = yk.reshape(ncols, K // 256, O.Q8K_BYTES)
+    d = b[:, :, :4].copy().view(np.float32)[:, :, 0]
+    q = b[:, :, 4:260].view(np.int8).astype(np.int64)
+    bs = b[:, :, 260:].copy().view(np.int16)
+    assert np.array_equal(bs, q.reshape(ncols, K // 256, 16, 16).sum(-1))
+    assert d[1, 0] == 0 and not q[1, 0].any()
+    xb = x.reshape(ncols, K // 256, 256)
+    idx = np.abs(xb).argmax(-1)
+    live = d != 0
+    assert np.all(np.take_along_axis(q, idx[..., None], -1)[..., 0][live] == -127)
+    y = O.gemv_q8k(w, yk, K, nthreads=4)
+    wd = O.dequant_q4k(w).reshape(N, K).astype(np.float64)
+    xd = (q * d[:, :, None]).reshape(ncols, K)
+    scale = np.abs(xd) @ np.abs(wd).T
+    assert np.max(np.abs(y - xd @ wd.T) / scale) < 1e-6
+    assert np.max(np.abs(y - x.astype(np.float64) @ wd.T) / (np.abs(x) @ np.abs(wd).T)) < 5e-3
