@@ -232,3 +232,11 @@ def test_cpu_baseline_q8k_path():
     scale = np.abs(xd) @ np.abs(wd).T
     assert np.max(np.abs(y - xd @ wd.T) / scale) < 1e-6
     assert np.max(np.abs(y - x.astype(np.float64) @ wd.T) / (np.abs(x) @ np.abs(wd).T)) < 5e-3
+
+
+def test_q8k_block_size_matches_gguf():
+    """The gguf package (llama.cpp's Python tooling) gives block_q8_K as 256
+    values in 292 bytes: fp32 d, 256 int8 and 16 int16 sums."""
+    gguf = pytest.importorskip("gguf")
+    assert gguf.GGML_QUANT_SIZES[gguf.GGMLQuantizationType.Q8_K] == (256, O.Q8K_BYTES)
+    assert O.quantize_q8_K(np.ones((1, 512), dtype=np.float32)).shape == (1, 2 * O.Q8K_BYTES)
