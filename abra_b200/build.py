@@ -2,7 +2,9 @@
 
 Each ``csrc/*.cu`` is compiled to an object in ``abra_b200/_build/`` (in
 parallel), then linked into ``abra_b200/libabra_b200.so`` with the static CUDA
-runtime.  NCCL is not linked: collectives go through torch.distributed.
+runtime.  NCCL is not linked: the tensor-parallel exchange is a peer-memory
+push from the MMVQ epilogue over NVLink (CUDA IPC mappings), and
+torch.distributed only carries the IPC handles and barriers.
 
     python abra_b200/build.py [--force] [--verbose]
 """
