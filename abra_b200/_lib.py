@@ -38,6 +38,8 @@ SIGNATURES: dict[str, tuple] = {
     "abra_q4k_mmvq_combined": (C.c_int, [_i32, _vp, _fp, _vp, _fp, _i64, _i64, _i32, _vp]),
     "abra_q4k_mmvq_combined_static": (C.c_int, [_i32, _vp, _fp, _fp, _i64, _i64, _i32, _vp]),
     "launch_pinned_upstream_q8_1_quantize": (None, [_fp, _vp, _i64, _vp]),
+    "quantize_row_q4_K_upstream_cpu": (None, [_vp, _vp, _i64]),
+    "dequantize_row_q4_K_upstream_cpu": (None, [_vp, _vp, _i64]),
     "abra_rmsnorm_quantize_q8_1": (C.c_int, [_fp, _fp, _f32, _vp, _fp, _i64, _i32, _vp]),
     "abra_gen_q4k": (C.c_int, [_vp, _i64, _u64, _u64, _i64, _vp]),
     "abra_gen_uniform_f32": (C.c_int, [_fp, _i64, _u64, _u64, _i64, _f32, _f32, _vp]),
@@ -87,6 +89,8 @@ SIGNATURES: dict[str, tuple] = {
     "abra_model_tp_connect": (C.c_int, [_vp, _vp, _i32]),
     "abra_model_load_tensor": (C.c_int, [_vp, _i32, _i32, _i32, _vp, C.c_uint64]),
     "abra_tp_tensor_slice": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _vp]),
+    "abra_model_path": (C.c_int, [_vp, C.POINTER(C.c_int32)]),
+    "abra_persist_plan": (C.c_int, [_vp, _i32, _vp]),
 }
 
 

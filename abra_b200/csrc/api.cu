@@ -189,6 +189,10 @@ int abra_q4k_mmvq_combined(int32_t candidate, const void *w, const float *x, voi
     int rc = check_mmvq_args(w, xq, y, N, K, ncols, N);
     if (rc) return rc;
     if (reinterpret_cast<uintptr_t>(x) & 3u) return fail(ABRA_E_INVALID, "x must be 4-byte aligned");
+    // resolve the candidate before anything is launched: a refused call
+    // leaves the Q8_1 buffer untouched
+    const int id = candidate ? candidate : abra_tune_get(N, K, ncols, 1);
+    if (!abra::mmvq_candidate_by_id(id)) return fail(ABRA_E_INVALID, "unknown candidate id %d", id);
     cudaError_t e = abra::launch_quantize_q8_1(x, xq, K, ncols, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
     return mmvq_common(w, nullptr, xq, y, N, K, ncols, N, candidate, 0, stream);

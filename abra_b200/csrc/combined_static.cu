@@ -21,6 +21,12 @@
 //   * The first call on each device sets up the scratch address for that
 //     device (cudaGetSymbolAddress, with that device current); make that
 //     first call before any stream capture.
+//   * That address is kept for the life of the process.  cudaDeviceReset (or
+//     anything else that destroys the device's primary context) reloads the
+//     array elsewhere, so after it this entry point must not be called again
+//     on that device in the same process.
+//   * A refused call (bad sizes or candidate id) launches nothing and leaves
+//     the scratch as it was.
 #include <cstdint>
 #include <mutex>
 

@@ -37,6 +37,7 @@ enum : unsigned {
     ERR_WAIT_TIMEOUT = 1u << 0,  // a consumer's wait for staged data gave up
     ERR_FLAG_TIMEOUT = 1u << 1,  // a cross-rank flag wait gave up
     ERR_WAIT_EMPTY = 1u << 2,    // a producer's wait for a free stage gave up
+    ERR_GRID_TIMEOUT = 1u << 3,  // a grid-wide barrier of the persistent decode gave up
 };
 
 // Wall-clock bound of every spin-wait in these kernels (nanoseconds).
@@ -175,6 +176,17 @@ __device__ __forceinline__ void scale_min_pair(uint32_t s0, uint32_t s1, uint32_
         sc1 = ((c >> 8) & 0xF) | ((((a >> 8) & 0xFF) >> 6) << 4);
         m0 = ((c & 0xFF) >> 4) | (((b & 0xFF) >> 6) << 4);
         m1 = (((c >> 8) & 0xFF) >> 4) | ((((b >> 8) & 0xFF) >> 6) << 4);
+    }
+}
+
+// 6-bit scale and min of sub-block j (get_scale_min_k4, tests/q4k_q8_test.cu:44-52).
+__host__ __device__ __forceinline__ void scale_min_one(const uint8_t *q, int j, int &sc, int &m) {
+    if (j < 4) {
+        sc = q[j] & 63;
+        m = q[j + 4] & 63;
+    } else {
+        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
     }
 }
 

@@ -58,6 +58,39 @@ cudaError_t launch_pos_advance(int32_t *pos, int n, int max_ctx, bool pdl, cudaS
 cudaError_t launch_swiglu_quant(const float *g, const float *u, void *y, int64_t n, bool pdl,
                                 cudaStream_t s);
 
+// ------------------------------------------------ persistent decode step ---
+// One batch-1 decode token of the all-Q4_K model as one cooperative kernel
+// (decode_persistent.cu); bit-identical to the kernel chain.
+struct PersistLayer {
+    const uint8_t *wqkv, *wo, *wgate, *wup, *wdown;
+    const float *attn_norm, *q_norm, *k_norm, *ffn_norm;
+};
+struct PersistModel {
+    int n_layers, hidden, n_heads, n_kv, ffn, vocab, max_ctx;
+    float eps;
+    const PersistLayer *layers;  // device array of n_layers entries
+    const uint8_t *embd;
+    const float *out_norm;
+    float *h0, *h1, *delta, *qkv, *att, *part_m, *part_l, *part_o, *act, *logits;
+    uint8_t *oq;
+    void *kc, *vc;  // fp16 caches [layer][kv head][max_ctx][128]
+    const float *rope;
+    int32_t *tokens, *picks, *pos;
+    const int32_t *nprompt;
+    unsigned long long *amax;
+    void *sync;  // persist_sync_bytes() zeroed bytes: barrier and arrival counters
+};
+size_t persist_sync_bytes(int n_kv);
+// False (with a reason) when the shape does not fit the kernel's ring and
+// shared-memory plan; the model then runs the kernel chain.
+bool persist_supported(int hidden, int n_heads, int n_kv, int ffn, int head_dim, const char **why);
+// Kernel attributes and the co-residency check (outside stream capture).
+cudaError_t persist_prepare(int hidden, int n_heads, int n_kv, int ffn);
+cudaError_t launch_persist_step(const PersistModel &pm, cudaStream_t st);
+// Host-side walk of every weight copy the kernel would issue on `sms` SMs.
+bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn, int vocab, int sms,
+                        int64_t out[9], const char **why);
+
 // Generator variants (gen_quant.cu).
 cudaError_t launch_gen_q4k_ex(void *dst, int64_t nblocks, uint64_t seed, uint64_t tensor_id,
                               int64_t block_offset, int flags, cudaStream_t stream);

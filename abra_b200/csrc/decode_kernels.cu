@@ -13,17 +13,6 @@
 
 namespace abra {
 
-// 6-bit scale and min of sub-block j (get_scale_min_k4, tests/q4k_q8_test.cu:44-52).
-__device__ __forceinline__ void scale_min_one(const uint8_t *q, int j, int &sc, int &m) {
-    if (j < 4) {
-        sc = q[j] & 63;
-        m = q[j + 4] & 63;
-    } else {
-        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
-        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
-    }
-}
-
 // ---------------------------------------------------------------- embed ---
 // h = dequant(E[tokens[*pos]]): w = fmaf(d * sc, q, -(dmin * m)).  Sequence
 // blockIdx.y of a batch reads tokens + y * tok_stride and writes h + y * hidden.

@@ -1,0 +1,1213 @@
+// decode_persistent.cu -- one decode token of the batch-1 Q4_K model as ONE
+// cooperative kernel: one CTA per SM, eight consumer warps and one producer
+// warp each.
+//
+// The kernel-chain step (model.cu, record_step) is ~290 dependent launches
+// per token, each paying launch, ramp and drain.  Here the token is a
+// sequence of phases separated by grid-wide barriers, and the weights of
+// every GEMV phase stream into a shared-memory ring AHEAD of the data
+// dependency: weights do not depend on activations, so the producer warp of
+// each CTA walks its whole token's share of the weight rows -- layer by
+// layer, phase by phase -- and only ever waits for a free ring slot.  While
+// the consumers work through attention or wait at a barrier, HBM keeps
+// streaming the next phases' rows.
+//
+// Phases of layer l (a grid barrier after each):
+//   QKV   residual add + RMSNorm + Q8_1 in every CTA's shared memory (layer 0:
+//         the token's embedding row dequantized in place), then the fused
+//         q|k|v MMVQ -> qkv
+//   ATT   per (kv head g, 256-position chunk c): QK-RMSNorm + NEOX RoPE of the
+//         group's q heads; on the chunk holding the current position also the
+//         k/v heads, appended to the fp16 cache; the chunk's softmax partials;
+//         one chunk: the CTA merges its heads itself; more: the last chunk of
+//         each group to finish (arrival counter) merges the group -> oq (Q8_1)
+//   O     MMVQ of oq -> delta
+//   GU    residual add + RMSNorm + Q8_1, fused gate/up SwiGLU MMVQ -> act
+//   DOWN  Q8_1 of act in every CTA's shared memory, MMVQ -> delta
+// then OUT: residual add + RMSNorm + Q8_1, the tied output MMVQ with the
+// argmax keys; the last CTA to arrive appends the greedy pick and advances
+// the position.
+//
+// Every value is computed by the same arithmetic, in the same order, as the
+// kernel chain (mmvq_impl.cuh, decode_kernels.cu, gen_quant.cu) and so as the
+// CPU oracle (oracle/model_oracle.c): logits and tokens are bit-identical to
+// both.  Data written inside the launch is read through L2 (ld.global.cg) or
+// from this CTA's shared memory, never through the non-coherent path.
+//
+// GEMV units: a unit is R consecutive rows (R = 8, 4, 2 or 1 per phase, so
+// that a unit fits one ring slot); lane (r, p) = r + R p of the consuming
+// warp owns superblocks p, p + 32/R, ... of row r and computes each whole
+// superblock value in registers (the eight exact int32 sub-block dots by
+// dp4a and the canonical fp32 tree); the lane of p == 0 then sums its row
+// over the eight canonical K-slices.
+//
+// Ring protocol: ticket t of a CTA (its t-th unit over the token) goes to
+// slot t % NSLOT (16 slots, or 8 when the activations of a wide or many-head
+// shape leave less shared memory), phase t / NSLOT of that slot's full/empty
+// mbarriers.  Within a GEMV phase unit u goes to consumer warp u % 8 (NSLOT
+// is a multiple of 8, so ticket t - NSLOT of the same phase belongs to the
+// same warp, which consumed it before waiting on t; across phases all
+// consumers pass a CTA barrier) -- so no parity wait can alias a phase two
+// ahead.
+//
+// Every wait is bounded (1 s of %globaltimer): a grid barrier that gives up
+// sets ERR_GRID_TIMEOUT in the device error word, later barriers of the
+// launch then pass at once, and named CTA barriers are never skipped, so the
+// kernel always ends.  The producer drains its own bulk copies before it
+// exits.  No copy uses cluster multicast.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "decode.cuh"
+#include "kernels.cuh"
+#include "mmvq_impl.cuh"
+#include "quant_common.cuh"
+
+namespace abra {
+
+namespace {
+
+constexpr int ATT_CHUNK_P = 256;              // attention positions per chunk (as the kernel chain)
+constexpr int PK_NCW = 8;                      // consumer warps: the canonical 256 lanes
+constexpr int PK_THREADS = (PK_NCW + 1) * 32;  // + the producer warp
+constexpr int PK_NSLOT = 16;                   // ring slots (8 when shared memory is short)
+// One ring slot: 8 rows x 10 superblocks at an odd pitch of 16-byte chunks
+// (eight rows of a 2560-wide Q4_K matrix); every phase picks its rows per
+// unit so that a unit fits.
+constexpr int PK_SLOT_BYTES = 8 * 1456;
+static_assert(PK_NSLOT % PK_NCW == 0 && PK_NSLOT / 2 == PK_NCW, "slots: 16 or 8, multiples of the consumer warps");
+// Activation record of one superblock in shared memory: its 256 int8 quants,
+// then d8[8] and A[8] = d8 * sum(q) per 32-block (fp32), padded to 336 bytes
+// = 21 16-byte chunks, so eight consecutive superblocks' records start in
+// eight distinct bank groups.
+constexpr int PK_AREC = 336;
+// Per-warp staging of the superblock values of one unit (rows x superblocks
+// x matrices <= 80: a unit fits an 11,648-byte slot).
+constexpr int PK_VMAX = 80;
+
+// GEMV kinds (index of the per-phase plan) and consumer phases.
+enum : int { PK_QKV = 0, PK_O = 1, PK_GU = 2, PK_DOWN = 3, PK_OUT = 4, PK_KINDS = 5 };
+enum : int { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_OUT = 5 };
+
+struct PkParams {
+    const PersistLayer *layers;  // device array, n_layers entries
+    const uint8_t *embd;
+    const float *out_norm;
+    int n_layers, hidden, n_heads, n_kv, ffn, vocab, max_ctx, max_chunks;
+    float eps, scale;
+    float *h[2];
+    float *delta, *qkv, *att, *part_m, *part_l, *part_o, *act, *logits;
+    uint8_t *oq;
+    __half *kc, *vc;
+    const float *rope;
+    int32_t *tokens, *picks, *pos;
+    const int32_t *nprompt;
+    unsigned long long *amax;
+    unsigned long long *bar, *gen;  // grid barrier arrivals, launches completed
+    unsigned *head_cnt;             // merge arrivals per kv head
+    int lr[PK_KINDS], pitch[PK_KINDS];  // log2 rows per unit and staged row pitch per GEMV kind
+    int slot_shift;                     // log2 of the ring slots (4: 16 slots, 3: 8)
+    int off_vbuf, off_arec, off_x, off_ring, smem;  // dynamic shared memory layout
+};
+
+#ifdef ABRA_PK_TRACE
+// Diagnostic build only: %globaltimer stamps of each CTA's phase starts,
+// ends and end of inputs (consumers) and of the producer's last copy of each
+// phase.
+constexpr int PK_TRACE_EV = 512;
+__device__ unsigned long long g_pk_trace[160][4][PK_TRACE_EV];
+#define PK_STAMP(kind, idx)                                                                            \
+    do {                                                                                               \
+        if ((idx) < PK_TRACE_EV && blockIdx.x < 160) g_pk_trace[blockIdx.x][kind][idx] = globaltimer_ns(); \
+    } while (0)
+#else
+#define PK_STAMP(kind, idx) \
+    do {                    \
+    } while (0)
+#endif
+
+// ------------------------------------------------------------ helpers ---
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void red_relaxed_gpu_add(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ bool pk_aborted() {
+    return (*static_cast<volatile unsigned *>(&g_abra_device_error) & ERR_GRID_TIMEOUT) != 0;
+}
+// Thread 0 of a CTA whose consumers have passed a CTA barrier after their
+// last writes of the phase: publish the CTA's arrival (release at GPU scope:
+// the fence orders every write the CTA barrier made visible to this thread).
+__device__ __forceinline__ void pk_arrive(unsigned long long *bar) {
+    fence_acq_rel_gpu();
+    red_relaxed_gpu_add(bar, 1ull);
+}
+// Thread 0: wait until every CTA has arrived (bounded; after one timeout in
+// this launch the remaining barriers pass at once), then acquire.
+__device__ __forceinline__ void pk_wait(const unsigned long long *bar, unsigned long long target) {
+    if (ld_relaxed_gpu(bar) < target && !pk_aborted()) {
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t i = 1;; ++i) {
+            if (ld_relaxed_gpu(bar) >= target) break;
+            if ((i & 63u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+                report_error(ERR_GRID_TIMEOUT);
+                break;
+            }
+        }
+    }
+    fence_acq_rel_gpu();
+}
+__device__ __forceinline__ void cta_sync() { named_bar_sync(1, PK_NCW * 32); }
+
+struct PkMm {
+    const uint8_t *w0, *w1;
+    int N, nsb, lr, pitch;
+};
+
+// GEMV kind of producer phase ph (per layer q|k|v, o, gate/up, down; then
+// the output).
+__device__ __forceinline__ int pk_kind(int ph, int nph) { return ph == nph - 1 ? PK_OUT : (ph & 3); }
+
+// The weight matrix (or gate/up pair) of GEMV `kind` of `layer`.
+__device__ __forceinline__ PkMm pk_mm(const PkParams &P, int layer, int kind) {
+    PkMm mm;
+    mm.w1 = nullptr;
+    mm.lr = P.lr[kind];
+    mm.pitch = P.pitch[kind];
+    const int nsb_h = P.hidden / QK_K;
+    if (kind == PK_OUT) {
+        mm.w0 = P.embd;
+        mm.N = P.vocab;
+        mm.nsb = nsb_h;
+        return mm;
+    }
+    const PersistLayer &L = P.layers[layer];
+    if (kind == PK_QKV) {
+        mm.w0 = L.wqkv;
+        mm.N = (P.n_heads + 2 * P.n_kv) * 128;
+        mm.nsb = nsb_h;
+    } else if (kind == PK_O) {
+        mm.w0 = L.wo;
+        mm.N = P.hidden;
+        mm.nsb = P.n_heads * 128 / QK_K;
+    } else if (kind == PK_GU) {
+        mm.w0 = L.wgate;
+        mm.w1 = L.wup;
+        mm.N = P.ffn;
+        mm.nsb = nsb_h;
+    } else {
+        mm.w0 = L.wdown;
+        mm.N = P.hidden;
+        mm.nsb = P.ffn / QK_K;
+    }
+    return mm;
+}
+
+// This CTA's contiguous share [u_begin, u_begin + nu) of the GEMV's units.
+__device__ __forceinline__ void pk_range(const PkMm &mm, int &u_begin, int &nu) {
+    const int total = (mm.N + (1 << mm.lr) - 1) >> mm.lr;
+    u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * total / gridDim.x);
+    nu = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x) - u_begin;
+}
+
+// ----------------------------------------------------------- producer ---
+__device__ __forceinline__ void pk_producer(const PkParams &P, uint8_t *ring, uint64_t *full, uint64_t *empty) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t pol = policy_evict_first();
+    uint32_t t = 0;
+    bool ok = true;
+    const int nph = 4 * P.n_layers + 1;
+    const int sh = P.slot_shift;
+    const uint32_t nslot = 1u << sh, smask = nslot - 1u;
+    for (int ph = 0; ph < nph && ok; ++ph) {
+        const PkMm mm = pk_mm(P, ph >> 2, pk_kind(ph, nph));
+        const int nmat = mm.w1 ? 2 : 1, R = 1 << mm.lr;
+        const uint32_t row_bytes = static_cast<uint32_t>(mm.nsb) * Q4K_BYTES;
+        int u_begin, nu;
+        pk_range(mm, u_begin, nu);
+        const int m = lane >> mm.lr, r = lane & (R - 1);  // lane -> (matrix, row of the unit)
+        for (int u = 0; u < nu; ++u, ++t) {
+            const int s = static_cast<int>(t & smask);
+            const uint32_t k = t >> sh;
+            if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1, ERR_WAIT_EMPTY)) {
+                ok = false;
+                break;
+            }
+            const int row0 = (u_begin + u) * R, nvalid = min(R, mm.N - row0);
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], nmat * nvalid * row_bytes);
+            __syncwarp();
+            if (m < nmat && r < nvalid) {
+                uint8_t *dst = ring + s * PK_SLOT_BYTES + (m * R + r) * mm.pitch;
+                const uint8_t *src = (m ? mm.w1 : mm.w0) + static_cast<int64_t>(row0 + r) * row_bytes;
+                bulk_g2s(dst, src, row_bytes, &full[s], pol);
+            }
+        }
+        if (lane == 0) PK_STAMP(2, ph);
+    }
+    if (ok && P.n_layers > 0) {
+        // the next token starts with this CTA's q|k|v rows of layer 0: into L2
+        const PkMm mm = pk_mm(P, 0, PK_QKV);
+        int u_begin, nu;
+        pk_range(mm, u_begin, nu);
+        const int64_t row_bytes = static_cast<int64_t>(mm.nsb) * Q4K_BYTES;
+        const int64_t row0 = static_cast<int64_t>(u_begin) << mm.lr;
+        const int64_t rows = min(static_cast<int64_t>(nu) << mm.lr, static_cast<int64_t>(mm.N) - row0);
+        const uint8_t *base = mm.w0 + row0 * row_bytes;
+        const int64_t bytes = rows > 0 ? rows * row_bytes : 0;  // a multiple of 16 (144 per block)
+        constexpr int64_t PIECE = 16384;
+        for (int64_t o = static_cast<int64_t>(lane) * PIECE; o < bytes; o += 32 * PIECE)
+            prefetch_l2_bulk(base + o, static_cast<uint32_t>(min(PIECE, bytes - o)));
+    }
+    // drain: every copy this warp issued has landed before the CTA can exit
+    if (lane == 0) {
+        const uint32_t first = t > nslot ? t - nslot : 0;
+        for (uint32_t tt = first; tt < t; ++tt) mbar_wait(&full[tt & smask], (tt >> sh) & 1);
+    }
+    __syncwarp();
+}
+
+// --------------------------------------------------- consumer: GEMV units ---
+// Value of one superblock of NMAT weight rows against the staged activation
+// record: the arithmetic of vec_dot_q4_K_q8_1 in the canonical order of
+// mmvq_q4k_kernel (exact int32 sub-block dots by dp4a, t_s = d8_s *
+// float(P_s * sc_s), u_s = A_s * float(m_s), S = ((0+1)+(2+3))+((4+5)+(6+7)),
+// fmaf(d, S_t, -(dmin * S_u))), all eight sub-blocks in one lane.
+template <int NMAT>
+__device__ __forceinline__ void pk_sb_value(const uint8_t *const (&wsb)[NMAT], const uint8_t *arec,
+                                            float (&v)[NMAT]) {
+    uint4 hdr[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) hdr[m] = *reinterpret_cast<const uint4 *>(wsb[m]);
+    float t[NMAT][8], u[NMAT][8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float2 d8 = *reinterpret_cast<const float2 *>(arec + 256 + 8 * q);
+        const float2 A = *reinterpret_cast<const float2 *>(arec + 288 + 8 * q);
+        const uint4 a0 = *reinterpret_cast<const uint4 *>(arec + 64 * q);
+        const uint4 a1 = *reinterpret_cast<const uint4 *>(arec + 64 * q + 16);
+        const uint4 a2 = *reinterpret_cast<const uint4 *>(arec + 64 * q + 32);
+        const uint4 a3 = *reinterpret_cast<const uint4 *>(arec + 64 * q + 48);
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            int sc0, m0, sc1, m1;
+            scale_min_pair(hdr[m].y, hdr[m].z, hdr[m].w, q, sc0, m0, sc1, m1);
+            const uint4 qa = *reinterpret_cast<const uint4 *>(wsb[m] + 16 + 32 * q);
+            const uint4 qb = *reinterpret_cast<const uint4 *>(wsb[m] + 32 + 32 * q);
+            int s0 = 0, s1 = 0;
+            s0 = dp4a_ss(static_cast<int>(qa.x & 0x0F0F0F0Fu), static_cast<int>(a0.x), s0);
+            s1 = dp4a_us(qa.x & 0xF0F0F0F0u, static_cast<int>(a2.x), s1);
+            s0 = dp4a_ss(static_cast<int>(qa.y & 0x0F0F0F0Fu), static_cast<int>(a0.y), s0);
+            s1 = dp4a_us(qa.y & 0xF0F0F0F0u, static_cast<int>(a2.y), s1);
+            s0 = dp4a_ss(static_cast<int>(qa.z & 0x0F0F0F0Fu), static_cast<int>(a0.z), s0);
+            s1 = dp4a_us(qa.z & 0xF0F0F0F0u, static_cast<int>(a2.z), s1);
+            s0 = dp4a_ss(static_cast<int>(qa.w & 0x0F0F0F0Fu), static_cast<int>(a0.w), s0);
+            s1 = dp4a_us(qa.w & 0xF0F0F0F0u, static_cast<int>(a2.w), s1);
+            s0 = dp4a_ss(static_cast<int>(qb.x & 0x0F0F0F0Fu), static_cast<int>(a1.x), s0);
+            s1 = dp4a_us(qb.x & 0xF0F0F0F0u, static_cast<int>(a3.x), s1);
+            s0 = dp4a_ss(static_cast<int>(qb.y & 0x0F0F0F0Fu), static_cast<int>(a1.y), s0);
+            s1 = dp4a_us(qb.y & 0xF0F0F0F0u, static_cast<int>(a3.y), s1);
+            s0 = dp4a_ss(static_cast<int>(qb.z & 0x0F0F0F0Fu), static_cast<int>(a1.z), s0);
+            s1 = dp4a_us(qb.z & 0xF0F0F0F0u, static_cast<int>(a3.z), s1);
+            s0 = dp4a_ss(static_cast<int>(qb.w & 0x0F0F0F0Fu), static_cast<int>(a1.w), s0);
+            s1 = dp4a_us(qb.w & 0xF0F0F0F0u, static_cast<int>(a3.w), s1);
+            s1 >>= 4;  // exact: the masked high nibbles carry a factor of 16
+            t[m][2 * q] = __fmul_rn(d8.x, __int2float_rn(s0 * sc0));
+            t[m][2 * q + 1] = __fmul_rn(d8.y, __int2float_rn(s1 * sc1));
+            u[m][2 * q] = __fmul_rn(A.x, static_cast<float>(m0));
+            u[m][2 * q + 1] = __fmul_rn(A.y, static_cast<float>(m1));
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+        const float St = __fadd_rn(__fadd_rn(__fadd_rn(t[m][0], t[m][1]), __fadd_rn(t[m][2], t[m][3])),
+                                   __fadd_rn(__fadd_rn(t[m][4], t[m][5]), __fadd_rn(t[m][6], t[m][7])));
+        const float Su = __fadd_rn(__fadd_rn(__fadd_rn(u[m][0], u[m][1]), __fadd_rn(u[m][2], u[m][3])),
+                                   __fadd_rn(__fadd_rn(u[m][4], u[m][5]), __fadd_rn(u[m][6], u[m][7])));
+        const float d = half_lo(hdr[m].x), dmin = half_hi(hdr[m].x);
+        v[m] = __fmaf_rn(d, St, -__fmul_rn(dmin, Su));
+    }
+}
+
+// A row's value from its staged superblock values: sequential within each of
+// the eight canonical K-slices, then the fixed tree over the slices.
+__device__ __forceinline__ float pk_row_sum(const float *vrow, int nsb) {
+    float sl[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int b0 = slice_start(nsb, i), b1 = slice_start(nsb, i + 1);
+        float acc = 0.0f;
+        for (int b = b0; b < b1; ++b) acc = b == b0 ? vrow[b] : __fadd_rn(acc, vrow[b]);
+        sl[i] = acc;
+    }
+    return tree_sum<8>(sl);
+}
+
+// The units of one GEMV phase that belong to this warp (unit u of the CTA's
+// range -> warp u % 8, ring slot (T + u) % NSLOT).  The superblock values
+// meet in this warp's staging buffer and the lane of p == 0 sums its row in
+// the canonical order, then stores y (and merges the argmax key).
+template <int NMAT>
+__device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, uint32_t T, const uint8_t *ring,
+                                         uint64_t *full, uint64_t *empty, float *vbuf, const uint8_t *arec,
+                                         float *Y, unsigned long long *s_amax, int sh, bool &poisoned) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int lr = mm.lr, R = 1 << lr, P = 32 >> lr;
+    const int r = lane & (R - 1), p = lane >> lr;
+    const int nsb = mm.nsb, N = mm.N;
+    const uint32_t smask = (1u << sh) - 1u;
+    for (int u = warp; u < nu; u += PK_NCW) {
+        const uint32_t t = T + static_cast<uint32_t>(u);
+        const int s = static_cast<int>(t & smask);
+        if (!poisoned && !mbar_wait(&full[s], (t >> sh) & 1)) poisoned = true;
+        const uint8_t *wrow[NMAT];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) wrow[m] = ring + s * PK_SLOT_BYTES + (m * R + r) * mm.pitch;
+        for (int b = p; b < nsb; b += P) {
+            const uint8_t *wsb[NMAT];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) wsb[m] = wrow[m] + b * Q4K_BYTES;
+            float v[NMAT];
+            pk_sb_value<NMAT>(wsb, arec + b * PK_AREC, v);
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) vbuf[(m * R + r) * nsb + b] = v[m];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // the slot's weights are consumed
+        const int row = ((u_begin + u) << lr) + r;
+        float yv = 0.0f;
+        if (lane < R) {
+            yv = pk_row_sum(vbuf + r * nsb, nsb);
+            if constexpr (NMAT == 2) yv = __fmul_rn(pk_row_sum(vbuf + (R + r) * nsb, nsb), abra_silu(yv));
+            if (row < N) Y[row] = yv;
+        }
+        if (s_amax) {
+            unsigned long long key = (lane < R && row < N) ? argmax_key(yv, row) : 0ull;
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                key = k2 > key ? k2 : key;
+            }
+            if (lane == 0) atomicMax(s_amax, key);
+        }
+        __syncwarp();  // the staging buffer is reused by the next unit
+    }
+}
+
+// --------------------------------------- consumer: activation prologues ---
+// Immutable RMSNorm weights into shared memory (done before the barrier that
+// releases the phase).
+__device__ __forceinline__ void pk_stage_norm(const float *w, float *s_w, int K) {
+    for (int i = threadIdx.x * 4; i < K; i += PK_NCW * 32 * 4)
+        *reinterpret_cast<float4 *>(s_w + i) = __ldg(reinterpret_cast<const float4 *>(w + i));
+}
+
+// Element i of the token's embedding row (embed_kernel's arithmetic).
+__device__ __forceinline__ float pk_embed(const uint8_t *row, int i) {
+    const int b = i >> 8, r = i & 255, p = r >> 6, hh = (r >> 5) & 1, l = r & 31;
+    const uint8_t *blk = row + b * Q4K_BYTES;
+    const float d = __half2float(*reinterpret_cast<const __half *>(blk));
+    const float dmin = __half2float(*reinterpret_cast<const __half *>(blk + 2));
+    int sc, m;
+    scale_min_one(blk + 4, 2 * p + hh, sc, m);
+    const int byte = blk[16 + 32 * p + l];
+    const int q = hh ? (byte >> 4) : (byte & 15);
+    const float a = __fmul_rn(d, static_cast<float>(sc));
+    const float bm = __fmul_rn(dmin, static_cast<float>(m));
+    return __fmaf_rn(a, static_cast<float>(q), -bm);
+}
+
+// Q8_1 block i of an activation into the records: quants, d8, A = d8 * sum.
+__device__ __forceinline__ void pk_put_block(uint8_t *arec, int i, int sub, uint32_t packed, float d8,
+                                             int sum) {
+    uint8_t *rec = arec + (i >> 3) * PK_AREC;
+    const int s = i & 7;
+    *reinterpret_cast<uint32_t *>(rec + 32 * s + 4 * sub) = packed;
+    if (sub == 0) {
+        reinterpret_cast<float *>(rec + 256)[s] = d8;
+        reinterpret_cast<float *>(rec + 288)[s] = __fmul_rn(d8, __int2float_rn(sum));
+    }
+}
+
+// The reference Q8_1 rounding of four values of a 32-block, eight lanes per
+// block (lane & 7 = the quarter of eight values... four consecutive values
+// each): d = amax / 127, q = roundf(x / d), the block's integer sum; then the
+// block into the records.
+__device__ __forceinline__ void pk_quant4(uint8_t *arec, int i, int sub, float x0, float x1, float x2, float x3) {
+    float amax = fmaxf(fmaxf(fabsf(x0), fabsf(x1)), fmaxf(fabsf(x2), fabsf(x3)));
+    amax = fmaxf(0.0f, amax);
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const int q0 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x0, id)))));
+    const int q1 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x1, id)))));
+    const int q2 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x2, id)))));
+    const int q3 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x3, id)))));
+    int sum = (q0 + q1) + (q2 + q3);
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+    const uint32_t packed = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
+                            ((static_cast<uint32_t>(q2) & 0xffu) << 16) | (static_cast<uint32_t>(q3) << 24);
+    pk_put_block(arec, i, sub, packed, __half2float(__float2half_rn(d)), sum);
+}
+
+// x = h_in + delta (or the embedding row erow), written to h_out by CTA 0;
+// then RMSNorm * w and Q8_1 into the activation records: the XIN prologue of
+// mmvq_q4k_kernel, operation for operation.
+__device__ __forceinline__ void pk_xin(int K, const float *h_in, const float *delta, const uint8_t *erow,
+                                       float *h_out, float *s_x, const float *s_w, float eps, uint8_t *arec,
+                                       float *s_nred) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float acc = 0.0f;
+    for (int i0 = t; i0 < K; i0 += 256 * 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = i0 + k * 256;
+            v[k] = i < K ? (erow ? pk_embed(erow, i) : __ldcg(h_in + i)) : 0.0f;
+        }
+        if (delta) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int i = i0 + k * 256;
+                if (i < K) v[k] = __fadd_rn(v[k], __ldcg(delta + i));
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = i0 + k * 256;
+            if (i < K) {
+                if (blockIdx.x == 0) h_out[i] = v[k];
+                s_x[i] = v[k];
+                acc = __fmaf_rn(v[k], v[k], acc);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+    if (lane == 0) s_nred[warp] = acc;
+    cta_sync();
+    float total = s_nred[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) total = __fadd_rn(total, s_nred[w]);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), eps)));
+    const int nblk = K / QK8_1;
+    const int sub = lane & 7;
+    for (int b0 = warp * 4; b0 < nblk; b0 += PK_NCW * 4) {  // warp-uniform: nblk % 8 == 0
+        const int i = b0 + (lane >> 3);
+        const float4 xv = *reinterpret_cast<const float4 *>(s_x + i * QK8_1 + sub * 4);
+        const float4 wv = *reinterpret_cast<const float4 *>(s_w + i * QK8_1 + sub * 4);
+        pk_quant4(arec, i, sub, __fmul_rn(__fmul_rn(xv.x, r), wv.x), __fmul_rn(__fmul_rn(xv.y, r), wv.y),
+                  __fmul_rn(__fmul_rn(xv.z, r), wv.z), __fmul_rn(__fmul_rn(xv.w, r), wv.w));
+    }
+    cta_sync();
+}
+
+// Q8_1 of an fp32 activation written earlier in this launch (the SwiGLU
+// output), straight into the records: the bytes quantize_q8_1_kernel writes
+// and mmvq_q4k_kernel stages.
+__device__ __forceinline__ void pk_quant_f32(const float *x, int K, uint8_t *arec) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane & 7;
+    const int nblk = K / QK8_1;
+    for (int b0 = warp * 4; b0 < nblk; b0 += PK_NCW * 4) {  // warp-uniform: nblk % 8 == 0
+        const int i = b0 + (lane >> 3);
+        const float4 xv = __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + sub * 4));
+        pk_quant4(arec, i, sub, xv.x, xv.y, xv.z, xv.w);
+    }
+    cta_sync();
+}
+
+// Q8_1 blocks written earlier in this launch (oq) into the records (the
+// staging loop of mmvq_q4k_kernel, loads through L2): eight lanes per block,
+// one 32-bit word of quants each.
+__device__ __forceinline__ void pk_stage_q8(const uint8_t *X, int K, uint8_t *arec) {
+    const int nblk = K / QK8_1;
+    const int lane = threadIdx.x & 31, sub = lane & 7;
+    for (int i = (threadIdx.x >> 3); i < nblk; i += PK_NCW * 4) {  // warp-uniform: nblk % 8 == 0
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(X + static_cast<int64_t>(i) * Q81_BYTES);
+        const uint32_t qw = __ldcg(src + 1 + sub);
+        const uint32_t h = __ldcg(src);
+        int msum = dp4a_ss(0x01010101, static_cast<int>(qw), 0);
+#pragma unroll
+        for (int m = 4; m >= 1; m >>= 1) msum += __shfl_xor_sync(0xffffffffu, msum, m);
+        pk_put_block(arec, i, sub, qw, half_lo(h), msum);
+    }
+    cta_sync();
+}
+
+// ------------------------------------------------ consumer: attention ---
+// QK-RMSNorm + NEOX RoPE of one head (qk_norm_rope_kv_kernel's arithmetic):
+// lane owns elements 4 lane .. 4 lane + 3; nw and cs staged in shared memory.
+__device__ __forceinline__ void pk_norm_rope(const float *x128, const float *nw, const float *cs,
+                                             float eps, int lane, float (&o)[4]) {
+    const float4 xv = __ldcg(reinterpret_cast<const float4 *>(x128 + 4 * lane));
+    const float x[4] = {xv.x, xv.y, xv.z, xv.w};
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc = __fmaf_rn(x[k], x[k], acc);
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, 128.0f), eps)));
+    float y[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) y[k] = __fmul_rn(__fmul_rn(x[k], r), nw[4 * lane + k]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float partner = __shfl_xor_sync(0xffffffffu, y[k], 16);
+        const int i = 4 * (lane & 15) + k;
+        const float c = cs[2 * i], s = cs[2 * i + 1];
+        if (lane < 16)
+            o[k] = __fmaf_rn(y[k], c, -__fmul_rn(partner, s));
+        else
+            o[k] = __fmaf_rn(partner, s, __fmul_rn(y[k], c));
+    }
+}
+
+// The merged output x of one q head (lane: dims 4 lane .. 4 lane + 3) to
+// att and its four Q8_1 blocks to oq (attention_merge_quant_kernel's
+// epilogue).
+__device__ __forceinline__ void pk_head_out(const PkParams &P, int hq, const float (&x)[4], int lane) {
+    *reinterpret_cast<float4 *>(P.att + static_cast<int64_t>(hq) * 128 + 4 * lane) = make_float4(x[0], x[1], x[2], x[3]);
+    float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+    amax = fmaxf(0.0f, amax);
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    int qv[4], sum = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        qv[k] = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x[k], id)))));
+        sum += qv[k];
+    }
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+    uint32_t *o32 = reinterpret_cast<uint32_t *>(P.oq + (static_cast<int64_t>(hq) * 4 + (lane >> 3)) * Q81_BYTES);
+    o32[1 + (lane & 7)] = (static_cast<uint32_t>(qv[0]) & 0xffu) | ((static_cast<uint32_t>(qv[1]) & 0xffu) << 8) |
+                          ((static_cast<uint32_t>(qv[2]) & 0xffu) << 16) | ((static_cast<uint32_t>(qv[3]) & 0xffu) << 24);
+    if ((lane & 7) == 0) {
+        const uint32_t hd = __half_as_ushort(__float2half_rn(d));
+        const uint32_t hs = __half_as_ushort(__float2half_rn(__fmul_rn(d, static_cast<float>(sum))));
+        o32[0] = hd | (hs << 16);
+    }
+}
+
+// Merge of one q head over nch chunks from the partials in global memory
+// (attention_merge_quant_kernel's arithmetic, read through L2).
+__device__ __forceinline__ void pk_merge_head(const PkParams &P, int hq, int nch, int lane) {
+    const int mc = P.max_chunks;
+    const float *pm = P.part_m + static_cast<int64_t>(hq) * mc;
+    const float *pl = P.part_l + static_cast<int64_t>(hq) * mc;
+    float M = __ldcg(pm);
+    for (int c = 1; c < nch; ++c) M = fmaxf(M, __ldcg(pm + c));
+    float Ls = 0.0f, O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int c = 0; c < nch; ++c) {
+        const float wc = abra_expf(__fsub_rn(__ldcg(pm + c), M));
+        Ls = __fmaf_rn(__ldcg(pl + c), wc, Ls);
+        const float4 o = __ldcg(reinterpret_cast<const float4 *>(
+            P.part_o + (static_cast<int64_t>(hq) * mc + c) * 128 + 4 * lane));
+        O[0] = __fmaf_rn(o.x, wc, O[0]);
+        O[1] = __fmaf_rn(o.y, wc, O[1]);
+        O[2] = __fmaf_rn(o.z, wc, O[2]);
+        O[3] = __fmaf_rn(o.w, wc, O[3]);
+    }
+    float x[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x[k] = __fdiv_rn(O[k], Ls);
+    pk_head_out(P, hq, x, lane);
+}
+
+// Shared-memory plan of the attention phase (floats): q[GQ][128],
+// e[GQ][256], red[GQ][8], o[8][GQ][128], then the staged q/k norm weights
+// and RoPE row (3 x 128), then the new k and v rows (fp16, 2 x 128 = 128
+// floats).
+__host__ __device__ constexpr int pk_att_floats(int gq) {
+    return gq * (128 + ATT_CHUNK_P + 8) + 8 * gq * 128 + 3 * 128 + 128;
+}
+
+// Inputs of the attention phase that do not depend on the previous phase,
+// staged before its barrier.
+__device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int pos, int gq, float *scr) {
+    float *s_in = scr + gq * (128 + ATT_CHUNK_P + 8) + 8 * gq * 128;
+    const PersistLayer &Ly = P.layers[layer];
+    const int t = threadIdx.x;
+    if (t < 128) {
+        s_in[t] = Ly.q_norm[t];
+        s_in[128 + t] = Ly.k_norm[t];
+        s_in[256 + t] = P.rope[static_cast<int64_t>(pos) * 128 + t];
+    }
+}
+
+// Attention of layer `layer` at position pos: items (kv head g, chunk c)
+// over the CTAs; each item is attention_chunk_kernel<GQ>'s arithmetic on
+// 256 positions, the group's q heads normed and rotated in place.  The
+// current position's k and v rows are also kept in shared memory for the
+// item that reads them.  One chunk: the CTA merges its own heads; more: the
+// last chunk of each group to finish merges the group from the partials.
+template <int GQ>
+__device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int pos, float *scr, unsigned *s_flag) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float(*s_q)[128] = reinterpret_cast<float(*)[128]>(scr);                              // [GQ][128]
+    float(*s_e)[ATT_CHUNK_P] = reinterpret_cast<float(*)[ATT_CHUNK_P]>(scr + GQ * 128);    // [GQ][256]
+    float(*s_red)[8] = reinterpret_cast<float(*)[8]>(scr + GQ * (128 + ATT_CHUNK_P));      // [GQ][8]
+    float *s_o = scr + GQ * (128 + ATT_CHUNK_P + 8);                                       // [8][GQ][128]
+    float *s_in = s_o + 8 * GQ * 128;                                                      // norms, rope row
+    __half *s_knew = reinterpret_cast<__half *>(s_in + 3 * 128);                           // [128]
+    __half *s_vnew = s_knew + 128;                                                         // [128]
+    const int L = pos + 1, nch = (L + ATT_CHUNK_P - 1) / ATT_CHUNK_P;
+    const int nkv = P.n_kv, max_ctx = P.max_ctx, mc = P.max_chunks;
+    const size_t kv_layer = static_cast<size_t>(nkv) * max_ctx * 128;
+    __half *kc = P.kc + layer * kv_layer, *vc = P.vc + layer * kv_layer;
+    const int items = nkv * nch;
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        const int g = it % nkv, c = it / nkv;
+        const bool tail = c == nch - 1;
+        // the group's q heads; on the chunk holding pos also the k and v
+        // heads, appended to the cache (rounded to fp16) and kept here
+        for (int hv = warp; hv < GQ + (tail ? 2 : 0); hv += PK_NCW) {
+            if (hv < GQ) {
+                float o[4];
+                pk_norm_rope(P.qkv + static_cast<int64_t>(g * GQ + hv) * 128, s_in, s_in + 256, P.eps, lane, o);
+                *reinterpret_cast<float4 *>(&s_q[hv][4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
+            } else if (hv == GQ) {
+                float o[4];
+                pk_norm_rope(P.qkv + static_cast<int64_t>(P.n_heads + g) * 128, s_in + 128, s_in + 256, P.eps, lane, o);
+                __half *dst = kc + (static_cast<int64_t>(g) * max_ctx + pos) * 128 + 4 * lane;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    dst[k] = __float2half_rn(o[k]);
+                    s_knew[4 * lane + k] = __float2half_rn(o[k]);
+                }
+            } else {
+                const float4 xv = __ldcg(reinterpret_cast<const float4 *>(
+                    P.qkv + static_cast<int64_t>(P.n_heads + nkv + g) * 128 + 4 * lane));
+                const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+                __half *dst = vc + (static_cast<int64_t>(g) * max_ctx + pos) * 128 + 4 * lane;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    dst[k] = __float2half_rn(xs[k]);
+                    s_vnew[4 * lane + k] = __float2half_rn(xs[k]);
+                }
+            }
+        }
+        cta_sync();
+        const int j = c * ATT_CHUNK_P + t;
+        const bool valid = j < L;
+        float s[GQ];
+#pragma unroll
+        for (int h = 0; h < GQ; ++h) s[h] = 0.0f;
+        if (valid) {
+            // earlier positions come from the cache (written by earlier
+            // launches), the current one from shared memory
+            const uint4 *krow = j == pos ? reinterpret_cast<const uint4 *>(s_knew)
+                                         : reinterpret_cast<const uint4 *>(kc + (static_cast<int64_t>(g) * max_ctx + j) * 128);
+            // the row's 16 loads issued together (two halves of 8 for eight
+            // heads, to bound registers); the fmaf order over d is unchanged
+            constexpr int KP = GQ > 4 ? 8 : 16;
+#pragma unroll
+            for (int h0 = 0; h0 < 16; h0 += KP) {
+                uint4 kv[KP];
+#pragma unroll
+                for (int d8 = 0; d8 < KP; ++d8) kv[d8] = krow[h0 + d8];
+#pragma unroll
+                for (int d8 = 0; d8 < KP; ++d8) {
+                    const __half2 *k2 = reinterpret_cast<const __half2 *>(&kv[d8]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 kf = __half22float2(k2[e]);
+#pragma unroll
+                        for (int h = 0; h < GQ; ++h) {
+                            const float2 qv = *reinterpret_cast<const float2 *>(&s_q[h][(h0 + d8) * 8 + 2 * e]);
+                            s[h] = __fmaf_rn(qv.x, kf.x, s[h]);
+                            s[h] = __fmaf_rn(qv.y, kf.y, s[h]);
+                        }
+                    }
+                }
+            }
+        }
+        float mxs[GQ];
+#pragma unroll
+        for (int h = 0; h < GQ; ++h) {
+            const float sv = valid ? __fmul_rn(s[h], P.scale) : -INFINITY;
+            float mx = sv;
+#pragma unroll
+            for (int m = 16; m >= 1; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+            if (lane == 0) s_red[h][warp] = mx;
+            s[h] = sv;
+        }
+        cta_sync();
+        float ev[GQ];
+#pragma unroll
+        for (int h = 0; h < GQ; ++h) {
+            float mx = s_red[h][0];
+#pragma unroll
+            for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_red[h][w]);
+            mxs[h] = mx;
+            ev[h] = valid ? abra_expf(__fsub_rn(s[h], mx)) : 0.0f;
+            s_e[h][t] = ev[h];
+            if (t == 0 && nch > 1) P.part_m[static_cast<int64_t>(g * GQ + h) * mc + c] = mx;
+        }
+        cta_sync();  // s_red is reused for the sums
+#pragma unroll
+        for (int h = 0; h < GQ; ++h) {
+            float v = ev[h];
+#pragma unroll
+            for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+            if (lane == 0) s_red[h][warp] = v;
+        }
+        __syncwarp();
+        float acc[GQ][4];
+#pragma unroll
+        for (int h = 0; h < GQ; ++h)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc[h][k] = 0.0f;
+        const int j0 = c * ATT_CHUNK_P + warp * 32;
+        const int nv = max(0, min(32, L - j0));
+        const __half *vbase = vc + (static_cast<int64_t>(g) * max_ctx + j0) * 128 + 4 * lane;
+#pragma unroll
+        for (int g8 = 0; g8 < 4; ++g8) {
+            if (g8 * 8 >= nv) break;
+            uint2 vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int jj = j0 + g8 * 8 + u;
+                if (g8 * 8 + u < nv)
+                    vv[u] = *reinterpret_cast<const uint2 *>(jj == pos ? s_vnew + 4 * lane : vbase + (g8 * 8 + u) * 128);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (g8 * 8 + u < nv) {
+                    const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vv[u].x));
+                    const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vv[u].y));
+                    const float vf[4] = {v01.x, v01.y, v23.x, v23.y};
+#pragma unroll
+                    for (int h = 0; h < GQ; ++h) {
+                        const float e = s_e[h][warp * 32 + g8 * 8 + u];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) acc[h][k] = __fmaf_rn(e, vf[k], acc[h][k]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < GQ; ++h)
+            *reinterpret_cast<float4 *>(s_o + (warp * GQ + h) * 128 + 4 * lane) =
+                make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        cta_sync();
+        if (nch == 1) {
+            // one chunk: merge this CTA's heads in place (the merge's
+            // arithmetic on the chunk's own max, sum and output)
+            if (warp < GQ) {
+                const int h = warp;
+                float l = s_red[h][0];
+#pragma unroll
+                for (int w = 1; w < 8; ++w) l = __fadd_rn(l, s_red[h][w]);
+                const float wc = abra_expf(__fsub_rn(mxs[h], mxs[h]));
+                const float Ls = __fmaf_rn(l, wc, 0.0f);
+                float x[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int d = 4 * lane + k;
+                    float o = s_o[h * 128 + d];
+#pragma unroll
+                    for (int w = 1; w < 8; ++w) o = __fadd_rn(o, s_o[(w * GQ + h) * 128 + d]);
+                    x[k] = __fdiv_rn(__fmaf_rn(o, wc, 0.0f), Ls);
+                }
+                pk_head_out(P, g * GQ + h, x, lane);
+            }
+            cta_sync();  // the scratch is reused by the next item
+            continue;
+        }
+        for (int i = t; i < GQ * 128; i += 256) {
+            const int h = i / 128, d = i % 128;
+            float o = s_o[h * 128 + d];
+#pragma unroll
+            for (int w = 1; w < 8; ++w) o = __fadd_rn(o, s_o[(w * GQ + h) * 128 + d]);
+            P.part_o[(static_cast<int64_t>(g * GQ + h) * mc + c) * 128 + d] = o;
+        }
+        if (t < GQ) {
+            float l = s_red[t][0];
+#pragma unroll
+            for (int w = 1; w < 8; ++w) l = __fadd_rn(l, s_red[t][w]);
+            P.part_l[static_cast<int64_t>(g * GQ + t) * mc + c] = l;
+        }
+        // the last chunk of the group to finish merges its heads
+        cta_sync();
+        if (t == 0) {
+            __threadfence();
+            const unsigned last = atomicAdd(&P.head_cnt[g], 1u) + 1u == static_cast<unsigned>(nch) ? 1u : 0u;
+            if (last) P.head_cnt[g] = 0u;
+            *s_flag = last;
+        }
+        cta_sync();
+        if (*s_flag) {
+            __threadfence();
+            if (warp < GQ) pk_merge_head(P, g * GQ + warp, nch, lane);
+        }
+        cta_sync();  // the scratch is reused by the next item
+    }
+}
+
+// --------------------------------------------------------------- kernel ---
+template <int GQ>
+__global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float s_nred[8];
+    __shared__ unsigned long long s_amax;
+    __shared__ unsigned s_flag;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + PK_NSLOT;
+    uint8_t *ring = smem + P.off_ring;
+    const int pos = __ldcg(P.pos);
+    if (pos < 0 || pos >= P.max_ctx) return;  // the host never steps past max_ctx
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < (1 << P.slot_shift); ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x >= PK_NCW * 32) {
+        pk_producer(P, ring, full, empty);
+        return;
+    }
+    // ------------------------------------------------------ consumers ---
+    const int t = threadIdx.x;
+    float *vbuf = reinterpret_cast<float *>(smem + P.off_vbuf) + (t >> 5) * PK_VMAX;
+    uint8_t *arec = smem + P.off_arec;
+    float *scr = reinterpret_cast<float *>(smem + P.off_x);
+    const int L = P.n_layers, hidden = P.hidden;
+    float *s_x = scr, *s_w = scr + hidden;
+    const unsigned long long G = gridDim.x;
+    const int nev = 5 * L + 1;  // phases of the token; a grid barrier between consecutive ones
+    unsigned long long kb = *reinterpret_cast<volatile unsigned long long *>(P.gen) * static_cast<unsigned long long>(nev);
+    uint32_t T = 0;
+    bool poisoned = false;
+    int cur = 0;
+    const uint8_t *erow = P.embd + static_cast<int64_t>(__ldcg(P.tokens + pos)) * (hidden / QK_K) * Q4K_BYTES;
+    for (int e = 0; e < nev; ++e) {
+        const int l = e / 5;
+        const int ph = e == nev - 1 ? PH_OUT : e % 5;
+        const bool xin = ph == PH_QKV || ph == PH_GU || ph == PH_OUT;
+        // inputs that do not depend on the previous phase, staged before its barrier
+        if (xin)
+            pk_stage_norm(ph == PH_OUT ? P.out_norm : ph == PH_QKV ? P.layers[l].attn_norm : P.layers[l].ffn_norm,
+                          s_w, hidden);
+        else if (ph == PH_ATT)
+            pk_stage_att(P, l, pos, GQ, scr);
+        if (ph == PH_OUT && t == 0) s_amax = 0ull;
+        if (e > 0) {
+            ++kb;
+            if (t == 0) pk_wait(P.bar, kb * G);
+        }
+        if (t == 0) PK_STAMP(0, e);
+        cta_sync();
+        // the phase's activation
+        if (xin) {
+            const bool first = ph == PH_QKV ? l == 0 : L == 0;  // the embedding row, no residual delta
+            pk_xin(hidden, P.h[cur], first ? nullptr : P.delta, first ? erow : nullptr, P.h[cur ^ 1], s_x, s_w,
+                   P.eps, arec, s_nred);
+            cur ^= 1;
+        } else if (ph == PH_O) {
+            pk_stage_q8(P.oq, P.n_heads * 128, arec);
+        } else if (ph == PH_DOWN) {
+            pk_quant_f32(P.act, P.ffn, arec);
+        }
+        if (t == 0) PK_STAMP(3, e);
+        // the phase's work
+        if (ph == PH_ATT) {
+            pk_attention<GQ>(P, l, pos, scr, &s_flag);
+        } else {
+            const int kind = ph == PH_QKV ? PK_QKV : ph == PH_O ? PK_O : ph == PH_GU ? PK_GU : ph == PH_DOWN ? PK_DOWN : PK_OUT;
+            float *Y = ph == PH_QKV ? P.qkv : ph == PH_GU ? P.act : ph == PH_OUT ? P.logits : P.delta;
+            const PkMm mm = pk_mm(P, l, kind);
+            int u_begin, nu;
+            pk_range(mm, u_begin, nu);
+            unsigned long long *amax = ph == PH_OUT ? &s_amax : nullptr;
+            if (mm.w1)
+                pk_units<2>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
+            else
+                pk_units<1>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
+            T += static_cast<uint32_t>(nu);
+        }
+        cta_sync();
+        if (t == 0) PK_STAMP(1, e);
+        if (e < nev - 1 && t == 0) pk_arrive(P.bar);
+    }
+    // the greedy pick: the last CTA to arrive decodes the merged key
+    if (t == 0) {
+        atomicMax(P.amax, s_amax);
+        __threadfence();
+        const unsigned long long old = atom_add_acq_rel_gpu(P.bar, 1ull);
+        if (old + 1ull == (kb + 1ull) * G) {  // the last CTA of the launch
+            __threadfence();
+            const unsigned long long key = __ldcg(P.amax);
+            *P.amax = 0ull;
+            const int bi = static_cast<int>(0xFFFFFFFFu - static_cast<unsigned>(key & 0xFFFFFFFFull));
+            P.picks[pos] = bi;
+            if (pos + 1 >= __ldcg(P.nprompt)) P.tokens[pos + 1] = bi;
+            *P.pos = pos + 1;
+            *P.gen = *reinterpret_cast<volatile unsigned long long *>(P.gen) + 1ull;
+            __threadfence();
+        }
+    }
+}
+
+using PkKernel = void (*)(const PkParams);
+
+PkKernel pk_kernel_for(int gq) {
+    switch (gq) {
+        case 1: return decode_token_kernel<1>;
+        case 2: return decode_token_kernel<2>;
+        case 4: return decode_token_kernel<4>;
+        case 8: return decode_token_kernel<8>;
+        default: return nullptr;
+    }
+}
+
+// ------------------------------------------------------------ planning ---
+struct PkPlan {
+    int rows[PK_KINDS], pitch[PK_KINDS];
+    int slot_shift;
+    int off_vbuf, off_arec, off_x, off_ring, smem;
+};
+
+int pk_align(int v, int a) { return (v + a - 1) / a * a; }
+
+// Row pitch (bytes) of a staged unit of R rows of nsb superblocks: the
+// smallest count of 16-byte chunks >= the row that keeps the lanes of each
+// quarter warp (lane = r + R p: R rows x 8 / R superblock positions) in
+// distinct bank groups: odd for 8 rows, 2 mod 4 for 4, 4 mod 8 for 2.
+int pk_pitch(int nsb, int R) {
+    int pc = nsb * Q4K_BYTES / 16;
+    auto good = [&](int c) {
+        switch (R) {
+            case 8: return (c & 1) == 1;
+            case 4: return (c & 3) == 2;
+            case 2: return (c & 7) == 4;
+            default: return true;
+        }
+    };
+    while (!good(pc)) ++pc;
+    return pc * 16;
+}
+
+int log2i(int v) {
+    int l = 0;
+    while ((1 << l) < v) ++l;
+    return l;
+}
+
+// Rows per unit and row pitch of each GEMV, chosen by the critical path of
+// the phase on `sms` CTAs (superblock passes of the busiest warp plus its row
+// sums), and the shared-memory layout.
+bool pk_plan(int hidden, int n_heads, int n_kv, int ffn, int head_dim, int vocab, int sms, PkPlan &pl,
+             const char **why) {
+    auto no = [&](const char *w) {
+        if (why) *why = w;
+        return false;
+    };
+    if (head_dim != 128 || n_kv <= 0 || n_heads % n_kv) return no("head layout");
+    const int gq = n_heads / n_kv;
+    if (gq != 1 && gq != 2 && gq != 4 && gq != 8) return no("q heads per kv head must be 1, 2, 4 or 8");
+    if (hidden % QK_K || ffn % QK_K || (n_heads * 128) % QK_K || hidden <= 0 || ffn <= 0 || vocab <= 0)
+        return no("dimensions must be multiples of 256");
+    if (sms < 1) sms = 1;
+    const int nsb[PK_KINDS] = {hidden / QK_K, n_heads * 128 / QK_K, hidden / QK_K, ffn / QK_K, hidden / QK_K};
+    const int nmat[PK_KINDS] = {1, 1, 2, 1, 1};
+    const int64_t N[PK_KINDS] = {static_cast<int64_t>(n_heads + 2 * n_kv) * 128, hidden, ffn, hidden, vocab};
+    for (int k = 0; k < PK_KINDS; ++k) {
+        pl.rows[k] = 0;
+        int64_t best = -1;
+        for (int R : {8, 4, 2, 1}) {
+            const int pitch = pk_pitch(nsb[k], R);
+            if (nmat[k] * R * pitch > PK_SLOT_BYTES || nmat[k] * R * nsb[k] > PK_VMAX) continue;
+            const int64_t units = (N[k] + R - 1) / R;
+            const int64_t per_cta = (units + sms - 1) / sms;
+            const int64_t per_warp = (per_cta + PK_NCW - 1) / PK_NCW;
+            const int64_t passes = (nsb[k] + 32 / R - 1) / (32 / R);
+            const int64_t cost = per_warp * (16 * passes * nmat[k] + nsb[k] * nmat[k]);
+            if (best < 0 || cost < best) {
+                best = cost;
+                pl.rows[k] = R;
+                pl.pitch[k] = pitch;
+            }
+        }
+        if (!pl.rows[k]) return no("a row does not fit a ring slot");
+    }
+    const int nsb_max = std::max(std::max(hidden, n_heads * 128), ffn) / QK_K;
+    const int scratch = std::max(8 * hidden, 4 * pk_att_floats(gq));
+    int o = 16 * PK_NSLOT;  // full + empty mbarriers (room for 16 slots)
+    pl.off_vbuf = pk_align(o, 16);
+    o = pl.off_vbuf + PK_NCW * PK_VMAX * 4;
+    pl.off_arec = pk_align(o, 128);
+    o = pl.off_arec + nsb_max * PK_AREC;
+    pl.off_x = pk_align(o, 16);
+    o = pl.off_x + scratch;
+    pl.off_ring = pk_align(o, 128);
+    for (int shift : {4, 3}) {  // 16 slots, or 8 when the activations leave less room
+        pl.slot_shift = shift;
+        pl.smem = pl.off_ring + (1 << shift) * PK_SLOT_BYTES;
+        if (pl.smem <= kMmvqMaxSmem) return true;
+    }
+    return no("shared memory");
+}
+
+}  // namespace
+
+size_t persist_sync_bytes(int n_kv) { return static_cast<size_t>(pk_align(16 + 4 * n_kv, 256)); }
+
+bool persist_supported(int hidden, int n_heads, int n_kv, int ffn, int head_dim, const char **why) {
+    PkPlan pl;
+    return pk_plan(hidden, n_heads, n_kv, ffn, head_dim, 1, 148, pl, why);
+}
+
+cudaError_t persist_prepare(int hidden, int n_heads, int n_kv, int ffn) {
+    PkPlan pl;
+    if (!pk_plan(hidden, n_heads, n_kv, ffn, 128, 1, device_sm_count(), pl, nullptr)) return cudaErrorInvalidValue;
+    PkKernel fn = pk_kernel_for(n_heads / n_kv);
+    if (!fn) return cudaErrorInvalidValue;
+    cudaError_t e = ensure_smem_attr_ptr(reinterpret_cast<const void *>(fn));
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, PK_THREADS, pl.smem);
+    if (e != cudaSuccess) return e;
+    return per_sm < 1 ? cudaErrorCooperativeLaunchTooLarge : cudaSuccess;
+}
+
+cudaError_t launch_persist_step(const PersistModel &pm, cudaStream_t st) {
+    PkPlan pl;
+    const int sms = device_sm_count();
+    if (!pk_plan(pm.hidden, pm.n_heads, pm.n_kv, pm.ffn, 128, pm.vocab, sms, pl, nullptr))
+        return cudaErrorInvalidValue;
+    PkKernel fn = pk_kernel_for(pm.n_heads / pm.n_kv);
+    if (!fn) return cudaErrorInvalidValue;
+    PkParams P = {};
+    P.layers = pm.layers;
+    P.embd = pm.embd;
+    P.out_norm = pm.out_norm;
+    P.n_layers = pm.n_layers;
+    P.hidden = pm.hidden;
+    P.n_heads = pm.n_heads;
+    P.n_kv = pm.n_kv;
+    P.ffn = pm.ffn;
+    P.vocab = pm.vocab;
+    P.max_ctx = pm.max_ctx;
+    P.max_chunks = (pm.max_ctx + ATT_CHUNK_P - 1) / ATT_CHUNK_P;
+    P.eps = pm.eps;
+    P.scale = static_cast<float>(1.0 / std::sqrt(128.0));
+    P.h[0] = pm.h0;
+    P.h[1] = pm.h1;
+    P.delta = pm.delta;
+    P.qkv = pm.qkv;
+    P.att = pm.att;
+    P.part_m = pm.part_m;
+    P.part_l = pm.part_l;
+    P.part_o = pm.part_o;
+    P.act = pm.act;
+    P.logits = pm.logits;
+    P.oq = pm.oq;
+    P.kc = static_cast<__half *>(pm.kc);
+    P.vc = static_cast<__half *>(pm.vc);
+    P.rope = pm.rope;
+    P.tokens = pm.tokens;
+    P.picks = pm.picks;
+    P.pos = pm.pos;
+    P.nprompt = pm.nprompt;
+    P.amax = pm.amax;
+    uint8_t *sync = static_cast<uint8_t *>(pm.sync);
+    P.bar = reinterpret_cast<unsigned long long *>(sync);
+    P.gen = P.bar + 1;
+    P.head_cnt = reinterpret_cast<unsigned *>(sync + 16);
+    for (int k = 0; k < PK_KINDS; ++k) {
+        P.lr[k] = log2i(pl.rows[k]);
+        P.pitch[k] = pl.pitch[k];
+    }
+    P.slot_shift = pl.slot_shift;
+    P.off_vbuf = pl.off_vbuf;
+    P.off_arec = pl.off_arec;
+    P.off_x = pl.off_x;
+    P.off_ring = pl.off_ring;
+    P.smem = pl.smem;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms);
+    cfg.blockDim = dim3(PK_THREADS);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, P);
+}
+
+// Host-side walk of every bulk copy the producers of `sms` CTAs would issue
+// for a model shape, checked against the ring slot and the weight tensors:
+// out = {smem, ring bytes, units of the busiest CTA, copies checked, rows per
+// unit of the five GEMVs}.  Returns false with *why set when a copy would
+// leave its slot or its tensor.
+bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn, int vocab, int sms,
+                        int64_t out[9], const char **why) {
+    PkPlan pl;
+    if (!pk_plan(hidden, n_heads, n_kv, ffn, 128, vocab, sms, pl, why)) return false;
+    const int nsb[PK_KINDS] = {hidden / QK_K, n_heads * 128 / QK_K, hidden / QK_K, ffn / QK_K, hidden / QK_K};
+    const int rows[PK_KINDS] = {(n_heads + 2 * n_kv) * 128, hidden, ffn, hidden, vocab};
+    const int nmat[PK_KINDS] = {1, 1, 2, 1, 1};
+    const int64_t nslot = int64_t(1) << pl.slot_shift;
+    int64_t max_tickets = 0, copies = 0;
+    auto fail = [&](const char *w) {
+        if (why) *why = w;
+        return false;
+    };
+    for (int b = 0; b < sms; ++b) {
+        int64_t t = 0;
+        const int nph = 4 * n_layers + 1;
+        for (int ph = 0; ph < nph; ++ph) {
+            const int kind = ph == nph - 1 ? PK_OUT : (ph & 3);
+            const int N = rows[kind], R = pl.rows[kind], pitch = pl.pitch[kind];
+            const int64_t row_bytes = static_cast<int64_t>(nsb[kind]) * Q4K_BYTES;
+            const int64_t total = (N + R - 1) / R;
+            const int u0 = static_cast<int>(b * total / sms), u1 = static_cast<int>((b + 1) * total / sms);
+            if (nmat[kind] * R * nsb[kind] > PK_VMAX || (R != 1 && R != 2 && R != 4 && R != 8))
+                return fail("unit exceeds the staging buffer");
+            for (int u = u0; u < u1; ++u, ++t) {
+                const int row0 = u * R, nvalid = std::min(R, N - row0);
+                if (nvalid <= 0 || row_bytes > pitch || (pitch & 15) || nmat[kind] * nvalid * row_bytes > (1 << 20) - 1)
+                    return fail("unit does not fit its row pitch");
+                for (int m = 0; m < nmat[kind]; ++m)
+                    for (int r = 0; r < nvalid; ++r) {
+                        const int64_t dst = (t % nslot) * PK_SLOT_BYTES + (m * R + r) * pitch;
+                        const int64_t src = static_cast<int64_t>(row0 + r) * row_bytes;
+                        const int64_t tensor = static_cast<int64_t>(N) * row_bytes;
+                        if (dst + row_bytes > nslot * PK_SLOT_BYTES || (dst & 15) || src + row_bytes > tensor ||
+                            (src & 15) || (m * R + r + 1) * pitch > PK_SLOT_BYTES)
+                            return fail("copy leaves its slot or its tensor");
+                        ++copies;
+                    }
+            }
+        }
+        max_tickets = std::max(max_tickets, t);
+    }
+    const int64_t v[9] = {pl.smem, int64_t(PK_SLOT_BYTES) << pl.slot_shift, max_tickets, copies,
+                          pl.rows[0], pl.rows[1], pl.rows[2], pl.rows[3], pl.rows[4]};
+    for (int i = 0; i < 9; ++i) out[i] = v[i];
+    return true;
+}
+
+}  // namespace abra
+
+#ifdef ABRA_PK_TRACE
+extern "C" int abra_pk_trace(unsigned long long *out, long long n) {
+    const long long all = static_cast<long long>(sizeof(abra::g_pk_trace) / 8);
+    return cudaMemcpyFromSymbol(out, abra::g_pk_trace, 8 * (n < all ? n : all)) == cudaSuccess ? 0 : -2;
+}
+#endif
+
+ABRA_ERROR_WORD_ACCESSOR(error_word_persist)

@@ -135,6 +135,12 @@ struct Model {
     size_t weight_bytes = 0, kv_bytes = 0;
     int32_t host_pos = 0;      // position after the queued steps (mirrors *pos)
     int32_t *pinned = nullptr; // 2 pinned ints for the streaming loop
+    // persistent decode step (batch 1, one GPU, all-Q4_K, unless
+    // ABRA_MODEL_KERNEL_CHAIN): one cooperative kernel per token
+    bool persist = false;
+    bool persist_eager = false;  // the cooperative launch could not be captured
+    PersistLayer *players = nullptr;
+    void *psync = nullptr;
 
     float *recv(int q, int slot) const {  // rank q's partial in slot, in peer[..]'s layout
         return reinterpret_cast<float *>(arena) + (static_cast<size_t>(slot) * sh.world + q) * cfg.hidden;
@@ -305,6 +311,23 @@ static cudaError_t build(Model &m) {
     TRY(cudaMemsetAsync(m.picks, 0, static_cast<size_t>(B) * (c.max_ctx + 1) * 4, st));
     TRY(cudaMemsetAsync(m.pos, 0, 4, st));
     TRY(cudaMemsetAsync(m.nprompt, 0, 4, st));
+    if (B == 1 && sh.world == 1 && !m.mix && !(c.flags & ABRA_MODEL_KERNEL_CHAIN) &&
+        persist_supported(c.hidden, c.n_heads, c.n_kv_heads, c.ffn, c.head_dim, nullptr)) {
+        std::vector<PersistLayer> pl(c.n_layers);
+        for (int l = 0; l < c.n_layers; ++l) {
+            const LayerW &y = m.layers[l];
+            pl[l] = {y.wqkv, y.wo, y.wgate, y.wup, y.wdown, y.attn_norm, y.q_norm, y.k_norm, y.ffn_norm};
+        }
+        if (c.n_layers > 0) {
+            TRY(alloc(m, &m.players, pl.size() * sizeof(PersistLayer)));
+            TRY(cudaMemcpyAsync(m.players, pl.data(), pl.size() * sizeof(PersistLayer),
+                                cudaMemcpyHostToDevice, st));
+        }
+        const size_t sb = persist_sync_bytes(c.n_kv_heads);
+        TRY(alloc(m, reinterpret_cast<uint8_t **>(&m.psync), sb));
+        TRY(cudaMemsetAsync(m.psync, 0, sb, st));
+        m.persist = true;
+    }
     if (sh.world > 1) {
         const size_t recv = static_cast<size_t>(2 * c.n_layers) * sh.world * c.hidden * 4;
         m.arena_recv = (recv + 255) / 256 * 256;
@@ -615,9 +638,47 @@ static int lookup_draft(const int32_t *h, int n, int key, int limit, int32_t *ou
     return 0;
 }
 
+static PersistModel persist_model(const Model &m) {
+    const abra_model_config &c = m.cfg;
+    PersistModel pm = {};
+    pm.n_layers = c.n_layers;
+    pm.hidden = c.hidden;
+    pm.n_heads = c.n_heads;
+    pm.n_kv = c.n_kv_heads;
+    pm.ffn = c.ffn;
+    pm.vocab = c.vocab;
+    pm.max_ctx = c.max_ctx;
+    pm.eps = c.eps;
+    pm.layers = m.players;
+    pm.embd = m.embd;
+    pm.out_norm = m.out_norm;
+    pm.h0 = m.h;
+    pm.h1 = m.h2;
+    pm.delta = m.delta;
+    pm.qkv = m.qkv;
+    pm.att = m.att;
+    pm.part_m = m.part_m;
+    pm.part_l = m.part_l;
+    pm.part_o = m.part_o;
+    pm.act = m.act;
+    pm.logits = m.logits;
+    pm.oq = m.oq;
+    pm.kc = m.kc;
+    pm.vc = m.vc;
+    pm.rope = m.rope;
+    pm.tokens = m.tokens;
+    pm.picks = m.picks;
+    pm.pos = m.pos;
+    pm.nprompt = m.nprompt;
+    pm.amax = m.amax;
+    pm.sync = m.psync;
+    return pm;
+}
+
 // The decode step for the token at tokens[*pos] (recorded into the graph).
 static cudaError_t record_step(const Model &m, cudaStream_t st) {
     if (m.batch > 1) return record_step_batched(m, st);
+    if (m.persist) return launch_persist_step(persist_model(m), st);
     const abra_model_config &c = m.cfg;
     const abra_tp_shard &sh = m.sh;
     const int W = sh.world;
@@ -792,6 +853,7 @@ static cudaError_t record_step(const Model &m, cudaStream_t st) {
 
 static cudaError_t prepare(const Model &m) {
     if (m.batch > 1) return prepare_mmvq_tc();
+    if (m.persist) return persist_prepare(m.cfg.hidden, m.cfg.n_heads, m.cfg.n_kv_heads, m.cfg.ffn);
     const StepShapes ss = step_shapes(m.cfg, m.sh);
     for (const int64_t *sh : {ss.qkv, ss.o, ss.gate_up, ss.down, ss.out, ss.qk}) {
         const MmvqConfig *cfg = tuned(sh);
@@ -811,16 +873,20 @@ static cudaError_t prepare(const Model &m) {
 static cudaError_t capture(Model &m) {
     if (m.graph) return cudaSuccess;
     TRY(prepare(m));  // kernel attributes are set outside the capture
-    if (m.cfg.flags & ABRA_MODEL_EAGER) return cudaSuccess;
+    if ((m.cfg.flags & ABRA_MODEL_EAGER) || m.persist_eager) return cudaSuccess;
     cudaGraph_t g = nullptr;
     TRY(cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = record_step(m, m.stream);
     cudaError_t e2 = cudaStreamEndCapture(m.stream, &g);
-    if (e != cudaSuccess) {
+    if (e != cudaSuccess || e2 != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
-        return e;
+        if (m.persist) {  // a cooperative launch this driver cannot capture: launch it per step
+            cudaGetLastError();
+            m.persist_eager = true;
+            return cudaSuccess;
+        }
+        return e != cudaSuccess ? e : e2;
     }
-    TRY(e2);
     e = cudaGraphInstantiate(&m.graph, g, 0);
     cudaGraphDestroy(g);
     return e;
@@ -859,6 +925,23 @@ int abra_model_default_config(abra_model_config *c) {
 }
 
 const char *abra_model_last_error(void) { return g_model_err; }
+
+int abra_model_path(void *model, int32_t *persistent) {
+    Model *m = static_cast<Model *>(model);
+    if (!m || !persistent) return model_fail(ABRA_E_INVALID, "null pointer", cudaSuccess);
+    *persistent = m->persist ? 1 : 0;
+    return ABRA_OK;
+}
+
+int abra_persist_plan(const abra_model_config *cfg, int32_t sms, int64_t out[9]) {
+    if (!cfg || !out || sms < 1) return model_fail(ABRA_E_INVALID, "bad arguments", cudaSuccess);
+    const char *why = "";
+    if (cfg->n_layers < 0 || cfg->vocab < 1 ||
+        !abra::persist_plan_check(cfg->n_layers, cfg->hidden, cfg->n_heads, cfg->n_kv_heads, cfg->ffn,
+                                  cfg->vocab, sms, out, &why))
+        return model_fail(ABRA_E_UNSUPPORTED, why, cudaSuccess);
+    return ABRA_OK;
+}
 
 int abra_tp_shard_info(const abra_model_config *cfg, int32_t rank, int32_t world,
                        abra_tp_shard *out) {

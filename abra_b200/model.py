@@ -38,6 +38,20 @@ EAGER = 1   # ABRA_MODEL_EAGER
 NO_PDL = 2  # ABRA_MODEL_NO_PDL
 NO_PREFETCH = 4  # ABRA_MODEL_NO_PREFETCH
 Q4_K_M = 8  # ABRA_MODEL_Q4_K_M: the real Qwen3-4B-Q4_K_M type map (Q6_K attn_v/ffn_down/output)
+KERNEL_CHAIN = 16  # ABRA_MODEL_KERNEL_CHAIN: per-operation kernels instead of the persistent step
+
+
+def persist_plan(sms: int = 148, **config) -> dict:
+    """Host-only check of the persistent decode kernel's plan for a model
+    shape (abra_persist_plan): every weight copy of every CTA checked against
+    its ring slot and its tensor.  Raises AbraError when the shape does not
+    fit the kernel."""
+    c = default_config(**config)
+    out = np.zeros(9, dtype=np.int64)
+    _check(_lib.lib.abra_persist_plan(C.byref(c), sms, out.ctypes.data), "abra_persist_plan")
+    keys = ("smem", "ring_bytes", "units_max", "copies", "rows_qkv", "rows_o", "rows_gate_up",
+            "rows_down", "rows_output")
+    return dict(zip(keys, (int(v) for v in out)))
 
 
 def lookup_draft(history, key: int, limit: int) -> np.ndarray:
@@ -213,6 +227,14 @@ class DecodeModel:
         import torch.distributed as dist
 
         dist.barrier(group=group)  # every rank mapped its peers and recorded its step
+
+    @property
+    def persistent(self) -> bool:
+        """True when each decode step is one launch of the persistent decode
+        kernel (abra_model_path), False for the per-operation kernel chain."""
+        v = C.c_int32()
+        _check(_lib.lib.abra_model_path(self.handle, C.byref(v)), "abra_model_path")
+        return bool(v.value)
 
     def close(self) -> None:
         if self.handle:

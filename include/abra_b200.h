@@ -79,9 +79,11 @@ int abra_q4k_mmvq_combined(int32_t candidate, const void *w_q4k, const float *x,
  * 131,072; larger requests return ABRA_E_UNSUPPORTED).  For callers that may
  * not allocate device memory where they multiply.  The first call on each
  * device resolves that device's scratch address; make it before any stream
- * capture.  Nothing in the scratch needs to start at zero.  Calls that can
- * overlap on one device (different streams or threads) race on the scratch.
- * This entry point has no counterpart in the reference. */
+ * capture.  That address is kept for the life of the process: after
+ * cudaDeviceReset on a device, do not call this entry point on it again.
+ * Nothing in the scratch needs to start at zero.  Calls that can overlap on
+ * one device (different streams or threads) race on the scratch.  This entry
+ * point has no counterpart in the reference. */
 int abra_q4k_mmvq_combined_static(int32_t candidate, const void *w_q4k, const float *x,
                                   float *y, int64_t N, int64_t K, int32_t ncols, void *stream);
 
@@ -137,6 +139,19 @@ int abra_q4k_mmvq_partials(const void *w_q4k, const void *x_q8_1, float *y, int3
  * (kernels/q4k/upstream_adapter.cuh:12-19): one Q8_1 column. */
 void launch_pinned_upstream_mmvq(const void *d_w_q4, const void *d_x_q8, float *d_y,
                                  int64_t N, int64_t K, void *stream);
+
+/* Drop-ins for the two host functions of the same shim
+ * (kernels/q4k/upstream_adapter.cuh:28-38), which the reference forwards to
+ * llama.cpp's quantize_row_q4_K_ref / dequantize_row_q4_K.  CPU only, no
+ * GPU needed.  x: k floats (k % 256 == 0) -> k/256 Q4_K blocks of 144 bytes
+ * (the reference declares y as block_q4_K *; the bytes are the same), by the
+ * published Q4_K algorithm (a weighted affine fit per 32-value sub-block, then
+ * 6-bit scale and min multipliers of fp16 superblock scales).  Dequantize:
+ * y = (d * sc) * q - dmin * m per value.  A k that is not a multiple of 256
+ * writes nothing and records the error for abra_last_error (the reference
+ * asserts). */
+void quantize_row_q4_K_upstream_cpu(const float *x, void *y, int64_t k);
+void dequantize_row_q4_K_upstream_cpu(const void *x, float *y, int64_t k);
 
 /* --------------------------------------------------------- Q8_1 -------- */
 /* x: ncols columns of K fp32 (K % 32 == 0) -> ncols x K/32 Q8_1 blocks.
@@ -279,8 +294,28 @@ typedef struct {
  * Q6_K tensors are generated like abra_gen_q6k from the same tensor ids (V
  * rows keep their row index in tensor 1).  One GPU, batch 1. */
 #define ABRA_MODEL_Q4_K_M 8
+/* Run the batch-1 step as the chain of per-operation kernels (one CUDA graph
+ * of ~290 launches) instead of the persistent decode kernel.  The persistent
+ * kernel is the default wherever it applies: batch 1, one GPU, all-Q4_K
+ * weights, q heads per kv head in {1, 2, 4, 8}; both give bit-identical
+ * logits and tokens. */
+#define ABRA_MODEL_KERNEL_CHAIN 16
 
 int abra_model_default_config(abra_model_config *cfg); /* Qwen3-4B, max_ctx 4096 */
+/* *persistent = 1 when each decode step of this model is one launch of the
+ * persistent decode kernel (the reference's per-token decode loop,
+ * tests/runtime_logits.cpp:59-108, as one cooperative kernel: a CTA per SM
+ * streams its share of every layer's weights through a shared-memory ring
+ * ahead of grid-wide phase barriers), 0 when it is the kernel chain. */
+int abra_model_path(void *model, int32_t *persistent);
+/* Host-only check of the persistent kernel's plan for a model shape on a GPU
+ * with `sms` SMs: walks every weight copy of every CTA's token and checks it
+ * against its ring slot and its tensor.  out = {dynamic shared memory, ring
+ * bytes (16 or 8 slots), weight units of the busiest CTA, copies checked,
+ * rows per unit of the q|k|v, o, gate/up, down and output GEMVs}.
+ * ABRA_E_UNSUPPORTED when the shape does not fit the kernel (the model then
+ * runs the kernel chain). */
+int abra_persist_plan(const abra_model_config *cfg, int32_t sms, int64_t out[9]);
 int abra_model_create(const abra_model_config *cfg, void **model);
 int abra_model_destroy(void *model);
 /* Load a prompt (token ids) and rewind to position 0 (synchronous). */

@@ -70,6 +70,21 @@ int main(void) {
     CHECK(sl[4] == 0 && sl[5] == 2560 && sl[6] == 1152 && sl[7] == 1152);
     CHECK(abra_tp_tensor_slice(&cfg, 1, 2, 0, 11, sl) == ABRA_E_INVALID);
 
+    /* the adapter's host functions: a row quantized to Q4_K and back */
+    {
+        float xr[512], yr[512];
+        unsigned char qb[2 * 144];
+        for (int i = 0; i < 512; ++i) xr[i] = (float)((i * 37) % 101 - 50) / 25.0f;
+        quantize_row_q4_K_upstream_cpu(xr, qb, 512);
+        dequantize_row_q4_K_upstream_cpu(qb, yr, 512);
+        double se = 0.0, sx = 0.0;
+        for (int i = 0; i < 512; ++i) {
+            se += (double)(xr[i] - yr[i]) * (xr[i] - yr[i]);
+            sx += (double)xr[i] * xr[i];
+        }
+        CHECK(se < 0.01 * sx);
+    }
+
     /* argument checks that fail before any launch */
     CHECK(abra_q4k_mmvq(NULL, NULL, NULL, 64, 2560, 1, NULL) == ABRA_E_INVALID);
     CHECK(abra_q4k_mmvq((void *)16, (void *)16, (float *)16, 64, 300, 1, NULL) == ABRA_E_INVALID);

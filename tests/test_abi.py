@@ -73,6 +73,10 @@ def test_rejects_bad_arguments_without_gpu():
     assert lib.abra_quantize_q8_1(16, 16, 33, 1, None) == _lib.ABRA_E_INVALID
     assert lib.abra_q4k_mmvq_combined(0, 16, None, 16, 16, 8, 256, 1, None) == _lib.ABRA_E_INVALID
     assert lib.abra_q4k_mmvq_combined(0, 16, 16, 16, 16, 8, 300, 1, None) == _lib.ABRA_E_INVALID
+    # an unknown candidate is refused before the quantize launch: with no GPU
+    # here a launch would fail as ABRA_E_CUDA, so E_INVALID shows nothing ran
+    assert lib.abra_q4k_mmvq_combined(4242, 16, 16, 16, 16, 8, 256, 1, None) == _lib.ABRA_E_INVALID
+    assert "candidate" in _lib.last_error()
     assert lib.abra_rmsnorm_quantize_q8_1(16, 16, 1e-6, 16, None, 32768, 1, None) == _lib.ABRA_E_INVALID
     assert lib.abra_rmsnorm_quantize_q8_1(16, 18, 1e-6, 16, None, 2560, 1, None) == _lib.ABRA_E_INVALID
     assert "4-byte" in _lib.last_error()

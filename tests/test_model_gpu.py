@@ -50,13 +50,64 @@ def test_small_model_logits_bit_exact_across_chunks(centered):
     c.close()
 
 
+def test_persistent_kernel_is_the_default_step():
+    """Batch 1 on one GPU with all-Q4_K weights runs the persistent decode
+    kernel; the flag selects the kernel chain; the Q4_K_M map keeps the chain."""
+    from abra_b200.model import KERNEL_CHAIN, Q4_K_M, DecodeModel
+
+    cfg = dict(n_layers=1, vocab=512, max_ctx=8)
+    with DecodeModel(**cfg) as m:
+        assert m.persistent
+    with DecodeModel(flags=KERNEL_CHAIN, **cfg) as m:
+        assert not m.persistent
+    with DecodeModel(flags=Q4_K_M, **cfg) as m:
+        assert not m.persistent
+
+
+@pytest.mark.parametrize("shape", [
+    dict(hidden=512, n_heads=4, n_kv_heads=2, ffn=1024),   # 2 q heads per kv head
+    dict(hidden=512, n_heads=8, n_kv_heads=1, ffn=768),    # 8
+    dict(hidden=256, n_heads=2, n_kv_heads=2, ffn=512),    # 1, one superblock per row
+])
+def test_persistent_gqa_shapes_bit_exact_across_chunks(shape):
+    """The persistent kernel's attention items, per-group merge counters and
+    GEMV plans on other head layouts and widths: logits bit-identical to the
+    oracle around each 256-position chunk boundary."""
+    from abra_b200.model import DecodeModel
+
+    cfg = dict(n_layers=2, vocab=1000, max_ctx=530, centered=1, seed=4, **shape)
+    g, c = DecodeModel(**cfg), O.OrcModel(**cfg)
+    assert g.persistent
+    prompt = _prompt(3, 1000, 5)
+    g.reset(prompt)
+    check = {0, 1, 2, 254, 255, 256, 257, 511, 512, 513, 528}
+    tok, picks = None, []
+    for pos in range(529):
+        feed = int(prompt[pos]) if pos < len(prompt) else tok
+        want_tok, want = c.step(feed, pos, logits=True)
+        g.step(1)
+        if pos in check:
+            got = g.logits()
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"logits differ at pos {pos}"
+        tok = want_tok
+        if pos >= 2:
+            picks.append(tok)
+    assert np.array_equal(g.tokens(530)[3:], np.array(picks, dtype=np.int32))
+    g.close()
+    c.close()
+
+
 def test_graph_eager_no_pdl_and_no_prefetch_agree():
-    from abra_b200.model import EAGER, NO_PDL, NO_PREFETCH, DecodeModel
+    """Every way of running the step -- the persistent kernel as a graph or
+    eager, the kernel chain with and without graphs, PDL and L2 prefetch --
+    gives the same tokens and logit bits."""
+    from abra_b200.model import EAGER, KERNEL_CHAIN, NO_PDL, NO_PREFETCH, DecodeModel
 
     cfg = dict(n_layers=3, vocab=2048, max_ctx=300, centered=1, seed=5)
     prompt = _prompt(7, 2048, 2)
     outs = []
-    for flags in (0, EAGER, NO_PDL, EAGER | NO_PDL, NO_PREFETCH):
+    for flags in (0, EAGER, KERNEL_CHAIN, KERNEL_CHAIN | EAGER, KERNEL_CHAIN | NO_PDL,
+                  KERNEL_CHAIN | EAGER | NO_PDL, KERNEL_CHAIN | NO_PREFETCH):
         with DecodeModel(flags=flags, **cfg) as m:
             toks = m.generate(prompt, 280)
             outs.append((toks, m.logits()))
