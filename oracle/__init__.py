@@ -381,6 +381,7 @@ def _bind_model():
         "orc_model_create": (vp, [C.POINTER(OrcModelConfig)]),
         "orc_model_destroy": (None, [vp]),
         "orc_model_step": (C.c_int32, [vp, C.c_int32, C.c_int32, vp, C.c_int32]),
+        "orc_model_step_cpu": (C.c_int32, [vp, C.c_int32, C.c_int32, C.c_int32]),
         "orc_model_generate": (None, [vp, vp, C.c_int32, C.c_int32, vp, C.c_int32]),
         "orc_model_hidden": (C.POINTER(C.c_float), [vp]),
         "orc_add_rmsnorm_quantize": (None, [_f32p, vp, _f32p, C.c_float, _u8p, _i64]),
@@ -438,6 +439,11 @@ class OrcModel:
         tok = lib.orc_model_step(self.ptr, token, pos, out.ctypes.data if logits else None,
                                  self.threads)
         return (tok, out) if logits else tok
+
+    def step_cpu(self, token: int, pos: int) -> int:
+        """One decode step on llama.cpp's CPU path (Q8_K activations): the
+        timed CPU baseline, not the canonical order."""
+        return lib.orc_model_step_cpu(self.ptr, token, pos, self.threads)
 
     def hidden(self) -> np.ndarray:
         p = lib.orc_model_hidden(self.ptr)

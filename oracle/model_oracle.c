@@ -41,6 +41,8 @@ struct orc_model {
     /* work buffers */
     float *h, *delta, *qkv, *q, *att, *act, *logits, *tmp;
     uint8_t *xq, *aq;
+    float *xn;   /* fp32 normalized activation (the llama.cpp CPU path) */
+    uint8_t *yk; /* its Q8_K blocks */
 };
 
 
@@ -161,6 +163,8 @@ orc_model *orc_model_create(const orc_model_config *cfg) {
     m->tmp = calloc((size_t)mx * 2, 4);
     m->xq = calloc((size_t)(mx / 32) * Q81_BYTES, 1);
     m->aq = calloc((size_t)(mx / 32) * Q81_BYTES, 1);
+    m->xn = calloc((size_t)mx, 4);
+    m->yk = calloc((size_t)(mx / 256) * 292, 1);
     return m;
 }
 
@@ -174,6 +178,7 @@ void orc_model_destroy(orc_model *m) {
     free(m->L); free(m->embd); free(m->out_norm); free(m->kcache); free(m->vcache);
     free(m->rope); free(m->h); free(m->delta); free(m->qkv); free(m->q); free(m->att);
     free(m->act); free(m->logits); free(m->tmp); free(m->xq); free(m->aq);
+    free(m->xn); free(m->yk);
     free(m);
 }
 
@@ -364,6 +369,67 @@ int32_t orc_model_step(orc_model *m, int32_t token, int32_t pos, float *logits_o
     else
         orc_q4k_gemv(m->embd, m->xq, m->logits, c->vocab, H, 1, nthreads);
     if (logits_out) memcpy(logits_out, m->logits, (size_t)c->vocab * 4);
+    return orc_argmax(m->logits, c->vocab);
+}
+
+/* ---- the same step on llama.cpp's CPU path (timed baseline) -------------
+ * The decode the reference runs when its model is on the host: every Q4_K
+ * matrix-vector product takes its activation as Q8_K blocks (ggml's CPU
+ * vec_dot_q4_K_q8_K, restated as orc_q4k_q8k_gemv) instead of Q8_1; norms,
+ * RoPE, fp16 KV and attention as in orc_model_step.  All-Q4_K models only.
+ * Its logits differ from the canonical step in the last bits; it times the
+ * CPU path and is not a parity target. */
+static void q8k_gemv(orc_model *m, const uint8_t *w, const float *x, float *y, int64_t N, int64_t K,
+                     int32_t nthreads) {
+    orc_quantize_q8_K(x, m->yk, K, 1);
+    orc_q4k_q8k_gemv(w, m->yk, y, N, K, 1, nthreads);
+}
+
+int32_t orc_model_step_cpu(orc_model *m, int32_t token, int32_t pos, int32_t nthreads) {
+    const orc_model_config *c = &m->cfg;
+    if (c->mix) return -1;
+    const int hd = c->head_dim, H = c->hidden;
+    const int64_t qd = (int64_t)c->n_heads * hd;
+    const int64_t qkv_rows = (int64_t)(c->n_heads + 2 * c->n_kv_heads) * hd;
+    const float scale = (float)(1.0 / sqrt((double)hd));
+    const int64_t kvstride = (int64_t)c->max_ctx * hd;
+    orc_dequant_q4k(m->embd + (int64_t)token * (H / 256) * Q4K_BYTES, m->h, H / 256);
+    int have_delta = 0;
+    for (int l = 0; l < c->n_layers; ++l) {
+        struct layer *y = &m->L[l];
+        if (have_delta)
+            for (int64_t i = 0; i < H; ++i) m->h[i] = m->h[i] + m->delta[i];
+        orc_rmsnorm_quantize_q8_1(m->h, y->attn_norm, c->eps, m->xq, m->xn, H, 1);
+        q8k_gemv(m, y->wqkv, m->xn, m->qkv, qkv_rows, H, nthreads);
+        uint16_t kt[8 * 256], vt[8 * 256];
+        orc_qk_norm_rope(m->qkv, y->q_norm, y->k_norm, c->eps, m->rope + (int64_t)pos * hd,
+                         c->n_heads, c->n_kv_heads, hd, m->q, kt, vt);
+        for (int g = 0; g < c->n_kv_heads; ++g) {
+            const int64_t base = ((int64_t)l * c->n_kv_heads + g) * kvstride + (int64_t)pos * hd;
+            memcpy(m->kcache + base, kt + g * hd, (size_t)hd * 2);
+            memcpy(m->vcache + base, vt + g * hd, (size_t)hd * 2);
+        }
+        const int gq = c->n_heads / c->n_kv_heads;
+#pragma omp parallel for num_threads(nthreads) schedule(static)
+        for (int h = 0; h < c->n_heads; ++h) {
+            const int g = h / gq;
+            const int64_t base = ((int64_t)l * c->n_kv_heads + g) * kvstride;
+            orc_attention_head(m->q + (int64_t)h * hd, m->kcache + base, m->vcache + base, pos + 1,
+                               hd, scale, m->att + (int64_t)h * hd);
+        }
+        q8k_gemv(m, y->wo, m->att, m->delta, H, qd, nthreads);
+        for (int64_t i = 0; i < H; ++i) m->h[i] = m->h[i] + m->delta[i];
+        orc_rmsnorm_quantize_q8_1(m->h, y->ffn_norm, c->eps, m->xq, m->xn, H, 1);
+        q8k_gemv(m, y->wgate, m->xn, m->tmp, c->ffn, H, nthreads);
+        orc_q4k_q8k_gemv(y->wup, m->yk, m->tmp + c->ffn, c->ffn, H, 1, nthreads);
+        orc_swiglu(m->tmp, m->tmp + c->ffn, m->act, c->ffn);
+        q8k_gemv(m, y->wdown, m->act, m->delta, H, c->ffn, nthreads);
+        have_delta = 1;
+    }
+    if (have_delta)
+        for (int64_t i = 0; i < H; ++i) m->h[i] = m->h[i] + m->delta[i];
+    orc_rmsnorm_quantize_q8_1(m->h, m->out_norm, c->eps, m->xq, m->xn, H, 1);
+    q8k_gemv(m, m->embd, m->xn, m->logits, c->vocab, H, nthreads);
     return orc_argmax(m->logits, c->vocab);
 }
 

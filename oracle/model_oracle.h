@@ -40,6 +40,10 @@ orc_model *orc_model_create(const orc_model_config *cfg);
 void orc_model_destroy(orc_model *m);
 int32_t orc_model_step(orc_model *m, int32_t token, int32_t pos, float *logits_out,
                        int32_t nthreads);
+/* One decode step on llama.cpp's CPU path (Q8_K activations for every Q4_K
+ * GEMV): the timed CPU baseline of bench.py, not a parity target.  All-Q4_K
+ * models only (returns -1 otherwise); returns the greedy pick. */
+int32_t orc_model_step_cpu(orc_model *m, int32_t token, int32_t pos, int32_t nthreads);
 void orc_model_generate(orc_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
                         int32_t *out, int32_t nthreads);
 const float *orc_model_hidden(const orc_model *m);
