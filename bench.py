@@ -3,10 +3,12 @@
 
 Default workload ("qwen3_4b_q4k_decode_tg"): greedy decode of the seeded
 Qwen3-4B-shaped model, all linear weights Q4_K, after a 16-token prompt; one
-step is one token (one CUDA graph of 291 kernels), ``value`` is tok/s at
-depth 0, ``e2e`` the same through the per-token host call, and ``roofline``
-the decode step's MMVQ launches (the weight sweep below) against measured
-HBM bandwidth.  Under torchrun the model is tensor parallel over the ranks.
+step is one token (one launch of the persistent decode kernel on one GPU),
+``value`` is tok/s at depth 0, ``e2e`` the same through the per-token host
+call, and ``roofline`` that kernel's algorithmic bytes per launch (the
+token's weights, KV rows and logits) over its measured duration against
+measured HBM bandwidth.  Under torchrun the model is tensor parallel over the
+ranks (kernel chain).
 
 GEMV workload (``--workload gemv``, "qwen3_4b_decode_weight_sweep"): one step is one pass of MMVQ over
 the full Qwen3-4B-shaped decode weight set, in the operators a decode step
@@ -29,8 +31,8 @@ and the CPU baseline on all host cores: llama.cpp's CPU Q4_K path restated in
 oracle/ (activations quantized to Q8_K, the Q4_K x Q8_K dot; llama.cpp itself
 is not in the image), beside the restatement of vec_dot_q4_K_q8_1.
 
-``--impl reference`` times that CPU path alone on a bounded sample of the
-same workload.
+``--impl reference`` times the CPU decode itself, token by token, on all
+host threads (the GEMV workload: the CPU GEMV on a bounded sample).
 
 Run: python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
 """
@@ -245,6 +247,51 @@ def cpu_sample_rate(batch: int, budget_s: float, seed: int = 0, path: str = "ggm
         if el >= budget_s:
             break
     return reps * nbytes / el / 1e9, threads, reps, el
+
+
+CPU_DECODE = ("the full 36-layer Qwen3-4B-shaped decode (seeded weights, the GPU model's), one "
+              "token per step after a {prompt}-token prompt, on llama.cpp's CPU path restated in "
+              "oracle/model_oracle.c (every Q4_K GEMV on Q8_K activations, ggml's "
+              "vec_dot_q4_K_q8_K; integer dots at SIMD level {simd}: 0 scalar, 1 AVX2, "
+              "2 AVX-512 VNNI), OpenMP on all host threads")
+
+
+class CpuDecoder:
+    """The CPU decode the reference runs when its model is on the host,
+    token by token (orc_model_step_cpu), on all host threads."""
+
+    def __init__(self, max_tokens: int, seed: int = 0):
+        import oracle as O
+
+        self.m = O.OrcModel(max_ctx=PROMPT + max_tokens + 1, seed=seed)
+        self.prompt = np.random.default_rng(seed).integers(0, self.m.cfg.vocab, PROMPT).astype(np.int32)
+        self.pos, self.tok = 0, int(self.prompt[0])
+        self.threads = self.m.threads
+
+    def step(self) -> float:
+        """One token; returns its wall time in ms."""
+        t0 = time.perf_counter()
+        pick = self.m.step_cpu(self.tok, self.pos)
+        el = (time.perf_counter() - t0) * 1e3
+        self.pos += 1
+        self.tok = int(self.prompt[self.pos]) if self.pos < PROMPT else pick
+        return el
+
+    def close(self):
+        self.m.close()
+
+
+def cpu_decode_rate(warmup: int, max_tokens: int, budget_s: float):
+    """Tokens per second of the CPU decode: ``warmup`` untimed tokens, then
+    tokens until ``max_tokens`` or ``budget_s`` seconds."""
+    d = CpuDecoder(warmup + max_tokens)
+    for _ in range(warmup):
+        d.step()
+    ms = []
+    while len(ms) < max_tokens and sum(ms) < budget_s * 1e3:
+        ms.append(d.step())
+    d.close()
+    return 1000.0 * len(ms) / sum(ms), d.threads, ms
 
 
 # --------------------------------------------------------------- GPU arm ---
@@ -665,6 +712,8 @@ PROMPT = 16
 # kernels per token: embed; per layer q|k|v (fused RMSNorm), QK-norm/RoPE/KV,
 # attention, merge+Q8_1, o, gate/up (fused RMSNorm), Q8_1, down; output, argmax
 LAUNCHES_PER_TOKEN = 1 + 36 * 8 + 2
+# fp16 K and V of every layer and kv head, per position of context
+KV_BYTES_PER_POS = 36 * 2 * 8 * 128 * 2
 
 
 def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, seed: int = 0,
@@ -699,14 +748,16 @@ def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, se
     e.synchronize()
     ms = s.elapsed_time(e) / steps
     info = m.info()
+    persistent = m.persistent
     toks = m.tokens(n_prompt + warmup + steps)[n_prompt:]
     if dist:
         dist.barrier()  # peers push into this rank's arena until they finish
     m.close()
     return {"depth": depth, "ms_per_token": round(ms, 4), "tok_s": round(1000.0 / ms, 2),
             "weight_bytes": info["weight_bytes"],
-            "kv_read_bytes_per_token": 36 * 2 * 8 * 128 * 2 * (n_prompt + warmup + steps // 2),
-            "tokens_head": toks[:8].tolist()}
+            "kv_read_bytes_per_token": KV_BYTES_PER_POS * (n_prompt + warmup + steps // 2),
+            "step": "persistent decode kernel" if persistent else "kernel chain",
+            "tokens_head": toks[:4].tolist()}
 
 
 def decode_samples(torch, warmup: int, steps: int, seed: int = 0):
@@ -732,8 +783,7 @@ def decode_samples(torch, warmup: int, steps: int, seed: int = 0):
     m.close()
     return {"unit": "ms/token", "n": steps, "median": round(float(np.median(ms)), 4),
             "min": round(float(ms.min()), 4), "max": round(float(ms.max()), 4),
-            "spread": round(float(ms.max() - ms.min()), 4), "stddev": round(float(ms.std()), 4),
-            "raw": [round(float(v), 4) for v in ms]}
+            "spread": round(float(ms.max() - ms.min()), 4), "stddev": round(float(ms.std()), 4)}
 
 
 def prompt_processing(torch, n: int = 512, reps: int = 3, seed: int = 0):
@@ -982,6 +1032,13 @@ def decode_batched(torch, warmup: int, steps: int, batch: int = 32, seed: int = 
             "path": "abra_model_create_batched: every GEMV on tcgen05 kind::i8 (abra_q4k_mmvq_tc)"}
 
 
+def decode_alg_bytes(res: dict, vocab: int = 151936) -> int:
+    """Algorithmic bytes of one decode step: every weight byte of the token,
+    the KV rows attention reads at the run's mean context, the new K/V rows
+    written, the fp32 logits written."""
+    return int(res["weight_bytes"] + res["kv_read_bytes_per_token"] + KV_BYTES_PER_POS + 4 * vocab)
+
+
 def decode_main(a, dist):
     import torch
 
@@ -996,6 +1053,7 @@ def decode_main(a, dist):
     clocks = clk.summary()
     ms = dist.max(res["ms_per_token"])
     tok_s = 1000.0 / ms  # one sequence, tensor parallel over all ranks
+    persistent = res["step"].startswith("persistent")
     e2e = decode_depth(torch, 0, a.warmup, a.steps, streaming=True, dist=dist)
     e2e_ms = dist.max(e2e["ms_per_token"])
     extras = {"decode": {"depth0": res}}
@@ -1003,19 +1061,46 @@ def decode_main(a, dist):
         r = decode_depth(torch, d, a.warmup, a.steps, streaming=False, dist=dist)
         r["ms_per_token"] = dist.max(r["ms_per_token"])
         r["tok_s"] = round(1000.0 / r["ms_per_token"], 2)
+        r["roofline_frac"] = round(decode_alg_bytes(r) / (r["ms_per_token"] * 1e-3) / 1e9 / peak, 4)
         extras["decode"][f"depth{d}"] = r
-    # the dominant kernel (MMVQ): its launches in the decode step, as one graph
+    # the dominant kernel: the persistent decode kernel is the whole step (one
+    # launch per token), timed above with CUDA events on the model's stream
+    alg = decode_alg_bytes(res)
+    achieved = alg / (res["ms_per_token"] * 1e-3) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "traffic_decode_token_kernel_qwen3_4b_depth0.json"
+    if persistent and tp.exists():
+        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+    # the MMVQ family alone: the decode step's weight sweep as one graph of
+    # 145 launches (batch 1), the same at batch 8
     sw = Sweep(torch.device("cuda", dist.local), 1)
     g = sw.capture()
     for _ in range(3):
         g.replay()
     ms_sw = sw.timed(max(3, a.steps // 16), g.replay)
-    achieved = sw.bytes / (ms_sw * 1e-3) / 1e9
     del g
-    extras["gemv_sweep"] = {"workload": WORKLOAD, "GBps": round(achieved, 1),
+    extras["gemv_sweep"] = {"workload": WORKLOAD, "batch": 1,
+                            "GBps": round(sw.bytes / (ms_sw * 1e-3) / 1e9, 1),
+                            "frac": round(sw.bytes / (ms_sw * 1e-3) / 1e9 / peak, 4),
                             "ms_per_step": round(ms_sw, 4), "launches_per_step": sw.launches}
     cpu = None
     if dist.world == 1:
+        # the same token through the per-operation kernel chain
+        from abra_b200.model import KERNEL_CHAIN, Q4_K_M
+        r = decode_depth(torch, 0, a.warmup, a.steps, streaming=False, flags=KERNEL_CHAIN)
+        extras["decode_kernel_chain"] = {"tok_s": r["tok_s"], "ms_per_token": r["ms_per_token"],
+                                         "launches_per_token": LAUNCHES_PER_TOKEN,
+                                         "same_tokens": r["tokens_head"] == res["tokens_head"]}
+        sw8 = Sweep(torch.device("cuda", dist.local), 8)
+        g8 = sw8.capture()
+        for _ in range(3):
+            g8.replay()
+        ms8 = sw8.timed(max(3, a.steps // 16), g8.replay)
+        del g8
+        extras["gemv_sweep_b8"] = {"GBps": round(sw8.bytes / (ms8 * 1e-3) / 1e9, 1),
+                                   "frac": round(sw8.bytes / (ms8 * 1e-3) / 1e9 / peak, 4),
+                                   "ms_per_step": round(ms8, 4)}
+        del sw8
         # batch 32 on the tensor cores: the decode weight set as one graph, and
         # the batched decode step
         sw32 = Sweep(torch.device("cuda", dist.local), 32)
@@ -1026,19 +1111,17 @@ def decode_main(a, dist):
         ms32 = sw32.timed(max(3, a.steps // 16), g32.replay)
         del g32
         extras["gemv_sweep_b32_tc"] = {
-            "workload": WORKLOAD, "batch": 32, "GBps": round(sw32.bytes / (ms32 * 1e-3) / 1e9, 1),
+            "GBps": round(sw32.bytes / (ms32 * 1e-3) / 1e9, 1),
             "weight_GBps": round(sw32.weight_bytes / (ms32 * 1e-3) / 1e9, 1),
-            "ms_per_step": round(ms32, 4), "launches_per_step": sw32.launches + LAYERS,
-            "kernel": "mmvq_tc_kernel (tcgen05.mma kind::i8, TMEM, 2-D TMA)"}
+            "ms_per_step": round(ms32, 4), "kernel": "mmvq_tc_kernel (tcgen05.mma kind::i8)"}
         del sw32, ws
         torch.cuda.empty_cache()
         extras["decode_b32"] = decode_batched(torch, a.warmup, a.steps)
         # the real Qwen3-4B-Q4_K_M type map: Q6_K attn_v/ffn_down in 18 layers
-        # and a Q6_K tied table
-        from abra_b200.model import Q4_K_M
+        # and a Q6_K tied table (kernel chain)
         r = decode_depth(torch, 0, a.warmup, a.steps, streaming=False, flags=Q4_K_M)
-        r["type_map"] = "Q4_K_M (Q6_K attn_v, ffn_down in 18 of 36 layers; Q6_K tied output)"
-        extras["decode_q4_k_m"] = r
+        extras["decode_q4_k_m"] = {"tok_s": r["tok_s"], "ms_per_token": r["ms_per_token"],
+                                   "weight_bytes": r["weight_bytes"]}
         for name, fn in (("prompt_pp512", lambda: prompt_processing(torch, 512)),
                          ("lookup_verify", lambda: lookup_verification(torch)),
                          ("decode_samples", lambda: decode_samples(torch, a.warmup, a.steps))):
@@ -1057,23 +1140,15 @@ def decode_main(a, dist):
                 extras["fused_rmsnorm_block"] = fused_rmsnorm_block(torch, a.steps)
             except Exception as exc:
                 extras["fused_rmsnorm_block"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
-        gbs, threads, reps, el = cpu_sample_rate(1, a.cpu_budget)
-        # the CPU path's decode rate: weight bytes per token at its GEMV rate
-        cpu_tok_s = gbs * 1e9 / res["weight_bytes"]
-        cpu = {"value": round(cpu_tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"{CPU_SAMPLE}, {reps} passes in {el:.1f}s "
-                         f"({gbs:.2f} GB/s), scaled to the 2.26 GB of Q4_K weights a token "
-                         f"reads; {CPU_PATHS['ggml']}, integer dots at SIMD level "
-                         f"{simd_level()} (0 scalar, 1 AVX2, 2 AVX-512 VNNI)"}
-        g2, t2, r2, e2 = cpu_sample_rate(1, max(1.0, a.cpu_budget / 4), path="q8_1")
-        extras["cpu_baseline_q8_1"] = {"value": round(g2 * 1e9 / res["weight_bytes"], 3),
-                                       "unit": "tok/s", "cores": t2, "GBps": round(g2, 2),
-                                       "sample": f"the same sample, {r2} passes in {e2:.1f}s; "
-                                                 f"{CPU_PATHS['q8_1']}"}
-    traffic = None
-    tp = ROOT / "profiles" / f"traffic_{WORKLOAD}_b1.json"
-    if tp.exists():
-        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+        rate, threads, cms = cpu_decode_rate(2, 64, a.cpu_budget)
+        cpu = {"value": round(rate, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{len(cms)} tokens timed after 2 warm-up tokens: "
+                         + CPU_DECODE.format(prompt=PROMPT, simd=simd_level())}
+        gbs, t2, reps, el = cpu_sample_rate(1, max(1.0, a.cpu_budget / 4))
+        extras["cpu_gemv_rate"] = {"GBps": round(gbs, 2), "cores": t2,
+                                   "tok_s_if_weight_bound": round(gbs * 1e9 / res["weight_bytes"], 3),
+                                   "sample": f"{CPU_SAMPLE}, {reps} passes in {el:.1f}s"}
+    del sw
     if dist.rank == 0:
         line = {
             "metric": "Qwen3-4B-shape decode tok/s", "value": round(tok_s, 2), "unit": "tok/s",
@@ -1086,14 +1161,13 @@ def decode_main(a, dist):
                        "depth": 0, "prompt": PROMPT, "gen": a.steps,
                        "parallelism": f"tp{dist.world}" if dist.world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (2.26 GB of weights per token)",
-                       "launch": "one CUDA graph per token, programmatic dependent launch"
-                                 + (", partial sums pushed to peers over NVLink from the MMVQ "
-                                    "epilogue" if dist.world > 1 else "")},
-            "gpu_launches": a.steps * LAUNCHES_PER_TOKEN * dist.world,
+                       "step": res["step"]},
+            "gpu_launches": a.steps * (1 if persistent else LAUNCHES_PER_TOKEN * dist.world),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": traffic, "kernel": "mmvq_q4k_kernel",
-                         "measured_on": f"the decode step's {sw.launches} MMVQ launches as one graph"},
+                         "traffic": traffic,
+                         "kernel": "decode_token_kernel" if persistent else "decode step (kernel chain)",
+                         "alg_bytes_per_launch": alg},
             "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                     "ms_per_step": round(e2e_ms, 4), "path": "abra_model_decode_streaming"},
@@ -1102,13 +1176,39 @@ def decode_main(a, dist):
         if cpu:
             line["cpu_baseline"] = cpu
         line.update(extras)
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     dist.close()
     return 0
 
 
 def reference_arm(a, dist):
     if dist.rank != 0:
+        return 0
+    if a.workload == "decode":
+        # one step = one token of the full CPU decode, timed on all host threads
+        d = CpuDecoder(a.warmup + a.steps)
+        for _ in range(a.warmup):
+            d.step()
+        ms = [d.step() for _ in range(a.steps)]
+        d.close()
+        val = 1000.0 * len(ms) / sum(ms)
+        sample = f"{a.steps} tokens after {a.warmup} warm-up tokens: " + CPU_DECODE.format(
+            prompt=PROMPT, simd=simd_level())
+        line = {
+            "impl": "reference", "metric": "Qwen3-4B-shape decode tok/s", "value": round(val, 3),
+            "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(sum(ms) / len(ms), 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u4 x s8 dot, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": DECODE_WORKLOAD, "model": "qwen3-4b-shape-q4k", "global_batch": 1,
+                       "batch_per_gpu": 1, "seq_len": PROMPT + a.warmup + a.steps, "depth": 0,
+                       "prompt": PROMPT, "gen": a.steps,
+                       "parallelism": f"CPU, {d.threads} host threads"},
+            "cpu_baseline": {"value": round(val, 3), "unit": "tok/s", "cores": d.threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(val, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
         return 0
     for _ in range(a.warmup):
         cpu_sample_rate(a.batch, budget_s=0.5)
