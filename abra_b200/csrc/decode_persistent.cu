@@ -35,11 +35,13 @@
 // from this CTA's shared memory, never through the non-coherent path.
 //
 // GEMV units: a unit is R consecutive rows (R = 8, 4, 2 or 1 per phase, so
-// that a unit fits one ring slot); lane (r, p) = r + R p of the consuming
-// warp owns superblocks p, p + 32/R, ... of row r and computes each whole
-// superblock value in registers (the eight exact int32 sub-block dots by
-// dp4a and the canonical fp32 tree); the lane of p == 0 then sums its row
-// over the eight canonical K-slices.
+// that a unit fits one ring slot), staged by ONE bulk copy per matrix (the
+// rows are contiguous in HBM; many small copies cap an SM's copy rate); the
+// lane owning (row r, superblock p) of the consuming warp computes
+// superblocks p, p + 32/R, ... of row r, each whole superblock value in
+// registers (the eight exact int32 sub-block dots by dp4a and the canonical
+// fp32 tree); lanes 0 .. R-1 then sum one row each over the eight canonical
+// K-slices.
 //
 // Ring protocol: ticket t of a CTA (its t-th unit over the token) goes to
 // slot t % NSLOT (16 slots, or 8 when the activations of a wide or many-head
@@ -230,7 +232,6 @@ __device__ __forceinline__ void pk_producer(const PkParams &P, uint8_t *ring, ui
         const uint32_t row_bytes = static_cast<uint32_t>(mm.nsb) * Q4K_BYTES;
         int u_begin, nu;
         pk_range(mm, u_begin, nu);
-        const int m = lane >> mm.lr, r = lane & (R - 1);  // lane -> (matrix, row of the unit)
         for (int u = 0; u < nu; ++u, ++t) {
             const int s = static_cast<int>(t & smask);
             const uint32_t k = t >> sh;
@@ -238,14 +239,14 @@ __device__ __forceinline__ void pk_producer(const PkParams &P, uint8_t *ring, ui
                 ok = false;
                 break;
             }
+            // the unit's rows are contiguous in HBM: one copy per matrix
             const int row0 = (u_begin + u) * R, nvalid = min(R, mm.N - row0);
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], nmat * nvalid * row_bytes);
+            const uint32_t bytes = static_cast<uint32_t>(nvalid) * row_bytes;
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], nmat * bytes);
             __syncwarp();
-            if (m < nmat && r < nvalid) {
-                uint8_t *dst = ring + s * PK_SLOT_BYTES + (m * R + r) * mm.pitch;
-                const uint8_t *src = (m ? mm.w1 : mm.w0) + static_cast<int64_t>(row0 + r) * row_bytes;
-                bulk_g2s(dst, src, row_bytes, &full[s], pol);
-            }
+            if (lane < nmat)
+                bulk_g2s(ring + s * PK_SLOT_BYTES + lane * R * row_bytes,
+                         (lane ? mm.w1 : mm.w0) + static_cast<int64_t>(row0) * row_bytes, bytes, &full[s], pol);
         }
         if (lane == 0) PK_STAMP(2, ph);
     }
@@ -357,7 +358,21 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
                                          float *Y, unsigned long long *s_amax, int sh, bool &poisoned) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int lr = mm.lr, R = 1 << lr, P = 32 >> lr;
-    const int r = lane & (R - 1), p = lane >> lr;
+    // lane -> (row r, first superblock p); rows are staged back to back
+    // (pitch nsb * 144 B = 9 nsb chunks of 16 B), so the chunk of (r, b) is
+    // 9 nsb r + 9 b + c == (nsb r + b) mod 8 bank groups.  P >= 8: a
+    // quarter warp is one row and eight consecutive superblocks (distinct);
+    // P == 4 (eight rows): a quarter warp is four rows x two superblocks,
+    // distinct for nsb == 2 mod 8 (the 2560-wide matrices)
+    int r, p;
+    if (P >= 8) {
+        r = lane / P;
+        p = lane % P;
+    } else {
+        const int q4 = lane >> 3, w8 = lane & 7;
+        r = (w8 >> 1) + 4 * (q4 & 1);
+        p = (w8 & 1) + 2 * (q4 >> 1);
+    }
     const int nsb = mm.nsb, N = mm.N;
     const uint32_t smask = (1u << sh) - 1u;
     for (int u = warp; u < nu; u += PK_NCW) {
@@ -378,11 +393,11 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);  // the slot's weights are consumed
-        const int row = ((u_begin + u) << lr) + r;
+        const int row = ((u_begin + u) << lr) + lane;  // lanes 0 .. R-1 sum one row each
         float yv = 0.0f;
         if (lane < R) {
-            yv = pk_row_sum(vbuf + r * nsb, nsb);
-            if constexpr (NMAT == 2) yv = __fmul_rn(pk_row_sum(vbuf + (R + r) * nsb, nsb), abra_silu(yv));
+            yv = pk_row_sum(vbuf + lane * nsb, nsb);
+            if constexpr (NMAT == 2) yv = __fmul_rn(pk_row_sum(vbuf + (R + lane) * nsb, nsb), abra_silu(yv));
             if (row < N) Y[row] = yv;
         }
         if (s_amax) {
@@ -456,35 +471,50 @@ __device__ __forceinline__ void pk_quant4(uint8_t *arec, int i, int sub, float x
     pk_put_block(arec, i, sub, packed, __half2float(__float2half_rn(d)), sum);
 }
 
-// x = h_in + delta (or the embedding row erow), written to h_out by CTA 0;
-// then RMSNorm * w and Q8_1 into the activation records: the XIN prologue of
-// mmvq_q4k_kernel, operation for operation.
-__device__ __forceinline__ void pk_xin(int K, const float *h_in, const float *delta, const uint8_t *erow,
-                                       float *h_out, float *s_x, const float *s_w, float eps, uint8_t *arec,
-                                       float *s_nred) {
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    float acc = 0.0f;
-    for (int i0 = t; i0 < K; i0 += 256 * 8) {
-        float v[8];
+// Before the phase's barrier: the residual stream h_in (stable since an
+// earlier phase), or the token's embedding row, into s_x.
+__device__ __forceinline__ void pk_xin_stage(int K, const float *h_in, const uint8_t *erow, float *s_x) {
+    constexpr int U = 8;
+    for (int i0 = threadIdx.x; i0 < K; i0 += 256 * U) {
+        float v[U];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < U; ++k) {
             const int i = i0 + k * 256;
             v[k] = i < K ? (erow ? pk_embed(erow, i) : __ldcg(h_in + i)) : 0.0f;
         }
-        if (delta) {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int i = i0 + k * 256;
-                if (i < K) v[k] = __fadd_rn(v[k], __ldcg(delta + i));
-            }
+        for (int k = 0; k < U; ++k) {
+            const int i = i0 + k * 256;
+            if (i < K) s_x[i] = v[k];
+        }
+    }
+}
+
+// After it: x = s_x + delta (all of this thread's delta loads issued
+// first), written to h_out by CTA 0; then RMSNorm * w and Q8_1 into the
+// activation records -- the XIN prologue of mmvq_q4k_kernel, operation for
+// operation (thread t sums x[t + 256 k]^2 with fmaf in k order).
+__device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, float *s_x, const float *s_w,
+                                       float eps, uint8_t *arec, float *s_nred) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    constexpr int U = 10;
+    float acc = 0.0f;
+    for (int i0 = t; i0 < K; i0 += 256 * U) {
+        float d[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = i0 + k * 256;
+            d[k] = (delta && i < K) ? __ldcg(delta + i) : 0.0f;
         }
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < U; ++k) {
             const int i = i0 + k * 256;
             if (i < K) {
-                if (blockIdx.x == 0) h_out[i] = v[k];
-                s_x[i] = v[k];
-                acc = __fmaf_rn(v[k], v[k], acc);
+                float v = s_x[i];
+                if (delta) v = __fadd_rn(v, d[k]);
+                if (blockIdx.x == 0) h_out[i] = v;
+                s_x[i] = v;
+                acc = __fmaf_rn(v, v, acc);
             }
         }
     }
@@ -510,32 +540,55 @@ __device__ __forceinline__ void pk_xin(int K, const float *h_in, const float *de
 
 // Q8_1 of an fp32 activation written earlier in this launch (the SwiGLU
 // output), straight into the records: the bytes quantize_q8_1_kernel writes
-// and mmvq_q4k_kernel stages.
+// and mmvq_q4k_kernel stages.  Each lane's loads are all issued first.
 __device__ __forceinline__ void pk_quant_f32(const float *x, int K, uint8_t *arec) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane & 7;
     const int nblk = K / QK8_1;
-    for (int b0 = warp * 4; b0 < nblk; b0 += PK_NCW * 4) {  // warp-uniform: nblk % 8 == 0
-        const int i = b0 + (lane >> 3);
-        const float4 xv = __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + sub * 4));
-        pk_quant4(arec, i, sub, xv.x, xv.y, xv.z, xv.w);
+    constexpr int U = 5;
+    for (int base = warp * 4; base < nblk; base += PK_NCW * 4 * U) {
+        float4 v[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = base + k * PK_NCW * 4 + (lane >> 3);
+            if (base + k * PK_NCW * 4 < nblk) v[k] = __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + sub * 4));
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int b0 = base + k * PK_NCW * 4;  // warp-uniform: nblk % 8 == 0
+            if (b0 < nblk) pk_quant4(arec, b0 + (lane >> 3), sub, v[k].x, v[k].y, v[k].z, v[k].w);
+        }
     }
     cta_sync();
 }
 
 // Q8_1 blocks written earlier in this launch (oq) into the records (the
 // staging loop of mmvq_q4k_kernel, loads through L2): eight lanes per block,
-// one 32-bit word of quants each.
+// one 32-bit word of quants each; every load issued first.
 __device__ __forceinline__ void pk_stage_q8(const uint8_t *X, int K, uint8_t *arec) {
     const int nblk = K / QK8_1;
     const int lane = threadIdx.x & 31, sub = lane & 7;
-    for (int i = (threadIdx.x >> 3); i < nblk; i += PK_NCW * 4) {  // warp-uniform: nblk % 8 == 0
-        const uint32_t *src = reinterpret_cast<const uint32_t *>(X + static_cast<int64_t>(i) * Q81_BYTES);
-        const uint32_t qw = __ldcg(src + 1 + sub);
-        const uint32_t h = __ldcg(src);
-        int msum = dp4a_ss(0x01010101, static_cast<int>(qw), 0);
+    constexpr int U = 4;
+    for (int base = threadIdx.x >> 3; base < nblk; base += PK_NCW * 4 * U) {
+        uint32_t qw[U], h[U];
 #pragma unroll
-        for (int m = 4; m >= 1; m >>= 1) msum += __shfl_xor_sync(0xffffffffu, msum, m);
-        pk_put_block(arec, i, sub, qw, half_lo(h), msum);
+        for (int k = 0; k < U; ++k) {
+            const int i = base + k * PK_NCW * 4;
+            if (i < nblk) {
+                const uint32_t *src = reinterpret_cast<const uint32_t *>(X + static_cast<int64_t>(i) * Q81_BYTES);
+                qw[k] = __ldcg(src + 1 + sub);
+                h[k] = __ldcg(src);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = base + k * PK_NCW * 4;  // warp-uniform: nblk % 8 == 0
+            if (i < nblk) {
+                int msum = dp4a_ss(0x01010101, static_cast<int>(qw[k]), 0);
+#pragma unroll
+                for (int m = 4; m >= 1; m >>= 1) msum += __shfl_xor_sync(0xffffffffu, msum, m);
+                pk_put_block(arec, i, sub, qw[k], half_lo(h[k]), msum);
+            }
+        }
     }
     cta_sync();
 }
@@ -895,11 +948,15 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         const int l = e / 5;
         const int ph = e == nev - 1 ? PH_OUT : e % 5;
         const bool xin = ph == PH_QKV || ph == PH_GU || ph == PH_OUT;
-        // inputs that do not depend on the previous phase, staged before its barrier
-        if (xin)
+        const bool first = xin && (ph == PH_QKV ? l == 0 : L == 0);  // the embedding row, no residual delta
+        // inputs that do not depend on the previous phase, staged before its
+        // barrier: norm weights, the residual stream (written two or more
+        // phases back) or the embedding row, the attention's norms and RoPE row
+        if (xin) {
             pk_stage_norm(ph == PH_OUT ? P.out_norm : ph == PH_QKV ? P.layers[l].attn_norm : P.layers[l].ffn_norm,
                           s_w, hidden);
-        else if (ph == PH_ATT)
+            pk_xin_stage(hidden, P.h[cur], first ? erow : nullptr, s_x);
+        } else if (ph == PH_ATT)
             pk_stage_att(P, l, pos, GQ, scr);
         if (ph == PH_OUT && t == 0) s_amax = 0ull;
         if (e > 0) {
@@ -910,9 +967,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         cta_sync();
         // the phase's activation
         if (xin) {
-            const bool first = ph == PH_QKV ? l == 0 : L == 0;  // the embedding row, no residual delta
-            pk_xin(hidden, P.h[cur], first ? nullptr : P.delta, first ? erow : nullptr, P.h[cur ^ 1], s_x, s_w,
-                   P.eps, arec, s_nred);
+            pk_xin(hidden, first ? nullptr : P.delta, P.h[cur ^ 1], s_x, s_w, P.eps, arec, s_nred);
             cur ^= 1;
         } else if (ph == PH_O) {
             pk_stage_q8(P.oq, P.n_heads * 128, arec);
@@ -980,24 +1035,6 @@ struct PkPlan {
 
 int pk_align(int v, int a) { return (v + a - 1) / a * a; }
 
-// Row pitch (bytes) of a staged unit of R rows of nsb superblocks: the
-// smallest count of 16-byte chunks >= the row that keeps the lanes of each
-// quarter warp (lane = r + R p: R rows x 8 / R superblock positions) in
-// distinct bank groups: odd for 8 rows, 2 mod 4 for 4, 4 mod 8 for 2.
-int pk_pitch(int nsb, int R) {
-    int pc = nsb * Q4K_BYTES / 16;
-    auto good = [&](int c) {
-        switch (R) {
-            case 8: return (c & 1) == 1;
-            case 4: return (c & 3) == 2;
-            case 2: return (c & 7) == 4;
-            default: return true;
-        }
-    };
-    while (!good(pc)) ++pc;
-    return pc * 16;
-}
-
 int log2i(int v) {
     int l = 0;
     while ((1 << l) < v) ++l;
@@ -1026,7 +1063,7 @@ bool pk_plan(int hidden, int n_heads, int n_kv, int ffn, int head_dim, int vocab
         pl.rows[k] = 0;
         int64_t best = -1;
         for (int R : {8, 4, 2, 1}) {
-            const int pitch = pk_pitch(nsb[k], R);
+            const int pitch = nsb[k] * Q4K_BYTES;  // rows back to back, as in HBM
             if (nmat[k] * R * pitch > PK_SLOT_BYTES || nmat[k] * R * nsb[k] > PK_VMAX) continue;
             const int64_t units = (N[k] + R - 1) / R;
             const int64_t per_cta = (units + sms - 1) / sms;
@@ -1179,18 +1216,18 @@ bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn
                 return fail("unit exceeds the staging buffer");
             for (int u = u0; u < u1; ++u, ++t) {
                 const int row0 = u * R, nvalid = std::min(R, N - row0);
-                if (nvalid <= 0 || row_bytes > pitch || (pitch & 15) || nmat[kind] * nvalid * row_bytes > (1 << 20) - 1)
+                if (nvalid <= 0 || row_bytes != pitch || (pitch & 15) || nmat[kind] * nvalid * row_bytes > (1 << 20) - 1)
                     return fail("unit does not fit its row pitch");
-                for (int m = 0; m < nmat[kind]; ++m)
-                    for (int r = 0; r < nvalid; ++r) {
-                        const int64_t dst = (t % nslot) * PK_SLOT_BYTES + (m * R + r) * pitch;
-                        const int64_t src = static_cast<int64_t>(row0 + r) * row_bytes;
-                        const int64_t tensor = static_cast<int64_t>(N) * row_bytes;
-                        if (dst + row_bytes > nslot * PK_SLOT_BYTES || (dst & 15) || src + row_bytes > tensor ||
-                            (src & 15) || (m * R + r + 1) * pitch > PK_SLOT_BYTES)
-                            return fail("copy leaves its slot or its tensor");
-                        ++copies;
-                    }
+                for (int m = 0; m < nmat[kind]; ++m) {  // one copy per (unit, matrix)
+                    const int64_t bytes = nvalid * row_bytes;
+                    const int64_t dst = (t % nslot) * PK_SLOT_BYTES + m * R * row_bytes;
+                    const int64_t src = static_cast<int64_t>(row0) * row_bytes;
+                    const int64_t tensor = static_cast<int64_t>(N) * row_bytes;
+                    if (dst + bytes > nslot * PK_SLOT_BYTES || (dst & 15) || (bytes & 15) || src + bytes > tensor ||
+                        (src & 15) || (m + 1) * R * row_bytes > PK_SLOT_BYTES)
+                        return fail("copy leaves its slot or its tensor");
+                    ++copies;
+                }
             }
         }
         max_tickets = std::max(max_tickets, t);
