@@ -118,12 +118,24 @@ struct PkParams {
 // ends and end of inputs (consumers) and of the producer's last copy of each
 // phase.
 constexpr int PK_TRACE_EV = 512;
-__device__ unsigned long long g_pk_trace[160][4][PK_TRACE_EV];
+__device__ unsigned long long g_pk_trace[160][5][PK_TRACE_EV];
+__shared__ unsigned long long g_pk_wait_ns;  // this CTA's warps' waits on ring slots, per phase
+__device__ unsigned long long g_pk_units[5][64][4];  // CTA 0 warp 0: stamps inside the units of 5 GEMVs
+__shared__ int g_pk_gemv;                           // which GEMV of the token is running (CTA 0)
+#define PK_USTAMP(u, k)                                                                      \
+    do {                                                                                     \
+        if (blockIdx.x == 0 && (threadIdx.x >> 5) == 0 && lane == 0 && (u) < 64 * PK_NCW &&   \
+            g_pk_gemv < 5)                                                                   \
+            g_pk_units[g_pk_gemv][(u) / PK_NCW][k] = globaltimer_ns();                       \
+    } while (0)
 #define PK_STAMP(kind, idx)                                                                            \
     do {                                                                                               \
         if ((idx) < PK_TRACE_EV && blockIdx.x < 160) g_pk_trace[blockIdx.x][kind][idx] = globaltimer_ns(); \
     } while (0)
 #else
+#define PK_USTAMP(u, k) \
+    do {                \
+    } while (0)
 #define PK_STAMP(kind, idx) \
     do {                    \
     } while (0)
@@ -334,24 +346,30 @@ __device__ __forceinline__ void pk_sb_value(const uint8_t *const (&wsb)[NMAT], c
     }
 }
 
-// A row's value from its staged superblock values: sequential within each of
-// the eight canonical K-slices, then the fixed tree over the slices.
-__device__ __forceinline__ float pk_row_sum(const float *vrow, int nsb) {
-    float sl[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int b0 = slice_start(nsb, i), b1 = slice_start(nsb, i + 1);
-        float acc = 0.0f;
-        for (int b = b0; b < b1; ++b) acc = b == b0 ? vrow[b] : __fadd_rn(acc, vrow[b]);
-        sl[i] = acc;
-    }
-    return tree_sum<8>(sl);
+// Sum of canonical K-slice i of a row from its staged superblock values
+// (sequential within the slice).
+__device__ __forceinline__ float pk_slice_sum(const float *vrow, int nsb, int i) {
+    const int b0 = slice_start(nsb, i), b1 = slice_start(nsb, i + 1);
+    float acc = 0.0f;
+    for (int b = b0; b < b1; ++b) acc = b == b0 ? vrow[b] : __fadd_rn(acc, vrow[b]);
+    return acc;
+}
+
+// The fixed tree over eight slice sums held by lanes 8g .. 8g+7 (slice i in
+// lane 8g + i): xor 1, 2, 4 give ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)) in every
+// lane of the group (IEEE addition commutes, so both partners form the same
+// bits).
+__device__ __forceinline__ float pk_slice_tree(float v) {
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    return __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
 }
 
 // The units of one GEMV phase that belong to this warp (unit u of the CTA's
 // range -> warp u % 8, ring slot (T + u) % NSLOT).  The superblock values
-// meet in this warp's staging buffer and the lane of p == 0 sums its row in
-// the canonical order, then stores y (and merges the argmax key).
+// meet in this warp's staging buffer; eight lanes per row form the canonical
+// K-slice sums and their fixed tree; the row's first lane stores y (and
+// merges the argmax key).
 template <int NMAT>
 __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, uint32_t T, const uint8_t *ring,
                                          uint64_t *full, uint64_t *empty, float *vbuf, const uint8_t *arec,
@@ -378,7 +396,14 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
     for (int u = warp; u < nu; u += PK_NCW) {
         const uint32_t t = T + static_cast<uint32_t>(u);
         const int s = static_cast<int>(t & smask);
+#ifdef ABRA_PK_TRACE
+        const uint64_t tw0 = globaltimer_ns();
+#endif
         if (!poisoned && !mbar_wait(&full[s], (t >> sh) & 1)) poisoned = true;
+#ifdef ABRA_PK_TRACE
+        if (lane == 0) atomicAdd(&g_pk_wait_ns, static_cast<unsigned long long>(globaltimer_ns() - tw0));
+#endif
+        PK_USTAMP(u, 0);
         const uint8_t *wrow[NMAT];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) wrow[m] = ring + s * PK_SLOT_BYTES + (m * R + r) * mm.pitch;
@@ -392,16 +417,34 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
             for (int m = 0; m < NMAT; ++m) vbuf[(m * R + r) * nsb + b] = v[m];
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // the slot's weights are consumed
-        const int row = ((u_begin + u) << lr) + lane;  // lanes 0 .. R-1 sum one row each
-        float yv = 0.0f;
-        if (lane < R) {
-            yv = pk_row_sum(vbuf + lane * nsb, nsb);
-            if constexpr (NMAT == 2) yv = __fmul_rn(pk_row_sum(vbuf + (R + lane) * nsb, nsb), abra_silu(yv));
-            if (row < N) Y[row] = yv;
+        PK_USTAMP(u, 1);
+        // the slot's weights are consumed: lane 31 stores nothing to global
+        // memory, so its release does not wait for this warp's output stores
+        if (lane == 31) mbar_arrive(&empty[s]);
+        // row sums: lane 8g + i forms slice i of rows g, g + 4 of the unit,
+        // the slice tree runs across the group's eight lanes, lane 8g stores
+        const int i = lane & 7, g = lane >> 3;
+        unsigned long long key = 0ull;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int rr = g + 4 * half;
+            if (half == 1 && R <= 4) break;  // warp-uniform
+            const int row = ((u_begin + u) << lr) + rr;
+            const bool live = rr < R;
+            float yv = pk_slice_tree(live ? pk_slice_sum(vbuf + rr * nsb, nsb, i) : 0.0f);
+            if constexpr (NMAT == 2) {
+                const float up = pk_slice_tree(live ? pk_slice_sum(vbuf + (R + rr) * nsb, nsb, i) : 0.0f);
+                yv = __fmul_rn(up, abra_silu(yv));
+            }
+            if (i == 0 && live && row < N) {
+                Y[row] = yv;
+                const unsigned long long k = argmax_key(yv, row);
+                key = k > key ? k : key;
+            }
         }
+        __syncwarp();
+        PK_USTAMP(u, 2);
         if (s_amax) {
-            unsigned long long key = (lane < R && row < N) ? argmax_key(yv, row) : 0ull;
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) {
                 const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
@@ -410,6 +453,7 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
             if (lane == 0) atomicMax(s_amax, key);
         }
         __syncwarp();  // the staging buffer is reused by the next unit
+        PK_USTAMP(u, 3);
     }
 }
 
@@ -491,7 +535,7 @@ __device__ __forceinline__ void pk_xin_stage(int K, const float *h_in, const uin
 }
 
 // After it: x = s_x + delta (all of this thread's delta loads issued
-// first), written to h_out by CTA 0; then RMSNorm * w and Q8_1 into the
+// first), written to h_out (element i by CTA i % grid); then RMSNorm * w and Q8_1 into the
 // activation records -- the XIN prologue of mmvq_q4k_kernel, operation for
 // operation (thread t sums x[t + 256 k]^2 with fmaf in k order).
 __device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, float *s_x, const float *s_w,
@@ -512,7 +556,7 @@ __device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, 
             if (i < K) {
                 float v = s_x[i];
                 if (delta) v = __fadd_rn(v, d[k]);
-                if (blockIdx.x == 0) h_out[i] = v;
+                if (i % gridDim.x == blockIdx.x) h_out[i] = v;  // every CTA holds the same x
                 s_x[i] = v;
                 acc = __fmaf_rn(v, v, acc);
             }
@@ -975,6 +1019,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             pk_quant_f32(P.act, P.ffn, arec);
         }
         if (t == 0) PK_STAMP(3, e);
+#ifdef ABRA_PK_TRACE
+        if (t == 0) g_pk_wait_ns = 0;
+        cta_sync();
+#endif
         // the phase's work
         if (ph == PH_ATT) {
             pk_attention<GQ>(P, l, pos, scr, &s_flag);
@@ -984,6 +1032,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             const PkMm mm = pk_mm(P, l, kind);
             int u_begin, nu;
             pk_range(mm, u_begin, nu);
+#ifdef ABRA_PK_TRACE
+            if (t == 0) g_pk_gemv = (l == 1 || ph == PH_OUT) ? kind : 99;
+            cta_sync();
+#endif
             unsigned long long *amax = ph == PH_OUT ? &s_amax : nullptr;
             if (mm.w1)
                 pk_units<2>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
@@ -993,6 +1045,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         }
         cta_sync();
         if (t == 0) PK_STAMP(1, e);
+#ifdef ABRA_PK_TRACE
+        if (t == 0 && e < PK_TRACE_EV && blockIdx.x < 160) g_pk_trace[blockIdx.x][4][e] = g_pk_wait_ns;
+#endif
         if (e < nev - 1 && t == 0) pk_arrive(P.bar);
     }
     // the greedy pick: the last CTA to arrive decodes the merged key
@@ -1244,6 +1299,9 @@ bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn
 extern "C" int abra_pk_trace(unsigned long long *out, long long n) {
     const long long all = static_cast<long long>(sizeof(abra::g_pk_trace) / 8);
     return cudaMemcpyFromSymbol(out, abra::g_pk_trace, 8 * (n < all ? n : all)) == cudaSuccess ? 0 : -2;
+}
+extern "C" int abra_pk_units(unsigned long long *out) {
+    return cudaMemcpyFromSymbol(out, abra::g_pk_units, sizeof(abra::g_pk_units)) == cudaSuccess ? 0 : -2;
 }
 #endif
 
