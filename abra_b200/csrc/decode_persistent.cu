@@ -122,6 +122,12 @@ __device__ unsigned long long g_pk_trace[160][5][PK_TRACE_EV];
 __shared__ unsigned long long g_pk_wait_ns;  // this CTA's warps' waits on ring slots, per phase
 __device__ unsigned long long g_pk_units[5][64][4];  // CTA 0 warp 0: stamps inside the units of 5 GEMVs
 __shared__ int g_pk_gemv;                           // which GEMV of the token is running (CTA 0)
+__device__ unsigned long long g_pk_att[12];         // CTA 0 thread 0: steps of layer 1's first attention item
+#define PK_ASTAMP(layer, k)                                                   \
+    do {                                                                      \
+        if (blockIdx.x == 0 && threadIdx.x == 0 && (layer) == 1 && it == 0)   \
+            g_pk_att[k] = globaltimer_ns();                                   \
+    } while (0)
 #define PK_USTAMP(u, k)                                                                      \
     do {                                                                                     \
         if (blockIdx.x == 0 && (threadIdx.x >> 5) == 0 && lane == 0 && (u) < 64 * PK_NCW &&   \
@@ -133,6 +139,9 @@ __shared__ int g_pk_gemv;                           // which GEMV of the token i
         if ((idx) < PK_TRACE_EV && blockIdx.x < 160) g_pk_trace[blockIdx.x][kind][idx] = globaltimer_ns(); \
     } while (0)
 #else
+#define PK_ASTAMP(layer, k) \
+    do {                    \
+    } while (0)
 #define PK_USTAMP(u, k) \
     do {                \
     } while (0)
@@ -535,13 +544,16 @@ __device__ __forceinline__ void pk_xin_stage(int K, const float *h_in, const uin
 }
 
 // After it: x = s_x + delta (all of this thread's delta loads issued
-// first), written to h_out (element i by CTA i % grid); then RMSNorm * w and Q8_1 into the
+// first), written to h_out (each CTA its contiguous share); then RMSNorm * w and Q8_1 into the
 // activation records -- the XIN prologue of mmvq_q4k_kernel, operation for
 // operation (thread t sums x[t + 256 k]^2 with fmaf in k order).
 __device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, float *s_x, const float *s_w,
                                        float eps, uint8_t *arec, float *s_nred) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     constexpr int U = 10;
+    // this CTA's share of the write-back: every CTA holds the same x
+    const int own0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * K / gridDim.x);
+    const int own1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * K / gridDim.x);
     float acc = 0.0f;
     for (int i0 = t; i0 < K; i0 += 256 * U) {
         float d[U];
@@ -556,7 +568,7 @@ __device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, 
             if (i < K) {
                 float v = s_x[i];
                 if (delta) v = __fadd_rn(v, d[k]);
-                if (i % gridDim.x == blockIdx.x) h_out[i] = v;  // every CTA holds the same x
+                if (i >= own0 && i < own1) h_out[i] = v;
                 s_x[i] = v;
                 acc = __fmaf_rn(v, v, acc);
             }
@@ -588,7 +600,7 @@ __device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, 
 __device__ __forceinline__ void pk_quant_f32(const float *x, int K, uint8_t *arec) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane & 7;
     const int nblk = K / QK8_1;
-    constexpr int U = 5;
+    constexpr int U = 8;
     for (int base = warp * 4; base < nblk; base += PK_NCW * 4 * U) {
         float4 v[U];
 #pragma unroll
@@ -762,6 +774,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
     __half *kc = P.kc + layer * kv_layer, *vc = P.vc + layer * kv_layer;
     const int items = nkv * nch;
     for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        PK_ASTAMP(layer, 0);
         const int g = it % nkv, c = it / nkv;
         const bool tail = c == nch - 1;
         // the group's q heads; on the chunk holding pos also the k and v
@@ -793,6 +806,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
             }
         }
         cta_sync();
+        PK_ASTAMP(layer, 1);
         const int j = c * ATT_CHUNK_P + t;
         const bool valid = j < L;
         float s[GQ];
@@ -827,6 +841,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
                 }
             }
         }
+        PK_ASTAMP(layer, 2);
         float mxs[GQ];
 #pragma unroll
         for (int h = 0; h < GQ; ++h) {
@@ -838,6 +853,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
             s[h] = sv;
         }
         cta_sync();
+        PK_ASTAMP(layer, 3);
         float ev[GQ];
 #pragma unroll
         for (int h = 0; h < GQ; ++h) {
@@ -850,6 +866,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
             if (t == 0 && nch > 1) P.part_m[static_cast<int64_t>(g * GQ + h) * mc + c] = mx;
         }
         cta_sync();  // s_red is reused for the sums
+        PK_ASTAMP(layer, 4);
 #pragma unroll
         for (int h = 0; h < GQ; ++h) {
             float v = ev[h];
@@ -896,6 +913,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
             *reinterpret_cast<float4 *>(s_o + (warp * GQ + h) * 128 + 4 * lane) =
                 make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
         cta_sync();
+        PK_ASTAMP(layer, 5);
         if (nch == 1) {
             // one chunk: merge this CTA's heads in place (the merge's
             // arithmetic on the chunk's own max, sum and output)
@@ -917,7 +935,9 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
                 }
                 pk_head_out(P, g * GQ + h, x, lane);
             }
+            PK_ASTAMP(layer, 6);
             cta_sync();  // the scratch is reused by the next item
+            PK_ASTAMP(layer, 7);
             continue;
         }
         for (int i = t; i < GQ * 128; i += 256) {
@@ -1299,6 +1319,9 @@ bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn
 extern "C" int abra_pk_trace(unsigned long long *out, long long n) {
     const long long all = static_cast<long long>(sizeof(abra::g_pk_trace) / 8);
     return cudaMemcpyFromSymbol(out, abra::g_pk_trace, 8 * (n < all ? n : all)) == cudaSuccess ? 0 : -2;
+}
+extern "C" int abra_pk_att(unsigned long long *out) {
+    return cudaMemcpyFromSymbol(out, abra::g_pk_att, sizeof(abra::g_pk_att)) == cudaSuccess ? 0 : -2;
 }
 extern "C" int abra_pk_units(unsigned long long *out) {
     return cudaMemcpyFromSymbol(out, abra::g_pk_units, sizeof(abra::g_pk_units)) == cudaSuccess ? 0 : -2;
