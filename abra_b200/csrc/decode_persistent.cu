@@ -170,13 +170,22 @@ __device__ __forceinline__ void pk_arrive(unsigned long long *bar) {
     fence_acq_rel_gpu();
     red_relaxed_gpu_add(bar, 1ull);
 }
-// Thread 0: wait until every CTA has arrived (bounded; after one timeout in
-// this launch the remaining barriers pass at once), then acquire.
-__device__ __forceinline__ void pk_wait(const unsigned long long *bar, unsigned long long target) {
-    if (ld_relaxed_gpu(bar) < target && !pk_aborted()) {
+__device__ __forceinline__ void cta_sync() { named_bar_sync(1, PK_NCW * 32); }
+
+// Lane 0 of each of the CTA's first four warps polls the arrival counter
+// (their loads are in flight at different times, so the release is seen
+// sooner than by one poller's round trips); the first to see it publishes
+// phase e in *s_rel for the others.  Bounded like pk_wait; acquire after.
+__device__ __forceinline__ void pk_wait4(const unsigned long long *bar, unsigned long long target, int e,
+                                         volatile int *s_rel) {
+    if (*s_rel < e && !pk_aborted()) {
         const uint64_t t0 = globaltimer_ns();
         for (uint32_t i = 1;; ++i) {
-            if (ld_relaxed_gpu(bar) >= target) break;
+            if (*s_rel >= e) break;
+            if (ld_relaxed_gpu(bar) >= target) {
+                *s_rel = e;
+                break;
+            }
             if ((i & 63u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
                 report_error(ERR_GRID_TIMEOUT);
                 break;
@@ -185,7 +194,6 @@ __device__ __forceinline__ void pk_wait(const unsigned long long *bar, unsigned 
     }
     fence_acq_rel_gpu();
 }
-__device__ __forceinline__ void cta_sync() { named_bar_sync(1, PK_NCW * 32); }
 
 struct PkMm {
     const uint8_t *w0, *w1;
@@ -750,6 +758,23 @@ __device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int p
         s_in[128 + t] = Ly.k_norm[t];
         s_in[256 + t] = P.rope[static_cast<int64_t>(pos) * 128 + t];
     }
+    // the cached K and V rows of this CTA's items into L2 (positions before
+    // pos: written by earlier launches), so that the phase's loads do not
+    // queue behind the weight stream in HBM
+    if (t < 32) {
+        const int L = pos, nch = (pos + ATT_CHUNK_P) / ATT_CHUNK_P;
+        const size_t kv_layer = static_cast<size_t>(P.n_kv) * P.max_ctx * 128;
+        for (int it = blockIdx.x; it < P.n_kv * nch; it += gridDim.x) {
+            const int g = it % P.n_kv, c = it / P.n_kv;
+            const int j0 = c * ATT_CHUNK_P, nrow = min(ATT_CHUNK_P, L - j0);
+            if (nrow <= 0) continue;
+            const int64_t off = layer * kv_layer + (static_cast<int64_t>(g) * P.max_ctx + j0) * 128;
+            const uint32_t bytes = static_cast<uint32_t>(nrow) * 256u;  // fp16 rows of 128
+            const __half *base = (t & 16) ? P.vc + off : P.kc + off;
+            const uint32_t piece = 16384u, lo = (t & 15) * piece;
+            if (lo < bytes) prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(base) + lo, min(piece, bytes - lo));
+        }
+    }
 }
 
 // Attention of layer `layer` at position pos: items (kv head g, chunk c)
@@ -977,6 +1002,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
     __shared__ float s_nred[8];
     __shared__ unsigned long long s_amax;
     __shared__ unsigned s_flag;
+    __shared__ int s_rel;  // the last phase whose barrier this CTA has seen released
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + PK_NSLOT;
     uint8_t *ring = smem + P.off_ring;
@@ -988,6 +1014,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             mbar_init(&empty[s], 1);
         }
         fence_mbar_init();
+        s_rel = -1;
     }
     __syncthreads();
     if (threadIdx.x >= PK_NCW * 32) {
@@ -1025,7 +1052,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         if (ph == PH_OUT && t == 0) s_amax = 0ull;
         if (e > 0) {
             ++kb;
-            if (t == 0) pk_wait(P.bar, kb * G);
+            if ((t & 31) == 0 && t < 128) pk_wait4(P.bar, kb * G, e, &s_rel);
         }
         if (t == 0) PK_STAMP(0, e);
         cta_sync();
