@@ -172,20 +172,13 @@ __device__ __forceinline__ void pk_arrive(unsigned long long *bar) {
 }
 __device__ __forceinline__ void cta_sync() { named_bar_sync(1, PK_NCW * 32); }
 
-// Lane 0 of each of the CTA's first four warps polls the arrival counter
-// (their loads are in flight at different times, so the release is seen
-// sooner than by one poller's round trips); the first to see it publishes
-// phase e in *s_rel for the others.  Bounded like pk_wait; acquire after.
-__device__ __forceinline__ void pk_wait4(const unsigned long long *bar, unsigned long long target, int e,
-                                         volatile int *s_rel) {
-    if (*s_rel < e && !pk_aborted()) {
+// Thread 0: wait until every CTA has arrived (bounded; after one timeout in
+// this launch the remaining barriers pass at once), then acquire.
+__device__ __forceinline__ void pk_wait(const unsigned long long *bar, unsigned long long target) {
+    if (ld_relaxed_gpu(bar) < target && !pk_aborted()) {
         const uint64_t t0 = globaltimer_ns();
         for (uint32_t i = 1;; ++i) {
-            if (*s_rel >= e) break;
-            if (ld_relaxed_gpu(bar) >= target) {
-                *s_rel = e;
-                break;
-            }
+            if (ld_relaxed_gpu(bar) >= target) break;
             if ((i & 63u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
                 report_error(ERR_GRID_TIMEOUT);
                 break;
@@ -532,6 +525,39 @@ __device__ __forceinline__ void pk_quant4(uint8_t *arec, int i, int sub, float x
     pk_put_block(arec, i, sub, packed, __half2float(__float2half_rn(d)), sum);
 }
 
+// The reference Q8_1 rounding of one whole 32-value block in one lane
+// (d = amax / 127, q = roundf(x / d), the block's integer sum; the bytes of
+// quantize_block_warp, with no cross-lane steps); then the block into the
+// records.
+__device__ __forceinline__ void pk_quant_block(uint8_t *arec, int i, const float (&x)[32]) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) amax = fmaxf(amax, fabsf(x[k]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[8];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int q = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x[4 * k + j], id)))));
+            sum += q;
+            word |= (static_cast<uint32_t>(q) & 0xffu) << (8 * j);
+        }
+        w[k] = word;
+    }
+    uint8_t *rec = arec + (i >> 3) * PK_AREC;
+    const int s = i & 7;
+    uint4 *dst = reinterpret_cast<uint4 *>(rec + 32 * s);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    const float d8 = __half2float(__float2half_rn(d));
+    reinterpret_cast<float *>(rec + 256)[s] = d8;
+    reinterpret_cast<float *>(rec + 288)[s] = __fmul_rn(d8, __int2float_rn(sum));
+}
+
 // Before the phase's barrier: the residual stream h_in (stable since an
 // earlier phase), or the token's embedding row, into s_x.
 __device__ __forceinline__ void pk_xin_stage(int K, const float *h_in, const uint8_t *erow, float *s_x) {
@@ -604,55 +630,44 @@ __device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, 
 
 // Q8_1 of an fp32 activation written earlier in this launch (the SwiGLU
 // output), straight into the records: the bytes quantize_q8_1_kernel writes
-// and mmvq_q4k_kernel stages.  Each lane's loads are all issued first.
+// and mmvq_q4k_kernel stages.  One lane per block.
 __device__ __forceinline__ void pk_quant_f32(const float *x, int K, uint8_t *arec) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane & 7;
     const int nblk = K / QK8_1;
-    constexpr int U = 8;
-    for (int base = warp * 4; base < nblk; base += PK_NCW * 4 * U) {
-        float4 v[U];
+    for (int i = threadIdx.x; i < nblk; i += PK_NCW * 32) {
+        float v[32];
 #pragma unroll
-        for (int k = 0; k < U; ++k) {
-            const int i = base + k * PK_NCW * 4 + (lane >> 3);
-            if (base + k * PK_NCW * 4 < nblk) v[k] = __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + sub * 4));
+        for (int k = 0; k < 8; ++k) {
+            const float4 f = __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + 4 * k));
+            v[4 * k] = f.x;
+            v[4 * k + 1] = f.y;
+            v[4 * k + 2] = f.z;
+            v[4 * k + 3] = f.w;
         }
-#pragma unroll
-        for (int k = 0; k < U; ++k) {
-            const int b0 = base + k * PK_NCW * 4;  // warp-uniform: nblk % 8 == 0
-            if (b0 < nblk) pk_quant4(arec, b0 + (lane >> 3), sub, v[k].x, v[k].y, v[k].z, v[k].w);
-        }
+        pk_quant_block(arec, i, v);
     }
     cta_sync();
 }
 
 // Q8_1 blocks written earlier in this launch (oq) into the records (the
-// staging loop of mmvq_q4k_kernel, loads through L2): eight lanes per block,
-// one 32-bit word of quants each; every load issued first.
+// staging loop of mmvq_q4k_kernel, loads through L2): one lane per block.
 __device__ __forceinline__ void pk_stage_q8(const uint8_t *X, int K, uint8_t *arec) {
     const int nblk = K / QK8_1;
-    const int lane = threadIdx.x & 31, sub = lane & 7;
-    constexpr int U = 4;
-    for (int base = threadIdx.x >> 3; base < nblk; base += PK_NCW * 4 * U) {
-        uint32_t qw[U], h[U];
+    for (int i = threadIdx.x; i < nblk; i += PK_NCW * 32) {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(X + static_cast<int64_t>(i) * Q81_BYTES);
+        uint32_t q[9];
 #pragma unroll
-        for (int k = 0; k < U; ++k) {
-            const int i = base + k * PK_NCW * 4;
-            if (i < nblk) {
-                const uint32_t *src = reinterpret_cast<const uint32_t *>(X + static_cast<int64_t>(i) * Q81_BYTES);
-                qw[k] = __ldcg(src + 1 + sub);
-                h[k] = __ldcg(src);
-            }
-        }
+        for (int k = 0; k < 9; ++k) q[k] = __ldcg(src + k);
+        int msum = 0;
 #pragma unroll
-        for (int k = 0; k < U; ++k) {
-            const int i = base + k * PK_NCW * 4;  // warp-uniform: nblk % 8 == 0
-            if (i < nblk) {
-                int msum = dp4a_ss(0x01010101, static_cast<int>(qw[k]), 0);
-#pragma unroll
-                for (int m = 4; m >= 1; m >>= 1) msum += __shfl_xor_sync(0xffffffffu, msum, m);
-                pk_put_block(arec, i, sub, qw[k], half_lo(h[k]), msum);
-            }
-        }
+        for (int k = 1; k < 9; ++k) msum = dp4a_ss(0x01010101, static_cast<int>(q[k]), msum);
+        uint8_t *rec = arec + (i >> 3) * PK_AREC;
+        const int s = i & 7;
+        uint4 *dst = reinterpret_cast<uint4 *>(rec + 32 * s);
+        dst[0] = make_uint4(q[1], q[2], q[3], q[4]);
+        dst[1] = make_uint4(q[5], q[6], q[7], q[8]);
+        const float d8 = half_lo(q[0]);
+        reinterpret_cast<float *>(rec + 256)[s] = d8;
+        reinterpret_cast<float *>(rec + 288)[s] = __fmul_rn(d8, __int2float_rn(msum));
     }
     cta_sync();
 }
@@ -1002,7 +1017,6 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
     __shared__ float s_nred[8];
     __shared__ unsigned long long s_amax;
     __shared__ unsigned s_flag;
-    __shared__ int s_rel;  // the last phase whose barrier this CTA has seen released
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + PK_NSLOT;
     uint8_t *ring = smem + P.off_ring;
@@ -1014,7 +1028,6 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             mbar_init(&empty[s], 1);
         }
         fence_mbar_init();
-        s_rel = -1;
     }
     __syncthreads();
     if (threadIdx.x >= PK_NCW * 32) {
@@ -1052,7 +1065,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         if (ph == PH_OUT && t == 0) s_amax = 0ull;
         if (e > 0) {
             ++kb;
-            if ((t & 31) == 0 && t < 128) pk_wait4(P.bar, kb * G, e, &s_rel);
+            if (t == 0) pk_wait(P.bar, kb * G);
         }
         if (t == 0) PK_STAMP(0, e);
         cta_sync();
