@@ -576,6 +576,8 @@ def run_case(a):
         return run_case_q6k(a)
     if a.case == "tc_b32_16384":
         return run_case_tc(a)
+    if a.case in ("decode_token", "decode_chain"):
+        return run_case_decode(a)
     if a.case == "fused_rmsnorm_block":
         torch.cuda.set_device(0)
         print(json.dumps({"case": a.case, **fused_rmsnorm_block(torch, a.steps, copies=max(8, a.copies))}),
@@ -660,6 +662,24 @@ def run_case_q6k(a):
     return 0
 
 
+def run_case_decode(a):
+    """Profiling case for the decode step at ``--depth``: the full-size
+    Qwen3-4B-shaped model (2.3 GB of weights), the prompt and depth prefix fed
+    token by token, ``--warmup`` then ``--steps`` tokens; decode_token is the
+    persistent kernel (one launch per token), decode_chain the per-operation
+    kernel chain (attention, QK-norm and merge kernels included)."""
+    import torch
+
+    from abra_b200.model import KERNEL_CHAIN
+
+    torch.cuda.set_device(0)
+    flags = KERNEL_CHAIN if a.case == "decode_chain" else 0
+    r = decode_depth(torch, a.depth, a.warmup, a.steps, streaming=False, flags=flags,
+                     n_layers=a.layers)
+    print(json.dumps({"case": a.case, "layers": a.layers, **r}), flush=True)
+    return 0
+
+
 TC_CASE_SHAPE = (16384, 2560)
 
 
@@ -717,7 +737,7 @@ KV_BYTES_PER_POS = 36 * 2 * 8 * 128 * 2
 
 
 def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, seed: int = 0,
-                 dist=None, flags: int = 0):
+                 dist=None, flags: int = 0, n_layers: int = 36):
     """One decode measurement: a model sized for the prompt + depth prefix +
     warm-up + timed tokens; the prefix is fed untimed (token by token through
     the same step), then ``warmup`` untimed tokens, then ``steps`` timed
@@ -730,7 +750,7 @@ def decode_depth(torch, depth: int, warmup: int, steps: int, streaming: bool, se
     n_prompt = PROMPT + depth
     rank, world = (dist.rank, dist.world) if dist else (0, 1)
     m = DecodeModel(rank=rank, world=world, max_ctx=n_prompt + warmup + steps, seed=seed,
-                    flags=flags)
+                    flags=flags, n_layers=n_layers)
     prompt = np.random.default_rng(seed + depth).integers(0, m.cfg.vocab, n_prompt).astype(np.int32)
     m.reset(prompt)
     m.step(n_prompt - 1 + warmup)
@@ -1263,9 +1283,12 @@ def main():
                     help="skip the per-shape table and the reference kernel family")
     ap.add_argument("--quick", action="store_true", help="decode: depth 0 only")
     ap.add_argument("--case", choices=[n for n, _, _ in DECODE_MATRICES] + ["qkv", "gate_up"]
-                    + [f"q6k_{n}" for n, _, _ in Q6K_SHAPES] + ["tc_b32_16384", "fused_rmsnorm_block"],
+                    + [f"q6k_{n}" for n, _, _ in Q6K_SHAPES]
+                    + ["tc_b32_16384", "fused_rmsnorm_block", "decode_token", "decode_chain"],
                     help="profiling mode: one operator, eager launches")
     ap.add_argument("--copies", type=int, default=2, help="weight copies in --case mode")
+    ap.add_argument("--depth", type=int, default=0, help="context depth in the decode_* cases")
+    ap.add_argument("--layers", type=int, default=36, help="transformer layers in the decode_* cases")
     a = ap.parse_args()
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
