@@ -763,6 +763,7 @@ __device__ __forceinline__ void pk_head_out(uint64_t *oq, uint32_t tag, int hq, 
         const uint32_t hd = __half_as_ushort(__float2half_rn(d));
         const uint32_t hs = __half_as_ushort(__float2half_rn(__fmul_rn(d, static_cast<float>(sum))));
         ll_st(blk, hd | (hs << 16), tag);
+        ll_st(blk + PK_OQ_WORDS - 1, 0u, tag);  // the pad word: read (and waited for) with its pair
     }
 }
 

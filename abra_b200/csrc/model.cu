@@ -1285,11 +1285,24 @@ int abra_model_invalidate(void *model) {
     return ABRA_OK;
 }
 
+// After a synchronize: a kernel's bounded wait that gave up (the device
+// error word, left set) fails the call instead of passing its garbage on.
+static int device_waits_ok() {
+    unsigned v = 0;
+    cudaError_t e = abra::read_error_words(&v, false);
+    if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "device error word", e);
+    if (v) {
+        snprintf(g_model_err, sizeof g_model_err, "a kernel's bounded wait gave up (device error word 0x%x)", v);
+        return ABRA_E_CUDA;
+    }
+    return ABRA_OK;
+}
+
 int abra_model_sync(void *model) {
     Model *m = static_cast<Model *>(model);
     if (!m) return ABRA_E_INVALID;
     cudaError_t e = cudaStreamSynchronize(m->stream);
-    return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "sync", e);
+    return e == cudaSuccess ? device_waits_ok() : model_fail(ABRA_E_CUDA, "sync", e);
 }
 
 int abra_model_read(void *model, int32_t *tokens, int32_t n_tokens, float *logits,
@@ -1304,7 +1317,7 @@ int abra_model_read(void *model, int32_t *tokens, int32_t n_tokens, float *logit
         e = cudaMemcpy(logits, m->logits, static_cast<size_t>(m->sh.vocab_hi - m->sh.vocab_lo) * 4,
                        cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && pos) e = cudaMemcpy(pos, m->pos, 4, cudaMemcpyDeviceToHost);
-    return e == cudaSuccess ? ABRA_OK : model_fail(ABRA_E_CUDA, "read", e);
+    return e == cudaSuccess ? device_waits_ok() : model_fail(ABRA_E_CUDA, "read", e);
 }
 
 int abra_model_generate(void *model, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
