@@ -195,51 +195,55 @@ __device__ __forceinline__ void ll_load(uint64_t *w, int k, Addr addr) {
         ll_ld2(addr(k), w[2 * k], w[2 * k + 1]);
 }
 
-// Polls one item until it carries `tag` (bounded: false once the launch
-// has given up).
-template <int W>
-__device__ __forceinline__ bool ll_poll(const uint64_t *p, uint32_t tag, uint64_t t0) {
-    for (;;) {
-        uint64_t a, b = 0;
-        bool ok;
-        if constexpr (W == 1) {
-            ll_ld1(p, a);
-            ok = ll_ok(a, tag);
-        } else {
-            ll_ld2(p, a, b);
-            ok = ll_ok(a, tag) && ll_ok(b, tag);
+// Waits until each stale item carries `tag`, re-reading all of them each
+// round (no values kept: the caller loads them again).  Bounded: after
+// WAIT_LIMIT_NS the launch records ERR_GRID_TIMEOUT and every later wait of
+// the launch passes at once.
+template <int N, int W, class Addr>
+__device__ __forceinline__ void ll_wait(uint32_t stale, uint32_t tag, Addr addr) {
+    const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+    while (stale) {
+        uint64_t v[N * W];
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if ((stale >> k) & 1u) ll_load<W>(v, k, addr);
+        uint32_t next = 0;
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            bool ok = ll_ok(v[W * k], tag);
+            if constexpr (W == 2) ok = ok && ll_ok(v[2 * k + 1], tag);
+            if (((stale >> k) & 1u) && !ok) next |= 1u << k;
         }
-        if (ok) return true;
-        if (pk_aborted() || globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+        stale = next;
+        if (stale && (pk_aborted() || globaltimer_ns() - t0 > WAIT_LIMIT_NS)) {
             report_error(ERR_GRID_TIMEOUT);
-            return false;
+            return;
         }
     }
 }
 
-// Loads the `live` items of w (all issued before any is checked) until every
-// one carries `tag`.  While some are stale only the lowest is polled (a few
-// bytes a round per thread, so waiting CTAs leave L2 to the weight stream);
-// when it turns, all are loaded again.  Bounded: after WAIT_LIMIT_NS the
-// launch records ERR_GRID_TIMEOUT and every later wait of the launch passes
-// at once.
+// Loads the `live` items of w, all issued before any is checked; if some
+// are stale, waits for them (ll_wait) and loads the items once more.
 template <int N, int W, class Addr>
 __device__ __forceinline__ void ll_fetch(uint64_t (&w)[N * W], uint32_t tag, uint32_t live, Addr addr) {
-    uint64_t t0 = 0;
-    for (;;) {
+    auto load_all = [&]() {
+        uint32_t stale = 0;
 #pragma unroll
         for (int k = 0; k < N; ++k)
             if ((live >> k) & 1u) ll_load<W>(w, k, addr);
-        uint32_t stale = 0;
 #pragma unroll
         for (int k = 0; k < N; ++k) {
             bool ok = ll_ok(w[W * k], tag);
             if constexpr (W == 2) ok = ok && ll_ok(w[2 * k + 1], tag);
             if (((live >> k) & 1u) && !ok) stale |= 1u << k;
         }
-        if (!stale) return;
-        if (!t0) t0 = globaltimer_ns();
-        if (!ll_poll<W>(addr(__ffs(stale) - 1), tag, t0)) return;
+        return stale;
+    };
+    const uint32_t stale = load_all();
+    if (stale) {
+        ll_wait<N, W>(stale, tag, addr);
+        load_all();
     }
 }
 
@@ -436,10 +440,9 @@ __device__ __forceinline__ float pk_slice_tree(float v) {
 // K-slice sums and their fixed tree; the row's first lane stores y (tagged
 // into Yt, or plain into Y for the logits, merging the argmax key).
 template <int NMAT>
-__device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, uint32_t T, const uint8_t *ring,
-                                         uint64_t *full, uint64_t *empty, float *vbuf, const uint8_t *arec,
-                                         float *Y, uint64_t *Yt, uint32_t tag, unsigned long long *s_amax, int sh,
-                                         bool &poisoned) {
+__device__ __noinline__ bool pk_units(const PkMm mm, int u_begin, int nu, uint32_t T, const uint8_t *ring,
+                                      uint64_t *full, uint64_t *empty, float *vbuf, const uint8_t *arec, float *Y,
+                                      uint64_t *Yt, uint32_t tag, unsigned long long *s_amax, int sh, bool poisoned) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int lr = mm.lr, R = 1 << lr, P = 32 >> lr;
     // lane -> (row r, first superblock p); rows are staged back to back
@@ -524,6 +527,7 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
         __syncwarp();  // the staging buffer is reused by the next unit
         PK_USTAMP(u, 3);
     }
+    return poisoned;
 }
 
 // --------------------------------------- consumer: activation prologues ---
@@ -649,7 +653,7 @@ __device__ __forceinline__ void pk_xin(int K, const uint64_t *delta, uint32_t ta
 __device__ __forceinline__ void pk_quant_act(const uint64_t *x, uint32_t tag, int K, uint8_t *arec) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane & 7;
     const int nblk = K / QK8_1;
-    constexpr int U = 10;                    // passes per batch: 2 pairs each
+    constexpr int U = 5;                     // passes per batch: 2 pairs each
     constexpr int STEP = PK_NCW * 4;         // blocks per pass of the CTA
     for (int p0 = 0; p0 * STEP < nblk; p0 += U) {
         uint64_t w[4 * U];
@@ -841,8 +845,8 @@ __device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int p
 // Each item waits for exactly its group's tagged q|k|v words; CTAs without
 // an item go straight on to the o GEMV.
 template <int GQ>
-__device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int pos, uint32_t tag, float *scr,
-                                             unsigned *s_flag) {
+__device__ __noinline__ void pk_attention(const PkParams &P, int layer, int pos, uint32_t tag, float *scr,
+                                          unsigned *s_flag) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     float(*s_q)[128] = reinterpret_cast<float(*)[128]>(scr);                              // [GQ][128]
     float(*s_e)[ATT_CHUNK_P] = reinterpret_cast<float(*)[ATT_CHUNK_P]>(scr + GQ * 128);    // [GQ][256]
@@ -1060,7 +1064,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
 
 // --------------------------------------------------------------- kernel ---
 template <int GQ>
-__global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkParams P) {
+__global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const __grid_constant__ PkParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_nred[8];
     __shared__ unsigned long long s_amax;
@@ -1152,11 +1156,11 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
 #endif
             unsigned long long *amax = ph == PH_OUT ? &s_amax : nullptr;
             if (mm.w1)
-                pk_units<2>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, P.logits, Yt, tag, amax,
-                            P.slot_shift, poisoned);
+                poisoned = pk_units<2>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, P.logits, Yt, tag,
+                                       amax, P.slot_shift, poisoned);
             else
-                pk_units<1>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, P.logits, Yt, tag, amax,
-                            P.slot_shift, poisoned);
+                poisoned = pk_units<1>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, P.logits, Yt, tag,
+                                       amax, P.slot_shift, poisoned);
             T += static_cast<uint32_t>(nu);
         }
         cta_sync();  // shared memory is reused by the next phase
