@@ -37,7 +37,7 @@ enum : unsigned {
     ERR_WAIT_TIMEOUT = 1u << 0,  // a consumer's wait for staged data gave up
     ERR_FLAG_TIMEOUT = 1u << 1,  // a cross-rank flag wait gave up
     ERR_WAIT_EMPTY = 1u << 2,    // a producer's wait for a free stage gave up
-    ERR_GRID_TIMEOUT = 1u << 3,  // the persistent decode's wait for another CTA's data gave up
+    ERR_GRID_TIMEOUT = 1u << 3,  // a grid-wide barrier of the persistent decode gave up
 };
 
 // Wall-clock bound of every spin-wait in these kernels (nanoseconds).

@@ -71,17 +71,16 @@ struct PersistModel {
     const PersistLayer *layers;  // device array of n_layers entries
     const uint8_t *embd;
     const float *out_norm;
-    float *logits;
-    void *scratch;  // persist_scratch_bytes() bytes, zeroed once: tagged words, attention partials
+    float *h0, *h1, *delta, *qkv, *att, *part_m, *part_l, *part_o, *act, *logits;
+    uint8_t *oq;
     void *kc, *vc;  // fp16 caches [layer][kv head][max_ctx][128]
     const float *rope;
     int32_t *tokens, *picks, *pos;
     const int32_t *nprompt;
     unsigned long long *amax;
-    void *sync;  // persist_sync_bytes() zeroed bytes: launch and merge arrival counters
+    void *sync;  // persist_sync_bytes() zeroed bytes: barrier and arrival counters
 };
-size_t persist_sync_bytes(int n_layers, int n_kv);
-size_t persist_scratch_bytes(int n_layers, int hidden, int n_heads, int n_kv, int ffn, int max_ctx);
+size_t persist_sync_bytes(int n_kv);
 // False (with a reason) when the shape does not fit the kernel's ring and
 // shared-memory plan; the model then runs the kernel chain.
 bool persist_supported(int hidden, int n_heads, int n_kv, int ffn, int head_dim, const char **why);

@@ -92,32 +92,25 @@ constexpr int PK_VMAX = 80;
 enum : int { PK_QKV = 0, PK_O = 1, PK_GU = 2, PK_DOWN = 3, PK_OUT = 4, PK_KINDS = 5 };
 enum : int { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_OUT = 5 };
 
-// Words of one Q8_1 block in the tagged attention output: d|s, eight quant
-// words, one pad word (80 bytes, so a block is five 16-byte pairs).
-constexpr int PK_OQ_WORDS = 10;
-
 struct PkParams {
     const PersistLayer *layers;  // device array, n_layers entries
     const uint8_t *embd;
     const float *out_norm;
     int n_layers, hidden, n_heads, n_kv, ffn, vocab, max_ctx, max_chunks;
     float eps, scale;
-    // tagged outputs, one buffer per layer: q|k|v [L][nqkv], Q8_1 attention
-    // output [L][n_heads * 4][PK_OQ_WORDS], residual deltas [L][2][hidden]
-    // (o, down), SwiGLU [L][ffn]
-    uint64_t *t_qkv, *t_oq, *t_dlt, *t_act;
-    float *part_m, *part_l, *part_o;  // [2][n_heads][max_chunks](x128): chunk partials by layer parity
-    float *logits;
+    float *h[2];
+    float *delta, *qkv, *att, *part_m, *part_l, *part_o, *act, *logits;
+    uint8_t *oq;
     __half *kc, *vc;
     const float *rope;
     int32_t *tokens, *picks, *pos;
     const int32_t *nprompt;
     unsigned long long *amax;
-    unsigned long long *bar, *gen;  // CTAs done with the launch's output, launches completed
-    unsigned *head_cnt;             // merge arrivals per (layer, kv head)
+    unsigned long long *bar, *gen;  // grid barrier arrivals, launches completed
+    unsigned *head_cnt;             // merge arrivals per kv head
     int lr[PK_KINDS], pitch[PK_KINDS];  // log2 rows per unit and staged row pitch per GEMV kind
     int slot_shift;                     // log2 of the ring slots (4: 16 slots, 3: 8)
-    int off_vbuf, off_arec, off_w, off_x, off_ring, smem;  // dynamic shared memory layout
+    int off_vbuf, off_arec, off_x, off_ring, smem;  // dynamic shared memory layout
 };
 
 #ifdef ABRA_PK_TRACE
@@ -158,93 +151,41 @@ __device__ unsigned long long g_pk_att[12];         // CTA 0 thread 0: steps of 
 #endif
 
 // ------------------------------------------------------------ helpers ---
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void red_relaxed_gpu_add(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ bool pk_aborted() {
     return (*static_cast<volatile unsigned *>(&g_abra_device_error) & ERR_GRID_TIMEOUT) != 0;
 }
+// Thread 0 of a CTA whose consumers have passed a CTA barrier after their
+// last writes of the phase: publish the CTA's arrival (release at GPU scope:
+// the fence orders every write the CTA barrier made visible to this thread).
+__device__ __forceinline__ void pk_arrive(unsigned long long *bar) {
+    fence_acq_rel_gpu();
+    red_relaxed_gpu_add(bar, 1ull);
+}
 __device__ __forceinline__ void cta_sync() { named_bar_sync(1, PK_NCW * 32); }
 
-// ----------------------------------------------------------- tagged words ---
-// Every value one CTA hands to another inside the launch (q|k|v, the Q8_1
-// attention output, the two residual deltas of each layer, the SwiGLU
-// output) travels as a 64-bit word: the value's 32 bits low, the launch's tag
-// (launches completed + 1) high, written and read as single relaxed
-// gpu-scope accesses.  A reader that sees the tag sees the value, so no grid
-// barrier, fence or counter sits between producer and consumer: each
-// consumer waits for exactly the words it reads.  Each (layer, phase) output
-// has its own buffer, so no word is rewritten within a launch.
-__device__ __forceinline__ void ll_st(uint64_t *p, uint32_t v, uint32_t tag) {
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"((static_cast<uint64_t>(tag) << 32) | v)
-                 : "memory");
-}
-__device__ __forceinline__ void ll_ld1(const uint64_t *p, uint64_t &a) {
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(a) : "l"(p));
-}
-__device__ __forceinline__ void ll_ld2(const uint64_t *p, uint64_t &a, uint64_t &b) {
-    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p));
-}
-__device__ __forceinline__ bool ll_ok(uint64_t w, uint32_t tag) { return static_cast<uint32_t>(w >> 32) == tag; }
-__device__ __forceinline__ float ll_f(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
-__device__ __forceinline__ uint32_t ll_u(uint64_t w) { return static_cast<uint32_t>(w); }
-
-// Loads item k (W = 1 or 2 words at addr(k); a pair is one 16-byte access).
-template <int W, class Addr>
-__device__ __forceinline__ void ll_load(uint64_t *w, int k, Addr addr) {
-    if constexpr (W == 1)
-        ll_ld1(addr(k), w[k]);
-    else
-        ll_ld2(addr(k), w[2 * k], w[2 * k + 1]);
-}
-
-// Waits until each stale item carries `tag`, re-reading all of them each
-// round (no values kept: the caller loads them again).  Bounded: after
-// WAIT_LIMIT_NS the launch records ERR_GRID_TIMEOUT and every later wait of
-// the launch passes at once.
-template <int N, int W, class Addr>
-__device__ __forceinline__ void ll_wait(uint32_t stale, uint32_t tag, Addr addr) {
-    const uint64_t t0 = globaltimer_ns();
-#pragma unroll 1
-    while (stale) {
-        uint64_t v[N * W];
-#pragma unroll
-        for (int k = 0; k < N; ++k)
-            if ((stale >> k) & 1u) ll_load<W>(v, k, addr);
-        uint32_t next = 0;
-#pragma unroll
-        for (int k = 0; k < N; ++k) {
-            bool ok = ll_ok(v[W * k], tag);
-            if constexpr (W == 2) ok = ok && ll_ok(v[2 * k + 1], tag);
-            if (((stale >> k) & 1u) && !ok) next |= 1u << k;
-        }
-        stale = next;
-        if (stale && (pk_aborted() || globaltimer_ns() - t0 > WAIT_LIMIT_NS)) {
-            report_error(ERR_GRID_TIMEOUT);
-            return;
+// Thread 0: wait until every CTA has arrived (bounded; after one timeout in
+// this launch the remaining barriers pass at once), then acquire.
+__device__ __forceinline__ void pk_wait(const unsigned long long *bar, unsigned long long target) {
+    if (ld_relaxed_gpu(bar) < target && !pk_aborted()) {
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t i = 1;; ++i) {
+            if (ld_relaxed_gpu(bar) >= target) break;
+            if ((i & 63u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+                report_error(ERR_GRID_TIMEOUT);
+                break;
+            }
         }
     }
-}
-
-// Loads the `live` items of w, all issued before any is checked; if some
-// are stale, waits for them (ll_wait) and loads the items once more.
-template <int N, int W, class Addr>
-__device__ __forceinline__ void ll_fetch(uint64_t (&w)[N * W], uint32_t tag, uint32_t live, Addr addr) {
-    auto load_all = [&]() {
-        uint32_t stale = 0;
-#pragma unroll
-        for (int k = 0; k < N; ++k)
-            if ((live >> k) & 1u) ll_load<W>(w, k, addr);
-#pragma unroll
-        for (int k = 0; k < N; ++k) {
-            bool ok = ll_ok(w[W * k], tag);
-            if constexpr (W == 2) ok = ok && ll_ok(w[2 * k + 1], tag);
-            if (((live >> k) & 1u) && !ok) stale |= 1u << k;
-        }
-        return stale;
-    };
-    const uint32_t stale = load_all();
-    if (stale) {
-        ll_wait<N, W>(stale, tag, addr);
-        load_all();
-    }
+    fence_acq_rel_gpu();
 }
 
 struct PkMm {
@@ -437,12 +378,12 @@ __device__ __forceinline__ float pk_slice_tree(float v) {
 // The units of one GEMV phase that belong to this warp (unit u of the CTA's
 // range -> warp u % 8, ring slot (T + u) % NSLOT).  The superblock values
 // meet in this warp's staging buffer; eight lanes per row form the canonical
-// K-slice sums and their fixed tree; the row's first lane stores y (tagged
-// into Yt, or plain into Y for the logits, merging the argmax key).
+// K-slice sums and their fixed tree; the row's first lane stores y (and
+// merges the argmax key).
 template <int NMAT>
-__device__ __noinline__ bool pk_units(const PkMm mm, int u_begin, int nu, uint32_t T, const uint8_t *ring,
-                                      uint64_t *full, uint64_t *empty, float *vbuf, const uint8_t *arec, float *Y,
-                                      uint64_t *Yt, uint32_t tag, unsigned long long *s_amax, int sh, bool poisoned) {
+__device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, uint32_t T, const uint8_t *ring,
+                                         uint64_t *full, uint64_t *empty, float *vbuf, const uint8_t *arec,
+                                         float *Y, unsigned long long *s_amax, int sh, bool &poisoned) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int lr = mm.lr, R = 1 << lr, P = 32 >> lr;
     // lane -> (row r, first superblock p); rows are staged back to back
@@ -506,10 +447,7 @@ __device__ __noinline__ bool pk_units(const PkMm mm, int u_begin, int nu, uint32
                 yv = __fmul_rn(up, abra_silu(yv));
             }
             if (i == 0 && live && row < N) {
-                if (Yt)
-                    ll_st(Yt + row, __float_as_uint(yv), tag);
-                else
-                    Y[row] = yv;
+                Y[row] = yv;
                 const unsigned long long k = argmax_key(yv, row);
                 key = k > key ? k : key;
             }
@@ -527,7 +465,6 @@ __device__ __noinline__ bool pk_units(const PkMm mm, int u_begin, int nu, uint32
         __syncwarp();  // the staging buffer is reused by the next unit
         PK_USTAMP(u, 3);
     }
-    return poisoned;
 }
 
 // --------------------------------------- consumer: activation prologues ---
@@ -588,39 +525,84 @@ __device__ __forceinline__ void pk_quant4(uint8_t *arec, int i, int sub, float x
     pk_put_block(arec, i, sub, packed, __half2float(__float2half_rn(d)), sum);
 }
 
-// The token's embedding row (embed_kernel's arithmetic) into the residual
-// stream s_x: the start of layer 0's QKV prologue.
-__device__ __forceinline__ void pk_embed_stage(int K, const uint8_t *erow, float *s_x) {
-    for (int i = threadIdx.x; i < K; i += PK_NCW * 32) s_x[i] = pk_embed(erow, i);
+// The reference Q8_1 rounding of one whole 32-value block in one lane
+// (d = amax / 127, q = roundf(x / d), the block's integer sum; the bytes of
+// quantize_block_warp, with no cross-lane steps); then the block into the
+// records.
+__device__ __forceinline__ void pk_quant_block(uint8_t *arec, int i, const float (&x)[32]) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) amax = fmaxf(amax, fabsf(x[k]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[8];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int q = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x[4 * k + j], id)))));
+            sum += q;
+            word |= (static_cast<uint32_t>(q) & 0xffu) << (8 * j);
+        }
+        w[k] = word;
+    }
+    uint8_t *rec = arec + (i >> 3) * PK_AREC;
+    const int s = i & 7;
+    uint4 *dst = reinterpret_cast<uint4 *>(rec + 32 * s);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    const float d8 = __half2float(__float2half_rn(d));
+    reinterpret_cast<float *>(rec + 256)[s] = d8;
+    reinterpret_cast<float *>(rec + 288)[s] = __fmul_rn(d8, __int2float_rn(sum));
 }
 
-// The residual add, RMSNorm * w and Q8_1 into the activation records: the
-// XIN prologue of mmvq_q4k_kernel, operation for operation (thread t sums
-// x[t + 256 k]^2 with fmaf in k order).  The residual stream lives in this
-// CTA's shared memory for the whole token (every CTA holds the same x); the
-// delta (the tagged output of the layer's o or down GEMV, or none for the
-// embedding row) is added in place, all of this thread's words loaded before
-// the first is waited for.
-__device__ __forceinline__ void pk_xin(int K, const uint64_t *delta, uint32_t tag, float *s_x, const float *s_w,
+// Before the phase's barrier: the residual stream h_in (stable since an
+// earlier phase), or the token's embedding row, into s_x.
+__device__ __forceinline__ void pk_xin_stage(int K, const float *h_in, const uint8_t *erow, float *s_x) {
+    constexpr int U = 8;
+    for (int i0 = threadIdx.x; i0 < K; i0 += 256 * U) {
+        float v[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = i0 + k * 256;
+            v[k] = i < K ? (erow ? pk_embed(erow, i) : __ldcg(h_in + i)) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = i0 + k * 256;
+            if (i < K) s_x[i] = v[k];
+        }
+    }
+}
+
+// After it: x = s_x + delta (all of this thread's delta loads issued
+// first), written to h_out (each CTA its contiguous share); then RMSNorm * w and Q8_1 into the
+// activation records -- the XIN prologue of mmvq_q4k_kernel, operation for
+// operation (thread t sums x[t + 256 k]^2 with fmaf in k order).
+__device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, float *s_x, const float *s_w,
                                        float eps, uint8_t *arec, float *s_nred) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     constexpr int U = 10;
+    // this CTA's share of the write-back: every CTA holds the same x
+    const int own0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * K / gridDim.x);
+    const int own1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * K / gridDim.x);
     float acc = 0.0f;
     for (int i0 = t; i0 < K; i0 += 256 * U) {
-        uint64_t d[U];
-        if (delta) {
-            uint32_t live = 0;
+        float d[U];
 #pragma unroll
-            for (int k = 0; k < U; ++k)
-                if (i0 + k * 256 < K) live |= 1u << k;
-            ll_fetch<U, 1>(d, tag, live, [&](int k) { return delta + i0 + k * 256; });
+        for (int k = 0; k < U; ++k) {
+            const int i = i0 + k * 256;
+            d[k] = (delta && i < K) ? __ldcg(delta + i) : 0.0f;
         }
 #pragma unroll
         for (int k = 0; k < U; ++k) {
             const int i = i0 + k * 256;
             if (i < K) {
                 float v = s_x[i];
-                if (delta) v = __fadd_rn(v, ll_f(d[k]));
+                if (delta) v = __fadd_rn(v, d[k]);
+                if (i >= own0 && i < own1) h_out[i] = v;
                 s_x[i] = v;
                 acc = __fmaf_rn(v, v, acc);
             }
@@ -646,48 +628,35 @@ __device__ __forceinline__ void pk_xin(int K, const uint64_t *delta, uint32_t ta
     cta_sync();
 }
 
-// Q8_1 of the tagged SwiGLU output straight into the records: the bytes
-// quantize_q8_1_kernel writes and mmvq_q4k_kernel stages.  Eight lanes per
-// block, four consecutive values (two 16-byte pairs) each; every pass of the
-// batch loaded before the first is waited for.
-__device__ __forceinline__ void pk_quant_act(const uint64_t *x, uint32_t tag, int K, uint8_t *arec) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane & 7;
+// Q8_1 of an fp32 activation written earlier in this launch (the SwiGLU
+// output), straight into the records: the bytes quantize_q8_1_kernel writes
+// and mmvq_q4k_kernel stages.  One lane per block.
+__device__ __forceinline__ void pk_quant_f32(const float *x, int K, uint8_t *arec) {
     const int nblk = K / QK8_1;
-    constexpr int U = 5;                     // passes per batch: 2 pairs each
-    constexpr int STEP = PK_NCW * 4;         // blocks per pass of the CTA
-    for (int p0 = 0; p0 * STEP < nblk; p0 += U) {
-        uint64_t w[4 * U];
-        uint32_t live = 0;
-        auto addr = [&](int k) {  // pair k: pass k / 2, half k % 2
-            const int i = (p0 + (k >> 1)) * STEP + warp * 4 + (lane >> 3);
-            return x + static_cast<int64_t>(i) * QK8_1 + sub * 4 + 2 * (k & 1);
-        };
+    for (int i = threadIdx.x; i < nblk; i += PK_NCW * 32) {
+        float v[32];
 #pragma unroll
-        for (int k = 0; k < 2 * U; ++k)
-            if ((p0 + (k >> 1)) * STEP + warp * 4 < nblk) live |= 1u << k;  // warp-uniform
-        ll_fetch<2 * U, 2>(w, tag, live, addr);
-#pragma unroll
-        for (int q = 0; q < U; ++q) {
-            const int b0 = (p0 + q) * STEP + warp * 4;
-            if (b0 < nblk)
-                pk_quant4(arec, b0 + (lane >> 3), sub, ll_f(w[4 * q]), ll_f(w[4 * q + 1]), ll_f(w[4 * q + 2]),
-                          ll_f(w[4 * q + 3]));
+        for (int k = 0; k < 8; ++k) {
+            const float4 f = __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + 4 * k));
+            v[4 * k] = f.x;
+            v[4 * k + 1] = f.y;
+            v[4 * k + 2] = f.z;
+            v[4 * k + 3] = f.w;
         }
+        pk_quant_block(arec, i, v);
     }
     cta_sync();
 }
 
-// The tagged Q8_1 attention output into the records (the staging loop of
-// mmvq_q4k_kernel): one lane per block, five 16-byte pairs.
-__device__ __forceinline__ void pk_stage_q8(const uint64_t *X, uint32_t tag, int K, uint8_t *arec) {
+// Q8_1 blocks written earlier in this launch (oq) into the records (the
+// staging loop of mmvq_q4k_kernel, loads through L2): one lane per block.
+__device__ __forceinline__ void pk_stage_q8(const uint8_t *X, int K, uint8_t *arec) {
     const int nblk = K / QK8_1;
     for (int i = threadIdx.x; i < nblk; i += PK_NCW * 32) {
-        const uint64_t *src = X + static_cast<int64_t>(i) * PK_OQ_WORDS;
-        uint64_t w[PK_OQ_WORDS];
-        ll_fetch<PK_OQ_WORDS / 2, 2>(w, tag, (1u << (PK_OQ_WORDS / 2)) - 1u, [&](int k) { return src + 2 * k; });
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(X + static_cast<int64_t>(i) * Q81_BYTES);
         uint32_t q[9];
 #pragma unroll
-        for (int k = 0; k < 9; ++k) q[k] = ll_u(w[k]);
+        for (int k = 0; k < 9; ++k) q[k] = __ldcg(src + k);
         int msum = 0;
 #pragma unroll
         for (int k = 1; k < 9; ++k) msum = dp4a_ss(0x01010101, static_cast<int>(q[k]), msum);
@@ -706,19 +675,10 @@ __device__ __forceinline__ void pk_stage_q8(const uint64_t *X, uint32_t tag, int
 // ------------------------------------------------ consumer: attention ---
 // QK-RMSNorm + NEOX RoPE of one head (qk_norm_rope_kv_kernel's arithmetic):
 // lane owns elements 4 lane .. 4 lane + 3; nw and cs staged in shared memory.
-// Four tagged values of a q|k|v head (lane: 4 lane .. 4 lane + 3).
-__device__ __forceinline__ void pk_head_in(const uint64_t *x128, uint32_t tag, int lane, float (&x)[4]) {
-    const uint64_t *src = x128 + 4 * lane;
-    uint64_t w[4];
-    ll_fetch<2, 2>(w, tag, 3u, [&](int k) { return src + 2 * k; });
-#pragma unroll
-    for (int k = 0; k < 4; ++k) x[k] = ll_f(w[k]);
-}
-
-__device__ __forceinline__ void pk_norm_rope(const uint64_t *x128, uint32_t tag, const float *nw, const float *cs,
+__device__ __forceinline__ void pk_norm_rope(const float *x128, const float *nw, const float *cs,
                                              float eps, int lane, float (&o)[4]) {
-    float x[4];
-    pk_head_in(x128, tag, lane, x);
+    const float4 xv = __ldcg(reinterpret_cast<const float4 *>(x128 + 4 * lane));
+    const float x[4] = {xv.x, xv.y, xv.z, xv.w};
     float acc = 0.0f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) acc = __fmaf_rn(x[k], x[k], acc);
@@ -740,10 +700,11 @@ __device__ __forceinline__ void pk_norm_rope(const uint64_t *x128, uint32_t tag,
     }
 }
 
-// The merged output x of one q head (lane: dims 4 lane .. 4 lane + 3) as its
-// four Q8_1 blocks, tagged, into the layer's oq (attention_merge_quant_kernel's
+// The merged output x of one q head (lane: dims 4 lane .. 4 lane + 3) to
+// att and its four Q8_1 blocks to oq (attention_merge_quant_kernel's
 // epilogue).
-__device__ __forceinline__ void pk_head_out(uint64_t *oq, uint32_t tag, int hq, const float (&x)[4], int lane) {
+__device__ __forceinline__ void pk_head_out(const PkParams &P, int hq, const float (&x)[4], int lane) {
+    *reinterpret_cast<float4 *>(P.att + static_cast<int64_t>(hq) * 128 + 4 * lane) = make_float4(x[0], x[1], x[2], x[3]);
     float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
     amax = fmaxf(0.0f, amax);
 #pragma unroll
@@ -758,35 +719,30 @@ __device__ __forceinline__ void pk_head_out(uint64_t *oq, uint32_t tag, int hq, 
     }
 #pragma unroll
     for (int m = 4; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-    uint64_t *blk = oq + (static_cast<int64_t>(hq) * 4 + (lane >> 3)) * PK_OQ_WORDS;
-    ll_st(blk + 1 + (lane & 7),
-          (static_cast<uint32_t>(qv[0]) & 0xffu) | ((static_cast<uint32_t>(qv[1]) & 0xffu) << 8) |
-              ((static_cast<uint32_t>(qv[2]) & 0xffu) << 16) | ((static_cast<uint32_t>(qv[3]) & 0xffu) << 24),
-          tag);
+    uint32_t *o32 = reinterpret_cast<uint32_t *>(P.oq + (static_cast<int64_t>(hq) * 4 + (lane >> 3)) * Q81_BYTES);
+    o32[1 + (lane & 7)] = (static_cast<uint32_t>(qv[0]) & 0xffu) | ((static_cast<uint32_t>(qv[1]) & 0xffu) << 8) |
+                          ((static_cast<uint32_t>(qv[2]) & 0xffu) << 16) | ((static_cast<uint32_t>(qv[3]) & 0xffu) << 24);
     if ((lane & 7) == 0) {
         const uint32_t hd = __half_as_ushort(__float2half_rn(d));
         const uint32_t hs = __half_as_ushort(__float2half_rn(__fmul_rn(d, static_cast<float>(sum))));
-        ll_st(blk, hd | (hs << 16), tag);
-        ll_st(blk + PK_OQ_WORDS - 1, 0u, tag);  // the pad word: read (and waited for) with its pair
+        o32[0] = hd | (hs << 16);
     }
 }
 
 // Merge of one q head over nch chunks from the partials in global memory
-// (attention_merge_quant_kernel's arithmetic, read through L2); par: the
-// layer's parity, which picks the partial buffers.
-__device__ __forceinline__ void pk_merge_head(const PkParams &P, uint64_t *oq, uint32_t tag, int par, int hq,
-                                              int nch, int lane) {
+// (attention_merge_quant_kernel's arithmetic, read through L2).
+__device__ __forceinline__ void pk_merge_head(const PkParams &P, int hq, int nch, int lane) {
     const int mc = P.max_chunks;
-    const int64_t ph = static_cast<int64_t>(par) * P.n_heads + hq;
-    const float *pm = P.part_m + ph * mc;
-    const float *pl = P.part_l + ph * mc;
+    const float *pm = P.part_m + static_cast<int64_t>(hq) * mc;
+    const float *pl = P.part_l + static_cast<int64_t>(hq) * mc;
     float M = __ldcg(pm);
     for (int c = 1; c < nch; ++c) M = fmaxf(M, __ldcg(pm + c));
     float Ls = 0.0f, O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int c = 0; c < nch; ++c) {
         const float wc = abra_expf(__fsub_rn(__ldcg(pm + c), M));
         Ls = __fmaf_rn(__ldcg(pl + c), wc, Ls);
-        const float4 o = __ldcg(reinterpret_cast<const float4 *>(P.part_o + (ph * mc + c) * 128 + 4 * lane));
+        const float4 o = __ldcg(reinterpret_cast<const float4 *>(
+            P.part_o + (static_cast<int64_t>(hq) * mc + c) * 128 + 4 * lane));
         O[0] = __fmaf_rn(o.x, wc, O[0]);
         O[1] = __fmaf_rn(o.y, wc, O[1]);
         O[2] = __fmaf_rn(o.z, wc, O[2]);
@@ -795,7 +751,7 @@ __device__ __forceinline__ void pk_merge_head(const PkParams &P, uint64_t *oq, u
     float x[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) x[k] = __fdiv_rn(O[k], Ls);
-    pk_head_out(oq, tag, hq, x, lane);
+    pk_head_out(P, hq, x, lane);
 }
 
 // Shared-memory plan of the attention phase (floats): q[GQ][128],
@@ -842,11 +798,8 @@ __device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int p
 // current position's k and v rows are also kept in shared memory for the
 // item that reads them.  One chunk: the CTA merges its own heads; more: the
 // last chunk of each group to finish merges the group from the partials.
-// Each item waits for exactly its group's tagged q|k|v words; CTAs without
-// an item go straight on to the o GEMV.
 template <int GQ>
-__device__ __noinline__ void pk_attention(const PkParams &P, int layer, int pos, uint32_t tag, float *scr,
-                                          unsigned *s_flag) {
+__device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int pos, float *scr, unsigned *s_flag) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     float(*s_q)[128] = reinterpret_cast<float(*)[128]>(scr);                              // [GQ][128]
     float(*s_e)[ATT_CHUNK_P] = reinterpret_cast<float(*)[ATT_CHUNK_P]>(scr + GQ * 128);    // [GQ][256]
@@ -859,10 +812,6 @@ __device__ __noinline__ void pk_attention(const PkParams &P, int layer, int pos,
     const int nkv = P.n_kv, max_ctx = P.max_ctx, mc = P.max_chunks;
     const size_t kv_layer = static_cast<size_t>(nkv) * max_ctx * 128;
     __half *kc = P.kc + layer * kv_layer, *vc = P.vc + layer * kv_layer;
-    const int nqkv = (P.n_heads + 2 * nkv) * 128;
-    const uint64_t *qkv = P.t_qkv + static_cast<int64_t>(layer) * nqkv;
-    uint64_t *oq = P.t_oq + static_cast<int64_t>(layer) * P.n_heads * 4 * PK_OQ_WORDS;
-    const int par = layer & 1;
     const int items = nkv * nch;
     for (int it = blockIdx.x; it < items; it += gridDim.x) {
         PK_ASTAMP(layer, 0);
@@ -873,12 +822,11 @@ __device__ __noinline__ void pk_attention(const PkParams &P, int layer, int pos,
         for (int hv = warp; hv < GQ + (tail ? 2 : 0); hv += PK_NCW) {
             if (hv < GQ) {
                 float o[4];
-                pk_norm_rope(qkv + static_cast<int64_t>(g * GQ + hv) * 128, tag, s_in, s_in + 256, P.eps, lane, o);
+                pk_norm_rope(P.qkv + static_cast<int64_t>(g * GQ + hv) * 128, s_in, s_in + 256, P.eps, lane, o);
                 *reinterpret_cast<float4 *>(&s_q[hv][4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
             } else if (hv == GQ) {
                 float o[4];
-                pk_norm_rope(qkv + static_cast<int64_t>(P.n_heads + g) * 128, tag, s_in + 128, s_in + 256, P.eps, lane,
-                             o);
+                pk_norm_rope(P.qkv + static_cast<int64_t>(P.n_heads + g) * 128, s_in + 128, s_in + 256, P.eps, lane, o);
                 __half *dst = kc + (static_cast<int64_t>(g) * max_ctx + pos) * 128 + 4 * lane;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
@@ -886,8 +834,9 @@ __device__ __noinline__ void pk_attention(const PkParams &P, int layer, int pos,
                     s_knew[4 * lane + k] = __float2half_rn(o[k]);
                 }
             } else {
-                float xs[4];
-                pk_head_in(qkv + static_cast<int64_t>(P.n_heads + nkv + g) * 128, tag, lane, xs);
+                const float4 xv = __ldcg(reinterpret_cast<const float4 *>(
+                    P.qkv + static_cast<int64_t>(P.n_heads + nkv + g) * 128 + 4 * lane));
+                const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
                 __half *dst = vc + (static_cast<int64_t>(g) * max_ctx + pos) * 128 + 4 * lane;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
@@ -954,7 +903,7 @@ __device__ __noinline__ void pk_attention(const PkParams &P, int layer, int pos,
             mxs[h] = mx;
             ev[h] = valid ? abra_expf(__fsub_rn(s[h], mx)) : 0.0f;
             s_e[h][t] = ev[h];
-            if (t == 0 && nch > 1) P.part_m[(static_cast<int64_t>(par) * P.n_heads + g * GQ + h) * mc + c] = mx;
+            if (t == 0 && nch > 1) P.part_m[static_cast<int64_t>(g * GQ + h) * mc + c] = mx;
         }
         cta_sync();  // s_red is reused for the sums
         PK_ASTAMP(layer, 4);
@@ -1024,7 +973,7 @@ __device__ __noinline__ void pk_attention(const PkParams &P, int layer, int pos,
                     for (int w = 1; w < 8; ++w) o = __fadd_rn(o, s_o[(w * GQ + h) * 128 + d]);
                     x[k] = __fdiv_rn(__fmaf_rn(o, wc, 0.0f), Ls);
                 }
-                pk_head_out(oq, tag, g * GQ + h, x, lane);
+                pk_head_out(P, g * GQ + h, x, lane);
             }
             PK_ASTAMP(layer, 6);
             cta_sync();  // the scratch is reused by the next item
@@ -1036,27 +985,26 @@ __device__ __noinline__ void pk_attention(const PkParams &P, int layer, int pos,
             float o = s_o[h * 128 + d];
 #pragma unroll
             for (int w = 1; w < 8; ++w) o = __fadd_rn(o, s_o[(w * GQ + h) * 128 + d]);
-            P.part_o[((static_cast<int64_t>(par) * P.n_heads + g * GQ + h) * mc + c) * 128 + d] = o;
+            P.part_o[(static_cast<int64_t>(g * GQ + h) * mc + c) * 128 + d] = o;
         }
         if (t < GQ) {
             float l = s_red[t][0];
 #pragma unroll
             for (int w = 1; w < 8; ++w) l = __fadd_rn(l, s_red[t][w]);
-            P.part_l[(static_cast<int64_t>(par) * P.n_heads + g * GQ + t) * mc + c] = l;
+            P.part_l[static_cast<int64_t>(g * GQ + t) * mc + c] = l;
         }
         // the last chunk of the group to finish merges its heads
         cta_sync();
         if (t == 0) {
             __threadfence();
-            unsigned *cnt = P.head_cnt + layer * nkv + g;
-            const unsigned last = atomicAdd(cnt, 1u) + 1u == static_cast<unsigned>(nch) ? 1u : 0u;
-            if (last) *cnt = 0u;  // next used by the next launch
+            const unsigned last = atomicAdd(&P.head_cnt[g], 1u) + 1u == static_cast<unsigned>(nch) ? 1u : 0u;
+            if (last) P.head_cnt[g] = 0u;
             *s_flag = last;
         }
         cta_sync();
         if (*s_flag) {
             __threadfence();
-            if (warp < GQ) pk_merge_head(P, oq, tag, par, g * GQ + warp, nch, lane);
+            if (warp < GQ) pk_merge_head(P, g * GQ + warp, nch, lane);
         }
         cta_sync();  // the scratch is reused by the next item
     }
@@ -1064,7 +1012,7 @@ __device__ __noinline__ void pk_attention(const PkParams &P, int layer, int pos,
 
 // --------------------------------------------------------------- kernel ---
 template <int GQ>
-__global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const __grid_constant__ PkParams P) {
+__global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_nred[8];
     __shared__ unsigned long long s_amax;
@@ -1090,47 +1038,45 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const __gri
     const int t = threadIdx.x;
     float *vbuf = reinterpret_cast<float *>(smem + P.off_vbuf) + (t >> 5) * PK_VMAX;
     uint8_t *arec = smem + P.off_arec;
-    float *s_w = reinterpret_cast<float *>(smem + P.off_w);
-    float *s_x = reinterpret_cast<float *>(smem + P.off_x);  // the residual stream, all token long
-    float *scr = reinterpret_cast<float *>(smem + P.off_vbuf);  // attention: over vbuf, arec and s_w
+    float *scr = reinterpret_cast<float *>(smem + P.off_x);
     const int L = P.n_layers, hidden = P.hidden;
+    float *s_x = scr, *s_w = scr + hidden;
     const unsigned long long G = gridDim.x;
-    const unsigned long long gen = *reinterpret_cast<volatile unsigned long long *>(P.gen);
-    const uint32_t tag = static_cast<uint32_t>(gen) + 1u;  // never 0, the words' initial tag
-    const int nev = 5 * L + 1;  // phases of the token
-    const int64_t nqkv = static_cast<int64_t>(P.n_heads + 2 * P.n_kv) * 128;
-    const int64_t noq = static_cast<int64_t>(P.n_heads) * 4 * PK_OQ_WORDS;
-    const int att_items = P.n_kv * ((pos + ATT_CHUNK_P) / ATT_CHUNK_P);
+    const int nev = 5 * L + 1;  // phases of the token; a grid barrier between consecutive ones
+    unsigned long long kb = *reinterpret_cast<volatile unsigned long long *>(P.gen) * static_cast<unsigned long long>(nev);
     uint32_t T = 0;
     bool poisoned = false;
+    int cur = 0;
     const uint8_t *erow = P.embd + static_cast<int64_t>(__ldcg(P.tokens + pos)) * (hidden / QK_K) * Q4K_BYTES;
     for (int e = 0; e < nev; ++e) {
         const int l = e / 5;
         const int ph = e == nev - 1 ? PH_OUT : e % 5;
         const bool xin = ph == PH_QKV || ph == PH_GU || ph == PH_OUT;
         const bool first = xin && (ph == PH_QKV ? l == 0 : L == 0);  // the embedding row, no residual delta
-        // inputs that do not come from other CTAs: norm weights, the
-        // embedding row, the attention's norms and RoPE row
+        // inputs that do not depend on the previous phase, staged before its
+        // barrier: norm weights, the residual stream (written two or more
+        // phases back) or the embedding row, the attention's norms and RoPE row
         if (xin) {
             pk_stage_norm(ph == PH_OUT ? P.out_norm : ph == PH_QKV ? P.layers[l].attn_norm : P.layers[l].ffn_norm,
                           s_w, hidden);
-            if (first) pk_embed_stage(hidden, erow, s_x);
-        } else if (ph == PH_ATT && static_cast<int>(blockIdx.x) < att_items)
+            pk_xin_stage(hidden, P.h[cur], first ? erow : nullptr, s_x);
+        } else if (ph == PH_ATT)
             pk_stage_att(P, l, pos, GQ, scr);
         if (ph == PH_OUT && t == 0) s_amax = 0ull;
+        if (e > 0) {
+            ++kb;
+            if (t == 0) pk_wait(P.bar, kb * G);
+        }
         if (t == 0) PK_STAMP(0, e);
         cta_sync();
-        // the phase's activation, from the tagged words of earlier phases
+        // the phase's activation
         if (xin) {
-            // the o output of this layer (GU), the down output of the layer
-            // before (QKV, OUT)
-            const uint64_t *delta =
-                first ? nullptr : P.t_dlt + static_cast<int64_t>(ph == PH_GU ? 2 * l : 2 * l - 1) * hidden;
-            pk_xin(hidden, delta, tag, s_x, s_w, P.eps, arec, s_nred);
+            pk_xin(hidden, first ? nullptr : P.delta, P.h[cur ^ 1], s_x, s_w, P.eps, arec, s_nred);
+            cur ^= 1;
         } else if (ph == PH_O) {
-            pk_stage_q8(P.t_oq + l * noq, tag, P.n_heads * 128, arec);
+            pk_stage_q8(P.oq, P.n_heads * 128, arec);
         } else if (ph == PH_DOWN) {
-            pk_quant_act(P.t_act + static_cast<int64_t>(l) * P.ffn, tag, P.ffn, arec);
+            pk_quant_f32(P.act, P.ffn, arec);
         }
         if (t == 0) PK_STAMP(3, e);
 #ifdef ABRA_PK_TRACE
@@ -1139,14 +1085,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const __gri
 #endif
         // the phase's work
         if (ph == PH_ATT) {
-            pk_attention<GQ>(P, l, pos, tag, scr, &s_flag);
+            pk_attention<GQ>(P, l, pos, scr, &s_flag);
         } else {
             const int kind = ph == PH_QKV ? PK_QKV : ph == PH_O ? PK_O : ph == PH_GU ? PK_GU : ph == PH_DOWN ? PK_DOWN : PK_OUT;
-            uint64_t *Yt = ph == PH_QKV  ? P.t_qkv + l * nqkv
-                           : ph == PH_GU ? P.t_act + static_cast<int64_t>(l) * P.ffn
-                           : ph == PH_O  ? P.t_dlt + static_cast<int64_t>(2 * l) * hidden
-                           : ph == PH_DOWN ? P.t_dlt + static_cast<int64_t>(2 * l + 1) * hidden
-                                           : nullptr;
+            float *Y = ph == PH_QKV ? P.qkv : ph == PH_GU ? P.act : ph == PH_OUT ? P.logits : P.delta;
             const PkMm mm = pk_mm(P, l, kind);
             int u_begin, nu;
             pk_range(mm, u_begin, nu);
@@ -1156,25 +1098,24 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const __gri
 #endif
             unsigned long long *amax = ph == PH_OUT ? &s_amax : nullptr;
             if (mm.w1)
-                poisoned = pk_units<2>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, P.logits, Yt, tag,
-                                       amax, P.slot_shift, poisoned);
+                pk_units<2>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
             else
-                poisoned = pk_units<1>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, P.logits, Yt, tag,
-                                       amax, P.slot_shift, poisoned);
+                pk_units<1>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
             T += static_cast<uint32_t>(nu);
         }
-        cta_sync();  // shared memory is reused by the next phase
+        cta_sync();
         if (t == 0) PK_STAMP(1, e);
 #ifdef ABRA_PK_TRACE
         if (t == 0 && e < PK_TRACE_EV && blockIdx.x < 160) g_pk_trace[blockIdx.x][4][e] = g_pk_wait_ns;
 #endif
+        if (e < nev - 1 && t == 0) pk_arrive(P.bar);
     }
     // the greedy pick: the last CTA to arrive decodes the merged key
     if (t == 0) {
         atomicMax(P.amax, s_amax);
         __threadfence();
         const unsigned long long old = atom_add_acq_rel_gpu(P.bar, 1ull);
-        if (old + 1ull == (gen + 1ull) * G) {  // the last CTA of the launch
+        if (old + 1ull == (kb + 1ull) * G) {  // the last CTA of the launch
             __threadfence();
             const unsigned long long key = __ldcg(P.amax);
             *P.amax = 0ull;
@@ -1182,7 +1123,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const __gri
             P.picks[pos] = bi;
             if (pos + 1 >= __ldcg(P.nprompt)) P.tokens[pos + 1] = bi;
             *P.pos = pos + 1;
-            *P.gen = gen + 1ull;
+            *P.gen = *reinterpret_cast<volatile unsigned long long *>(P.gen) + 1ull;
             __threadfence();
         }
     }
@@ -1204,7 +1145,7 @@ PkKernel pk_kernel_for(int gq) {
 struct PkPlan {
     int rows[PK_KINDS], pitch[PK_KINDS];
     int slot_shift;
-    int off_vbuf, off_arec, off_w, off_x, off_ring, smem;
+    int off_vbuf, off_arec, off_x, off_ring, smem;
 };
 
 int pk_align(int v, int a) { return (v + a - 1) / a * a; }
@@ -1252,18 +1193,15 @@ bool pk_plan(int hidden, int n_heads, int n_kv, int ffn, int head_dim, int vocab
         }
         if (!pl.rows[k]) return no("a row does not fit a ring slot");
     }
-    // [mbarriers][vbuf][arec][norm weights] -- the attention's scratch over
-    // the same bytes -- [residual stream][ring]
     const int nsb_max = std::max(std::max(hidden, n_heads * 128), ffn) / QK_K;
+    const int scratch = std::max(8 * hidden, 4 * pk_att_floats(gq));
     int o = 16 * PK_NSLOT;  // full + empty mbarriers (room for 16 slots)
     pl.off_vbuf = pk_align(o, 16);
     o = pl.off_vbuf + PK_NCW * PK_VMAX * 4;
     pl.off_arec = pk_align(o, 128);
     o = pl.off_arec + nsb_max * PK_AREC;
-    pl.off_w = pk_align(o, 16);
-    o = std::max(pl.off_w + 4 * hidden, pl.off_vbuf + 4 * pk_att_floats(gq));
     pl.off_x = pk_align(o, 16);
-    o = pl.off_x + 4 * hidden;
+    o = pl.off_x + scratch;
     pl.off_ring = pk_align(o, 128);
     for (int shift : {4, 3}) {  // 16 slots, or 8 when the activations leave less room
         pl.slot_shift = shift;
@@ -1273,42 +1211,9 @@ bool pk_plan(int hidden, int n_heads, int n_kv, int ffn, int head_dim, int vocab
     return no("shared memory");
 }
 
-// Byte offsets of the tagged words and the attention partials in the
-// model's persistent-step scratch.
-struct PkScratch {
-    size_t qkv, oq, dlt, act, pm, pl, po, bytes;
-};
-
-PkScratch pk_scratch(int n_layers, int hidden, int n_heads, int n_kv, int ffn, int max_ctx) {
-    PkScratch sc;
-    const size_t L = static_cast<size_t>(n_layers);
-    const size_t mc = static_cast<size_t>((max_ctx + ATT_CHUNK_P - 1) / ATT_CHUNK_P);
-    size_t o = 0;
-    auto take = [&](size_t bytes) {
-        const size_t at = o;
-        o += (bytes + 255) / 256 * 256;
-        return at;
-    };
-    sc.qkv = take(L * (n_heads + 2 * n_kv) * 128 * 8);
-    sc.oq = take(L * n_heads * 4 * PK_OQ_WORDS * 8);
-    sc.dlt = take(L * 2 * hidden * 8);
-    sc.act = take(L * ffn * 8);
-    sc.pm = take(2 * n_heads * mc * 4);
-    sc.pl = take(2 * n_heads * mc * 4);
-    sc.po = take(2 * n_heads * mc * 128 * 4);
-    sc.bytes = o;
-    return sc;
-}
-
 }  // namespace
 
-size_t persist_sync_bytes(int n_layers, int n_kv) {
-    return static_cast<size_t>(pk_align(16 + 4 * std::max(n_layers, 1) * n_kv, 256));
-}
-
-size_t persist_scratch_bytes(int n_layers, int hidden, int n_heads, int n_kv, int ffn, int max_ctx) {
-    return pk_scratch(n_layers, hidden, n_heads, n_kv, ffn, max_ctx).bytes;
-}
+size_t persist_sync_bytes(int n_kv) { return static_cast<size_t>(pk_align(16 + 4 * n_kv, 256)); }
 
 bool persist_supported(int hidden, int n_heads, int n_kv, int ffn, int head_dim, const char **why) {
     PkPlan pl;
@@ -1349,16 +1254,17 @@ cudaError_t launch_persist_step(const PersistModel &pm, cudaStream_t st) {
     P.max_chunks = (pm.max_ctx + ATT_CHUNK_P - 1) / ATT_CHUNK_P;
     P.eps = pm.eps;
     P.scale = static_cast<float>(1.0 / std::sqrt(128.0));
-    const PkScratch sc = pk_scratch(pm.n_layers, pm.hidden, pm.n_heads, pm.n_kv, pm.ffn, pm.max_ctx);
-    uint8_t *scr = static_cast<uint8_t *>(pm.scratch);
-    P.t_qkv = reinterpret_cast<uint64_t *>(scr + sc.qkv);
-    P.t_oq = reinterpret_cast<uint64_t *>(scr + sc.oq);
-    P.t_dlt = reinterpret_cast<uint64_t *>(scr + sc.dlt);
-    P.t_act = reinterpret_cast<uint64_t *>(scr + sc.act);
-    P.part_m = reinterpret_cast<float *>(scr + sc.pm);
-    P.part_l = reinterpret_cast<float *>(scr + sc.pl);
-    P.part_o = reinterpret_cast<float *>(scr + sc.po);
+    P.h[0] = pm.h0;
+    P.h[1] = pm.h1;
+    P.delta = pm.delta;
+    P.qkv = pm.qkv;
+    P.att = pm.att;
+    P.part_m = pm.part_m;
+    P.part_l = pm.part_l;
+    P.part_o = pm.part_o;
+    P.act = pm.act;
     P.logits = pm.logits;
+    P.oq = pm.oq;
     P.kc = static_cast<__half *>(pm.kc);
     P.vc = static_cast<__half *>(pm.vc);
     P.rope = pm.rope;
@@ -1378,7 +1284,6 @@ cudaError_t launch_persist_step(const PersistModel &pm, cudaStream_t st) {
     P.slot_shift = pl.slot_shift;
     P.off_vbuf = pl.off_vbuf;
     P.off_arec = pl.off_arec;
-    P.off_w = pl.off_w;
     P.off_x = pl.off_x;
     P.off_ring = pl.off_ring;
     P.smem = pl.smem;

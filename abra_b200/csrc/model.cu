@@ -141,7 +141,6 @@ struct Model {
     bool persist_eager = false;  // the cooperative launch could not be captured
     PersistLayer *players = nullptr;
     void *psync = nullptr;
-    void *pscratch = nullptr;
 
     float *recv(int q, int slot) const {  // rank q's partial in slot, in peer[..]'s layout
         return reinterpret_cast<float *>(arena) + (static_cast<size_t>(slot) * sh.world + q) * cfg.hidden;
@@ -324,12 +323,9 @@ static cudaError_t build(Model &m) {
             TRY(cudaMemcpyAsync(m.players, pl.data(), pl.size() * sizeof(PersistLayer),
                                 cudaMemcpyHostToDevice, st));
         }
-        const size_t sb = persist_sync_bytes(c.n_layers, c.n_kv_heads);
+        const size_t sb = persist_sync_bytes(c.n_kv_heads);
         TRY(alloc(m, reinterpret_cast<uint8_t **>(&m.psync), sb));
         TRY(cudaMemsetAsync(m.psync, 0, sb, st));
-        const size_t sc = persist_scratch_bytes(c.n_layers, c.hidden, c.n_heads, c.n_kv_heads, c.ffn, c.max_ctx);
-        TRY(alloc(m, reinterpret_cast<uint8_t **>(&m.pscratch), sc));
-        TRY(cudaMemsetAsync(m.pscratch, 0, sc, st));
         m.persist = true;
     }
     if (sh.world > 1) {
@@ -656,8 +652,17 @@ static PersistModel persist_model(const Model &m) {
     pm.layers = m.players;
     pm.embd = m.embd;
     pm.out_norm = m.out_norm;
+    pm.h0 = m.h;
+    pm.h1 = m.h2;
+    pm.delta = m.delta;
+    pm.qkv = m.qkv;
+    pm.att = m.att;
+    pm.part_m = m.part_m;
+    pm.part_l = m.part_l;
+    pm.part_o = m.part_o;
+    pm.act = m.act;
     pm.logits = m.logits;
-    pm.scratch = m.pscratch;
+    pm.oq = m.oq;
     pm.kc = m.kc;
     pm.vc = m.vc;
     pm.rope = m.rope;
