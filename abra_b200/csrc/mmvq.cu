@@ -8,7 +8,12 @@
 
 namespace abra {
 
-// id = 1000*mode' + 10*ks + ctas_per_sm (mode' = 1 TMA rows, 2 TMA whole, 3 direct)
+// id = 1000*mode' + 100*h + 10*ks + ctas_per_sm (mode' = 1 TMA rows, 2 TMA
+// whole, 3 direct).  h = 1: the ring is sized so that the CTAs of a launch
+// fill only half of each SM (96 KiB of ring at one CTA per SM, 48 KiB at
+// two), leaving room for the next launch's CTAs: with programmatic dependent
+// launch they start at once and stream their weights (which do not depend on
+// the previous kernel) while this launch computes.
 static const MmvqConfig kCandidates[] = {
     // id, mode, ks, ctas_per_sm, stage_kb
     {1011, MODE_TMA_ROWS, 1, 1, 200},  {1012, MODE_TMA_ROWS, 1, 2, 100},
@@ -22,6 +27,9 @@ static const MmvqConfig kCandidates[] = {
     {3041, MODE_DIRECT, 4, 1, 0},      {3042, MODE_DIRECT, 4, 2, 0},
     {3044, MODE_DIRECT, 4, 4, 0},      {3081, MODE_DIRECT, 8, 1, 0},
     {3082, MODE_DIRECT, 8, 2, 0},      {3084, MODE_DIRECT, 8, 4, 0},
+    {1111, MODE_TMA_ROWS, 1, 1, 96},   {1121, MODE_TMA_ROWS, 2, 1, 96},
+    {1141, MODE_TMA_ROWS, 4, 1, 96},   {1112, MODE_TMA_ROWS, 1, 2, 48},
+    {2111, MODE_TMA_WHOLE, 1, 1, 96},  {2112, MODE_TMA_WHOLE, 1, 2, 48},
 };
 
 const MmvqConfig *mmvq_candidates(int *count) {

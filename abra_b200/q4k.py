@@ -91,7 +91,8 @@ def _enumerate() -> dict[int, Q4KCandidateSpec]:
         vals = [C.c_int32() for _ in range(6)]
         call("abra_candidate_info", i, *[C.byref(v) for v in vals])
         cid, mode, ks, ncw, cps, skb = (v.value for v in vals)
-        out[cid] = Q4KCandidateSpec(cid, f"Q4K_SM100_{MODE_NAMES[mode]}_KS{ks}_C{cps}", mode, ks,
+        half = "_H" if (cid // 100) % 10 == 1 else ""  # ring sized for half an SM
+        out[cid] = Q4KCandidateSpec(cid, f"Q4K_SM100_{MODE_NAMES[mode]}_KS{ks}_C{cps}{half}", mode, ks,
                                     ncw, cps, skb)
     return out
 
