@@ -12,8 +12,9 @@ namespace abra {
 // One tuning candidate of the Q4_K x Q8_1 MMVQ family.
 struct MmvqConfig {
     int id;           // stable candidate id (used in tuning tables)
-    int mode;         // MmvqMode: 0 TMA per-row copies, 1 TMA whole unit, 2 direct loads
-    int ks;           // k-parts per row group (1, 2, 4, 8): warps sharing a row group
+    int mode;         // MmvqMode: 0 TMA per-row copies, 1 TMA whole unit, 2 direct loads, 3 lane-mapped
+    int ks;           // k-parts per row group (1, 2, 4, 8): warps sharing a row group;
+                      // MODE_LANE: the largest rows per unit (8, 4, 2, 1)
     int ctas_per_sm;  // grid = min(row groups, SMs * ctas_per_sm)
     int stage_kb;     // shared-memory budget for the weight ring, KiB (TMA modes)
 };
@@ -76,6 +77,16 @@ struct MmvqXin {
 };
 // Batch-1 MMVQ whose activation is built in each CTA from the fp32 residual
 // stream (residual add + RMSNorm + Q8_1 fused into the prologue).
+// The lane-mapped batch-1 kernel (mmvq_lane.cu): plan out = {grid, block,
+// ring slots, slot bytes, shared memory, log2 rows per unit, activation and
+// ring offsets}; false when the shape does not fit the candidate.
+bool mmvq_lane_plan(const MmvqConfig &cfg, int64_t N, int nsb, int nmat, int sms, int64_t out[8]);
+cudaError_t launch_mmvq_lane(const MmvqConfig &cfg, const void *w, const void *w2, const void *x_q8, float *y,
+                             int64_t N, int64_t K, int flags, cudaStream_t stream, unsigned long long *amax);
+// The candidate a MODE_LANE candidate stands for where the lane kernel does
+// not apply (batch > 1, fused input, tensor-parallel options); others as given.
+const MmvqConfig &mmvq_classic(const MmvqConfig &cfg);
+
 cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void *w2,
                                 const MmvqXin &xin, float *y, int64_t N, int64_t K, int flags,
                                 cudaStream_t stream, unsigned long long *amax = nullptr,

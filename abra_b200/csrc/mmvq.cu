@@ -9,7 +9,7 @@
 namespace abra {
 
 // id = 1000*mode' + 100*h + 10*ks + ctas_per_sm (mode' = 1 TMA rows, 2 TMA
-// whole, 3 direct).  h = 1: the ring is sized so that the CTAs of a launch
+// whole, 3 direct, 4 lane-mapped with ks = its rows per unit).  h = 1: the ring is sized so that the CTAs of a launch
 // fill only half of each SM (96 KiB of ring at one CTA per SM, 48 KiB at
 // two), leaving room for the next launch's CTAs: with programmatic dependent
 // launch they start at once and stream their weights (which do not depend on
@@ -30,6 +30,11 @@ static const MmvqConfig kCandidates[] = {
     {1111, MODE_TMA_ROWS, 1, 1, 96},   {1121, MODE_TMA_ROWS, 2, 1, 96},
     {1141, MODE_TMA_ROWS, 4, 1, 96},   {1112, MODE_TMA_ROWS, 1, 2, 48},
     {2111, MODE_TMA_WHOLE, 1, 1, 96},  {2112, MODE_TMA_WHOLE, 1, 2, 48},
+    // lane-mapped batch-1 kernel (mmvq_lane.cu): ks = the largest rows per unit
+    {4081, MODE_LANE, 8, 1, 200},      {4082, MODE_LANE, 8, 2, 100},
+    {4041, MODE_LANE, 4, 1, 200},      {4042, MODE_LANE, 4, 2, 100},
+    {4021, MODE_LANE, 2, 1, 200},      {4022, MODE_LANE, 2, 2, 100},
+    {4011, MODE_LANE, 1, 1, 200},
 };
 
 const MmvqConfig *mmvq_candidates(int *count) {
@@ -42,6 +47,10 @@ const MmvqConfig *mmvq_candidate_by_id(int id) {
     for (int i = 0; i < n; ++i)
         if (c[i].id == id) return &c[i];
     return nullptr;
+}
+
+const MmvqConfig &mmvq_classic(const MmvqConfig &cfg) {
+    return cfg.mode == MODE_LANE ? *mmvq_candidate_by_id(1021) : cfg;
 }
 
 int device_sm_count() {
@@ -95,6 +104,11 @@ cudaError_t ensure_smem_attr_ptr(const void *fn) {
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kOptinSmem - static_cast<int>(fa.sharedSizeBytes));
     if (e != cudaSuccess) return e;
+    // the whole unified L1/shared array as shared memory: a CTA that needs
+    // less leaves room for the next launch's CTAs on the same SM (otherwise
+    // the SM may be configured with just enough for one)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
     if (ndone < 1024) {
         done[ndone] = fn;
         done_dev[ndone] = dev;
@@ -130,8 +144,9 @@ bool mmvq_shard_of(const MmvqOpts *tp, int nsb, int &sl_nsb, int &sl_base, int &
 }
 
 // sms: the SM count to plan for (0: this device's).
-static bool plan_mmvq(const MmvqConfig &cfg, int64_t N, int nsb, int ncols, int nmat,
+static bool plan_mmvq(const MmvqConfig &cfg_in, int64_t N, int nsb, int ncols, int nmat,
                       MmvqPlan &pl, bool xin = false, const MmvqOpts *tp = nullptr, int sms = 0) {
+    const MmvqConfig &cfg = mmvq_classic(cfg_in);
     const int ks = cfg.ks;
     const bool staged = cfg.mode != MODE_DIRECT;
     const int nsl = 8 / ks;
@@ -230,10 +245,13 @@ static cudaError_t launch_plan(MmvqFn fn, const MmvqPlan &pl, bool pdl, MmvqPara
     return cudaLaunchKernelEx(&cfg, fn, prm);
 }
 
-cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2,
+cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg_in, const void *w, const void *w2,
                             const void *x_q8, float *y, int64_t N, int64_t K, int ncols,
                             int64_t ldy, int flags, cudaStream_t stream,
                             unsigned long long *amax, const MmvqOpts *tp) {
+    if (cfg_in.mode == MODE_LANE && ncols == 1 && !tp)
+        return launch_mmvq_lane(cfg_in, w, w2, x_q8, y, N, K, flags, stream, amax);
+    const MmvqConfig &cfg = mmvq_classic(cfg_in);
     const int nsb = static_cast<int>(K / QK_K);
     const int nmat = w2 ? 2 : 1;
     const MmvqTable *t = table_for(ncols);
@@ -258,15 +276,29 @@ cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg, const void *w, const void *w2
 
 int mmvq_grid(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, bool xin,
               const MmvqOpts *tp) {
+    if (cfg.mode == MODE_LANE && ncols == 1 && !xin && !tp) {
+        int64_t lp[8];
+        return mmvq_lane_plan(cfg, N, static_cast<int>(K / QK_K), nmat, 0, lp) ? static_cast<int>(lp[0]) : -1;
+    }
     MmvqPlan pl;
     if (!plan_mmvq(cfg, N, static_cast<int>(K / QK_K), ncols, nmat, pl, xin, tp)) return -1;
     return pl.grid;
 }
 
-bool mmvq_plan_info(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int nmat, bool xin,
+bool mmvq_plan_info(const MmvqConfig &cfg_in, int64_t N, int64_t K, int ncols, int nmat, bool xin,
                     const MmvqOpts *tp, int sms, int64_t out[8]) {
     MmvqPlan pl;
     const int nsb = static_cast<int>(K / QK_K);
+    if (cfg_in.mode == MODE_LANE && ncols == 1 && !xin && !tp) {
+        // {grid, block, ring slots, row pitch, slot bytes, shared memory, units, ring offset}
+        int64_t lp[8];
+        if (!mmvq_lane_plan(cfg_in, N, nsb, nmat, sms, lp)) return false;
+        const int64_t R = int64_t(1) << lp[5];
+        const int64_t v[8] = {lp[0], lp[1], lp[2], int64_t(nsb) * Q4K_BYTES, lp[3], lp[4], (N + R - 1) / R, lp[7]};
+        for (int i = 0; i < 8; ++i) out[i] = v[i];
+        return true;
+    }
+    const MmvqConfig &cfg = mmvq_classic(cfg_in);
     if (!plan_mmvq(cfg, N, nsb, ncols, nmat, pl, xin, tp, sms)) return false;
     const bool staged = cfg.mode != MODE_DIRECT;
     const MmvqLayout L = mmvq_layout(ncols, cfg.ks, ABRA_MMVQ_NCW, nsb, pl.nstage, pl.pitch, nmat,
@@ -277,9 +309,10 @@ bool mmvq_plan_info(const MmvqConfig &cfg, int64_t N, int64_t K, int ncols, int 
     return true;
 }
 
-cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg, const void *w, const void *w2,
+cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg_in, const void *w, const void *w2,
                                 const MmvqXin &xin, float *y, int64_t N, int64_t K, int flags,
                                 cudaStream_t stream, unsigned long long *amax, const MmvqOpts *tp) {
+    const MmvqConfig &cfg = mmvq_classic(cfg_in);
     const int nsb = static_cast<int>(K / QK_K);
     const int nmat = w2 ? 2 : 1;
     const int ki = ks_index(cfg.ks);

@@ -67,7 +67,7 @@ def q8_1_nbytes(K: int, ncols: int = 1) -> int:
 
 
 # ----------------------------------------------------------- candidates ---
-MODE_NAMES = {0: "TMAROWS", 1: "TMAWHOLE", 2: "DIRECT"}
+MODE_NAMES = {0: "TMAROWS", 1: "TMAWHOLE", 2: "DIRECT", 3: "LANE"}
 
 
 @dataclass(frozen=True)

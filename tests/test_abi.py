@@ -39,7 +39,7 @@ def test_candidates_and_tuning_table():
     for cid in ids:
         s = A.get_candidate_spec(cid)
         assert s.ks in (1, 2, 4, 8) and s.ncw % s.ks == 0 and s.threads_per_block % 32 == 0
-        assert s.mode in (0, 1, 2) and (s.mode != 1 or s.ks == 1)
+        assert s.mode in (0, 1, 2, 3) and (s.mode != 1 or s.ks == 1)
     with pytest.raises(ValueError):
         A.get_candidate_spec(12345)
     A.register_autotuned_table_entry(777, 2560, 100, ids[0])

@@ -36,7 +36,7 @@ NCW = 8
 MAX_SMEM = 227 * 1024 - 1024
 TX_LIMIT = (1 << 20) - 1
 Q4K, Q6K = 144, 210
-MODE_NAMES = {0: "rows", 1: "whole", 2: "direct"}
+MODE_NAMES = {0: "rows", 1: "whole", 2: "direct", 3: "lane"}
 
 
 def slice_start(nsb: int, i: int) -> int:
@@ -103,11 +103,49 @@ def _part_bounds(nsb, ks, shard):
     return lo, hi
 
 
+def check_q4k_lane(pl, N, K, nmat):
+    """The lane-mapped kernel (mmvq_lane.cu): units of R consecutive rows,
+    one bulk copy per (unit, matrix) of nvalid whole rows into slot u % nslot
+    of the ring; lanes read whole superblocks of rows < R from the slot."""
+    nsb = K // 256
+    row_bytes = nsb * Q4K
+    G, total, nslot = pl["grid"], pl["rg_total"], pl["nstage"]
+    slot, off = pl["stage_bytes"], pl["off_stage"]
+    assert pl["pitch"] == row_bytes and slot % (nmat * row_bytes) == 0
+    R = slot // (nmat * row_bytes)
+    assert R in (1, 2, 4, 8) and R * nmat * nsb <= 80, "a unit does not fit the warp's staging buffer"
+    assert total == (N + R - 1) // R and G <= total and pl["block"] == (NCW + 1) * 32
+    assert pl["smem"] <= MAX_SMEM and off % 128 == 0 and off + nslot * slot <= pl["smem"]
+    b = np.arange(G, dtype=np.int64)
+    ub, ue = b * total // G, (b + 1) * total // G
+    nu = ue - ub
+    assert nu.min() >= 1 and nu.sum() == total
+    assert np.all((nslot >= nu) | (nslot % NCW == 0)), "ring depth breaks the parity rule"
+    cta = np.repeat(b, nu)
+    u = np.arange(total, dtype=np.int64) - np.repeat(np.cumsum(nu) - nu, nu)
+    row0 = (ub[cta] + u) * R
+    nvalid = np.minimum(R, N - row0)
+    assert nvalid.min() >= 1
+    s = u % nslot
+    src, nbytes = row0 * row_bytes, nvalid * row_bytes
+    for m in range(nmat):
+        dst = off + s * slot + m * R * row_bytes
+        assert np.all(src % 16 == 0) and np.all(nbytes % 16 == 0) and np.all(dst % 16 == 0)
+        assert (src + nbytes).max() <= N * row_bytes
+        assert np.all(dst + nbytes <= off + (s + 1) * slot)
+    assert (nmat * nbytes).max() <= TX_LIMIT
+    return True
+
+
 def check_q4k(cand, mode, ks, cps, N, K, ncols, nmat=1, xin=0, shard=None):
     kf, sb, sc = (shard[0] * 256, shard[1], shard[2]) if shard else (0, 0, 8)
     pl = plan(12, cand, N, K, ncols, nmat, xin, kf, sb, sc)
     if pl is None:
         return False
+    if mode == 3:
+        if ncols == 1 and not xin and not shard:
+            return check_q4k_lane(pl, N, K, nmat)
+        mode, ks, cps = 0, 2, 1  # elsewhere the candidate runs the TMA-rows KS=2 plan
     nsb = K // 256
     staged = mode != 2
     assert pl["block"] == (NCW + staged) * 32
