@@ -49,8 +49,12 @@ const MmvqConfig *mmvq_candidate_by_id(int id) {
     return nullptr;
 }
 
+// Lane candidates of four or eight rows per unit win on the wide shapes,
+// where whole-unit copies do best among the template's plans; those of one
+// or two rows on the narrow ones, where KS=2 row copies do.
 const MmvqConfig &mmvq_classic(const MmvqConfig &cfg) {
-    return cfg.mode == MODE_LANE ? *mmvq_candidate_by_id(1021) : cfg;
+    if (cfg.mode != MODE_LANE) return cfg;
+    return *mmvq_candidate_by_id(cfg.ks >= 4 ? (cfg.ctas_per_sm >= 2 ? 2012 : 2011) : 1021);
 }
 
 int device_sm_count() {

@@ -38,7 +38,7 @@ namespace abra {
 
 // MODE_LANE (3) is the lane-mapped batch-1 kernel of mmvq_lane.cu, not this
 // template; at other batch widths, and with a fused input or tensor-parallel
-// options, its candidates run the MODE_TMA_ROWS KS=2 plan.
+// options, its candidates run a plan of this template (mmvq_classic).
 enum MmvqMode : int { MODE_TMA_ROWS = 0, MODE_TMA_WHOLE = 1, MODE_DIRECT = 2, MODE_LANE = 3 };
 
 struct MmvqParams {

@@ -145,7 +145,8 @@ def check_q4k(cand, mode, ks, cps, N, K, ncols, nmat=1, xin=0, shard=None):
     if mode == 3:
         if ncols == 1 and not xin and not shard:
             return check_q4k_lane(pl, N, K, nmat)
-        mode, ks, cps = 0, 2, 1  # elsewhere the candidate runs the TMA-rows KS=2 plan
+        # elsewhere the candidate runs a template plan (mmvq_classic)
+        mode, ks, cps = (1, 1, min(cps, 2)) if ks >= 4 else (0, 2, 1)
     nsb = K // 256
     staged = mode != 2
     assert pl["block"] == (NCW + staged) * 32
