@@ -81,6 +81,7 @@ struct MmvqXin {
 // ring slots, slot bytes, shared memory, log2 rows per unit, activation and
 // ring offsets}; false when the shape does not fit the candidate.
 bool mmvq_lane_plan(const MmvqConfig &cfg, int64_t N, int nsb, int nmat, int sms, int64_t out[8]);
+cudaError_t prepare_mmvq_lane(const MmvqConfig &cfg, int nmat);  // kernel attributes, outside a capture
 cudaError_t launch_mmvq_lane(const MmvqConfig &cfg, const void *w, const void *w2, const void *x_q8, float *y,
                              int64_t N, int64_t K, int flags, cudaStream_t stream, unsigned long long *amax);
 // The candidate a MODE_LANE candidate stands for where the lane kernel does

@@ -260,7 +260,7 @@ cudaError_t launch_mmvq_q4k(const MmvqConfig &cfg_in, const void *w, const void 
     const int nmat = w2 ? 2 : 1;
     const MmvqTable *t = table_for(ncols);
     const int ki = ks_index(cfg.ks);
-    if (!t || ki < 0) return cudaErrorInvalidValue;
+    if (!t || ki < 0 || cfg.mode < 0 || cfg.mode > MODE_DIRECT) return cudaErrorInvalidValue;
     MmvqFn fn = t->fn[cfg.mode][ki][nmat - 1];
     if (!fn) return cudaErrorInvalidValue;
     MmvqPlan pl;
@@ -320,7 +320,7 @@ cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg_in, const void *w, const v
     const int nsb = static_cast<int>(K / QK_K);
     const int nmat = w2 ? 2 : 1;
     const int ki = ks_index(cfg.ks);
-    if (ki < 0) return cudaErrorInvalidValue;
+    if (ki < 0 || cfg.mode < 0 || cfg.mode > MODE_DIRECT) return cudaErrorInvalidValue;
     MmvqFn fn = mmvq_table_c1().xin[cfg.mode][ki][nmat - 1];
     if (!fn || !xin.h_in || !xin.norm_w) return cudaErrorInvalidValue;
     if (reinterpret_cast<uintptr_t>(xin.norm_w) & 15) return cudaErrorInvalidValue;  // float4 loads
@@ -346,6 +346,14 @@ cudaError_t launch_mmvq_q4k_xin(const MmvqConfig &cfg_in, const void *w, const v
 }
 
 cudaError_t prepare_mmvq(const MmvqConfig &cfg, int ncols, int nmat, bool xin) {
+    if (cfg.mode == MODE_LANE) {
+        if (ncols == 1 && !xin) {
+            cudaError_t e = prepare_mmvq_lane(cfg, nmat);
+            if (e != cudaSuccess) return e;
+        }
+        return prepare_mmvq(mmvq_classic(cfg), ncols, nmat, xin);  // the plan it stands for elsewhere
+    }
+    if (cfg.mode < 0 || cfg.mode > MODE_DIRECT) return cudaErrorInvalidValue;
     const MmvqTable *t = table_for(ncols);
     const int ki = ks_index(cfg.ks);
     if (!t || ki < 0 || nmat < 1 || nmat > 2) return cudaErrorInvalidValue;

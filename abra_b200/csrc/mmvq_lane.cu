@@ -214,6 +214,11 @@ bool mmvq_lane_plan(const MmvqConfig &cfg, int64_t N, int nsb, int nmat, int sms
     return true;
 }
 
+cudaError_t prepare_mmvq_lane(const MmvqConfig &cfg, int nmat) {
+    if (cfg.mode != MODE_LANE || (nmat != 1 && nmat != 2)) return cudaErrorInvalidValue;
+    return ensure_smem_attr_ptr(reinterpret_cast<const void *>(lane_kernel(nmat, cfg.ctas_per_sm >= 2 ? 2 : 1)));
+}
+
 cudaError_t launch_mmvq_lane(const MmvqConfig &cfg, const void *w, const void *w2, const void *x_q8, float *y,
                              int64_t N, int64_t K, int flags, cudaStream_t stream, unsigned long long *amax) {
     const int nsb = static_cast<int>(K / QK_K), nmat = w2 ? 2 : 1;
