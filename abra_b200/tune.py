@@ -253,17 +253,18 @@ def tune(shapes, ncols_list, out: Path, quick: bool = False, ids=None, merge: bo
                   flush=True)
         del bufs
         torch.cuda.empty_cache()
-    if merge and out.exists():
-        old = json.loads(out.read_text())
+    old = json.loads(out.read_text()) if merge and out.exists() else {}
+    if old:
         keys = {(e["N"], e["K"], e["ncols"], e["nmat"]) for e in entries}
         entries = [e for e in old.get("entries", [])
                    if (e["N"], e["K"], e["ncols"], e["nmat"]) not in keys] + entries
         failures = old.get("failures", []) + failures
-    data = {"arch": 100, "device": torch.cuda.get_device_name(0),
-            "when": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime()),
-            "method": "CUDA graph of back-to-back launches over >= 4 x L2 of weight copies, "
-                      "PDL on, best of 3 replays; ties within 0.5% to the lower id",
-            "entries": entries, "failures": failures}
+    data = dict(old)  # other sections (decode_in_situ, q6k_entries) are kept
+    data.update({"arch": 100, "device": torch.cuda.get_device_name(0),
+                 "when": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime()),
+                 "method": "CUDA graph of back-to-back launches over >= 4 x L2 of weight copies, "
+                           "PDL on, best of 3 replays; ties within 0.5% to the lower id",
+                 "entries": entries, "failures": failures})
     out.parent.mkdir(parents=True, exist_ok=True)
     out.write_text(json.dumps(data, indent=1) + "\n")
     return data
