@@ -80,7 +80,7 @@ struct PersistModel {
     unsigned long long *amax;
     void *sync;  // persist_sync_bytes() zeroed bytes: barrier and arrival counters
 };
-size_t persist_sync_bytes(int n_kv);
+size_t persist_sync_bytes(int n_heads);
 // False (with a reason) when the shape does not fit the kernel's ring and
 // shared-memory plan; the model then runs the kernel chain.
 bool persist_supported(int hidden, int n_heads, int n_kv, int ffn, int head_dim, const char **why);

@@ -16,11 +16,13 @@
 //   QKV   residual add + RMSNorm + Q8_1 in every CTA's shared memory (layer 0:
 //         the token's embedding row dequantized in place), then the fused
 //         q|k|v MMVQ -> qkv
-//   ATT   per (kv head g, 256-position chunk c): QK-RMSNorm + NEOX RoPE of the
-//         group's q heads; on the chunk holding the current position also the
-//         k/v heads, appended to the fp16 cache; the chunk's softmax partials;
-//         one chunk: the CTA merges its heads itself; more: the last chunk of
-//         each group to finish (arrival counter) merges the group -> oq (Q8_1)
+//   ATT   per (q heads, 256-position chunk c) item -- a kv group's heads, or
+//         one q head while the context is short: QK-RMSNorm + NEOX RoPE of
+//         the item's q heads; on the chunk holding the current position also
+//         the group's k/v heads (appended to the fp16 cache by the group's
+//         first item); the chunk's softmax partials; one chunk: the CTA merges
+//         its heads itself; more: the last chunk of the item's heads to
+//         finish (arrival counter) merges them -> oq (Q8_1)
 //   O     MMVQ of oq -> delta
 //   GU    residual add + RMSNorm + Q8_1, fused gate/up SwiGLU MMVQ -> act
 //   DOWN  Q8_1 of act in every CTA's shared memory, MMVQ -> delta
@@ -105,7 +107,7 @@ struct PkParams {
     const int32_t *nprompt;
     unsigned long long *amax;
     unsigned long long *bar, *gen;  // grid barrier arrivals, launches completed
-    unsigned *head_cnt;             // merge arrivals per kv head
+    unsigned *head_cnt;             // merge arrivals per attention item's first q head
     int lr[PK_KINDS], pitch[PK_KINDS];  // log2 rows per unit and staged row pitch per GEMV kind
     int slot_shift;                     // log2 of the ring slots (4: 16 slots, 3: 8)
     int off_vbuf, off_arec, off_x, off_ring, smem;  // dynamic shared memory layout
@@ -672,18 +674,27 @@ __device__ __forceinline__ void pk_merge_head(const PkParams &P, int hq, int nch
     pk_head_out(P, hq, x, lane);
 }
 
-// Shared-memory plan of the attention phase (floats): q[GQ][128],
-// e[GQ][256], red[GQ][8], o[8][GQ][128], then the staged q/k norm weights
-// and RoPE row (3 x 128), then the new k and v rows (fp16, 2 x 128 = 128
-// floats).
-__host__ __device__ constexpr int pk_att_floats(int gq) {
-    return gq * (128 + ATT_CHUNK_P + 8) + 8 * gq * 128 + 3 * 128 + 128;
+// Shared-memory plan of the attention phase for items of hpi q heads
+// (floats): q[hpi][128], e[hpi][256], red[hpi][8], o[8][hpi][128], then the
+// staged q/k norm weights and RoPE row (3 x 128), then the new k and v rows
+// (fp16, 2 x 128 = 128 floats).
+__host__ __device__ constexpr int pk_att_floats(int hpi) {
+    return hpi * (128 + ATT_CHUNK_P + 8) + 8 * hpi * 128 + 3 * 128 + 128;
+}
+
+// Attention items of a token at position pos: (q heads per item, items).
+// Whole kv groups per item (hpi = gq) read each K/V row once per group; one
+// q head per item (hpi = 1) spreads a short context over 4x the CTAs and is
+// used while all its items fit one round of the grid.
+__device__ __forceinline__ int pk_att_hpi(const PkParams &P, int pos, int gq) {
+    const int nch = (pos + ATT_CHUNK_P) / ATT_CHUNK_P;
+    return P.n_heads * nch <= static_cast<int>(gridDim.x) ? 1 : gq;
 }
 
 // Inputs of the attention phase that do not depend on the previous phase,
 // staged before its barrier.
-__device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int pos, int gq, float *scr) {
-    float *s_in = scr + gq * (128 + ATT_CHUNK_P + 8) + 8 * gq * 128;
+__device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int pos, int gq, int hpi, float *scr) {
+    float *s_in = scr + hpi * (128 + ATT_CHUNK_P + 8) + 8 * hpi * 128;
     const PersistLayer &Ly = P.layers[layer];
     const int t = threadIdx.x;
     if (t < 128) {
@@ -697,8 +708,9 @@ __device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int p
     if (t < 32) {
         const int L = pos, nch = (pos + ATT_CHUNK_P) / ATT_CHUNK_P;
         const size_t kv_layer = static_cast<size_t>(P.n_kv) * P.max_ctx * 128;
-        for (int it = blockIdx.x; it < P.n_kv * nch; it += gridDim.x) {
-            const int g = it % P.n_kv, c = it / P.n_kv;
+        const int nu = P.n_heads / hpi;
+        for (int it = blockIdx.x; it < nu * nch; it += gridDim.x) {
+            const int g = (it % nu) * hpi / gq, c = it / nu;
             const int j0 = c * ATT_CHUNK_P, nrow = min(ATT_CHUNK_P, L - j0);
             if (nrow <= 0) continue;
             const int64_t off = layer * kv_layer + (static_cast<int64_t>(g) * P.max_ctx + j0) * 128;
@@ -710,14 +722,18 @@ __device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int p
     }
 }
 
-// Attention of layer `layer` at position pos: items (kv head g, chunk c)
-// over the CTAs; each item is attention_chunk_kernel<GQ>'s arithmetic on
-// 256 positions, the group's q heads normed and rotated in place.  The
-// current position's k and v rows are also kept in shared memory for the
-// item that reads them.  One chunk: the CTA merges its own heads; more: the
-// last chunk of each group to finish merges the group from the partials.
-template <int GQ>
-__device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int pos, float *scr, unsigned *s_flag) {
+// Attention of layer `layer` at position pos: items (HPI consecutive q heads
+// of kv group g, chunk c) over the CTAs; each item is attention_chunk_kernel's
+// arithmetic on 256 positions for its heads (every head's operations in the
+// same order whatever HPI is), its q heads normed and rotated in place.  On
+// the chunk holding pos the item also forms the group's new k and v rows and
+// keeps them in shared memory; the group's first item appends them to the
+// cache.  One chunk: the CTA merges its own heads; more: the last chunk of
+// each item's heads to finish merges them from the partials.
+template <int HPI>
+__device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int pos, int gq, float *scr,
+                                             unsigned *s_flag) {
+    constexpr int GQ = HPI;  // q heads of this item
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     float(*s_q)[128] = reinterpret_cast<float(*)[128]>(scr);                              // [GQ][128]
     float(*s_e)[ATT_CHUNK_P] = reinterpret_cast<float(*)[ATT_CHUNK_P]>(scr + GQ * 128);    // [GQ][256]
@@ -730,17 +746,18 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
     const int nkv = P.n_kv, max_ctx = P.max_ctx, mc = P.max_chunks;
     const size_t kv_layer = static_cast<size_t>(nkv) * max_ctx * 128;
     __half *kc = P.kc + layer * kv_layer, *vc = P.vc + layer * kv_layer;
-    const int items = nkv * nch;
+    const int nu = P.n_heads / HPI, items = nu * nch;
     for (int it = blockIdx.x; it < items; it += gridDim.x) {
         PK_ASTAMP(layer, 0);
-        const int g = it % nkv, c = it / nkv;
-        const bool tail = c == nch - 1;
+        const int u = it % nu, c = it / nu;
+        const int h0 = u * HPI, g = h0 / gq;  // first q head, kv group
+        const bool tail = c == nch - 1, first = h0 % gq == 0;
         // the group's q heads; on the chunk holding pos also the k and v
         // heads, appended to the cache (rounded to fp16) and kept here
         for (int hv = warp; hv < GQ + (tail ? 2 : 0); hv += PK_NCW) {
             if (hv < GQ) {
                 float o[4];
-                pk_norm_rope(P.qkv + static_cast<int64_t>(g * GQ + hv) * 128, s_in, s_in + 256, P.eps, lane, o);
+                pk_norm_rope(P.qkv + static_cast<int64_t>(h0 + hv) * 128, s_in, s_in + 256, P.eps, lane, o);
                 *reinterpret_cast<float4 *>(&s_q[hv][4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
             } else if (hv == GQ) {
                 float o[4];
@@ -748,7 +765,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
                 __half *dst = kc + (static_cast<int64_t>(g) * max_ctx + pos) * 128 + 4 * lane;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    dst[k] = __float2half_rn(o[k]);
+                    if (first) dst[k] = __float2half_rn(o[k]);
                     s_knew[4 * lane + k] = __float2half_rn(o[k]);
                 }
             } else {
@@ -758,7 +775,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
                 __half *dst = vc + (static_cast<int64_t>(g) * max_ctx + pos) * 128 + 4 * lane;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    dst[k] = __float2half_rn(xs[k]);
+                    if (first) dst[k] = __float2half_rn(xs[k]);
                     s_vnew[4 * lane + k] = __float2half_rn(xs[k]);
                 }
             }
@@ -821,7 +838,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
             mxs[h] = mx;
             ev[h] = valid ? abra_expf(__fsub_rn(s[h], mx)) : 0.0f;
             s_e[h][t] = ev[h];
-            if (t == 0 && nch > 1) P.part_m[static_cast<int64_t>(g * GQ + h) * mc + c] = mx;
+            if (t == 0 && nch > 1) P.part_m[static_cast<int64_t>(h0 + h) * mc + c] = mx;
         }
         cta_sync();  // s_red is reused for the sums
         PK_ASTAMP(layer, 4);
@@ -891,7 +908,7 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
                     for (int w = 1; w < 8; ++w) o = __fadd_rn(o, s_o[(w * GQ + h) * 128 + d]);
                     x[k] = __fdiv_rn(__fmaf_rn(o, wc, 0.0f), Ls);
                 }
-                pk_head_out(P, g * GQ + h, x, lane);
+                pk_head_out(P, h0 + h, x, lane);
             }
             PK_ASTAMP(layer, 6);
             cta_sync();  // the scratch is reused by the next item
@@ -903,26 +920,26 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
             float o = s_o[h * 128 + d];
 #pragma unroll
             for (int w = 1; w < 8; ++w) o = __fadd_rn(o, s_o[(w * GQ + h) * 128 + d]);
-            P.part_o[(static_cast<int64_t>(g * GQ + h) * mc + c) * 128 + d] = o;
+            P.part_o[(static_cast<int64_t>(h0 + h) * mc + c) * 128 + d] = o;
         }
         if (t < GQ) {
             float l = s_red[t][0];
 #pragma unroll
             for (int w = 1; w < 8; ++w) l = __fadd_rn(l, s_red[t][w]);
-            P.part_l[static_cast<int64_t>(g * GQ + t) * mc + c] = l;
+            P.part_l[static_cast<int64_t>(h0 + t) * mc + c] = l;
         }
-        // the last chunk of the group to finish merges its heads
+        // the last chunk of the item's heads to finish merges them
         cta_sync();
         if (t == 0) {
             __threadfence();
-            const unsigned last = atomicAdd(&P.head_cnt[g], 1u) + 1u == static_cast<unsigned>(nch) ? 1u : 0u;
-            if (last) P.head_cnt[g] = 0u;
+            const unsigned last = atomicAdd(&P.head_cnt[h0], 1u) + 1u == static_cast<unsigned>(nch) ? 1u : 0u;
+            if (last) P.head_cnt[h0] = 0u;
             *s_flag = last;
         }
         cta_sync();
         if (*s_flag) {
             __threadfence();
-            if (warp < GQ) pk_merge_head(P, g * GQ + warp, nch, lane);
+            if (warp < GQ) pk_merge_head(P, h0 + warp, nch, lane);
         }
         cta_sync();  // the scratch is reused by the next item
     }
@@ -979,7 +996,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
                           s_w, hidden);
             pk_xin_stage(hidden, P.h[cur], first ? erow : nullptr, s_x);
         } else if (ph == PH_ATT)
-            pk_stage_att(P, l, pos, GQ, scr);
+            pk_stage_att(P, l, pos, GQ, pk_att_hpi(P, pos, GQ), scr);
         if (ph == PH_OUT && t == 0) s_amax = 0ull;
         if (e > 0) {
             ++kb;
@@ -1003,7 +1020,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
 #endif
         // the phase's work
         if (ph == PH_ATT) {
-            pk_attention<GQ>(P, l, pos, scr, &s_flag);
+            if (GQ > 1 && pk_att_hpi(P, pos, GQ) == 1)
+                pk_attention<1>(P, l, pos, GQ, scr, &s_flag);
+            else
+                pk_attention<GQ>(P, l, pos, GQ, scr, &s_flag);
         } else {
             const int kind = ph == PH_QKV ? PK_QKV : ph == PH_O ? PK_O : ph == PH_GU ? PK_GU : ph == PH_DOWN ? PK_DOWN : PK_OUT;
             float *Y = ph == PH_QKV ? P.qkv : ph == PH_GU ? P.act : ph == PH_OUT ? P.logits : P.delta;
@@ -1131,7 +1151,7 @@ bool pk_plan(int hidden, int n_heads, int n_kv, int ffn, int head_dim, int vocab
 
 }  // namespace
 
-size_t persist_sync_bytes(int n_kv) { return static_cast<size_t>(pk_align(16 + 4 * n_kv, 256)); }
+size_t persist_sync_bytes(int n_heads) { return static_cast<size_t>(pk_align(16 + 4 * n_heads, 256)); }
 
 bool persist_supported(int hidden, int n_heads, int n_kv, int ffn, int head_dim, const char **why) {
     PkPlan pl;

@@ -323,7 +323,7 @@ static cudaError_t build(Model &m) {
             TRY(cudaMemcpyAsync(m.players, pl.data(), pl.size() * sizeof(PersistLayer),
                                 cudaMemcpyHostToDevice, st));
         }
-        const size_t sb = persist_sync_bytes(c.n_kv_heads);
+        const size_t sb = persist_sync_bytes(c.n_heads);
         TRY(alloc(m, reinterpret_cast<uint8_t **>(&m.psync), sb));
         TRY(cudaMemsetAsync(m.psync, 0, sb, st));
         m.persist = true;
