@@ -109,7 +109,6 @@ struct PkParams {
     unsigned long long *bar, *gen;  // grid barrier arrivals, launches completed
     unsigned *head_cnt;             // merge arrivals per attention item's first q head
     int lr[PK_KINDS], pitch[PK_KINDS];  // log2 rows per unit and staged row pitch per GEMV kind
-    int nbig[PK_KINDS];                 // units of 1 << lr rows per GEMV kind (then one-row units)
     int slot_shift;                     // log2 of the ring slots (4: 16 slots, 3: 8)
     int off_vbuf, off_arec, off_x, off_ring, smem;  // dynamic shared memory layout
 };
@@ -192,7 +191,6 @@ __device__ __forceinline__ void pk_wait(const unsigned long long *bar, unsigned 
 struct PkMm {
     const uint8_t *w0, *w1;
     int N, nsb, lr, pitch;
-    int nbig;  // units of 1 << lr rows; the rows after them are one-row units
 };
 
 // GEMV kind of producer phase ph (per layer q|k|v, o, gate/up, down; then
@@ -205,7 +203,6 @@ __device__ __forceinline__ PkMm pk_mm(const PkParams &P, int layer, int kind) {
     mm.w1 = nullptr;
     mm.lr = P.lr[kind];
     mm.pitch = P.pitch[kind];
-    mm.nbig = P.nbig[kind];
     const int nsb_h = P.hidden / QK_K;
     if (kind == PK_OUT) {
         mm.w0 = P.embd;
@@ -235,38 +232,11 @@ __device__ __forceinline__ PkMm pk_mm(const PkParams &P, int layer, int kind) {
     return mm;
 }
 
-// This CTA's share of a GEMV: nb units of R = 1 << lr rows from unit ub,
-// then nt one-row units from tail row ut.  The R-row units are a multiple
-// of the grid's consumer warps (or all of the matrix), so every warp gets
-// the same number of them; the rows left over are spread one by one, so no
-// warp carries a whole extra R-row unit.
-struct PkShare {
-    int ub, nb, ut, nt;
-};
-
-__device__ __forceinline__ PkShare pk_share(const PkMm &mm) {
-    const int64_t G = gridDim.x, b = blockIdx.x;
-    const int ntail = max(0, mm.N - (mm.nbig << mm.lr));
-    PkShare sh;
-    sh.ub = static_cast<int>(b * mm.nbig / G);
-    sh.nb = static_cast<int>((b + 1) * mm.nbig / G) - sh.ub;
-    sh.ut = static_cast<int>(b * ntail / G);
-    sh.nt = static_cast<int>((b + 1) * ntail / G) - sh.ut;
-    return sh;
-}
-
-// Unit k of the share: its first row, its rows, log2 of its row capacity.
-__device__ __forceinline__ void pk_unit(const PkMm &mm, const PkShare &sh, int k, int &row0, int &nrows,
-                                        int &lr) {
-    if (k < sh.nb) {
-        lr = mm.lr;
-        row0 = (sh.ub + k) << lr;
-        nrows = min(1 << lr, mm.N - row0);
-    } else {
-        lr = 0;
-        row0 = (mm.nbig << mm.lr) + sh.ut + (k - sh.nb);
-        nrows = 1;
-    }
+// This CTA's contiguous share [u_begin, u_begin + nu) of the GEMV's units.
+__device__ __forceinline__ void pk_range(const PkMm &mm, int &u_begin, int &nu) {
+    const int total = (mm.N + (1 << mm.lr) - 1) >> mm.lr;
+    u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * total / gridDim.x);
+    nu = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x) - u_begin;
 }
 
 // ----------------------------------------------------------- producer ---
@@ -280,10 +250,11 @@ __device__ __forceinline__ void pk_producer(const PkParams &P, uint8_t *ring, ui
     const uint32_t nslot = 1u << sh, smask = nslot - 1u;
     for (int ph = 0; ph < nph && ok; ++ph) {
         const PkMm mm = pk_mm(P, ph >> 2, pk_kind(ph, nph));
-        const int nmat = mm.w1 ? 2 : 1;
+        const int nmat = mm.w1 ? 2 : 1, R = 1 << mm.lr;
         const uint32_t row_bytes = static_cast<uint32_t>(mm.nsb) * Q4K_BYTES;
-        const PkShare shr = pk_share(mm);
-        for (int u = 0; u < shr.nb + shr.nt; ++u, ++t) {
+        int u_begin, nu;
+        pk_range(mm, u_begin, nu);
+        for (int u = 0; u < nu; ++u, ++t) {
             const int s = static_cast<int>(t & smask);
             const uint32_t k = t >> sh;
             if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1, ERR_WAIT_EMPTY)) {
@@ -291,13 +262,12 @@ __device__ __forceinline__ void pk_producer(const PkParams &P, uint8_t *ring, ui
                 break;
             }
             // the unit's rows are contiguous in HBM: one copy per matrix
-            int row0, nvalid, ulr;
-            pk_unit(mm, shr, u, row0, nvalid, ulr);
+            const int row0 = (u_begin + u) * R, nvalid = min(R, mm.N - row0);
             const uint32_t bytes = static_cast<uint32_t>(nvalid) * row_bytes;
             if (lane == 0) mbar_arrive_expect_tx(&full[s], nmat * bytes);
             __syncwarp();
             if (lane < nmat)
-                bulk_g2s(ring + s * PK_SLOT_BYTES + (lane << ulr) * row_bytes,
+                bulk_g2s(ring + s * PK_SLOT_BYTES + lane * R * row_bytes,
                          (lane ? mm.w1 : mm.w0) + static_cast<int64_t>(row0) * row_bytes, bytes, &full[s], pol);
         }
         if (lane == 0) PK_STAMP(2, ph);
@@ -305,21 +275,16 @@ __device__ __forceinline__ void pk_producer(const PkParams &P, uint8_t *ring, ui
     if (ok && P.n_layers > 0) {
         // the next token starts with this CTA's q|k|v rows of layer 0: into L2
         const PkMm mm = pk_mm(P, 0, PK_QKV);
-        const PkShare shr = pk_share(mm);
+        int u_begin, nu;
+        pk_range(mm, u_begin, nu);
         const int64_t row_bytes = static_cast<int64_t>(mm.nsb) * Q4K_BYTES;
-        // the share's R-row units, then its one-row units: two row ranges
-        const int64_t r0[2] = {static_cast<int64_t>(shr.ub) << mm.lr,
-                               (static_cast<int64_t>(mm.nbig) << mm.lr) + shr.ut};
-        const int64_t nr[2] = {min(static_cast<int64_t>(shr.nb) << mm.lr, static_cast<int64_t>(mm.N) - r0[0]),
-                               static_cast<int64_t>(shr.nt)};
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const uint8_t *base = mm.w0 + r0[q] * row_bytes;
-            const int64_t bytes = nr[q] > 0 ? nr[q] * row_bytes : 0;  // a multiple of 16 (144 per block)
-            constexpr int64_t PIECE = 16384;
-            for (int64_t o = static_cast<int64_t>(lane) * PIECE; o < bytes; o += 32 * PIECE)
-                prefetch_l2_bulk(base + o, static_cast<uint32_t>(min(PIECE, bytes - o)));
-        }
+        const int64_t row0 = static_cast<int64_t>(u_begin) << mm.lr;
+        const int64_t rows = min(static_cast<int64_t>(nu) << mm.lr, static_cast<int64_t>(mm.N) - row0);
+        const uint8_t *base = mm.w0 + row0 * row_bytes;
+        const int64_t bytes = rows > 0 ? rows * row_bytes : 0;  // a multiple of 16 (144 per block)
+        constexpr int64_t PIECE = 16384;
+        for (int64_t o = static_cast<int64_t>(lane) * PIECE; o < bytes; o += 32 * PIECE)
+            prefetch_l2_bulk(base + o, static_cast<uint32_t>(min(PIECE, bytes - o)));
     }
     // drain: every copy this warp issued has landed before the CTA can exit
     if (lane == 0) {
@@ -336,31 +301,29 @@ __device__ __forceinline__ void pk_producer(const PkParams &P, uint8_t *ring, ui
 // K-slice sums and their fixed tree; the row's first lane stores y (and
 // merges the argmax key).
 template <int NMAT>
-__device__ __forceinline__ void pk_units(const PkMm &mm, const PkShare &shr, uint32_t T, const uint8_t *ring,
+__device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, uint32_t T, const uint8_t *ring,
                                          uint64_t *full, uint64_t *empty, float *vbuf, const uint8_t *arec,
                                          float *Y, unsigned long long *s_amax, int sh, bool &poisoned) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nsb = mm.nsb, nu = shr.nb + shr.nt;
+    const int lr = mm.lr, R = 1 << lr, P = 32 >> lr;
+    // lane -> (row r, first superblock p); rows are staged back to back
+    // (pitch nsb * 144 B = 9 nsb chunks of 16 B), so the chunk of (r, b) is
+    // 9 nsb r + 9 b + c == (nsb r + b) mod 8 bank groups.  P >= 8: a
+    // quarter warp is one row and eight consecutive superblocks (distinct);
+    // P == 4 (eight rows): a quarter warp is four rows x two superblocks,
+    // distinct for nsb == 2 mod 8 (the 2560-wide matrices)
+    int r, p;
+    if (P >= 8) {
+        r = lane / P;
+        p = lane % P;
+    } else {
+        const int q4 = lane >> 3, w8 = lane & 7;
+        r = (w8 >> 1) + 4 * (q4 & 1);
+        p = (w8 & 1) + 2 * (q4 >> 1);
+    }
+    const int nsb = mm.nsb, N = mm.N;
     const uint32_t smask = (1u << sh) - 1u;
     for (int u = warp; u < nu; u += PK_NCW) {
-        int row0, nrows, lr;
-        pk_unit(mm, shr, u, row0, nrows, lr);
-        const int R = 1 << lr, P = 32 >> lr;
-        // lane -> (row r, first superblock p); rows are staged back to back
-        // (pitch nsb * 144 B = 9 nsb chunks of 16 B), so the chunk of (r, b)
-        // is 9 nsb r + 9 b + c == (nsb r + b) mod 8 bank groups.  P >= 8: a
-        // quarter warp is one row and eight consecutive superblocks
-        // (distinct); P == 4 (eight rows): a quarter warp is four rows x two
-        // superblocks, distinct for nsb == 2 mod 8 (the 2560-wide matrices)
-        int r, p;
-        if (P >= 8) {
-            r = lane / P;
-            p = lane % P;
-        } else {
-            const int q4 = lane >> 3, w8 = lane & 7;
-            r = (w8 >> 1) + 4 * (q4 & 1);
-            p = (w8 & 1) + 2 * (q4 >> 1);
-        }
         const uint32_t t = T + static_cast<uint32_t>(u);
         const int s = static_cast<int>(t & smask);
 #ifdef ABRA_PK_TRACE
@@ -396,14 +359,14 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, const PkShare &shr, uin
         for (int half = 0; half < 2; ++half) {
             const int rr = g + 4 * half;
             if (half == 1 && R <= 4) break;  // warp-uniform
-            const int row = row0 + rr;
-            const bool live = rr < nrows;
+            const int row = ((u_begin + u) << lr) + rr;
+            const bool live = rr < R;
             float yv = pk_slice_tree(live ? pk_slice_sum(vbuf + rr * nsb, nsb, i) : 0.0f);
             if constexpr (NMAT == 2) {
                 const float up = pk_slice_tree(live ? pk_slice_sum(vbuf + (R + rr) * nsb, nsb, i) : 0.0f);
                 yv = __fmul_rn(up, abra_silu(yv));
             }
-            if (i == 0 && live) {
+            if (i == 0 && live && row < N) {
                 Y[row] = yv;
                 const unsigned long long k = argmax_key(yv, row);
                 key = k > key ? k : key;
@@ -1065,17 +1028,18 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             const int kind = ph == PH_QKV ? PK_QKV : ph == PH_O ? PK_O : ph == PH_GU ? PK_GU : ph == PH_DOWN ? PK_DOWN : PK_OUT;
             float *Y = ph == PH_QKV ? P.qkv : ph == PH_GU ? P.act : ph == PH_OUT ? P.logits : P.delta;
             const PkMm mm = pk_mm(P, l, kind);
-            const PkShare shr = pk_share(mm);
+            int u_begin, nu;
+            pk_range(mm, u_begin, nu);
 #ifdef ABRA_PK_TRACE
             if (t == 0) g_pk_gemv = (l == 1 || ph == PH_OUT) ? kind : 99;
             cta_sync();
 #endif
             unsigned long long *amax = ph == PH_OUT ? &s_amax : nullptr;
             if (mm.w1)
-                pk_units<2>(mm, shr, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
+                pk_units<2>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
             else
-                pk_units<1>(mm, shr, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
-            T += static_cast<uint32_t>(shr.nb + shr.nt);
+                pk_units<1>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
+            T += static_cast<uint32_t>(nu);
         }
         cta_sync();
         if (t == 0) PK_STAMP(1, e);
@@ -1117,7 +1081,7 @@ PkKernel pk_kernel_for(int gq) {
 
 // ------------------------------------------------------------ planning ---
 struct PkPlan {
-    int rows[PK_KINDS], pitch[PK_KINDS], nbig[PK_KINDS];
+    int rows[PK_KINDS], pitch[PK_KINDS];
     int slot_shift;
     int off_vbuf, off_arec, off_x, off_ring, smem;
 };
@@ -1166,10 +1130,6 @@ bool pk_plan(int hidden, int n_heads, int n_kv, int ffn, int head_dim, int vocab
             }
         }
         if (!pl.rows[k]) return no("a row does not fit a ring slot");
-        // R-row units in multiples of the grid's consumer warps; the rows
-        // left over become one-row units spread over the CTAs
-        const int64_t units = (N[k] + pl.rows[k] - 1) / pl.rows[k], W = static_cast<int64_t>(sms) * PK_NCW;
-        pl.nbig[k] = static_cast<int>(units > W ? units / W * W : units);
     }
     const int nsb_max = std::max(std::max(hidden, n_heads * 128), ffn) / QK_K;
     const int scratch = std::max(8 * hidden, 4 * pk_att_floats(gq));
@@ -1258,7 +1218,6 @@ cudaError_t launch_persist_step(const PersistModel &pm, cudaStream_t st) {
     for (int k = 0; k < PK_KINDS; ++k) {
         P.lr[k] = log2i(pl.rows[k]);
         P.pitch[k] = pl.pitch[k];
-        P.nbig[k] = pl.nbig[k];
     }
     P.slot_shift = pl.slot_shift;
     P.off_vbuf = pl.off_vbuf;
@@ -1302,29 +1261,23 @@ bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn
         const int nph = 4 * n_layers + 1;
         for (int ph = 0; ph < nph; ++ph) {
             const int kind = ph == nph - 1 ? PK_OUT : (ph & 3);
-            const int N = rows[kind], R = pl.rows[kind], pitch = pl.pitch[kind], nbig = pl.nbig[kind];
+            const int N = rows[kind], R = pl.rows[kind], pitch = pl.pitch[kind];
             const int64_t row_bytes = static_cast<int64_t>(nsb[kind]) * Q4K_BYTES;
-            const int64_t ntail = std::max<int64_t>(0, N - static_cast<int64_t>(nbig) * R);
+            const int64_t total = (N + R - 1) / R;
+            const int u0 = static_cast<int>(b * total / sms), u1 = static_cast<int>((b + 1) * total / sms);
             if (nmat[kind] * R * nsb[kind] > PK_VMAX || (R != 1 && R != 2 && R != 4 && R != 8))
                 return fail("unit exceeds the staging buffer");
-            if (static_cast<int64_t>(nbig) * R < N && nbig % (sms * PK_NCW) != 0)
-                return fail("R-row units are not a multiple of the consumer warps");
-            // this CTA's R-row units, then its one-row units (pk_share, pk_unit)
-            const int64_t ub = b * int64_t(nbig) / sms, nb = (b + 1) * int64_t(nbig) / sms - ub;
-            const int64_t ut = b * ntail / sms, nt = (b + 1) * ntail / sms - ut;
-            for (int64_t u = 0; u < nb + nt; ++u, ++t) {
-                const int64_t ur = u < nb ? R : 1;
-                const int64_t row0 = u < nb ? (ub + u) * R : int64_t(nbig) * R + ut + (u - nb);
-                const int64_t nvalid = std::min<int64_t>(ur, N - row0);
+            for (int u = u0; u < u1; ++u, ++t) {
+                const int row0 = u * R, nvalid = std::min(R, N - row0);
                 if (nvalid <= 0 || row_bytes != pitch || (pitch & 15) || nmat[kind] * nvalid * row_bytes > (1 << 20) - 1)
                     return fail("unit does not fit its row pitch");
                 for (int m = 0; m < nmat[kind]; ++m) {  // one copy per (unit, matrix)
                     const int64_t bytes = nvalid * row_bytes;
-                    const int64_t dst = (t % nslot) * PK_SLOT_BYTES + m * ur * row_bytes;
-                    const int64_t src = row0 * row_bytes;
+                    const int64_t dst = (t % nslot) * PK_SLOT_BYTES + m * R * row_bytes;
+                    const int64_t src = static_cast<int64_t>(row0) * row_bytes;
                     const int64_t tensor = static_cast<int64_t>(N) * row_bytes;
                     if (dst + bytes > nslot * PK_SLOT_BYTES || (dst & 15) || (bytes & 15) || src + bytes > tensor ||
-                        (src & 15) || (m + 1) * ur * row_bytes > PK_SLOT_BYTES)
+                        (src & 15) || (m + 1) * R * row_bytes > PK_SLOT_BYTES)
                         return fail("copy leaves its slot or its tensor");
                     ++copies;
                 }
