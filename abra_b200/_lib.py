@@ -81,6 +81,7 @@ SIGNATURES: dict[str, tuple] = {
                                   C.POINTER(C.c_uint64)]),
     "abra_model_last_error": (C.c_char_p, []),
     "abra_model_create_batched": (C.c_int, [_vp, _i32, C.POINTER(C.c_void_p)]),
+    "abra_model_create_batched_tp": (C.c_int, [_vp, _i32, _i32, _i32, C.POINTER(C.c_void_p)]),
     "abra_model_reset_batched": (C.c_int, [_vp, _vp, _i32]),
     "abra_model_read_batched": (C.c_int, [_vp, _vp, _i32, _vp]),
     "abra_tp_shard_info": (C.c_int, [_vp, _i32, _i32, _vp]),

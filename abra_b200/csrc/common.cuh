@@ -212,6 +212,15 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long
     return v;
 }
 
+// Order-preserving 64-bit key of (value, row): the float's bits mapped to an
+// unsigned order in the high word, ~row in the low word, so the largest key
+// is the largest value and, among equal values, the lowest row.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+    unsigned u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<unsigned>(row));
+}
+
 // Spins until *cnt >= target or WAIT_LIMIT_NS passes (then flags
 // ERR_FLAG_TIMEOUT and returns false); polls with relaxed loads and acquires
 // once at the end.  Once a cross-rank wait of this translation unit has

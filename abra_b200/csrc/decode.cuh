@@ -23,9 +23,13 @@ cudaError_t launch_embed(const void *E, int hidden, const int32_t *tokens, const
 cudaError_t launch_embed_q6k(const void *E, int hidden, const int32_t *tokens, const int32_t *pos,
                              float *h, bool pdl, cudaStream_t s, int batch = 1,
                              int64_t tok_stride = 0);
+// With wait_cnt (tensor parallel): first wait, bounded, until *wait_cnt >=
+// (*epoch + 1) * per_step -- every rank's partial sums of the step have arrived.
 cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const float *w,
                                           float eps, void *y, int K, int ncols, bool pdl,
-                                          cudaStream_t s);
+                                          cudaStream_t s, const unsigned long long *wait_cnt = nullptr,
+                                          const unsigned long long *epoch = nullptr,
+                                          unsigned long long per_step = 0);
 cudaError_t launch_qk_norm_rope_kv(const float *qkv, const float *q_norm, const float *k_norm,
                                    float eps, const float *rope, const int32_t *pos, float *q_out,
                                    void *kc, void *vc, int n_heads, int n_kv, int max_ctx,
@@ -49,6 +53,23 @@ cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t
                                 int32_t *picks, int64_t tok_stride, int32_t *pos,
                                 const int32_t *n_prompt, int max_ctx, int batch, bool pdl,
                                 cudaStream_t s);
+// Tensor parallel, batch: where each rank's per-sequence argmax keys go.
+struct TpKeyPush {
+    int npeer;
+    unsigned long long *key[8];  // rank q's key words [batch]
+    unsigned long long *cnt[8];  // rank q's arrival counter of the output
+    unsigned long long *cta_cnt; // this rank's CTA count of the launch
+};
+// Each sequence's key over this rank's vocab rows (logits rows ldl apart,
+// row ids offset by row_offset), merged into every rank's key words.
+cudaError_t launch_argmax_keys_batch(const float *logits, int n, int64_t ldl, int row_offset,
+                                     const TpKeyPush &push, int batch, bool pdl, cudaStream_t s);
+// Waits for every rank's keys, writes the picks and next tokens of the batch,
+// resets the keys, advances the epoch and the shared position.
+cudaError_t launch_argmax_finish_batch(unsigned long long *keys, int batch, int32_t *tokens, int32_t *picks,
+                                       int64_t tok_stride, int32_t *pos, const int32_t *n_prompt, int max_ctx,
+                                       const unsigned long long *wait_cnt, unsigned long long *epoch,
+                                       unsigned long long per_step, bool pdl, cudaStream_t s);
 // out[c] = argmax of column c of logits (ldl floats apart), c < ncols.
 cudaError_t launch_argmax_cols(const float *logits, int n, int64_t ldl, int32_t *out, int ncols,
                                bool pdl, cudaStream_t s);

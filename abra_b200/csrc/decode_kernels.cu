@@ -76,13 +76,19 @@ constexpr int RES_THREADS = 1024;
 __global__ void __launch_bounds__(RES_THREADS)
     residual_rmsnorm_quant_kernel(float *__restrict__ h, const DeltaSet ds,
                                   const float *__restrict__ w, float eps,
-                                  block_q8_1 *__restrict__ y, int K) {
+                                  block_q8_1 *__restrict__ y, int K,
+                                  const unsigned long long *wait_cnt, const unsigned long long *epoch,
+                                  unsigned long long per_step) {
     extern __shared__ float s_x[];
     __shared__ float red[RMS_THREADS / 32];
     __shared__ float s_r;
     pdl_wait();
     pdl_launch_dependents();
     const int c = blockIdx.x, t = threadIdx.x;
+    if (wait_cnt) {  // tensor parallel: every rank's partial sums have arrived (bounded)
+        if (t == 0) wait_count(wait_cnt, (__ldcg(epoch) + 1ull) * per_step);
+        __syncthreads();
+    }
     float *hc = h + static_cast<int64_t>(c) * K;
     for (int i = t; i < K; i += RES_THREADS) {
         float v = hc[i];
@@ -490,6 +496,79 @@ __global__ void __launch_bounds__(1024)
     }
 }
 
+// Tensor parallel, batch: the key of each sequence's largest logit among
+// this rank's vocab rows (argmax_key of (value, row_offset + row): ties to
+// the lowest id), merged into that sequence's key word on every rank; each
+// CTA then counts itself on cta_cnt and the launch's last CTA adds 1 to every
+// rank's counter with release semantics at system scope.  One CTA of 1024
+// threads per sequence.
+__global__ void __launch_bounds__(1024)
+    argmax_keys_batch_kernel(const float *__restrict__ x, int n, int64_t ldl, int row_offset,
+                             const TpKeyPush push) {
+    __shared__ unsigned long long sk[32];
+    pdl_wait();
+    pdl_launch_dependents();
+    x += blockIdx.x * ldl;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const unsigned long long k = argmax_key(x[i], row_offset + i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, m);
+        best = o > best ? o : best;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) sk[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = sk[w] > best ? sk[w] : best;
+        for (int q = 0; q < push.npeer; ++q) atomicMax_system(push.key[q] + blockIdx.x, best);
+        const unsigned long long old = atom_add_acq_rel_gpu(push.cta_cnt, 1ull);
+        if ((old + 1ull) % gridDim.x == 0ull)
+            for (int q = 0; q < push.npeer; ++q) red_release_sys_add(push.cnt[q], 1ull);
+    }
+}
+
+// Tensor parallel, batch: once every rank's keys have arrived (bounded wait
+// on wait_cnt), each sequence's pick from its key word (then reset), the
+// picks and, past the prompt, the next tokens; then the step's epoch and the
+// shared position advance.
+__global__ void argmax_finish_batch_kernel(unsigned long long *__restrict__ keys, int batch,
+                                           int32_t *__restrict__ tokens, int32_t *__restrict__ picks,
+                                           int64_t tok_stride, int32_t *__restrict__ pos_p,
+                                           const int32_t *__restrict__ n_prompt_p, int max_ctx,
+                                           const unsigned long long *wait_cnt, unsigned long long *epoch,
+                                           unsigned long long per_step) {
+    __shared__ int s_pos;
+    __shared__ unsigned long long s_e;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = threadIdx.x;
+    if (t == 0) {
+        s_e = __ldcg(epoch);
+        wait_count(wait_cnt, (s_e + 1ull) * per_step);
+        s_pos = *pos_p;
+    }
+    __syncthreads();
+    const int p = s_pos;
+    for (int b = t; b < batch; b += blockDim.x) {
+        const unsigned long long k = __ldcg(keys + b);
+        keys[b] = 0ull;
+        const int bi = static_cast<int>(0xFFFFFFFFu - static_cast<unsigned>(k & 0xFFFFFFFFull));
+        if (p < max_ctx) {  // the host never steps past max_ctx
+            picks[b * tok_stride + p] = bi;
+            if (p + 1 >= *n_prompt_p) tokens[b * tok_stride + p + 1] = bi;
+        }
+    }
+    __syncthreads();
+    if (t == 0) {
+        *epoch = s_e + 1ull;
+        if (p < max_ctx) *pos_p = p + 1;
+    }
+}
+
 // out[c] = argmax of logits column c (ties to the lowest index, the order of
 // argmax_batch_kernel); one CTA of 1024 threads per column.
 __global__ void argmax_cols_kernel(const float *__restrict__ x, int n, int64_t ldl,
@@ -589,7 +668,8 @@ cudaError_t launch_embed_q6k(const void *E, int hidden, const int32_t *tokens, c
 
 cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const float *w,
                                           float eps, void *y, int K, int ncols, bool pdl,
-                                          cudaStream_t s) {
+                                          cudaStream_t s, const unsigned long long *wait_cnt,
+                                          const unsigned long long *epoch, unsigned long long per_step) {
     const size_t smem = static_cast<size_t>(K) * sizeof(float);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(residual_rmsnorm_quant_kernel,
@@ -598,7 +678,7 @@ cudaError_t launch_residual_rmsnorm_quant(float *h, const DeltaSet &ds, const fl
         if (e != cudaSuccess) return e;
     }
     return launch_pdl(residual_rmsnorm_quant_kernel, dim3(ncols), dim3(RES_THREADS), smem, s, pdl,
-                      h, ds, w, eps, static_cast<block_q8_1 *>(y), K);
+                      h, ds, w, eps, static_cast<block_q8_1 *>(y), K, wait_cnt, epoch, per_step);
 }
 
 cudaError_t launch_qk_norm_rope_kv(const float *qkv, const float *q_norm, const float *k_norm,
@@ -649,6 +729,22 @@ cudaError_t launch_argmax_batch(const float *logits, int n, int64_t ldl, int32_t
                                n_prompt, max_ctx);
     if (e != cudaSuccess) return e;
     return launch_pdl(pos_advance_kernel, dim3(1), dim3(32), 0, s, pdl, pos, 1, max_ctx);
+}
+
+cudaError_t launch_argmax_keys_batch(const float *logits, int n, int64_t ldl, int row_offset,
+                                     const TpKeyPush &push, int batch, bool pdl, cudaStream_t s) {
+    if (push.npeer < 1 || push.npeer > 8 || !push.cta_cnt) return cudaErrorInvalidValue;
+    return launch_pdl(argmax_keys_batch_kernel, dim3(batch), dim3(1024), 0, s, pdl, logits, n, ldl, row_offset,
+                      push);
+}
+
+cudaError_t launch_argmax_finish_batch(unsigned long long *keys, int batch, int32_t *tokens, int32_t *picks,
+                                       int64_t tok_stride, int32_t *pos, const int32_t *n_prompt, int max_ctx,
+                                       const unsigned long long *wait_cnt, unsigned long long *epoch,
+                                       unsigned long long per_step, bool pdl, cudaStream_t s) {
+    if (!wait_cnt || !epoch) return cudaErrorInvalidValue;
+    return launch_pdl(argmax_finish_batch_kernel, dim3(1), dim3(64), 0, s, pdl, keys, batch, tokens, picks,
+                      tok_stride, pos, n_prompt, max_ctx, wait_cnt, epoch, per_step);
 }
 
 cudaError_t launch_argmax_cols(const float *logits, int n, int64_t ldl, int32_t *out, int ncols,

@@ -106,8 +106,21 @@ cudaError_t launch_mmvq_q4k_partials(const void *w, const void *x_q8, float *y, 
 // Batch-32 MMVQ on the tensor cores (tcgen05 kind::i8): ncols = 32 Q8_1
 // columns, ks k-parts (1, 2, 4, 8) over the canonical slices; ks > 1 needs
 // part = ks * 32 * N floats of scratch and adds a combine launch.
+// A K-shard and tensor-parallel push for one tcgen05 MMVQ launch (off by
+// default).  part >= 0: the launch holds exactly k-part `part` of a ks-way
+// split of a K of nsb_sl superblocks (its first superblock is sb_base) and
+// writes that part's slice-tree top to y, or pushes it (npeer > 0) to every
+// peer_y[q] and counts on cta_cnt; the launch's last CTA adds 1 to each
+// peer_cnt[q] with release semantics at system scope.
+struct TcOpts {
+    int nsb_sl = 0, sb_base = 0, part = -1;
+    int npeer = 0;
+    float *peer_y[8] = {};
+    unsigned long long *peer_cnt[8] = {};
+    unsigned long long *cta_cnt = nullptr;
+};
 cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N, int64_t K,
-                           int64_t ldy, int ks, float *part, int flags, cudaStream_t stream);
+                           int64_t ldy, int ks, float *part, int flags, cudaStream_t stream, const TcOpts *opt = nullptr);
 // Sets the tensor-core kernels' attributes (outside stream capture).
 cudaError_t prepare_mmvq_tc();
 

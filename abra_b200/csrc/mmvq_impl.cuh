@@ -120,15 +120,6 @@ __host__ __device__ __forceinline__ int shard_slice(int sl_nsb, int sl_base, int
            slice_start(sl_nsb, sl_base);
 }
 
-// Order-preserving 64-bit key of (value, row): the float's bits mapped to an
-// unsigned order in the high word, ~row in the low word, so the largest key
-// is the largest value and, among equal values, the lowest row.
-__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
-    unsigned u = __float_as_uint(v);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<unsigned>(row));
-}
-
 __host__ __device__ __forceinline__ int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
 struct MmvqLayout {

@@ -78,6 +78,17 @@ struct TcParams {
     float *part;       // KS > 1: [KS][32][N]
     int N, nsb;
     int64_t ldy;
+    // K-shard: slice bounds come from the whole K's nsb_sl superblocks;
+    // local superblock = whole-K superblock - sb_base; k-part = j_base +
+    // blockIdx.y; direct: the single k-part's tree top goes to Y
+    int nsb_sl, sb_base, j_base, direct;
+    // tensor-parallel push (npeer > 0): rows go to peer_y[q] instead of Y;
+    // each CTA then counts itself on cta_cnt and the launch's last CTA adds
+    // 1 to every peer_cnt[q] with release semantics at system scope
+    int npeer;
+    float *peer_y[8];
+    unsigned long long *peer_cnt[8];
+    unsigned long long *cta_cnt;
 };
 
 // Exact tree over a power-of-two number of slices, fed left to right: the
@@ -136,9 +147,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     float *sam = reinterpret_cast<float *>(smem + L.am);
 
     const int N = prm.N, nsb = prm.nsb, nblk = nsb * 8;
-    const int row0 = blockIdx.x * TC_M, j = blockIdx.y;
+    const int row0 = blockIdx.x * TC_M, j = prm.j_base + blockIdx.y;
     const int nvalid = min(TC_M, N - row0);
-    const int sb_lo = slice_start(nsb, j * NSL), sb_hi = slice_start(nsb, (j + 1) * NSL);
+    // canonical slice i of the whole K, in this launch's local superblocks
+    auto sl = [&](int i) { return slice_start(prm.nsb_sl, i) - prm.sb_base; };
+    const int sb_lo = sl(j * NSL), sb_hi = sl((j + 1) * NSL);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -239,7 +252,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
     for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
     int e_slice = 0;
-    int e_lo = sb_lo, e_hi = slice_start(nsb, j * NSL + 1);
+    int e_lo = sb_lo, e_hi = sl(j * NSL + 1);
     auto next_slices = [&](int b) {  // push finished (and empty) slices until b lies in e_slice
         while (b >= e_hi && e_slice < NSL) {
             tree.push(e_slice, acc);
@@ -247,7 +260,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
             ++e_slice;
             e_lo = e_hi;
-            e_hi = slice_start(nsb, j * NSL + e_slice + 1);
+            e_hi = sl(j * NSL + e_slice + 1);
         }
     };
     auto epilogue = [&](int u, int buf) {
@@ -333,10 +346,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int c = 0; c < 8; ++c) {
             const int col = 8 * cg + c;
             const float v = tree.lv[TOP][c];
-            if constexpr (KS == 1)
-                prm.Y[col * prm.ldy + row0 + rloc] = v;
-            else
+            if (KS == 1 || prm.direct) {
+                const int64_t at = col * prm.ldy + row0 + rloc;
+                if (prm.npeer > 0)
+                    for (int q = 0; q < prm.npeer; ++q) prm.peer_y[q][at] = v;
+                else
+                    prm.Y[at] = v;
+            } else {
                 prm.part[(static_cast<int64_t>(j) * TC_N + col) * N + row0 + rloc] = v;
+            }
         }
     }
     tc_fence_before();
@@ -344,6 +362,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, TC_TMEM_COLS);
+    }
+    if (prm.npeer > 0 && threadIdx.x == 0) {
+        // every consumer's stores are done (the barrier above): count this
+        // CTA; the launch's last CTA publishes the launch to every rank
+        const unsigned long long old = atom_add_acq_rel_gpu(prm.cta_cnt, 1ull);
+        if ((old + 1ull) % (static_cast<unsigned long long>(gridDim.x) * gridDim.y) == 0ull)
+            for (int q = 0; q < prm.npeer; ++q) red_release_sys_add(prm.peer_cnt[q], 1ull);
     }
 }
 
@@ -405,11 +430,33 @@ cudaError_t prepare_mmvq_tc() {
 }
 
 cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N, int64_t K,
-                           int64_t ldy, int ks, float *part, int flags, cudaStream_t stream) {
+                           int64_t ldy, int ks, float *part, int flags, cudaStream_t stream,
+                           const TcOpts *opt) {
+    const bool single = opt && opt->part >= 0;  // one k-part of a ks-way split, straight to y
     if (K % QK_K || K <= 0 || N <= 0 || ldy < N || !(ks == 1 || ks == 2 || ks == 4 || ks == 8) ||
-        (ks > 1 && !part))
+        (ks > 1 && !part && !single) || (opt && (opt->npeer < 0 || opt->npeer > 8)) ||
+        (opt && opt->npeer > 0 && !opt->cta_cnt))
         return cudaErrorInvalidValue;
     TcParams prm = {};
+    const int nsb_local = static_cast<int>(K / QK_K);
+    prm.nsb_sl = opt && opt->nsb_sl > 0 ? opt->nsb_sl : nsb_local;
+    prm.sb_base = opt ? opt->sb_base : 0;
+    prm.j_base = single ? opt->part : 0;
+    prm.direct = single ? 1 : 0;
+    if (single && (opt->part >= ks || slice_start(prm.nsb_sl, opt->part * (8 / ks)) != prm.sb_base ||
+                   slice_start(prm.nsb_sl, (opt->part + 1) * (8 / ks)) - prm.sb_base != nsb_local))
+        return cudaErrorInvalidValue;  // the shard must be exactly the k-part's slices
+    if (!single && prm.nsb_sl != nsb_local) return cudaErrorInvalidValue;
+    if (opt && opt->npeer > 0) {
+        prm.npeer = opt->npeer;
+        for (int q = 0; q < opt->npeer; ++q) {
+            if (!opt->peer_y[q] || !opt->peer_cnt[q]) return cudaErrorInvalidValue;
+            prm.peer_y[q] = opt->peer_y[q];
+            prm.peer_cnt[q] = opt->peer_cnt[q];
+        }
+        prm.cta_cnt = opt->cta_cnt;
+        if (ks > 1 && !single) return cudaErrorInvalidValue;  // the push is the launch's own output
+    }
     prm.W = static_cast<const uint8_t *>(w);
     prm.X = static_cast<const uint8_t *>(x_q8);
     prm.Y = y;
@@ -449,7 +496,7 @@ cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N,
         attr_set[dev][ki] = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((N + TC_M - 1) / TC_M), static_cast<unsigned>(ks));
+    cfg.gridDim = dim3(static_cast<unsigned>((N + TC_M - 1) / TC_M), static_cast<unsigned>(single ? 1 : ks));
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -459,7 +506,7 @@ cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N,
     cfg.attrs = attr;
     cfg.numAttrs = (flags & MMVQ_PDL) ? 1 : 0;
     e = cudaLaunchKernelEx(&cfg, fn, prm, wmap);
-    if (e != cudaSuccess || ks == 1) return e;
+    if (e != cudaSuccess || ks == 1 || single) return e;
     void (*cfn)(const float *, float *, int, int64_t) = ks == 2 ? mmvq_tc_combine_kernel<2>
                                                        : ks == 4 ? mmvq_tc_combine_kernel<4>
                                                                  : mmvq_tc_combine_kernel<8>;

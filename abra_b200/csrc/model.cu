@@ -142,15 +142,24 @@ struct Model {
     PersistLayer *players = nullptr;
     void *psync = nullptr;
 
+    // Exchange arena: [slot 0 .. 2L)[rank][batch][hidden] fp32 partials, then
+    // the counters: arrivals per slot (2L + 1: o and down of each layer, the
+    // output), the argmax key word of each sequence, the step epoch, this
+    // rank's CTA count per slot.
     float *recv(int q, int slot) const {  // rank q's partial in slot, in peer[..]'s layout
-        return reinterpret_cast<float *>(arena) + (static_cast<size_t>(slot) * sh.world + q) * cfg.hidden;
+        return reinterpret_cast<float *>(arena) +
+               (static_cast<size_t>(slot) * sh.world + q) * static_cast<size_t>(batch) * cfg.hidden;
+    }
+    float *recv_of(uint8_t *base, int q, int slot) const {
+        return reinterpret_cast<float *>(base) +
+               (static_cast<size_t>(slot) * sh.world + q) * static_cast<size_t>(batch) * cfg.hidden;
     }
     unsigned long long *cnt_of(uint8_t *base, int slot) const {
         return reinterpret_cast<unsigned long long *>(base + arena_recv) + slot;
     }
-    unsigned long long *key_of(uint8_t *base) const { return cnt_of(base, 2 * cfg.n_layers + 1); }
-    unsigned long long *epoch() const { return cnt_of(arena, 2 * cfg.n_layers + 2); }
-    unsigned long long *cta_cnt(int slot) const { return cnt_of(arena, 2 * cfg.n_layers + 3 + slot); }
+    unsigned long long *key_of(uint8_t *base, int b = 0) const { return cnt_of(base, 2 * cfg.n_layers + 1 + b); }
+    unsigned long long *epoch() const { return cnt_of(arena, 2 * cfg.n_layers + 1 + batch); }
+    unsigned long long *cta_cnt(int slot) const { return cnt_of(arena, 2 * cfg.n_layers + 2 + batch + slot); }
 };
 
 static uint64_t tensor_id(int layer, int which) {
@@ -329,9 +338,9 @@ static cudaError_t build(Model &m) {
         m.persist = true;
     }
     if (sh.world > 1) {
-        const size_t recv = static_cast<size_t>(2 * c.n_layers) * sh.world * c.hidden * 4;
+        const size_t recv = static_cast<size_t>(2 * c.n_layers) * sh.world * B * c.hidden * 4;
         m.arena_recv = (recv + 255) / 256 * 256;
-        m.arena_bytes = m.arena_recv + (static_cast<size_t>(4 * c.n_layers + 4) * 8 + 255) / 256 * 256;
+        m.arena_bytes = m.arena_recv + (static_cast<size_t>(4 * c.n_layers + 3 + B) * 8 + 255) / 256 * 256;
         TRY(cudaMalloc(&m.arena, m.arena_bytes));
         TRY(cudaMemsetAsync(m.arena, 0, m.arena_bytes, st));
         m.peer[sh.rank] = m.arena;
@@ -465,12 +474,16 @@ static const MmvqConfig *tuned6(const int64_t sh[4]) {
 // kernel for kernel, so the logits are the same bits.
 static cudaError_t record_step_batched(const Model &m, cudaStream_t st) {
     const abra_model_config &c = m.cfg;
-    const int B = m.batch, L = c.n_layers;
+    const abra_tp_shard &sh = m.sh;
+    const int B = m.batch, L = c.n_layers, W = sh.world;
+    const bool tp = W > 1;
     const bool pdl = (c.flags & ABRA_MODEL_NO_PDL) == 0;
     const int pf = pdl ? MMVQ_PDL : 0;
-    const int64_t hd = c.head_dim, qd = c.n_heads * hd;
-    const int64_t qkv_rows = (c.n_heads + 2 * c.n_kv_heads) * hd;
-    const size_t kv_layer = static_cast<size_t>(c.n_kv_heads) * c.max_ctx * c.head_dim;
+    const int64_t hd = c.head_dim;
+    const int64_t qd = static_cast<int64_t>(sh.q_heads) * hd;  // this rank's q heads
+    const int64_t qkv_rows = static_cast<int64_t>(sh.q_heads + 2 * sh.kv_heads) * hd;
+    const int64_t ffn = sh.ffn_hi - sh.ffn_lo, vocab = sh.vocab_hi - sh.vocab_lo;
+    const size_t kv_layer = static_cast<size_t>(sh.kv_heads) * c.max_ctx * c.head_dim;
     const int64_t tok_stride = c.max_ctx + 1;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(c.head_dim)));
     SeqStrides sb;
@@ -484,30 +497,80 @@ static cudaError_t record_step_batched(const Model &m, cudaStream_t st) {
     auto tc = [&](const void *w, const void *x, float *y, int64_t N, int64_t K, int ks) {
         return launch_mmvq_tc(w, x, y, N, K, N, ks, m.tc_ws, pf, st);
     };
+    // Tensor parallel: o and down are K-sharded on canonical slices, so a
+    // rank's output is k-part `rank` of a W-way split; it is pushed into slot
+    // `slot` of every rank's arena, and the next residual + RMSNorm waits for
+    // all W and adds them in the fixed tree (bit-identical to one GPU)
+    const int part = tp ? sh.sl_base / sh.sl_cnt : 0;
+    auto kshard = [&](const void *w, const void *x, int64_t K, int nsb_full, int slot) {
+        TcOpts o;
+        o.nsb_sl = nsb_full;
+        o.sb_base = slice_start(nsb_full, sh.sl_base);
+        o.part = part;
+        o.npeer = W;
+        for (int q = 0; q < W; ++q) {
+            o.peer_y[q] = m.recv_of(m.peer[q], sh.rank, slot);
+            o.peer_cnt[q] = m.cnt_of(m.peer[q], slot);
+        }
+        o.cta_cnt = m.cta_cnt(slot);
+        return launch_mmvq_tc(w, x, nullptr, c.hidden, K, c.hidden, W, nullptr, pf, st, &o);
+    };
+    auto slot_deltas = [&](int slot) {
+        DeltaSet d = {};
+        d.G = W;
+        for (int q = 0; q < W; ++q) d.p[q] = m.recv(q, slot);
+        return d;
+    };
+    auto resnorm = [&](const DeltaSet &ds, const float *norm, int wait_slot) {
+        if (tp && wait_slot >= 0)
+            return launch_residual_rmsnorm_quant(m.h, slot_deltas(wait_slot), norm, c.eps, m.xq, c.hidden, B,
+                                                 pdl, st, m.cnt_of(m.arena, wait_slot), m.epoch(),
+                                                 static_cast<unsigned long long>(W));
+        return launch_residual_rmsnorm_quant(m.h, ds, norm, c.eps, m.xq, c.hidden, B, pdl, st);
+    };
     TRY(launch_embed(m.embd, c.hidden, m.tokens, m.pos, m.h, pdl, st, B, tok_stride));
     for (int l = 0; l < L; ++l) {
         const LayerW &y = m.layers[l];
-        TRY(launch_residual_rmsnorm_quant(m.h, l == 0 ? none : one, y.attn_norm, c.eps, m.xq, c.hidden,
-                                          B, pdl, st));
+        TRY(resnorm(l == 0 ? none : one, y.attn_norm, l == 0 ? -1 : 2 * l - 1));
         TRY(tc(y.wqkv, m.xq, m.qkv, qkv_rows, c.hidden, 2));
         TRY(launch_qk_norm_rope_kv(m.qkv, y.q_norm, y.k_norm, c.eps, m.rope, m.pos, m.q,
-                                   m.kc + l * kv_layer, m.vc + l * kv_layer, c.n_heads, c.n_kv_heads,
+                                   m.kc + l * kv_layer, m.vc + l * kv_layer, sh.q_heads, sh.kv_heads,
                                    c.max_ctx, pdl, st, sb));
-        TRY(launch_attention(m.q, m.kc + l * kv_layer, m.vc + l * kv_layer, m.pos, scale, c.n_heads,
-                             c.n_kv_heads, c.max_ctx, m.part_m, m.part_l, m.part_o, m.att, m.oq, pdl,
+        TRY(launch_attention(m.q, m.kc + l * kv_layer, m.vc + l * kv_layer, m.pos, scale, sh.q_heads,
+                             sh.kv_heads, c.max_ctx, m.part_m, m.part_l, m.part_o, m.att, m.oq, pdl,
                              st, sb));
-        TRY(tc(y.wo, m.oq, m.delta, c.hidden, qd, 8));
-        TRY(launch_residual_rmsnorm_quant(m.h, one, y.ffn_norm, c.eps, m.xq, c.hidden, B, pdl, st));
-        TRY(tc(y.wgate, m.xq, m.gbuf, c.ffn, c.hidden, 2));
-        TRY(tc(y.wup, m.xq, m.ubuf, c.ffn, c.hidden, 2));
-        TRY(launch_swiglu_quant(m.gbuf, m.ubuf, m.aq, static_cast<int64_t>(B) * c.ffn, pdl, st));
-        TRY(tc(y.wdown, m.aq, m.delta, c.hidden, c.ffn, 8));
+        if (tp)
+            TRY(kshard(y.wo, m.oq, qd, static_cast<int>(c.n_heads * hd / QK_K), 2 * l));
+        else
+            TRY(tc(y.wo, m.oq, m.delta, c.hidden, qd, 8));
+        TRY(resnorm(one, y.ffn_norm, 2 * l));
+        TRY(tc(y.wgate, m.xq, m.gbuf, ffn, c.hidden, 2));
+        TRY(tc(y.wup, m.xq, m.ubuf, ffn, c.hidden, 2));
+        TRY(launch_swiglu_quant(m.gbuf, m.ubuf, m.aq, static_cast<int64_t>(B) * ffn, pdl, st));
+        if (tp)
+            TRY(kshard(y.wdown, m.aq, ffn, c.ffn / QK_K, 2 * l + 1));
+        else
+            TRY(tc(y.wdown, m.aq, m.delta, c.hidden, ffn, 8));
     }
-    TRY(launch_residual_rmsnorm_quant(m.h, L > 0 ? one : none, m.out_norm, c.eps, m.xq, c.hidden, B,
-                                      pdl, st));
-    TRY(tc(m.embd, m.xq, m.logits, c.vocab, c.hidden, 1));
-    return launch_argmax_batch(m.logits, c.vocab, c.vocab, m.tokens, m.picks, tok_stride, m.pos,
-                               m.nprompt, c.max_ctx, B, pdl, st);
+    TRY(resnorm(L > 0 ? one : none, m.out_norm, L > 0 ? 2 * L - 1 : -1));
+    const size_t row_h = q4k_bytes(1, c.hidden);
+    TRY(tc(m.embd + static_cast<size_t>(sh.vocab_lo) * row_h, m.xq, m.logits, vocab, c.hidden, 1));
+    if (!tp)
+        return launch_argmax_batch(m.logits, c.vocab, c.vocab, m.tokens, m.picks, tok_stride, m.pos,
+                                   m.nprompt, c.max_ctx, B, pdl, st);
+    // each rank's per-sequence keys meet in every rank's key words
+    TpKeyPush push = {};
+    push.npeer = W;
+    for (int q = 0; q < W; ++q) {
+        push.key[q] = m.key_of(m.peer[q]);
+        push.cnt[q] = m.cnt_of(m.peer[q], 2 * L);
+    }
+    push.cta_cnt = m.cta_cnt(2 * L);
+    TRY(launch_argmax_keys_batch(m.logits, static_cast<int>(vocab), vocab, static_cast<int>(sh.vocab_lo), push, B,
+                                 pdl, st));
+    return launch_argmax_finish_batch(m.key_of(m.arena), B, m.tokens, m.picks, tok_stride, m.pos, m.nprompt,
+                                      c.max_ctx, m.cnt_of(m.arena, 2 * L), m.epoch(),
+                                      static_cast<unsigned long long>(W), pdl, st);
 }
 
 // Prefill: the P prompt tokens at tokens[*pos .. *pos + P) of the batch-1
@@ -964,6 +1027,12 @@ int abra_model_create_tp(const abra_model_config *cfg, int32_t rank, int32_t wor
 int abra_model_create_batched(const abra_model_config *cfg, int32_t batch, void **out) {
     if (batch != 1 && batch != 32) return model_fail(ABRA_E_UNSUPPORTED, "batch must be 1 or 32", cudaSuccess);
     return create_model(cfg, 0, 1, batch, out);
+}
+
+int abra_model_create_batched_tp(const abra_model_config *cfg, int32_t batch, int32_t rank, int32_t world,
+                                 void **out) {
+    if (batch != 1 && batch != 32) return model_fail(ABRA_E_UNSUPPORTED, "batch must be 1 or 32", cudaSuccess);
+    return create_model(cfg, rank, world, batch, out);
 }
 
 static int create_model(const abra_model_config *cfg, int32_t rank, int32_t world, int32_t batch,

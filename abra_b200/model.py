@@ -115,17 +115,27 @@ def _check(rc: int, what: str) -> None:
 class BatchedDecodeModel:
     """32 sequences decoded in lockstep at one shared position, every GEMV on
     the tcgen05 tensor cores (abra_model_create_batched); per sequence the
-    logits and tokens equal the batch-1 model's bit for bit."""
+    logits and tokens equal the batch-1 model's bit for bit.  With world > 1
+    this process holds rank ``rank`` of the tensor-parallel split
+    (abra_model_create_batched_tp; handles exchanged as for DecodeModel), and
+    ``logits()`` returns this rank's vocab rows."""
 
-    def __init__(self, batch: int = 32, **config):
+    def __init__(self, batch: int = 32, rank: int = 0, world: int = 1, group=None, **config):
         self.handle = None
         self.batch = batch
         self.cfg = default_config(**config)
+        self.shard = shard_info(rank, world, **config)
         self._destroy = _lib.lib.abra_model_destroy  # still bound at interpreter exit
         h = C.c_void_p()
-        _check(_lib.lib.abra_model_create_batched(C.byref(self.cfg), batch, C.byref(h)),
-               "abra_model_create_batched")
+        if world > 1:
+            _check(_lib.lib.abra_model_create_batched_tp(C.byref(self.cfg), batch, rank, world, C.byref(h)),
+                   "abra_model_create_batched_tp")
+        else:
+            _check(_lib.lib.abra_model_create_batched(C.byref(self.cfg), batch, C.byref(h)),
+                   "abra_model_create_batched")
         self.handle = h
+        if world > 1:
+            DecodeModel._connect(self, group)
 
     def close(self) -> None:
         if self.handle:
@@ -162,7 +172,7 @@ class BatchedDecodeModel:
         return out
 
     def logits(self) -> np.ndarray:
-        out = np.empty((self.batch, self.cfg.vocab), dtype=np.float32)
+        out = np.empty((self.batch, int(self.shard.vocab_hi - self.shard.vocab_lo)), dtype=np.float32)
         _check(_lib.lib.abra_model_read_batched(self.handle, None, 0, out.ctypes.data),
                "abra_model_read_batched")
         return out

@@ -460,6 +460,14 @@ int abra_model_tp_handle(void *model, void *handle, int32_t size);
 /* Map every other rank's arena (handles: world entries of size_each bytes,
  * indexed by rank).  Required before the first step. */
 int abra_model_tp_connect(void *model, const void *handles, int32_t size_each);
+/* This rank's shard of the batch-32 model (abra_model_create_batched split
+ * the same way): every GEMV on the tensor cores over the rank's rows or
+ * K-slices; the o and down partial sums are pushed from the tcgen05 MMVQ's
+ * epilogue into every rank's arena and each sequence's argmax keys meet on
+ * every rank, so the tokens equal the one-GPU batch-32 model's.  Connect
+ * with abra_model_tp_handle / abra_model_tp_connect as above. */
+int abra_model_create_batched_tp(const abra_model_config *cfg, int32_t batch, int32_t rank,
+                                 int32_t world, void **model);
 
 #ifdef __cplusplus
 }

@@ -120,3 +120,67 @@ def test_tp_model_matches_one_gpu(world, cfg, n_steps):
         pytest.skip(f"needs {world} GPUs")
     prompt = np.random.default_rng(world).integers(0, cfg.get("vocab", 151936), 9).astype(np.int32)
     mp.spawn(_tp_worker, args=(world, _free_port(), cfg, n_steps, prompt), nprocs=world, join=True)
+
+
+def _tp_batched_worker(rank, world, port, cfg, n_steps, prompts):
+    import torch
+    import torch.distributed as dist
+
+    import abra_b200 as A
+    from abra_b200.model import BatchedDecodeModel
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=180))
+    m = None
+    try:
+        m = BatchedDecodeModel(batch=32, rank=rank, world=world, **cfg)
+        m.reset(prompts)
+        m.step(n_steps)
+        m.sync()
+        n_prompt = prompts.shape[1]
+        toks = m.tokens(n_prompt + n_steps)
+        logits = m.logits()
+        err = A.device_error()
+        got = [None] * world
+        dist.all_gather_object(got, (toks, logits, err))
+        dist.barrier()  # every rank is done stepping before any arena is freed
+        m.close()
+        m = None
+        dist.barrier()
+        if rank == 0:
+            assert all(g[2] == 0 for g in got), "a bounded cross-rank wait gave up"
+            ref = BatchedDecodeModel(batch=32, **cfg)
+            ref.reset(prompts)
+            ref.step(n_steps)
+            ref.sync()
+            ref_toks = ref.tokens(n_prompt + n_steps)
+            ref_logits = ref.logits()
+            ref.close()
+            for r, g in enumerate(got):
+                assert np.array_equal(g[0], ref_toks), f"rank {r} tokens differ"
+            tp_logits = np.concatenate([g[1] for g in got], axis=1)
+            assert np.array_equal(tp_logits, ref_logits), "logits differ from one GPU"
+    finally:
+        if m is not None:
+            try:
+                dist.barrier()
+            finally:
+                m.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("cfg,n_steps", [(SMALL, 10), (FULL, 6)], ids=["small", "qwen3_4b"])
+def test_tp_batched_model_matches_one_gpu(world, cfg, n_steps):
+    """Batch 32 on the tensor cores split over world GPUs: every sequence's
+    tokens and every logit equal the one-GPU batch-32 model's, bit for bit
+    (o/down partial sums pushed from the tcgen05 MMVQ epilogue, the per-
+    sequence argmax keys merged across ranks)."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    prompts = np.random.default_rng(100 + world).integers(0, cfg.get("vocab", 151936), (32, 5)).astype(np.int32)
+    mp.spawn(_tp_batched_worker, args=(world, _free_port(), cfg, n_steps, prompts), nprocs=world, join=True)
