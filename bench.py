@@ -1027,17 +1027,22 @@ def fused_rmsnorm_block(torch, steps: int, copies: int = 8, seed: int = 0):
     return out
 
 
-def decode_batched(torch, warmup: int, steps: int, batch: int = 32, seed: int = 0):
+def decode_batched(torch, warmup: int, steps: int, batch: int = 32, seed: int = 0, dist=None):
     """Batch-32 decode (32 sequences in lockstep, tcgen05 GEMVs): aggregate
     tok/s over ``steps`` graph replays after the 16-token prompts and
-    ``warmup`` untimed steps, CUDA events on the model's stream."""
+    ``warmup`` untimed steps, CUDA events on the model's stream.  Under
+    torchrun (world > 1) every rank holds its tensor-parallel shard of the
+    batch-32 model and the time is the max over ranks."""
     from abra_b200.model import BatchedDecodeModel
 
-    m = BatchedDecodeModel(batch, max_ctx=PROMPT + warmup + steps, seed=seed)
+    rank, world = (dist.rank, dist.world) if dist else (0, 1)
+    m = BatchedDecodeModel(batch, rank=rank, world=world, max_ctx=PROMPT + warmup + steps, seed=seed)
     prompts = np.random.default_rng(seed).integers(0, m.cfg.vocab, (batch, PROMPT)).astype(np.int32)
     m.reset(prompts)
     m.step(PROMPT - 1 + warmup)
     m.sync()
+    if dist:
+        dist.barrier()
     st = torch.cuda.ExternalStream(m.stream)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(st)
@@ -1046,10 +1051,16 @@ def decode_batched(torch, warmup: int, steps: int, batch: int = 32, seed: int = 
     e.synchronize()
     ms = s.elapsed_time(e) / steps
     toks = m.tokens(PROMPT + warmup + steps)[:, PROMPT:]
+    if dist:
+        dist.barrier()  # peers push into this rank's arena until they finish
+        ms = dist.max(ms)
     m.close()
     return {"batch": batch, "depth": 0, "ms_per_step": round(ms, 4),
             "tok_s_aggregate": round(batch * 1000.0 / ms, 1), "tokens_head_seq0": toks[0, :8].tolist(),
-            "path": "abra_model_create_batched: every GEMV on tcgen05 kind::i8 (abra_q4k_mmvq_tc)"}
+            "parallelism": f"tp{world}" if world > 1 else "single GPU",
+            "path": ("abra_model_create_batched_tp: every GEMV on tcgen05 kind::i8, o/down partial sums pushed "
+                     "from the MMVQ epilogue over NVLink" if world > 1 else
+                     "abra_model_create_batched: every GEMV on tcgen05 kind::i8 (abra_q4k_mmvq_tc)")}
 
 
 def decode_alg_bytes(res: dict, vocab: int = 151936) -> int:
@@ -1104,6 +1115,9 @@ def decode_main(a, dist):
                             "frac": round(sw.bytes / (ms_sw * 1e-3) / 1e9 / peak, 4),
                             "ms_per_step": round(ms_sw, 4), "launches_per_step": sw.launches}
     cpu = None
+    if dist.world > 1:
+        # batch 32 on the tensor cores, tensor parallel over the same ranks
+        extras["decode_b32"] = decode_batched(torch, a.warmup, a.steps, dist=dist)
     if dist.world == 1:
         # the same token through the per-operation kernel chain
         from abra_b200.model import KERNEL_CHAIN, Q4_K_M
