@@ -107,13 +107,14 @@ cudaError_t launch_mmvq_q4k_partials(const void *w, const void *x_q8, float *y, 
 // columns, ks k-parts (1, 2, 4, 8) over the canonical slices; ks > 1 needs
 // part = ks * 32 * N floats of scratch and adds a combine launch.
 // A K-shard and tensor-parallel push for one tcgen05 MMVQ launch (off by
-// default).  part >= 0: the launch holds exactly k-part `part` of a ks-way
-// split of a K of nsb_sl superblocks (its first superblock is sb_base) and
-// writes that part's slice-tree top to y, or pushes it (npeer > 0) to every
-// peer_y[q] and counts on cta_cnt; the launch's last CTA adds 1 to each
-// peer_cnt[q] with release semantics at system scope.
+// default).  part >= 0: the launch holds exactly k-parts [part, part +
+// nparts) of a ks-way split of a K of nsb_sl superblocks (its first
+// superblock is sb_base) and writes the tree over them (the shard's subtree
+// of the slice tree) to y, or pushes it (npeer > 0) to every peer_y[q] and
+// counts on cta_cnt; the launch's last CTA adds 1 to each peer_cnt[q] with
+// release semantics at system scope.  nparts > 1 needs the part workspace.
 struct TcOpts {
-    int nsb_sl = 0, sb_base = 0, part = -1;
+    int nsb_sl = 0, sb_base = 0, part = -1, nparts = 1;
     int npeer = 0;
     float *peer_y[8] = {};
     unsigned long long *peer_cnt[8] = {};

@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 else
                     prm.Y[at] = v;
             } else {
-                prm.part[(static_cast<int64_t>(j) * TC_N + col) * N + row0 + rloc] = v;
+                prm.part[(static_cast<int64_t>(j - prm.j_base) * TC_N + col) * N + row0 + rloc] = v;
             }
         }
     }
@@ -372,10 +372,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
-// y[c][n] = tree over the KS k-part partials (the top of the slice tree).
+// Where a combine kernel sends its rows (tensor parallel), as TcParams.
+struct TcPush {
+    int npeer;
+    float *peer_y[8];
+    unsigned long long *peer_cnt[8];
+    unsigned long long *cta_cnt;
+};
+
+// y[c][n] = tree over the KS k-part partials (the top of the slice tree, or
+// of a K-shard's subtree); with push.npeer > 0 the rows go to every
+// peer_y[q] instead and the launch's last CTA publishes to every rank.
 template <int KS>
 __global__ void __launch_bounds__(256) mmvq_tc_combine_kernel(const float *__restrict__ part, float *__restrict__ Y,
-                                                              int N, int64_t ldy) {
+                                                              int N, int64_t ldy, const TcPush push) {
     pdl_wait();
     pdl_launch_dependents();
     const int64_t total = static_cast<int64_t>(TC_N) * N;
@@ -394,7 +404,18 @@ __global__ void __launch_bounds__(256) mmvq_tc_combine_kernel(const float *__res
             y = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
                           __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
         }
-        Y[c * ldy + n] = y;
+        if (push.npeer > 0)
+            for (int q = 0; q < push.npeer; ++q) push.peer_y[q][c * ldy + n] = y;
+        else
+            Y[c * ldy + n] = y;
+    }
+    if (push.npeer > 0) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned long long old = atom_add_acq_rel_gpu(push.cta_cnt, 1ull);
+            if ((old + 1ull) % gridDim.x == 0ull)
+                for (int q = 0; q < push.npeer; ++q) red_release_sys_add(push.peer_cnt[q], 1ull);
+        }
     }
 }
 
@@ -432,30 +453,41 @@ cudaError_t prepare_mmvq_tc() {
 cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N, int64_t K,
                            int64_t ldy, int ks, float *part, int flags, cudaStream_t stream,
                            const TcOpts *opt) {
-    const bool single = opt && opt->part >= 0;  // one k-part of a ks-way split, straight to y
+    const bool shard = opt && opt->part >= 0;          // k-parts [part, part + nparts) of a ks-way split
+    const int nparts = shard ? opt->nparts : ks;
+    const bool single = shard && nparts == 1;          // one k-part, straight to y
     if (K % QK_K || K <= 0 || N <= 0 || ldy < N || !(ks == 1 || ks == 2 || ks == 4 || ks == 8) ||
-        (ks > 1 && !part && !single) || (opt && (opt->npeer < 0 || opt->npeer > 8)) ||
-        (opt && opt->npeer > 0 && !opt->cta_cnt))
+        !(nparts == 1 || nparts == 2 || nparts == 4 || nparts == 8) || (nparts > 1 && !part) ||
+        (opt && (opt->npeer < 0 || opt->npeer > 8)) || (opt && opt->npeer > 0 && !opt->cta_cnt))
         return cudaErrorInvalidValue;
     TcParams prm = {};
     const int nsb_local = static_cast<int>(K / QK_K);
     prm.nsb_sl = opt && opt->nsb_sl > 0 ? opt->nsb_sl : nsb_local;
     prm.sb_base = opt ? opt->sb_base : 0;
-    prm.j_base = single ? opt->part : 0;
+    prm.j_base = shard ? opt->part : 0;
     prm.direct = single ? 1 : 0;
-    if (single && (opt->part >= ks || slice_start(prm.nsb_sl, opt->part * (8 / ks)) != prm.sb_base ||
-                   slice_start(prm.nsb_sl, (opt->part + 1) * (8 / ks)) - prm.sb_base != nsb_local))
-        return cudaErrorInvalidValue;  // the shard must be exactly the k-part's slices
-    if (!single && prm.nsb_sl != nsb_local) return cudaErrorInvalidValue;
+    if (shard && (opt->part + nparts > ks || slice_start(prm.nsb_sl, opt->part * (8 / ks)) != prm.sb_base ||
+                  slice_start(prm.nsb_sl, (opt->part + nparts) * (8 / ks)) - prm.sb_base != nsb_local))
+        return cudaErrorInvalidValue;  // the shard must be exactly its k-parts' slices
+    if (!shard && prm.nsb_sl != nsb_local) return cudaErrorInvalidValue;
+    TcPush push = {};
     if (opt && opt->npeer > 0) {
-        prm.npeer = opt->npeer;
+        if (ks > 1 && !shard) return cudaErrorInvalidValue;
+        push.npeer = opt->npeer;
         for (int q = 0; q < opt->npeer; ++q) {
             if (!opt->peer_y[q] || !opt->peer_cnt[q]) return cudaErrorInvalidValue;
-            prm.peer_y[q] = opt->peer_y[q];
-            prm.peer_cnt[q] = opt->peer_cnt[q];
+            push.peer_y[q] = opt->peer_y[q];
+            push.peer_cnt[q] = opt->peer_cnt[q];
         }
-        prm.cta_cnt = opt->cta_cnt;
-        if (ks > 1 && !single) return cudaErrorInvalidValue;  // the push is the launch's own output
+        push.cta_cnt = opt->cta_cnt;
+        if (single || ks == 1) {  // the MMVQ's own epilogue pushes
+            prm.npeer = push.npeer;
+            for (int q = 0; q < push.npeer; ++q) {
+                prm.peer_y[q] = push.peer_y[q];
+                prm.peer_cnt[q] = push.peer_cnt[q];
+            }
+            prm.cta_cnt = push.cta_cnt;
+        }
     }
     prm.W = static_cast<const uint8_t *>(w);
     prm.X = static_cast<const uint8_t *>(x_q8);
@@ -496,7 +528,7 @@ cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N,
         attr_set[dev][ki] = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((N + TC_M - 1) / TC_M), static_cast<unsigned>(single ? 1 : ks));
+    cfg.gridDim = dim3(static_cast<unsigned>((N + TC_M - 1) / TC_M), static_cast<unsigned>(nparts));
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -507,15 +539,15 @@ cudaError_t launch_mmvq_tc(const void *w, const void *x_q8, float *y, int64_t N,
     cfg.numAttrs = (flags & MMVQ_PDL) ? 1 : 0;
     e = cudaLaunchKernelEx(&cfg, fn, prm, wmap);
     if (e != cudaSuccess || ks == 1 || single) return e;
-    void (*cfn)(const float *, float *, int, int64_t) = ks == 2 ? mmvq_tc_combine_kernel<2>
-                                                       : ks == 4 ? mmvq_tc_combine_kernel<4>
-                                                                 : mmvq_tc_combine_kernel<8>;
+    void (*cfn)(const float *, float *, int, int64_t, const TcPush) = nparts == 2 ? mmvq_tc_combine_kernel<2>
+                                                                    : nparts == 4 ? mmvq_tc_combine_kernel<4>
+                                                                                  : mmvq_tc_combine_kernel<8>;
     cudaLaunchConfig_t c2 = cfg;
     const int64_t total = static_cast<int64_t>(TC_N) * N;
     c2.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 8)));
     c2.blockDim = dim3(256);
     c2.dynamicSmemBytes = 0;
-    return cudaLaunchKernelEx(&c2, cfn, static_cast<const float *>(part), y, static_cast<int>(N), ldy);
+    return cudaLaunchKernelEx(&c2, cfn, static_cast<const float *>(part), y, static_cast<int>(N), ldy, push);
 }
 
 }  // namespace abra

@@ -498,22 +498,23 @@ static cudaError_t record_step_batched(const Model &m, cudaStream_t st) {
         return launch_mmvq_tc(w, x, y, N, K, N, ks, m.tc_ws, pf, st);
     };
     // Tensor parallel: o and down are K-sharded on canonical slices, so a
-    // rank's output is k-part `rank` of a W-way split; it is pushed into slot
-    // `slot` of every rank's arena, and the next residual + RMSNorm waits for
-    // all W and adds them in the fixed tree (bit-identical to one GPU)
-    const int part = tp ? sh.sl_base / sh.sl_cnt : 0;
+    // rank's output is the subtree over its k-parts sl_base .. sl_base +
+    // sl_cnt - 1 of the 8-way split; it is pushed into slot `slot` of every
+    // rank's arena, and the next residual + RMSNorm waits for all W and adds
+    // them in the fixed tree (bit-identical to one GPU)
     auto kshard = [&](const void *w, const void *x, int64_t K, int nsb_full, int slot) {
         TcOpts o;
         o.nsb_sl = nsb_full;
         o.sb_base = slice_start(nsb_full, sh.sl_base);
-        o.part = part;
+        o.part = sh.sl_base;
+        o.nparts = sh.sl_cnt;
         o.npeer = W;
         for (int q = 0; q < W; ++q) {
             o.peer_y[q] = m.recv_of(m.peer[q], sh.rank, slot);
             o.peer_cnt[q] = m.cnt_of(m.peer[q], slot);
         }
         o.cta_cnt = m.cta_cnt(slot);
-        return launch_mmvq_tc(w, x, nullptr, c.hidden, K, c.hidden, W, nullptr, pf, st, &o);
+        return launch_mmvq_tc(w, x, nullptr, c.hidden, K, c.hidden, 8, m.tc_ws, pf, st, &o);
     };
     auto slot_deltas = [&](int slot) {
         DeltaSet d = {};
