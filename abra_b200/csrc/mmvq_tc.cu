@@ -120,6 +120,16 @@ struct SliceTree {
     }
 };
 
+// Exact int32 -> fp32 for |x| < 2^22 on the full-rate pipes (the magic-
+// number conversion): x added to the bits of 1.5 * 2^23 lands in the low
+// mantissa bits of a float of exponent 23, and subtracting 1.5 * 2^23 leaves
+// x exactly -- the value __int2float_rn gives, without the conversion unit,
+// whose lower throughput bounds this epilogue (64 conversions per thread per
+// superblock).  |P_s * sc_s| <= 32 * 15 * 127 * 63 < 2^22.
+__device__ __forceinline__ float i2f_small(int x) {
+    return __fsub_rn(__int_as_float(0x4B400000 + x), 12582912.0f);
+}
+
 // One 2-D tiled TMA load of box (x bytes, y rows) into this CTA's shared memory.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar, uint64_t policy) {
@@ -299,8 +309,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const float va1[8] = {a1a.x, a1a.y, a1a.z, a1a.w, a1b.x, a1b.y, a1b.z, a1b.w};
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
-                    const float t0 = __fmul_rn(vd0[c], __int2float_rn(P[2 * pp][c] * sc0));
-                    const float t1 = __fmul_rn(vd1[c], __int2float_rn(P[2 * pp + 1][c] * sc1));
+                    const float t0 = __fmul_rn(vd0[c], i2f_small(P[2 * pp][c] * sc0));
+                    const float t1 = __fmul_rn(vd1[c], i2f_small(P[2 * pp + 1][c] * sc1));
                     const float tp = __fadd_rn(t0, t1);
                     const float up = __fadd_rn(__fmul_rn(va0[c], fm0), __fmul_rn(va1[c], fm1));
                     tph[half][c] = pp == 0 ? tp : __fadd_rn(tph[half][c], tp);
