@@ -93,7 +93,7 @@ struct PersistModel {
     const uint8_t *embd;
     const float *out_norm;
     float *h0, *h1, *delta, *qkv, *att, *part_m, *part_l, *part_o, *act, *logits;
-    uint8_t *oq, *aq;  // Q8_1 of the attention output, of the SwiGLU output
+    uint8_t *oq;
     void *kc, *vc;  // fp16 caches [layer][kv head][max_ctx][128]
     const float *rope;
     int32_t *tokens, *picks, *pos;

@@ -100,7 +100,7 @@ struct PkParams {
     float eps, scale;
     float *h[2];
     float *delta, *qkv, *att, *part_m, *part_l, *part_o, *act, *logits;
-    uint8_t *oq, *aq;  // Q8_1 of the attention output and of the SwiGLU output
+    uint8_t *oq;
     __half *kc, *vc;
     const float *rope;
     int32_t *tokens, *picks, *pos;
@@ -110,7 +110,6 @@ struct PkParams {
     unsigned *head_cnt;             // merge arrivals per attention item's first q head
     int lr[PK_KINDS], pitch[PK_KINDS];  // log2 rows per unit and staged row pitch per GEMV kind
     int slot_shift;                     // log2 of the ring slots (4: 16 slots, 3: 8)
-    int gu_smem;                        // the SwiGLU rows of a CTA fit its scratch
     int off_vbuf, off_arec, off_x, off_ring, smem;  // dynamic shared memory layout
 };
 
@@ -192,7 +191,6 @@ __device__ __forceinline__ void pk_wait(const unsigned long long *bar, unsigned 
 struct PkMm {
     const uint8_t *w0, *w1;
     int N, nsb, lr, pitch;
-    int align;  // units per group a CTA's range is aligned to (gate/up: one 32-row Q8_1 block)
 };
 
 // GEMV kind of producer phase ph (per layer q|k|v, o, gate/up, down; then
@@ -205,7 +203,6 @@ __device__ __forceinline__ PkMm pk_mm(const PkParams &P, int layer, int kind) {
     mm.w1 = nullptr;
     mm.lr = P.lr[kind];
     mm.pitch = P.pitch[kind];
-    mm.align = kind == PK_GU ? QK8_1 >> mm.lr : 1;
     const int nsb_h = P.hidden / QK_K;
     if (kind == PK_OUT) {
         mm.w0 = P.embd;
@@ -235,16 +232,11 @@ __device__ __forceinline__ PkMm pk_mm(const PkParams &P, int layer, int kind) {
     return mm;
 }
 
-// This CTA's contiguous share [u_begin, u_begin + nu) of the GEMV's units,
-// in whole groups of mm.align units (gate/up: whole 32-row blocks, which the
-// CTA then quantizes itself).
+// This CTA's contiguous share [u_begin, u_begin + nu) of the GEMV's units.
 __device__ __forceinline__ void pk_range(const PkMm &mm, int &u_begin, int &nu) {
     const int total = (mm.N + (1 << mm.lr) - 1) >> mm.lr;
-    const int groups = (total + mm.align - 1) / mm.align;
-    const int g0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * groups / gridDim.x);
-    const int g1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * groups / gridDim.x);
-    u_begin = g0 * mm.align;
-    nu = min(total, g1 * mm.align) - u_begin;
+    u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * total / gridDim.x);
+    nu = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x) - u_begin;
 }
 
 // ----------------------------------------------------------- producer ---
@@ -574,37 +566,6 @@ __device__ __forceinline__ void pk_quant_f32(const float *x, int K, uint8_t *are
         pk_quant_block(arec, i, v);
     }
     cta_sync();
-}
-
-// One 32-value block x (a lane's value each) to its Q8_1 record at dst: the
-// reference rounding (d = amax / 127, q = roundf(x / d)) and layout (d and
-// d * sum as fp16, then the 32 quants), as quantize_block_warp.
-__device__ __forceinline__ void pk_quant_rec(const float *x, uint8_t *dst, int lane) {
-    const float v = x[lane];
-    float amax = fabsf(v);
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-    amax = fmaxf(0.0f, amax);
-    const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    const int q = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(v, id)))));
-    int sum = q;
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-    // lane k (< 8) gathers quants 4k .. 4k + 3 into word k + 1
-    uint32_t word = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int qj = __shfl_sync(0xffffffffu, q, (4 * lane + j) & 31);
-        word |= (static_cast<uint32_t>(qj) & 0xffu) << (8 * j);
-    }
-    uint32_t *o32 = reinterpret_cast<uint32_t *>(dst);
-    if (lane < 8) o32[1 + lane] = word;
-    if (lane == 8) {
-        const uint32_t hd = __half_as_ushort(__float2half_rn(d));
-        const uint32_t hs = __half_as_ushort(__float2half_rn(__fmul_rn(d, static_cast<float>(sum))));
-        o32[0] = hd | (hs << 16);
-    }
 }
 
 // Q8_1 blocks written earlier in this launch (oq) into the records (the
@@ -1050,7 +1011,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         } else if (ph == PH_O) {
             pk_stage_q8(P.oq, P.n_heads * 128, arec);
         } else if (ph == PH_DOWN) {
-            pk_stage_q8(P.aq, P.ffn, arec);
+            pk_quant_f32(P.act, P.ffn, arec);
         }
         if (t == 0) PK_STAMP(3, e);
 #ifdef ABRA_PK_TRACE
@@ -1065,15 +1026,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
                 pk_attention<GQ>(P, l, pos, GQ, scr, &s_flag);
         } else {
             const int kind = ph == PH_QKV ? PK_QKV : ph == PH_O ? PK_O : ph == PH_GU ? PK_GU : ph == PH_DOWN ? PK_DOWN : PK_OUT;
+            float *Y = ph == PH_QKV ? P.qkv : ph == PH_GU ? P.act : ph == PH_OUT ? P.logits : P.delta;
             const PkMm mm = pk_mm(P, l, kind);
             int u_begin, nu;
             pk_range(mm, u_begin, nu);
-            // the SwiGLU rows stay in this CTA's shared memory (its whole
-            // 32-row blocks), quantized below
-            float *Y = ph == PH_QKV ? P.qkv
-                       : ph == PH_GU ? (P.gu_smem ? scr - (static_cast<int64_t>(u_begin) << mm.lr) : P.act)
-                       : ph == PH_OUT ? P.logits
-                                      : P.delta;
 #ifdef ABRA_PK_TRACE
             if (t == 0) g_pk_gemv = (l == 1 || ph == PH_OUT) ? kind : 99;
             cta_sync();
@@ -1086,18 +1042,6 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             T += static_cast<uint32_t>(nu);
         }
         cta_sync();
-        if (ph == PH_GU) {
-            // this CTA's 32-row blocks of the SwiGLU output to Q8_1 records
-            // in global memory (the bytes quantize_q8_1_kernel writes), one
-            // block per warp, before the arrival publishes them
-            const PkMm mm = pk_mm(P, l, PK_GU);
-            int u_begin, nu;
-            pk_range(mm, u_begin, nu);
-            const int b0 = (u_begin << mm.lr) / QK8_1, nb = (nu << mm.lr) / QK8_1;
-            const float *rows = P.gu_smem ? scr : P.act + static_cast<int64_t>(b0) * QK8_1;
-            for (int b = t >> 5; b < nb; b += PK_NCW) pk_quant_rec(rows + b * QK8_1, P.aq + (b0 + b) * Q81_BYTES, t & 31);
-            cta_sync();
-        }
         if (t == 0) PK_STAMP(1, e);
 #ifdef ABRA_PK_TRACE
         if (t == 0 && e < PK_TRACE_EV && blockIdx.x < 160) g_pk_trace[blockIdx.x][4][e] = g_pk_wait_ns;
@@ -1139,7 +1083,6 @@ PkKernel pk_kernel_for(int gq) {
 struct PkPlan {
     int rows[PK_KINDS], pitch[PK_KINDS];
     int slot_shift;
-    bool gu_smem;
     int off_vbuf, off_arec, off_x, off_ring, smem;
 };
 
@@ -1190,10 +1133,6 @@ bool pk_plan(int hidden, int n_heads, int n_kv, int ffn, int head_dim, int vocab
     }
     const int nsb_max = std::max(std::max(hidden, n_heads * 128), ffn) / QK_K;
     const int scratch = std::max(8 * hidden, 4 * pk_att_floats(gq));
-    // gate/up: a CTA's whole 32-row blocks of SwiGLU output wait in the
-    // scratch when they fit (else in global memory, read back by the CTA)
-    const int64_t gu_blocks = (ffn / QK8_1 + sms - 1) / sms;
-    pl.gu_smem = gu_blocks * QK8_1 * 4 <= scratch;
     int o = 16 * PK_NSLOT;  // full + empty mbarriers (room for 16 slots)
     pl.off_vbuf = pk_align(o, 16);
     o = pl.off_vbuf + PK_NCW * PK_VMAX * 4;
@@ -1264,7 +1203,6 @@ cudaError_t launch_persist_step(const PersistModel &pm, cudaStream_t st) {
     P.act = pm.act;
     P.logits = pm.logits;
     P.oq = pm.oq;
-    P.aq = pm.aq;
     P.kc = static_cast<__half *>(pm.kc);
     P.vc = static_cast<__half *>(pm.vc);
     P.rope = pm.rope;
@@ -1282,7 +1220,6 @@ cudaError_t launch_persist_step(const PersistModel &pm, cudaStream_t st) {
         P.pitch[k] = pl.pitch[k];
     }
     P.slot_shift = pl.slot_shift;
-    P.gu_smem = pl.gu_smem ? 1 : 0;
     P.off_vbuf = pl.off_vbuf;
     P.off_arec = pl.off_arec;
     P.off_x = pl.off_x;
@@ -1327,14 +1264,7 @@ bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn
             const int N = rows[kind], R = pl.rows[kind], pitch = pl.pitch[kind];
             const int64_t row_bytes = static_cast<int64_t>(nsb[kind]) * Q4K_BYTES;
             const int64_t total = (N + R - 1) / R;
-            // pk_range: gate/up ranges in whole 32-row blocks
-            const int64_t align = kind == PK_GU ? QK8_1 / R : 1, groups = (total + align - 1) / align;
-            const int u0 = static_cast<int>(b * groups / sms * align);
-            const int u1 = static_cast<int>(std::min<int64_t>(total, (b + 1) * groups / sms * align));
-            if (kind == PK_GU && ((pl.gu_smem && static_cast<int64_t>(u1 - u0) * R * 4 >
-                                                     std::max(8 * hidden, 4 * pk_att_floats(n_heads / n_kv))) ||
-                                  N % QK8_1 != 0))
-                return fail("a CTA's SwiGLU rows do not fit its scratch");
+            const int u0 = static_cast<int>(b * total / sms), u1 = static_cast<int>((b + 1) * total / sms);
             if (nmat[kind] * R * nsb[kind] > PK_VMAX || (R != 1 && R != 2 && R != 4 && R != 8))
                 return fail("unit exceeds the staging buffer");
             for (int u = u0; u < u1; ++u, ++t) {

@@ -727,7 +727,6 @@ static PersistModel persist_model(const Model &m) {
     pm.act = m.act;
     pm.logits = m.logits;
     pm.oq = m.oq;
-    pm.aq = m.aq;
     pm.kc = m.kc;
     pm.vc = m.vc;
     pm.rope = m.rope;
