@@ -31,12 +31,14 @@ from .q4k import (
     load_tuning_table,
     mmvq,
     mmvq_kshard,
+    mmvq_packed,
     mmvq_partials,
     mmvq_rmsnorm,
     mmvq_swiglu,
     mmvq_tc,
     plan_info,
     q4k_nbytes,
+    pack_q4k,
     q8_1_nbytes,
     register_autotuned_table_entry,
     rmsnorm_quantize_q8_1,

@@ -27,6 +27,8 @@ SIGNATURES: dict[str, tuple] = {
     "abra_device_error": (C.c_int, [C.POINTER(C.c_uint32), _i32]),
     "abra_test_flag_timeout": (C.c_int, [C.POINTER(C.c_uint32), C.POINTER(C.c_uint64)]),
     "abra_q4k_mmvq": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _vp]),
+    "abra_q4k_pack": (C.c_int, [_vp, _vp, _i64, _vp]),
+    "abra_q4k_mmvq_packed": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _i32, _vp]),
     "abra_q4k_mmvq_candidate": (C.c_int, [_i32, _vp, _vp, _fp, _i64, _i64, _i32, _vp]),
     "abra_q4k_mmvq_ex": (C.c_int, [_vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _i32, _vp]),
     "abra_q4k_mmvq_swiglu": (C.c_int, [_vp, _vp, _vp, _fp, _i64, _i64, _i32, _i64, _i32, _i32, _vp]),

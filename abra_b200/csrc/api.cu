@@ -141,6 +141,34 @@ int abra_q4k_mmvq_swiglu(const void *w_gate, const void *w_up, const void *x, fl
     return mmvq_common(w_gate, w_up, x, y, N, K, ncols, ldy, candidate, flags, stream);
 }
 
+int abra_q4k_pack(const void *w, void *w_packed, int64_t nblocks, void *stream) {
+    if (!w || !w_packed) return fail(ABRA_E_INVALID, "null pointer");
+    if (nblocks <= 0) return fail(ABRA_E_INVALID, "nblocks must be positive");
+    if (!aligned16(w) || !aligned16(w_packed)) return fail(ABRA_E_INVALID, "weights must be 16-byte aligned");
+    cudaError_t e = abra::launch_q4k_pack(w, w_packed, nblocks, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "pack launch");
+    return ABRA_OK;
+}
+
+int abra_q4k_mmvq_packed(const void *w_packed, const void *x, float *y, int64_t N, int64_t K, int32_t flags,
+                         void *stream) {
+    int rc = check_mmvq_args(w_packed, x, y, N, K, 1, N);
+    if (rc) return rc;
+    // the lane-mapped kernel, 2 CTAs per SM, the largest unit whose copies
+    // stay 16-byte aligned for this width
+    for (int id : {4082, 4042, 4022}) {
+        const abra::MmvqConfig *cfg = abra::mmvq_candidate_by_id(id);
+        int64_t pl[8];
+        if (!cfg || !abra::mmvq_lane_plan(*cfg, N, static_cast<int>(K / abra::QK_K), 1, 0, pl, true)) continue;
+        cudaError_t e = abra::launch_mmvq_lane(*cfg, w_packed, nullptr, x, y, N, K,
+                                               (flags & ABRA_MMVQ_PDL) ? abra::MMVQ_PDL : 0,
+                                               static_cast<cudaStream_t>(stream), nullptr, true);
+        if (e != cudaSuccess) return cuda_fail(e, "packed mmvq launch");
+        return ABRA_OK;
+    }
+    return fail(ABRA_E_UNSUPPORTED, "no packed plan for N=%lld K=%lld", (long long)N, (long long)K);
+}
+
 int abra_q4k_mmvq(const void *w, const void *x, float *y, int64_t N, int64_t K, int32_t ncols,
                   void *stream) {
     return abra_q4k_mmvq_ex(w, x, y, N, K, ncols, N, 0, 0, stream);

@@ -80,10 +80,15 @@ struct MmvqXin {
 // The lane-mapped batch-1 kernel (mmvq_lane.cu): plan out = {grid, block,
 // ring slots, slot bytes, shared memory, log2 rows per unit, activation and
 // ring offsets}; false when the shape does not fit the candidate.
-bool mmvq_lane_plan(const MmvqConfig &cfg, int64_t N, int nsb, int nmat, int sms, int64_t out[8]);
+// packed: the weights are the 148-byte prepacked form (launch_q4k_pack).
+bool mmvq_lane_plan(const MmvqConfig &cfg, int64_t N, int nsb, int nmat, int sms, int64_t out[8],
+                    bool packed = false);
 cudaError_t prepare_mmvq_lane(const MmvqConfig &cfg, int nmat);  // kernel attributes, outside a capture
 cudaError_t launch_mmvq_lane(const MmvqConfig &cfg, const void *w, const void *w2, const void *x_q8, float *y,
-                             int64_t N, int64_t K, int flags, cudaStream_t stream, unsigned long long *amax);
+                             int64_t N, int64_t K, int flags, cudaStream_t stream, unsigned long long *amax,
+                             bool packed = false);
+// Q4_K superblocks -> the reference's 148-byte prepacked form.
+cudaError_t launch_q4k_pack(const void *w, void *w_packed, int64_t nblocks, cudaStream_t stream);
 // The candidate a MODE_LANE candidate stands for where the lane kernel does
 // not apply (batch > 1, fused input, tensor-parallel options); others as given.
 const MmvqConfig &mmvq_classic(const MmvqConfig &cfg);

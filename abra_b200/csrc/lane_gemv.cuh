@@ -81,6 +81,68 @@ __device__ __forceinline__ void pk_sb_value(const uint8_t *const (&wsb)[NMAT], c
     }
 }
 
+// The reference's 148-byte packed superblock (kernels/q4k/abra-packed-q4.cuh:
+// 3-8): fp16 d and dmin, then for each pair j of sub-blocks one 32-bit word of
+// bytes [sc_2j, sc_2j+1, m_2j, m_2j+1] (the 6-bit scales and mins unpacked),
+// then the 128 bytes of nibbles.  Rows of packed superblocks are only 4-byte
+// aligned, so everything is read as 32-bit words.
+constexpr int LG_PACKED_BYTES = 148;
+
+// pk_sb_value on packed superblocks: the same integers (the unpacked bytes
+// equal scale_min_pair's), the same fp32 operations in the same order.
+template <int NMAT>
+__device__ __forceinline__ void pk_sb_value_packed(const uint8_t *const (&wsb)[NMAT], const uint8_t *arec,
+                                                   float (&v)[NMAT]) {
+    uint32_t dm[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) dm[m] = *reinterpret_cast<const uint32_t *>(wsb[m]);
+    float t[NMAT][8], u[NMAT][8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float2 d8 = *reinterpret_cast<const float2 *>(arec + 256 + 8 * q);
+        const float2 A = *reinterpret_cast<const float2 *>(arec + 288 + 8 * q);
+        const uint4 a0 = *reinterpret_cast<const uint4 *>(arec + 64 * q);
+        const uint4 a1 = *reinterpret_cast<const uint4 *>(arec + 64 * q + 16);
+        const uint4 a2 = *reinterpret_cast<const uint4 *>(arec + 64 * q + 32);
+        const uint4 a3 = *reinterpret_cast<const uint4 *>(arec + 64 * q + 48);
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            const uint32_t *w32 = reinterpret_cast<const uint32_t *>(wsb[m]);
+            const uint32_t smp = w32[1 + q];
+            const int sc0 = smp & 0xff, sc1 = (smp >> 8) & 0xff, m0 = (smp >> 16) & 0xff, m1 = smp >> 24;
+            uint32_t qw[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) qw[k] = w32[5 + 8 * q + k];
+            const int lo[8] = {static_cast<int>(a0.x), static_cast<int>(a0.y), static_cast<int>(a0.z),
+                               static_cast<int>(a0.w), static_cast<int>(a1.x), static_cast<int>(a1.y),
+                               static_cast<int>(a1.z), static_cast<int>(a1.w)};
+            const int hi[8] = {static_cast<int>(a2.x), static_cast<int>(a2.y), static_cast<int>(a2.z),
+                               static_cast<int>(a2.w), static_cast<int>(a3.x), static_cast<int>(a3.y),
+                               static_cast<int>(a3.z), static_cast<int>(a3.w)};
+            int s0 = 0, s1 = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                s0 = dp4a_ss(static_cast<int>(qw[k] & 0x0F0F0F0Fu), lo[k], s0);
+                s1 = dp4a_us(qw[k] & 0xF0F0F0F0u, hi[k], s1);
+            }
+            s1 >>= 4;  // exact: the masked high nibbles carry a factor of 16
+            t[m][2 * q] = __fmul_rn(d8.x, __int2float_rn(s0 * sc0));
+            t[m][2 * q + 1] = __fmul_rn(d8.y, __int2float_rn(s1 * sc1));
+            u[m][2 * q] = __fmul_rn(A.x, static_cast<float>(m0));
+            u[m][2 * q + 1] = __fmul_rn(A.y, static_cast<float>(m1));
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+        const float St = __fadd_rn(__fadd_rn(__fadd_rn(t[m][0], t[m][1]), __fadd_rn(t[m][2], t[m][3])),
+                                   __fadd_rn(__fadd_rn(t[m][4], t[m][5]), __fadd_rn(t[m][6], t[m][7])));
+        const float Su = __fadd_rn(__fadd_rn(__fadd_rn(u[m][0], u[m][1]), __fadd_rn(u[m][2], u[m][3])),
+                                   __fadd_rn(__fadd_rn(u[m][4], u[m][5]), __fadd_rn(u[m][6], u[m][7])));
+        const float d = half_lo(dm[m]), dmin = half_hi(dm[m]);
+        v[m] = __fmaf_rn(d, St, -__fmul_rn(dmin, Su));
+    }
+}
+
 // Sum of canonical K-slice i of a row from its staged superblock values
 // (sequential within the slice).
 __device__ __forceinline__ float pk_slice_sum(const float *vrow, int nsb, int i) {

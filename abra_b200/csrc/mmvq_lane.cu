@@ -37,15 +37,16 @@ struct LaneParams {
     int off_vbuf, off_arec, off_ring;
 };
 
-template <int NMAT, int MINB>
+template <int NMAT, int MINB, bool PACKED>
 __global__ void __launch_bounds__((LN_NCW + 1) * 32, MINB) mmvq_lane_kernel(const LaneParams prm) {
+    constexpr int SB = PACKED ? LG_PACKED_BYTES : Q4K_BYTES;  // bytes per superblock
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ unsigned long long s_amax;
     const int nslot = prm.nslot, nsb = prm.nsb, lr = prm.lr, R = 1 << lr, N = prm.N;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + nslot;
     uint8_t *ring = smem + prm.off_ring;
-    const int row_bytes = nsb * Q4K_BYTES;
+    const int row_bytes = nsb * SB;
     const int total = (N + R - 1) >> lr;
     const int u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * total / gridDim.x);
     const int nu = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x) - u_begin;
@@ -133,9 +134,12 @@ __global__ void __launch_bounds__((LN_NCW + 1) * 32, MINB) mmvq_lane_kernel(cons
         for (int b = p; b < nsb; b += P) {
             const uint8_t *wsb[NMAT];
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) wsb[m] = wrow[m] + b * Q4K_BYTES;
+            for (int m = 0; m < NMAT; ++m) wsb[m] = wrow[m] + b * SB;
             float v[NMAT];
-            pk_sb_value<NMAT>(wsb, arec + b * LG_AREC, v);
+            if constexpr (PACKED)
+                pk_sb_value_packed<NMAT>(wsb, arec + b * LG_AREC, v);
+            else
+                pk_sb_value<NMAT>(wsb, arec + b * LG_AREC, v);
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) vbuf[(m * R + r) * nsb + b] = v[m];
         }
@@ -179,21 +183,48 @@ __global__ void __launch_bounds__((LN_NCW + 1) * 32, MINB) mmvq_lane_kernel(cons
 
 using LaneFn = void (*)(const LaneParams);
 
-LaneFn lane_kernel(int nmat, int minb) {
-    if (nmat == 1) return minb == 2 ? mmvq_lane_kernel<1, 2> : mmvq_lane_kernel<1, 1>;
-    return minb == 2 ? mmvq_lane_kernel<2, 2> : mmvq_lane_kernel<2, 1>;
+LaneFn lane_kernel(int nmat, int minb, bool packed = false) {
+    if (packed) return nmat == 1 ? mmvq_lane_kernel<1, 2, true> : nullptr;
+    if (nmat == 1) return minb == 2 ? mmvq_lane_kernel<1, 2, false> : mmvq_lane_kernel<1, 1, false>;
+    return minb == 2 ? mmvq_lane_kernel<2, 2, false> : mmvq_lane_kernel<2, 1, false>;
+}
+
+// The reference's prepack of one Q4_K superblock into its 148-byte form
+// (kernels/q4k/abra-packed-q4.cuh:10-27): d and dmin, the eight 6-bit scales
+// and mins as bytes [sc_2j, sc_2j+1, m_2j, m_2j+1] per pair j, the nibbles.
+__global__ void q4k_pack_kernel(const uint8_t *__restrict__ in, uint8_t *__restrict__ out, int64_t nblocks) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    const uint8_t *b = in + i * Q4K_BYTES;
+    uint32_t *o = reinterpret_cast<uint32_t *>(out + i * LG_PACKED_BYTES);
+    const uint32_t *b32 = reinterpret_cast<const uint32_t *>(b);
+    o[0] = b32[0];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        int sc0, m0, sc1, m1;
+        scale_min_one(b + 4, 2 * j, sc0, m0);
+        scale_min_one(b + 4, 2 * j + 1, sc1, m1);
+        o[1 + j] = static_cast<uint32_t>(sc0) | (static_cast<uint32_t>(sc1) << 8) | (static_cast<uint32_t>(m0) << 16) |
+                   (static_cast<uint32_t>(m1) << 24);
+    }
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) o[5 + k] = b32[4 + k];
 }
 
 }  // namespace
 
-bool mmvq_lane_plan(const MmvqConfig &cfg, int64_t N, int nsb, int nmat, int sms, int64_t out[8]) {
+bool mmvq_lane_plan(const MmvqConfig &cfg, int64_t N, int nsb, int nmat, int sms, int64_t out[8],
+                    bool packed) {
     if (cfg.mode != MODE_LANE || nsb <= 0 || N <= 0 || (nmat != 1 && nmat != 2)) return false;
     int R = cfg.ks;  // the candidate's largest rows per unit
     while (R > 1 && R * nmat * nsb > LN_VMAX) R >>= 1;
     if (R * nmat * nsb > LN_VMAX) return false;
+    // packed rows (148 bytes per superblock) are 4-byte aligned: a unit's
+    // copy needs R * nsb * 148 to be a multiple of 16 bytes
+    if (packed && (R * nsb) % 4 != 0) return false;
     int lr = 0;
     while ((1 << lr) < R) ++lr;
-    const int64_t row_bytes = static_cast<int64_t>(nsb) * Q4K_BYTES;
+    const int64_t row_bytes = static_cast<int64_t>(nsb) * (packed ? LG_PACKED_BYTES : Q4K_BYTES);
     const int slot_bytes = static_cast<int>(R * nmat * row_bytes);
     const int64_t total = (N + R - 1) / R;
     if (sms <= 0) sms = device_sm_count();
@@ -219,12 +250,21 @@ cudaError_t prepare_mmvq_lane(const MmvqConfig &cfg, int nmat) {
     return ensure_smem_attr_ptr(reinterpret_cast<const void *>(lane_kernel(nmat, cfg.ctas_per_sm >= 2 ? 2 : 1)));
 }
 
+cudaError_t launch_q4k_pack(const void *w, void *w_packed, int64_t nblocks, cudaStream_t stream) {
+    if (nblocks <= 0) return cudaErrorInvalidValue;
+    q4k_pack_kernel<<<static_cast<unsigned>((nblocks + 255) / 256), 256, 0, stream>>>(
+        static_cast<const uint8_t *>(w), static_cast<uint8_t *>(w_packed), nblocks);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_mmvq_lane(const MmvqConfig &cfg, const void *w, const void *w2, const void *x_q8, float *y,
-                             int64_t N, int64_t K, int flags, cudaStream_t stream, unsigned long long *amax) {
+                             int64_t N, int64_t K, int flags, cudaStream_t stream, unsigned long long *amax,
+                             bool packed) {
     const int nsb = static_cast<int>(K / QK_K), nmat = w2 ? 2 : 1;
     int64_t pl[8];
-    if (!mmvq_lane_plan(cfg, N, nsb, nmat, 0, pl)) return cudaErrorInvalidConfiguration;
-    LaneFn fn = lane_kernel(nmat, cfg.ctas_per_sm >= 2 ? 2 : 1);
+    if (!mmvq_lane_plan(cfg, N, nsb, nmat, 0, pl, packed)) return cudaErrorInvalidConfiguration;
+    LaneFn fn = lane_kernel(nmat, cfg.ctas_per_sm >= 2 ? 2 : 1, packed);
+    if (!fn) return cudaErrorInvalidConfiguration;
     cudaError_t e = ensure_smem_attr_ptr(reinterpret_cast<const void *>(fn));
     if (e != cudaSuccess) return e;
     LaneParams prm = {};

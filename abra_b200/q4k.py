@@ -200,6 +200,19 @@ def mmvq(d_w, d_x, d_y, N: int, K: int, ncols: int = 1, ldy: int | None = None,
          stream_handle(stream))
 
 
+def pack_q4k(d_w, d_packed, nblocks: int, stream=None) -> None:
+    """The reference's 148-byte prepack of nblocks Q4_K superblocks
+    (abra_q4k_pack; kernels/q4k/abra-packed-q4.cuh:10-27)."""
+    call("abra_q4k_pack", ptr(d_w), ptr(d_packed), nblocks, stream_handle(stream))
+
+
+def mmvq_packed(d_wp, d_x, d_y, N: int, K: int, pdl: bool = False, stream=None) -> None:
+    """y = W x at batch 1 over packed weights (abra_q4k_mmvq_packed)."""
+    _check_k(K)
+    call("abra_q4k_mmvq_packed", ptr(d_wp), ptr(d_x), ptr(d_y), N, K,
+         _lib.ABRA_MMVQ_PDL if pdl else 0, stream_handle(stream))
+
+
 def mmvq_swiglu(d_w_gate, d_w_up, d_x, d_y, N: int, K: int, ncols: int = 1,
                 ldy: int | None = None, candidate: int = 0, pdl: bool = False,
                 stream=None) -> None:

@@ -483,6 +483,42 @@ def shape_table(sw: Sweep, reps: int = 3):
     return out
 
 
+def packed_table(sw: Sweep, reps: int = 3):
+    """The reference's 148-byte prepack against the plain 144-byte layout on
+    config 0 (gate 9728x2560) and the tied output: the same lane-mapped MMVQ
+    (2 CTAs per SM, 8-row units) over each, one CUDA graph of back-to-back
+    launches over >= 4 x L2 of weight copies, best of ``reps``."""
+    torch, A = sw.torch, sw.A
+    out = {}
+    for name, N, K in (("gate", 9728, 2560), ("output", 151936, 2560)):
+        nb = N * K // 256
+        copies = max(8, -(-4 * L2_BYTES // (nb * 144)))
+        plain, packed = [], []
+        for i in range(copies):
+            t = torch.empty(nb * 144, dtype=torch.uint8, device=sw.dev)
+            A.gen_q4k(t, nb, 0, 9500 + i)
+            p = torch.empty(nb * 148, dtype=torch.uint8, device=sw.dev)
+            A.pack_q4k(t, p, nb)
+            plain.append(t)
+            packed.append(p)
+        torch.cuda.synchronize()
+        row = {"N": N, "K": K, "copies": copies}
+        for form, bufs, nbytes in (("q4k_144", plain, 144), ("packed_148", packed, 148)):
+            if form == "q4k_144":
+                run = lambda: [A.mmvq(b, sw.xq[K], sw.y, N, K, candidate=4082, pdl=True) for b in bufs]
+            else:
+                run = lambda: [A.mmvq_packed(b, sw.xq[K], sw.y, N, K, pdl=True) for b in bufs]
+            g = sw.capture(run)
+            ms = min(sw.timed(1, g.replay) for _ in range(reps))
+            us = ms * 1e3 / copies
+            row[form] = {"us": round(us, 3), "GBps": round((nb * nbytes + K // 32 * 36 + N * 4) / (us * 1e-6) / 1e9, 1)}
+            del g
+        out[name] = row
+        del plain, packed
+        torch.cuda.empty_cache()
+    return out
+
+
 Q6K_SHAPES = [("attn_v", 1024, 2560), ("ffn_down", 2560, 9728), ("output", 151936, 2560)]
 
 
@@ -1167,6 +1203,10 @@ def decode_main(a, dist):
         if not a.no_extras:
             extras["per_shape"] = shape_table(sw)
             extras["per_shape_q6k"] = shape_table_q6k(sw)
+            try:
+                extras["packed_q4k"] = packed_table(sw)
+            except Exception as exc:
+                extras["packed_q4k"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
             r = ref_gpu_sweep(sw, 5)
             if r:
                 extras["reference_kernels_on_b200"] = r

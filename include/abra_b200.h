@@ -153,6 +153,20 @@ void launch_pinned_upstream_mmvq(const void *d_w_q4, const void *d_x_q8, float *
 void quantize_row_q4_K_upstream_cpu(const float *x, void *y, int64_t k);
 void dequantize_row_q4_K_upstream_cpu(const void *x, float *y, int64_t k);
 
+/* The reference's opt-in 148-byte prepack of Q4_K weights
+ * (kernels/q4k/abra-packed-q4.cuh:3-31; made by abra_prepare_q4 when
+ * ABRA_PREPACK=1, tools/prepare-packed-weights.py:49-69): per superblock fp16
+ * d and dmin, the eight 6-bit scales and mins unpacked to bytes
+ * [sc_2j, sc_2j+1, m_2j, m_2j+1] for each pair j, then the 128 nibble bytes.
+ * nblocks superblocks of 144 bytes in, of 148 out (both 16-byte aligned). */
+int abra_q4k_pack(const void *w_q4k, void *w_packed, int64_t nblocks, void *stream);
+/* y = W x at batch 1 over packed weights (N rows of K/256 packed
+ * superblocks): the lane-mapped MMVQ reading the unpacked scale bytes; y is
+ * bit-identical to abra_q4k_mmvq on the unpacked weights.  ABRA_E_UNSUPPORTED
+ * when no unit size keeps the packed rows' copies 16-byte aligned. */
+int abra_q4k_mmvq_packed(const void *w_packed, const void *x_q8_1, float *y, int64_t N, int64_t K,
+                         int32_t flags, void *stream);
+
 /* --------------------------------------------------------- Q8_1 -------- */
 /* x: ncols columns of K fp32 (K % 32 == 0) -> ncols x K/32 Q8_1 blocks.
  * Replaces launch_quantize_f32_to_q8_1 / launch_custom_reference_q8_1_quantizer
