@@ -1153,7 +1153,11 @@ def decode_main(a, dist):
     cpu = None
     if dist.world > 1:
         # batch 32 on the tensor cores, tensor parallel over the same ranks
-        extras["decode_b32"] = decode_batched(torch, a.warmup, a.steps, dist=dist)
+        # (an error here is reported in the field; every rank raises alike)
+        try:
+            extras["decode_b32"] = decode_batched(torch, a.warmup, a.steps, dist=dist)
+        except Exception as exc:
+            extras["decode_b32"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     if dist.world == 1:
         # the same token through the per-operation kernel chain
         from abra_b200.model import KERNEL_CHAIN, Q4_K_M
