@@ -38,6 +38,7 @@ enum : unsigned {
     ERR_FLAG_TIMEOUT = 1u << 1,  // a cross-rank flag wait gave up
     ERR_WAIT_EMPTY = 1u << 2,    // a producer's wait for a free stage gave up
     ERR_GRID_TIMEOUT = 1u << 3,  // a grid-wide barrier of the persistent decode gave up
+    ERR_BAD_INDEX = 1u << 4,     // a data-dependent index (a token id) was out of range; its access was skipped
 };
 
 // Wall-clock bound of every spin-wait in these kernels (nanoseconds).

@@ -120,19 +120,11 @@ struct PkParams {
 constexpr int PK_TRACE_EV = 512;
 __device__ unsigned long long g_pk_trace[160][5][PK_TRACE_EV];
 __shared__ unsigned long long g_pk_wait_ns;  // this CTA's warps' waits on ring slots, per phase
-__device__ unsigned long long g_pk_units[5][64][4];  // CTA 0 warp 0: stamps inside the units of 5 GEMVs
-__shared__ int g_pk_gemv;                           // which GEMV of the token is running (CTA 0)
 __device__ unsigned long long g_pk_att[12];         // CTA 0 thread 0: steps of layer 1's first attention item
 #define PK_ASTAMP(layer, k)                                                   \
     do {                                                                      \
         if (blockIdx.x == 0 && threadIdx.x == 0 && (layer) == 1 && it == 0)   \
             g_pk_att[k] = globaltimer_ns();                                   \
-    } while (0)
-#define PK_USTAMP(u, k)                                                                      \
-    do {                                                                                     \
-        if (blockIdx.x == 0 && (threadIdx.x >> 5) == 0 && lane == 0 && (u) < 64 * PK_NCW &&   \
-            g_pk_gemv < 5)                                                                   \
-            g_pk_units[g_pk_gemv][(u) / PK_NCW][k] = globaltimer_ns();                       \
     } while (0)
 #define PK_STAMP(kind, idx)                                                                            \
     do {                                                                                               \
@@ -141,9 +133,6 @@ __device__ unsigned long long g_pk_att[12];         // CTA 0 thread 0: steps of 
 #else
 #define PK_ASTAMP(layer, k) \
     do {                    \
-    } while (0)
-#define PK_USTAMP(u, k) \
-    do {                \
     } while (0)
 #define PK_STAMP(kind, idx) \
     do {                    \
@@ -333,7 +322,6 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
 #ifdef ABRA_PK_TRACE
         if (lane == 0) atomicAdd(&g_pk_wait_ns, static_cast<unsigned long long>(globaltimer_ns() - tw0));
 #endif
-        PK_USTAMP(u, 0);
         const uint8_t *wrow[NMAT];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) wrow[m] = ring + s * PK_SLOT_BYTES + (m * R + r) * mm.pitch;
@@ -347,7 +335,6 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
             for (int m = 0; m < NMAT; ++m) vbuf[(m * R + r) * nsb + b] = v[m];
         }
         __syncwarp();
-        PK_USTAMP(u, 1);
         // the slot's weights are consumed: lane 31 stores nothing to global
         // memory, so its release does not wait for this warp's output stores
         if (lane == 31) mbar_arrive(&empty[s]);
@@ -373,7 +360,6 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
             }
         }
         __syncwarp();
-        PK_USTAMP(u, 2);
         if (s_amax) {
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) {
@@ -383,7 +369,6 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
             if (lane == 0) atomicMax(s_amax, key);
         }
         __syncwarp();  // the staging buffer is reused by the next unit
-        PK_USTAMP(u, 3);
     }
 }
 
@@ -393,6 +378,29 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
 __device__ __forceinline__ void pk_stage_norm(const float *w, float *s_w, int K) {
     for (int i = threadIdx.x * 4; i < K; i += PK_NCW * 32 * 4)
         *reinterpret_cast<float4 *>(s_w + i) = __ldg(reinterpret_cast<const float4 *>(w + i));
+}
+
+// 16 bytes from global memory (through L2, not L1) into shared memory without
+// passing through registers; complete for this thread after cp_async_wait,
+// for the CTA after a CTA barrier that follows it.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)),
+                 "l"(static_cast<uint64_t>(__cvta_generic_to_global(src)))
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// The next residual prologue's inputs -- its RMSNorm weights and the residual
+// stream h (written before the last grid barrier this CTA passed) -- copied
+// into shared memory in the background while this CTA works on or waits for
+// other phases; the prologue waits for them.  Issued as early as the data is
+// stable and s_x / s_w are free, so that a CTA arriving last at a barrier
+// does not start its loads only then.
+__device__ __forceinline__ void pk_stage_xin_async(const float *w, const float *h, float *s_w, float *s_x, int K) {
+    for (int i = threadIdx.x * 4; i < K; i += PK_NCW * 32 * 4) {
+        cp_async16(s_w + i, w + i);
+        cp_async16(s_x + i, h + i);
+    }
 }
 
 // Element i of the token's embedding row (embed_kernel's arithmetic).
@@ -443,39 +451,6 @@ __device__ __forceinline__ void pk_quant4(uint8_t *arec, int i, int sub, float x
     const uint32_t packed = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
                             ((static_cast<uint32_t>(q2) & 0xffu) << 16) | (static_cast<uint32_t>(q3) << 24);
     pk_put_block(arec, i, sub, packed, __half2float(__float2half_rn(d)), sum);
-}
-
-// The reference Q8_1 rounding of one whole 32-value block in one lane
-// (d = amax / 127, q = roundf(x / d), the block's integer sum; the bytes of
-// quantize_block_warp, with no cross-lane steps); then the block into the
-// records.
-__device__ __forceinline__ void pk_quant_block(uint8_t *arec, int i, const float (&x)[32]) {
-    float amax = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) amax = fmaxf(amax, fabsf(x[k]));
-    const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    uint32_t w[8];
-    int sum = 0;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int q = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x[4 * k + j], id)))));
-            sum += q;
-            word |= (static_cast<uint32_t>(q) & 0xffu) << (8 * j);
-        }
-        w[k] = word;
-    }
-    uint8_t *rec = arec + (i >> 3) * PK_AREC;
-    const int s = i & 7;
-    uint4 *dst = reinterpret_cast<uint4 *>(rec + 32 * s);
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    const float d8 = __half2float(__float2half_rn(d));
-    reinterpret_cast<float *>(rec + 256)[s] = d8;
-    reinterpret_cast<float *>(rec + 288)[s] = __fmul_rn(d8, __int2float_rn(sum));
 }
 
 // Before the phase's barrier: the residual stream h_in (stable since an
@@ -550,20 +525,26 @@ __device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, 
 
 // Q8_1 of an fp32 activation written earlier in this launch (the SwiGLU
 // output), straight into the records: the bytes quantize_q8_1_kernel writes
-// and mmvq_q4k_kernel stages.  One lane per block.
+// and mmvq_q4k_kernel stages.  Eight lanes per block, four values each; every
+// load of a pass group is issued before the first block is rounded, so the
+// CTA pays one L2 round trip per eight passes of 32 blocks (K / 32 must be a
+// multiple of 4: a warp's four blocks are all in range or all out).
 __device__ __forceinline__ void pk_quant_f32(const float *x, int K, uint8_t *arec) {
-    const int nblk = K / QK8_1;
-    for (int i = threadIdx.x; i < nblk; i += PK_NCW * 32) {
-        float v[32];
+    constexpr int U = 8;  // passes in flight
+    const int nblk = K / QK8_1, t = threadIdx.x, sub = t & 7;
+    for (int g0 = 0; g0 < nblk; g0 += U * PK_NCW * 4) {
+        float4 f[U];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float4 f = __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + 4 * k));
-            v[4 * k] = f.x;
-            v[4 * k + 1] = f.y;
-            v[4 * k + 2] = f.z;
-            v[4 * k + 3] = f.w;
+        for (int k = 0; k < U; ++k) {
+            const int i = g0 + k * PK_NCW * 4 + (t >> 3);
+            f[k] = i < nblk ? __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + 4 * sub))
+                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        pk_quant_block(arec, i, v);
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = g0 + k * PK_NCW * 4 + (t >> 3);
+            if (i < nblk) pk_quant4(arec, i, sub, f[k].x, f[k].y, f[k].z, f[k].w);  // warp-uniform
+        }
     }
     cta_sync();
 }
@@ -697,10 +678,9 @@ __device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int p
     float *s_in = scr + hpi * (128 + ATT_CHUNK_P + 8) + 8 * hpi * 128;
     const PersistLayer &Ly = P.layers[layer];
     const int t = threadIdx.x;
-    if (t < 128) {
-        s_in[t] = Ly.q_norm[t];
-        s_in[128 + t] = Ly.k_norm[t];
-        s_in[256 + t] = P.rope[static_cast<int64_t>(pos) * 128 + t];
+    if (t < 96) {  // 16-byte pieces: the q and k norm weights and the RoPE row
+        const float *src = t < 32 ? Ly.q_norm : t < 64 ? Ly.k_norm : P.rope + static_cast<int64_t>(pos) * 128;
+        cp_async16(s_in + 4 * t, src + 4 * (t & 31));
     }
     // the cached K and V rows of this CTA's items into L2 (positions before
     // pos: written by earlier launches), so that the phase's loads do not
@@ -982,7 +962,12 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
     uint32_t T = 0;
     bool poisoned = false;
     int cur = 0;
-    const uint8_t *erow = P.embd + static_cast<int64_t>(__ldcg(P.tokens + pos)) * (hidden / QK_K) * Q4K_BYTES;
+    int tok = __ldcg(P.tokens + pos);
+    if (tok < 0 || tok >= P.vocab) {  // never from a valid pick or prompt: flag it, read row 0
+        if (t == 0) report_error(ERR_BAD_INDEX);
+        tok = 0;
+    }
+    const uint8_t *erow = P.embd + static_cast<int64_t>(tok) * (hidden / QK_K) * Q4K_BYTES;
     for (int e = 0; e < nev; ++e) {
         const int l = e / 5;
         const int ph = e == nev - 1 ? PH_OUT : e % 5;
@@ -991,10 +976,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         // inputs that do not depend on the previous phase, staged before its
         // barrier: norm weights, the residual stream (written two or more
         // phases back) or the embedding row, the attention's norms and RoPE row
-        if (xin) {
-            pk_stage_norm(ph == PH_OUT ? P.out_norm : ph == PH_QKV ? P.layers[l].attn_norm : P.layers[l].ffn_norm,
-                          s_w, hidden);
-            pk_xin_stage(hidden, P.h[cur], first ? erow : nullptr, s_x);
+        if (first) {  // the embedding row: no earlier phase to stage it in
+            pk_stage_norm(ph == PH_OUT ? P.out_norm : P.layers[l].attn_norm, s_w, hidden);
+            pk_xin_stage(hidden, nullptr, erow, s_x);
         } else if (ph == PH_ATT)
             pk_stage_att(P, l, pos, GQ, pk_att_hpi(P, pos, GQ), scr);
         if (ph == PH_OUT && t == 0) s_amax = 0ull;
@@ -1003,6 +987,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             if (t == 0) pk_wait(P.bar, kb * G);
         }
         if (t == 0) PK_STAMP(0, e);
+        cp_async_wait();  // this thread's staged inputs (the barrier below shares them)
         cta_sync();
         // the phase's activation
         if (xin) {
@@ -1011,6 +996,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         } else if (ph == PH_O) {
             pk_stage_q8(P.oq, P.n_heads * 128, arec);
         } else if (ph == PH_DOWN) {
+            // the next prologue's inputs: the residual stream written in this
+            // layer's GU prologue (visible since this phase's barrier)
+            pk_stage_xin_async(l + 1 < L ? P.layers[l + 1].attn_norm : P.out_norm, P.h[cur], s_w, s_x, hidden);
             pk_quant_f32(P.act, P.ffn, arec);
         }
         if (t == 0) PK_STAMP(3, e);
@@ -1030,10 +1018,6 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             const PkMm mm = pk_mm(P, l, kind);
             int u_begin, nu;
             pk_range(mm, u_begin, nu);
-#ifdef ABRA_PK_TRACE
-            if (t == 0) g_pk_gemv = (l == 1 || ph == PH_OUT) ? kind : 99;
-            cta_sync();
-#endif
             unsigned long long *amax = ph == PH_OUT ? &s_amax : nullptr;
             if (mm.w1)
                 pk_units<2>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
@@ -1043,6 +1027,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         }
         cta_sync();
         if (t == 0) PK_STAMP(1, e);
+        // the attention scratch is free: the GU prologue's inputs (the residual
+        // stream written in this layer's QKV prologue) in the background
+        if (ph == PH_ATT) pk_stage_xin_async(P.layers[l].ffn_norm, P.h[cur], s_w, s_x, hidden);
 #ifdef ABRA_PK_TRACE
         if (t == 0 && e < PK_TRACE_EV && blockIdx.x < 160) g_pk_trace[blockIdx.x][4][e] = g_pk_wait_ns;
 #endif
@@ -1057,7 +1044,11 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             __threadfence();
             const unsigned long long key = __ldcg(P.amax);
             *P.amax = 0ull;
-            const int bi = static_cast<int>(0xFFFFFFFFu - static_cast<unsigned>(key & 0xFFFFFFFFull));
+            int bi = static_cast<int>(0xFFFFFFFFu - static_cast<unsigned>(key & 0xFFFFFFFFull));
+            if (bi < 0 || bi >= P.vocab) {  // no key was merged: flag it, pick row 0
+                report_error(ERR_BAD_INDEX);
+                bi = 0;
+            }
             P.picks[pos] = bi;
             if (pos + 1 >= __ldcg(P.nprompt)) P.tokens[pos + 1] = bi;
             *P.pos = pos + 1;
@@ -1300,9 +1291,6 @@ extern "C" int abra_pk_trace(unsigned long long *out, long long n) {
 }
 extern "C" int abra_pk_att(unsigned long long *out) {
     return cudaMemcpyFromSymbol(out, abra::g_pk_att, sizeof(abra::g_pk_att)) == cudaSuccess ? 0 : -2;
-}
-extern "C" int abra_pk_units(unsigned long long *out) {
-    return cudaMemcpyFromSymbol(out, abra::g_pk_units, sizeof(abra::g_pk_units)) == cudaSuccess ? 0 : -2;
 }
 #endif
 

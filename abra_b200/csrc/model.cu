@@ -1360,14 +1360,16 @@ int abra_model_invalidate(void *model) {
     return ABRA_OK;
 }
 
-// After a synchronize: a kernel's bounded wait that gave up (the device
-// error word, left set) fails the call instead of passing its garbage on.
+// After a synchronize: a kernel's bounded wait that gave up, or an
+// out-of-range token id it refused to index with (the device error word,
+// left set), fails the call instead of passing its garbage on.
 static int device_waits_ok() {
     unsigned v = 0;
     cudaError_t e = abra::read_error_words(&v, false);
     if (e != cudaSuccess) return model_fail(ABRA_E_CUDA, "device error word", e);
     if (v) {
-        snprintf(g_model_err, sizeof g_model_err, "a kernel's bounded wait gave up (device error word 0x%x)", v);
+        snprintf(g_model_err, sizeof g_model_err, "%s (device error word 0x%x)",
+                 v == 0x10u ? "a kernel met an out-of-range token id" : "a kernel's bounded wait gave up", v);
         return ABRA_E_CUDA;
     }
     return ABRA_OK;
