@@ -395,9 +395,12 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_al
 // into shared memory in the background while this CTA works on or waits for
 // other phases; the prologue waits for them.  Issued as early as the data is
 // stable and s_x / s_w are free, so that a CTA arriving last at a barrier
-// does not start its loads only then.
+// does not start its loads only then.  Warp 0 issues none: its thread 0
+// arrives at and polls the grid barriers, and its fences would otherwise wait
+// for these copies to land.
 __device__ __forceinline__ void pk_stage_xin_async(const float *w, const float *h, float *s_w, float *s_x, int K) {
-    for (int i = threadIdx.x * 4; i < K; i += PK_NCW * 32 * 4) {
+    if (threadIdx.x < 32) return;
+    for (int i = (threadIdx.x - 32) * 4; i < K; i += (PK_NCW - 1) * 32 * 4) {
         cp_async16(s_w + i, w + i);
         cp_async16(s_x + i, h + i);
     }
@@ -527,10 +530,11 @@ __device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, 
 // output), straight into the records: the bytes quantize_q8_1_kernel writes
 // and mmvq_q4k_kernel stages.  Eight lanes per block, four values each; every
 // load of a pass group is issued before the first block is rounded, so the
-// CTA pays one L2 round trip per eight passes of 32 blocks (K / 32 must be a
-// multiple of 4: a warp's four blocks are all in range or all out).
+// CTA pays one L2 round trip per ten passes of 32 blocks (the 304 blocks of
+// a 9728-wide FFN in one) (K / 32 must be a multiple of 4: a warp's four
+// blocks are all in range or all out).
 __device__ __forceinline__ void pk_quant_f32(const float *x, int K, uint8_t *arec) {
-    constexpr int U = 8;  // passes in flight
+    constexpr int U = 10;  // passes in flight
     const int nblk = K / QK8_1, t = threadIdx.x, sub = t & 7;
     for (int g0 = 0; g0 < nblk; g0 += U * PK_NCW * 4) {
         float4 f[U];
@@ -678,9 +682,10 @@ __device__ __forceinline__ void pk_stage_att(const PkParams &P, int layer, int p
     float *s_in = scr + hpi * (128 + ATT_CHUNK_P + 8) + 8 * hpi * 128;
     const PersistLayer &Ly = P.layers[layer];
     const int t = threadIdx.x;
-    if (t < 96) {  // 16-byte pieces: the q and k norm weights and the RoPE row
-        const float *src = t < 32 ? Ly.q_norm : t < 64 ? Ly.k_norm : P.rope + static_cast<int64_t>(pos) * 128;
-        cp_async16(s_in + 4 * t, src + 4 * (t & 31));
+    if (t >= 32 && t < 128) {  // 16-byte pieces of the q and k norm weights and the RoPE row (not warp 0)
+        const int j = t - 32;
+        const float *src = j < 32 ? Ly.q_norm : j < 64 ? Ly.k_norm : P.rope + static_cast<int64_t>(pos) * 128;
+        cp_async16(s_in + 4 * j, src + 4 * (j & 31));
     }
     // the cached K and V rows of this CTA's items into L2 (positions before
     // pos: written by earlier launches), so that the phase's loads do not
@@ -996,10 +1001,11 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         } else if (ph == PH_O) {
             pk_stage_q8(P.oq, P.n_heads * 128, arec);
         } else if (ph == PH_DOWN) {
-            // the next prologue's inputs: the residual stream written in this
-            // layer's GU prologue (visible since this phase's barrier)
-            pk_stage_xin_async(l + 1 < L ? P.layers[l + 1].attn_norm : P.out_norm, P.h[cur], s_w, s_x, hidden);
             pk_quant_f32(P.act, P.ffn, arec);
+            // the next prologue's inputs: the residual stream written in this
+            // layer's GU prologue (visible since this phase's barrier), behind
+            // this prologue's own loads
+            pk_stage_xin_async(l + 1 < L ? P.layers[l + 1].attn_norm : P.out_norm, P.h[cur], s_w, s_x, hidden);
         }
         if (t == 0) PK_STAMP(3, e);
 #ifdef ABRA_PK_TRACE
@@ -1027,13 +1033,13 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
         }
         cta_sync();
         if (t == 0) PK_STAMP(1, e);
-        // the attention scratch is free: the GU prologue's inputs (the residual
-        // stream written in this layer's QKV prologue) in the background
-        if (ph == PH_ATT) pk_stage_xin_async(P.layers[l].ffn_norm, P.h[cur], s_w, s_x, hidden);
 #ifdef ABRA_PK_TRACE
         if (t == 0 && e < PK_TRACE_EV && blockIdx.x < 160) g_pk_trace[blockIdx.x][4][e] = g_pk_wait_ns;
 #endif
         if (e < nev - 1 && t == 0) pk_arrive(P.bar);
+        // the attention scratch is free: the GU prologue's inputs (the residual
+        // stream written in this layer's QKV prologue) in the background
+        if (ph == PH_ATT) pk_stage_xin_async(P.layers[l].ffn_norm, P.h[cur], s_w, s_x, hidden);
     }
     // the greedy pick: the last CTA to arrive decodes the merged key
     if (t == 0) {
