@@ -421,39 +421,42 @@ __device__ __forceinline__ float pk_embed(const uint8_t *row, int i) {
     return __fmaf_rn(a, static_cast<float>(q), -bm);
 }
 
-// Q8_1 block i of an activation into the records: quants, d8, A = d8 * sum.
-__device__ __forceinline__ void pk_put_block(uint8_t *arec, int i, int sub, uint32_t packed, float d8,
-                                             int sum) {
+// The reference Q8_1 rounding of one 32-value block (d = amax / 127,
+// q = roundf(x / d), the block's integer sum; the bytes quantize_q8_1_kernel
+// writes) by a lane pair, lane h (= lane & 1) holding values 16 h .. 16 h + 15
+// (max and integer sum are exact in any order), into the activation records:
+// quants, d8, A = d8 * sum.  Every lane of the warp calls it (the shuffles
+// span the warp); `store` is false for a pair past the last block.
+__device__ __forceinline__ void pk_quant16(uint8_t *arec, int i, int h, const float (&x)[16], bool store) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(x[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[4];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int q = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x[4 * k + j], id)))));
+            sum += q;
+            word |= (static_cast<uint32_t>(q) & 0xffu) << (8 * j);
+        }
+        w[k] = word;
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    if (!store) return;
     uint8_t *rec = arec + (i >> 3) * PK_AREC;
     const int s = i & 7;
-    *reinterpret_cast<uint32_t *>(rec + 32 * s + 4 * sub) = packed;
-    if (sub == 0) {
+    *reinterpret_cast<uint4 *>(rec + 32 * s + 16 * h) = make_uint4(w[0], w[1], w[2], w[3]);
+    if (h == 0) {
+        const float d8 = __half2float(__float2half_rn(d));
         reinterpret_cast<float *>(rec + 256)[s] = d8;
         reinterpret_cast<float *>(rec + 288)[s] = __fmul_rn(d8, __int2float_rn(sum));
     }
-}
-
-// The reference Q8_1 rounding of four values of a 32-block, eight lanes per
-// block (lane & 7 = the quarter of eight values... four consecutive values
-// each): d = amax / 127, q = roundf(x / d), the block's integer sum; then the
-// block into the records.
-__device__ __forceinline__ void pk_quant4(uint8_t *arec, int i, int sub, float x0, float x1, float x2, float x3) {
-    float amax = fmaxf(fmaxf(fabsf(x0), fabsf(x1)), fmaxf(fabsf(x2), fabsf(x3)));
-    amax = fmaxf(0.0f, amax);
-#pragma unroll
-    for (int m = 4; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-    const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    const int q0 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x0, id)))));
-    const int q1 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x1, id)))));
-    const int q2 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x2, id)))));
-    const int q3 = static_cast<int>(static_cast<int8_t>(static_cast<int>(roundf(__fmul_rn(x3, id)))));
-    int sum = (q0 + q1) + (q2 + q3);
-#pragma unroll
-    for (int m = 4; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-    const uint32_t packed = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
-                            ((static_cast<uint32_t>(q2) & 0xffu) << 16) | (static_cast<uint32_t>(q3) << 24);
-    pk_put_block(arec, i, sub, packed, __half2float(__float2half_rn(d)), sum);
 }
 
 // Before the phase's barrier: the residual stream h_in (stable since an
@@ -514,40 +517,57 @@ __device__ __forceinline__ void pk_xin(int K, const float *delta, float *h_out, 
 #pragma unroll
     for (int w = 1; w < 8; ++w) total = __fadd_rn(total, s_nred[w]);
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), eps)));
-    const int nblk = K / QK8_1;
-    const int sub = lane & 7;
-    for (int b0 = warp * 4; b0 < nblk; b0 += PK_NCW * 4) {  // warp-uniform: nblk % 8 == 0
-        const int i = b0 + (lane >> 3);
-        const float4 xv = *reinterpret_cast<const float4 *>(s_x + i * QK8_1 + sub * 4);
-        const float4 wv = *reinterpret_cast<const float4 *>(s_w + i * QK8_1 + sub * 4);
-        pk_quant4(arec, i, sub, __fmul_rn(__fmul_rn(xv.x, r), wv.x), __fmul_rn(__fmul_rn(xv.y, r), wv.y),
-                  __fmul_rn(__fmul_rn(xv.z, r), wv.z), __fmul_rn(__fmul_rn(xv.w, r), wv.w));
+    const int nblk = K / QK8_1, h = t & 1;
+    for (int i0 = 0; i0 < nblk; i0 += PK_NCW * 16) {  // a lane pair per block, 128 blocks per pass
+        const int i = i0 + (t >> 1);
+        const bool in = i < nblk;
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int j = i * QK8_1 + 16 * h + 4 * k;
+            const float4 xv = in ? *reinterpret_cast<const float4 *>(s_x + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const float4 wv = in ? *reinterpret_cast<const float4 *>(s_w + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            v[4 * k] = __fmul_rn(__fmul_rn(xv.x, r), wv.x);
+            v[4 * k + 1] = __fmul_rn(__fmul_rn(xv.y, r), wv.y);
+            v[4 * k + 2] = __fmul_rn(__fmul_rn(xv.z, r), wv.z);
+            v[4 * k + 3] = __fmul_rn(__fmul_rn(xv.w, r), wv.w);
+        }
+        pk_quant16(arec, i, h, v, in);
     }
     cta_sync();
 }
 
 // Q8_1 of an fp32 activation written earlier in this launch (the SwiGLU
 // output), straight into the records: the bytes quantize_q8_1_kernel writes
-// and mmvq_q4k_kernel stages.  Eight lanes per block, four values each; every
-// load of a pass group is issued before the first block is rounded, so the
-// CTA pays one L2 round trip per ten passes of 32 blocks (the 304 blocks of
-// a 9728-wide FFN in one) (K / 32 must be a multiple of 4: a warp's four
-// blocks are all in range or all out).
+// and mmvq_q4k_kernel stages.  A lane pair per block, 16 values each; all
+// loads of up to three passes of 128 blocks are issued before the first block
+// is rounded, so the 304 blocks of a 9728-wide FFN cost one L2 round trip.
 __device__ __forceinline__ void pk_quant_f32(const float *x, int K, uint8_t *arec) {
-    constexpr int U = 10;  // passes in flight
-    const int nblk = K / QK8_1, t = threadIdx.x, sub = t & 7;
-    for (int g0 = 0; g0 < nblk; g0 += U * PK_NCW * 4) {
-        float4 f[U];
+    constexpr int U = 3;  // passes in flight
+    const int nblk = K / QK8_1, t = threadIdx.x, h = t & 1;
+    for (int g0 = 0; g0 < nblk; g0 += U * PK_NCW * 16) {
+        float4 f[U][4];
 #pragma unroll
         for (int k = 0; k < U; ++k) {
-            const int i = g0 + k * PK_NCW * 4 + (t >> 3);
-            f[k] = i < nblk ? __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + 4 * sub))
-                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const int i = g0 + k * PK_NCW * 16 + (t >> 1);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                f[k][c] = i < nblk ? __ldcg(reinterpret_cast<const float4 *>(x + i * QK8_1 + 16 * h + 4 * c))
+                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
 #pragma unroll
         for (int k = 0; k < U; ++k) {
-            const int i = g0 + k * PK_NCW * 4 + (t >> 3);
-            if (i < nblk) pk_quant4(arec, i, sub, f[k].x, f[k].y, f[k].z, f[k].w);  // warp-uniform
+            const int i = g0 + k * PK_NCW * 16 + (t >> 1);
+            if (g0 + k * PK_NCW * 16 >= nblk) break;  // CTA-uniform
+            float v[16];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                v[4 * c] = f[k][c].x;
+                v[4 * c + 1] = f[k][c].y;
+                v[4 * c + 2] = f[k][c].z;
+                v[4 * c + 3] = f[k][c].w;
+            }
+            pk_quant16(arec, i, h, v, i < nblk);
         }
     }
     cta_sync();
