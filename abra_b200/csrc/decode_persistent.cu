@@ -140,41 +140,39 @@ __device__ unsigned long long g_pk_att[12];         // CTA 0 thread 0: steps of 
 #endif
 
 // ------------------------------------------------------------ helpers ---
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-__device__ __forceinline__ void red_relaxed_gpu_add(unsigned long long *p, unsigned long long v) {
-    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_gpu(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
 __device__ __forceinline__ bool pk_aborted() {
     return (*static_cast<volatile unsigned *>(&g_abra_device_error) & ERR_GRID_TIMEOUT) != 0;
 }
 // Thread 0 of a CTA whose consumers have passed a CTA barrier after their
-// last writes of the phase: publish the CTA's arrival (release at GPU scope:
-// the fence orders every write the CTA barrier made visible to this thread).
+// last writes of the phase: publish the CTA's arrival with one release add at
+// GPU scope (cumulative: it orders every write the CTA barrier made visible
+// to this thread).  A separate fence.acq_rel before a relaxed add, the same
+// ordering, measured 6 % slower over the token's 181 barriers.
 __device__ __forceinline__ void pk_arrive(unsigned long long *bar) {
-    fence_acq_rel_gpu();
-    red_relaxed_gpu_add(bar, 1ull);
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(bar), "l"(1ull) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
 }
 __device__ __forceinline__ void cta_sync() { named_bar_sync(1, PK_NCW * 32); }
 
-// Thread 0: wait until every CTA has arrived (bounded; after one timeout in
-// this launch the remaining barriers pass at once), then acquire.
+// Thread 0: wait until every CTA has arrived, polling with acquire loads (the
+// load that sees the last arrival orders this CTA's later reads after every
+// CTA's released writes; the CTA barrier that follows passes that on).
+// Bounded; after one timeout in this launch the remaining barriers pass at
+// once.
 __device__ __forceinline__ void pk_wait(const unsigned long long *bar, unsigned long long target) {
-    if (ld_relaxed_gpu(bar) < target && !pk_aborted()) {
-        const uint64_t t0 = globaltimer_ns();
-        for (uint32_t i = 1;; ++i) {
-            if (ld_relaxed_gpu(bar) >= target) break;
-            if ((i & 63u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
-                report_error(ERR_GRID_TIMEOUT);
-                break;
-            }
+    if (ld_acquire_gpu(bar) >= target || pk_aborted()) return;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (ld_acquire_gpu(bar) >= target) return;
+        if ((i & 63u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+            report_error(ERR_GRID_TIMEOUT);
+            return;
         }
     }
-    fence_acq_rel_gpu();
 }
 
 struct PkMm {
@@ -933,19 +931,19 @@ __device__ __forceinline__ void pk_attention(const PkParams &P, int layer, int p
             for (int w = 1; w < 8; ++w) l = __fadd_rn(l, s_red[t][w]);
             P.part_l[static_cast<int64_t>(h0 + t) * mc + c] = l;
         }
-        // the last chunk of the item's heads to finish merges them
+        // the last chunk of the item's heads to finish merges them: one
+        // acquire-release add publishes this chunk's partials (the CTA barrier
+        // made them visible to thread 0) and, for the last, acquires the others'
         cta_sync();
         if (t == 0) {
-            __threadfence();
-            const unsigned last = atomicAdd(&P.head_cnt[h0], 1u) + 1u == static_cast<unsigned>(nch) ? 1u : 0u;
+            unsigned old;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(P.head_cnt + h0) : "memory");
+            const unsigned last = old + 1u == static_cast<unsigned>(nch) ? 1u : 0u;
             if (last) P.head_cnt[h0] = 0u;
             *s_flag = last;
         }
         cta_sync();
-        if (*s_flag) {
-            __threadfence();
-            if (warp < GQ) pk_merge_head(P, h0 + warp, nch, lane);
-        }
+        if (*s_flag && warp < GQ) pk_merge_head(P, h0 + warp, nch, lane);
         cta_sync();  // the scratch is reused by the next item
     }
 }
