@@ -1,15 +1,15 @@
 // decode_persistent.cu -- one decode token of the batch-1 Q4_K model as ONE
-// cooperative kernel: one CTA per SM, eight consumer warps and one producer
-// warp each.
+// cooperative kernel: one CTA per SM, eight warps each.
 //
 // The kernel-chain step (model.cu, record_step) is ~290 dependent launches
 // per token, each paying launch, ramp and drain.  Here the token is a
 // sequence of phases separated by grid-wide barriers, and the weights of
 // every GEMV phase stream into a shared-memory ring AHEAD of the data
-// dependency: weights do not depend on activations, so the producer warp of
-// each CTA walks its whole token's share of the weight rows -- layer by
-// layer, phase by phase -- and only ever waits for a free ring slot.  While
-// the consumers work through attention or wait at a barrier, HBM keeps
+// dependency: weights do not depend on activations, so each CTA's ring
+// always holds the next NSLOT units of its whole token's share of the weight
+// rows -- layer by layer, phase by phase: the warp that finishes a slot
+// refills it with the unit NSLOT tickets ahead.  While the warps work through
+// attention or wait at a barrier, the copies already issued keep HBM
 // streaming the next phases' rows.
 //
 // Phases of layer l (a grid barrier after each):
@@ -47,20 +47,22 @@
 //
 // Ring protocol: ticket t of a CTA (its t-th unit over the token) goes to
 // slot t % NSLOT (16 slots, or 8 when the activations of a wide or many-head
-// shape leave less shared memory), phase t / NSLOT of that slot's full/empty
-// mbarriers.  Within a GEMV phase unit u goes to consumer warp u % 8 (NSLOT
-// is a multiple of 8, so ticket t - NSLOT of the same phase belongs to the
-// same warp, which consumed it before waiting on t; across phases all
-// consumers pass a CTA barrier) -- so no parity wait can alias a phase two
-// ahead.
+// shape leave less shared memory), phase t / NSLOT of that slot's full
+// mbarrier; the warp that consumed ticket t - NSLOT issued t.  Within a GEMV
+// phase unit u goes to warp u % 8 (NSLOT is a multiple of 8, so ticket
+// t - NSLOT of the same phase belongs to the same warp, which consumed it
+// before waiting on t; across phases all warps pass a CTA barrier) -- so no
+// parity wait can alias a phase two ahead.
 //
 // Every wait is bounded (1 s of %globaltimer): a grid barrier that gives up
 // sets ERR_GRID_TIMEOUT in the device error word, later barriers of the
 // launch then pass at once, and named CTA barriers are never skipped, so the
-// kernel always ends.  The producer drains its own bulk copies before it
-// exits.  No copy uses cluster multicast.
+// kernel always ends.  Every ticket issued is consumed (waited for) before
+// the CTA exits, so no copy is in flight at exit.  No copy uses cluster
+// multicast.
 #include <algorithm>
 #include <cmath>
+#include <vector>
 
 #include "common.cuh"
 #include "decode.cuh"
@@ -75,7 +77,7 @@ namespace {
 
 constexpr int ATT_CHUNK_P = 256;              // attention positions per chunk (as the kernel chain)
 constexpr int PK_NCW = 8;                      // consumer warps: the canonical 256 lanes
-constexpr int PK_THREADS = (PK_NCW + 1) * 32;  // + the producer warp
+constexpr int PK_THREADS = PK_NCW * 32;        // every warp consumes and refills the ring
 constexpr int PK_NSLOT = 16;                   // ring slots (8 when shared memory is short)
 // One ring slot: 8 rows x 10 superblocks at an odd pitch of 16-byte chunks
 // (eight rows of a 2560-wide Q4_K matrix); every phase picks its rows per
@@ -115,8 +117,7 @@ struct PkParams {
 
 #ifdef ABRA_PK_TRACE
 // Diagnostic build only: %globaltimer stamps of each CTA's phase starts,
-// ends and end of inputs (consumers) and of the producer's last copy of each
-// phase.
+// ends and end of inputs.
 constexpr int PK_TRACE_EV = 512;
 __device__ unsigned long long g_pk_trace[160][5][PK_TRACE_EV];
 __shared__ unsigned long long g_pk_wait_ns;  // this CTA's warps' waits on ring slots, per phase
@@ -180,10 +181,6 @@ struct PkMm {
     int N, nsb, lr, pitch;
 };
 
-// GEMV kind of producer phase ph (per layer q|k|v, o, gate/up, down; then
-// the output).
-__device__ __forceinline__ int pk_kind(int ph, int nph) { return ph == nph - 1 ? PK_OUT : (ph & 3); }
-
 // The weight matrix (or gate/up pair) of GEMV `kind` of `layer`.
 __device__ __forceinline__ PkMm pk_mm(const PkParams &P, int layer, int kind) {
     PkMm mm;
@@ -226,59 +223,91 @@ __device__ __forceinline__ void pk_range(const PkMm &mm, int &u_begin, int &nu) 
     nu = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x) - u_begin;
 }
 
-// ----------------------------------------------------------- producer ---
-__device__ __forceinline__ void pk_producer(const PkParams &P, uint8_t *ring, uint64_t *full, uint64_t *empty) {
-    const int lane = threadIdx.x & 31;
-    const uint64_t pol = policy_evict_first();
-    uint32_t t = 0;
-    bool ok = true;
-    const int nph = 4 * P.n_layers + 1;
-    const int sh = P.slot_shift;
-    const uint32_t nslot = 1u << sh, smask = nslot - 1u;
-    for (int ph = 0; ph < nph && ok; ++ph) {
-        const PkMm mm = pk_mm(P, ph >> 2, pk_kind(ph, nph));
-        const int nmat = mm.w1 ? 2 : 1, R = 1 << mm.lr;
-        const uint32_t row_bytes = static_cast<uint32_t>(mm.nsb) * Q4K_BYTES;
-        int u_begin, nu;
-        pk_range(mm, u_begin, nu);
-        for (int u = 0; u < nu; ++u, ++t) {
-            const int s = static_cast<int>(t & smask);
-            const uint32_t k = t >> sh;
-            if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1, ERR_WAIT_EMPTY)) {
-                ok = false;
-                break;
-            }
-            // the unit's rows are contiguous in HBM: one copy per matrix
-            const int row0 = (u_begin + u) * R, nvalid = min(R, mm.N - row0);
-            const uint32_t bytes = static_cast<uint32_t>(nvalid) * row_bytes;
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], nmat * bytes);
-            __syncwarp();
-            if (lane < nmat)
-                bulk_g2s(ring + s * PK_SLOT_BYTES + lane * R * row_bytes,
-                         (lane ? mm.w1 : mm.w0) + static_cast<int64_t>(row0) * row_bytes, bytes, &full[s], pol);
+// ------------------------------------------------------ weight stream ---
+// There is no producer warp: the warp that finishes with ring slot s
+// (ticket t) refills it with ticket t + NSLOT, and the CTA's first NSLOT
+// tickets are issued at launch.  A producer warp refilled a slot as soon as it
+// was released and was otherwise blocked NSLOT tickets ahead, so the stream's
+// timing is the same; what changes is the warp count: eight warps put two on
+// each SM sub-partition (a ninth put three on one, whose 16K registers then
+// capped every thread at 168 and spilled).
+//
+// Ticket map of a CTA: its unit count and first unit per GEMV kind (the same
+// in every layer), the units of one layer, the token's total.
+struct PkTickets {
+    int nu[PK_KINDS], ub[PK_KINDS];
+    int per_layer;
+    uint32_t total;
+};
+// For CTA b of G, rows N[kind] in units of 2^lr[kind] rows (pk_range's split).
+__host__ __device__ __forceinline__ void pk_tickets_for(const int (&N)[PK_KINDS], const int (&lr)[PK_KINDS],
+                                                        int n_layers, int b, int G, PkTickets &k) {
+    k.per_layer = 0;
+    for (int kind = 0; kind < PK_KINDS; ++kind) {
+        const int total = (N[kind] + (1 << lr[kind]) - 1) >> lr[kind];
+        k.ub[kind] = static_cast<int>(static_cast<int64_t>(b) * total / G);
+        k.nu[kind] = static_cast<int>(static_cast<int64_t>(b + 1) * total / G) - k.ub[kind];
+        if (kind < PK_OUT) k.per_layer += k.nu[kind];
+    }
+    k.total = static_cast<uint32_t>(n_layers) * static_cast<uint32_t>(k.per_layer) + static_cast<uint32_t>(k.nu[PK_OUT]);
+}
+__device__ __forceinline__ void pk_tickets(const PkParams &P, PkTickets &k) {
+    const int N[PK_KINDS] = {(P.n_heads + 2 * P.n_kv) * 128, P.hidden, P.ffn, P.hidden, P.vocab};
+    const int lr[PK_KINDS] = {P.lr[0], P.lr[1], P.lr[2], P.lr[3], P.lr[4]};
+    pk_tickets_for(N, lr, P.n_layers, blockIdx.x, gridDim.x, k);
+}
+
+// Position of a ticket in the token: GEMV kind, layer (P.n_layers for the
+// output) and unit within the CTA's share.
+struct PkTicketPos {
+    int kind, layer, u;
+};
+// The position `ahead` tickets after `at` (walks forward over the phases).
+__host__ __device__ __forceinline__ PkTicketPos pk_ticket_ahead(const PkTickets &k, int n_layers, PkTicketPos at, int ahead) {
+    int rem = at.u + ahead;
+    while (at.kind != PK_OUT && rem >= k.nu[at.kind]) {
+        rem -= k.nu[at.kind];
+        if (at.kind < PK_DOWN) {
+            ++at.kind;
+        } else if (at.layer + 1 < n_layers) {
+            ++at.layer;
+            at.kind = PK_QKV;
+        } else {
+            at.layer = n_layers;
+            at.kind = PK_OUT;
         }
-        if (lane == 0) PK_STAMP(2, ph);
     }
-    if (ok && P.n_layers > 0) {
-        // the next token starts with this CTA's q|k|v rows of layer 0: into L2
-        const PkMm mm = pk_mm(P, 0, PK_QKV);
-        int u_begin, nu;
-        pk_range(mm, u_begin, nu);
-        const int64_t row_bytes = static_cast<int64_t>(mm.nsb) * Q4K_BYTES;
-        const int64_t row0 = static_cast<int64_t>(u_begin) << mm.lr;
-        const int64_t rows = min(static_cast<int64_t>(nu) << mm.lr, static_cast<int64_t>(mm.N) - row0);
-        const uint8_t *base = mm.w0 + row0 * row_bytes;
-        const int64_t bytes = rows > 0 ? rows * row_bytes : 0;  // a multiple of 16 (144 per block)
-        constexpr int64_t PIECE = 16384;
-        for (int64_t o = static_cast<int64_t>(lane) * PIECE; o < bytes; o += 32 * PIECE)
-            prefetch_l2_bulk(base + o, static_cast<uint32_t>(min(PIECE, bytes - o)));
-    }
-    // drain: every copy this warp issued has landed before the CTA can exit
-    if (lane == 0) {
-        const uint32_t first = t > nslot ? t - nslot : 0;
-        for (uint32_t tt = first; tt < t; ++tt) mbar_wait(&full[tt & smask], (tt >> sh) & 1);
-    }
-    __syncwarp();
+    at.u = rem;  // past nu[PK_OUT]: beyond the token
+    return at;
+}
+
+// One lane: the rows of the unit at `pos` into ring slot s (one bulk copy per
+// matrix), the slot's full barrier expecting their bytes.
+__device__ __forceinline__ void pk_issue(const PkParams &P, const PkTickets &k, PkTicketPos pos, int s, uint8_t *ring,
+                                         uint64_t *full, uint64_t pol) {
+    const PkMm mm = pk_mm(P, pos.kind == PK_OUT ? 0 : pos.layer, pos.kind);
+    const int nmat = mm.w1 ? 2 : 1, R = 1 << mm.lr;
+    const uint32_t row_bytes = static_cast<uint32_t>(mm.nsb) * Q4K_BYTES;
+    const int row0 = (k.ub[pos.kind] + pos.u) * R, nvalid = min(R, mm.N - row0);
+    const uint32_t bytes = static_cast<uint32_t>(nvalid) * row_bytes;
+    mbar_arrive_expect_tx(&full[s], nmat * bytes);
+    for (int m = 0; m < nmat; ++m)
+        bulk_g2s(ring + s * PK_SLOT_BYTES + m * R * row_bytes, (m ? mm.w1 : mm.w0) + static_cast<int64_t>(row0) * row_bytes,
+                 bytes, &full[s], pol);
+}
+
+// The CTA's q|k|v rows of layer 0 -- where the next token starts -- into L2
+// (one lane; asynchronous).
+__device__ __forceinline__ void pk_prefetch_next(const PkParams &P, const PkTickets &k) {
+    if (P.n_layers <= 0) return;
+    const PkMm mm = pk_mm(P, 0, PK_QKV);
+    const int64_t row_bytes = static_cast<int64_t>(mm.nsb) * Q4K_BYTES;
+    const int64_t row0 = static_cast<int64_t>(k.ub[PK_QKV]) << mm.lr;
+    const int64_t rows = min(static_cast<int64_t>(k.nu[PK_QKV]) << mm.lr, static_cast<int64_t>(mm.N) - row0);
+    const uint8_t *base = mm.w0 + row0 * row_bytes;
+    const int64_t bytes = rows > 0 ? rows * row_bytes : 0;  // a multiple of 16 (144 per block)
+    constexpr int64_t PIECE = 16384;
+    for (int64_t o = 0; o < bytes; o += PIECE) prefetch_l2_bulk(base + o, static_cast<uint32_t>(min(PIECE, bytes - o)));
 }
 
 // --------------------------------------------------- consumer: GEMV units ---
@@ -288,21 +317,22 @@ __device__ __forceinline__ void pk_producer(const PkParams &P, uint8_t *ring, ui
 // K-slice sums and their fixed tree; the row's first lane stores y (and
 // merges the argmax key).
 template <int NMAT>
-__device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, uint32_t T, const uint8_t *ring,
-                                         uint64_t *full, uint64_t *empty, float *vbuf, const uint8_t *arec,
+__device__ __forceinline__ void pk_units(const PkParams &P, const PkTickets &tk, PkTicketPos at, uint64_t pol,
+                                         const PkMm &mm, int u_begin, int nu, uint32_t T, uint8_t *ring,
+                                         uint64_t *full, float *vbuf, const uint8_t *arec,
                                          float *Y, unsigned long long *s_amax, int sh, bool &poisoned) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int lr = mm.lr, R = 1 << lr, P = 32 >> lr;
+    const int lr = mm.lr, R = 1 << lr, LP = 32 >> lr;  // LP lanes per row
     // lane -> (row r, first superblock p); rows are staged back to back
     // (pitch nsb * 144 B = 9 nsb chunks of 16 B), so the chunk of (r, b) is
-    // 9 nsb r + 9 b + c == (nsb r + b) mod 8 bank groups.  P >= 8: a
+    // 9 nsb r + 9 b + c == (nsb r + b) mod 8 bank groups.  LP >= 8: a
     // quarter warp is one row and eight consecutive superblocks (distinct);
-    // P == 4 (eight rows): a quarter warp is four rows x two superblocks,
+    // LP == 4 (eight rows): a quarter warp is four rows x two superblocks,
     // distinct for nsb == 2 mod 8 (the 2560-wide matrices)
     int r, p;
-    if (P >= 8) {
-        r = lane / P;
-        p = lane % P;
+    if (LP >= 8) {
+        r = lane / LP;
+        p = lane % LP;
     } else {
         const int q4 = lane >> 3, w8 = lane & 7;
         r = (w8 >> 1) + 4 * (q4 & 1);
@@ -323,7 +353,7 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
         const uint8_t *wrow[NMAT];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) wrow[m] = ring + s * PK_SLOT_BYTES + (m * R + r) * mm.pitch;
-        for (int b = p; b < nsb; b += P) {
+        for (int b = p; b < nsb; b += LP) {
             const uint8_t *wsb[NMAT];
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) wsb[m] = wrow[m] + b * Q4K_BYTES;
@@ -333,9 +363,15 @@ __device__ __forceinline__ void pk_units(const PkMm &mm, int u_begin, int nu, ui
             for (int m = 0; m < NMAT; ++m) vbuf[(m * R + r) * nsb + b] = v[m];
         }
         __syncwarp();
-        // the slot's weights are consumed: lane 31 stores nothing to global
-        // memory, so its release does not wait for this warp's output stores
-        if (lane == 31) mbar_arrive(&empty[s]);
+        // the slot's weights are consumed: lane 31 refills it with the ticket
+        // NSLOT ahead (ordered after the lanes' reads of the slot: the warp
+        // barrier, then a proxy fence before the asynchronous copy)
+        if (lane == 31 && t + (1u << sh) < tk.total) {
+            at.u = u;
+            const PkTicketPos nx = pk_ticket_ahead(tk, P.n_layers, at, 1 << sh);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            pk_issue(P, tk, nx, s, ring, full, pol);
+        }
         // row sums: lane 8g + i forms slice i of rows g, g + 4 of the unit,
         // the slice tree runs across the group's eight lanes, lane 8g stores
         const int i = lane & 7, g = lane >> 3;
@@ -955,29 +991,31 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
     __shared__ float s_nred[8];
     __shared__ unsigned long long s_amax;
     __shared__ unsigned s_flag;
+    __shared__ PkTickets s_tk;  // this CTA's ticket map (indexed by GEMV kind at run time)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *empty = full + PK_NSLOT;
     uint8_t *ring = smem + P.off_ring;
     const int pos = __ldcg(P.pos);
     if (pos < 0 || pos >= P.max_ctx) return;  // the host never steps past max_ctx
     if (threadIdx.x == 0) {
-        for (int s = 0; s < (1 << P.slot_shift); ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
+        for (int s = 0; s < (1 << P.slot_shift); ++s) mbar_init(&full[s], 1);
         fence_mbar_init();
+        pk_tickets(P, s_tk);
     }
     __syncthreads();
-    if (threadIdx.x >= PK_NCW * 32) {
-        pk_producer(P, ring, full, empty);
-        return;
-    }
-    // ------------------------------------------------------ consumers ---
     const int t = threadIdx.x;
+    const int L = P.n_layers;
+    const PkTickets &tk = s_tk;
+    const uint64_t pol = policy_evict_first();
+    const PkTicketPos start = {L > 0 ? PK_QKV : PK_OUT, 0, 0};
+    if ((t & 31) == 0) {  // the first NSLOT tickets, lane 0 of warp w: w, w + 8
+        const uint32_t first = min(tk.total, 1u << P.slot_shift);
+        for (uint32_t tt = t >> 5; tt < first; tt += PK_NCW)
+            pk_issue(P, tk, pk_ticket_ahead(tk, L, start, static_cast<int>(tt)), static_cast<int>(tt), ring, full, pol);
+    }
     float *vbuf = reinterpret_cast<float *>(smem + P.off_vbuf) + (t >> 5) * PK_VMAX;
     uint8_t *arec = smem + P.off_arec;
     float *scr = reinterpret_cast<float *>(smem + P.off_x);
-    const int L = P.n_layers, hidden = P.hidden;
+    const int hidden = P.hidden;
     float *s_x = scr, *s_w = scr + hidden;
     const unsigned long long G = gridDim.x;
     const int nev = 5 * L + 1;  // phases of the token; a grid barrier between consecutive ones
@@ -1043,10 +1081,12 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_token_kernel(const PkPar
             int u_begin, nu;
             pk_range(mm, u_begin, nu);
             unsigned long long *amax = ph == PH_OUT ? &s_amax : nullptr;
+            const PkTicketPos at = {kind, ph == PH_OUT ? L : l, 0};
+            if (ph == PH_OUT && t == PK_NCW * 32 - 1) pk_prefetch_next(P, tk);
             if (mm.w1)
-                pk_units<2>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
+                pk_units<2>(P, tk, at, pol, mm, u_begin, nu, T, ring, full, vbuf, arec, Y, amax, P.slot_shift, poisoned);
             else
-                pk_units<1>(mm, u_begin, nu, T, ring, full, empty, vbuf, arec, Y, amax, P.slot_shift, poisoned);
+                pk_units<1>(P, tk, at, pol, mm, u_begin, nu, T, ring, full, vbuf, arec, Y, amax, P.slot_shift, poisoned);
             T += static_cast<uint32_t>(nu);
         }
         cta_sync();
@@ -1253,7 +1293,7 @@ cudaError_t launch_persist_step(const PersistModel &pm, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, fn, P);
 }
 
-// Host-side walk of every bulk copy the producers of `sms` CTAs would issue
+// Host-side walk of every bulk copy the warps of `sms` CTAs would issue
 // for a model shape, checked against the ring slot and the weight tensors:
 // out = {smem, ring bytes, units of the busiest CTA, copies checked, rows per
 // unit of the five GEMVs}.  Returns false with *why set when a copy would
@@ -1271,6 +1311,33 @@ bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn
         if (why) *why = w;
         return false;
     };
+    // the ticket walk the consumer warps refill the ring with: from the start,
+    // and NSLOT ahead of every ticket, it must name the unit of the sequential
+    // phase-by-phase order
+    const int Nk[PK_KINDS] = {rows[0], rows[1], rows[2], rows[3], rows[4]};
+    int lrk[PK_KINDS];
+    for (int k = 0; k < PK_KINDS; ++k) lrk[k] = pl.rows[k] == 8 ? 3 : pl.rows[k] == 4 ? 2 : pl.rows[k] == 2 ? 1 : 0;
+    for (int b = 0; b < sms; ++b) {
+        PkTickets tk;
+        pk_tickets_for(Nk, lrk, n_layers, b, sms, tk);
+        std::vector<PkTicketPos> seq;
+        for (int l = 0; l < n_layers; ++l)
+            for (int k = 0; k < PK_OUT; ++k)
+                for (int u = 0; u < tk.nu[k]; ++u) seq.push_back({k, l, u});
+        for (int u = 0; u < tk.nu[PK_OUT]; ++u) seq.push_back({PK_OUT, n_layers, u});
+        if (seq.size() != tk.total) return fail("ticket count");
+        const PkTicketPos start = {n_layers > 0 ? PK_QKV : PK_OUT, 0, 0};
+        const int ahead = 1 << pl.slot_shift;
+        auto same = [](const PkTicketPos &x, const PkTicketPos &y) {
+            return x.kind == y.kind && x.layer == y.layer && x.u == y.u;
+        };
+        for (size_t i = 0; i < seq.size(); ++i) {
+            if (i < static_cast<size_t>(ahead) && !same(pk_ticket_ahead(tk, n_layers, start, static_cast<int>(i)), seq[i]))
+                return fail("first tickets of the ring");
+            if (i + ahead < seq.size() && !same(pk_ticket_ahead(tk, n_layers, seq[i], ahead), seq[i + ahead]))
+                return fail("ring refill ticket");
+        }
+    }
     for (int b = 0; b < sms; ++b) {
         int64_t t = 0;
         const int nph = 4 * n_layers + 1;
