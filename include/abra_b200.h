@@ -41,8 +41,10 @@ extern "C" {
 const char *abra_version(void);
 const char *abra_last_error(void);
 /* Device error word set by kernels whose bounded waits gave up (bit 0: an
- * mbarrier wait, bit 1: a cross-rank flag wait).  clear != 0 resets it.
- * Synchronises the current device. */
+ * mbarrier wait, bit 1: a cross-rank flag wait, bit 2: a wait for a free
+ * ring stage, bit 3: a grid barrier of the persistent decode step) or that
+ * met a token id outside the vocabulary and read row 0 instead (bit 4).
+ * clear != 0 resets it.  Synchronises the current device. */
 int abra_device_error(uint32_t *out, int32_t clear);
 /* Failure detection without a fault: waits on a device counter that nothing
  * increments with the bounded cross-rank wait of the tensor-parallel kernels;
