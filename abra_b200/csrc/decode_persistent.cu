@@ -283,9 +283,8 @@ __host__ __device__ __forceinline__ PkTicketPos pk_ticket_ahead(const PkTickets 
 
 // One lane: the rows of the unit at `pos` into ring slot s (one bulk copy per
 // matrix), the slot's full barrier expecting their bytes.
-__device__ __forceinline__ void pk_issue(const PkParams &P, const PkTickets &k, PkTicketPos pos, int s, uint8_t *ring,
-                                         uint64_t *full, uint64_t pol) {
-    const PkMm mm = pk_mm(P, pos.kind == PK_OUT ? 0 : pos.layer, pos.kind);
+__device__ __forceinline__ void pk_issue_mm(const PkMm &mm, const PkTickets &k, PkTicketPos pos, int s, uint8_t *ring,
+                                            uint64_t *full, uint64_t pol) {
     const int nmat = mm.w1 ? 2 : 1, R = 1 << mm.lr;
     const uint32_t row_bytes = static_cast<uint32_t>(mm.nsb) * Q4K_BYTES;
     const int row0 = (k.ub[pos.kind] + pos.u) * R, nvalid = min(R, mm.N - row0);
@@ -294,6 +293,10 @@ __device__ __forceinline__ void pk_issue(const PkParams &P, const PkTickets &k, 
     for (int m = 0; m < nmat; ++m)
         bulk_g2s(ring + s * PK_SLOT_BYTES + m * R * row_bytes, (m ? mm.w1 : mm.w0) + static_cast<int64_t>(row0) * row_bytes,
                  bytes, &full[s], pol);
+}
+__device__ __forceinline__ void pk_issue(const PkParams &P, const PkTickets &k, PkTicketPos pos, int s, uint8_t *ring,
+                                         uint64_t *full, uint64_t pol) {
+    pk_issue_mm(pk_mm(P, pos.kind == PK_OUT ? 0 : pos.layer, pos.kind), k, pos, s, ring, full, pol);
 }
 
 // The CTA's q|k|v rows of layer 0 -- where the next token starts -- into L2
@@ -346,6 +349,17 @@ __device__ __forceinline__ void pk_units(const PkParams &P, const PkTickets &tk,
 #ifdef ABRA_PK_TRACE
         const uint64_t tw0 = globaltimer_ns();
 #endif
+        // the ticket this slot is refilled with and its weight pointers (read
+        // from the layer table in global memory), fetched now so that the
+        // load overlaps this unit's superblocks
+        const bool refill = t + (1u << sh) < tk.total;
+        PkTicketPos nx = at;
+        PkMm nmm = mm;
+        if (refill) {
+            at.u = u;
+            nx = pk_ticket_ahead(tk, P.n_layers, at, 1 << sh);
+            nmm = pk_mm(P, nx.kind == PK_OUT ? 0 : nx.layer, nx.kind);
+        }
         if (!poisoned && !mbar_wait(&full[s], (t >> sh) & 1)) poisoned = true;
 #ifdef ABRA_PK_TRACE
         if (lane == 0) atomicAdd(&g_pk_wait_ns, static_cast<unsigned long long>(globaltimer_ns() - tw0));
@@ -366,11 +380,9 @@ __device__ __forceinline__ void pk_units(const PkParams &P, const PkTickets &tk,
         // the slot's weights are consumed: lane 31 refills it with the ticket
         // NSLOT ahead (ordered after the lanes' reads of the slot: the warp
         // barrier, then a proxy fence before the asynchronous copy)
-        if (lane == 31 && t + (1u << sh) < tk.total) {
-            at.u = u;
-            const PkTicketPos nx = pk_ticket_ahead(tk, P.n_layers, at, 1 << sh);
+        if (lane == 31 && refill) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            pk_issue(P, tk, nx, s, ring, full, pol);
+            pk_issue_mm(nmm, tk, nx, s, ring, full, pol);
         }
         // row sums: lane 8g + i forms slice i of rows g, g + 4 of the unit,
         // the slice tree runs across the group's eight lanes, lane 8g stores
