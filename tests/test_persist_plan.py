@@ -1,11 +1,14 @@
 """Host-side checks of the persistent decode kernel's plan (no GPU).
 
-abra_persist_plan walks every weight copy each CTA's producer warp would
-issue over one token -- per layer the q|k|v, o, gate/up and down units, then
+abra_persist_plan walks every weight copy each CTA's warps would issue over
+one token -- per layer the q|k|v, o, gate/up and down units, then
 the tied output -- and checks it against its shared-memory ring slot (bounds,
 16-byte alignment, the mbarrier transaction limit) and against its weight
-tensor.  The sizes are the decode model's shapes on B200's 148 SMs and on
-other SM counts, so that the grid split leaves ragged row ranges."""
+tensor, and it checks the ticket walk by which each warp refills the slot
+it finished (from the start, and NSLOT tickets ahead of every ticket) against
+the sequential phase-by-phase order.  The sizes are the decode model's shapes
+on B200's 148 SMs and on other SM counts, so that the grid split leaves
+ragged row ranges."""
 from __future__ import annotations
 
 import pytest
@@ -21,6 +24,8 @@ SHAPES = [
     dict(n_layers=2, hidden=512, n_heads=8, n_kv_heads=1, ffn=768, vocab=1000),
     dict(n_layers=2, hidden=256, n_heads=2, n_kv_heads=2, ffn=512, vocab=1000),
     dict(n_layers=0, vocab=300),
+    # wide activations: the eight-slot ring (the refill walk NSLOT = 8 ahead)
+    dict(n_layers=3, hidden=4096, n_heads=32, n_kv_heads=8, ffn=14336, vocab=5000),
 ]
 
 
@@ -31,6 +36,15 @@ def test_every_copy_fits_its_slot_and_tensor(shape, sms):
     assert p["smem"] <= 227 * 1024 - 1024
     assert p["ring_bytes"] % (8 * 16) == 0
     assert p["copies"] > 0
+
+
+def test_wide_shape_uses_eight_slots():
+    """A 4096-wide model with a 14336-wide FFN leaves room for eight ring
+    slots only; its plan (every copy, and the walk by which each warp refills
+    the slot it finished with the unit eight tickets ahead) is checked like
+    the sixteen-slot plans."""
+    p = persist_plan(148, n_layers=3, hidden=4096, n_heads=32, n_kv_heads=8, ffn=14336, vocab=5000)
+    assert p["ring_bytes"] == 8 * 8 * 1456
 
 
 def test_qwen_plan():
