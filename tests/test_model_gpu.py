@@ -97,6 +97,31 @@ def test_persistent_gqa_shapes_bit_exact_across_chunks(shape):
     c.close()
 
 
+def test_persistent_eight_slot_ring_bit_exact():
+    """A 4096-wide model with a 14336-wide FFN: its activations leave shared
+    memory for eight ring slots only, so each warp refills the slot it
+    finished with the unit eight tickets ahead.  Logits bit-identical to the
+    oracle at every step."""
+    from abra_b200.model import DecodeModel, persist_plan
+
+    shape = dict(hidden=4096, n_heads=32, n_kv_heads=8, ffn=14336)
+    assert persist_plan(148, n_layers=2, vocab=1000, **shape)["ring_bytes"] == 8 * 8 * 1456
+    cfg = dict(n_layers=2, vocab=1000, max_ctx=64, centered=1, seed=6, **shape)
+    g, c = DecodeModel(**cfg), O.OrcModel(**cfg)
+    assert g.persistent
+    prompt = _prompt(3, 1000, 7)
+    g.reset(prompt)
+    tok = None
+    for pos in range(24):
+        feed = int(prompt[pos]) if pos < len(prompt) else tok
+        tok, want = c.step(feed, pos, logits=True)
+        g.step(1)
+        got = g.logits()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"logits differ at pos {pos}"
+    g.close()
+    c.close()
+
+
 def test_graph_eager_no_pdl_and_no_prefetch_agree():
     """Every way of running the step -- the persistent kernel as a graph or
     eager, the kernel chain with and without graphs, PDL and L2 prefetch --
