@@ -76,14 +76,14 @@ namespace abra {
 namespace {
 
 constexpr int ATT_CHUNK_P = 256;              // attention positions per chunk (as the kernel chain)
-constexpr int PK_NCW = 8;                      // consumer warps: the canonical 256 lanes
+constexpr int PK_NCW = 8;                      // warps: the canonical 256 lanes
 constexpr int PK_THREADS = PK_NCW * 32;        // every warp consumes and refills the ring
 constexpr int PK_NSLOT = 16;                   // ring slots (8 when shared memory is short)
 // One ring slot: 8 rows x 10 superblocks at an odd pitch of 16-byte chunks
 // (eight rows of a 2560-wide Q4_K matrix); every phase picks its rows per
 // unit so that a unit fits.
 constexpr int PK_SLOT_BYTES = 8 * 1456;
-static_assert(PK_NSLOT % PK_NCW == 0 && PK_NSLOT / 2 == PK_NCW, "slots: 16 or 8, multiples of the consumer warps");
+static_assert(PK_NSLOT % PK_NCW == 0 && PK_NSLOT / 2 == PK_NCW, "slots: 16 or 8, multiples of the warps");
 // Activation record of one superblock in shared memory (lane_gemv.cuh).
 constexpr int PK_AREC = LG_AREC;
 // Per-warp staging of the superblock values of one unit (rows x superblocks
@@ -1200,7 +1200,7 @@ bool pk_plan(int hidden, int n_heads, int n_kv, int ffn, int head_dim, int vocab
     }
     const int nsb_max = std::max(std::max(hidden, n_heads * 128), ffn) / QK_K;
     const int scratch = std::max(8 * hidden, 4 * pk_att_floats(gq));
-    int o = 16 * PK_NSLOT;  // full + empty mbarriers (room for 16 slots)
+    int o = 16 * PK_NSLOT;  // the slots' full mbarriers (room reserved for two per slot)
     pl.off_vbuf = pk_align(o, 16);
     o = pl.off_vbuf + PK_NCW * PK_VMAX * 4;
     pl.off_arec = pk_align(o, 128);
@@ -1323,7 +1323,7 @@ bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn
         if (why) *why = w;
         return false;
     };
-    // the ticket walk the consumer warps refill the ring with: from the start,
+    // the ticket walk the warps refill the ring with: from the start,
     // and NSLOT ahead of every ticket, it must name the unit of the sequential
     // phase-by-phase order
     const int Nk[PK_KINDS] = {rows[0], rows[1], rows[2], rows[3], rows[4]};
