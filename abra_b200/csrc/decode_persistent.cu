@@ -1323,6 +1323,37 @@ bool persist_plan_check(int n_layers, int hidden, int n_heads, int n_kv, int ffn
         if (why) *why = w;
         return false;
     };
+    // the consumer side of a unit (the same for every unit of a GEMV kind):
+    // every lane's superblock reads inside its slot, its staging-buffer
+    // writes and the row sums' reads inside PK_VMAX, its activation records
+    // inside the staged K -- the lane map of pk_units, restated
+    for (int kind = 0; kind < PK_KINDS; ++kind) {
+        const int R = pl.rows[kind], lr = R == 8 ? 3 : R == 4 ? 2 : R == 2 ? 1 : 0, LP = 32 >> lr;
+        const int nb = nsb[kind], nm = nmat[kind];
+        for (int lane = 0; lane < 32; ++lane) {
+            int r, p0;
+            if (LP >= 8) {
+                r = lane / LP;
+                p0 = lane % LP;
+            } else {
+                const int q4 = lane >> 3, w8 = lane & 7;
+                r = (w8 >> 1) + 4 * (q4 & 1);
+                p0 = (w8 & 1) + 2 * (q4 >> 1);
+            }
+            if (r >= R) return fail("lane row outside its unit");
+            for (int bb = p0; bb < nb; bb += LP)
+                for (int m = 0; m < nm; ++m) {
+                    const int64_t off = static_cast<int64_t>(m * R + r) * pl.pitch[kind] + bb * Q4K_BYTES;
+                    if (off + Q4K_BYTES > static_cast<int64_t>(nm) * R * pl.pitch[kind] || off + Q4K_BYTES > PK_SLOT_BYTES ||
+                        (m * R + r) * nb + bb >= PK_VMAX)
+                        return fail("a lane's superblock leaves its slot or staging buffer");
+                }
+            for (int half = 0; half < 2; ++half) {  // row sums: rows g, g + 4 of the unit
+                const int rr = (lane >> 3) + 4 * half;
+                if (rr < R && ((nm - 1) * R + rr + 1) * nb > PK_VMAX) return fail("row sums leave the staging buffer");
+            }
+        }
+    }
     // the ticket walk the warps refill the ring with: from the start,
     // and NSLOT ahead of every ticket, it must name the unit of the sequential
     // phase-by-phase order

@@ -4,7 +4,9 @@ abra_persist_plan walks every weight copy each CTA's warps would issue over
 one token -- per layer the q|k|v, o, gate/up and down units, then
 the tied output -- and checks it against its shared-memory ring slot (bounds,
 16-byte alignment, the mbarrier transaction limit) and against its weight
-tensor, and it checks the ticket walk by which each warp refills the slot
+tensor; it follows every lane of a unit through its superblock reads, its
+staging-buffer writes and the row sums' reads (the kernel's lane map); and it
+checks the ticket walk by which each warp refills the slot
 it finished (from the start, and NSLOT tickets ahead of every ticket) against
 the sequential phase-by-phase order.  The sizes are the decode model's shapes
 on B200's 148 SMs and on other SM counts, so that the grid split leaves
